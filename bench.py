@@ -1,0 +1,747 @@
+"""Benchmark of the hexkernels hot path on B200s (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+                    [--impl ours|reference] [--ops all|none]
+
+Workloads (the benchmark configurations, synthetic seeded inputs, all inputs
+larger than the 126 MB L2 so no flush is needed between steps):
+  reduce     fp32 row softmax + layernorm over 65536 x 4096 (x = 8 N(0,1),
+             gamma N(1,0.1), beta N(0,0.1), eps 1e-5); a step is one softmax
+             pass and one layernorm pass; metric GB/s moved (default, headline)
+  gemm_u8s8  u8 x s8 GEMM M=16384 N=K=8192, zpA 128, per-channel requant to
+             u8; metric TOPS (2 M N K per step)
+  gemm_f16   fp16 GEMM M=N=K=8192, B column-major, fp32 accumulate; TFLOP/s
+  attn       causal fp16 SDPA B=8 H=32 S=4096 D=128; TFLOP/s with the causal
+             FLOP count 4 B H D S (S+1) / 2
+  gemm_i8    int8 GEMM M=N=K=256 + requant (the CPU-runnable configuration)
+
+With N > 1 (torchrun) the rows (M rows, or B*H heads) are split across the
+ranks (strong scaling, no data-path collective); each rank times on its own
+device with CUDA events and the job time is the max over ranks.
+
+Rank 0 prints one JSON line.  `--impl reference` times the reference's scalar
+CPU code (or its restatement where the reference has no such shape) on all
+host cores for the same workload and prints the same line with
+"impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+BASELINE_METRIC = "int8 GEMM TOPS, fp16 attn TFLOP/s, reduce GB/s; % roofline @1/2/4/8 B200"
+
+
+# ------------------------------------------------------------------ helpers
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def load_traffic():
+    p = REPO / "profiles" / "traffic.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+class ClockSampler:
+    """Polls NVML (SM clock, clock-event reasons) every 20 ms in a thread."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, ordinal: int):
+        self.ok = False
+        self.samples = []
+        self.reasons = 0
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(ordinal)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: report nothing rather than guess
+            self.err = str(e)
+
+    def _run(self):
+        nv = self.nvml
+        while not self.stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self.ok:
+            self.stop = threading.Event()
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self.stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        med = float(np.median(self.samples)) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+class Dist:
+    def __init__(self, gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+        if gpus > 1 and self.world == 1:
+            raise SystemExit(f"--gpus {gpus} needs torchrun with {gpus} processes")
+
+    def init(self, backend: str):
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+def shard(total: int, world: int, rank: int):
+    return total * rank // world, total * (rank + 1) // world
+
+
+# ---------------------------------------------------------------- workloads
+
+class Workload:
+    """One benchmark configuration.  Subclasses define the per-rank device
+    buffers, one step (device path), the host-API step (e2e) and a bounded CPU
+    sample."""
+    name = ""
+    unit = ""
+    dtype = ""
+    bound = "hbm"
+
+    def __init__(self, world=1, rank=0):
+        self.world, self.rank = world, rank
+
+    # total algorithmic units (bytes or ops) of one whole-job step
+    def units_per_step(self) -> float:
+        raise NotImplementedError
+
+    def scale(self) -> float:
+        return 1e9 if self.unit == "GB/s" else 1e12
+
+
+class Reduce(Workload):
+    name = "reduce"
+    unit = "GB/s"
+    dtype = "f32"
+    R, C, EPS = 65536, 4096, 1e-5
+
+    def config(self):
+        return {"workload": "fp32 row softmax + layernorm 65536x4096", "rows": self.R,
+                "cols": self.C, "eps": self.EPS, "x": "8*N(0,1)", "gamma": "N(1,0.1)",
+                "beta": "N(0,0.1)", "seed": 0, "l2": "inputs 1 GiB > L2, no flush",
+                "sharding": "rows", "parallelism": f"rows/{self.world}"}
+
+    def units_per_step(self):
+        # softmax and layernorm each read R*C and write R*C fp32 (+ gamma, beta)
+        return 2 * 2 * self.R * self.C * 4 + 2 * self.C * 4
+
+    def host_inputs(self):
+        r0, r1 = shard(self.R, self.world, self.rank)
+        rng = np.random.default_rng(0)
+        # generate only this rank's rows, deterministically per row block
+        x = np.empty((r1 - r0, self.C), np.float32)
+        blk = 4096
+        for b0 in range(r0 - r0 % blk, r1, blk):
+            xb = (np.random.default_rng([0, b0]).standard_normal((blk, self.C), dtype=np.float32) * 8)
+            lo, hi = max(b0, r0), min(b0 + blk, r1)
+            x[lo - r0:hi - r0] = xb[lo - b0:hi - b0]
+        g = rng.normal(1, 0.1, self.C).astype(np.float32)
+        b = rng.normal(0, 0.1, self.C).astype(np.float32)
+        return x, g, b
+
+    def setup_device(self, torch):
+        x, g, b = self.host_inputs()
+        self.nrows = x.shape[0]
+        self.x = torch.from_numpy(x).cuda()
+        self.g = torch.from_numpy(g).cuda()
+        self.b = torch.from_numpy(b).cuda()
+        self.o1 = torch.empty_like(self.x)
+        self.o2 = torch.empty_like(self.x)
+        self.hx_host = (x, g, b)
+
+    def kernels(self):
+        # (label, algorithmic units of one launch on this rank)
+        per = 2 * self.nrows * self.C * 4
+        return [("softmax_f32", per), ("layernorm_f32", per + 2 * self.C * 4)]
+
+    def launch(self, device, k):
+        if k == 0:
+            device.launch("softmax_f32", 0, self.x, self.o1, self.nrows, self.C)
+        else:
+            device.launch("layernorm_f32", 0, self.x, self.g, self.b, self.o2, self.nrows, self.C,
+                          self.EPS)
+
+    # e2e through the public host API with pinned host buffers
+    def setup_e2e(self, torch):
+        x, g, b = self.hx_host
+        self.px = torch.from_numpy(x).pin_memory()
+        self.pg_ = torch.from_numpy(g).pin_memory()
+        self.pb = torch.from_numpy(b).pin_memory()
+        self.po1 = torch.empty_like(self.px).pin_memory()
+        self.po2 = torch.empty_like(self.px).pin_memory()
+
+    def e2e_step(self, lib, check):
+        n = self.nrows
+        check(lib.hexcuda_host_softmax_f32(self.px.data_ptr(), self.po1.data_ptr(), n, self.C))
+        check(lib.hexcuda_host_layernorm_f32(self.px.data_ptr(), self.pg_.data_ptr(),
+                                             self.pb.data_ptr(), self.po2.data_ptr(), n, self.C,
+                                             self.EPS))
+
+    def e2e_bytes(self):
+        n = self.nrows
+        return {"h2d_bytes_per_step": 2 * n * self.C * 4 + 2 * self.C * 4,
+                "d2h_bytes_per_step": 2 * n * self.C * 4}
+
+    def cpu_step(self, o, rows, nthreads):
+        """Reference CPU code on `rows` rows; returns algorithmic bytes."""
+        x = self.cpu_x[:rows]
+        out = self.cpu_out[:rows]
+        o.parallel(o.OP_SOFTMAX_F32, o.rows_args(x=x, out=out, R=rows, C=self.C), 0, rows, nthreads)
+        o.parallel(o.OP_LAYERNORM_F32, o.rows_args(x=x, gamma=self.cpu_g, beta=self.cpu_b, out=out,
+                                                   R=rows, C=self.C, eps=self.EPS), 0, rows,
+                   nthreads)
+        return 2 * 2 * rows * self.C * 4 + 2 * self.C * 4
+
+    def cpu_setup(self, rows):
+        rng = np.random.default_rng(0)
+        self.cpu_x = (rng.standard_normal((rows, self.C), dtype=np.float32) * 8)
+        self.cpu_out = np.empty_like(self.cpu_x)
+        self.cpu_g = rng.normal(1, 0.1, self.C).astype(np.float32)
+        self.cpu_b = rng.normal(0, 0.1, self.C).astype(np.float32)
+
+    cpu_kind = "port"
+    cpu_what = ("oracle/hexoracle.c restatement of fp16_softmax/reference.c:8-29 and "
+                "fp16_layernorm/reference.c:7-24 in fp32 (the reference caps C at 256 / one row)")
+
+
+class GemmU8S8(Workload):
+    name = "gemm_u8s8"
+    unit = "TOPS"
+    dtype = "u8*s8->s32"
+    bound = "tensor"
+    M, N, K = 16384, 8192, 8192
+
+    def config(self):
+        return {"workload": "u8 x s8 GEMM 16384x8192x8192 per-channel requant to u8",
+                "M": self.M, "N": self.N, "K": self.K, "zpA": 128, "zp_out": 128,
+                "bias": "N(0,1000)", "mult": "[2^30,2^31)", "shift": 44, "seed": 0,
+                "l2": "inputs 192 MiB > L2, no flush", "sharding": "M rows",
+                "parallelism": f"M/{self.world}"}
+
+    def units_per_step(self):
+        return 2.0 * self.M * self.N * self.K
+
+    def setup_device(self, torch):
+        r0, r1 = shard(self.M, self.world, self.rank)
+        self.m = r1 - r0
+        g = torch.Generator(device="cuda").manual_seed(0)
+        self.A = torch.randint(0, 256, (self.m, self.K), dtype=torch.uint8, device="cuda",
+                               generator=g)
+        self.B = torch.randint(-128, 128, (self.K, self.N), dtype=torch.int8, device="cuda",
+                               generator=g)
+        self.bias = torch.round(torch.randn(self.N, device="cuda", generator=g) * 1000).int()
+        self.mult = torch.randint(2**30, 2**31 - 1, (self.N,), device="cuda", generator=g).int()
+        self.shift = torch.full((self.N,), 44, dtype=torch.int32, device="cuda")
+        self.out = torch.empty((self.m, self.N), dtype=torch.uint8, device="cuda")
+
+    def kernels(self):
+        return [("gemm_u8s8_pc", 2.0 * self.m * self.N * self.K)]
+
+    def launch(self, device, k):
+        device.launch("gemm_u8s8_pc", 0, self.A, self.B, self.bias, self.out, self.m, self.N,
+                      self.K, 128, self.mult, self.shift, 128)
+
+    def cpu_setup(self, rows):
+        rng = np.random.default_rng(0)
+        self.cA = rng.integers(0, 256, (rows, self.K), dtype=np.uint8)
+        self.cB = rng.integers(-128, 128, (self.K, self.N), dtype=np.int8)
+        self.cbias = np.round(rng.normal(0, 1000, self.N)).astype(np.int32)
+        self.cmult = rng.integers(2**30, 2**31, self.N, dtype=np.int64).astype(np.int32)
+        self.cshift = np.full(self.N, 44, np.int32)
+        self.cout = np.empty((rows, self.N), np.uint8)
+
+    def cpu_step(self, o, rows, nthreads):
+        a = o.gemm_args(A=self.cA, B=self.cB, bias=self.cbias, out=self.cout, M=rows, N=self.N,
+                        K=self.K, zpA=128, zp=128, mult_pc=self.cmult, shift_pc=self.cshift)
+        o.parallel(o.OP_GEMM_U8S8_PC, a, 0, rows, nthreads)
+        return 2.0 * rows * self.N * self.K
+
+    cpu_kind = "port"
+    cpu_what = ("oracle restatement composing gemm_tile_zp_i8/reference.c:10-28, "
+                "i8_gemm_bias_requant/reference.c:13, requant_per_channel/reference.c:4-15, "
+                "requantize_i32_u8_dma/reference.c:5-13")
+
+
+class GemmF16(Workload):
+    name = "gemm_f16"
+    unit = "TFLOP/s"
+    dtype = "f16*f16->f32"
+    bound = "tensor"
+    M = N = K = 8192
+
+    def config(self):
+        return {"workload": "fp16 GEMM 8192^3 A row-major B column-major", "M": self.M,
+                "N": self.N, "K": self.K, "entries": "N(0,1)/sqrt(K)", "seed": 0,
+                "l2": "inputs 256 MiB > L2, no flush", "sharding": "M rows",
+                "parallelism": f"M/{self.world}"}
+
+    def units_per_step(self):
+        return 2.0 * self.M * self.N * self.K
+
+    def setup_device(self, torch):
+        r0, r1 = shard(self.M, self.world, self.rank)
+        self.m = r1 - r0
+        g = torch.Generator(device="cuda").manual_seed(0)
+        s = 1.0 / math.sqrt(self.K)
+        self.A = (torch.randn((self.m, self.K), device="cuda", generator=g) * s).half()
+        self.Bt = (torch.randn((self.N, self.K), device="cuda", generator=g) * s).half()
+        self.out = torch.empty((self.m, self.N), dtype=torch.float16, device="cuda")
+
+    def kernels(self):
+        return [("gemm_f16_nt", 2.0 * self.m * self.N * self.K)]
+
+    def launch(self, device, k):
+        device.launch("gemm_f16_nt", 0, self.A, self.Bt, self.out, self.m, self.N, self.K)
+
+    def cpu_setup(self, rows):
+        rng = np.random.default_rng(0)
+        s = 1.0 / math.sqrt(self.K)
+        self.cA = (rng.standard_normal((rows, self.K), dtype=np.float32) * s).astype(np.float16)
+        self.cB = (rng.standard_normal((self.N, self.K), dtype=np.float32) * s).astype(np.float16)
+        self.cout = np.empty((rows, self.N), np.float16)
+
+    def cpu_step(self, o, rows, nthreads):
+        a = o.gemm_args(A=self.cA, B=self.cB, out=self.cout, M=rows, N=self.N, K=self.K)
+        o.parallel(o.OP_GEMM_F16_NT, a, 0, rows, nthreads)
+        return 2.0 * rows * self.N * self.K
+
+    cpu_kind = "port"
+    cpu_what = "oracle restatement of fp16_attention_qkt_hmx/reference.c:8-14 (M x N x K)"
+
+
+class Attn(Workload):
+    name = "attn"
+    unit = "TFLOP/s"
+    dtype = "f16, f32 softmax"
+    bound = "tensor"
+    B, H, S, D = 8, 32, 4096, 128
+
+    def config(self):
+        return {"workload": "causal fp16 SDPA B=8 H=32 S=4096 D=128", "B": self.B, "H": self.H,
+                "S": self.S, "D": self.D, "scale": 1 / math.sqrt(self.D), "causal": True,
+                "qkv": "N(0,1)", "seed": 0, "l2": "inputs 768 MiB > L2, no flush",
+                "sharding": "B*H heads", "parallelism": f"heads/{self.world}",
+                "flop_count": "causal: 4*B*H*D*S*(S+1)/2"}
+
+    def flops(self, heads):
+        return 4.0 * heads * self.D * self.S * (self.S + 1) / 2
+
+    def units_per_step(self):
+        return self.flops(self.B * self.H)
+
+    def setup_device(self, torch):
+        h0, h1 = shard(self.B * self.H, self.world, self.rank)
+        self.h = h1 - h0
+        g = torch.Generator(device="cuda").manual_seed(0)
+        shp = (self.h, self.S, self.D)
+        self.Q = torch.randn(shp, device="cuda", generator=g).half()
+        self.K_ = torch.randn(shp, device="cuda", generator=g).half()
+        self.V = torch.randn(shp, device="cuda", generator=g).half()
+        self.O = torch.empty_like(self.Q)
+
+    def kernels(self):
+        return [("attn_f16", self.flops(self.h))]
+
+    def launch(self, device, k):
+        device.launch("attn_f16", 0, self.Q, self.K_, self.V, self.O, self.h, self.S, self.S,
+                      self.D, 1 / math.sqrt(self.D), 1)
+
+    def cpu_setup(self, rows):
+        rng = np.random.default_rng(0)
+        shp = (1, self.S, self.D)
+        self.cQ, self.cK, self.cV = (rng.standard_normal(shp, dtype=np.float32).astype(np.float16)
+                                     for _ in range(3))
+        self.cO = np.empty_like(self.cQ)
+
+    def cpu_step(self, o, rows, nthreads):
+        # `rows` query rows of one head, spread over the causal triangle
+        a = o.attn_args(Q=self.cQ, K=self.cK, V=self.cV, O=self.cO, BH=1, SQ=self.S, SK=self.S,
+                        D=self.D, scale=1 / math.sqrt(self.D), causal=1)
+        q0 = self.S - rows
+        o.parallel(o.OP_ATTN_F16, a, q0, self.S, nthreads)
+        keys = sum(i + 1 for i in range(q0, self.S))
+        return 4.0 * self.D * keys
+
+    cpu_kind = "port"
+    cpu_what = ("oracle restatement of fp16_flash_attention_tile/reference.c:9-28 with causal "
+                "window and scale parameter")
+
+
+class GemmI8(Workload):
+    name = "gemm_i8"
+    unit = "TOPS"
+    dtype = "s8*s8->s32"
+    bound = "tensor"
+    M = N = K = 256
+
+    def config(self):
+        return {"workload": "int8 GEMM 256^3 + requant (mult [2^30,2^31), shift 8..15)",
+                "M": 256, "N": 256, "K": 256, "seed": 0, "l2": "fits in L2 (launch-bound)",
+                "sharding": "none (replicas)", "parallelism": f"replicas/{self.world}"}
+
+    def units_per_step(self):
+        return 2.0 * self.M * self.N * self.K * self.world
+
+    def setup_device(self, torch):
+        rng = np.random.default_rng(0)
+        A = rng.integers(-128, 128, (256, 256), dtype=np.int8)
+        B = rng.integers(-128, 128, (256, 256), dtype=np.int8)
+        self.mult = int(rng.integers(2**30, 2**31))
+        self.shift = int(rng.integers(8, 16))
+        self.A, self.B = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+        self.out = torch.empty((256, 256), dtype=torch.int8, device="cuda")
+
+    def kernels(self):
+        return [("gemm_i8_requant", 2.0 * 256 ** 3)]
+
+    def launch(self, device, k):
+        device.launch("gemm_i8_requant", 0, self.A, self.B, self.out, 256, 256, 256, self.mult,
+                      self.shift, 0)
+
+    def cpu_setup(self, rows):
+        rng = np.random.default_rng(0)
+        self.cA = rng.integers(-128, 128, (256, 256), dtype=np.int8)
+        self.cB = rng.integers(-128, 128, (256, 256), dtype=np.int8)
+        self.cout = np.empty((256, 256), np.int8)
+
+    def cpu_step(self, o, rows, nthreads):
+        ref = o.ref_lib()
+        if ref is not None:
+            import ctypes as C
+            ref.ref_i8_gemm_requant(self.cA.ctypes.data, self.cB.ctypes.data, self.cout.ctypes.data,
+                                    256, 256, 256, C.c_int32(1 << 30), C.c_int(10), C.c_int8(0))
+        else:
+            a = o.gemm_args(A=self.cA, B=self.cB, out=self.cout, M=256, N=256, K=256,
+                            mult=1 << 30, shift=10, zp=0)
+            o.parallel(o.OP_I8_GEMM_REQUANT, a, 0, 256, 1)
+        return 2.0 * 256 ** 3
+
+    @property
+    def cpu_kind(self):
+        from oracle import oracle as o
+        return "reference" if o.ref_lib() is not None else "port"
+
+    cpu_what = "kernels/expert/i8_gemm_requant/reference.c (one thread)"
+
+
+WORKLOADS = {w.name: w for w in (Reduce, GemmU8S8, GemmF16, Attn, GemmI8)}
+
+
+# ------------------------------------------------------------------- timing
+
+def time_device(wl, torch, device, steps, warmup, dist, lib):
+    """Timed region: barrier + sync, K steps on torch's current stream with
+    per-kernel CUDA events, sync + barrier.  Returns a dict."""
+    kernels = wl.kernels()
+    for _ in range(warmup):
+        for k in range(len(kernels)):
+            wl.launch(device, k)
+    torch.cuda.synchronize()
+    device.sync(0)
+    stream = torch.cuda.current_stream()
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in kernels] for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = lib.hexcuda_launch_count()
+    dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        start.record(stream)
+        for s in range(steps):
+            for k in range(len(kernels)):
+                ev[s][k][0].record(stream)
+                wl.launch(device, k)
+                ev[s][k][1].record(stream)
+        end.record(stream)
+        torch.cuda.synchronize()
+    dist.barrier()
+    device.sync(0)
+    launches = lib.hexcuda_launch_count() - launches0
+    ms = start.elapsed_time(end)
+    per_kernel = []
+    for k, (label, units) in enumerate(kernels):
+        dur = [ev[s][k][0].elapsed_time(ev[s][k][1]) for s in range(steps)]
+        per_kernel.append((label, units, float(np.mean(dur))))
+    return {"ms": ms, "per_kernel": per_kernel, "clocks": clk.summary(), "launches": launches}
+
+
+def time_e2e(wl, torch, lib, check, steps, warmup, dist):
+    wl.setup_e2e(torch)
+    for _ in range(max(1, warmup // 2)):
+        wl.e2e_step(lib, check)
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        wl.e2e_step(lib, check)
+    dt = time.perf_counter() - t0
+    return dt
+
+
+def cpu_measure(wl, budget_s: float, nthreads: int, max_rows: int):
+    """Bounded CPU sample: grows the sample until one call takes ~budget/4,
+    then times repeated calls for about `budget_s` seconds."""
+    from oracle import oracle as o
+    o.lib()
+    rows = 8 if wl.name != "reduce" else 256
+    rows = min(rows, max_rows)
+    while True:
+        wl.cpu_setup(rows)
+        t0 = time.perf_counter()
+        units = wl.cpu_step(o, rows, nthreads)
+        dt = time.perf_counter() - t0
+        if dt > budget_s / 4 or rows >= max_rows:
+            break
+        rows = min(max_rows, rows * 4)
+    reps, tot, units_tot = 0, 0.0, 0.0
+    while tot < budget_s * 0.75 or reps < 1:
+        t0 = time.perf_counter()
+        units_tot += wl.cpu_step(o, rows, nthreads)
+        tot += time.perf_counter() - t0
+        reps += 1
+    return units_tot / tot, rows, reps, tot
+
+
+def cpu_rows_cap(wl):
+    return {"reduce": wl.R if hasattr(wl, "R") else 0, "gemm_u8s8": 4096, "gemm_f16": 4096,
+            "attn": 4096, "gemm_i8": 256}[wl.name]
+
+
+def cpu_sample_text(wl, rows, reps, secs):
+    if wl.name == "reduce":
+        return f"{rows} of 65536 rows, softmax+layernorm, {reps} reps, {secs:.1f} s"
+    if wl.name == "attn":
+        return f"last {rows} query rows of one causal head (S=4096, D=128), {reps} reps, {secs:.1f} s"
+    if wl.name == "gemm_i8":
+        return f"the full 256^3 GEMM, {reps} reps, {secs:.1f} s"
+    return f"{rows} rows of M with full N, K, {reps} reps, {secs:.1f} s"
+
+
+# --------------------------------------------------------------------- arms
+
+def run_ours(args, dist):
+    import torch
+
+    from hexkernels_b200 import _lib, device, ops
+
+    torch.cuda.set_device(dist.local)
+    lib = _lib.load()
+    ops.init_devices([dist.local])
+    device.bind_stream(0)
+    peaks = load_peaks()
+    traffic = load_traffic()
+
+    def measure(wl_cls, with_e2e, with_cpu):
+        wl = wl_cls(dist.world, dist.rank)
+        wl.setup_device(torch)
+        t = time_device(wl, torch, device, args.steps, args.warmup, dist, lib)
+        ms_max = dist.max(t["ms"])
+        per_step_ms = ms_max / args.steps
+        value = wl.units_per_step() / (per_step_ms / 1e3) / wl.scale()
+        # dominant kernel roofline (this rank's launches)
+        label, units, dur = max(t["per_kernel"], key=lambda r: r[2])
+        achieved = units / (dur / 1e3) / wl.scale()
+        if wl.bound == "hbm":
+            peak, punit, pname = peaks["hbm_gbs"], "GB/s", "hbm_gbs"
+        else:
+            # int8 peaks are not measured by the driver: the dense int8 rate is
+            # twice the dense bf16 rate on this part, so the int8 roofline is
+            # 2x the measured bf16 figure
+            mul = 2.0 if wl.unit == "TOPS" else 1.0
+            peak, punit, pname = peaks["bf16_tflops"] * mul, wl.unit.replace("/s", "") + "/s", "bf16_tflops"
+        tr = traffic.get(label)
+        res = {
+            "metric": BASELINE_METRIC, "value": round(value, 3), "unit": wl.unit,
+            "ms_per_step": round(per_step_ms, 4), "dtype": wl.dtype, "config": wl.config(),
+            "roofline": {"bound": wl.bound, "kernel": label, "achieved": round(achieved, 2),
+                         "peak": peak, "unit": punit if wl.bound == "tensor" else "GB/s",
+                         "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peaks['source']} {pname}" +
+                                        (" x2 (int8 = 2x bf16 dense)" if wl.unit == "TOPS" else ""),
+                         "traffic": tr["bytes_per_launch"] * units / tr["units"] if tr else None,
+                         "kernel_ms": round(dur, 4)},
+            "clocks": t["clocks"], "gpu_launches": int(t["launches"]),
+        }
+        if with_e2e and hasattr(wl, "setup_e2e"):
+            check = _lib.check
+            dt = time_e2e(wl, torch, lib, check, max(2, args.steps // 10), args.warmup, dist)
+            dt = dist.max(dt)
+            nst = max(2, args.steps // 10)
+            res["e2e"] = {"value": round(wl.units_per_step() / (dt / nst) / wl.scale(), 3),
+                          "unit": wl.unit, **wl.e2e_bytes(),
+                          "api": "hexcuda_host_* (candidate_kernel shims' calls), pinned host buffers"}
+        if with_cpu and dist.rank == 0 and dist.world == 1:
+            nthreads = len(os.sched_getaffinity(0))
+            if wl.name == "gemm_i8":
+                nthreads = 1
+            v, rows, reps, secs = cpu_measure(wl, args.cpu_budget, nthreads, cpu_rows_cap(wl))
+            res["cpu_baseline"] = {"value": round(v / wl.scale(), 6), "unit": wl.unit,
+                                   "cores": nthreads, "kind": wl.cpu_kind,
+                                   "sample": cpu_sample_text(wl, rows, reps, secs),
+                                   "code": wl.cpu_what}
+        del wl
+        torch.cuda.empty_cache()
+        return res
+
+    head = measure(WORKLOADS[args.workload], True, True)
+    ops = {}
+    if args.ops == "all":
+        for name in ("gemm_u8s8", "gemm_f16", "attn", "gemm_i8"):
+            if name == args.workload:
+                continue
+            r = measure(WORKLOADS[name], False, args.cpu_all)
+            ops[name] = {k: r[k] for k in ("value", "unit", "ms_per_step", "dtype", "config",
+                                           "roofline", "clocks", "gpu_launches")
+                         if k in r}
+            if "cpu_baseline" in r:
+                ops[name]["cpu_baseline"] = r["cpu_baseline"]
+    line = {"metric": head["metric"], "value": head["value"], "unit": head["unit"],
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong" if args.workload != "gemm_i8" else "weak",
+            "vs_baseline": None, "dtype": head["dtype"], "data": "synthetic (seeded)",
+            "config": head["config"], "roofline": head["roofline"], "clocks": head["clocks"],
+            "gpu_launches": head["gpu_launches"]}
+    for k in ("e2e", "cpu_baseline"):
+        if k in head:
+            line[k] = head[k]
+    if ops:
+        line["ops"] = ops
+    return line
+
+
+def run_reference(args, dist):
+    """The reference's CPU implementation on this host's cores, same
+    workload, bounded per-step samples."""
+    wl = WORKLOADS[args.workload](1, 0)
+    from oracle import oracle as o
+    o.lib()
+    nthreads = 1 if wl.name == "gemm_i8" else len(os.sched_getaffinity(0))
+    # size the per-step sample so the whole run stays within ~2 minutes
+    per_step_budget = max(0.2, 100.0 / max(1, args.steps + args.warmup))
+    rows = 8 if wl.name != "reduce" else 256
+    cap = cpu_rows_cap(wl)
+    while True:
+        wl.cpu_setup(rows)
+        t0 = time.perf_counter()
+        wl.cpu_step(o, rows, nthreads)
+        if time.perf_counter() - t0 > per_step_budget / 2 or rows >= cap:
+            break
+        rows = min(cap, rows * 2)
+    for _ in range(args.warmup):
+        wl.cpu_step(o, rows, nthreads)
+    t0 = time.perf_counter()
+    units = 0.0
+    for _ in range(args.steps):
+        units += wl.cpu_step(o, rows, nthreads)
+    dt = time.perf_counter() - t0
+    value = units / dt / wl.scale()
+    sample = cpu_sample_text(wl, rows, args.steps, dt)
+    return {"metric": BASELINE_METRIC, "value": round(value, 6), "unit": wl.unit, "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype,
+            "data": "synthetic (seeded)", "config": wl.config(),
+            "cpu_baseline": {"value": round(value, 6), "unit": wl.unit, "cores": nthreads,
+                             "kind": wl.cpu_kind, "sample": sample, "code": wl.cpu_what},
+            "e2e": {"value": round(value, 6), "unit": wl.unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="reduce", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ops", default="all", choices=["all", "none"])
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
+                    help="seconds of CPU work per cpu_baseline sample")
+    ap.add_argument("--cpu-all", action="store_true",
+                    help="also time a CPU baseline for every extra op")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    dist = Dist(args.gpus)
+    if args.impl == "reference":
+        if dist.rank == 0:
+            print(json.dumps(run_reference(args, dist)), flush=True)
+        return
+    dist.init("nccl")
+    try:
+        line = run_ours(args, dist)
+        if dist.rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

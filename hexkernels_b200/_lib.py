@@ -1,0 +1,118 @@
+"""ctypes binding of libhexcuda's C ABI (include/hexcuda.h).
+
+The shared library is built in-tree (hexkernels_b200/libhexcuda.so) by
+``make -C hexkernels_b200/csrc``.  Loading fails loudly when it is missing:
+there is no CPU fallback for any operator.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "libhexcuda.so"
+
+P = C.c_void_p
+I = C.c_int
+I32 = C.c_int32
+I64 = C.c_int64
+U8 = C.c_uint8
+I8 = C.c_int8
+F = C.c_float
+SZ = C.c_size_t
+
+# name -> (restype, argtypes); mirrors include/hexcuda.h
+SIGNATURES: dict[str, tuple] = {
+    "hexcuda_init": (I, [I]),
+    "hexcuda_init_devices": (I, [P, I]),
+    "hexcuda_shutdown": (None, []),
+    "hexcuda_device_count": (I, []),
+    "hexcuda_device_ordinal": (I, [I]),
+    "hexcuda_alloc": (P, [I, SZ]),
+    "hexcuda_free": (I, [I, P]),
+    "hexcuda_host_alloc": (P, [SZ]),
+    "hexcuda_host_free": (I, [P]),
+    "hexcuda_h2d": (I, [I, P, P, SZ]),
+    "hexcuda_d2h": (I, [I, P, P, SZ]),
+    "hexcuda_memset": (I, [I, P, I, SZ]),
+    "hexcuda_sync": (I, [I]),
+    "hexcuda_stream": (P, [I]),
+    "hexcuda_set_stream": (I, [I, P]),
+    "hexcuda_last_error": (I, []),
+    "hexcuda_last_error_string": (C.c_char_p, []),
+    "hexcuda_set_timing": (I, [I]),
+    "hexcuda_last_kernel_ms": (F, []),
+    "hexcuda_launch_count": (C.c_uint64, []),
+    # device-pointer launchers
+    "hexcuda_softmax_f32": (I, [I, P, P, I, I]),
+    "hexcuda_softmax_f16": (I, [I, P, P, I, I]),
+    "hexcuda_layernorm_f32": (I, [I, P, P, P, P, I, I, F]),
+    "hexcuda_layernorm_f16": (I, [I, P, P, P, P, I, I, F]),
+    "hexcuda_rmsnorm_f32": (I, [I, P, P, P, I, I, F]),
+    "hexcuda_rmsnorm_f16": (I, [I, P, P, P, I, I, F]),
+    "hexcuda_rowreduce_f32": (I, [I, P, P, I, I, I]),
+    "hexcuda_requant_per_channel": (I, [I, P, P, I, I, P, P, I8]),
+    "hexcuda_requantize_i32_u8": (I, [I, P, P, I64, I32, I, U8]),
+    "hexcuda_gemm_i8_requant": (I, [I, P, P, P, I, I, I, I32, I, I8]),
+    "hexcuda_gemm_i8_bias_requant": (I, [I, P, P, P, P, I, I, I, I32, I, I8]),
+    "hexcuda_gemm_i8_zp": (I, [I, P, P, P, I, I, I, I32, I32, I]),
+    "hexcuda_gemm_u8s8_pc": (I, [I, P, P, P, P, I, I, I, I32, P, P, U8]),
+    "hexcuda_gemm_f16_nt": (I, [I, P, P, P, I, I, I]),
+    "hexcuda_gemm_f16_nn": (I, [I, P, P, P, I, I, I]),
+    "hexcuda_attn_f16": (I, [I, P, P, P, P, I, I, I, I, F, I]),
+    "hexcuda_online_softmax_step_f16": (I, [I, P, P, P, P, P, I, I]),
+    # host-pointer entries
+    "hexcuda_host_softmax_f32": (I, [P, P, I, I]),
+    "hexcuda_host_softmax_f16": (I, [P, P, I, I]),
+    "hexcuda_host_layernorm_f32": (I, [P, P, P, P, I, I, F]),
+    "hexcuda_host_layernorm_f16": (I, [P, P, P, P, I, I, F]),
+    "hexcuda_host_rmsnorm_f16": (I, [P, P, P, I, I, F]),
+    "hexcuda_host_rowreduce_f32": (I, [P, P, I, I, I]),
+    "hexcuda_host_requant_per_channel": (I, [P, P, I, I, P, P, I8]),
+    "hexcuda_host_requantize_i32_u8": (I, [P, P, I64, I32, I, U8]),
+    "hexcuda_host_gemm_i8_requant": (I, [P, P, P, I, I, I, I32, I, I8]),
+    "hexcuda_host_gemm_i8_bias_requant": (I, [P, P, P, P, I, I, I, I32, I, I8]),
+    "hexcuda_host_gemm_i8_zp": (I, [P, P, P, I, I, I, I32, I32, I]),
+    "hexcuda_host_gemm_u8s8_pc": (I, [P, P, P, P, I, I, I, I32, P, P, U8]),
+    "hexcuda_host_gemm_f16_nt": (I, [P, P, P, I, I, I]),
+    "hexcuda_host_gemm_f16_nn": (I, [P, P, P, I, I, I]),
+    "hexcuda_host_attn_f16": (I, [P, P, P, P, I, I, I, I, F, I]),
+    "hexcuda_host_online_softmax_step_f16": (I, [P, P, P, P, P, I, I]),
+}
+
+ERRORS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_NODEV", 4: "ERR_TIMEOUT", 5: "ERR_OOM"}
+
+_lib = None
+
+
+class HexcudaError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"hexcuda {ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+def load(path: str | os.PathLike | None = None) -> C.CDLL:
+    """Load libhexcuda.so and declare every exported signature."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise ImportError(
+            f"{p} is missing: build it with `make -C {PKG_DIR / 'csrc'}` "
+            "(the operators have no CPU fallback)")
+    lib = C.CDLL(str(p))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        lib = load()
+        raise HexcudaError(rc, lib.hexcuda_last_error_string().decode(errors="replace"))

@@ -1,0 +1,613 @@
+// gemm.cu -- tcgen05 GEMM engine for the corpus's fp16 and int8 GEMMs.
+//
+// out[M,N] = epilogue( A[M,K] . B[K,N] ), A and B^T both staged K-major.
+//
+// Persistent, warp-specialised kernel, one CTA per SM (192 threads):
+//   warp 0      TMA producer: 128 x 128-byte A box + BN x 128-byte B box per
+//               stage (128-byte swizzle), kStages-deep ring of full/empty
+//               mbarriers;
+//   warp 1      allocates 2*BN TMEM columns (two fp32/s32 accumulators) and,
+//               from one elected lane, issues tcgen05.mma (M=128, N=BN, 32 B
+//               of K per instruction: K=16 f16 or K=32 int8), releasing each
+//               smem stage with tcgen05.commit;
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, apply
+//               the fp16 rounding or the fixed-point requant, store to HBM,
+//               then hand the accumulator back to the MMA warp.
+// The two accumulators let the epilogue of tile i overlap the MMAs of tile
+// i+1.  Tiles are walked in grouped order (kGroupM M-blocks share each
+// N-block) so a wave of CTAs reuses A and B from L2.
+//
+// Operand preparation (HBM-bound pre-passes, only where needed): a row-major
+// B[K,N] is transposed into a K-major copy (and, for the zero-point GEMMs, its
+// int32 column sums are accumulated in the same pass); an A whose row pitch is
+// not a multiple of 16 bytes is copied into a padded buffer, because TMA rows
+// must start on 16-byte boundaries.
+//
+// Every mbarrier wait is bounded (tc::mbar_wait); on expiry the kernel raises
+// a CTA-wide abort flag, records the device error word, drains its own
+// outstanding TMA loads and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdio.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include "hx_internal.h"
+#include "requant.cuh"
+#include "tc_common.cuh"
+
+namespace hx {
+namespace {
+
+using tc::MmaKind;
+
+constexpr int kBM = 128;             // rows of A per tile (UMMA M)
+constexpr int kBKBytes = 128;        // K extent of one stage, in bytes
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;
+
+enum EpiKind { kEpiF16 = 0, kEpiRequant = 1 };
+
+struct EpiParams {
+    void *out;
+    int64_t ldo;               // output row pitch, elements
+    int M, N;
+    // requant epilogue (int8 GEMMs):
+    //   acc32  = rawdot - zpA * colsum[j]      (int32 wrap, as the C reference)
+    //   x      = (int64) acc32 + bias[j]
+    //   q      = sat(round_half_away(x * mult_j >> shift_j) + zp, lo, hi)
+    const int32_t *colsum;     // null: no zero-point term
+    int32_t zpA;
+    const int32_t *bias;       // null: no bias
+    const int32_t *mult_pc;    // null: scalar mult / shift
+    const int *shift_pc;
+    int32_t mult;
+    int shift;
+    int zp;
+    int lo, hi;
+};
+
+struct GemmArgs {
+    int tiles_m, tiles_n, num_kb;
+    int *err_word;
+    EpiParams epi;
+};
+
+template <int BN>
+struct Smem {
+    static constexpr int kABytes = kBM * kBKBytes;        // 16 KB
+    static constexpr int kBBytes = BN * kBKBytes;         // 16 or 32 KB
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    // full[S], empty[S], tfull[2], tempty[2], drain
+    static constexpr int kNumBars = 2 * kStages + 5;
+    static constexpr int kTotal = kBarOffset + kNumBars * 8 + 16 + 1024;  // + align slack
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &mb, int &nb) {
+    const int per_group = kGroupM * tiles_n;
+    const int group = t / per_group;
+    const int first_m = group * kGroupM;
+    const int gsize = min(tiles_m - first_m, kGroupM);
+    const int r = t - group * per_group;
+    mb = first_m + r % gsize;
+    nb = r / gsize;
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32_t (&r)[32],
+                                               int row, int col0) {
+    if (row >= ep.M) return;
+    if constexpr (EPI == kEpiF16) {
+        __half *o = reinterpret_cast<__half *>(ep.out) + (size_t)row * ep.ldo + col0;
+        if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
+            uint4 v[4];
+            uint32_t *w = reinterpret_cast<uint32_t *>(v);
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                __half2 h = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                w[i] = *reinterpret_cast<uint32_t *>(&h);
+            }
+            uint4 *dst = reinterpret_cast<uint4 *>(o);
+#pragma unroll
+            for (int i = 0; i < 4; i++) dst[i] = v[i];
+        } else {
+            for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = __float2half_rn(__uint_as_float(r[i]));
+        }
+    } else {
+        uint8_t *o = reinterpret_cast<uint8_t *>(ep.out) + (size_t)row * ep.ldo + col0;
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) w[i] = 0;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const int j = col0 + i;
+            if (j < ep.N) {
+                uint32_t acc = r[i];
+                if (ep.colsum) acc -= (uint32_t)ep.zpA * (uint32_t)__ldg(ep.colsum + j);
+                int64_t x = (int64_t)(int32_t)acc;
+                if (ep.bias) x += __ldg(ep.bias + j);
+                const int32_t m = ep.mult_pc ? __ldg(ep.mult_pc + j) : ep.mult;
+                const int s = ep.shift_pc ? __ldg(ep.shift_pc + j) : ep.shift;
+                int64_t q = rq_round(x * (int64_t)m, s) + ep.zp;
+                q = q > ep.hi ? ep.hi : q;
+                q = q < ep.lo ? ep.lo : q;
+                w[i >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (i & 3));
+            }
+        }
+        if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
+            uint4 *dst = reinterpret_cast<uint4 *>(o);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        } else {
+            for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = (uint8_t)(w[i >> 2] >> (8 * (i & 3)));
+        }
+    }
+}
+
+template <MmaKind KIND, int BN, int EPI, bool A_SIGNED, bool B_SIGNED>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+    using L = Smem<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBarOffset);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + kStages;
+    uint64_t *tfull = bars + 2 * kStages;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_tiles = args.tiles_m * args.tiles_n;
+    constexpr uint32_t kTmemCols = 2 * BN;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            tc::mbar_init(&tfull[b], 1);
+            tc::mbar_init(&tempty[b], 4);   // one arrive per epilogue warp
+        }
+        tc::mbar_init(drain, 1);
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+        tc::tma_prefetch_desc(&tmA);
+        tc::tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0;    // bit s: stage s has a load in flight we may need to drain
+            uint32_t armed_phase = 0;
+            for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+                int mb, nb;
+                tile_coords(t, args.tiles_m, args.tiles_n, mb, nb);
+                for (int kb = 0; kb < args.num_kb; kb++) {
+                    if (!tc::mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.err_word,
+                                       kErrWaitEmpty))
+                        break;
+                    uint8_t *sa = smem + stage * L::kStageBytes;
+                    uint8_t *sb = sa + L::kABytes;
+                    tc::mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+                    const int kx = kb * (KIND == MmaKind::F16 ? kBKBytes / 2 : kBKBytes);
+                    tc::tma_load_2d(sa, &tmA, &full[stage], kx, mb * kBM);
+                    tc::tma_load_2d(sb, &tmB, &full[stage], kx, nb * BN);
+                    armed |= 1u << stage;
+                    armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Drain: every load this thread issued must land before the CTA
+            // exits (normally all were consumed already and this is a no-op).
+            for (int s = 0; s < kStages; s++)
+                if (armed & (1u << s)) {
+                    const uint64_t t0 = tc::globaltimer();
+                    while (!tc::mbar_try_wait(&full[s], (armed_phase >> s) & 1u) &&
+                           tc::globaltimer() - t0 < kWaitBudgetNs) {
+                    }
+                }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer
+            constexpr uint32_t idesc = (KIND == MmaKind::F16)
+                                           ? tc::idesc_f16_f32(kBM, BN)
+                                           : tc::idesc_i8_s32(kBM, BN, A_SIGNED, B_SIGNED);
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool issued = false;
+            for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, local++) {
+                const int buf = local & 1;
+                const uint32_t aphase = (local >> 1) & 1;
+                if (!tc::mbar_wait(&tempty[buf], aphase ^ 1, abort_flag, args.err_word,
+                                   kErrWaitAccum))
+                    break;
+                tc::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+                for (int kb = 0; kb < args.num_kb; kb++) {
+                    if (!tc::mbar_wait(&full[stage], phase, abort_flag, args.err_word,
+                                       kErrWaitFull))
+                        break;
+                    tc::tc_fence_after();
+                    const uint32_t sa = tc::smem_u32(smem + stage * L::kStageBytes);
+                    const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+                    for (int k = 0; k < kBKBytes / 32; k++) {
+                        const uint64_t ad = tc::sdesc_kmajor_sw128(sa + k * 32);
+                        const uint64_t bd = tc::sdesc_kmajor_sw128(sb + k * 32);
+                        tc::mma_ss<KIND>(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    issued = true;
+                    tc::mma_commit(&empty[stage]);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                tc::mma_commit(&tfull[buf]);
+            }
+            // Drain: wait until every MMA issued by this thread has finished.
+            if (issued) {
+                tc::mma_commit(drain);
+                const uint64_t t0 = tc::globaltimer();
+                while (!tc::mbar_try_wait(drain, 0) && tc::globaltimer() - t0 < kWaitBudgetNs) {
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 2..5: TMEM lane quarter = warp % 4
+        const int q = warp & 3;
+        int local = 0;
+        for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, local++) {
+            int mb, nb;
+            tile_coords(t, args.tiles_m, args.tiles_n, mb, nb);
+            const int buf = local & 1;
+            const uint32_t aphase = (local >> 1) & 1;
+            if (!tc::mbar_wait(&tfull[buf], aphase, abort_flag, args.err_word, kErrWaitAccum))
+                break;
+            tc::tc_fence_after();
+            const int row = mb * kBM + q * 32 + lane;
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                uint32_t r[32];
+                tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
+                tc::tmem_ld_wait();
+                epilogue_chunk<EPI>(args.epi, r, row, nb * BN + c);
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&tempty[buf]);
+        }
+    }
+
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tc::tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------- pre-pass kernels
+
+// Bt[n][k] = B[k][n] for k < K, 0 for K <= k < Kp (Kp a multiple of 64);
+// optionally colsum[n] += sum_k B[k][n] (int8 only; colsum pre-zeroed).
+template <typename T, bool COLSUM>
+__global__ void __launch_bounds__(256) transpose_pack_kernel(const T *__restrict__ B,
+                                                              T *__restrict__ Bt,
+                                                              int32_t *__restrict__ colsum, int K,
+                                                              int N, int64_t ldb, int64_t Kp) {
+    __shared__ T tile[64][64 + 4];
+    const int k0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    // load: thread (kr, nc) reads 16 consecutive n of row k
+    {
+        const int kr = threadIdx.x >> 2, nc = (threadIdx.x & 3) * 16;
+        const int k = k0 + kr;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+            const int n = n0 + nc + i;
+            tile[kr][nc + i] = (k < K && n < N) ? B[(size_t)k * ldb + n] : T(0);
+        }
+    }
+    __syncthreads();
+    if (COLSUM && threadIdx.x < 64) {
+        const int n = n0 + threadIdx.x;
+        int32_t s = 0;
+        for (int kr = 0; kr < 64; kr++) s += (int32_t)(int8_t)tile[kr][threadIdx.x];
+        if (n < N) atomicAdd(colsum + n, s);
+    }
+    // store: thread (nr, kc) writes 16 consecutive k of column n
+    {
+        const int nr = threadIdx.x >> 2, kc = (threadIdx.x & 3) * 16;
+        const int n = n0 + nr;
+        if (n < N && k0 + kc < Kp) {
+            T v[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) v[i] = tile[kc + i][nr];
+            uint4 *dst = reinterpret_cast<uint4 *>(Bt + (size_t)n * Kp + k0 + kc);
+            const uint4 *src = reinterpret_cast<const uint4 *>(v);
+#pragma unroll
+            for (int i = 0; i < (int)(16 * sizeof(T) / 16); i++) dst[i] = src[i];
+        }
+    }
+}
+
+// dst[r][k] = src[r][k] for k < K, 0 for K <= k < ldd (never reads src when
+// K == 0).
+template <typename T>
+__global__ void __launch_bounds__(256) pad_rows_kernel(const T *__restrict__ src, int64_t lds,
+                                                        T *__restrict__ dst, int64_t ldd, int rows,
+                                                        int K) {
+    const int64_t total = (int64_t)rows * ldd;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / ldd, k = i % ldd;
+        dst[i] = k < K ? src[r * lds + k] : T(0);
+    }
+}
+
+// ------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// 2D K-major operand map: rows x K elements, row pitch `pitch_bytes`, box
+// 128 bytes of K x box_rows rows, 128-byte swizzle, zero fill out of bounds.
+int make_kmajor_map(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int esize,
+                    int64_t K, int64_t rows, int64_t pitch_bytes, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(HEXCUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)pitch_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)(kBKBytes / esize), (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(HEXCUDA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): K=%lld rows=%lld pitch=%lld",
+                    (int)r, (long long)K, (long long)rows, (long long)pitch_bytes);
+    return HEXCUDA_OK;
+}
+
+inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+template <MmaKind KIND, int BN, int EPI, bool AS, bool BS>
+int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K,
+                       const EpiParams &ep) {
+    using L = Smem<BN>;
+    auto kern = gemm_tc_kernel<KIND, BN, EPI, AS, BS>;
+    static bool attr_done[64] = {};
+    const int dev_slot = d->ordinal & 63;
+    if (!attr_done[dev_slot]) {
+        if (int rc = check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                L::kTotal),
+                           "cudaFuncSetAttribute(gemm smem)"))
+            return rc;
+        attr_done[dev_slot] = true;
+    }
+    GemmArgs args;
+    args.tiles_m = (M + kBM - 1) / kBM;
+    args.tiles_n = (N + BN - 1) / BN;
+    const int kelems = KIND == MmaKind::F16 ? kBKBytes / 2 : kBKBytes;
+    args.num_kb = (K + kelems - 1) / kelems;
+    args.err_word = d->err_word;
+    args.epi = ep;
+    int tiles = args.tiles_m * args.tiles_n;
+    int grid = tiles < d->sms ? tiles : d->sms;
+    kern<<<grid, kThreads, L::kTotal, d->stream>>>(ta, tb, args);
+    return HEXCUDA_OK;
+}
+
+// Common driver: A [M,K] K-major (pitch lda elements), B given either as
+// Bt [N,K] K-major (b_kmajor) or as row-major B [K,N] (transposed here).
+// Operands whose rows are not 16-byte aligned, or shorter than one 128-byte
+// K block, are copied into zero-padded [rows, Kp] buffers (Kp * esize a
+// multiple of 128 bytes); TMA zero-fills every other out-of-range element.
+template <MmaKind KIND, int EPI, bool AS, bool BS>
+int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, int M, int N,
+             int K, EpiParams ep, bool want_colsum, const char *name) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "%s: bad shape %dx%dx%d", name, M, N, K);
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if ((K > 0 && (!A || !B)) || !ep.out) return fail(HEXCUDA_ERR_ARG, "%s: null pointer", name);
+    if (want_colsum && b_kmajor)
+        return fail(HEXCUDA_ERR_ARG, "%s: column sums need a row-major B", name);
+    constexpr int esize = KIND == MmaKind::F16 ? 2 : 1;
+    constexpr int kelems = kBKBytes / esize;
+    constexpr CUtensorMapDataType dt =
+        KIND == MmaKind::F16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    using T = typename std::conditional<KIND == MmaKind::F16, uint16_t, uint8_t>::type;
+    const int64_t Kp = round_up(K > 0 ? K : 1, kelems);
+    const bool short_k = K < kelems;
+
+    launch_begin(d);
+    int nl = 0;
+    // ---- B operand
+    const T *bt = reinterpret_cast<const T *>(B);
+    int64_t bt_pitch = (int64_t)K * esize, b_kdim = K;
+    int32_t *colsum = nullptr;
+    if (want_colsum) {
+        colsum = reinterpret_cast<int32_t *>(scratch(d, 1, sizeof(int32_t) * (size_t)N));
+        if (!colsum) return HEXCUDA_ERR_OOM;
+        if (int rc = check(cudaMemsetAsync(colsum, 0, sizeof(int32_t) * (size_t)N, d->stream),
+                           "memset colsum"))
+            return rc;
+    }
+    if (!b_kmajor) {
+        T *tmp = reinterpret_cast<T *>(scratch(d, 0, (size_t)N * Kp * esize));
+        if (!tmp) return HEXCUDA_ERR_OOM;
+        dim3 g((unsigned)((N + 63) / 64), (unsigned)(Kp / 64));
+        if (want_colsum)
+            transpose_pack_kernel<T, true><<<g, 256, 0, d->stream>>>(
+                reinterpret_cast<const T *>(B), tmp, colsum, K, N, N, Kp);
+        else
+            transpose_pack_kernel<T, false><<<g, 256, 0, d->stream>>>(
+                reinterpret_cast<const T *>(B), tmp, nullptr, K, N, N, Kp);
+        nl++;
+        bt = tmp;
+        bt_pitch = Kp * esize;
+        b_kdim = Kp;
+    } else if ((bt_pitch % 16) != 0 || !aligned16(B) || short_k) {
+        T *tmp = reinterpret_cast<T *>(scratch(d, 0, (size_t)N * Kp * esize));
+        if (!tmp) return HEXCUDA_ERR_OOM;
+        pad_rows_kernel<T><<<(unsigned)std::min<int64_t>((N * Kp + 255) / 256, 4096), 256, 0,
+                             d->stream>>>(reinterpret_cast<const T *>(B), K, tmp, Kp, N, K);
+        nl++;
+        bt = tmp;
+        bt_pitch = Kp * esize;
+        b_kdim = Kp;
+    }
+    // ---- A operand
+    const T *a = reinterpret_cast<const T *>(A);
+    int64_t a_pitch = lda * esize, a_kdim = K;
+    if ((a_pitch % 16) != 0 || !aligned16(A) || short_k) {
+        T *tmp = reinterpret_cast<T *>(scratch(d, 2, (size_t)M * Kp * esize));
+        if (!tmp) return HEXCUDA_ERR_OOM;
+        pad_rows_kernel<T><<<(unsigned)std::min<int64_t>((M * Kp + 255) / 256, 4096), 256, 0,
+                             d->stream>>>(reinterpret_cast<const T *>(A), lda, tmp, Kp, M, K);
+        nl++;
+        a = tmp;
+        a_pitch = Kp * esize;
+        a_kdim = Kp;
+    }
+    CUtensorMap ta, tb;
+    if (int rc = make_kmajor_map(&ta, a, dt, esize, a_kdim, M, a_pitch, kBM)) return rc;
+    ep.colsum = colsum;
+    ep.M = M;
+    ep.N = N;
+    const int kdim = (int)std::max(a_kdim, b_kdim);
+    int rc;
+    if (N <= 128) {
+        if ((rc = make_kmajor_map(&tb, bt, dt, esize, b_kdim, N, bt_pitch, 128))) return rc;
+        rc = launch_gemm_kernel<KIND, 128, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep);
+    } else {
+        if ((rc = make_kmajor_map(&tb, bt, dt, esize, b_kdim, N, bt_pitch, 256))) return rc;
+        rc = launch_gemm_kernel<KIND, 256, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep);
+    }
+    if (rc) return rc;
+    return launch_end(d, name, nl + 1);
+}
+
+EpiParams requant_epi(void *out, int N, int32_t mult, int shift, int zp, int lo, int hi) {
+    EpiParams ep{};
+    ep.out = out;
+    ep.ldo = N;
+    ep.mult = mult;
+    ep.shift = shift;
+    ep.zp = zp;
+    ep.lo = lo;
+    ep.hi = hi;
+    return ep;
+}
+
+}  // namespace
+}  // namespace hx
+
+using namespace hx;
+
+HX_EXPORT int hexcuda_gemm_f16_nt(int dev, const uint16_t *A, const uint16_t *Bt, uint16_t *out,
+                                  int M, int N, int K) {
+    EpiParams ep{};
+    ep.out = out;
+    ep.ldo = N;
+    return run_gemm<MmaKind::F16, kEpiF16, false, false>(dev, A, K, Bt, true, M, N, K, ep, false,
+                                                         "gemm_f16_nt");
+}
+
+HX_EXPORT int hexcuda_gemm_f16_nn(int dev, const uint16_t *A, const uint16_t *B, uint16_t *out,
+                                  int M, int N, int K) {
+    EpiParams ep{};
+    ep.out = out;
+    ep.ldo = N;
+    return run_gemm<MmaKind::F16, kEpiF16, false, false>(dev, A, K, B, false, M, N, K, ep, false,
+                                                         "gemm_f16_nn");
+}
+
+HX_EXPORT int hexcuda_gemm_i8_requant(int dev, const int8_t *A, const int8_t *B, int8_t *out,
+                                      int M, int N, int K, int32_t mult, int shift, int8_t zp) {
+    if (shift < 0 || shift > 63) return fail(HEXCUDA_ERR_ARG, "gemm_i8_requant: shift %d", shift);
+    EpiParams ep = requant_epi(out, N, mult, shift, zp, -128, 127);
+    return run_gemm<MmaKind::I8, kEpiRequant, true, true>(dev, A, K, B, false, M, N, K, ep, false,
+                                                          "gemm_i8_requant");
+}
+
+HX_EXPORT int hexcuda_gemm_i8_bias_requant(int dev, const int8_t *A, const int8_t *B,
+                                           const int32_t *bias, int8_t *out, int M, int N, int K,
+                                           int32_t mult, int shift, int8_t zp) {
+    if (shift < 0 || shift > 63)
+        return fail(HEXCUDA_ERR_ARG, "gemm_i8_bias_requant: shift %d", shift);
+    if (!bias && N > 0) return fail(HEXCUDA_ERR_ARG, "gemm_i8_bias_requant: null bias");
+    EpiParams ep = requant_epi(out, N, mult, shift, zp, -128, 127);
+    ep.bias = bias;
+    return run_gemm<MmaKind::I8, kEpiRequant, true, true>(dev, A, K, B, false, M, N, K, ep, false,
+                                                          "gemm_i8_bias_requant");
+}
+
+HX_EXPORT int hexcuda_gemm_i8_zp(int dev, const int8_t *A, const int8_t *B, int8_t *out, int M,
+                                 int N, int K, int32_t zpA, int32_t scale_mult, int scale_shift) {
+    if (scale_shift < 0 || scale_shift > 63)
+        return fail(HEXCUDA_ERR_ARG, "gemm_i8_zp: shift %d", scale_shift);
+    EpiParams ep = requant_epi(out, N, scale_mult, scale_shift, 0, -128, 127);
+    ep.zpA = zpA;
+    return run_gemm<MmaKind::I8, kEpiRequant, true, true>(dev, A, K, B, false, M, N, K, ep,
+                                                          zpA != 0, "gemm_i8_zp");
+}
+
+HX_EXPORT int hexcuda_gemm_u8s8_pc(int dev, const uint8_t *A, const int8_t *B, const int32_t *bias,
+                                   uint8_t *out, int M, int N, int K, int32_t zpA,
+                                   const int32_t *mult, const int *shift, uint8_t zp_out) {
+    if ((!bias || !mult || !shift) && N > 0)
+        return fail(HEXCUDA_ERR_ARG, "gemm_u8s8_pc: null bias/mult/shift");
+    EpiParams ep = requant_epi(out, N, 0, 0, zp_out, 0, 255);
+    ep.zpA = zpA;
+    ep.bias = bias;
+    ep.mult_pc = mult;
+    ep.shift_pc = shift;
+    return run_gemm<MmaKind::I8, kEpiRequant, false, true>(dev, A, K, B, false, M, N, K, ep,
+                                                           zpA != 0, "gemm_u8s8_pc");
+}

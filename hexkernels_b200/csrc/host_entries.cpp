@@ -1,0 +1,366 @@
+// host_entries.cpp -- host-pointer entry points (hexcuda_host_*): the calls
+// the candidate_kernel shims make.  Rows are split into contiguous shards,
+// one per initialised device; each shard is copied in on that device's
+// stream, computed, and only after every device finished without error copied
+// back, so a failed call leaves the caller's output untouched.  Per-column /
+// per-feature operands are replicated to every device.
+#include <string.h>
+
+#include <algorithm>
+#include <functional>
+#include <vector>
+
+#include "hx_internal.h"
+
+namespace hx {
+namespace {
+
+// staging slots of the device scratch pool used by the host entries
+enum : int { kSlotIn0 = 8, kSlotIn1, kSlotIn2, kSlotIn3, kSlotIn4, kSlotIn5, kSlotOut };
+
+struct Part {
+    int slot;           // device slot
+    Dev *d;
+    int64_t r0, r1;     // shard of the row range
+    void *dout;         // device output of this shard
+};
+
+template <typename T>
+T *stage_in(Dev *d, int slot, const T *host, size_t count) {
+    T *p = reinterpret_cast<T *>(scratch(d, slot, count * sizeof(T)));
+    if (!p) return nullptr;
+    if (count && check(cudaMemcpyAsync(p, host, count * sizeof(T), cudaMemcpyHostToDevice,
+                                       d->stream),
+                       "h2d"))
+        return nullptr;
+    return p;
+}
+
+// Runs `enqueue(part)` on every shard (it stages inputs, launches and sets
+// part.dout), waits for all devices, then copies each shard's output rows
+// [r0, r1) (out_row_bytes each) back into `host_out`.
+int run_sharded(int64_t rows, void *host_out, size_t out_row_bytes,
+                const std::function<int(Part &)> &enqueue) {
+    if (!ensure_init()) return HEXCUDA_ERR_NODEV;
+    const int n = ndev();
+    std::vector<Part> parts;
+    for (int i = 0; i < n; i++) {
+        int64_t r0 = rows * i / n, r1 = rows * (i + 1) / n;
+        if (r1 > r0) parts.push_back(Part{i, nullptr, r0, r1, nullptr});
+    }
+    if (parts.empty()) return HEXCUDA_OK;
+    scope_begin();
+    int rc = HEXCUDA_OK;
+    for (auto &p : parts) {
+        p.d = get_dev(p.slot);
+        if (!p.d) {
+            rc = HEXCUDA_ERR_NODEV;
+            break;
+        }
+        if ((rc = enqueue(p))) break;
+    }
+    for (auto &p : parts) {
+        if (!p.d) continue;
+        int r = hexcuda_sync(p.slot);
+        if (r && !rc) rc = r;
+    }
+    scope_end();
+    if (rc) return rc;
+    for (auto &p : parts) {
+        size_t bytes = (size_t)(p.r1 - p.r0) * out_row_bytes;
+        if (!bytes) continue;
+        cudaSetDevice(p.d->ordinal);
+        if ((rc = check(cudaMemcpyAsync(reinterpret_cast<uint8_t *>(host_out) + p.r0 * out_row_bytes,
+                                        p.dout, bytes, cudaMemcpyDeviceToHost, p.d->stream),
+                        "d2h")))
+            return rc;
+    }
+    for (auto &p : parts)
+        if (int r = hexcuda_sync(p.slot)) return r;
+    return HEXCUDA_OK;
+}
+
+inline int null_check(const char *name, std::initializer_list<const void *> ptrs) {
+    for (const void *p : ptrs)
+        if (!p) return fail(HEXCUDA_ERR_ARG, "%s: null pointer", name);
+    return HEXCUDA_OK;
+}
+
+}  // namespace
+}  // namespace hx
+
+using namespace hx;
+
+HX_EXPORT int hexcuda_host_softmax_f32(const float *x, float *out, int R, int C) {
+    if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_softmax_f32: R=%d C=%d", R, C);
+    if (int rc = null_check("host_softmax_f32", {x, out})) return rc;
+    return run_sharded(R, out, sizeof(float) * (size_t)C, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const float *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
+        float *dout = reinterpret_cast<float *>(scratch(p.d, kSlotOut, sizeof(float) * nr * C));
+        if (!dx || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_softmax_f32(p.slot, dx, dout, (int)nr, C);
+    });
+}
+
+HX_EXPORT int hexcuda_host_softmax_f16(const uint16_t *x, uint16_t *out, int R, int C) {
+    if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_softmax_f16: R=%d C=%d", R, C);
+    if (int rc = null_check("host_softmax_f16", {x, out})) return rc;
+    return run_sharded(R, out, 2 * (size_t)C, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const uint16_t *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
+        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * nr * C));
+        if (!dx || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_softmax_f16(p.slot, dx, dout, (int)nr, C);
+    });
+}
+
+HX_EXPORT int hexcuda_host_layernorm_f32(const float *x, const float *gamma, const float *beta,
+                                         float *out, int R, int C, float eps) {
+    if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_layernorm_f32: R=%d C=%d", R, C);
+    if (int rc = null_check("host_layernorm_f32", {x, gamma, beta, out})) return rc;
+    return run_sharded(R, out, sizeof(float) * (size_t)C, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const float *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
+        const float *dg = stage_in(p.d, kSlotIn1, gamma, (size_t)C);
+        const float *db = stage_in(p.d, kSlotIn2, beta, (size_t)C);
+        float *dout = reinterpret_cast<float *>(scratch(p.d, kSlotOut, sizeof(float) * nr * C));
+        if (!dx || !dg || !db || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_layernorm_f32(p.slot, dx, dg, db, dout, (int)nr, C, eps);
+    });
+}
+
+HX_EXPORT int hexcuda_host_layernorm_f16(const uint16_t *x, const uint16_t *gamma,
+                                         const uint16_t *beta, uint16_t *out, int R, int C,
+                                         float eps) {
+    if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_layernorm_f16: R=%d C=%d", R, C);
+    if (int rc = null_check("host_layernorm_f16", {x, gamma, beta, out})) return rc;
+    return run_sharded(R, out, 2 * (size_t)C, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const uint16_t *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
+        const uint16_t *dg = stage_in(p.d, kSlotIn1, gamma, (size_t)C);
+        const uint16_t *db = stage_in(p.d, kSlotIn2, beta, (size_t)C);
+        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * nr * C));
+        if (!dx || !dg || !db || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_layernorm_f16(p.slot, dx, dg, db, dout, (int)nr, C, eps);
+    });
+}
+
+HX_EXPORT int hexcuda_host_rmsnorm_f16(const uint16_t *x, const uint16_t *gamma, uint16_t *out,
+                                       int R, int C, float eps) {
+    if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_rmsnorm_f16: R=%d C=%d", R, C);
+    if (int rc = null_check("host_rmsnorm_f16", {x, gamma, out})) return rc;
+    return run_sharded(R, out, 2 * (size_t)C, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const uint16_t *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
+        const uint16_t *dg = stage_in(p.d, kSlotIn1, gamma, (size_t)C);
+        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * nr * C));
+        if (!dx || !dg || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_rmsnorm_f16(p.slot, dx, dg, dout, (int)nr, C, eps);
+    });
+}
+
+HX_EXPORT int hexcuda_host_rowreduce_f32(const float *x, float *out, int R, int C, int op) {
+    if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_rowreduce_f32: R=%d C=%d", R, C);
+    if (int rc = null_check("host_rowreduce_f32", {x, out})) return rc;
+    return run_sharded(R, out, sizeof(float), [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const float *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
+        float *dout = reinterpret_cast<float *>(scratch(p.d, kSlotOut, sizeof(float) * nr));
+        if (!dx || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_rowreduce_f32(p.slot, dx, dout, (int)nr, C, op);
+    });
+}
+
+HX_EXPORT int hexcuda_host_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
+                                               const int32_t *mult, const int *shift, int8_t zp) {
+    if (R < 0 || C < 0) return fail(HEXCUDA_ERR_ARG, "host_requant_per_channel: R=%d C=%d", R, C);
+    if (R == 0 || C == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_requant_per_channel", {a, out, mult, shift})) return rc;
+    return run_sharded(R, out, (size_t)C, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const int32_t *da = stage_in(p.d, kSlotIn0, a + p.r0 * C, (size_t)(nr * C));
+        const int32_t *dm = stage_in(p.d, kSlotIn1, mult + p.r0, (size_t)nr);
+        const int *ds = stage_in(p.d, kSlotIn2, shift + p.r0, (size_t)nr);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * C)));
+        if (!da || !dm || !ds || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_requant_per_channel(p.slot, da, dout, (int)nr, C, dm, ds, zp);
+    });
+}
+
+HX_EXPORT int hexcuda_host_requantize_i32_u8(const int32_t *a, uint8_t *out, int64_t n,
+                                             int32_t mult, int shift, uint8_t zp) {
+    if (n < 0) return fail(HEXCUDA_ERR_ARG, "host_requantize_i32_u8: n=%lld", (long long)n);
+    if (n == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_requantize_i32_u8", {a, out})) return rc;
+    return run_sharded(n, out, 1, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const int32_t *da = stage_in(p.d, kSlotIn0, a + p.r0, (size_t)nr);
+        uint8_t *dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)nr));
+        if (!da || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_requantize_i32_u8(p.slot, da, dout, nr, mult, shift, zp);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out, int M,
+                                           int N, int K, int32_t mult, int shift, int8_t zp) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_i8_requant: bad shape");
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_i8_requant", {A, B, out})) return rc;
+    return run_sharded(M, out, (size_t)N, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const int8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * N)));
+        if (!dA || !dB || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_i8_requant(p.slot, dA, dB, dout, (int)nr, N, K, mult, shift, zp);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gemm_i8_bias_requant(const int8_t *A, const int8_t *B,
+                                                const int32_t *bias, int8_t *out, int M, int N,
+                                                int K, int32_t mult, int shift, int8_t zp) {
+    if (M < 0 || N < 0 || K < 0)
+        return fail(HEXCUDA_ERR_ARG, "host_gemm_i8_bias_requant: bad shape");
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_i8_bias_requant", {A, B, bias, out})) return rc;
+    return run_sharded(M, out, (size_t)N, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const int8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        const int32_t *dbias = stage_in(p.d, kSlotIn2, bias, (size_t)N);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * N)));
+        if (!dA || !dB || !dbias || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_i8_bias_requant(p.slot, dA, dB, dbias, dout, (int)nr, N, K, mult,
+                                            shift, zp);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gemm_i8_zp(const int8_t *A, const int8_t *B, int8_t *out, int M, int N,
+                                      int K, int32_t zpA, int32_t scale_mult, int scale_shift) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_i8_zp: bad shape");
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_i8_zp", {A, B, out})) return rc;
+    return run_sharded(M, out, (size_t)N, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const int8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * N)));
+        if (!dA || !dB || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_i8_zp(p.slot, dA, dB, dout, (int)nr, N, K, zpA, scale_mult,
+                                  scale_shift);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gemm_u8s8_pc(const uint8_t *A, const int8_t *B, const int32_t *bias,
+                                        uint8_t *out, int M, int N, int K, int32_t zpA,
+                                        const int32_t *mult, const int *shift, uint8_t zp_out) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_u8s8_pc: bad shape");
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_u8s8_pc", {A, B, bias, out, mult, shift})) return rc;
+    return run_sharded(M, out, (size_t)N, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const uint8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        const int32_t *dbias = stage_in(p.d, kSlotIn2, bias, (size_t)N);
+        const int32_t *dm = stage_in(p.d, kSlotIn3, mult, (size_t)N);
+        const int *ds = stage_in(p.d, kSlotIn4, shift, (size_t)N);
+        uint8_t *dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * N)));
+        if (!dA || !dB || !dbias || !dm || !ds || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_u8s8_pc(p.slot, dA, dB, dbias, dout, (int)nr, N, K, zpA, dm, ds,
+                                    zp_out);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
+                                       int M, int N, int K) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_f16_nt: bad shape");
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_f16_nt", {A, Bt, out})) return rc;
+    return run_sharded(M, out, 2 * (size_t)N, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const uint16_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const uint16_t *dB = stage_in(p.d, kSlotIn1, Bt, (size_t)N * K);
+        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * (size_t)(nr * N)));
+        if (!dA || !dB || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_f16_nt(p.slot, dA, dB, dout, (int)nr, N, K);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uint16_t *out, int M,
+                                       int N, int K) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_f16_nn: bad shape");
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_f16_nn", {A, B, out})) return rc;
+    return run_sharded(M, out, 2 * (size_t)N, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const uint16_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const uint16_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * (size_t)(nr * N)));
+        if (!dA || !dB || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_f16_nn(p.slot, dA, dB, dout, (int)nr, N, K);
+    });
+}
+
+HX_EXPORT int hexcuda_host_attn_f16(const uint16_t *Q, const uint16_t *K, const uint16_t *V,
+                                    uint16_t *O, int BH, int SQ, int SK, int D, float scale,
+                                    int causal) {
+    if (BH < 0 || SQ < 0 || SK <= 0 || D <= 0)
+        return fail(HEXCUDA_ERR_ARG, "host_attn_f16: BH=%d SQ=%d SK=%d D=%d", BH, SQ, SK, D);
+    if (BH == 0 || SQ == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_attn_f16", {Q, K, V, O})) return rc;
+    const size_t qh = (size_t)SQ * D, kh = (size_t)SK * D;
+    return run_sharded(BH, O, 2 * qh, [&](Part &p) {
+        int64_t nh = p.r1 - p.r0;
+        const uint16_t *dQ = stage_in(p.d, kSlotIn0, Q + p.r0 * qh, nh * qh);
+        const uint16_t *dK = stage_in(p.d, kSlotIn1, K + p.r0 * kh, nh * kh);
+        const uint16_t *dV = stage_in(p.d, kSlotIn2, V + p.r0 * kh, nh * kh);
+        uint16_t *dO = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * nh * qh));
+        if (!dQ || !dK || !dV || !dO) return hexcuda_last_error();
+        p.dout = dO;
+        return hexcuda_attn_f16(p.slot, dQ, dK, dV, dO, (int)nh, SQ, SK, D, scale, causal);
+    });
+}
+
+HX_EXPORT int hexcuda_host_online_softmax_step_f16(const uint16_t *scores, const uint16_t *V,
+                                                   uint16_t *running_max, uint16_t *running_sum,
+                                                   uint16_t *acc, int BLK, int D) {
+    if (BLK <= 0 || D < 0)
+        return fail(HEXCUDA_ERR_ARG, "host_online_softmax_step_f16: BLK=%d D=%d", BLK, D);
+    if (int rc = null_check("host_online_softmax_step_f16", {scores, V, running_max, running_sum}))
+        return rc;
+    if (D > 0 && !acc) return fail(HEXCUDA_ERR_ARG, "host_online_softmax_step_f16: null acc");
+    // state layout on the device: [max, sum, acc[0..D)]
+    std::vector<uint16_t> state((size_t)D + 2);
+    state[0] = *running_max;
+    state[1] = *running_sum;
+    std::copy(acc, acc + D, state.begin() + 2);
+    std::vector<uint16_t> result(state.size());
+    int rc = run_sharded(1, result.data(), 2 * state.size(), [&](Part &p) {
+        const uint16_t *ds = stage_in(p.d, kSlotIn0, scores, (size_t)BLK);
+        const uint16_t *dv = stage_in(p.d, kSlotIn1, V, (size_t)BLK * D);
+        uint16_t *dst = stage_in(p.d, kSlotOut, state.data(), state.size());
+        if (!ds || !dv || !dst) return hexcuda_last_error();
+        p.dout = dst;
+        return hexcuda_online_softmax_step_f16(p.slot, ds, dv, dst, dst + 1, dst + 2, BLK, D);
+    });
+    if (rc) return rc;
+    *running_max = result[0];
+    *running_sum = result[1];
+    std::copy(result.begin() + 2, result.end(), acc);
+    return HEXCUDA_OK;
+}

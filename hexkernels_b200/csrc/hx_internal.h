@@ -1,0 +1,67 @@
+// hx_internal.h -- shared internals of libhexcuda (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "hexcuda.h"
+
+#define HX_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace hx {
+
+constexpr int kScratchSlots = 16;
+
+// Per-device state.  `stream` is where every launcher enqueues work; it is the
+// device's own non-blocking stream unless a caller installed another one.
+struct Dev {
+    int ordinal = -1;
+    int sms = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    bool ev0_recorded = false;          // ev0 marks the start of the timed scope
+    bool timed = false;                 // ev0/ev1 bracket the last launch(es)
+    int *err_word = nullptr;            // device watchdog word (0 = ok)
+    void *slot_ptr[kScratchSlots] = {};
+    size_t slot_bytes[kScratchSlots] = {};
+};
+
+// Device slot -> state; records HEXCUDA_ERR_NODEV and returns null when the
+// slot is invalid.  Makes the device current.
+Dev *get_dev(int slot);
+int ndev();
+bool ensure_init();
+
+// Error recording: prints "HEXCUDA_ERROR <code> <msg>" to stderr once per
+// failure and returns `code`.
+int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int check(cudaError_t e, const char *what);
+
+// Grow-only device buffer owned by libhexcuda, reused across calls.  Slots are
+// assigned by the caller (each call site uses its own slot numbers).
+void *scratch(Dev *d, int slot, size_t bytes);
+
+// Bracket a kernel launch: records the timing events (when enabled) and, after
+// the launch, checks cudaGetLastError and counts the launch.  Inside a scope
+// (a host entry spanning several devices and launches) each device's event
+// pair spans its first to its last launch.
+void scope_begin();
+void scope_end();
+void launch_begin(Dev *d);
+int launch_end(Dev *d, const char *name, int nlaunches = 1);
+
+// Watchdog budget for device-side bounded waits, in nanoseconds of
+// %globaltimer.  A wait that exceeds it sets the device error word.
+constexpr unsigned long long kWaitBudgetNs = 4000000000ull;
+
+// Error word codes set by kernels (bit flags, OR-ed).
+enum : int {
+    kErrWaitFull = 1,      // consumer wait on a filled-stage barrier expired
+    kErrWaitEmpty = 2,     // producer wait on a free-stage barrier expired
+    kErrWaitAccum = 4,     // accumulator hand-off wait expired
+    kErrWaitOther = 8,
+};
+
+}  // namespace hx

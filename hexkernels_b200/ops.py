@@ -1,0 +1,192 @@
+"""NumPy-level operators over libhexcuda's host-pointer entries.
+
+Each function mirrors one corpus task's ``candidate_kernel`` (same argument
+meaning, same result) and runs it on the initialised B200 devices, rows
+sharded across them.  fp16 data is ``numpy.float16``.  Errors raise
+``HexcudaError``; nothing falls back to the CPU.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from ._lib import check, load
+
+
+def _p(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def _c(a, dtype) -> np.ndarray:
+    a = np.ascontiguousarray(a)
+    if a.dtype != np.dtype(dtype):
+        raise TypeError(f"expected {np.dtype(dtype)}, got {a.dtype}")
+    return a
+
+
+def init(ngpus: int = 0) -> int:
+    """Initialise devices 0..ngpus-1 (0 = all); returns the device count."""
+    lib = load()
+    check(lib.hexcuda_init(ngpus))
+    return lib.hexcuda_device_count()
+
+
+def init_devices(devs) -> int:
+    lib = load()
+    arr = (C.c_int * len(devs))(*devs)
+    check(lib.hexcuda_init_devices(arr, len(devs)))
+    return lib.hexcuda_device_count()
+
+
+def last_kernel_ms() -> float:
+    return float(load().hexcuda_last_kernel_ms())
+
+
+# ----------------------------------------------------------- integer family
+
+def gemm_i8_requant(A, B, mult: int, shift: int, zp: int) -> np.ndarray:
+    """i8_gemm_requant: A [M,K] s8, B [K,N] s8 -> [M,N] s8."""
+    A, B = _c(A, np.int8), _c(B, np.int8)
+    (M, K), (K2, N) = A.shape, B.shape
+    assert K == K2
+    out = np.empty((M, N), np.int8)
+    check(load().hexcuda_host_gemm_i8_requant(_p(A), _p(B), _p(out), M, N, K, mult, shift, zp))
+    return out
+
+
+def gemm_i8_bias_requant(A, B, bias, mult: int, shift: int, zp: int) -> np.ndarray:
+    A, B, bias = _c(A, np.int8), _c(B, np.int8), _c(bias, np.int32)
+    (M, K), (K2, N) = A.shape, B.shape
+    assert K == K2 and bias.shape == (N,)
+    out = np.empty((M, N), np.int8)
+    check(load().hexcuda_host_gemm_i8_bias_requant(_p(A), _p(B), _p(bias), _p(out), M, N, K, mult,
+                                                   shift, zp))
+    return out
+
+
+def gemm_i8_zp(A, B, zpA: int, scale_mult: int, scale_shift: int) -> np.ndarray:
+    A, B = _c(A, np.int8), _c(B, np.int8)
+    (M, K), (K2, N) = A.shape, B.shape
+    assert K == K2
+    out = np.empty((M, N), np.int8)
+    check(load().hexcuda_host_gemm_i8_zp(_p(A), _p(B), _p(out), M, N, K, zpA, scale_mult,
+                                         scale_shift))
+    return out
+
+
+def gemm_u8s8_pc(A, B, bias, zpA: int, mult, shift, zp_out: int) -> np.ndarray:
+    A, B = _c(A, np.uint8), _c(B, np.int8)
+    bias, mult, shift = _c(bias, np.int32), _c(mult, np.int32), _c(shift, np.int32)
+    (M, K), (K2, N) = A.shape, B.shape
+    assert K == K2 and bias.shape == mult.shape == shift.shape == (N,)
+    out = np.empty((M, N), np.uint8)
+    check(load().hexcuda_host_gemm_u8s8_pc(_p(A), _p(B), _p(bias), _p(out), M, N, K, zpA,
+                                           _p(mult), _p(shift), zp_out))
+    return out
+
+
+def requant_per_channel(a, mult, shift, zp: int) -> np.ndarray:
+    a, mult, shift = _c(a, np.int32), _c(mult, np.int32), _c(shift, np.int32)
+    R, Cc = a.shape
+    out = np.empty((R, Cc), np.int8)
+    check(load().hexcuda_host_requant_per_channel(_p(a), _p(out), R, Cc, _p(mult), _p(shift), zp))
+    return out
+
+
+def requantize_i32_u8(a, mult: int, shift: int, zp: int) -> np.ndarray:
+    a = _c(a, np.int32)
+    out = np.empty(a.shape, np.uint8)
+    check(load().hexcuda_host_requantize_i32_u8(_p(a), _p(out), a.size, mult, shift, zp))
+    return out
+
+
+# --------------------------------------------------------------- fp16 GEMM
+
+def gemm_f16_nt(A, Bt) -> np.ndarray:
+    """out[M,N] = A[M,K] . Bt[N,K]^T, fp32 accumulate, fp16 out."""
+    A, Bt = _c(A, np.float16), _c(Bt, np.float16)
+    (M, K), (N, K2) = A.shape, Bt.shape
+    assert K == K2
+    out = np.empty((M, N), np.float16)
+    check(load().hexcuda_host_gemm_f16_nt(_p(A), _p(Bt), _p(out), M, N, K))
+    return out
+
+
+def gemm_f16_nn(A, B) -> np.ndarray:
+    A, B = _c(A, np.float16), _c(B, np.float16)
+    (M, K), (K2, N) = A.shape, B.shape
+    assert K == K2
+    out = np.empty((M, N), np.float16)
+    check(load().hexcuda_host_gemm_f16_nn(_p(A), _p(B), _p(out), M, N, K))
+    return out
+
+
+# --------------------------------------------------------------- attention
+
+def attn_f16(Q, K, V, scale: float, causal: bool) -> np.ndarray:
+    """Q [..., SQ, D], K/V [..., SK, D] (leading dims flattened into heads)."""
+    Q, K, V = _c(Q, np.float16), _c(K, np.float16), _c(V, np.float16)
+    SQ, D = Q.shape[-2:]
+    SK = K.shape[-2]
+    BH = int(np.prod(Q.shape[:-2])) if Q.ndim > 2 else 1
+    assert K.shape[-1] == D and V.shape == K.shape
+    O = np.empty(Q.shape, np.float16)
+    check(load().hexcuda_host_attn_f16(_p(Q), _p(K), _p(V), _p(O), BH, SQ, SK, D, scale,
+                                       int(bool(causal))))
+    return O
+
+
+def online_softmax_step_f16(scores, V, running_max, running_sum, acc):
+    """Returns the updated (running_max, running_sum, acc)."""
+    scores, V = _c(scores, np.float16), _c(V, np.float16)
+    acc = np.array(acc, np.float16, copy=True)
+    BLK, D = V.shape
+    m = np.array([running_max], np.float16)
+    s = np.array([running_sum], np.float16)
+    check(load().hexcuda_host_online_softmax_step_f16(_p(scores), _p(V), _p(m), _p(s), _p(acc),
+                                                      BLK, D))
+    return m[0], s[0], acc
+
+
+# ------------------------------------------------------------ row operators
+
+def softmax(x) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    R, Cc = x.reshape(-1, x.shape[-1]).shape
+    out = np.empty_like(x)
+    if x.dtype == np.float32:
+        check(load().hexcuda_host_softmax_f32(_p(x), _p(out), R, Cc))
+    elif x.dtype == np.float16:
+        check(load().hexcuda_host_softmax_f16(_p(x), _p(out), R, Cc))
+    else:
+        raise TypeError(x.dtype)
+    return out
+
+
+def layernorm(x, gamma, beta, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    R, Cc = x.reshape(-1, x.shape[-1]).shape
+    gamma, beta = _c(gamma, x.dtype), _c(beta, x.dtype)
+    out = np.empty_like(x)
+    fn = {np.float32: load().hexcuda_host_layernorm_f32,
+          np.float16: load().hexcuda_host_layernorm_f16}[x.dtype.type]
+    check(fn(_p(x), _p(gamma), _p(beta), _p(out), R, Cc, eps))
+    return out
+
+
+def rmsnorm_f16(x, gamma, eps: float) -> np.ndarray:
+    x, gamma = _c(x, np.float16), _c(gamma, np.float16)
+    R, Cc = x.reshape(-1, x.shape[-1]).shape
+    out = np.empty_like(x)
+    check(load().hexcuda_host_rmsnorm_f16(_p(x), _p(gamma), _p(out), R, Cc, eps))
+    return out
+
+
+def rowreduce(x, op: int) -> np.ndarray:
+    """op 0 = row sum, op 1 = row max; fp32."""
+    x = _c(x, np.float32)
+    R, Cc = x.reshape(-1, x.shape[-1]).shape
+    out = np.empty(R, np.float32)
+    check(load().hexcuda_host_rowreduce_f32(_p(x), _p(out), R, Cc, op))
+    return out

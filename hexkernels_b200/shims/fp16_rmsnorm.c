@@ -1,0 +1,7 @@
+/* candidate_kernel for fp16_rmsnorm on the B200: one row, eps 1e-3. */
+#include "hexcuda.h"
+#include "kernel_api/fp16_rmsnorm.h"
+void candidate_kernel(const hvx_hf *x, const hvx_hf *gamma, hvx_hf *out, int n) {
+    hexcuda_host_rmsnorm_f16((const uint16_t *)x, (const uint16_t *)gamma, (uint16_t *)out, 1, n,
+                             1e-3f);
+}

@@ -1,0 +1,219 @@
+/* hexcuda.h -- C ABI of libhexcuda, the B200 (sm_100a) implementation of the
+ * hexkernels DL-operator hot path.
+ *
+ * The corpus's drop-in boundary is one C function per task,
+ *     void candidate_kernel(...);
+ * declared in each bundle's kernel_api.h and called by that bundle's harness.c
+ * (sriharshapy/hexkernels: README.md:94-95, e.g.
+ * kernels/expert/i8_gemm_requant/kernel_api.h:9-11 and harness.c:55).  The
+ * corpus has no other FFI: its Python tooling (hexkernels/core/evaluate.py:
+ * 554-567) compiles harness.c + the candidate into one program and parses the
+ * HVXENV_* lines it prints.  libhexcuda therefore exports
+ *
+ *   1. runtime calls (device set, allocation, copies, streams, errors, timing)
+ *      that the thin candidate_kernel shims in hexkernels_b200/shims/ use;
+ *   2. one DEVICE-POINTER launcher per operator (asynchronous on the device's
+ *      stream; inputs and outputs already in HBM);
+ *   3. one HOST-POINTER entry per operator (hexcuda_host_*): shards rows over
+ *      the initialised devices, copies in, launches, copies out, synchronises.
+ *      Each candidate_kernel shim is a one-line call of one of these.
+ *
+ * Conventions: plain pointers and sizes only; fp16 data is passed as uint16_t
+ * bit patterns (IEEE binary16, same bits as the corpus's __fp16); row-major
+ * unless stated.  Every entry returns 0 (HEXCUDA_OK) or an error code; on
+ * error the host entries leave the caller's output buffer untouched, print one
+ * "HEXCUDA_ERROR <code> <message>" line to stderr and record the code for
+ * hexcuda_last_error().  Nothing aborts or traps.  Not thread-safe: one caller
+ * thread at a time, like the corpus harnesses.
+ */
+#ifndef HEXCUDA_H
+#define HEXCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HEXCUDA_OK 0
+#define HEXCUDA_ERR_ARG 1         /* bad size, null pointer, unsupported shape */
+#define HEXCUDA_ERR_CUDA 2        /* a CUDA runtime/driver call failed */
+#define HEXCUDA_ERR_NODEV 3       /* no usable sm_100 device / not initialised */
+#define HEXCUDA_ERR_TIMEOUT 4     /* a device-side bounded wait expired */
+#define HEXCUDA_ERR_OOM 5         /* device or pinned allocation failed */
+
+/* ------------------------------------------------------------------ runtime */
+
+/* Initialise on devices 0..ngpus-1 (ngpus <= 0: all visible devices).
+ * Idempotent; a second call with a different set re-initialises. */
+int hexcuda_init(int ngpus);
+/* Initialise on an explicit device list (e.g. one LOCAL_RANK per process). */
+int hexcuda_init_devices(const int *devs, int n);
+void hexcuda_shutdown(void);
+/* Number of initialised devices; the host entries shard rows over them. */
+int hexcuda_device_count(void);
+/* CUDA ordinal of initialised device slot `slot`. */
+int hexcuda_device_ordinal(int slot);
+
+/* All `dev` arguments below are slots 0..hexcuda_device_count()-1. */
+void *hexcuda_alloc(int dev, size_t bytes);
+int hexcuda_free(int dev, void *ptr);
+void *hexcuda_host_alloc(size_t bytes);       /* pinned host memory */
+int hexcuda_host_free(void *ptr);
+int hexcuda_h2d(int dev, void *dst, const void *src, size_t bytes);   /* async */
+int hexcuda_d2h(int dev, void *dst, const void *src, size_t bytes);   /* async */
+int hexcuda_memset(int dev, void *dst, int value, size_t bytes);       /* async */
+/* Waits for the device's stream, then checks the device watchdog word.
+ * dev < 0: every initialised device. */
+int hexcuda_sync(int dev);
+/* The device's launch stream (a cudaStream_t).  Replace it with a caller's
+ * stream, e.g. the one a framework is using (NULL restores the own stream). */
+void *hexcuda_stream(int dev);
+int hexcuda_set_stream(int dev, void *stream);
+
+int hexcuda_last_error(void);
+const char *hexcuda_last_error_string(void);
+/* Record a cudaEvent pair around each launch (default on).  The device time
+ * of the most recent launch (max over devices for a sharded host entry),
+ * in ms, or -1 when timing is off or nothing was launched. */
+int hexcuda_set_timing(int on);
+float hexcuda_last_kernel_ms(void);
+/* Number of kernels libhexcuda has launched since load (all devices). */
+uint64_t hexcuda_launch_count(void);
+
+/* --------------------------------------------- device-pointer launchers */
+
+/* Row softmax over the last axis of an R x C matrix.
+ * kernels/expert/fp16_softmax/kernel_api.h:4-15 (fp32 and fp16 storage). */
+int hexcuda_softmax_f32(int dev, const float *x, float *out, int R, int C);
+int hexcuda_softmax_f16(int dev, const uint16_t *x, uint16_t *out, int R, int C);
+
+/* Per-row layernorm, mean/var by E[x^2] - mean^2 clamped at 0.
+ * kernels/expert/fp16_layernorm/kernel_api.h:4-18 with eps a parameter. */
+int hexcuda_layernorm_f32(int dev, const float *x, const float *gamma,
+                          const float *beta, float *out, int R, int C, float eps);
+int hexcuda_layernorm_f16(int dev, const uint16_t *x, const uint16_t *gamma,
+                          const uint16_t *beta, uint16_t *out, int R, int C,
+                          float eps);
+
+/* Per-row RMS norm.  kernels/expert/fp16_rmsnorm/reference.c:6-17 with eps a
+ * parameter. */
+int hexcuda_rmsnorm_f32(int dev, const float *x, const float *gamma, float *out,
+                        int R, int C, float eps);
+int hexcuda_rmsnorm_f16(int dev, const uint16_t *x, const uint16_t *gamma,
+                        uint16_t *out, int R, int C, float eps);
+
+/* Row sum (op 0) or row max (op 1): out[R].  kernels/mined/fp32_sum/
+ * reference.c:6-17 per row. */
+int hexcuda_rowreduce_f32(int dev, const float *x, float *out, int R, int C, int op);
+
+/* int32 -> int8 per-channel (row) requant.
+ * kernels/expert/requant_per_channel/kernel_api.h:4-11. */
+int hexcuda_requant_per_channel(int dev, const int32_t *a, int8_t *out, int R,
+                                int C, const int32_t *mult, const int *shift,
+                                int8_t zp);
+/* int32 -> uint8 requant.  kernels/expert/requantize_i32_u8_dma/kernel_api.h:4-14. */
+int hexcuda_requantize_i32_u8(int dev, const int32_t *a, uint8_t *out, int64_t n,
+                              int32_t mult, int shift, uint8_t zp);
+
+/* int8 GEMM + requant: A [M,K] s8, B [K,N] s8 row-major, out [M,N] s8.
+ * kernels/expert/i8_gemm_requant/kernel_api.h:4-11. */
+int hexcuda_gemm_i8_requant(int dev, const int8_t *A, const int8_t *B, int8_t *out,
+                            int M, int N, int K, int32_t mult, int shift, int8_t zp);
+/* + per-column int32 bias before the requant.
+ * kernels/expert/i8_gemm_bias_requant/kernel_api.h:4-18. */
+int hexcuda_gemm_i8_bias_requant(int dev, const int8_t *A, const int8_t *B,
+                                 const int32_t *bias, int8_t *out, int M, int N,
+                                 int K, int32_t mult, int shift, int8_t zp);
+/* zero-point decomposition acc = A.B - zpA * colsum(B), no output zp.
+ * kernels/expert/gemm_tile_zp_i8/kernel_api.h:4-28. */
+int hexcuda_gemm_i8_zp(int dev, const int8_t *A, const int8_t *B, int8_t *out,
+                       int M, int N, int K, int32_t zpA, int32_t scale_mult,
+                       int scale_shift);
+/* u8 x s8 asymmetric GEMM, per-output-channel requant to u8:
+ * acc = A.B - zpA * colsum(B); biased = acc + bias[j];
+ * out = sat_u8(round_half_away(biased * mult[j] >> shift[j]) + zp_out).
+ * Composition of gemm_tile_zp_i8/reference.c:10-19, i8_gemm_bias_requant/
+ * reference.c:13, requant_per_channel/reference.c:5-10 and
+ * requantize_i32_u8_dma/reference.c:5-13; candidate_kernel header
+ * include/kernel_api/gemm_u8s8_pc.h. */
+int hexcuda_gemm_u8s8_pc(int dev, const uint8_t *A, const int8_t *B,
+                         const int32_t *bias, uint8_t *out, int M, int N, int K,
+                         int32_t zpA, const int32_t *mult, const int *shift,
+                         uint8_t zp_out);
+
+/* fp16 GEMM, fp32 accumulate, one fp16 rounding: out[M,N] = A[M,K] . Bt[N,K]^T
+ * (B column-major).  kernels/expert/fp16_attention_qkt_hmx/kernel_api.h:4-20. */
+int hexcuda_gemm_f16_nt(int dev, const uint16_t *A, const uint16_t *Bt,
+                        uint16_t *out, int M, int N, int K);
+/* Same with row-major B[K,N].  kernels/expert/hmx_matmul_fp16_deepk/
+ * kernel_api.h:4-10 and fp16_attention_av_hmx/kernel_api.h. */
+int hexcuda_gemm_f16_nn(int dev, const uint16_t *A, const uint16_t *B,
+                        uint16_t *out, int M, int N, int K);
+
+/* fp16 scaled-dot-product attention with fp32 softmax statistics:
+ * O = softmax(scale * Q K^T [+ causal mask j <= i]) V per head.
+ * Q, O: [BH, SQ, D]; K, V: [BH, SK, D].
+ * kernels/expert/fp16_flash_attention_tile/kernel_api.h:4-42 (recurrence
+ * :12-27); candidate_kernel header include/kernel_api/attn_f16.h. */
+int hexcuda_attn_f16(int dev, const uint16_t *Q, const uint16_t *K,
+                     const uint16_t *V, uint16_t *O, int BH, int SQ, int SK,
+                     int D, float scale, int causal);
+
+/* One online-softmax update of a query row's (max, sum, acc) state.
+ * kernels/expert/online_softmax_step_fp16/kernel_api.h:4-33. */
+int hexcuda_online_softmax_step_f16(int dev, const uint16_t *scores,
+                                    const uint16_t *V, uint16_t *running_max,
+                                    uint16_t *running_sum, uint16_t *acc,
+                                    int BLK, int D);
+
+/* ------------------------------------------------- host-pointer entries */
+/* Same operators on HOST buffers (pageable or pinned).  Rows (M, R, or B*H
+ * heads) are split into contiguous shards over the initialised devices;
+ * per-column / per-feature operands are replicated.  Blocking.  If nobody
+ * called hexcuda_init, the first call initialises device 0 only, or devices
+ * 0..HEXCUDA_NGPUS-1 when that environment variable is set. */
+
+int hexcuda_host_softmax_f32(const float *x, float *out, int R, int C);
+int hexcuda_host_softmax_f16(const uint16_t *x, uint16_t *out, int R, int C);
+int hexcuda_host_layernorm_f32(const float *x, const float *gamma, const float *beta,
+                               float *out, int R, int C, float eps);
+int hexcuda_host_layernorm_f16(const uint16_t *x, const uint16_t *gamma,
+                               const uint16_t *beta, uint16_t *out, int R, int C,
+                               float eps);
+int hexcuda_host_rmsnorm_f16(const uint16_t *x, const uint16_t *gamma,
+                             uint16_t *out, int R, int C, float eps);
+int hexcuda_host_rowreduce_f32(const float *x, float *out, int R, int C, int op);
+int hexcuda_host_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
+                                     const int32_t *mult, const int *shift, int8_t zp);
+int hexcuda_host_requantize_i32_u8(const int32_t *a, uint8_t *out, int64_t n,
+                                   int32_t mult, int shift, uint8_t zp);
+int hexcuda_host_gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out,
+                                 int M, int N, int K, int32_t mult, int shift,
+                                 int8_t zp);
+int hexcuda_host_gemm_i8_bias_requant(const int8_t *A, const int8_t *B,
+                                      const int32_t *bias, int8_t *out, int M,
+                                      int N, int K, int32_t mult, int shift,
+                                      int8_t zp);
+int hexcuda_host_gemm_i8_zp(const int8_t *A, const int8_t *B, int8_t *out, int M,
+                            int N, int K, int32_t zpA, int32_t scale_mult,
+                            int scale_shift);
+int hexcuda_host_gemm_u8s8_pc(const uint8_t *A, const int8_t *B, const int32_t *bias,
+                              uint8_t *out, int M, int N, int K, int32_t zpA,
+                              const int32_t *mult, const int *shift, uint8_t zp_out);
+int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
+                             int M, int N, int K);
+int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uint16_t *out,
+                             int M, int N, int K);
+int hexcuda_host_attn_f16(const uint16_t *Q, const uint16_t *K, const uint16_t *V,
+                          uint16_t *O, int BH, int SQ, int SK, int D, float scale,
+                          int causal);
+int hexcuda_host_online_softmax_step_f16(const uint16_t *scores, const uint16_t *V,
+                                         uint16_t *running_max, uint16_t *running_sum,
+                                         uint16_t *acc, int BLK, int D);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HEXCUDA_H */

@@ -1,0 +1,547 @@
+/* hexoracle.c -- CPU oracle for the hot-path operators (TEST INFRASTRUCTURE).
+ *
+ * The checker for the CUDA path, never the product.  Each function restates
+ * one scalar reference.c of sriharshapy/hexkernels (cited per function) with
+ * the same arithmetic, accumulation order and rounding.  Parity of this file
+ * with the reference itself is pinned by the golden vectors in tests/golden/,
+ * produced by the reference's own reference.c files (see oracle/Makefile).
+ */
+#include "hexoracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+
+static inline float h2f(uint16_t b) {
+    _Float16 h;
+    memcpy(&h, &b, 2);
+    return (float)h;
+}
+static inline uint16_t f2h(float f) {
+    _Float16 h = (_Float16)f;
+    uint16_t b;
+    memcpy(&b, &h, 2);
+    return b;
+}
+
+/* Round-half-away-from-zero fixed-point requant shared by every integer
+ * reference: i8_gemm_requant/reference.c:11-13,
+ * requant_per_channel/reference.c:7-10, requantize_i32_u8_dma/reference.c:6-8. */
+static inline int64_t rq_round(int64_t v, int shift) {
+    int64_t half = shift > 0 ? ((int64_t)1 << (shift - 1)) : 0;
+    return (v >= 0) ? ((v + half) >> shift) : -(((-v) + half) >> shift);
+}
+static inline int8_t sat_i8(int64_t r) {
+    if (r > 127) r = 127;
+    if (r < -128) r = -128;
+    return (int8_t)r;
+}
+static inline uint8_t sat_u8(int64_t r) {
+    if (r > 255) r = 255;
+    if (r < 0) r = 0;
+    return (uint8_t)r;
+}
+
+/* The integer GEMMs accumulate with the k loop outermost over a row of int32
+ * partial sums.  Integer addition is associative, so this is bit-identical to
+ * the reference's j-outer / k-inner order while letting gcc vectorise. */
+
+/* kernels/expert/i8_gemm_requant/reference.c:5-19 */
+void oracle_i8_gemm_requant_rows(const int8_t *A, const int8_t *B, int8_t *out,
+                                 int M, int N, int K, int32_t mult, int shift,
+                                 int8_t zp, int r0, int r1) {
+    (void)M;
+    int32_t *acc = (int32_t *)malloc(sizeof(int32_t) * (size_t)N);
+    for (int i = r0; i < r1; i++) {
+        memset(acc, 0, sizeof(int32_t) * (size_t)N);
+        for (int k = 0; k < K; k++) {
+            int32_t a = A[(size_t)i * K + k];
+            const int8_t *b = B + (size_t)k * N;
+            for (int j = 0; j < N; j++) acc[j] += a * (int32_t)b[j];
+        }
+        for (int j = 0; j < N; j++) {
+            int64_t v = (int64_t)acc[j] * (int64_t)mult;
+            int64_t r = rq_round(v, shift) + zp;
+            out[(size_t)i * N + j] = sat_i8(r);
+        }
+    }
+    free(acc);
+}
+
+/* kernels/expert/i8_gemm_bias_requant/reference.c:6-22 */
+void oracle_i8_gemm_bias_requant_rows(const int8_t *A, const int8_t *B,
+                                      const int32_t *bias, int8_t *out,
+                                      int M, int N, int K, int32_t mult,
+                                      int shift, int8_t zp, int r0, int r1) {
+    (void)M;
+    int32_t *acc = (int32_t *)malloc(sizeof(int32_t) * (size_t)N);
+    for (int i = r0; i < r1; i++) {
+        memset(acc, 0, sizeof(int32_t) * (size_t)N);
+        for (int k = 0; k < K; k++) {
+            int32_t a = A[(size_t)i * K + k];
+            const int8_t *b = B + (size_t)k * N;
+            for (int j = 0; j < N; j++) acc[j] += a * (int32_t)b[j];
+        }
+        for (int j = 0; j < N; j++) {
+            int64_t biased = (int64_t)acc[j] + (int64_t)bias[j];
+            int64_t v = biased * (int64_t)mult;
+            out[(size_t)i * N + j] = sat_i8(rq_round(v, shift) + zp);
+        }
+    }
+    free(acc);
+}
+
+/* kernels/expert/gemm_tile_zp_i8/reference.c:10-29.  colsum and the
+ * zpA * colsum product are int32 exactly as the reference computes them
+ * (two's-complement wrap where the C would overflow). */
+void oracle_gemm_tile_zp_i8_rows(const int8_t *A, const int8_t *B, int8_t *out,
+                                 int M, int N, int K, int32_t zpA,
+                                 int32_t scale_mult, int scale_shift,
+                                 int r0, int r1) {
+    (void)M;
+    int32_t *colsum = (int32_t *)calloc((size_t)N, sizeof(int32_t));
+    int32_t *acc = (int32_t *)malloc(sizeof(int32_t) * (size_t)N);
+    for (int k = 0; k < K; k++)
+        for (int j = 0; j < N; j++) colsum[j] += (int32_t)B[(size_t)k * N + j];
+    for (int i = r0; i < r1; i++) {
+        memset(acc, 0, sizeof(int32_t) * (size_t)N);
+        for (int k = 0; k < K; k++) {
+            int32_t a = A[(size_t)i * K + k];
+            const int8_t *b = B + (size_t)k * N;
+            for (int j = 0; j < N; j++) acc[j] += a * (int32_t)b[j];
+        }
+        for (int j = 0; j < N; j++) {
+            int32_t zc = (int32_t)((uint32_t)zpA * (uint32_t)colsum[j]);
+            int32_t a32 = (int32_t)((uint32_t)acc[j] - (uint32_t)zc);
+            int64_t r = (int64_t)a32 * (int64_t)scale_mult;
+            out[(size_t)i * N + j] = sat_i8(rq_round(r, scale_shift));
+        }
+    }
+    free(acc);
+    free(colsum);
+}
+
+/* Composed u8 x s8 per-channel GEMM (see header for the four cited lines). */
+void oracle_gemm_u8s8_pc_rows(const uint8_t *A, const int8_t *B,
+                              const int32_t *bias, uint8_t *out,
+                              int M, int N, int K, int32_t zpA,
+                              const int32_t *mult, const int *shift,
+                              uint8_t zp_out, int r0, int r1) {
+    (void)M;
+    int32_t *colsum = (int32_t *)calloc((size_t)N, sizeof(int32_t));
+    int32_t *acc = (int32_t *)malloc(sizeof(int32_t) * (size_t)N);
+    for (int k = 0; k < K; k++)
+        for (int j = 0; j < N; j++) colsum[j] += (int32_t)B[(size_t)k * N + j];
+    for (int i = r0; i < r1; i++) {
+        memset(acc, 0, sizeof(int32_t) * (size_t)N);
+        for (int k = 0; k < K; k++) {
+            int32_t a = A[(size_t)i * K + k];
+            const int8_t *b = B + (size_t)k * N;
+            for (int j = 0; j < N; j++) acc[j] += a * (int32_t)b[j];
+        }
+        for (int j = 0; j < N; j++) {
+            int32_t zc = (int32_t)((uint32_t)zpA * (uint32_t)colsum[j]);
+            int32_t a32 = (int32_t)((uint32_t)acc[j] - (uint32_t)zc);
+            int64_t biased = (int64_t)a32 + (int64_t)bias[j];
+            int64_t v = biased * (int64_t)mult[j];
+            int64_t r = rq_round(v, shift[j]) + (int64_t)zp_out;
+            out[(size_t)i * N + j] = sat_u8(r);
+        }
+    }
+    free(acc);
+    free(colsum);
+}
+
+/* kernels/expert/requant_per_channel/reference.c:4-16 */
+void oracle_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
+                                const int32_t *mult, const int *shift, int8_t zp) {
+    for (int r = 0; r < R; r++) {
+        int32_t m = mult[r];
+        int s = shift[r];
+        for (int c = 0; c < C; c++) {
+            int64_t v = (int64_t)a[(size_t)r * C + c] * (int64_t)m;
+            out[(size_t)r * C + c] = sat_i8(rq_round(v, s) + zp);
+        }
+    }
+}
+
+/* kernels/expert/requantize_i32_u8_dma/reference.c:5-18 */
+void oracle_requantize_i32_u8(const int32_t *a, uint8_t *out, int64_t n,
+                              int32_t mult, int shift, uint8_t zp) {
+    for (int64_t i = 0; i < n; i++) {
+        int64_t v = (int64_t)a[i] * (int64_t)mult;
+        out[i] = sat_u8(rq_round(v, shift) + (int64_t)(uint64_t)zp);
+    }
+}
+
+/* kernels/expert/fp16_attention_qkt_hmx/reference.c:8-14, M x N x K.
+ * Each output keeps the reference's sequential d-order fp32 sum; the j loop
+ * is innermost over a row of partial sums so it vectorises without changing
+ * any element's summation order. */
+void oracle_gemm_f16_nt_rows(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
+                             int M, int N, int K, int r0, int r1) {
+    (void)M;
+    float *arow = (float *)malloc(sizeof(float) * (size_t)K);
+    float *acc = (float *)malloc(sizeof(float) * (size_t)N);
+    float *bcol = (float *)malloc(sizeof(float) * (size_t)N * 64);
+    for (int i = r0; i < r1; i++) {
+        for (int d = 0; d < K; d++) arow[d] = h2f(A[(size_t)i * K + d]);
+        memset(acc, 0, sizeof(float) * (size_t)N);
+        for (int d0 = 0; d0 < K; d0 += 64) {
+            int dn = K - d0 < 64 ? K - d0 : 64;
+            for (int j = 0; j < N; j++)
+                for (int dd = 0; dd < dn; dd++)
+                    bcol[(size_t)dd * N + j] = h2f(Bt[(size_t)j * K + d0 + dd]);
+            for (int dd = 0; dd < dn; dd++) {
+                float a = arow[d0 + dd];
+                const float *b = bcol + (size_t)dd * N;
+                for (int j = 0; j < N; j++) acc[j] += a * b[j];
+            }
+        }
+        for (int j = 0; j < N; j++) out[(size_t)i * N + j] = f2h(acc[j]);
+    }
+    free(bcol);
+    free(acc);
+    free(arow);
+}
+
+/* kernels/expert/hmx_matmul_fp16_deepk/reference.c:20-26, M x N x K */
+void oracle_gemm_f16_nn_rows(const uint16_t *A, const uint16_t *B, uint16_t *out,
+                             int M, int N, int K, int r0, int r1) {
+    (void)M;
+    float *acc = (float *)malloc(sizeof(float) * (size_t)N);
+    for (int i = r0; i < r1; i++) {
+        memset(acc, 0, sizeof(float) * (size_t)N);
+        for (int k = 0; k < K; k++) {
+            float a = h2f(A[(size_t)i * K + k]);
+            const uint16_t *b = B + (size_t)k * N;
+            for (int j = 0; j < N; j++) acc[j] += a * h2f(b[j]);
+        }
+        for (int j = 0; j < N; j++) out[(size_t)i * N + j] = f2h(acc[j]);
+    }
+    free(acc);
+}
+
+/* kernels/expert/fp16_flash_attention_tile/reference.c:11-27 for one head:
+ * scores in d order, running row max seeded at -1e30f, expf, sequential row
+ * sum, then per d the sequential sum over j of e[j]*V[j,d], divided once. */
+void oracle_attn_f16_head_rows(const uint16_t *Q, const uint16_t *K,
+                               const uint16_t *V, uint16_t *O, int SK, int D,
+                               float scale, int causal, int q0, int q1) {
+    float *sc = (float *)malloc(sizeof(float) * (size_t)(SK > 0 ? SK : 1));
+    float *qrow = (float *)malloc(sizeof(float) * (size_t)D);
+    float *acc = (float *)malloc(sizeof(float) * (size_t)D);
+    for (int i = q0; i < q1; i++) {
+        int nk = (causal && i + 1 < SK) ? i + 1 : SK;
+        for (int d = 0; d < D; d++) qrow[d] = h2f(Q[(size_t)i * D + d]);
+        float rowmax = -1e30f;
+        for (int j = 0; j < nk; j++) {
+            float a = 0.0f;
+            const uint16_t *kr = K + (size_t)j * D;
+            for (int d = 0; d < D; d++) a += qrow[d] * h2f(kr[d]);
+            sc[j] = a * scale;
+            if (sc[j] > rowmax) rowmax = sc[j];
+        }
+        float rowsum = 0.0f;
+        for (int j = 0; j < nk; j++) {
+            sc[j] = expf(sc[j] - rowmax);
+            rowsum += sc[j];
+        }
+        /* acc[d] = sum_j e[j] * V[j,d] in j order for every d (same order as
+         * the reference's d-outer / j-inner loop, vectorised over d). */
+        for (int d = 0; d < D; d++) acc[d] = 0.0f;
+        for (int j = 0; j < nk; j++) {
+            float e = sc[j];
+            const uint16_t *vr = V + (size_t)j * D;
+            for (int d = 0; d < D; d++) acc[d] += e * h2f(vr[d]);
+        }
+        for (int d = 0; d < D; d++) O[(size_t)i * D + d] = f2h(acc[d] / rowsum);
+    }
+    free(acc);
+    free(qrow);
+    free(sc);
+}
+
+void oracle_attn_f16_heads(const uint16_t *Q, const uint16_t *K,
+                           const uint16_t *V, uint16_t *O, int BH, int SQ,
+                           int SK, int D, float scale, int causal, int h0,
+                           int h1) {
+    (void)BH;
+    size_t qs = (size_t)SQ * D, ks = (size_t)SK * D;
+    for (int h = h0; h < h1; h++)
+        oracle_attn_f16_head_rows(Q + h * qs, K + h * ks, V + h * ks, O + h * qs,
+                                  SK, D, scale, causal, 0, SQ);
+}
+
+/* kernels/expert/online_softmax_step_fp16/reference.c:9-37 */
+void oracle_online_softmax_step_f16(const uint16_t *scores, const uint16_t *V,
+                                    uint16_t *running_max, uint16_t *running_sum,
+                                    uint16_t *acc, int BLK, int D) {
+    float m_old = h2f(*running_max);
+    float l_old = h2f(*running_sum);
+    float m_blk = h2f(scores[0]);
+    for (int j = 1; j < BLK; j++) {
+        float v = h2f(scores[j]);
+        if (v > m_blk) m_blk = v;
+    }
+    float m_new = (m_old > m_blk) ? m_old : m_blk;
+    float corr = expf(m_old - m_new);
+    float *p = (float *)malloc(sizeof(float) * (size_t)(BLK > 0 ? BLK : 1));
+    float psum = 0.0f;
+    for (int j = 0; j < BLK; j++) {
+        p[j] = expf(h2f(scores[j]) - m_new);
+        psum += p[j];
+    }
+    float l_new = l_old * corr + psum;
+    for (int d = 0; d < D; d++) {
+        float a = h2f(acc[d]) * corr;
+        for (int j = 0; j < BLK; j++) a += p[j] * h2f(V[(size_t)j * D + d]);
+        acc[d] = f2h(a);
+    }
+    *running_max = f2h(m_new);
+    *running_sum = f2h(l_new);
+    free(p);
+}
+
+/* kernels/expert/fp16_softmax/reference.c:9-28, fp32 storage */
+void oracle_softmax_f32_rows(const float *x, float *out, int R, int C,
+                             int r0, int r1) {
+    (void)R;
+    for (int r = r0; r < r1; r++) {
+        const float *xr = x + (size_t)r * C;
+        float *outr = out + (size_t)r * C;
+        float rowmax = xr[0];
+        for (int j = 1; j < C; j++)
+            if (xr[j] > rowmax) rowmax = xr[j];
+        float rowsum = 0.0f;
+        for (int j = 0; j < C; j++) {
+            outr[j] = expf(xr[j] - rowmax);
+            rowsum += outr[j];
+        }
+        for (int j = 0; j < C; j++) outr[j] = outr[j] / rowsum;
+    }
+}
+
+/* kernels/expert/fp16_softmax/reference.c:9-28, fp16 storage */
+void oracle_softmax_f16_rows(const uint16_t *x, uint16_t *out, int R, int C,
+                             int r0, int r1) {
+    (void)R;
+    float *e = (float *)malloc(sizeof(float) * (size_t)(C > 0 ? C : 1));
+    for (int r = r0; r < r1; r++) {
+        const uint16_t *xr = x + (size_t)r * C;
+        uint16_t *outr = out + (size_t)r * C;
+        float rowmax = h2f(xr[0]);
+        for (int j = 1; j < C; j++) {
+            float v = h2f(xr[j]);
+            if (v > rowmax) rowmax = v;
+        }
+        float rowsum = 0.0f;
+        for (int j = 0; j < C; j++) {
+            e[j] = expf(h2f(xr[j]) - rowmax);
+            rowsum += e[j];
+        }
+        for (int j = 0; j < C; j++) outr[j] = f2h(e[j] / rowsum);
+    }
+    free(e);
+}
+
+/* kernels/expert/fp16_layernorm/reference.c:9-23 per row, eps parameter */
+void oracle_layernorm_f32_rows(const float *x, const float *gamma,
+                               const float *beta, float *out, int R, int C,
+                               float eps, int r0, int r1) {
+    (void)R;
+    for (int r = r0; r < r1; r++) {
+        const float *xr = x + (size_t)r * C;
+        float *outr = out + (size_t)r * C;
+        float sumx = 0.0f, sumsq = 0.0f;
+        for (int i = 0; i < C; i++) {
+            float v = xr[i];
+            sumx += v;
+            sumsq += v * v;
+        }
+        float mean = sumx / (float)C;
+        float var = sumsq / (float)C - mean * mean;
+        if (var < 0.0f) var = 0.0f;
+        float inv_std = 1.0f / sqrtf(var + eps);
+        for (int i = 0; i < C; i++) {
+            float d = (xr[i] - mean) * inv_std;
+            outr[i] = d * gamma[i] + beta[i];
+        }
+    }
+}
+
+void oracle_layernorm_f16_rows(const uint16_t *x, const uint16_t *gamma,
+                               const uint16_t *beta, uint16_t *out, int R,
+                               int C, float eps, int r0, int r1) {
+    (void)R;
+    for (int r = r0; r < r1; r++) {
+        const uint16_t *xr = x + (size_t)r * C;
+        uint16_t *outr = out + (size_t)r * C;
+        float sumx = 0.0f, sumsq = 0.0f;
+        for (int i = 0; i < C; i++) {
+            float v = h2f(xr[i]);
+            sumx += v;
+            sumsq += v * v;
+        }
+        float mean = sumx / (float)C;
+        float var = sumsq / (float)C - mean * mean;
+        if (var < 0.0f) var = 0.0f;
+        float inv_std = 1.0f / sqrtf(var + eps);
+        for (int i = 0; i < C; i++) {
+            float d = (h2f(xr[i]) - mean) * inv_std;
+            outr[i] = f2h(d * h2f(gamma[i]) + h2f(beta[i]));
+        }
+    }
+}
+
+/* kernels/expert/fp16_rmsnorm/reference.c:7-17 per row, eps parameter */
+void oracle_rmsnorm_f32_rows(const float *x, const float *gamma, float *out,
+                             int R, int C, float eps, int r0, int r1) {
+    (void)R;
+    for (int r = r0; r < r1; r++) {
+        const float *xr = x + (size_t)r * C;
+        float *outr = out + (size_t)r * C;
+        float sumsq = 0.0f;
+        for (int i = 0; i < C; i++) sumsq += xr[i] * xr[i];
+        float ms = sumsq / (float)C;
+        float inv_rms = 1.0f / sqrtf(ms + eps);
+        for (int i = 0; i < C; i++) outr[i] = xr[i] * inv_rms * gamma[i];
+    }
+}
+
+void oracle_rmsnorm_f16_rows(const uint16_t *x, const uint16_t *gamma,
+                             uint16_t *out, int R, int C, float eps, int r0,
+                             int r1) {
+    (void)R;
+    for (int r = r0; r < r1; r++) {
+        const uint16_t *xr = x + (size_t)r * C;
+        uint16_t *outr = out + (size_t)r * C;
+        float sumsq = 0.0f;
+        for (int i = 0; i < C; i++) {
+            float v = h2f(xr[i]);
+            sumsq += v * v;
+        }
+        float ms = sumsq / (float)C;
+        float inv_rms = 1.0f / sqrtf(ms + eps);
+        for (int i = 0; i < C; i++)
+            outr[i] = f2h(h2f(xr[i]) * inv_rms * h2f(gamma[i]));
+    }
+}
+
+/* kernels/mined/fp32_sum/reference.c:8-14 (acc = acc + x, in order) per
+ * row; max seeded at -INFINITY like the mined amax references. */
+void oracle_rowreduce_f32_rows(const float *x, float *out, int R, int C,
+                               int op, int r0, int r1) {
+    (void)R;
+    for (int r = r0; r < r1; r++) {
+        const float *xr = x + (size_t)r * C;
+        float acc;
+        if (op == 0) {
+            acc = 0.0f;
+            for (int j = 0; j < C; j++) acc = acc + xr[j];
+        } else {
+            acc = -INFINITY;
+            for (int j = 0; j < C; j++) acc = xr[j] > acc ? xr[j] : acc;
+        }
+        out[r] = acc;
+    }
+}
+
+/* ---- threaded driver ---- */
+
+typedef struct {
+    int op;
+    const void *args;
+    int r0, r1;
+} oracle_job;
+
+static void *oracle_job_run(void *p) {
+    const oracle_job *j = (const oracle_job *)p;
+    switch (j->op) {
+    case ORACLE_OP_I8_GEMM_REQUANT: {
+        const oracle_gemm_args *a = (const oracle_gemm_args *)j->args;
+        oracle_i8_gemm_requant_rows((const int8_t *)a->A, (const int8_t *)a->B,
+                                    (int8_t *)a->out, a->M, a->N, a->K, a->mult,
+                                    a->shift, (int8_t)a->zp, j->r0, j->r1);
+        break;
+    }
+    case ORACLE_OP_GEMM_U8S8_PC: {
+        const oracle_gemm_args *a = (const oracle_gemm_args *)j->args;
+        oracle_gemm_u8s8_pc_rows((const uint8_t *)a->A, (const int8_t *)a->B,
+                                 a->bias, (uint8_t *)a->out, a->M, a->N, a->K,
+                                 a->zpA, a->mult_pc, a->shift_pc,
+                                 (uint8_t)a->zp, j->r0, j->r1);
+        break;
+    }
+    case ORACLE_OP_GEMM_F16_NT: {
+        const oracle_gemm_args *a = (const oracle_gemm_args *)j->args;
+        oracle_gemm_f16_nt_rows((const uint16_t *)a->A, (const uint16_t *)a->B,
+                                (uint16_t *)a->out, a->M, a->N, a->K, j->r0, j->r1);
+        break;
+    }
+    case ORACLE_OP_ATTN_F16: {
+        /* rows here are (head, query-row) pairs flattened as h * SQ + q */
+        const oracle_attn_args *a = (const oracle_attn_args *)j->args;
+        size_t qs = (size_t)a->SQ * a->D, ks = (size_t)a->SK * a->D;
+        for (int t = j->r0; t < j->r1;) {
+            int h = t / a->SQ, q = t % a->SQ;
+            int qe = a->SQ;
+            if ((h + 1) * a->SQ > j->r1) qe = j->r1 - h * a->SQ;
+            oracle_attn_f16_head_rows(a->Q + h * qs, a->K + h * ks, a->V + h * ks,
+                                      a->O + h * qs, a->SK, a->D, a->scale,
+                                      a->causal, q, qe);
+            t = h * a->SQ + qe;
+        }
+        break;
+    }
+    case ORACLE_OP_SOFTMAX_F32: {
+        const oracle_rows_args *a = (const oracle_rows_args *)j->args;
+        oracle_softmax_f32_rows(a->x, a->out, a->R, a->C, j->r0, j->r1);
+        break;
+    }
+    case ORACLE_OP_LAYERNORM_F32: {
+        const oracle_rows_args *a = (const oracle_rows_args *)j->args;
+        oracle_layernorm_f32_rows(a->x, a->gamma, a->beta, a->out, a->R, a->C,
+                                  a->eps, j->r0, j->r1);
+        break;
+    }
+    case ORACLE_OP_ROWREDUCE_F32: {
+        const oracle_rows_args *a = (const oracle_rows_args *)j->args;
+        oracle_rowreduce_f32_rows(a->x, a->out, a->R, a->C, a->op, j->r0, j->r1);
+        break;
+    }
+    default:
+        break;
+    }
+    return NULL;
+}
+
+int oracle_parallel(int op, const void *args, int r0, int r1, int nthreads) {
+    if (r1 <= r0) return 0;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > r1 - r0) nthreads = r1 - r0;
+    oracle_job *jobs = (oracle_job *)calloc((size_t)nthreads, sizeof(oracle_job));
+    pthread_t *th = (pthread_t *)calloc((size_t)nthreads, sizeof(pthread_t));
+    if (!jobs || !th) {
+        free(jobs);
+        free(th);
+        return -1;
+    }
+    int n = r1 - r0, rc = 0;
+    for (int t = 0; t < nthreads; t++) {
+        jobs[t].op = op;
+        jobs[t].args = args;
+        jobs[t].r0 = r0 + (int)((int64_t)n * t / nthreads);
+        jobs[t].r1 = r0 + (int)((int64_t)n * (t + 1) / nthreads);
+        if (pthread_create(&th[t], NULL, oracle_job_run, &jobs[t]) != 0) {
+            oracle_job_run(&jobs[t]);
+            th[t] = 0;
+        }
+    }
+    for (int t = 0; t < nthreads; t++)
+        if (th[t]) pthread_join(th[t], NULL);
+    free(th);
+    free(jobs);
+    return rc;
+}

@@ -1,0 +1,164 @@
+/* hexoracle.h -- CPU oracle for the hot-path operators (TEST INFRASTRUCTURE).
+ *
+ * This library is the checker, never the product: only tests/, the smoke()
+ * entry of __graft_entry__.py and the cpu_baseline / --impl reference legs of
+ * bench.py may load it.  The CUDA path in hexkernels_b200/ never calls it.
+ *
+ * Every function restates one scalar reference.c of the hexkernels corpus
+ * (sriharshapy/hexkernels, paths relative to that repository) with the same
+ * arithmetic, the same summation order and the same rounding; the restatement
+ * only lifts fixed-size stack arrays and adds row ranges [r0, r1) so a caller
+ * can split the rows across threads.  Parity is pinned by tests/golden/, whose
+ * expected outputs were produced by the reference's own reference.c files
+ * compiled here (oracle/Makefile target `ref`, script tests/golden/make_golden.py).
+ *
+ * fp16 values travel as uint16_t bit patterns (IEEE binary16); the C side
+ * converts with _Float16, which rounds to nearest-even like the reference's
+ * __fp16 casts.
+ */
+#ifndef HEXORACLE_H
+#define HEXORACLE_H
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- integer GEMM + fixed-point requant family ---- */
+
+/* kernels/expert/i8_gemm_requant/reference.c:2-20 */
+void oracle_i8_gemm_requant_rows(const int8_t *A, const int8_t *B, int8_t *out,
+                                 int M, int N, int K, int32_t mult, int shift,
+                                 int8_t zp, int r0, int r1);
+
+/* kernels/expert/i8_gemm_bias_requant/reference.c:2-24 */
+void oracle_i8_gemm_bias_requant_rows(const int8_t *A, const int8_t *B,
+                                      const int32_t *bias, int8_t *out,
+                                      int M, int N, int K, int32_t mult,
+                                      int shift, int8_t zp, int r0, int r1);
+
+/* kernels/expert/gemm_tile_zp_i8/reference.c:6-30 */
+void oracle_gemm_tile_zp_i8_rows(const int8_t *A, const int8_t *B, int8_t *out,
+                                 int M, int N, int K, int32_t zpA,
+                                 int32_t scale_mult, int scale_shift,
+                                 int r0, int r1);
+
+/* Composed u8 x s8 asymmetric GEMM with per-output-channel requant to u8:
+ * zero-point decomposition of gemm_tile_zp_i8/reference.c:10-19, bias add of
+ * i8_gemm_bias_requant/reference.c:13, per-channel (column j) mult/shift of
+ * requant_per_channel/reference.c:5-10, u8 saturation with zp of
+ * requantize_i32_u8_dma/reference.c:5-13. */
+void oracle_gemm_u8s8_pc_rows(const uint8_t *A, const int8_t *B,
+                              const int32_t *bias, uint8_t *out,
+                              int M, int N, int K, int32_t zpA,
+                              const int32_t *mult, const int *shift,
+                              uint8_t zp_out, int r0, int r1);
+
+/* kernels/expert/requant_per_channel/reference.c:2-17 (rows = channels) */
+void oracle_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
+                                const int32_t *mult, const int *shift, int8_t zp);
+
+/* kernels/expert/requantize_i32_u8_dma/reference.c:5-18 */
+void oracle_requantize_i32_u8(const int32_t *a, uint8_t *out, int64_t n,
+                              int32_t mult, int shift, uint8_t zp);
+
+/* ---- fp16 GEMM ---- */
+
+/* kernels/expert/fp16_attention_qkt_hmx/reference.c:7-15 generalised to
+ * M x N x K: out[i*N+j] = (fp16) sum_d A[i*K+d] * Bt[j*K+d], fp32 accumulate
+ * in d order, one fp16 rounding. */
+void oracle_gemm_f16_nt_rows(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
+                             int M, int N, int K, int r0, int r1);
+
+/* kernels/expert/hmx_matmul_fp16_deepk/reference.c:19-27 generalised to
+ * M x N x K with row-major B[K][N]. */
+void oracle_gemm_f16_nn_rows(const uint16_t *A, const uint16_t *B, uint16_t *out,
+                             int M, int N, int K, int r0, int r1);
+
+/* ---- fp16 attention ---- */
+
+/* kernels/expert/fp16_flash_attention_tile/reference.c:9-28 with the scale
+ * as a parameter, heap score buffers (no SK <= 64 cap), an optional causal
+ * window (key j visible to query i iff j <= i, top-left aligned) and a loop
+ * over BH heads: Q and O are [BH, SQ, D], K and V are [BH, SK, D].
+ * Heads [h0, h1) of the flattened B*H range. */
+void oracle_attn_f16_heads(const uint16_t *Q, const uint16_t *K,
+                           const uint16_t *V, uint16_t *O, int BH, int SQ,
+                           int SK, int D, float scale, int causal, int h0,
+                           int h1);
+
+/* One head, query rows [q0, q1) only (bounded CPU samples).  Q and O point
+ * at the head's row 0; K and V at the head's key 0. */
+void oracle_attn_f16_head_rows(const uint16_t *Q, const uint16_t *K,
+                               const uint16_t *V, uint16_t *O, int SK, int D,
+                               float scale, int causal, int q0, int q1);
+
+/* kernels/expert/online_softmax_step_fp16/kernel_api.h:17-24 recurrence,
+ * restated from its reference.c */
+void oracle_online_softmax_step_f16(const uint16_t *scores, const uint16_t *V,
+                                    uint16_t *running_max, uint16_t *running_sum,
+                                    uint16_t *acc, int BLK, int D);
+
+/* ---- row reductions ---- */
+
+/* kernels/expert/fp16_softmax/reference.c:8-29 in fp32 (no C <= 256 cap) */
+void oracle_softmax_f32_rows(const float *x, float *out, int R, int C,
+                             int r0, int r1);
+/* same, fp16 storage, exactly reference.c:8-29 */
+void oracle_softmax_f16_rows(const uint16_t *x, uint16_t *out, int R, int C,
+                             int r0, int r1);
+
+/* kernels/expert/fp16_layernorm/reference.c:7-24 applied per row of an R x C
+ * matrix with eps as a parameter (the reference hardwires 1e-3f). */
+void oracle_layernorm_f32_rows(const float *x, const float *gamma,
+                               const float *beta, float *out, int R, int C,
+                               float eps, int r0, int r1);
+void oracle_layernorm_f16_rows(const uint16_t *x, const uint16_t *gamma,
+                               const uint16_t *beta, uint16_t *out, int R,
+                               int C, float eps, int r0, int r1);
+
+/* kernels/expert/fp16_rmsnorm/reference.c:6-17 per row, eps parameter
+ * (the reference hardwires 1e-3f). */
+void oracle_rmsnorm_f32_rows(const float *x, const float *gamma, float *out,
+                             int R, int C, float eps, int r0, int r1);
+void oracle_rmsnorm_f16_rows(const uint16_t *x, const uint16_t *gamma,
+                             uint16_t *out, int R, int C, float eps, int r0,
+                             int r1);
+
+/* kernels/mined/fp32_sum/reference.c:6-17 (sequential fp32 accumulate) per
+ * row; op 0 = sum, op 1 = max (fp32_max_other style max, NaN-free inputs). */
+void oracle_rowreduce_f32_rows(const float *x, float *out, int R, int C,
+                               int op, int r0, int r1);
+
+/* ---- threaded drivers: split [0, rows) into nthreads contiguous blocks ---- */
+enum {
+    ORACLE_OP_I8_GEMM_REQUANT = 1,
+    ORACLE_OP_GEMM_U8S8_PC = 2,
+    ORACLE_OP_GEMM_F16_NT = 3,
+    ORACLE_OP_ATTN_F16 = 4,
+    ORACLE_OP_SOFTMAX_F32 = 5,
+    ORACLE_OP_LAYERNORM_F32 = 6,
+    ORACLE_OP_ROWREDUCE_F32 = 7,
+};
+/* Runs `op` with its arguments packed in `args` (see hexoracle.c) over rows
+ * (or heads) [r0, r1) split across nthreads pthreads.  Returns 0 on success. */
+int oracle_parallel(int op, const void *args, int r0, int r1, int nthreads);
+
+/* Packed argument blocks for oracle_parallel */
+typedef struct {
+    const void *A, *B; const int32_t *bias; void *out;
+    int M, N, K; int32_t zpA; int32_t mult; int shift; int zp;
+    const int32_t *mult_pc; const int *shift_pc;
+} oracle_gemm_args;
+typedef struct {
+    const uint16_t *Q, *K, *V; uint16_t *O; int BH, SQ, SK, D; float scale; int causal;
+} oracle_attn_args;
+typedef struct {
+    const float *x, *gamma, *beta; float *out; int R, C; float eps; int op;
+} oracle_rows_args;
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HEXORACLE_H */

@@ -1,0 +1,249 @@
+"""NumPy wrapper of the CPU oracle (hexoracle.c) -- TEST INFRASTRUCTURE.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs use
+this module, as the checker or the timed CPU baseline.  The product path
+(hexkernels_b200) never imports it.  liboracle.so is built on first use with
+the oracle Makefile (gcc only).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+P = C.c_void_p
+_lib = None
+_ref = None
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        so = HERE / "liboracle.so"
+        if not so.exists():
+            build()
+        _lib = C.CDLL(str(so))
+    return _lib
+
+
+def ref_lib() -> C.CDLL | None:
+    """The reference's own scalar code (oracle/_ref/libhexref.so) if built."""
+    global _ref
+    if _ref is None:
+        so = HERE / "_ref" / "libhexref.so"
+        if so.exists():
+            _ref = C.CDLL(str(so))
+    return _ref
+
+
+def _p(a):
+    return a.ctypes.data_as(P)
+
+
+def nthreads_default() -> int:
+    return len(os.sched_getaffinity(0))
+
+
+# ------------------------------------------------------------------ integer
+
+def gemm_i8_requant(A, B, mult, shift, zp, rows=None):
+    A, B = np.ascontiguousarray(A, np.int8), np.ascontiguousarray(B, np.int8)
+    (M, K), (_, N) = A.shape, B.shape
+    r0, r1 = rows or (0, M)
+    out = np.zeros((M, N), np.int8)
+    lib().oracle_i8_gemm_requant_rows(_p(A), _p(B), _p(out), M, N, K, C.c_int32(mult),
+                                      C.c_int(shift), C.c_int8(zp), r0, r1)
+    return out
+
+
+def gemm_i8_bias_requant(A, B, bias, mult, shift, zp):
+    A, B = np.ascontiguousarray(A, np.int8), np.ascontiguousarray(B, np.int8)
+    bias = np.ascontiguousarray(bias, np.int32)
+    (M, K), (_, N) = A.shape, B.shape
+    out = np.zeros((M, N), np.int8)
+    lib().oracle_i8_gemm_bias_requant_rows(_p(A), _p(B), _p(bias), _p(out), M, N, K,
+                                           C.c_int32(mult), C.c_int(shift), C.c_int8(zp), 0, M)
+    return out
+
+
+def gemm_i8_zp(A, B, zpA, mult, shift):
+    A, B = np.ascontiguousarray(A, np.int8), np.ascontiguousarray(B, np.int8)
+    (M, K), (_, N) = A.shape, B.shape
+    out = np.zeros((M, N), np.int8)
+    lib().oracle_gemm_tile_zp_i8_rows(_p(A), _p(B), _p(out), M, N, K, C.c_int32(zpA),
+                                      C.c_int32(mult), C.c_int(shift), 0, M)
+    return out
+
+
+def gemm_u8s8_pc(A, B, bias, zpA, mult, shift, zp_out, rows=None):
+    A, B = np.ascontiguousarray(A, np.uint8), np.ascontiguousarray(B, np.int8)
+    bias = np.ascontiguousarray(bias, np.int32)
+    mult, shift = np.ascontiguousarray(mult, np.int32), np.ascontiguousarray(shift, np.int32)
+    (M, K), (_, N) = A.shape, B.shape
+    r0, r1 = rows or (0, M)
+    out = np.zeros((M, N), np.uint8)
+    lib().oracle_gemm_u8s8_pc_rows(_p(A), _p(B), _p(bias), _p(out), M, N, K, C.c_int32(zpA),
+                                   _p(mult), _p(shift), C.c_uint8(zp_out), r0, r1)
+    return out
+
+
+def requant_per_channel(a, mult, shift, zp):
+    a = np.ascontiguousarray(a, np.int32)
+    R, Cc = a.shape
+    mult, shift = np.ascontiguousarray(mult, np.int32), np.ascontiguousarray(shift, np.int32)
+    out = np.zeros((R, Cc), np.int8)
+    lib().oracle_requant_per_channel(_p(a), _p(out), R, Cc, _p(mult), _p(shift), C.c_int8(zp))
+    return out
+
+
+def requantize_i32_u8(a, mult, shift, zp):
+    a = np.ascontiguousarray(a, np.int32)
+    out = np.zeros(a.shape, np.uint8)
+    lib().oracle_requantize_i32_u8(_p(a), _p(out), C.c_int64(a.size), C.c_int32(mult),
+                                   C.c_int(shift), C.c_uint8(zp))
+    return out
+
+
+# --------------------------------------------------------------------- fp16
+
+def gemm_f16_nt(A, Bt, rows=None):
+    A, Bt = np.ascontiguousarray(A, np.float16), np.ascontiguousarray(Bt, np.float16)
+    (M, K), (N, _) = A.shape, Bt.shape
+    r0, r1 = rows or (0, M)
+    out = np.zeros((M, N), np.float16)
+    lib().oracle_gemm_f16_nt_rows(_p(A), _p(Bt), _p(out), M, N, K, r0, r1)
+    return out
+
+
+def gemm_f16_nn(A, B):
+    A, B = np.ascontiguousarray(A, np.float16), np.ascontiguousarray(B, np.float16)
+    (M, K), (_, N) = A.shape, B.shape
+    out = np.zeros((M, N), np.float16)
+    lib().oracle_gemm_f16_nn_rows(_p(A), _p(B), _p(out), M, N, K, 0, M)
+    return out
+
+
+def attn_f16(Q, K, V, scale, causal, heads=None):
+    Q, K, V = (np.ascontiguousarray(t, np.float16) for t in (Q, K, V))
+    SQ, D = Q.shape[-2:]
+    SK = K.shape[-2]
+    BH = int(np.prod(Q.shape[:-2])) if Q.ndim > 2 else 1
+    h0, h1 = heads or (0, BH)
+    O = np.zeros(Q.shape, np.float16)
+    lib().oracle_attn_f16_heads(_p(Q), _p(K), _p(V), _p(O), BH, SQ, SK, D, C.c_float(scale),
+                                int(bool(causal)), h0, h1)
+    return O
+
+
+def online_softmax_step_f16(scores, V, running_max, running_sum, acc):
+    scores, V = np.ascontiguousarray(scores, np.float16), np.ascontiguousarray(V, np.float16)
+    acc = np.array(acc, np.float16, copy=True)
+    BLK, D = V.shape
+    m = np.array([running_max], np.float16)
+    s = np.array([running_sum], np.float16)
+    lib().oracle_online_softmax_step_f16(_p(scores), _p(V), _p(m), _p(s), _p(acc), BLK, D)
+    return m[0], s[0], acc
+
+
+# --------------------------------------------------------------------- rows
+
+def softmax(x):
+    x = np.ascontiguousarray(x)
+    R, Cc = x.reshape(-1, x.shape[-1]).shape
+    out = np.zeros_like(x)
+    if x.dtype == np.float32:
+        lib().oracle_softmax_f32_rows(_p(x), _p(out), R, Cc, 0, R)
+    else:
+        lib().oracle_softmax_f16_rows(_p(x), _p(out), R, Cc, 0, R)
+    return out
+
+
+def layernorm(x, gamma, beta, eps):
+    x = np.ascontiguousarray(x)
+    R, Cc = x.reshape(-1, x.shape[-1]).shape
+    gamma, beta = np.ascontiguousarray(gamma, x.dtype), np.ascontiguousarray(beta, x.dtype)
+    out = np.zeros_like(x)
+    if x.dtype == np.float32:
+        lib().oracle_layernorm_f32_rows(_p(x), _p(gamma), _p(beta), _p(out), R, Cc,
+                                        C.c_float(eps), 0, R)
+    else:
+        lib().oracle_layernorm_f16_rows(_p(x), _p(gamma), _p(beta), _p(out), R, Cc,
+                                        C.c_float(eps), 0, R)
+    return out
+
+
+def rmsnorm(x, gamma, eps):
+    x = np.ascontiguousarray(x)
+    R, Cc = x.reshape(-1, x.shape[-1]).shape
+    gamma = np.ascontiguousarray(gamma, x.dtype)
+    out = np.zeros_like(x)
+    if x.dtype == np.float32:
+        lib().oracle_rmsnorm_f32_rows(_p(x), _p(gamma), _p(out), R, Cc, C.c_float(eps), 0, R)
+    else:
+        lib().oracle_rmsnorm_f16_rows(_p(x), _p(gamma), _p(out), R, Cc, C.c_float(eps), 0, R)
+    return out
+
+
+def rowreduce(x, op):
+    x = np.ascontiguousarray(x, np.float32)
+    R, Cc = x.reshape(-1, x.shape[-1]).shape
+    out = np.zeros(R, np.float32)
+    lib().oracle_rowreduce_f32_rows(_p(x), _p(out), R, Cc, op, 0, R)
+    return out
+
+
+# ------------------------------------------------------ threaded (baseline)
+
+class _GemmArgs(C.Structure):
+    _fields_ = [("A", P), ("B", P), ("bias", P), ("out", P), ("M", C.c_int), ("N", C.c_int),
+                ("K", C.c_int), ("zpA", C.c_int32), ("mult", C.c_int32), ("shift", C.c_int),
+                ("zp", C.c_int), ("mult_pc", P), ("shift_pc", P)]
+
+
+class _AttnArgs(C.Structure):
+    _fields_ = [("Q", P), ("K", P), ("V", P), ("O", P), ("BH", C.c_int), ("SQ", C.c_int),
+                ("SK", C.c_int), ("D", C.c_int), ("scale", C.c_float), ("causal", C.c_int)]
+
+
+class _RowsArgs(C.Structure):
+    _fields_ = [("x", P), ("gamma", P), ("beta", P), ("out", P), ("R", C.c_int), ("C", C.c_int),
+                ("eps", C.c_float), ("op", C.c_int)]
+
+
+OP_I8_GEMM_REQUANT, OP_GEMM_U8S8_PC, OP_GEMM_F16_NT, OP_ATTN_F16 = 1, 2, 3, 4
+OP_SOFTMAX_F32, OP_LAYERNORM_F32, OP_ROWREDUCE_F32 = 5, 6, 7
+
+
+def parallel(op: int, args: C.Structure, r0: int, r1: int, nthreads: int) -> None:
+    rc = lib().oracle_parallel(op, C.byref(args), r0, r1, nthreads)
+    if rc:
+        raise RuntimeError(f"oracle_parallel failed ({rc})")
+
+
+def gemm_args(**kw) -> _GemmArgs:
+    a = _GemmArgs()
+    for k, v in kw.items():
+        setattr(a, k, _p(v) if isinstance(v, np.ndarray) else v)
+    return a
+
+
+def attn_args(**kw) -> _AttnArgs:
+    a = _AttnArgs()
+    for k, v in kw.items():
+        setattr(a, k, _p(v) if isinstance(v, np.ndarray) else v)
+    return a
+
+
+def rows_args(**kw) -> _RowsArgs:
+    a = _RowsArgs()
+    for k, v in kw.items():
+        setattr(a, k, _p(v) if isinstance(v, np.ndarray) else v)
+    return a

@@ -1,0 +1,435 @@
+"""Generate the golden vectors in tests/golden/ from the reference's own code.
+
+Run in a container where the hexkernels reference tree is mounted (default
+/root/reference, override with HEXKERNELS_REF).  It builds the reference's
+scalar reference.c files into oracle/_ref/libhexref.so (oracle/Makefile target
+`ref`), regenerates each expert harness's inputs with the harness's own LCG
+recipe (seed, value map, planted edge cases, parameter sweep), calls the
+REFERENCE implementation on them and stores inputs + expected outputs as
+compressed .npz files.  Large-shape cases draw inputs from
+numpy.random.default_rng(seed) with the value distributions of the benchmark
+configurations.
+
+The fixtures are committed; the GPU box never runs this script.
+
+    python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import base64
+import ctypes as C
+import os
+import re
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+REF_ROOT = Path(os.environ.get("HEXKERNELS_REF", "/root/reference"))
+
+P = C.c_void_p
+
+
+def lcg_stream(seed: int):
+    s = seed & 0xFFFFFFFF
+    while True:
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+        yield s
+
+
+def i8_top_byte(v: int) -> int:
+    """(int8_t)(lcg >> 24)"""
+    b = v >> 24
+    return b - 256 if b >= 128 else b
+
+
+def ptr(a: np.ndarray):
+    return a.ctypes.data_as(P)
+
+
+def load_ref():
+    subprocess.run(["make", "-s", "-C", str(REPO / "oracle"), "ref",
+                    f"REF_ROOT={REF_ROOT}"], check=True)
+    return C.CDLL(str(REPO / "oracle" / "_ref" / "libhexref.so"))
+
+
+def save(name: str, **arrays):
+    np.savez_compressed(HERE / f"{name}.npz", **arrays)
+    print(f"wrote {name}.npz: " + ", ".join(f"{k}{list(v.shape)}" for k, v in arrays.items()))
+
+
+# ----------------------------------------------------------------- integer
+
+def gen_i8_gemm_requant(ref):
+    # kernels/expert/i8_gemm_requant/harness.c:3-35 (M 32, N 32, K 66,
+    # seed 0xA3C7F1, edges A[0]=127 B[0]=127 A[1]=-128 B[N]=127,
+    # (mult, shift, zp) sets (3,4,0) and (1,0,0)).
+    M, N, K = 32, 32, 66
+    g = lcg_stream(0xA3C7F1)
+    A = np.array([i8_top_byte(next(g)) for _ in range(M * K)], np.int8)
+    B = np.array([i8_top_byte(next(g)) for _ in range(K * N)], np.int8)
+    A[0], B[0], A[1], B[N] = 127, 127, -128, 127
+    params = np.array([[3, 4, 0], [1, 0, 0]], np.int64)
+    outs = []
+    f = ref.ref_i8_gemm_requant
+    for mult, shift, zp in params:
+        out = np.full(M * N, -91, np.int8)
+        f(ptr(A), ptr(B), ptr(out), M, N, K, C.c_int32(int(mult)), C.c_int(int(shift)),
+          C.c_int8(int(zp)))
+        outs.append(out.copy())
+    save("i8_gemm_requant_harness", A=A, B=B, dims=np.array([M, N, K]), params=params,
+         out=np.stack(outs))
+
+
+def gen_i8_gemm_requant_256(ref):
+    # Benchmark configuration: int8 x int8 -> int32 GEMM M=N=K=256, uniform
+    # int8, mult in [2^30, 2^31), shift 8..15, seed 0.  That requant saturates
+    # almost everywhere, so the fixture adds a non-saturating sweep (shift
+    # 36..44, zp -3..3) that exercises rounding, plus small-mult cases.
+    M = N = K = 256
+    rng = np.random.default_rng(0)
+    A = rng.integers(-128, 128, size=(M, K), dtype=np.int8)
+    B = rng.integers(-128, 128, size=(K, N), dtype=np.int8)
+    mult0 = int(rng.integers(2**30, 2**31))
+    shift0 = int(rng.integers(8, 16))
+    params = [[mult0, shift0, 0]]
+    for shift in (36, 38, 40, 42, 44):
+        params.append([int(rng.integers(2**30, 2**31)), shift, int(rng.integers(-3, 4))])
+    params += [[1, 0, 0], [3, 4, -7], [-5, 9, 11], [2**31 - 1, 62, 0], [1234567, 30, 0]]
+    params = np.array(params, np.int64)
+    outs = []
+    for mult, shift, zp in params:
+        out = np.full(M * N, -91, np.int8)
+        ref.ref_i8_gemm_requant(ptr(A), ptr(B), ptr(out), M, N, K, C.c_int32(int(mult)),
+                                C.c_int(int(shift)), C.c_int8(int(zp)))
+        outs.append(out.reshape(M, N).copy())
+    save("i8_gemm_requant_256", A=A, B=B, params=params, out=np.stack(outs))
+
+
+def gen_i8_gemm_bias_requant(ref):
+    # kernels/expert/i8_gemm_bias_requant/harness.c:3-48 (32^3, seed 0xC9D4E2,
+    # bias = (lcg & 0xFFFF) - 0x8000, edges incl. bias[0] = -2e6, bias[1] = 2e6).
+    M = N = K = 32
+    g = lcg_stream(0xC9D4E2)
+    A = np.array([i8_top_byte(next(g)) for _ in range(M * K)], np.int8)
+    B = np.array([i8_top_byte(next(g)) for _ in range(K * N)], np.int8)
+    bias = np.array([(next(g) & 0xFFFF) - 0x8000 for _ in range(N)], np.int32)
+    A[0], B[0], A[1], B[N] = 127, 127, -128, 127
+    bias[0], bias[1], bias[2] = -2000000, 2000000, 0
+    params = np.array([[3, 4, 0], [1, 0, 0], [1 << 20, 28, 5]], np.int64)
+    outs = []
+    for mult, shift, zp in params:
+        out = np.full(M * N, -91, np.int8)
+        ref.ref_i8_gemm_bias_requant(ptr(A), ptr(B), ptr(bias), ptr(out), M, N, K,
+                                     C.c_int32(int(mult)), C.c_int(int(shift)),
+                                     C.c_int8(int(zp)))
+        outs.append(out.copy())
+    save("i8_gemm_bias_requant_harness", A=A, B=B, bias=bias, dims=np.array([M, N, K]),
+         params=params, out=np.stack(outs))
+
+
+def gen_gemm_tile_zp_i8(ref):
+    # kernels/expert/gemm_tile_zp_i8/harness.c:3-64 (M 8, N 8, K 94 with a
+    # K tail, seed 0x3B77F210, (zpA, mult, shift) = (0,3,7), (-10,5,4), (20,1,0)).
+    M, N, K = 8, 8, 94
+    g = lcg_stream(0x3B77F210)
+    A = np.array([i8_top_byte(next(g)) for _ in range(M * K)], np.int8)
+    B = np.array([i8_top_byte(next(g)) for _ in range(K * N)], np.int8)
+    A[0], B[0], A[1], B[N] = 127, 127, -128, 127
+    for i in range(M):
+        A[i * K + 92], A[i * K + 93] = 100, -50
+    for j in range(N):
+        B[92 * N + j], B[93 * N + j] = -80, 60
+    params = np.array([[0, 3, 7], [-10, 5, 4], [20, 1, 0]], np.int64)
+    outs = []
+    for zpa, mult, shift in params:
+        out = np.full(M * N, -91, np.int8)
+        ref.ref_gemm_tile_zp_i8(ptr(A), ptr(B), ptr(out), M, N, K, C.c_int32(int(zpa)),
+                                C.c_int32(int(mult)), C.c_int(int(shift)))
+        outs.append(out.copy())
+    save("gemm_tile_zp_i8_harness", A=A, B=B, dims=np.array([M, N, K]), params=params,
+         out=np.stack(outs))
+
+
+def gen_requant_per_channel(ref):
+    # kernels/expert/requant_per_channel/harness.c:4-75 (R 40, C 25, seed
+    # 0xBEEF77, a = (int32)lcg % 601 - 300 with C's truncating %, 5 sets).
+    R, Cc = 40, 25
+    g = lcg_stream(0xBEEF77)
+    a = []
+    for _ in range(R * Cc):
+        v = next(g)
+        v = v - (1 << 32) if v >= (1 << 31) else v
+        r = abs(v) % 601
+        a.append((r if v >= 0 else -r) - 300)
+    a = np.array(a, np.int32)
+    a[:5] = [4, -4, 300, -300, 0]
+    mult_sets = np.array([
+        [5, 5, 5, -3, 127] + [5] * 35,
+        [13] * 40,
+        [7, -7] * 20,
+        [1, 2, 3, 4] * 10,
+        [1, 2, 4, 8, 16] * 8,
+    ], np.int32)
+    shift_sets = np.array([
+        [3, 0, 7, 2, 4] + [3] * 35,
+        [7] * 40,
+        [3] * 40,
+        [0, 1, 2, 3] * 10,
+        [0, 1, 2, 3, 4] * 8,
+    ], np.int32)
+    zps = np.array([0, -5, 0, 10, 0], np.int8)
+    outs = []
+    for k in range(5):
+        out = np.full(R * Cc, -91, np.int8)
+        m = np.ascontiguousarray(mult_sets[k])
+        s = np.ascontiguousarray(shift_sets[k])
+        ref.ref_requant_per_channel(ptr(a), ptr(out), R, Cc, ptr(m), ptr(s), C.c_int8(int(zps[k])))
+        outs.append(out.copy())
+    save("requant_per_channel_harness", a=a, dims=np.array([R, Cc]), mult=mult_sets,
+         shift=shift_sets, zp=zps, out=np.stack(outs))
+
+
+def gen_requantize_i32_u8(ref):
+    # kernels/expert/requantize_i32_u8_dma/harness.c:18-77: N 262144,
+    # a[i] = ((i*2731 + 5) & 0xFFFF) - 32768, edges a[0..5], MULT 5, SHIFT 8,
+    # ZP 128; plus two more (mult, shift, zp) sets over the same input.
+    n = 262144
+    i = np.arange(n, dtype=np.int64)
+    a = (((i * 2731 + 5) & 0xFFFF) - 32768).astype(np.int32)
+    a[:6] = [32767, -32768, 0, 6400, 13000, -13000]
+    params = np.array([[5, 8, 128], [-3, 2, 17], [40000, 20, 255]], np.int64)
+    outs = []
+    for mult, shift, zp in params:
+        out = np.full(n, 0xA5, np.uint8)
+        ref.ref_requantize_i32_u8_dma(ptr(a), ptr(out), n, C.c_int32(int(mult)),
+                                      C.c_int(int(shift)), C.c_uint8(int(zp)))
+        outs.append(out.copy())
+    save("requantize_i32_u8_harness", params=params, out=np.stack(outs))
+
+
+def gen_gemm_u8s8_pc(ref):
+    # Composed u8 x s8 per-channel GEMM at a small shape with the benchmark's
+    # value distributions (A u8, zpA 128, B s8, bias N(0,1000), mult in
+    # [2^30, 2^31), shift spread so outputs cover [0, 255], zp_out 128).  The
+    # int32 accumulator rawdot - zpA*colsum is exact integer arithmetic
+    # (numpy int64, no overflow at these sizes); the per-channel requant and u8
+    # saturation run through the reference's own requantize_i32_u8_dma
+    # reference.c, one output column (channel) at a time.
+    rng = np.random.default_rng(4)
+    cases = []
+    for (M, N, K) in [(64, 96, 160), (130, 72, 200)]:
+        A = rng.integers(0, 256, size=(M, K), dtype=np.uint8)
+        B = rng.integers(-128, 128, size=(K, N), dtype=np.int8)
+        bias = np.round(rng.normal(0, 1000, size=N)).astype(np.int32)
+        zpa = 128
+        mult = rng.integers(2**30, 2**31, size=N, dtype=np.int64).astype(np.int32)
+        acc = A.astype(np.int64) @ B.astype(np.int64) - zpa * B.astype(np.int64).sum(0)
+        biased = acc + bias
+        sigma = max(float(np.std(biased)), 1.0)
+        # shift so that sigma * mult / 2^shift ~ 48
+        shift = np.clip(np.round(np.log2(sigma * mult.astype(np.float64) / 48.0)), 0, 62).astype(np.int32)
+        shift[0] = 0          # saturating channel
+        shift[1] = 62         # all-zero channel (before zp)
+        zp_out = 128
+        out = np.zeros((M, N), np.uint8)
+        col = np.zeros(M, np.uint8)
+        for j in range(N):
+            bj = np.ascontiguousarray(biased[:, j].astype(np.int32))
+            ref.ref_requantize_i32_u8_dma(ptr(bj), ptr(col), M, C.c_int32(int(mult[j])),
+                                          C.c_int(int(shift[j])), C.c_uint8(zp_out))
+            out[:, j] = col
+        cases.append(dict(A=A, B=B, bias=bias, mult=mult, shift=shift, zpa=np.int32(zpa),
+                          zp_out=np.uint8(zp_out), out=out))
+    arrays = {}
+    for ci, c in enumerate(cases):
+        for k, v in c.items():
+            arrays[f"c{ci}_{k}"] = np.asarray(v)
+    arrays["ncases"] = np.array(len(cases))
+    save("gemm_u8s8_pc_small", **arrays)
+
+
+# ----------------------------------------------------------------- fp16
+
+def gen_hf_q(g, mod, off, step):
+    return np.array([((next(g) % mod) - off) * step], np.float16)[0]
+
+
+def hf_array(seed_iter, n, mod, off, step):
+    return np.array([((next(seed_iter) % mod) - off) * step for _ in range(n)],
+                    np.float32).astype(np.float16)
+
+
+def gen_f16_gemms(ref):
+    # kernels/expert/fp16_attention_qkt_hmx/harness.c:10-33 (n 32, k_dim 128,
+    # seed 0x9C412, values (lcg % 7 - 3) * 0.25, K stored [n, k_dim]).
+    g = lcg_stream(0x9C412)
+    n, kd = 32, 128
+    Q = hf_array(g, n * kd, 7, 3, 0.25)
+    K = hf_array(g, n * kd, 7, 3, 0.25)
+    out = np.zeros(n * n, np.float16)
+    ref.ref_fp16_attention_qkt_hmx(ptr(Q), ptr(K), ptr(out), n, kd)
+    save("gemm_f16_nt_harness", A=Q, Bt=K, dims=np.array([n, n, kd]), out=out)
+
+    # kernels/expert/hmx_matmul_fp16_deepk/harness.c (n 32, k_dim 128,
+    # seed 0xC0FFEE) -- row-major B[k_dim][n].
+    g = lcg_stream(0xC0FFEE)
+    A = hf_array(g, n * kd, 7, 3, 0.25)
+    B = hf_array(g, kd * n, 7, 3, 0.25)
+    out = np.zeros(n * n, np.float16)
+    ref.ref_hmx_matmul_fp16_deepk(ptr(A), ptr(B), ptr(out), n, kd)
+    save("gemm_f16_nn_harness", A=A, B=B, dims=np.array([n, n, kd]), out=out)
+
+    # kernels/expert/fp16_attention_av_hmx/harness.c (n 32, Skv 128, seed 0x5A17F)
+    g = lcg_stream(0x5A17F)
+    Pm = hf_array(g, n * kd, 7, 3, 0.25)
+    V = hf_array(g, kd * n, 7, 3, 0.25)
+    out = np.zeros(n * n, np.float16)
+    ref.ref_fp16_attention_av_hmx(ptr(Pm), ptr(V), ptr(out), n, kd)
+    save("attn_av_f16_harness", A=Pm, B=V, dims=np.array([n, n, kd]), out=out)
+
+    # Multi-tile shapes with the benchmark distribution N(0,1)/sqrt(K) through
+    # the same reference (square n x n output, any k_dim).
+    rng = np.random.default_rng(3)
+    for (n, kd) in [(256, 512), (192, 320)]:
+        A = (rng.standard_normal((n, kd)) / np.sqrt(kd)).astype(np.float16)
+        Bt = (rng.standard_normal((n, kd)) / np.sqrt(kd)).astype(np.float16)
+        out = np.zeros((n, n), np.float16)
+        ref.ref_fp16_attention_qkt_hmx(ptr(A), ptr(Bt), ptr(out), n, kd)
+        save(f"gemm_f16_nt_{n}x{kd}", A=A, Bt=Bt, out=out)
+
+
+def gen_flash_attention(ref):
+    # kernels/expert/fp16_flash_attention_tile/harness.c:12-60 (SQ 16, SK 64,
+    # DH 64, seed 0xF1A54A11, values (lcg % 9 - 4) * 0.25, Q row 0 and K row
+    # SK-1 forced to 1.0 so the running max moves on the final tile).
+    SQ, SK, DH = 16, 64, 64
+    g = lcg_stream(0xF1A54A11)
+    Q = hf_array(g, SQ * DH, 9, 4, 0.25)
+    K = hf_array(g, SK * DH, 9, 4, 0.25)
+    V = hf_array(g, SK * DH, 9, 4, 0.25)
+    Q[:DH] = 1.0
+    K[(SK - 1) * DH:] = 1.0
+    O = np.zeros(SQ * DH, np.float16)
+    ref.ref_fp16_flash_attention_tile(ptr(Q), ptr(K), ptr(V), ptr(O), SQ, SK, DH)
+    save("flash_attn_tile_harness", Q=Q, K=K, V=V, dims=np.array([SQ, SK, DH]), O=O)
+
+    # Larger non-causal tiles (the reference caps SK at 64) with N(0,1) inputs
+    # and the reference's FLASH_SCALE of 0.125.
+    rng = np.random.default_rng(5)
+    for (SQ, SK, DH) in [(256, 64, 64), (200, 48, 128)]:
+        Q = rng.standard_normal((SQ, DH)).astype(np.float16)
+        K = rng.standard_normal((SK, DH)).astype(np.float16)
+        V = rng.standard_normal((SK, DH)).astype(np.float16)
+        O = np.zeros((SQ, DH), np.float16)
+        ref.ref_fp16_flash_attention_tile(ptr(Q), ptr(K), ptr(V), ptr(O), SQ, SK, DH)
+        save(f"flash_attn_{SQ}x{SK}x{DH}", Q=Q, K=K, V=V, O=O)
+
+
+def gen_online_softmax_step(ref):
+    # kernels/expert/online_softmax_step_fp16/harness.c:16-135: BLK 24, D 48,
+    # three cases (init m, init l, init acc, seed, biased index, biased value).
+    BLK, D = 24, 48
+    cases = [(-30000.0, 0.0, 0.0, 0xA5C31, -1, 0.0),
+             (1.0, 3.0, 0.5, 0xBEEF77, 3, 5.0),
+             (20.0, 2.0, 1.5, 0xC0DE99, -1, 0.0)]
+    arrays = {}
+    for ci, (m0, l0, a0, seed, bi, bv) in enumerate(cases):
+        g = lcg_stream(seed)
+        scores = hf_array(g, BLK, 17, 8, 0.5)
+        if bi >= 0:
+            scores[bi] = bv
+        V = hf_array(g, BLK * D, 9, 4, 0.5)
+        rmax = np.array([m0], np.float16)
+        rsum = np.array([l0], np.float16)
+        acc = np.full(D, a0, np.float16)
+        arrays[f"c{ci}_scores"], arrays[f"c{ci}_V"] = scores.copy(), V.copy()
+        arrays[f"c{ci}_state_in"] = np.concatenate([rmax, rsum, acc])
+        ref.ref_online_softmax_step_fp16(ptr(scores), ptr(V), ptr(rmax), ptr(rsum), ptr(acc),
+                                         BLK, D)
+        arrays[f"c{ci}_state_out"] = np.concatenate([rmax, rsum, acc])
+    arrays["dims"] = np.array([BLK, D])
+    save("online_softmax_step_harness", **arrays)
+
+
+def gen_rows(ref):
+    # kernels/expert/fp16_softmax/harness.c:4-36 (R 8, C 256, seed 0x50F7,
+    # values (lcg % 13 - 6) * 0.5, row 0 one dominant max, row 1 uniform).
+    R, Cc = 8, 256
+    g = lcg_stream(0x50F7)
+    x = hf_array(g, R * Cc, 13, 6, 0.5)
+    x[:Cc] = -3.0
+    x[7] = 3.0
+    x[Cc:2 * Cc] = 1.0
+    out = np.zeros(R * Cc, np.float16)
+    ref.ref_fp16_softmax(ptr(x), ptr(out), R, Cc)
+    save("softmax_f16_harness", x=x, dims=np.array([R, Cc]), out=out)
+
+    # wider random fp16 softmax (the reference caps C at 256)
+    rng = np.random.default_rng(6)
+    x = (rng.standard_normal((96, 256)) * 4).astype(np.float16)
+    out = np.zeros((96, 256), np.float16)
+    ref.ref_fp16_softmax(ptr(x), ptr(out), 96, 256)
+    save("softmax_f16_96x256", x=x, out=out)
+
+    # kernels/expert/fp16_layernorm/harness.c:4-43 (n 2048, seed 0x1A9E5,
+    # gamma 1 + 0.25*((i%5)-2), beta 0.25*((i%7)-3), edges x[0]=3 x[1]=-3 x[n-1]=0)
+    n = 2048
+    g = lcg_stream(0x1A9E5)
+    x = hf_array(g, n, 13, 6, 0.5)
+    i = np.arange(n)
+    gamma = (1.0 + 0.25 * ((i % 5) - 2)).astype(np.float16)
+    beta = (0.25 * ((i % 7) - 3)).astype(np.float16)
+    x[0], x[1], x[n - 1] = 3.0, -3.0, 0.0
+    out = np.zeros(n, np.float16)
+    ref.ref_fp16_layernorm(ptr(x), ptr(gamma), ptr(beta), ptr(out), n)
+    save("layernorm_f16_harness", x=x, gamma=gamma, beta=beta, out=out)
+
+    # kernels/expert/fp16_rmsnorm/harness.c (n 2048, same recipe without beta)
+    rms_src = (REF_ROOT / "kernels/expert/fp16_rmsnorm/harness.c").read_text()
+    seed = int(re.search(r"uint32_t s = (0x[0-9A-Fa-f]+)u", rms_src).group(1), 16)
+    g = lcg_stream(seed)
+    x = hf_array(g, n, 13, 6, 0.5)
+    x[0], x[1], x[n - 1] = 3.0, -3.0, 0.0
+    out = np.zeros(n, np.float16)
+    ref.ref_fp16_rmsnorm(ptr(x), ptr(gamma), ptr(out), n)
+    save("rmsnorm_f16_harness", x=x, gamma=gamma, out=out, seed=np.array(seed))
+
+
+def gen_mined_fp32_sum():
+    # kernels/mined/fp32_sum/harness.c: the torch-made golden embedded as
+    # base64 (48 x 128 fp32 input) and its hex-float expected sum.
+    src = (REF_ROOT / "kernels/mined/fp32_sum/harness.c").read_text()
+    body = src.split("static const char b64_in_0[] =", 1)[1].split(";", 1)[0]
+    b64 = "".join(re.findall(r'"([^"]*)"', body))
+    x = np.frombuffer(base64.b64decode(b64), dtype=np.float32).copy()
+    gold = re.search(r"golden_out_0\[1\][^=]*=\s*\{\s*([^}]+)\}", src).group(1).strip()
+    exp = np.float32(float.fromhex(gold.rstrip("f")))
+    knu = re.search(r"forge2_close_acc\([^;]*?accum_s_0\[i\],\s*([^,]+),", src).group(1)
+    save("rowsum_fp32_mined", x=x, out=np.array([exp], np.float32),
+         knu=np.array([float.fromhex(knu.strip().rstrip("f"))], np.float32))
+
+
+def main():
+    if not (REF_ROOT / "kernels").is_dir():
+        sys.exit(f"reference tree not found at {REF_ROOT}")
+    ref = load_ref()
+    gen_i8_gemm_requant(ref)
+    gen_i8_gemm_requant_256(ref)
+    gen_i8_gemm_bias_requant(ref)
+    gen_gemm_tile_zp_i8(ref)
+    gen_requant_per_channel(ref)
+    gen_requantize_i32_u8(ref)
+    gen_gemm_u8s8_pc(ref)
+    gen_f16_gemms(ref)
+    gen_flash_attention(ref)
+    gen_online_softmax_step(ref)
+    gen_rows(ref)
+    gen_mined_fp32_sum()
+
+
+if __name__ == "__main__":
+    main()

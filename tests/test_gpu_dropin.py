@@ -1,0 +1,87 @@
+"""Drop-in boundary on the B200: the corpus's own harness.c programs, linked
+unchanged against the candidate_kernel shims (built from the reference tree
+into oracle/_ref/ by `make -C oracle ref-gpu`), print HVXENV_CORRECT; and the
+new task headers' shims compute the same as the oracle when called through
+candidate_kernel itself."""
+import ctypes as C
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+REF = REPO / "oracle" / "_ref"
+SHIMS = REPO / "hexkernels_b200" / "shims"
+
+pytestmark = pytest.mark.gpu
+
+HARNESSES = sorted(REF.glob("gpu_harness_*")) if REF.exists() else []
+
+
+@pytest.mark.skipif(not HARNESSES, reason="reference harnesses not built here (make -C oracle ref-gpu)")
+@pytest.mark.parametrize("exe", HARNESSES, ids=lambda p: p.name[len("gpu_harness_"):])
+def test_reference_harness_links_and_passes(hx, exe):
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert "HEXCUDA_ERROR" not in r.stderr, r.stderr
+    assert re.search(r"^HVXENV_CORRECT errors=0", r.stdout, re.M), r.stdout + r.stderr
+    assert "HEXCUDA_KERNEL_US" in r.stdout
+    assert r.returncode == 0
+
+
+def shim(name):
+    so = SHIMS / f"libcand_{name}.so"
+    if not so.exists():
+        subprocess.run(["make", "-s", "-C", str(SHIMS)], check=True)
+    lib = C.CDLL(str(so))
+    lib.candidate_kernel.restype = None
+    return lib.candidate_kernel
+
+
+def p(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def test_shim_softmax_layernorm_rowreduce_f32(hx, oracle):
+    rng = np.random.default_rng(1)
+    x = (rng.standard_normal((64, 4096)) * 8).astype(np.float32)
+    g = rng.normal(1, 0.1, 4096).astype(np.float32)
+    b = rng.normal(0, 0.1, 4096).astype(np.float32)
+    out = np.zeros_like(x)
+    shim("softmax_f32")(p(x), p(out), 64, 4096)
+    np.testing.assert_allclose(out, oracle.softmax(x), rtol=1e-5, atol=1e-7)
+    fn = shim("layernorm_f32")
+    fn.argtypes = [C.c_void_p] * 4 + [C.c_int, C.c_int, C.c_float]
+    fn(p(x), p(g), p(b), p(out), 64, 4096, 1e-5)
+    np.testing.assert_allclose(out, oracle.layernorm(x, g, b, 1e-5), rtol=1e-5, atol=1e-4)
+    red = np.zeros(64, np.float32)
+    shim("rowreduce_f32")(p(x), p(red), 64, 4096, 1)
+    np.testing.assert_array_equal(red, oracle.rowreduce(x, 1))
+
+
+def test_shim_gemm_u8s8_pc(hx, oracle):
+    rng = np.random.default_rng(2)
+    M, N, K = 300, 200, 640
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    bias = np.round(rng.normal(0, 1000, N)).astype(np.int32)
+    mult = rng.integers(2**30, 2**31, N, dtype=np.int64).astype(np.int32)
+    shift = np.full(N, 38, np.int32)
+    out = np.zeros((M, N), np.uint8)
+    fn = shim("gemm_u8s8_pc")
+    fn.argtypes = [C.c_void_p] * 4 + [C.c_int] * 3 + [C.c_int32, C.c_void_p, C.c_void_p, C.c_uint8]
+    fn(p(A), p(B), p(bias), p(out), M, N, K, 128, p(mult), p(shift), 128)
+    np.testing.assert_array_equal(out, oracle.gemm_u8s8_pc(A, B, bias, 128, mult, shift, 128))
+
+
+def test_shim_attn_f16(hx, oracle):
+    rng = np.random.default_rng(3)
+    Bn, H, S, D = 2, 3, 200, 128
+    Q, K, V = (rng.standard_normal((Bn, H, S, D)).astype(np.float16) for _ in range(3))
+    O = np.zeros_like(Q)
+    fn = shim("attn_f16")
+    fn.argtypes = [C.c_void_p] * 4 + [C.c_int] * 4 + [C.c_float, C.c_int]
+    fn(p(Q), p(K), p(V), p(O), Bn, H, S, D, 1 / np.sqrt(D), 1)
+    exp = oracle.attn_f16(Q, K, V, 1 / np.sqrt(D), True)
+    assert np.all(np.abs(O.astype(np.float64) - exp) <= 1e-2 * np.abs(exp.astype(np.float64)) + 2e-3)

@@ -1,0 +1,210 @@
+"""tcgen05 GEMMs and requant kernels on the B200 vs the reference.
+
+Integer paths are bit-exact against the reference's golden outputs and the
+oracle.  fp16 GEMMs: |got - exp| <= 1e-2 * |exp| + 1e-3 * max|exp| against the
+fp32-accumulating reference (in practice at most 1 fp16 ulp apart).
+"""
+import numpy as np
+import pytest
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+# ----------------------------------------------------------- requant kernels
+
+def test_requant_per_channel_golden(hx):
+    g = golden("requant_per_channel_harness")
+    R, Cc = g["dims"]
+    a = g["a"].reshape(R, Cc)
+    for k in range(len(g["zp"])):
+        out = hx.requant_per_channel(a, g["mult"][k], g["shift"][k], int(g["zp"][k]))
+        np.testing.assert_array_equal(out.ravel(), g["out"][k])
+
+
+def test_requantize_i32_u8_golden(hx):
+    g = golden("requantize_i32_u8_harness")
+    n = 262144
+    i = np.arange(n, dtype=np.int64)
+    a = (((i * 2731 + 5) & 0xFFFF) - 32768).astype(np.int32)
+    a[:6] = [32767, -32768, 0, 6400, 13000, -13000]
+    for p, (mult, shift, zp) in enumerate(g["params"]):
+        np.testing.assert_array_equal(hx.requantize_i32_u8(a, int(mult), int(shift), int(zp)),
+                                      g["out"][p])
+    # ragged length and misaligned start take the scalar path
+    out = hx.requantize_i32_u8(a[3:100003], 5, 8, 128)
+    np.testing.assert_array_equal(out, g["out"][0][3:100003])
+
+
+# ------------------------------------------------------------- int8 GEMMs
+
+def test_i8_gemm_requant_harness(hx):
+    g = golden("i8_gemm_requant_harness")
+    M, N, K = g["dims"]
+    A, B = g["A"].reshape(M, K), g["B"].reshape(K, N)
+    for p, (mult, shift, zp) in enumerate(g["params"]):
+        out = hx.gemm_i8_requant(A, B, int(mult), int(shift), int(zp))
+        np.testing.assert_array_equal(out.ravel(), g["out"][p])
+
+
+def test_i8_gemm_requant_256_config(hx):
+    """int8 x int8 -> int32 GEMM M=N=K=256 (seed 0) and its rounding sweep."""
+    g = golden("i8_gemm_requant_256")
+    for p, (mult, shift, zp) in enumerate(g["params"]):
+        out = hx.gemm_i8_requant(g["A"], g["B"], int(mult), int(shift), int(zp))
+        np.testing.assert_array_equal(out, g["out"][p])
+
+
+def test_i8_gemm_bias_requant_harness(hx):
+    g = golden("i8_gemm_bias_requant_harness")
+    M, N, K = g["dims"]
+    A, B = g["A"].reshape(M, K), g["B"].reshape(K, N)
+    for p, (mult, shift, zp) in enumerate(g["params"]):
+        out = hx.gemm_i8_bias_requant(A, B, g["bias"], int(mult), int(shift), int(zp))
+        np.testing.assert_array_equal(out.ravel(), g["out"][p])
+
+
+def test_gemm_tile_zp_i8_harness(hx):
+    g = golden("gemm_tile_zp_i8_harness")
+    M, N, K = g["dims"]
+    A, B = g["A"].reshape(M, K), g["B"].reshape(K, N)
+    for p, (zpa, mult, shift) in enumerate(g["params"]):
+        out = hx.gemm_i8_zp(A, B, int(zpa), int(mult), int(shift))
+        np.testing.assert_array_equal(out.ravel(), g["out"][p])
+
+
+def test_gemm_u8s8_pc_golden(hx):
+    g = golden("gemm_u8s8_pc_small")
+    for c in range(int(g["ncases"])):
+        k = lambda s: g[f"c{c}_{s}"]
+        out = hx.gemm_u8s8_pc(k("A"), k("B"), k("bias"), int(k("zpa")), k("mult"), k("shift"),
+                              int(k("zp_out")))
+        np.testing.assert_array_equal(out, k("out"))
+
+
+I8_SHAPES = [(1, 1, 1), (1, 300, 17), (129, 257, 130), (256, 384, 512), (200, 64, 0),
+             (300, 520, 1000), (128, 256, 4096), (513, 129, 96)]
+
+
+@pytest.mark.parametrize("M,N,K", I8_SHAPES)
+def test_gemm_u8s8_pc_random(hx, oracle, M, N, K):
+    rng = np.random.default_rng(M * 31 + N * 7 + K)
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    bias = np.round(rng.normal(0, 1000, N)).astype(np.int32)
+    mult = rng.integers(2**30, 2**31, N, dtype=np.int64).astype(np.int32)
+    shift = rng.integers(30, 46, N).astype(np.int32)
+    for zpa in (128, 0, -7):
+        got = hx.gemm_u8s8_pc(A, B, bias, zpa, mult, shift, 128)
+        exp = oracle.gemm_u8s8_pc(A, B, bias, zpa, mult, shift, 128)
+        np.testing.assert_array_equal(got, exp)
+
+
+@pytest.mark.parametrize("M,N,K", I8_SHAPES)
+def test_gemm_i8_variants_random(hx, oracle, M, N, K):
+    rng = np.random.default_rng(M + N * 3 + K * 5)
+    A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    bias = rng.integers(-40000, 40000, N).astype(np.int32)
+    for mult, shift, zp in ((1, 0, 0), (3, 5, -2), (1234567, 30, 4), (2**31 - 1, 40, 0)):
+        np.testing.assert_array_equal(hx.gemm_i8_requant(A, B, mult, shift, zp),
+                                      oracle.gemm_i8_requant(A, B, mult, shift, zp))
+        np.testing.assert_array_equal(hx.gemm_i8_bias_requant(A, B, bias, mult, shift, zp),
+                                      oracle.gemm_i8_bias_requant(A, B, bias, mult, shift, zp))
+        np.testing.assert_array_equal(hx.gemm_i8_zp(A, B, -13, mult, shift),
+                                      oracle.gemm_i8_zp(A, B, -13, mult, shift))
+
+
+def test_gemm_u8s8_extreme_values(hx, oracle):
+    # all-max / all-min operands: largest |acc| the shape allows
+    M, N, K = 130, 200, 2048
+    A = np.full((M, K), 255, np.uint8)
+    A[::2] = 0
+    B = np.full((K, N), -128, np.int8)
+    B[:, ::3] = 127
+    bias = np.zeros(N, np.int32)
+    mult = np.full(N, 2**31 - 1, np.int32)
+    shift = np.full(N, 40, np.int32)
+    np.testing.assert_array_equal(hx.gemm_u8s8_pc(A, B, bias, 128, mult, shift, 128),
+                                  oracle.gemm_u8s8_pc(A, B, bias, 128, mult, shift, 128))
+
+
+# --------------------------------------------------------------- fp16 GEMMs
+
+def assert_f16_gemm_close(got, exp):
+    g, e = got.astype(np.float64), exp.astype(np.float64)
+    lim = 1e-2 * np.abs(e) + 1e-3 * np.abs(e).max()
+    bad = np.abs(g - e) > lim
+    assert not bad.any(), f"{bad.sum()} of {bad.size} off"
+    ulp = np.abs(got.view(np.int16).astype(np.int32) - exp.view(np.int16).astype(np.int32))
+    assert np.mean(ulp <= 1) > 0.999
+
+
+@pytest.mark.parametrize("name,kind", [("gemm_f16_nt_harness", "nt"),
+                                       ("gemm_f16_nn_harness", "nn"),
+                                       ("attn_av_f16_harness", "nn")])
+def test_f16_gemm_harness_golden(hx, name, kind):
+    g = golden(name)
+    M, N, K = g["dims"]
+    if kind == "nt":
+        got = hx.gemm_f16_nt(g["A"].reshape(M, K), g["Bt"].reshape(N, K))
+    else:
+        got = hx.gemm_f16_nn(g["A"].reshape(M, K), g["B"].reshape(K, N))
+    # the harnesses' own deep-K tolerance (atol 8e-3, rtol 1.2e-2)
+    e = g["out"].astype(np.float32).reshape(M, N)
+    assert np.all(np.abs(got.astype(np.float32) - e) <= 8e-3 + 1.2e-2 * np.abs(e))
+    assert_f16_gemm_close(got, g["out"].reshape(M, N))
+
+
+@pytest.mark.parametrize("name", ["gemm_f16_nt_256x512", "gemm_f16_nt_192x320"])
+def test_f16_gemm_multi_tile_golden(hx, name):
+    g = golden(name)
+    assert_f16_gemm_close(hx.gemm_f16_nt(g["A"], g["Bt"]), g["out"])
+
+
+F16_SHAPES = [(1, 1, 1), (7, 300, 24), (129, 257, 130), (256, 512, 1024), (384, 128, 64),
+              (300, 520, 1000), (128, 256, 8192), (1000, 40, 77)]
+
+
+@pytest.mark.parametrize("M,N,K", F16_SHAPES)
+def test_f16_gemm_random(hx, oracle, M, N, K):
+    rng = np.random.default_rng(M * 13 + N + K * 3)
+    A = (rng.standard_normal((M, K)) / np.sqrt(K)).astype(np.float16)
+    Bt = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float16)
+    assert_f16_gemm_close(hx.gemm_f16_nt(A, Bt), oracle.gemm_f16_nt(A, Bt))
+    B = np.ascontiguousarray(Bt.T)
+    assert_f16_gemm_close(hx.gemm_f16_nn(A, B), oracle.gemm_f16_nn(A, B))
+
+
+# ------------------------------------------------- benchmark configurations
+
+@pytest.mark.slow
+def test_u8s8_benchmark_shape(hx, oracle):
+    """u8 x s8 GEMM M=16384, N=K=8192 (zpA 128, bias N(0,1000), per-channel
+    mult/shift, zp_out 128): full GPU run, 48 sampled rows bit-exact vs the
+    oracle, output spread over the u8 range."""
+    M, N, K = 16384, 8192, 8192
+    rng = np.random.default_rng(0)
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    bias = np.round(rng.normal(0, 1000, N)).astype(np.int32)
+    mult = rng.integers(2**30, 2**31, N, dtype=np.int64).astype(np.int32)
+    shift = np.full(N, 44, np.int32)
+    got = hx.gemm_u8s8_pc(A, B, bias, 128, mult, shift, 128)
+    rows = np.sort(rng.choice(M, 48, replace=False))
+    exp = oracle.gemm_u8s8_pc(A[rows], B, bias, 128, mult, shift, 128)
+    np.testing.assert_array_equal(got[rows], exp)
+    assert 20 < got.std() < 100
+
+
+@pytest.mark.slow
+def test_f16_benchmark_shape(hx, oracle):
+    """fp16 GEMM M=N=K=8192, A row-major, B column-major, N(0,1)/sqrt(K)."""
+    M = N = K = 8192
+    rng = np.random.default_rng(0)
+    A = (rng.standard_normal((M, K), dtype=np.float32) / np.sqrt(K)).astype(np.float16)
+    Bt = (rng.standard_normal((N, K), dtype=np.float32) / np.sqrt(K)).astype(np.float16)
+    got = hx.gemm_f16_nt(A, Bt)
+    rows = np.sort(rng.choice(M, 24, replace=False))
+    assert_f16_gemm_close(got[rows], oracle.gemm_f16_nt(A[rows], Bt))

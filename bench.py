@@ -593,7 +593,11 @@ def run_ours(args, dist):
     torch.cuda.set_device(dist.local)
     lib = _lib.load()
     ops.init_devices([dist.local])
-    device.bind_stream(0)
+    # one dedicated stream carries both torch's work and libhexcuda's launches,
+    # so the CUDA events recorded on it bracket exactly the timed kernels
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    device.bind_stream(0, stream)
     peaks = load_peaks()
     traffic = load_traffic()
 

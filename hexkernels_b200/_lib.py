@@ -39,6 +39,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_sync": (I, [I]),
     "hexcuda_stream": (P, [I]),
     "hexcuda_set_stream": (I, [I, P]),
+    "hexcuda_reset_stream": (I, [I]),
     "hexcuda_last_error": (I, []),
     "hexcuda_last_error_string": (C.c_char_p, []),
     "hexcuda_set_timing": (I, [I]),

@@ -281,21 +281,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------- epilogue warps 2..5: TMEM lane quarter = warp % 4
+        // Every decision below is warp-uniform (__all_sync / __any_sync), so
+        // the .sync.aligned TMEM loads always run with the full warp.
         const int q = warp & 3;
         int local = 0;
-        for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, local++) {
+        for (int t = blockIdx.x; t < num_tiles && !__any_sync(0xffffffffu, *abort_flag);
+             t += gridDim.x, local++) {
             int mb, nb;
             tile_coords(t, args.tiles_m, args.tiles_n, mb, nb);
             const int buf = local & 1;
             const uint32_t aphase = (local >> 1) & 1;
-            if (!tc::mbar_wait(&tfull[buf], aphase, abort_flag, args.err_word, kErrWaitAccum))
-                break;
+            const bool ok =
+                tc::mbar_wait(&tfull[buf], aphase, abort_flag, args.err_word, kErrWaitAccum);
+            if (!__all_sync(0xffffffffu, ok)) break;
             tc::tc_fence_after();
             const int row = mb * kBM + q * 32 + lane;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 uint32_t r[32];
+                __syncwarp();
                 tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
                 tc::tmem_ld_wait();
                 epilogue_chunk<EPI>(args.epi, r, row, nb * BN + c);

@@ -295,7 +295,14 @@ HX_EXPORT void *hexcuda_stream(int dev) {
 HX_EXPORT int hexcuda_set_stream(int dev, void *stream) {
     Dev *d = get_dev(dev);
     if (!d) return g_last_err;
-    d->stream = stream ? (cudaStream_t)stream : d->own_stream;
+    d->stream = (cudaStream_t)stream;
+    return HEXCUDA_OK;
+}
+
+HX_EXPORT int hexcuda_reset_stream(int dev) {
+    Dev *d = get_dev(dev);
+    if (!d) return g_last_err;
+    d->stream = d->own_stream;
     return HEXCUDA_OK;
 }
 

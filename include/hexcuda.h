@@ -67,10 +67,13 @@ int hexcuda_memset(int dev, void *dst, int value, size_t bytes);       /* async 
 /* Waits for the device's stream, then checks the device watchdog word.
  * dev < 0: every initialised device. */
 int hexcuda_sync(int dev);
-/* The device's launch stream (a cudaStream_t).  Replace it with a caller's
- * stream, e.g. the one a framework is using (NULL restores the own stream). */
+/* The device's launch stream (a cudaStream_t).  hexcuda_set_stream installs a
+ * caller's stream, e.g. the one a framework is using, as given (NULL is CUDA's
+ * legacy default stream); hexcuda_reset_stream returns to libhexcuda's own
+ * non-blocking stream. */
 void *hexcuda_stream(int dev);
 int hexcuda_set_stream(int dev, void *stream);
+int hexcuda_reset_stream(int dev);
 
 int hexcuda_last_error(void);
 const char *hexcuda_last_error_string(void);

@@ -62,7 +62,7 @@ def load_traffic():
 
 
 class ClockSampler:
-    """Polls NVML (SM clock, clock-event reasons) every 20 ms in a thread."""
+    """Polls NVML (SM clock, clock-event reasons) every 2 ms in a thread."""
 
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
@@ -90,7 +90,7 @@ class ClockSampler:
                 self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
             except Exception:
                 pass
-            time.sleep(0.02)
+            time.sleep(0.002)
 
     def __enter__(self):
         if self.ok:
@@ -123,6 +123,7 @@ class Dist:
             raise SystemExit(f"--gpus {gpus} needs torchrun with {gpus} processes")
 
     def init(self, backend: str):
+        self.backend = backend
         if self.world > 1:
             import datetime
 
@@ -140,7 +141,8 @@ class Dist:
             return v
         import torch
         import torch.distributed as dist
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dev = "cuda" if self.backend == "nccl" else "cpu"
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 

@@ -63,6 +63,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_gemm_f16_nn": (I, [I, P, P, P, I, I, I]),
     "hexcuda_attn_f16": (I, [I, P, P, P, P, I, I, I, I, F, I]),
     "hexcuda_online_softmax_step_f16": (I, [I, P, P, P, P, P, I, I]),
+    "hexcuda_selftest_watchdog": (I, [I, C.c_uint32]),
     # host-pointer entries
     "hexcuda_host_softmax_f32": (I, [P, P, I, I]),
     "hexcuda_host_softmax_f16": (I, [P, P, I, I]),

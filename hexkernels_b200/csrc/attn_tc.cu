@@ -1,15 +1,510 @@
-// attn_tc.cu -- tcgen05 flash-attention path (placeholder: shapes are routed
-// to the CUDA-core path in attn.cu until this kernel is enabled).
+// attn_tc.cu -- fp16 flash attention on the 5th-generation tensor cores.
+//
+// O = softmax(scale * Q K^T [causal: key j <= query i]) V per head, fp32
+// scores and softmax statistics, fp16 P and O (the recurrence of
+// kernels/expert/fp16_flash_attention_tile/kernel_api.h:12-27).
+//
+// Work item = (head, 128-query tile); items are walked heaviest first (the
+// causal triangle makes late query tiles the longest) by a persistent grid of
+// one CTA per SM.  Per CTA, 192 threads:
+//   warp 0      TMA: Q tile once per item; K and V tiles (128 keys x D) into
+//               two 2-stage rings, 128-byte swizzle, one box per 64 columns;
+//   warp 1      TMEM owner (512 columns: S0, S1, O) and MMA issuer:
+//                 S[j%2] = Q K_j^T      (M=128, N=128, K=D; K-major operands)
+//                 O     += P_j V_j      (M=128, N=D, K=128; V is MN-major)
+//               issuing S_{j+1} before O += P_j V_j, so the next score tile is
+//               computed while the softmax warps work on the current one;
+//   warps 2..5  softmax, one query row per thread (TMEM lane = row): load S_j,
+//               mask, row max, P = 2^(s*scale*log2e - m) with the MUFU ex2,
+//               running row sum in fp32, P as fp16 into shared memory (the
+//               A operand of the P V MMA), then the epilogue O / l.
+// The running max is only moved when it grows by more than 8 (log2 units):
+// P <= 2^8 stays exact enough in fp16 and O (in TMEM) is rescaled rarely;
+// O and l always share the same reference max, so the result is exact
+// softmax.  A rescale waits for the previous P V MMA, then loads, scales and
+// stores O in TMEM.
+//
+// Every mbarrier wait is bounded; on expiry the kernel records the device
+// error word, lets every role leave its loop, drains its own TMA loads and
+// MMAs and frees TMEM.
+#include <cuda.h>
 #include <cuda_fp16.h>
+#include <math.h>
 
 #include "hx_internal.h"
+#include "tc_common.cuh"
 
 namespace hx {
+namespace {
 
-int attn_tc_launch(Dev *, const __half *, const __half *, const __half *, __half *, int, int, int,
-                   int, float, int, bool *handled) {
-    *handled = false;
+constexpr int kAT = 192;          // threads
+constexpr int kTQ = 128;          // queries per tile
+constexpr int kTK = 128;          // keys per tile
+constexpr int kSub = 128 * 128;   // one 64-column fp16 sub-tile: 128 rows x 128 B
+
+template <int D>
+struct AttnSmem {
+    static constexpr int kTile = 128 * D * 2;
+    static constexpr int kQ = 0;
+    static constexpr int kK = kQ + kTile;          // 2 stages
+    static constexpr int kV = kK + 2 * kTile;      // 2 stages
+    static constexpr int kP = kV + 2 * kTile;      // 128 x 128 fp16
+    static constexpr int kBar = kP + kTQ * kTK * 2;
+    // q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2],
+    // s_full[2], s_empty[2], p_full, pv_done, o_free, drain
+    static constexpr int kNumBars = 20;
+    static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
+};
+
+struct AttnArgs {
+    int BH, SQ, SK, nq, nitems;
+    float scale_log2;   // scale * log2(e)
+    int causal;
+    __half *O;
+    int *err_word;
+};
+
+// Items are walked in groups of kHeadGroup heads: inside a group the last
+// (heaviest, for causal) query tiles of all its heads come first, then the
+// next query tile of each head, and so on.  The CTAs in flight therefore work
+// on a handful of heads at a time, so each head's K and V (2 MiB at S=4096,
+// D=128) are read from DRAM once and then served from L2 to all of that
+// head's query tiles, while heavy-first order inside the group keeps the
+// causal triangle balanced across CTAs.
+constexpr int kHeadGroup = 8;
+
+__device__ __forceinline__ void item_coords(int w, const AttnArgs &a, int &h, int &qt, int &nkv) {
+    const int per_group = kHeadGroup * a.nq;
+    const int group = w / per_group;
+    const int first_h = group * kHeadGroup;
+    const int gs = min(kHeadGroup, a.BH - first_h);
+    const int r = w - group * per_group;
+    qt = a.nq - 1 - r / gs;
+    h = first_h + r % gs;
+    const int nk_all = (a.SK + kTK - 1) / kTK;
+    if (a.causal) {
+        const int last_key = min(a.SK - 1, qt * kTQ + kTQ - 1);
+        nkv = last_key / kTK + 1;
+    } else {
+        nkv = nk_all;
+    }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kAT, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
+    using L = AttnSmem<D>;
+    constexpr int kSubs = D / 64;                  // 64-column sub-tiles per Q/K/V tile
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBar);
+    uint64_t *q_full = bars + 0, *q_empty = bars + 1;
+    uint64_t *k_full = bars + 2, *k_empty = bars + 4;
+    uint64_t *v_full = bars + 6, *v_empty = bars + 8;
+    uint64_t *s_full = bars + 10, *s_empty = bars + 12;
+    uint64_t *p_full = bars + 14, *pv_done = bars + 15, *o_free = bars + 16, *drain = bars + 17;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        tc::mbar_init(q_full, 1);
+        tc::mbar_init(q_empty, 1);
+        for (int s = 0; s < 2; s++) {
+            tc::mbar_init(&k_full[s], 1);
+            tc::mbar_init(&k_empty[s], 1);
+            tc::mbar_init(&v_full[s], 1);
+            tc::mbar_init(&v_empty[s], 1);
+            tc::mbar_init(&s_full[s], 1);
+            tc::mbar_init(&s_empty[s], 4);
+        }
+        tc::mbar_init(p_full, 4);
+        tc::mbar_init(pv_done, 1);
+        tc::mbar_init(o_free, 4);
+        tc::mbar_init(drain, 1);
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+        tc::tma_prefetch_desc(&tmQ);
+        tc::tma_prefetch_desc(&tmK);
+        tc::tma_prefetch_desc(&tmV);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t tmem_o = tmem_base + 256;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------------- TMA
+            uint32_t g = 0;          // global K/V tile counter
+            int item = 0;
+            uint32_t armed_q = 0, armed_k = 0, armed_v = 0;   // last armed phase + 1 (0 = never)
+            uint32_t armed_k_ph[2] = {0, 0}, armed_v_ph[2] = {0, 0};
+            for (int w = blockIdx.x; w < args.nitems && !*abort_flag; w += gridDim.x, item++) {
+                int h, qt, nkv;
+                item_coords(w, args, h, qt, nkv);
+                if (!tc::mbar_wait(q_empty, (item & 1) ^ 1, abort_flag, args.err_word, kErrWaitEmpty))
+                    break;
+                tc::mbar_arrive_expect_tx(q_full, L::kTile);
+                for (int c = 0; c < kSubs; c++)
+                    tc::tma_load_3d(smem + L::kQ + c * kSub, &tmQ, q_full, c * 64, qt * kTQ, h);
+                armed_q = (item & 1) + 1;
+                for (int j = 0; j < nkv; j++, g++) {
+                    const int st = g & 1;
+                    const uint32_t ph = (g >> 1) & 1;
+                    if (!tc::mbar_wait(&k_empty[st], ph ^ 1, abort_flag, args.err_word, kErrWaitEmpty))
+                        break;
+                    tc::mbar_arrive_expect_tx(&k_full[st], L::kTile);
+                    for (int c = 0; c < kSubs; c++)
+                        tc::tma_load_3d(smem + L::kK + st * L::kTile + c * kSub, &tmK, &k_full[st],
+                                        c * 64, j * kTK, h);
+                    armed_k |= 1u << st;
+                    armed_k_ph[st] = ph;
+                    if (!tc::mbar_wait(&v_empty[st], ph ^ 1, abort_flag, args.err_word, kErrWaitEmpty))
+                        break;
+                    tc::mbar_arrive_expect_tx(&v_full[st], L::kTile);
+                    for (int c = 0; c < kSubs; c++)
+                        tc::tma_load_3d(smem + L::kV + st * L::kTile + c * kSub, &tmV, &v_full[st],
+                                        c * 64, j * kTK, h);
+                    armed_v |= 1u << st;
+                    armed_v_ph[st] = ph;
+                }
+            }
+            // drain our own loads (a no-op when every load was consumed)
+            const uint64_t t0 = tc::globaltimer();
+            auto drain_wait = [&](uint64_t *bar, uint32_t par) {
+                while (!tc::mbar_try_wait(bar, par) && tc::globaltimer() - t0 < kWaitBudgetNs) {
+                }
+            };
+            if (armed_q) drain_wait(q_full, armed_q - 1);
+            for (int s = 0; s < 2; s++) {
+                if (armed_k & (1u << s)) drain_wait(&k_full[s], armed_k_ph[s]);
+                if (armed_v & (1u << s)) drain_wait(&v_full[s], armed_v_ph[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------------- MMA
+            constexpr uint32_t idesc_s = tc::idesc_f16_f32(kTQ, kTK, false);
+            constexpr uint32_t idesc_pv = tc::idesc_f16_f32(kTQ, D, true);
+            const uint32_t sQ = tc::smem_u32(smem + L::kQ);
+            const uint32_t sK = tc::smem_u32(smem + L::kK);
+            const uint32_t sV = tc::smem_u32(smem + L::kV);
+            const uint32_t sP = tc::smem_u32(smem + L::kP);
+            uint32_t g = 0;
+            int item = 0;
+            bool issued = false;
+            bool ok = true;
+            for (int w = blockIdx.x; w < args.nitems && ok && !*abort_flag; w += gridDim.x, item++) {
+                int h, qt, nkv;
+                item_coords(w, args, h, qt, nkv);
+                ok = tc::mbar_wait(q_full, item & 1, abort_flag, args.err_word, kErrWaitFull);
+                if (!ok) break;
+                for (int j = 0; j <= nkv && ok; j++) {
+                    if (j < nkv) {
+                        const uint32_t gj = g + j;
+                        const int st = gj & 1;
+                        const uint32_t ph = (gj >> 1) & 1;
+                        ok = tc::mbar_wait(&k_full[st], ph, abort_flag, args.err_word, kErrWaitFull) &&
+                             tc::mbar_wait(&s_empty[st], ph ^ 1, abort_flag, args.err_word,
+                                           kErrWaitAccum);
+                        if (!ok) break;
+                        tc::tc_fence_after();
+                        const uint32_t kb = sK + st * L::kTile;
+#pragma unroll
+                        for (int k = 0; k < D / 16; k++) {
+                            const uint32_t off = (k >> 2) * kSub + (k & 3) * 32;
+                            tc::mma_ss<tc::MmaKind::F16>(tmem_base + st * kTK,
+                                                         tc::sdesc_kmajor_sw128(sQ + off),
+                                                         tc::sdesc_kmajor_sw128(kb + off), idesc_s,
+                                                         k > 0 ? 1u : 0u);
+                        }
+                        issued = true;
+                        tc::mma_commit(&k_empty[st]);
+                        tc::mma_commit(&s_full[st]);
+                        if (j == nkv - 1) tc::mma_commit(q_empty);
+                    }
+                    if (j >= 1) {
+                        const int i = j - 1;
+                        const uint32_t gi = g + i;
+                        const int st = gi & 1;
+                        const uint32_t ph = (gi >> 1) & 1;
+                        ok = tc::mbar_wait(&v_full[st], ph, abort_flag, args.err_word, kErrWaitFull) &&
+                             tc::mbar_wait(p_full, gi & 1, abort_flag, args.err_word, kErrWaitFull) &&
+                             (i > 0 || tc::mbar_wait(o_free, (item & 1) ^ 1, abort_flag,
+                                                     args.err_word, kErrWaitAccum));
+                        if (!ok) break;
+                        tc::tc_fence_after();
+                        const uint32_t vb = sV + st * L::kTile;
+#pragma unroll
+                        for (int k = 0; k < kTK / 16; k++) {
+                            const uint32_t aoff = (k >> 2) * kSub + (k & 3) * 32;
+                            tc::mma_ss<tc::MmaKind::F16>(
+                                tmem_o, tc::sdesc_kmajor_sw128(sP + aoff),
+                                tc::sdesc_mnmajor_sw128(vb + k * 2048, kSub, 1024), idesc_pv,
+                                (i > 0 || k > 0) ? 1u : 0u);
+                        }
+                        tc::mma_commit(&v_empty[st]);
+                        tc::mma_commit(pv_done);
+                    }
+                }
+                g += nkv;
+            }
+            if (issued) {
+                tc::mma_commit(drain);
+                const uint64_t t0 = tc::globaltimer();
+                while (!tc::mbar_try_wait(drain, 0) && tc::globaltimer() - t0 < kWaitBudgetNs) {
+                }
+            }
+        }
+    } else {
+        // ----------------------------------------------------------- softmax
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        uint8_t *sP = smem + L::kP;
+        const uint32_t prow = (uint32_t)((row >> 3) * 1024 + (row & 7) * 128);
+        uint32_t g = 0;
+        int item = 0;
+        for (int w = blockIdx.x; w < args.nitems; w += gridDim.x, item++) {
+            if (__any_sync(0xffffffffu, *abort_flag)) break;
+            int h, qt, nkv;
+            item_coords(w, args, h, qt, nkv);
+            const int q0 = qt * kTQ;
+            const int qi = q0 + row;
+            float m_ref = -INFINITY, l = 0.0f;
+            bool ok = true;
+            for (int j = 0; j < nkv; j++) {
+                const uint32_t gj = g + j;
+                const int st = gj & 1;
+                ok = tc::mbar_wait(&s_full[st], (gj >> 1) & 1, abort_flag, args.err_word,
+                                   kErrWaitAccum);
+                if (!__all_sync(0xffffffffu, ok)) break;
+                tc::tc_fence_after();
+                uint32_t s[4][32];
+#pragma unroll
+                for (int c = 0; c < 4; c++)
+                    tc::tmem_ld_32x32b_x32(tmem_base + lane_base + st * kTK + c * 32, s[c]);
+                tc::tmem_ld_wait(s[0]);
+                tc::reg_fence(s[1]);
+                tc::reg_fence(s[2]);
+                tc::reg_fence(s[3]);
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&s_empty[st]);
+                // scale, mask, tile max
+                const int key0 = j * kTK;
+                const bool need_mask =
+                    (args.causal && key0 + kTK - 1 > q0) || key0 + kTK > args.SK;
+                float mt = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 4; c++)
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        float v = __uint_as_float(s[c][e]) * args.scale_log2;
+                        if (need_mask) {
+                            const int kk = key0 + c * 32 + e;
+                            if (kk >= args.SK || (args.causal && kk > qi)) v = -INFINITY;
+                        }
+                        s[c][e] = __float_as_uint(v);
+                        mt = fmaxf(mt, v);
+                    }
+                const float m_new = fmaxf(m_ref, mt);
+                if (j == 0) {
+                    m_ref = m_new;
+                } else {
+                    const bool need = m_new > m_ref + 8.0f;
+                    if (__any_sync(0xffffffffu, need)) {
+                        ok = tc::mbar_wait(pv_done, (gj - 1) & 1, abort_flag, args.err_word,
+                                           kErrWaitAccum);
+                        if (!__all_sync(0xffffffffu, ok)) break;
+                        tc::tc_fence_after();
+                        const float corr = need ? tc::ex2(m_ref - m_new) : 1.0f;
+#pragma unroll 1
+                        for (int c = 0; c < D / 32; c++) {
+                            uint32_t o[32];
+                            tc::tmem_ld_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                            tc::tmem_ld_wait(o);
+#pragma unroll
+                            for (int e = 0; e < 32; e++)
+                                o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+                            tc::tmem_st_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                        }
+                        tc::tmem_st_wait();
+                        if (need) {
+                            l *= corr;
+                            m_ref = m_new;
+                        }
+                    }
+                }
+                // the P buffer is free once the previous P V MMA has finished
+                if (gj >= 1) {
+                    ok = tc::mbar_wait(pv_done, (gj - 1) & 1, abort_flag, args.err_word,
+                                       kErrWaitAccum);
+                    if (!__all_sync(0xffffffffu, ok)) break;
+                }
+                // P = 2^(v - m_ref) as fp16 into the swizzled K-major tile (keys
+                // 32c..32c+31 = sub-tile c/2, 16-byte chunks 4(c%2)..+3), row
+                // sum in fp32
+                float rs = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    uint32_t p[16];
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2) {
+                        const float p0 = tc::ex2(__uint_as_float(s[c][e]) - m_ref);
+                        const float p1 = tc::ex2(__uint_as_float(s[c][e + 1]) - m_ref);
+                        rs += p0 + p1;
+                        __half2 hp = __floats2half2_rn(p0, p1);
+                        p[e / 2] = *reinterpret_cast<uint32_t *>(&hp);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int c8 = (c & 1) * 4 + u;
+                        const uint32_t off =
+                            (c >> 1) * kSub + prow + (uint32_t)(((c8 ^ (row & 7)) << 4));
+                        *reinterpret_cast<uint4 *>(sP + off) =
+                            make_uint4(p[4 * u], p[4 * u + 1], p[4 * u + 2], p[4 * u + 3]);
+                    }
+                }
+                l += rs;
+                // order the P stores (async proxy) and any O rescale (tcgen05.st)
+                // before the MMA warp's P V MMA
+                tc::fence_proxy_async_smem();
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(p_full);
+            }
+            if (!__all_sync(0xffffffffu, ok)) break;
+            // epilogue: O / l -> fp16 rows
+            const uint32_t glast = g + nkv - 1;
+            ok = tc::mbar_wait(pv_done, glast & 1, abort_flag, args.err_word, kErrWaitAccum);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc::tc_fence_after();
+            const float inv = 1.0f / l;
+            __half *orow = args.O + ((size_t)h * args.SQ + qi) * D;
+#pragma unroll 1
+            for (int c = 0; c < D / 32; c++) {
+                uint32_t o[32];
+                tc::tmem_ld_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                tc::tmem_ld_wait(o);
+                if (qi < args.SQ) {
+                    uint32_t w16[16];
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        __half2 hv = __floats2half2_rn(__uint_as_float(o[2 * e]) * inv,
+                                                       __uint_as_float(o[2 * e + 1]) * inv);
+                        w16[e] = *reinterpret_cast<uint32_t *>(&hv);
+                    }
+                    uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 32);
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        dst[e] = make_uint4(w16[4 * e], w16[4 * e + 1], w16[4 * e + 2], w16[4 * e + 3]);
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(o_free);
+            g += nkv;
+        }
+    }
+
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tc::tmem_dealloc(tmem_base, 512);
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn_attn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// [BH, S, D] fp16 as a 3D map {D, S, BH}; box 64 x 128 x 1, 128-byte swizzle.
+int make_head_map(CUtensorMap *map, const void *base, int BH, int S, int D) {
+    EncodeTiledFn fn = encode_fn_attn();
+    if (!fn) return fail(HEXCUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)BH};
+    cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)S * D * 2};
+    cuuint32_t box[3] = {64, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void *>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(HEXCUDA_ERR_CUDA, "cuTensorMapEncodeTiled (attention) failed (%d)", (int)r);
     return HEXCUDA_OK;
+}
+
+template <int D>
+int launch_attn_tc(Dev *d, const __half *Q, const __half *K, const __half *V, __half *O, int BH,
+                   int SQ, int SK, float scale, int causal) {
+    using L = AttnSmem<D>;
+    static bool attr_done[64] = {};
+    if (!attr_done[d->ordinal & 63]) {
+        if (int rc = check(cudaFuncSetAttribute(attn_tc_kernel<D>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                L::kTotal),
+                           "cudaFuncSetAttribute(attn_tc)"))
+            return rc;
+        attr_done[d->ordinal & 63] = true;
+    }
+    CUtensorMap mq, mk, mv;
+    if (int rc = make_head_map(&mq, Q, BH, SQ, D)) return rc;
+    if (int rc = make_head_map(&mk, K, BH, SK, D)) return rc;
+    if (int rc = make_head_map(&mv, V, BH, SK, D)) return rc;
+    AttnArgs a;
+    a.BH = BH;
+    a.SQ = SQ;
+    a.SK = SK;
+    a.nq = (SQ + kTQ - 1) / kTQ;
+    a.nitems = BH * a.nq;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.causal = causal;
+    a.O = O;
+    a.err_word = d->err_word;
+    const int grid = a.nitems < d->sms ? a.nitems : d->sms;
+    attn_tc_kernel<D><<<grid, kAT, L::kTotal, d->stream>>>(mq, mk, mv, a);
+    return HEXCUDA_OK;
+}
+
+}  // namespace
+
+// The tcgen05 path takes D = 64 or 128 with 16-byte aligned tensors; other
+// shapes stay on the CUDA-core kernel in attn.cu.
+int attn_tc_launch(Dev *d, const __half *Q, const __half *K, const __half *V, __half *O, int BH,
+                   int SQ, int SK, int D, float scale, int causal, bool *handled) {
+    *handled = false;
+    auto al = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
+    if (!(D == 64 || D == 128) || !al(Q) || !al(K) || !al(V) || !al(O)) return HEXCUDA_OK;
+    if ((long long)BH * ((SQ + kTQ - 1) / kTQ) > 0x7fffffffLL) return HEXCUDA_OK;
+    *handled = true;
+    return D == 128 ? launch_attn_tc<128>(d, Q, K, V, O, BH, SQ, SK, scale, causal)
+                    : launch_attn_tc<64>(d, Q, K, V, O, BH, SQ, SK, scale, causal);
 }
 
 }  // namespace hx

@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t r[32];
                 __syncwarp();
                 tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
-                tc::tmem_ld_wait();
+                tc::tmem_ld_wait(r);
                 epilogue_chunk<EPI>(args.epi, r, row, nb * BN + c);
             }
             tc::tc_fence_before();

@@ -80,6 +80,105 @@ int run_sharded(int64_t rows, void *host_out, size_t out_row_bytes,
     return HEXCUDA_OK;
 }
 
+// Pipelined variant for operators with one row-sharded input and one
+// row-sharded output (the HBM-bound row operators).  Each device's shard is
+// cut into up to kPipeChunks chunks of about 32 MiB; chunk k is copied in on
+// the device's input stream, computed on its launch stream once its copy
+// has landed (event), and copied out on its output stream once its kernel
+// has finished (event).  With pinned host memory the two copy directions and
+// the kernels of different chunks overlap.  All copies in and launches are
+// enqueued before any copy out, so an argument or launch error still leaves
+// the caller's output untouched.
+int run_rows_pipelined(int64_t rows, const void *host_in, size_t in_row_bytes, void *host_out,
+                       size_t out_row_bytes, const std::function<int(Part &)> &stage_replicated,
+                       const std::function<int(Part &, const void *, void *, int64_t)> &launch) {
+    if (!ensure_init()) return HEXCUDA_ERR_NODEV;
+    const int n = ndev();
+    std::vector<Part> parts;
+    for (int i = 0; i < n; i++) {
+        int64_t r0 = rows * i / n, r1 = rows * (i + 1) / n;
+        if (r1 > r0) parts.push_back(Part{i, nullptr, r0, r1, nullptr});
+    }
+    if (parts.empty()) return HEXCUDA_OK;
+    struct Plan {
+        uint8_t *din, *dout;
+        int64_t chunk, nchunks;
+    };
+    std::vector<Plan> plans(parts.size());
+    scope_begin();
+    int rc = HEXCUDA_OK;
+    const int64_t target = 32ll << 20;
+    for (size_t pi = 0; pi < parts.size() && !rc; pi++) {
+        Part &p = parts[pi];
+        Plan &pl = plans[pi];
+        p.d = get_dev(p.slot);
+        if (!p.d) {
+            rc = HEXCUDA_ERR_NODEV;
+            break;
+        }
+        const int64_t nr = p.r1 - p.r0;
+        pl.din = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotIn0, (size_t)nr * in_row_bytes));
+        pl.dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)nr * out_row_bytes));
+        if (!pl.din || !pl.dout) {
+            rc = hexcuda_last_error();
+            break;
+        }
+        p.dout = pl.dout;
+        int64_t chunk = std::max<int64_t>(1, target / (int64_t)std::max<size_t>(in_row_bytes, 1));
+        chunk = std::max(chunk, (nr + kPipeChunks - 1) / kPipeChunks);
+        pl.chunk = std::min(chunk, nr);
+        pl.nchunks = (nr + pl.chunk - 1) / pl.chunk;
+        // replicated operands go first on the input stream, so every chunk's
+        // input event also covers them
+        cudaStream_t launch_stream = p.d->stream;
+        p.d->stream = p.d->s_in;
+        rc = stage_replicated(p);
+        p.d->stream = launch_stream;
+        for (int64_t k = 0; k < pl.nchunks && !rc; k++) {
+            const int64_t c0 = k * pl.chunk, cn = std::min(pl.chunk, nr - c0);
+            rc = check(cudaMemcpyAsync(pl.din + c0 * in_row_bytes,
+                                       reinterpret_cast<const uint8_t *>(host_in) +
+                                           (p.r0 + c0) * in_row_bytes,
+                                       (size_t)cn * in_row_bytes, cudaMemcpyHostToDevice,
+                                       p.d->s_in),
+                       "h2d");
+            if (!rc) rc = check(cudaEventRecord(p.d->ev_in[k], p.d->s_in), "event");
+            if (!rc) rc = check(cudaStreamWaitEvent(p.d->stream, p.d->ev_in[k], 0), "wait event");
+            if (!rc) rc = launch(p, pl.din + c0 * in_row_bytes, pl.dout + c0 * out_row_bytes, cn);
+            if (!rc) rc = check(cudaEventRecord(p.d->ev_done[k], p.d->stream), "event");
+        }
+    }
+    if (!rc) {
+        for (size_t pi = 0; pi < parts.size() && !rc; pi++) {
+            Part &p = parts[pi];
+            Plan &pl = plans[pi];
+            cudaSetDevice(p.d->ordinal);
+            const int64_t nr = p.r1 - p.r0;
+            for (int64_t k = 0; k < pl.nchunks && !rc; k++) {
+                const int64_t c0 = k * pl.chunk, cn = std::min(pl.chunk, nr - c0);
+                rc = check(cudaStreamWaitEvent(p.d->s_out, p.d->ev_done[k], 0), "wait event");
+                if (!rc)
+                    rc = check(cudaMemcpyAsync(reinterpret_cast<uint8_t *>(host_out) +
+                                                   (p.r0 + c0) * out_row_bytes,
+                                               pl.dout + c0 * out_row_bytes,
+                                               (size_t)cn * out_row_bytes, cudaMemcpyDeviceToHost,
+                                               p.d->s_out),
+                               "d2h");
+            }
+        }
+    }
+    for (auto &p : parts) {
+        if (!p.d) continue;
+        cudaSetDevice(p.d->ordinal);
+        int r = check(cudaStreamSynchronize(p.d->s_in), "sync in");
+        if (!r) r = check(cudaStreamSynchronize(p.d->s_out), "sync out");
+        if (!r) r = hexcuda_sync(p.slot);
+        if (r && !rc) rc = r;
+    }
+    scope_end();
+    return rc;
+}
+
 inline int null_check(const char *name, std::initializer_list<const void *> ptrs) {
     for (const void *p : ptrs)
         if (!p) return fail(HEXCUDA_ERR_ARG, "%s: null pointer", name);
@@ -94,43 +193,42 @@ using namespace hx;
 HX_EXPORT int hexcuda_host_softmax_f32(const float *x, float *out, int R, int C) {
     if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_softmax_f32: R=%d C=%d", R, C);
     if (int rc = null_check("host_softmax_f32", {x, out})) return rc;
-    return run_sharded(R, out, sizeof(float) * (size_t)C, [&](Part &p) {
-        int64_t nr = p.r1 - p.r0;
-        const float *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
-        float *dout = reinterpret_cast<float *>(scratch(p.d, kSlotOut, sizeof(float) * nr * C));
-        if (!dx || !dout) return hexcuda_last_error();
-        p.dout = dout;
-        return hexcuda_softmax_f32(p.slot, dx, dout, (int)nr, C);
-    });
+    const size_t rb = sizeof(float) * (size_t)C;
+    return run_rows_pipelined(
+        R, x, rb, out, rb, [](Part &) { return HEXCUDA_OK; },
+        [&](Part &p, const void *din, void *dout, int64_t nr) {
+            return hexcuda_softmax_f32(p.slot, (const float *)din, (float *)dout, (int)nr, C);
+        });
 }
 
 HX_EXPORT int hexcuda_host_softmax_f16(const uint16_t *x, uint16_t *out, int R, int C) {
     if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_softmax_f16: R=%d C=%d", R, C);
     if (int rc = null_check("host_softmax_f16", {x, out})) return rc;
-    return run_sharded(R, out, 2 * (size_t)C, [&](Part &p) {
-        int64_t nr = p.r1 - p.r0;
-        const uint16_t *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
-        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * nr * C));
-        if (!dx || !dout) return hexcuda_last_error();
-        p.dout = dout;
-        return hexcuda_softmax_f16(p.slot, dx, dout, (int)nr, C);
-    });
+    const size_t rb = 2 * (size_t)C;
+    return run_rows_pipelined(
+        R, x, rb, out, rb, [](Part &) { return HEXCUDA_OK; },
+        [&](Part &p, const void *din, void *dout, int64_t nr) {
+            return hexcuda_softmax_f16(p.slot, (const uint16_t *)din, (uint16_t *)dout, (int)nr, C);
+        });
 }
 
 HX_EXPORT int hexcuda_host_layernorm_f32(const float *x, const float *gamma, const float *beta,
                                          float *out, int R, int C, float eps) {
     if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_layernorm_f32: R=%d C=%d", R, C);
     if (int rc = null_check("host_layernorm_f32", {x, gamma, beta, out})) return rc;
-    return run_sharded(R, out, sizeof(float) * (size_t)C, [&](Part &p) {
-        int64_t nr = p.r1 - p.r0;
-        const float *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
-        const float *dg = stage_in(p.d, kSlotIn1, gamma, (size_t)C);
-        const float *db = stage_in(p.d, kSlotIn2, beta, (size_t)C);
-        float *dout = reinterpret_cast<float *>(scratch(p.d, kSlotOut, sizeof(float) * nr * C));
-        if (!dx || !dg || !db || !dout) return hexcuda_last_error();
-        p.dout = dout;
-        return hexcuda_layernorm_f32(p.slot, dx, dg, db, dout, (int)nr, C, eps);
-    });
+    const size_t rb = sizeof(float) * (size_t)C;
+    std::vector<const float *> dg(ndev()), db(ndev());
+    return run_rows_pipelined(
+        R, x, rb, out, rb,
+        [&](Part &p) {
+            dg[p.slot] = stage_in(p.d, kSlotIn1, gamma, (size_t)C);
+            db[p.slot] = stage_in(p.d, kSlotIn2, beta, (size_t)C);
+            return (dg[p.slot] && db[p.slot]) ? HEXCUDA_OK : hexcuda_last_error();
+        },
+        [&](Part &p, const void *din, void *dout, int64_t nr) {
+            return hexcuda_layernorm_f32(p.slot, (const float *)din, dg[p.slot], db[p.slot],
+                                         (float *)dout, (int)nr, C, eps);
+        });
 }
 
 HX_EXPORT int hexcuda_host_layernorm_f16(const uint16_t *x, const uint16_t *gamma,
@@ -168,14 +266,11 @@ HX_EXPORT int hexcuda_host_rmsnorm_f16(const uint16_t *x, const uint16_t *gamma,
 HX_EXPORT int hexcuda_host_rowreduce_f32(const float *x, float *out, int R, int C, int op) {
     if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_rowreduce_f32: R=%d C=%d", R, C);
     if (int rc = null_check("host_rowreduce_f32", {x, out})) return rc;
-    return run_sharded(R, out, sizeof(float), [&](Part &p) {
-        int64_t nr = p.r1 - p.r0;
-        const float *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
-        float *dout = reinterpret_cast<float *>(scratch(p.d, kSlotOut, sizeof(float) * nr));
-        if (!dx || !dout) return hexcuda_last_error();
-        p.dout = dout;
-        return hexcuda_rowreduce_f32(p.slot, dx, dout, (int)nr, C, op);
-    });
+    return run_rows_pipelined(
+        R, x, sizeof(float) * (size_t)C, out, sizeof(float), [](Part &) { return HEXCUDA_OK; },
+        [&](Part &p, const void *din, void *dout, int64_t nr) {
+            return hexcuda_rowreduce_f32(p.slot, (const float *)din, (float *)dout, (int)nr, C, op);
+        });
 }
 
 HX_EXPORT int hexcuda_host_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
@@ -200,13 +295,23 @@ HX_EXPORT int hexcuda_host_requantize_i32_u8(const int32_t *a, uint8_t *out, int
     if (n < 0) return fail(HEXCUDA_ERR_ARG, "host_requantize_i32_u8: n=%lld", (long long)n);
     if (n == 0) return HEXCUDA_OK;
     if (int rc = null_check("host_requantize_i32_u8", {a, out})) return rc;
-    return run_sharded(n, out, 1, [&](Part &p) {
-        int64_t nr = p.r1 - p.r0;
-        const int32_t *da = stage_in(p.d, kSlotIn0, a + p.r0, (size_t)nr);
-        uint8_t *dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)nr));
+    // rows of 4096 elements (the last one ragged) keep every chunk 16-byte aligned
+    const int64_t rowlen = 4096, full = n / rowlen, tail = n - full * rowlen;
+    int rc = HEXCUDA_OK;
+    if (full > 0)
+        rc = run_rows_pipelined(
+            full, a, 4 * rowlen, out, rowlen, [](Part &) { return HEXCUDA_OK; },
+            [&](Part &p, const void *din, void *dout, int64_t nr) {
+                return hexcuda_requantize_i32_u8(p.slot, (const int32_t *)din, (uint8_t *)dout,
+                                                 nr * rowlen, mult, shift, zp);
+            });
+    if (rc || tail == 0) return rc;
+    return run_sharded(1, out + full * rowlen, (size_t)tail, [&](Part &p) {
+        const int32_t *da = stage_in(p.d, kSlotIn0, a + full * rowlen, (size_t)tail);
+        uint8_t *dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)tail));
         if (!da || !dout) return hexcuda_last_error();
         p.dout = dout;
-        return hexcuda_requantize_i32_u8(p.slot, da, dout, nr, mult, shift, zp);
+        return hexcuda_requantize_i32_u8(p.slot, da, dout, tail, mult, shift, zp);
     });
 }
 

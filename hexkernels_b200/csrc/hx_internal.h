@@ -12,6 +12,7 @@
 namespace hx {
 
 constexpr int kScratchSlots = 16;
+constexpr int kPipeChunks = 64;     // max chunks in flight per pipelined host call
 
 // Per-device state.  `stream` is where every launcher enqueues work; it is the
 // device's own non-blocking stream unless a caller installed another one.
@@ -24,6 +25,9 @@ struct Dev {
     bool ev0_recorded = false;          // ev0 marks the start of the timed scope
     bool timed = false;                 // ev0/ev1 bracket the last launch(es)
     int *err_word = nullptr;            // device watchdog word (0 = ok)
+    // copy streams and per-chunk events of the pipelined host entries
+    cudaStream_t s_in = nullptr, s_out = nullptr;
+    cudaEvent_t ev_in[kPipeChunks] = {}, ev_done[kPipeChunks] = {};
     void *slot_ptr[kScratchSlots] = {};
     size_t slot_bytes[kScratchSlots] = {};
 };

@@ -41,10 +41,17 @@ static void release_all() {
     for (auto &d : g_devs) {
         if (d.ordinal < 0) continue;
         cudaSetDevice(d.ordinal);
-        cudaStreamSynchronize(d.stream ? d.stream : d.own_stream);
+        cudaStreamSynchronize(d.stream);
+        cudaStreamSynchronize(d.own_stream);
         for (int s = 0; s < kScratchSlots; s++)
             if (d.slot_ptr[s]) cudaFree(d.slot_ptr[s]);
         if (d.err_word) cudaFree(d.err_word);
+        for (int k = 0; k < kPipeChunks; k++) {
+            if (d.ev_in[k]) cudaEventDestroy(d.ev_in[k]);
+            if (d.ev_done[k]) cudaEventDestroy(d.ev_done[k]);
+        }
+        if (d.s_in) cudaStreamDestroy(d.s_in);
+        if (d.s_out) cudaStreamDestroy(d.s_out);
         if (d.ev0) cudaEventDestroy(d.ev0);
         if (d.ev1) cudaEventDestroy(d.ev1);
         if (d.own_stream) cudaStreamDestroy(d.own_stream);
@@ -86,6 +93,14 @@ static int init_list(const int *devs, int n) {
         d.stream = d.own_stream;
         if (!rc) rc = check(cudaEventCreate(&d.ev0), "cudaEventCreate");
         if (!rc) rc = check(cudaEventCreate(&d.ev1), "cudaEventCreate");
+        if (!rc) rc = check(cudaStreamCreateWithFlags(&d.s_in, cudaStreamNonBlocking),
+                            "cudaStreamCreate(in)");
+        if (!rc) rc = check(cudaStreamCreateWithFlags(&d.s_out, cudaStreamNonBlocking),
+                            "cudaStreamCreate(out)");
+        for (int k = 0; k < kPipeChunks && !rc; k++) {
+            rc = check(cudaEventCreateWithFlags(&d.ev_in[k], cudaEventDisableTiming), "event");
+            if (!rc) rc = check(cudaEventCreateWithFlags(&d.ev_done[k], cudaEventDisableTiming), "event");
+        }
         if (!rc) rc = check(cudaMalloc(&d.err_word, 256), "cudaMalloc(err_word)");
         if (!rc) rc = check(cudaMemset(d.err_word, 0, 256), "cudaMemset(err_word)");
         if (rc) {

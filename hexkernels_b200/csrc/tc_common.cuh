@@ -63,13 +63,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // role of the CTA; on its own expiry it ORs `code` into the device error word
 // and raises *abort.  Returns true when the phase completed.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                          int *err_word, int code) {
+                                          int *err_word, int code,
+                                          uint64_t budget_ns = kWaitBudgetNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort) return false;
-        if (globaltimer() - t0 > kWaitBudgetNs) {
+        if (globaltimer() - t0 > budget_ns) {
             atomicOr(err_word, code);
             *abort = 1;
             return false;
@@ -168,6 +169,49 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// Wait for outstanding TMEM loads and tie `r` to the wait, so the compiler
+// cannot move any use of the loaded registers above it.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+// Ordering point for registers filled by a TMEM load that an earlier
+// tmem_ld_wait already completed.
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
+    asm volatile("" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+
+// Store 32 lanes x 32 consecutive 32-bit columns (inverse of the load above).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Generic-proxy shared-memory writes made visible to the async proxy (the
+// tensor cores reading an operand the threads just stored).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Hardware base-2 exponential (MUFU), ftz; exp2(-inf) = +0.
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // K-major operand tile staged by TMA with 128-byte swizzle: rows of 128 bytes,
 // 8-row (1024 B) swizzle atoms stacked along M/N at stride 1024 B.  The k-th
@@ -182,9 +226,24 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
     return d;
 }
 
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+// MN-major operand tile with 128-byte swizzle: atoms of 8 K-rows x 128 bytes
+// (64 fp16 along M/N); consecutive 8-row K groups `sbo` bytes apart,
+// consecutive 128-byte M/N chunks `lbo` bytes apart.
+__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t lbo,
+                                                         uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major = false) {
     return (1u << 4)                          // D = f32
            | (0u << 7) | (0u << 10)           // A, B = f16
+           | ((b_mn_major ? 1u : 0u) << 16)   // B major-ness
            | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 __host__ __device__ constexpr uint32_t idesc_i8_s32(int M, int N, bool a_signed, bool b_signed) {

@@ -171,6 +171,14 @@ int hexcuda_online_softmax_step_f16(int dev, const uint16_t *scores,
                                     uint16_t *running_sum, uint16_t *acc,
                                     int BLK, int D);
 
+/* ------------------------------------------------------------ diagnostics */
+/* Launch a one-CTA kernel whose bounded wait can never be satisfied: it gives
+ * up after budget_ms (1..2000), sets the device watchdog word and returns, so
+ * the next hexcuda_sync(dev) returns HEXCUDA_ERR_TIMEOUT and the device stays
+ * usable.  Exercises the failure path of every tcgen05 kernel's waits without
+ * faulting or hanging the GPU. */
+int hexcuda_selftest_watchdog(int dev, uint32_t budget_ms);
+
 /* ------------------------------------------------- host-pointer entries */
 /* Same operators on HOST buffers (pageable or pinned).  Rows (M, R, or B*H
  * heads) are split into contiguous shards over the initialised devices;

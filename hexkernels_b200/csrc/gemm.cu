@@ -616,3 +616,4 @@ HX_EXPORT int hexcuda_gemm_u8s8_pc(int dev, const uint8_t *A, const int8_t *B, c
     return run_gemm<MmaKind::I8, kEpiRequant, false, true>(dev, A, K, B, false, M, N, K, ep,
                                                            zpA != 0, "gemm_u8s8_pc");
 }
+

@@ -617,3 +617,115 @@ HX_EXPORT int hexcuda_gemm_u8s8_pc(int dev, const uint8_t *A, const int8_t *B, c
                                                            zpA != 0, "gemm_u8s8_pc");
 }
 
+// ------------------------------------------------ no-allocation u8 x s8 GEMM
+//
+// hexcuda_gemm_u8s8_pc_noalloc: the u8 x s8 per-channel GEMM for callers that
+// must not have the library allocate device memory -- a runtime that reserved
+// the GPU's memory up front for its own arena, where a library cudaMalloc
+// would fail or fragment it, or a latency-bound caller that cannot take the
+// implicit device synchronisation of cudaMalloc / cudaFree.  The regular entry
+// keeps its K-major copy of B and the column sums in grow-only scratch it
+// allocates on first use; this one uses a fixed region compiled into the
+// library instead (every GPU that loads libhexcuda holds it until exit):
+//   g_na_bt      K-major copy of B, at most kNoAllocBtBytes bytes
+//                (round_up(K, 128) * N <= 16 MiB);
+//   g_na_colsum  column sums of B, N <= kNoAllocMaxN.
+// A is read in place, so its rows must start on 16 bytes (K % 16 == 0, K >= 128).
+// Larger or unaligned problems are rejected with HEXCUDA_ERR_ARG.
+namespace hx {
+namespace {
+
+constexpr size_t kNoAllocBtBytes = 16u << 20;
+constexpr int kNoAllocMaxN = 16384;
+
+static __device__ __align__(256) uint8_t g_na_bt[kNoAllocBtBytes];
+static __device__ __align__(256) int32_t g_na_colsum[kNoAllocMaxN];
+
+struct NoAllocPtrs {
+    bool ready = false;
+    uint8_t *bt = nullptr;
+    int32_t *colsum = nullptr;
+};
+
+// Device addresses of the fixed region on device `d` (current).  In host code
+// the arrays' names are host-side stand-ins, not device addresses; the real
+// addresses come from cudaGetSymbolAddress, queried once per device.
+int noalloc_ptrs(Dev *d, NoAllocPtrs **out) {
+    static NoAllocPtrs per_dev[64];
+    NoAllocPtrs &p = per_dev[d->ordinal & 63];
+    if (!p.ready) {
+        if (int rc = check(cudaGetSymbolAddress(reinterpret_cast<void **>(&p.bt), g_na_bt),
+                           "cudaGetSymbolAddress(g_na_bt)"))
+            return rc;
+        if (int rc = check(cudaGetSymbolAddress(reinterpret_cast<void **>(&p.colsum), g_na_colsum),
+                           "cudaGetSymbolAddress(g_na_colsum)"))
+            return rc;
+        p.ready = true;
+    }
+    *out = &p;
+    return HEXCUDA_OK;
+}
+
+}  // namespace
+}  // namespace hx
+
+HX_EXPORT int hexcuda_gemm_u8s8_pc_noalloc(int dev, const uint8_t *A, const int8_t *B,
+                                           const int32_t *bias, uint8_t *out, int M, int N, int K,
+                                           int32_t zpA, const int32_t *mult, const int *shift,
+                                           uint8_t zp_out) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (M < 0 || N < 0 || K < 0)
+        return fail(HEXCUDA_ERR_ARG, "gemm_u8s8_pc_noalloc: bad shape %dx%dx%d", M, N, K);
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (!A || !B || !bias || !mult || !shift || !out)
+        return fail(HEXCUDA_ERR_ARG, "gemm_u8s8_pc_noalloc: null pointer");
+    const int64_t Kp = round_up(K, kBKBytes);
+    if (N > kNoAllocMaxN || Kp * (int64_t)N > (int64_t)kNoAllocBtBytes)
+        return fail(HEXCUDA_ERR_ARG,
+                    "gemm_u8s8_pc_noalloc: N=%d K=%d exceeds the fixed scratch (N <= %d, "
+                    "round_up(K,128)*N <= %zu bytes); use hexcuda_gemm_u8s8_pc",
+                    N, K, kNoAllocMaxN, kNoAllocBtBytes);
+    if (K < kBKBytes || (K % 16) != 0 || !aligned16(A))
+        return fail(HEXCUDA_ERR_ARG,
+                    "gemm_u8s8_pc_noalloc: A rows must be 16-byte aligned with K >= 128 and "
+                    "K %% 16 == 0 (K=%d)",
+                    K);
+    NoAllocPtrs *np = nullptr;
+    if (int rc = noalloc_ptrs(d, &np)) return rc;
+
+    EpiParams ep = requant_epi(out, N, 0, 0, zp_out, 0, 255);
+    ep.zpA = zpA;
+    ep.bias = bias;
+    ep.mult_pc = mult;
+    ep.shift_pc = shift;
+    ep.colsum = np->colsum;
+    ep.M = M;
+    ep.N = N;
+
+    launch_begin(d);
+    // the column sums accumulate atomically: clear them first (every call
+    // shares this region; calls that overlap on the GPU race on it)
+    if (int rc = check(cudaMemsetAsync(np->colsum, 0, sizeof(int32_t) * (size_t)N, d->stream),
+                       "memset colsum"))
+        return rc;
+    dim3 g((unsigned)((N + 63) / 64), (unsigned)(Kp / 64));
+    transpose_pack_kernel<uint8_t, true><<<g, 256, 0, d->stream>>>(
+        reinterpret_cast<const uint8_t *>(B), np->bt, np->colsum, K, N, N, Kp);
+    CUtensorMap ta, tb;
+    if (int rc = make_kmajor_map(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, K, kBM)) return rc;
+    int rc;
+    if (N <= 128) {
+        if ((rc = make_kmajor_map(&tb, np->bt, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Kp, N, Kp, 128)))
+            return rc;
+        rc = launch_gemm_kernel<MmaKind::I8, 128, kEpiRequant, false, true>(d, ta, tb, M, N,
+                                                                            (int)Kp, ep);
+    } else {
+        if ((rc = make_kmajor_map(&tb, np->bt, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Kp, N, Kp, 256)))
+            return rc;
+        rc = launch_gemm_kernel<MmaKind::I8, 256, kEpiRequant, false, true>(d, ta, tb, M, N,
+                                                                            (int)Kp, ep);
+    }
+    if (rc) return rc;
+    return launch_end(d, "gemm_u8s8_pc_noalloc", 2);
+}

@@ -146,6 +146,25 @@ int hexcuda_gemm_u8s8_pc(int dev, const uint8_t *A, const int8_t *B,
                          int32_t zpA, const int32_t *mult, const int *shift,
                          uint8_t zp_out);
 
+/* Same operator, for callers that cannot have the library allocate device
+ * memory (a runtime that reserved the GPU's memory for its own arena, where a
+ * library cudaMalloc would fail; a latency-bound caller that cannot take
+ * cudaMalloc's implicit synchronisation).  This entry has no counterpart in
+ * the reference; it calls no cudaMalloc / cudaFree.  Its scratch (a K-major
+ * copy of B and the column sums) is a fixed region compiled into libhexcuda
+ * that every GPU loading the library holds until exit: limits
+ * round_up(K, 128) * N <= 16 MiB and N <= 16384; A rows must be 16-byte
+ * aligned (K % 16 == 0, K >= 128).  Other shapes return HEXCUDA_ERR_ARG.
+ * The first call on a device looks up the region's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  All calls share the region and it keeps the
+ * last call's contents (the column sums are cleared on every call): calls
+ * that overlap on the GPU, from different streams, race on it. */
+int hexcuda_gemm_u8s8_pc_noalloc(int dev, const uint8_t *A, const int8_t *B,
+                                 const int32_t *bias, uint8_t *out, int M, int N,
+                                 int K, int32_t zpA, const int32_t *mult,
+                                 const int *shift, uint8_t zp_out);
+
 /* fp16 GEMM, fp32 accumulate, one fp16 rounding: out[M,N] = A[M,K] . Bt[N,K]^T
  * (B column-major).  kernels/expert/fp16_attention_qkt_hmx/kernel_api.h:4-20. */
 int hexcuda_gemm_f16_nt(int dev, const uint16_t *A, const uint16_t *Bt,

@@ -289,34 +289,38 @@ __global__ void __launch_bounds__(kAT, 1)
                                    kErrWaitAccum);
                 if (!__all_sync(0xffffffffu, ok)) break;
                 tc::tc_fence_after();
-                uint32_t s[4][32];
-#pragma unroll
-                for (int c = 0; c < 4; c++)
-                    tc::tmem_ld_32x32b_x32(tmem_base + lane_base + st * kTK + c * 32, s[c]);
-                tc::tmem_ld_wait(s[0]);
-                tc::reg_fence(s[1]);
-                tc::reg_fence(s[2]);
-                tc::reg_fence(s[3]);
-                tc::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&s_empty[st]);
-                // scale, mask, tile max
+                // Pass 1 over the score tile in TMEM: mask (diagonal / ragged
+                // tiles only) and row max on the raw scores (the scale > 0 is
+                // folded into the exponent in pass 2).  Chunks of 32 columns
+                // keep 32 score registers live; eight partial maxima keep the
+                // dependency chains short.
+                const uint32_t s_addr = tmem_base + lane_base + st * kTK;
                 const int key0 = j * kTK;
                 const bool need_mask =
                     (args.causal && key0 + kTK - 1 > q0) || key0 + kTK > args.SK;
-                float mt = -INFINITY;
-#pragma unroll
-                for (int c = 0; c < 4; c++)
+                auto mask_chunk = [&](uint32_t (&r)[32], int c) {
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
-                        float v = __uint_as_float(s[c][e]) * args.scale_log2;
-                        if (need_mask) {
-                            const int kk = key0 + c * 32 + e;
-                            if (kk >= args.SK || (args.causal && kk > qi)) v = -INFINITY;
-                        }
-                        s[c][e] = __float_as_uint(v);
-                        mt = fmaxf(mt, v);
+                        const int kk = key0 + c * 32 + e;
+                        if (kk >= args.SK || (args.causal && kk > qi))
+                            r[e] = __float_as_uint(-INFINITY);
                     }
+                };
+                float mx[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) mx[u] = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    uint32_t r[32];
+                    tc::tmem_ld_32x32b_x32(s_addr + c * 32, r);
+                    tc::tmem_ld_wait(r);
+                    if (need_mask) mask_chunk(r, c);
+#pragma unroll
+                    for (int e = 0; e < 32; e++) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(r[e]));
+                }
+                const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                       fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
+                                 args.scale_log2;
                 const float m_new = fmaxf(m_ref, mt);
                 if (j == 0) {
                     m_ref = m_new;
@@ -351,18 +355,25 @@ __global__ void __launch_bounds__(kAT, 1)
                                        kErrWaitAccum);
                     if (!__all_sync(0xffffffffu, ok)) break;
                 }
-                // P = 2^(v - m_ref) as fp16 into the swizzled K-major tile (keys
-                // 32c..32c+31 = sub-tile c/2, 16-byte chunks 4(c%2)..+3), row
-                // sum in fp32
-                float rs = 0.0f;
+                // Pass 2: P = 2^(s * scale*log2e - m_ref) as fp16 into the
+                // swizzled K-major tile (keys 32c..32c+31 = sub-tile c/2,
+                // 16-byte chunks 4(c%2)..+3), row sum in fp32.
+                float rsp[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) rsp[u] = 0.0f;
+                const float sl = args.scale_log2, msub = m_ref;
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
+                    uint32_t r[32];
+                    tc::tmem_ld_32x32b_x32(s_addr + c * 32, r);
+                    tc::tmem_ld_wait(r);
+                    if (need_mask) mask_chunk(r, c);
                     uint32_t p[16];
 #pragma unroll
                     for (int e = 0; e < 32; e += 2) {
-                        const float p0 = tc::ex2(__uint_as_float(s[c][e]) - m_ref);
-                        const float p1 = tc::ex2(__uint_as_float(s[c][e + 1]) - m_ref);
-                        rs += p0 + p1;
+                        const float p0 = tc::ex2(fmaf(__uint_as_float(r[e]), sl, -msub));
+                        const float p1 = tc::ex2(fmaf(__uint_as_float(r[e + 1]), sl, -msub));
+                        rsp[(e >> 1) & 7] += p0 + p1;
                         __half2 hp = __floats2half2_rn(p0, p1);
                         p[e / 2] = *reinterpret_cast<uint32_t *>(&hp);
                     }
@@ -375,6 +386,12 @@ __global__ void __launch_bounds__(kAT, 1)
                             make_uint4(p[4 * u], p[4 * u + 1], p[4 * u + 2], p[4 * u + 3]);
                     }
                 }
+                // the score tile has been read twice: hand its TMEM back
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&s_empty[st]);
+                const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) +
+                                 ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
                 l += rs;
                 // order the P stores (async proxy) and any O rescale (tcgen05.st)
                 // before the MMA warp's P V MMA

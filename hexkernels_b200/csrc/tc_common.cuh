@@ -58,6 +58,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Same test, letting the hardware suspend the thread for up to `hint_ns`
+// while the phase is incomplete (it resumes as soon as the phase completes),
+// so a waiting warp does not take issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.  Gives up
 // after kWaitBudgetNs of %globaltimer, or as soon as *abort is set by another
 // role of the CTA; on its own expiry it ORs `code` into the device error word
@@ -68,7 +84,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
         if (*abort) return false;
         if (globaltimer() - t0 > budget_ns) {
             atomicOr(err_word, code);
@@ -246,9 +262,11 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_maj
            | ((b_mn_major ? 1u : 0u) << 16)   // B major-ness
            | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-__host__ __device__ constexpr uint32_t idesc_i8_s32(int M, int N, bool a_signed, bool b_signed) {
+__host__ __device__ constexpr uint32_t idesc_i8_s32(int M, int N, bool a_signed, bool b_signed,
+                                                    bool b_mn_major = false) {
     return (2u << 4)                          // D = s32
            | ((a_signed ? 1u : 0u) << 7) | ((b_signed ? 1u : 0u) << 10) |
+           ((b_mn_major ? 1u : 0u) << 16) |
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 

@@ -6,7 +6,7 @@
 //
 // Work item = (head, 128-query tile); items are walked heaviest first (the
 // causal triangle makes late query tiles the longest) by a persistent grid of
-// one CTA per SM.  Per CTA, 192 threads:
+// one CTA per SM.  Per CTA, 320 threads:
 //   warp 0      TMA: Q tile once per item; K and V tiles (128 keys x D) into
 //               two 2-stage rings, 128-byte swizzle, one box per 64 columns;
 //   warp 1      TMEM owner (512 columns: S0, S1, O) and MMA issuer:
@@ -14,10 +14,11 @@
 //                 O     += P_j V_j      (M=128, N=D, K=128; V is MN-major)
 //               issuing S_{j+1} before O += P_j V_j, so the next score tile is
 //               computed while the softmax warps work on the current one;
-//   warps 2..5  softmax, one query row per thread (TMEM lane = row): load S_j,
-//               mask, row max, P = 2^(s*scale*log2e - m) with the MUFU ex2,
-//               running row sum in fp32, P as fp16 into shared memory (the
-//               A operand of the P V MMA), then the epilogue O / l.
+//   warps 2..9  softmax, one query row per thread (TMEM lane = row), two
+//               warps per row (each half of the key columns): load S_j, mask,
+//               row max, P = 2^(s*scale*log2e - m) with the MUFU ex2, row sum
+//               in fp32, P as fp16 into shared memory (the A operand of the
+//               P V MMA), then the epilogue O / l.
 // The running max is only moved when it grows by more than 8 (log2 units):
 // P <= 2^8 stays exact enough in fp16 and O (in TMEM) is rescaled rarely;
 // O and l always share the same reference max, so the result is exact
@@ -37,7 +38,7 @@
 namespace hx {
 namespace {
 
-constexpr int kAT = 192;          // threads
+constexpr int kAT = 320;          // threads: TMA, MMA, 8 softmax warps
 constexpr int kTQ = 128;          // queries per tile
 constexpr int kTK = 128;          // keys per tile
 constexpr int kSub = 128 * 128;   // one 64-column fp16 sub-tile: 128 rows x 128 B
@@ -49,10 +50,11 @@ struct AttnSmem {
     static constexpr int kK = kQ + kTile;          // 2 stages
     static constexpr int kV = kK + 2 * kTile;      // 2 stages
     static constexpr int kP = kV + 2 * kTile;      // 128 x 128 fp16
-    static constexpr int kBar = kP + kTQ * kTK * 2;
+    static constexpr int kRed = kP + kTQ * kTK * 2;        // [2][2][128] fp32 exchange
+    static constexpr int kBar = kRed + 2 * 2 * 128 * 4;
     // q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2],
-    // s_full[2], s_empty[2], p_full, pv_done, o_free, drain
-    static constexpr int kNumBars = 20;
+    // s_full[2], s_empty[2], p_full, pv_done, o_free, drain, xbar[4]
+    static constexpr int kNumBars = 24;
     static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
 };
 
@@ -105,6 +107,7 @@ __global__ void __launch_bounds__(kAT, 1)
     uint64_t *v_full = bars + 6, *v_empty = bars + 8;
     uint64_t *s_full = bars + 10, *s_empty = bars + 12;
     uint64_t *p_full = bars + 14, *pv_done = bars + 15, *o_free = bars + 16, *drain = bars + 17;
+    uint64_t *xbar = bars + 18;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -119,12 +122,13 @@ __global__ void __launch_bounds__(kAT, 1)
             tc::mbar_init(&v_full[s], 1);
             tc::mbar_init(&v_empty[s], 1);
             tc::mbar_init(&s_full[s], 1);
-            tc::mbar_init(&s_empty[s], 4);
+            tc::mbar_init(&s_empty[s], 8);     // one arrive per softmax warp
         }
-        tc::mbar_init(p_full, 4);
+        tc::mbar_init(p_full, 8);
         tc::mbar_init(pv_done, 1);
-        tc::mbar_init(o_free, 4);
+        tc::mbar_init(o_free, 8);
         tc::mbar_init(drain, 1);
+        for (int qq = 0; qq < 4; qq++) tc::mbar_init(&xbar[qq], 2);   // the pair of a lane quarter
         *abort_flag = 0;
         tc::fence_mbar_init();
         tc::tma_prefetch_desc(&tmQ);
@@ -267,13 +271,34 @@ __global__ void __launch_bounds__(kAT, 1)
         }
     } else {
         // ----------------------------------------------------------- softmax
+        // Eight warps: two per TMEM lane quarter (query rows 32q..32q+31),
+        // each owning one half of the 128 score columns (keys 64h..64h+63),
+        // the matching P sub-tile and half of the O columns.  The pair
+        // exchanges its two partial row maxima once per tile (and its two
+        // partial row sums once per item) through shared memory, handshaking
+        // on the quarter's mbarrier, so every wait stays bounded.
         const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int row = q * 32 + lane;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         uint8_t *sP = smem + L::kP;
+        float *xred = reinterpret_cast<float *>(smem + L::kRed);   // [2][2][128]
         const uint32_t prow = (uint32_t)((row >> 3) * 1024 + (row & 7) * 128);
-        uint32_t g = 0;
+        constexpr int kOCols = D / 2;                               // O columns per half
+        const uint32_t o_base = tmem_o + lane_base + half * kOCols;
+        uint32_t g = 0, xc = 0;
         int item = 0;
+        // exchange `v` with the pair warp; returns the pair's value
+        auto exchange = [&](float v, bool &okx) -> float {
+            const int b = xc & 1;
+            xred[(b * 2 + half) * 128 + row] = v;
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&xbar[q]);
+            okx = tc::mbar_wait(&xbar[q], xc & 1, abort_flag, args.err_word, kErrWaitOther);
+            const float other = xred[(b * 2 + (half ^ 1)) * 128 + row];
+            xc++;
+            return other;
+        };
         for (int w = blockIdx.x; w < args.nitems; w += gridDim.x, item++) {
             if (__any_sync(0xffffffffu, *abort_flag)) break;
             int h, qt, nkv;
@@ -289,15 +314,13 @@ __global__ void __launch_bounds__(kAT, 1)
                                    kErrWaitAccum);
                 if (!__all_sync(0xffffffffu, ok)) break;
                 tc::tc_fence_after();
-                // Pass 1 over the score tile in TMEM: mask (diagonal / ragged
-                // tiles only) and row max on the raw scores (the scale > 0 is
-                // folded into the exponent in pass 2).  Chunks of 32 columns
-                // keep 32 score registers live; eight partial maxima keep the
-                // dependency chains short.
-                const uint32_t s_addr = tmem_base + lane_base + st * kTK;
-                const int key0 = j * kTK;
+                // Pass 1 over this warp's half of the score tile in TMEM: mask
+                // (diagonal / ragged tiles only) and row max on the raw scores
+                // (the scale > 0 is folded into the exponent in pass 2).
+                const uint32_t s_addr = tmem_base + lane_base + st * kTK + half * 64;
+                const int key0 = j * kTK + half * 64;
                 const bool need_mask =
-                    (args.causal && key0 + kTK - 1 > q0) || key0 + kTK > args.SK;
+                    (args.causal && j * kTK + kTK - 1 > q0) || j * kTK + kTK > args.SK;
                 auto mask_chunk = [&](uint32_t (&r)[32], int c) {
 #pragma unroll
                     for (int e = 0; e < 32; e++) {
@@ -310,7 +333,7 @@ __global__ void __launch_bounds__(kAT, 1)
 #pragma unroll
                 for (int u = 0; u < 8; u++) mx[u] = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
+                for (int c = 0; c < 2; c++) {
                     uint32_t r[32];
                     tc::tmem_ld_32x32b_x32(s_addr + c * 32, r);
                     tc::tmem_ld_wait(r);
@@ -318,13 +341,20 @@ __global__ void __launch_bounds__(kAT, 1)
 #pragma unroll
                     for (int e = 0; e < 32; e++) mx[e & 7] = fmaxf(mx[e & 7], __uint_as_float(r[e]));
                 }
-                const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                       fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) *
-                                 args.scale_log2;
+                float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                bool okx;
+                mt = fmaxf(mt, exchange(mt, okx)) * args.scale_log2;
+                if (!__all_sync(0xffffffffu, okx)) {
+                    ok = false;
+                    break;
+                }
                 const float m_new = fmaxf(m_ref, mt);
                 if (j == 0) {
                     m_ref = m_new;
                 } else {
+                    // both warps of the pair see the same m_ref and m_new, so
+                    // they make the same rescale decision for every row
                     const bool need = m_new > m_ref + 8.0f;
                     if (__any_sync(0xffffffffu, need)) {
                         ok = tc::mbar_wait(pv_done, (gj - 1) & 1, abort_flag, args.err_word,
@@ -333,14 +363,14 @@ __global__ void __launch_bounds__(kAT, 1)
                         tc::tc_fence_after();
                         const float corr = need ? tc::ex2(m_ref - m_new) : 1.0f;
 #pragma unroll 1
-                        for (int c = 0; c < D / 32; c++) {
+                        for (int c = 0; c < kOCols / 32; c++) {
                             uint32_t o[32];
-                            tc::tmem_ld_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                            tc::tmem_ld_32x32b_x32(o_base + c * 32, o);
                             tc::tmem_ld_wait(o);
 #pragma unroll
                             for (int e = 0; e < 32; e++)
                                 o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
-                            tc::tmem_st_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                            tc::tmem_st_32x32b_x32(o_base + c * 32, o);
                         }
                         tc::tmem_st_wait();
                         if (need) {
@@ -355,15 +385,15 @@ __global__ void __launch_bounds__(kAT, 1)
                                        kErrWaitAccum);
                     if (!__all_sync(0xffffffffu, ok)) break;
                 }
-                // Pass 2: P = 2^(s * scale*log2e - m_ref) as fp16 into the
-                // swizzled K-major tile (keys 32c..32c+31 = sub-tile c/2,
-                // 16-byte chunks 4(c%2)..+3), row sum in fp32.
+                // Pass 2: P = 2^(s * scale*log2e - m_ref) as fp16 into P sub-tile
+                // `half` (swizzled K-major: keys 32c'..32c'+31 of the half are
+                // 16-byte chunks 4c'..4c'+3), partial row sum in fp32.
                 float rsp[8];
 #pragma unroll
                 for (int u = 0; u < 8; u++) rsp[u] = 0.0f;
                 const float sl = args.scale_log2, msub = m_ref;
 #pragma unroll
-                for (int c = 0; c < 4; c++) {
+                for (int c = 0; c < 2; c++) {
                     uint32_t r[32];
                     tc::tmem_ld_32x32b_x32(s_addr + c * 32, r);
                     tc::tmem_ld_wait(r);
@@ -379,9 +409,9 @@ __global__ void __launch_bounds__(kAT, 1)
                     }
 #pragma unroll
                     for (int u = 0; u < 4; u++) {
-                        const int c8 = (c & 1) * 4 + u;
+                        const int c8 = c * 4 + u;
                         const uint32_t off =
-                            (c >> 1) * kSub + prow + (uint32_t)(((c8 ^ (row & 7)) << 4));
+                            half * kSub + prow + (uint32_t)(((c8 ^ (row & 7)) << 4));
                         *reinterpret_cast<uint4 *>(sP + off) =
                             make_uint4(p[4 * u], p[4 * u + 1], p[4 * u + 2], p[4 * u + 3]);
                     }
@@ -390,9 +420,8 @@ __global__ void __launch_bounds__(kAT, 1)
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&s_empty[st]);
-                const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) +
-                                 ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-                l += rs;
+                l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) +
+                     ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
                 // order the P stores (async proxy) and any O rescale (tcgen05.st)
                 // before the MMA warp's P V MMA
                 tc::fence_proxy_async_smem();
@@ -401,17 +430,20 @@ __global__ void __launch_bounds__(kAT, 1)
                 if (lane == 0) tc::mbar_arrive(p_full);
             }
             if (!__all_sync(0xffffffffu, ok)) break;
-            // epilogue: O / l -> fp16 rows
+            // epilogue: the pair's partial row sums make l; O / l -> fp16
+            bool okx;
+            const float lt = l + exchange(l, okx);
+            if (!__all_sync(0xffffffffu, okx)) break;
             const uint32_t glast = g + nkv - 1;
             ok = tc::mbar_wait(pv_done, glast & 1, abort_flag, args.err_word, kErrWaitAccum);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc::tc_fence_after();
-            const float inv = 1.0f / l;
-            __half *orow = args.O + ((size_t)h * args.SQ + qi) * D;
+            const float inv = 1.0f / lt;
+            __half *orow = args.O + ((size_t)h * args.SQ + qi) * D + half * kOCols;
 #pragma unroll 1
-            for (int c = 0; c < D / 32; c++) {
+            for (int c = 0; c < kOCols / 32; c++) {
                 uint32_t o[32];
-                tc::tmem_ld_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                tc::tmem_ld_32x32b_x32(o_base + c * 32, o);
                 tc::tmem_ld_wait(o);
                 if (qi < args.SQ) {
                     uint32_t w16[16];

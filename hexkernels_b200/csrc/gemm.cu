@@ -147,10 +147,17 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
     }
 }
 
-template <MmaKind KIND, int BN, int EPI, bool A_SIGNED, bool B_SIGNED>
+template <MmaKind KIND, int BN, int EPI, bool A_SIGNED, bool B_SIGNED, bool B_MN = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmArgs args) {
+    // B_MN: B is read straight from its row-major [K, N] layout as an MN-major
+    // operand: per stage BN/(128/esize) boxes of (128 bytes of N) x (one K
+    // block of rows), each box a column of 128-byte swizzle atoms.
+    constexpr int kEsize = KIND == MmaKind::F16 ? 2 : 1;
+    constexpr int kKElems = kBKBytes / kEsize;          // K rows per stage
+    constexpr int kNBox = 128 / kEsize;                 // N elements per box
+    constexpr int kBoxBytes = kKElems * 128;            // one MN-major box
     using L = Smem<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -212,7 +219,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc::mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
                     const int kx = kb * (KIND == MmaKind::F16 ? kBKBytes / 2 : kBKBytes);
                     tc::tma_load_2d(sa, &tmA, &full[stage], kx, mb * kBM);
-                    tc::tma_load_2d(sb, &tmB, &full[stage], kx, nb * BN);
+                    if constexpr (B_MN) {
+#pragma unroll
+                        for (int c = 0; c < BN / kNBox; c++)
+                            tc::tma_load_2d(sb + c * kBoxBytes, &tmB, &full[stage],
+                                            nb * BN + c * kNBox, kx);
+                    } else {
+                        tc::tma_load_2d(sb, &tmB, &full[stage], kx, nb * BN);
+                    }
                     armed |= 1u << stage;
                     armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == kStages) {
@@ -235,8 +249,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // ---------------- MMA issuer
             constexpr uint32_t idesc = (KIND == MmaKind::F16)
-                                           ? tc::idesc_f16_f32(kBM, BN)
-                                           : tc::idesc_i8_s32(kBM, BN, A_SIGNED, B_SIGNED);
+                                           ? tc::idesc_f16_f32(kBM, BN, B_MN)
+                                           : tc::idesc_i8_s32(kBM, BN, A_SIGNED, B_SIGNED, B_MN);
             int stage = 0;
             uint32_t phase = 0;
             int local = 0;
@@ -259,7 +273,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int k = 0; k < kBKBytes / 32; k++) {
                         const uint64_t ad = tc::sdesc_kmajor_sw128(sa + k * 32);
-                        const uint64_t bd = tc::sdesc_kmajor_sw128(sb + k * 32);
+                        // one MMA consumes 32 bytes of K: 32 bytes of each
+                        // K-major row, or 32/esize rows of an MN-major box
+                        const uint64_t bd =
+                            B_MN ? tc::sdesc_mnmajor_sw128(sb + k * (32 / kEsize) * 128, kBoxBytes, 1024)
+                                 : tc::sdesc_kmajor_sw128(sb + k * 32);
                         tc::mma_ss<KIND>(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
                     }
                     issued = true;
@@ -378,6 +396,32 @@ __global__ void __launch_bounds__(256) pad_rows_kernel(const T *__restrict__ src
     }
 }
 
+// colsum[n] += sum_k B[k][n] for a row-major int8 B [K, N] (colsum pre-zeroed).
+// Thread = 16 consecutive columns (one 128-bit load per row) over a chunk of
+// rows; integer sums, so the atomics' order does not matter.
+__global__ void __launch_bounds__(128) colsum_kernel(const int8_t *__restrict__ B,
+                                                     int32_t *__restrict__ colsum, int K, int N,
+                                                     int kchunk, int vec) {
+    const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * 16;
+    if (n0 >= N) return;
+    const int k0 = blockIdx.y * kchunk, k1 = min(K, k0 + kchunk);
+    int32_t acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) acc[i] = 0;
+    if (vec && n0 + 16 <= N) {
+        for (int k = k0; k < k1; k++) {
+            const int4 v = __ldg(reinterpret_cast<const int4 *>(B + (size_t)k * N + n0));
+            const int w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 16; i++) acc[i] += (int32_t)(int8_t)(w[i >> 2] >> (8 * (i & 3)));
+        }
+    } else {
+        for (int k = k0; k < k1; k++)
+            for (int i = 0; i < 16 && n0 + i < N; i++) acc[i] += B[(size_t)k * N + n0 + i];
+    }
+    for (int i = 0; i < 16 && n0 + i < N; i++) atomicAdd(colsum + n0 + i, acc[i]);
+}
+
 // ------------------------------------------------------------ host side
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -417,14 +461,33 @@ int make_kmajor_map(CUtensorMap *map, const void *base, CUtensorMapDataType dt, 
     return HEXCUDA_OK;
 }
 
+// Row-major B [K, N] read as an MN-major operand: boxes of 128 bytes of N x
+// k_rows rows of K, 128-byte swizzle, zero fill out of bounds.
+int make_mnmajor_map(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int esize,
+                     int64_t N, int64_t K, int k_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(HEXCUDA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)K};
+    cuuint64_t strides[1] = {(cuuint64_t)(N * esize)};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / esize), (cuuint32_t)k_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(HEXCUDA_ERR_CUDA, "cuTensorMapEncodeTiled (MN-major B) failed (%d): N=%lld K=%lld",
+                    (int)r, (long long)N, (long long)K);
+    return HEXCUDA_OK;
+}
+
 inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
-template <MmaKind KIND, int BN, int EPI, bool AS, bool BS>
+template <MmaKind KIND, int BN, int EPI, bool AS, bool BS, bool BMN = false>
 int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K,
                        const EpiParams &ep) {
     using L = Smem<BN>;
-    auto kern = gemm_tc_kernel<KIND, BN, EPI, AS, BS>;
+    auto kern = gemm_tc_kernel<KIND, BN, EPI, AS, BS, BMN>;
     static bool attr_done[64] = {};
     const int dev_slot = d->ordinal & 63;
     if (!attr_done[dev_slot]) {
@@ -483,7 +546,18 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
                            "memset colsum"))
             return rc;
     }
-    if (!b_kmajor) {
+    // row-major B that TMA can read in place: MN-major operand, no copy
+    const bool b_mn = !b_kmajor && ((int64_t)N * esize) % 16 == 0 && aligned16(B) &&
+                      (int64_t)N * esize >= 128 && K >= kelems;
+    if (b_mn) {
+        if (want_colsum) {
+            const int kchunk = 64;
+            dim3 g((unsigned)((N + 16 * 128 - 1) / (16 * 128)), (unsigned)((K + kchunk - 1) / kchunk));
+            colsum_kernel<<<g, 128, 0, d->stream>>>(reinterpret_cast<const int8_t *>(B), colsum, K,
+                                                     N, kchunk, 1);
+            nl++;
+        }
+    } else if (!b_kmajor) {
         T *tmp = reinterpret_cast<T *>(scratch(d, 0, (size_t)N * Kp * esize));
         if (!tmp) return HEXCUDA_ERR_OOM;
         dim3 g((unsigned)((N + 63) / 64), (unsigned)(Kp / 64));
@@ -527,7 +601,13 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
     ep.N = N;
     const int kdim = (int)std::max(a_kdim, b_kdim);
     int rc;
-    if (N <= 128) {
+    if (b_mn) {
+        if ((rc = make_mnmajor_map(&tb, B, dt, esize, N, K, kelems))) return rc;
+        if (N <= 128)
+            rc = launch_gemm_kernel<KIND, 128, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep);
+        else
+            rc = launch_gemm_kernel<KIND, 256, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep);
+    } else if (N <= 128) {
         if ((rc = make_kmajor_map(&tb, bt, dt, esize, b_kdim, N, bt_pitch, 128))) return rc;
         rc = launch_gemm_kernel<KIND, 128, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep);
     } else {

@@ -2,7 +2,7 @@
 //
 // out[M,N] = epilogue( A[M,K] . B[K,N] ), A and B^T both staged K-major.
 //
-// Persistent, warp-specialised kernel, one CTA per SM (192 threads):
+// Persistent, warp-specialised kernel, one CTA per SM (320 threads):
 //   warp 0      TMA producer: 128 x 128-byte A box + BN x 128-byte B box per
 //               stage (128-byte swizzle), kStages-deep ring of full/empty
 //               mbarriers;
@@ -10,8 +10,10 @@
 //               from one elected lane, issues tcgen05.mma (M=128, N=BN, 32 B
 //               of K per instruction: K=16 f16 or K=32 int8), releasing each
 //               smem stage with tcgen05.commit;
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, apply
-//               the fp16 rounding or the fixed-point requant, store to HBM,
+//   warps 2..9  epilogue, two warps per TMEM lane quarter (one per half of
+//               the tile's columns): tcgen05.ld 32 lanes x 32 columns at a
+//               time, apply the fp16 rounding or the fixed-point requant
+//               (per-column parameters staged in shared memory), store to HBM,
 //               then hand the accumulator back to the MMA warp.
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile
 // i+1.  Tiles are walked in grouped order (kGroupM M-blocks share each
@@ -45,7 +47,7 @@ using tc::MmaKind;
 constexpr int kBM = 128;             // rows of A per tile (UMMA M)
 constexpr int kBKBytes = 128;        // K extent of one stage, in bytes
 constexpr int kStages = 4;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;      // TMA warp, MMA warp, 8 epilogue warps
 constexpr int kGroupM = 16;
 
 enum EpiKind { kEpiF16 = 0, kEpiRequant = 1 };
@@ -83,7 +85,11 @@ struct Smem {
     static constexpr int kBarOffset = kStages * kStageBytes;
     // full[S], empty[S], tfull[2], tempty[2], drain
     static constexpr int kNumBars = 2 * kStages + 5;
-    static constexpr int kTotal = kBarOffset + kNumBars * 8 + 16 + 1024;  // + align slack
+    // per epilogue warp: the requant parameters of its current 32 columns,
+    // read with 16-byte loads, so the region starts on a 128-byte boundary
+    static constexpr int kParamOffset = (kBarOffset + kNumBars * 8 + 16 + 127) / 128 * 128;
+    static constexpr int kParamBytes = 8 * 512;
+    static constexpr int kTotal = kParamOffset + kParamBytes + 1024;  // + align slack
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &mb, int &nb) {
@@ -96,11 +102,16 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
     nb = r / gsize;
 }
 
+// Requant parameters of one epilogue warp's current 32 columns.
+struct ColParams {
+    int32_t corr[32], bias[32], mult[32], shift[32];
+};
+
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32_t (&r)[32],
-                                               int row, int col0) {
-    if (row >= ep.M) return;
+                                               int row, int col0, const ColParams *cp) {
     if constexpr (EPI == kEpiF16) {
+        if (row >= ep.M) return;
         __half *o = reinterpret_cast<__half *>(ep.out) + (size_t)row * ep.ldo + col0;
         if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
             uint4 v[4];
@@ -117,26 +128,36 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = __float2half_rn(__uint_as_float(r[i]));
         }
     } else {
+        // requant: the 32 columns' parameters were staged in `cp` by this warp
         uint8_t *o = reinterpret_cast<uint8_t *>(ep.out) + (size_t)row * ep.ldo + col0;
         uint32_t w[8];
 #pragma unroll
-        for (int i = 0; i < 8; i++) w[i] = 0;
+        for (int i4 = 0; i4 < 8; i4++) {
+            const int4 c4 = *reinterpret_cast<const int4 *>(&cp->corr[4 * i4]);
+            const int4 b4 = *reinterpret_cast<const int4 *>(&cp->bias[4 * i4]);
+            const int4 m4 = *reinterpret_cast<const int4 *>(&cp->mult[4 * i4]);
+            const int4 s4 = *reinterpret_cast<const int4 *>(&cp->shift[4 * i4]);
+            const int cc[4] = {c4.x, c4.y, c4.z, c4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
+            const int mm[4] = {m4.x, m4.y, m4.z, m4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+            uint32_t packed = 0;
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-            const int j = col0 + i;
-            if (j < ep.N) {
-                uint32_t acc = r[i];
-                if (ep.colsum) acc -= (uint32_t)ep.zpA * (uint32_t)__ldg(ep.colsum + j);
-                int64_t x = (int64_t)(int32_t)acc;
-                if (ep.bias) x += __ldg(ep.bias + j);
-                const int32_t m = ep.mult_pc ? __ldg(ep.mult_pc + j) : ep.mult;
-                const int s = ep.shift_pc ? __ldg(ep.shift_pc + j) : ep.shift;
-                int64_t q = rq_round(x * (int64_t)m, s) + ep.zp;
+            for (int u = 0; u < 4; u++) {
+                // acc32 = rawdot - zpA * colsum[j] with int32 wrap, then the
+                // int64 bias add, multiply and round-half-away shift
+                const int32_t a32 = (int32_t)(r[4 * i4 + u] - (uint32_t)cc[u]);
+                const int64_t v = ((int64_t)a32 + bb[u]) * (int64_t)mm[u];
+                const int sh = ss[u];
+                const uint64_t half = sh > 0 ? (1ull << (sh - 1)) : 0ull;
+                const uint64_t av = v < 0 ? (uint64_t)(-v) : (uint64_t)v;
+                int64_t q = (int64_t)((av + half) >> sh);
+                q = (v < 0 ? -q : q) + ep.zp;
                 q = q > ep.hi ? ep.hi : q;
                 q = q < ep.lo ? ep.lo : q;
-                w[i >> 2] |= ((uint32_t)q & 0xFFu) << (8 * (i & 3));
+                packed |= ((uint32_t)q & 0xFFu) << (8 * u);
             }
+            w[i4] = packed;
         }
+        if (row >= ep.M) return;
         if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
             uint4 *dst = reinterpret_cast<uint4 *>(o);
             dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -145,6 +166,25 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = (uint8_t)(w[i >> 2] >> (8 * (i & 3)));
         }
     }
+}
+
+// Stage the requant parameters of columns col0..col0+31 (lane = column) into
+// the warp's shared-memory slice: zpA * colsum[j] (int32 wrap), bias[j],
+// mult[j], shift[j] clamped to 0..63 (the C reference is undefined beyond).
+__device__ __forceinline__ void stage_params(const EpiParams &ep, ColParams *cp, int col0,
+                                             int lane) {
+    const int j = col0 + lane;
+    int32_t c = 0, b = 0, m = ep.mult, sh = ep.shift;
+    if (j < ep.N) {
+        if (ep.colsum) c = (int32_t)((uint32_t)ep.zpA * (uint32_t)__ldg(ep.colsum + j));
+        if (ep.bias) b = __ldg(ep.bias + j);
+        if (ep.mult_pc) m = __ldg(ep.mult_pc + j);
+        if (ep.shift_pc) sh = __ldg(ep.shift_pc + j);
+    }
+    cp->corr[lane] = c;
+    cp->bias[lane] = b;
+    cp->mult[lane] = m;
+    cp->shift[lane] = sh < 0 ? 0 : (sh > 63 ? 63 : sh);
 }
 
 template <MmaKind KIND, int BN, int EPI, bool A_SIGNED, bool B_SIGNED, bool B_MN = false>
@@ -183,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; b++) {
             tc::mbar_init(&tfull[b], 1);
-            tc::mbar_init(&tempty[b], 4);   // one arrive per epilogue warp
+            tc::mbar_init(&tempty[b], 8);   // one arrive per epilogue warp
         }
         tc::mbar_init(drain, 1);
         *abort_flag = 0;
@@ -298,10 +338,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ---------------- epilogue warps 2..5: TMEM lane quarter = warp % 4
-        // Every decision below is warp-uniform (__all_sync / __any_sync), so
-        // the .sync.aligned TMEM loads always run with the full warp.
+        // ---------------- epilogue warps 2..9: TMEM lane quarter = warp % 4,
+        // column half = (warp - 2) / 4.  Every decision below is warp-uniform
+        // (__all_sync / __any_sync), so the .sync.aligned TMEM loads always run
+        // with the full warp.
         const int q = warp & 3;
+        const int chalf = (warp - 2) >> 2;
+        ColParams *cp = reinterpret_cast<ColParams *>(smem + L::kParamOffset) + (warp - 2);
         int local = 0;
         for (int t = blockIdx.x; t < num_tiles && !__any_sync(0xffffffffu, *abort_flag);
              t += gridDim.x, local++) {
@@ -316,12 +359,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int row = mb * kBM + q * 32 + lane;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
 #pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
+            for (int c = chalf * (BN / 2); c < (chalf + 1) * (BN / 2); c += 32) {
                 uint32_t r[32];
+                if constexpr (EPI == kEpiRequant) {
+                    stage_params(args.epi, cp, nb * BN + c, lane);
+                }
                 __syncwarp();
                 tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
                 tc::tmem_ld_wait(r);
-                epilogue_chunk<EPI>(args.epi, r, row, nb * BN + c);
+                epilogue_chunk<EPI>(args.epi, r, row, nb * BN + c, cp);
+                __syncwarp();
             }
             tc::tc_fence_before();
             __syncwarp();

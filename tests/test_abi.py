@@ -68,8 +68,14 @@ def test_kernel_sources_are_sm100a_native():
                    "tcgen05.alloc", "tcgen05.ld.sync.aligned", "cp.async.bulk.tensor.2d"):
         assert needle in allsrc, needle
     assert "float4" in src["rows.cu"] and "uint4" in src["rows.cu"]
-    # no TMA multicast anywhere (the package runs on several GPUs)
-    assert "multicast::cluster" not in allsrc
+    # every TMA load is one of the two plain per-CTA forms (each CTA loads its
+    # own tiles; the package runs on several GPUs)
+    allowed = {
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes",
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes",
+    }
+    forms = set(re.findall(r"cp\.async\.bulk\.tensor[\w.:]*", allsrc))
+    assert forms == allowed, forms
     # no legacy tensor-core paths
     for legacy in ("mma.sync", "wmma::", "wgmma"):
         assert legacy not in allsrc, legacy

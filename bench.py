@@ -127,8 +127,12 @@ class Dist:
         if self.world > 1:
             import datetime
 
+            import torch
             import torch.distributed as dist
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            kw = {}
+            if backend == "nccl":
+                kw["device_id"] = torch.device("cuda", self.local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
             self.pg = True
 
     def barrier(self):

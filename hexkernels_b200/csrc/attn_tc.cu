@@ -9,16 +9,18 @@
 // one CTA per SM.  Per CTA, 320 threads:
 //   warp 0      TMA: Q tile once per item; K and V tiles (128 keys x D) into
 //               two 2-stage rings, 128-byte swizzle, one box per 64 columns;
-//   warp 1      TMEM owner (512 columns: S0, S1, O) and MMA issuer:
+//   warp 1      TMEM owner (512 columns: S0, S1, O, P0, P1) and MMA issuer:
 //                 S[j%2] = Q K_j^T      (M=128, N=128, K=D; K-major operands)
-//                 O     += P_j V_j      (M=128, N=D, K=128; V is MN-major)
+//                 O     += P[j%2] V_j   (M=128, N=D, K=128; P read from TMEM,
+//                                        V is MN-major in shared memory)
 //               issuing S_{j+1} before O += P_j V_j, so the next score tile is
 //               computed while the softmax warps work on the current one;
 //   warps 2..9  softmax, one query row per thread (TMEM lane = row), two
 //               warps per row (each half of the key columns): load S_j, mask,
 //               row max, P = 2^(s*scale*log2e - m) with the MUFU ex2, row sum
-//               in fp32, P as fp16 into shared memory (the A operand of the
-//               P V MMA), then the epilogue O / l.
+//               in fp32, P as fp16 pairs into TMEM (the A operand of the
+//               P V MMA; double-buffered, so writing P_j never waits for the
+//               P V MMA of tile j-1), then the epilogue O / l.
 // The running max is only moved when it grows by more than 8 (log2 units):
 // P <= 2^8 stays exact enough in fp16 and O (in TMEM) is rescaled rarely;
 // O and l always share the same reference max, so the result is exact
@@ -49,12 +51,11 @@ struct AttnSmem {
     static constexpr int kQ = 0;
     static constexpr int kK = kQ + kTile;          // 2 stages
     static constexpr int kV = kK + 2 * kTile;      // 2 stages
-    static constexpr int kP = kV + 2 * kTile;      // 128 x 128 fp16
-    static constexpr int kRed = kP + kTQ * kTK * 2;        // [2][2][128] fp32 exchange
+    static constexpr int kRed = kV + 2 * kTile;    // [2][2][128] fp32 exchange
     static constexpr int kBar = kRed + 2 * 2 * 128 * 4;
     // q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2],
-    // s_full[2], s_empty[2], p_full, pv_done, o_free, drain, xbar[4]
-    static constexpr int kNumBars = 24;
+    // s_full[2], s_empty[2], p_full[2], pv_done[2], o_free, drain, xbar[4]
+    static constexpr int kNumBars = 26;
     static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
 };
 
@@ -106,8 +107,8 @@ __global__ void __launch_bounds__(kAT, 1)
     uint64_t *k_full = bars + 2, *k_empty = bars + 4;
     uint64_t *v_full = bars + 6, *v_empty = bars + 8;
     uint64_t *s_full = bars + 10, *s_empty = bars + 12;
-    uint64_t *p_full = bars + 14, *pv_done = bars + 15, *o_free = bars + 16, *drain = bars + 17;
-    uint64_t *xbar = bars + 18;
+    uint64_t *p_full = bars + 14, *pv_done = bars + 16, *o_free = bars + 18, *drain = bars + 19;
+    uint64_t *xbar = bars + 20;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -123,9 +124,9 @@ __global__ void __launch_bounds__(kAT, 1)
             tc::mbar_init(&v_empty[s], 1);
             tc::mbar_init(&s_full[s], 1);
             tc::mbar_init(&s_empty[s], 8);     // one arrive per softmax warp
+            tc::mbar_init(&p_full[s], 8);
+            tc::mbar_init(&pv_done[s], 1);
         }
-        tc::mbar_init(p_full, 8);
-        tc::mbar_init(pv_done, 1);
         tc::mbar_init(o_free, 8);
         tc::mbar_init(drain, 1);
         for (int qq = 0; qq < 4; qq++) tc::mbar_init(&xbar[qq], 2);   // the pair of a lane quarter
@@ -142,8 +143,11 @@ __global__ void __launch_bounds__(kAT, 1)
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
+    // TMEM columns: S0 [0,128), S1 [128,256), O [256,256+D), P0 [384,448),
+    // P1 [448,512) (P: fp16 pairs, key 2c in the low half of column c)
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t tmem_o = tmem_base + 256;
+    const uint32_t tmem_p = tmem_base + 384;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -202,7 +206,6 @@ __global__ void __launch_bounds__(kAT, 1)
             const uint32_t sQ = tc::smem_u32(smem + L::kQ);
             const uint32_t sK = tc::smem_u32(smem + L::kK);
             const uint32_t sV = tc::smem_u32(smem + L::kV);
-            const uint32_t sP = tc::smem_u32(smem + L::kP);
             uint32_t g = 0;
             int item = 0;
             bool issued = false;
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(kAT, 1)
                         const int st = gi & 1;
                         const uint32_t ph = (gi >> 1) & 1;
                         ok = tc::mbar_wait(&v_full[st], ph, abort_flag, args.err_word, kErrWaitFull) &&
-                             tc::mbar_wait(p_full, gi & 1, abort_flag, args.err_word, kErrWaitFull) &&
+                             tc::mbar_wait(&p_full[st], ph, abort_flag, args.err_word, kErrWaitFull) &&
                              (i > 0 || tc::mbar_wait(o_free, (item & 1) ^ 1, abort_flag,
                                                      args.err_word, kErrWaitAccum));
                         if (!ok) break;
@@ -250,14 +253,13 @@ __global__ void __launch_bounds__(kAT, 1)
                         const uint32_t vb = sV + st * L::kTile;
 #pragma unroll
                         for (int k = 0; k < kTK / 16; k++) {
-                            const uint32_t aoff = (k >> 2) * kSub + (k & 3) * 32;
-                            tc::mma_ss<tc::MmaKind::F16>(
-                                tmem_o, tc::sdesc_kmajor_sw128(sP + aoff),
-                                tc::sdesc_mnmajor_sw128(vb + k * 2048, kSub, 1024), idesc_pv,
-                                (i > 0 || k > 0) ? 1u : 0u);
+                            // A = P from TMEM: keys 16k..16k+15 are columns 8k..8k+7
+                            tc::mma_ts_f16(tmem_o, tmem_p + st * 64 + k * 8,
+                                           tc::sdesc_mnmajor_sw128(vb + k * 2048, kSub, 1024),
+                                           idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
                         }
                         tc::mma_commit(&v_empty[st]);
-                        tc::mma_commit(pv_done);
+                        tc::mma_commit(&pv_done[st]);
                     }
                 }
                 g += nkv;
@@ -281,9 +283,7 @@ __global__ void __launch_bounds__(kAT, 1)
         const int half = (warp - 2) >> 2;
         const int row = q * 32 + lane;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        uint8_t *sP = smem + L::kP;
         float *xred = reinterpret_cast<float *>(smem + L::kRed);   // [2][2][128]
-        const uint32_t prow = (uint32_t)((row >> 3) * 1024 + (row & 7) * 128);
         constexpr int kOCols = D / 2;                               // O columns per half
         const uint32_t o_base = tmem_o + lane_base + half * kOCols;
         uint32_t g = 0, xc = 0;
@@ -357,8 +357,9 @@ __global__ void __launch_bounds__(kAT, 1)
                     // they make the same rescale decision for every row
                     const bool need = m_new > m_ref + 8.0f;
                     if (__any_sync(0xffffffffu, need)) {
-                        ok = tc::mbar_wait(pv_done, (gj - 1) & 1, abort_flag, args.err_word,
-                                           kErrWaitAccum);
+                        const uint32_t gp = gj - 1;      // O is stable once P V of tile gp is done
+                        ok = tc::mbar_wait(&pv_done[gp & 1], (gp >> 1) & 1, abort_flag,
+                                           args.err_word, kErrWaitAccum);
                         if (!__all_sync(0xffffffffu, ok)) break;
                         tc::tc_fence_after();
                         const float corr = need ? tc::ex2(m_ref - m_new) : 1.0f;
@@ -379,55 +380,50 @@ __global__ void __launch_bounds__(kAT, 1)
                         }
                     }
                 }
-                // the P buffer is free once the previous P V MMA has finished
-                if (gj >= 1) {
-                    ok = tc::mbar_wait(pv_done, (gj - 1) & 1, abort_flag, args.err_word,
+                // P buffer st was last read by the P V MMA of tile gj - 2
+                if (gj >= 2) {
+                    const uint32_t gp = gj - 2;
+                    ok = tc::mbar_wait(&pv_done[gp & 1], (gp >> 1) & 1, abort_flag, args.err_word,
                                        kErrWaitAccum);
                     if (!__all_sync(0xffffffffu, ok)) break;
+                    tc::tc_fence_after();
                 }
-                // Pass 2: P = 2^(s * scale*log2e - m_ref) as fp16 into P sub-tile
-                // `half` (swizzled K-major: keys 32c'..32c'+31 of the half are
-                // 16-byte chunks 4c'..4c'+3), partial row sum in fp32.
+                // Pass 2: P = 2^(s * scale*log2e - m_ref) as fp16 pairs into P
+                // buffer st, columns 32*half..32*half+31 (keys 64*half + 2c and
+                // 64*half + 2c + 1 in column 32*half + c), partial row sum in fp32.
                 float rsp[8];
 #pragma unroll
                 for (int u = 0; u < 8; u++) rsp[u] = 0.0f;
                 const float sl = args.scale_log2, msub = m_ref;
+                uint32_t pk[32];
 #pragma unroll
                 for (int c = 0; c < 2; c++) {
                     uint32_t r[32];
                     tc::tmem_ld_32x32b_x32(s_addr + c * 32, r);
                     tc::tmem_ld_wait(r);
                     if (need_mask) mask_chunk(r, c);
-                    uint32_t p[16];
 #pragma unroll
                     for (int e = 0; e < 32; e += 2) {
                         const float p0 = tc::ex2(fmaf(__uint_as_float(r[e]), sl, -msub));
                         const float p1 = tc::ex2(fmaf(__uint_as_float(r[e + 1]), sl, -msub));
                         rsp[(e >> 1) & 7] += p0 + p1;
                         __half2 hp = __floats2half2_rn(p0, p1);
-                        p[e / 2] = *reinterpret_cast<uint32_t *>(&hp);
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int c8 = c * 4 + u;
-                        const uint32_t off =
-                            half * kSub + prow + (uint32_t)(((c8 ^ (row & 7)) << 4));
-                        *reinterpret_cast<uint4 *>(sP + off) =
-                            make_uint4(p[4 * u], p[4 * u + 1], p[4 * u + 2], p[4 * u + 3]);
+                        pk[c * 16 + e / 2] = *reinterpret_cast<uint32_t *>(&hp);
                     }
                 }
+                tc::tmem_st_32x32b_x32(tmem_p + lane_base + st * 64 + half * 32, pk);
+                tc::tmem_st_wait();
                 // the score tile has been read twice: hand its TMEM back
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&s_empty[st]);
                 l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) +
                      ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-                // order the P stores (async proxy) and any O rescale (tcgen05.st)
-                // before the MMA warp's P V MMA
-                tc::fence_proxy_async_smem();
+                // order the P stores and any O rescale (tcgen05.st) before the
+                // MMA warp's P V MMA
                 tc::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(p_full);
+                if (lane == 0) tc::mbar_arrive(&p_full[st]);
             }
             if (!__all_sync(0xffffffffu, ok)) break;
             // epilogue: the pair's partial row sums make l; O / l -> fp16
@@ -435,7 +431,8 @@ __global__ void __launch_bounds__(kAT, 1)
             const float lt = l + exchange(l, okx);
             if (!__all_sync(0xffffffffu, okx)) break;
             const uint32_t glast = g + nkv - 1;
-            ok = tc::mbar_wait(pv_done, glast & 1, abort_flag, args.err_word, kErrWaitAccum);
+            ok = tc::mbar_wait(&pv_done[glast & 1], (glast >> 1) & 1, abort_flag, args.err_word,
+                               kErrWaitAccum);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc::tc_fence_after();
             const float inv = 1.0f / lt;

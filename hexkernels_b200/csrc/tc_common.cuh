@@ -160,6 +160,18 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t
     }
 }
 
+// Same MMA with the A operand read from tensor memory (M rows = TMEM lanes,
+// two 16-bit K elements per 32-bit column, low half = even k).
+__device__ __forceinline__ void mma_ts_f16(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive on `bar` once every tcgen05.mma issued so far by this thread is done.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile(

@@ -6,7 +6,7 @@
 //
 // Work item = (head, 128-query tile); items are walked heaviest first (the
 // causal triangle makes late query tiles the longest) by a persistent grid of
-// one CTA per SM.  Per CTA, 320 threads:
+// one CTA per SM.  Per CTA, 64 + 32 * 4 * kSplit threads:
 //   warp 0      TMA: Q tile once per item; K and V tiles (128 keys x D) into
 //               two 2-stage rings, 128-byte swizzle, one box per 64 columns;
 //   warp 1      TMEM owner (512 columns: S0, S1, O, P0, P1) and MMA issuer:
@@ -15,8 +15,8 @@
 //                                        V is MN-major in shared memory)
 //               issuing S_{j+1} before O += P_j V_j, so the next score tile is
 //               computed while the softmax warps work on the current one;
-//   warps 2..9  softmax, one query row per thread (TMEM lane = row), two
-//               warps per row (each half of the key columns): load S_j, mask,
+//   warps 2..   softmax, one query row per thread (TMEM lane = row), kSplit
+//               warps per row (each a slice of the key columns): load S_j, mask,
 //               row max, P = 2^(s*scale*log2e - m) with the MUFU ex2, row sum
 //               in fp32, P as fp16 pairs into TMEM (the A operand of the
 //               P V MMA; double-buffered, so writing P_j never waits for the
@@ -40,10 +40,20 @@
 namespace hx {
 namespace {
 
-constexpr int kAT = 320;          // threads: TMA, MMA, 8 softmax warps
 constexpr int kTQ = 128;          // queries per tile
 constexpr int kTK = 128;          // keys per tile
 constexpr int kSub = 128 * 128;   // one 64-column fp16 sub-tile: 128 rows x 128 B
+
+// Softmax warps per TMEM lane quarter: each owns 128/kSplit score columns
+// and D/kSplit output columns of the quarter's 32 query rows.
+template <int D>
+struct AttnCfg {
+    static constexpr int kSplit = 2;
+    static constexpr int kSCols = 128 / kSplit;
+    static constexpr int kOCols = D / kSplit;
+    static constexpr int kSoftmaxWarps = 4 * kSplit;
+    static constexpr int kThreads = 64 + 32 * kSoftmaxWarps;   // TMA warp, MMA warp, softmax
+};
 
 template <int D>
 struct AttnSmem {
@@ -51,8 +61,8 @@ struct AttnSmem {
     static constexpr int kQ = 0;
     static constexpr int kK = kQ + kTile;          // 2 stages
     static constexpr int kV = kK + 2 * kTile;      // 2 stages
-    static constexpr int kRed = kV + 2 * kTile;    // [2][2][128] fp32 exchange
-    static constexpr int kBar = kRed + 2 * 2 * 128 * 4;
+    static constexpr int kRed = kV + 2 * kTile;    // [2][kSplit][128] fp32 exchange
+    static constexpr int kBar = kRed + 2 * AttnCfg<D>::kSplit * 128 * 4;
     // q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2],
     // s_full[2], s_empty[2], p_full[2], pv_done[2], o_free, drain, xbar[4]
     static constexpr int kNumBars = 26;
@@ -94,11 +104,13 @@ __device__ __forceinline__ void item_coords(int w, const AttnArgs &a, int &h, in
 }
 
 template <int D>
-__global__ void __launch_bounds__(kAT, 1)
+__global__ void __launch_bounds__(AttnCfg<D>::kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
     using L = AttnSmem<D>;
+    using Cfg = AttnCfg<D>;
     constexpr int kSubs = D / 64;                  // 64-column sub-tiles per Q/K/V tile
+    constexpr int kSW = Cfg::kSoftmaxWarps;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -123,13 +135,13 @@ __global__ void __launch_bounds__(kAT, 1)
             tc::mbar_init(&v_full[s], 1);
             tc::mbar_init(&v_empty[s], 1);
             tc::mbar_init(&s_full[s], 1);
-            tc::mbar_init(&s_empty[s], 8);     // one arrive per softmax warp
-            tc::mbar_init(&p_full[s], 8);
+            tc::mbar_init(&s_empty[s], kSW);   // one arrive per softmax warp
+            tc::mbar_init(&p_full[s], kSW);
             tc::mbar_init(&pv_done[s], 1);
         }
-        tc::mbar_init(o_free, 8);
+        tc::mbar_init(o_free, kSW);
         tc::mbar_init(drain, 1);
-        for (int qq = 0; qq < 4; qq++) tc::mbar_init(&xbar[qq], 2);   // the pair of a lane quarter
+        for (int qq = 0; qq < 4; qq++) tc::mbar_init(&xbar[qq], Cfg::kSplit);   // a quarter's warps
         *abort_flag = 0;
         tc::fence_mbar_init();
         tc::tma_prefetch_desc(&tmQ);
@@ -273,31 +285,37 @@ __global__ void __launch_bounds__(kAT, 1)
         }
     } else {
         // ----------------------------------------------------------- softmax
-        // Eight warps: two per TMEM lane quarter (query rows 32q..32q+31),
-        // each owning one half of the 128 score columns (keys 64h..64h+63),
-        // the matching P sub-tile and half of the O columns.  The pair
-        // exchanges its two partial row maxima once per tile (and its two
-        // partial row sums once per item) through shared memory, handshaking
-        // on the quarter's mbarrier, so every wait stays bounded.
+        // kSplit warps per TMEM lane quarter (query rows 32q..32q+31), warp
+        // `split` owning score columns [kSCols*split, +kSCols) (keys of the
+        // tile), the matching P columns and output columns [kOCols*split,
+        // +kOCols).  The quarter's warps exchange their partial row maxima
+        // once per tile (and partial row sums once per item) through shared
+        // memory, handshaking on the quarter's mbarrier: every wait is bounded.
+        constexpr int kSC = Cfg::kSCols, kOC = Cfg::kOCols, kSplit = Cfg::kSplit;
         const int q = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int split = (warp - 2) >> 2;
         const int row = q * 32 + lane;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        float *xred = reinterpret_cast<float *>(smem + L::kRed);   // [2][2][128]
-        constexpr int kOCols = D / 2;                               // O columns per half
-        const uint32_t o_base = tmem_o + lane_base + half * kOCols;
+        float *xred = reinterpret_cast<float *>(smem + L::kRed);   // [2][kSplit][128]
+        const uint32_t o_base = tmem_o + lane_base + split * kOC;
         uint32_t g = 0, xc = 0;
         int item = 0;
-        // exchange `v` with the pair warp; returns the pair's value
-        auto exchange = [&](float v, bool &okx) -> float {
+        // publish `v`; returns the quarter's kSplit values combined by `op`,
+        // in split order (every warp of the quarter gets the same result)
+        auto exchange = [&](float v, bool use_max, bool &okx) -> float {
             const int b = xc & 1;
-            xred[(b * 2 + half) * 128 + row] = v;
+            xred[(b * kSplit + split) * 128 + row] = v;
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&xbar[q]);
             okx = tc::mbar_wait(&xbar[q], xc & 1, abort_flag, args.err_word, kErrWaitOther);
-            const float other = xred[(b * 2 + (half ^ 1)) * 128 + row];
+            float acc = xred[(b * kSplit) * 128 + row];
+#pragma unroll
+            for (int o = 1; o < kSplit; o++) {
+                const float u = xred[(b * kSplit + o) * 128 + row];
+                acc = use_max ? fmaxf(acc, u) : acc + u;
+            }
             xc++;
-            return other;
+            return acc;
         };
         for (int w = blockIdx.x; w < args.nitems; w += gridDim.x, item++) {
             if (__any_sync(0xffffffffu, *abort_flag)) break;
@@ -314,11 +332,11 @@ __global__ void __launch_bounds__(kAT, 1)
                                    kErrWaitAccum);
                 if (!__all_sync(0xffffffffu, ok)) break;
                 tc::tc_fence_after();
-                // Pass 1 over this warp's half of the score tile in TMEM: mask
+                // Pass 1 over this warp's score columns in TMEM: mask
                 // (diagonal / ragged tiles only) and row max on the raw scores
                 // (the scale > 0 is folded into the exponent in pass 2).
-                const uint32_t s_addr = tmem_base + lane_base + st * kTK + half * 64;
-                const int key0 = j * kTK + half * 64;
+                const uint32_t s_addr = tmem_base + lane_base + st * kTK + split * kSC;
+                const int key0 = j * kTK + split * kSC;
                 const bool need_mask =
                     (args.causal && j * kTK + kTK - 1 > q0) || j * kTK + kTK > args.SK;
                 auto mask_chunk = [&](uint32_t (&r)[32], int c) {
@@ -333,7 +351,7 @@ __global__ void __launch_bounds__(kAT, 1)
 #pragma unroll
                 for (int u = 0; u < 8; u++) mx[u] = -INFINITY;
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
+                for (int c = 0; c < kSC / 32; c++) {
                     uint32_t r[32];
                     tc::tmem_ld_32x32b_x32(s_addr + c * 32, r);
                     tc::tmem_ld_wait(r);
@@ -344,7 +362,7 @@ __global__ void __launch_bounds__(kAT, 1)
                 float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                  fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
                 bool okx;
-                mt = fmaxf(mt, exchange(mt, okx)) * args.scale_log2;
+                mt = exchange(mt, true, okx) * args.scale_log2;
                 if (!__all_sync(0xffffffffu, okx)) {
                     ok = false;
                     break;
@@ -353,8 +371,8 @@ __global__ void __launch_bounds__(kAT, 1)
                 if (j == 0) {
                     m_ref = m_new;
                 } else {
-                    // both warps of the pair see the same m_ref and m_new, so
-                    // they make the same rescale decision for every row
+                    // the quarter's warps see the same m_ref and m_new, so they
+                    // make the same rescale decision for every row
                     const bool need = m_new > m_ref + 8.0f;
                     if (__any_sync(0xffffffffu, need)) {
                         const uint32_t gp = gj - 1;      // O is stable once P V of tile gp is done
@@ -364,7 +382,7 @@ __global__ void __launch_bounds__(kAT, 1)
                         tc::tc_fence_after();
                         const float corr = need ? tc::ex2(m_ref - m_new) : 1.0f;
 #pragma unroll 1
-                        for (int c = 0; c < kOCols / 32; c++) {
+                        for (int c = 0; c < kOC / 32; c++) {
                             uint32_t o[32];
                             tc::tmem_ld_32x32b_x32(o_base + c * 32, o);
                             tc::tmem_ld_wait(o);
@@ -389,15 +407,15 @@ __global__ void __launch_bounds__(kAT, 1)
                     tc::tc_fence_after();
                 }
                 // Pass 2: P = 2^(s * scale*log2e - m_ref) as fp16 pairs into P
-                // buffer st, columns 32*half..32*half+31 (keys 64*half + 2c and
-                // 64*half + 2c + 1 in column 32*half + c), partial row sum in fp32.
+                // buffer st (keys 2c and 2c+1 of the tile in column c), partial
+                // row sum in fp32.
                 float rsp[8];
 #pragma unroll
                 for (int u = 0; u < 8; u++) rsp[u] = 0.0f;
                 const float sl = args.scale_log2, msub = m_ref;
-                uint32_t pk[32];
+                uint32_t pk[kSC / 2];
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
+                for (int c = 0; c < kSC / 32; c++) {
                     uint32_t r[32];
                     tc::tmem_ld_32x32b_x32(s_addr + c * 32, r);
                     tc::tmem_ld_wait(r);
@@ -411,24 +429,27 @@ __global__ void __launch_bounds__(kAT, 1)
                         pk[c * 16 + e / 2] = *reinterpret_cast<uint32_t *>(&hp);
                     }
                 }
-                tc::tmem_st_32x32b_x32(tmem_p + lane_base + st * 64 + half * 32, pk);
+                const uint32_t p_addr = tmem_p + lane_base + st * 64 + split * (kSC / 2);
+                if constexpr (kSC / 2 == 32)
+                    tc::tmem_st_32x32b_x32(p_addr, pk);
+                else
+                    tc::tmem_st_32x32b_x16(p_addr, pk);
                 tc::tmem_st_wait();
-                // the score tile has been read twice: hand its TMEM back
-                tc::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&s_empty[st]);
                 l += ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) +
                      ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-                // order the P stores and any O rescale (tcgen05.st) before the
-                // MMA warp's P V MMA
+                // hand the score tile back, and order the P stores and any O
+                // rescale (tcgen05.st) before the MMA warp's P V MMA
                 tc::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&p_full[st]);
+                if (lane == 0) {
+                    tc::mbar_arrive(&s_empty[st]);
+                    tc::mbar_arrive(&p_full[st]);
+                }
             }
             if (!__all_sync(0xffffffffu, ok)) break;
-            // epilogue: the pair's partial row sums make l; O / l -> fp16
+            // epilogue: the quarter's partial row sums make l; O / l -> fp16
             bool okx;
-            const float lt = l + exchange(l, okx);
+            const float lt = exchange(l, false, okx);
             if (!__all_sync(0xffffffffu, okx)) break;
             const uint32_t glast = g + nkv - 1;
             ok = tc::mbar_wait(&pv_done[glast & 1], (glast >> 1) & 1, abort_flag, args.err_word,
@@ -436,9 +457,9 @@ __global__ void __launch_bounds__(kAT, 1)
             if (!__all_sync(0xffffffffu, ok)) break;
             tc::tc_fence_after();
             const float inv = 1.0f / lt;
-            __half *orow = args.O + ((size_t)h * args.SQ + qi) * D + half * kOCols;
+            __half *orow = args.O + ((size_t)h * args.SQ + qi) * D + split * kOC;
 #pragma unroll 1
-            for (int c = 0; c < kOCols / 32; c++) {
+            for (int c = 0; c < kOC / 32; c++) {
                 uint32_t o[32];
                 tc::tmem_ld_32x32b_x32(o_base + c * 32, o);
                 tc::tmem_ld_wait(o);
@@ -460,6 +481,467 @@ __global__ void __launch_bounds__(kAT, 1)
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(o_free);
             g += nkv;
+        }
+    }
+
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tc::tmem_dealloc(tmem_base, 512);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Softmax arithmetic for the ping-pong kernel: packed fp32 pairs (the
+// f32x2 FMA / ADD of sm_100), three-input max, and a second exponential
+// path on the FMA pipe, so the MUFU unit is not the only one computing 2^x.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void up2(uint64_t v, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x for both halves of x2 without the MUFU unit.  x = n + f with n =
+// rint(x) (adding 1.5 * 2^23 rounds x to an integer in the low mantissa
+// bits) and f in [-0.5, 0.5]; 2^f is a degree-3 polynomial fitted for this
+// kernel (relative error below 8e-5, ample for the fp16 P it feeds), and 2^n
+// is added to the exponent field: bits(p) + n * 2^23, where bits(t) * 2^23
+// equals n * 2^23 modulo 2^32.  x is clamped to >= -125 so 2^x stays a
+// normal number (it only feeds a row sum and an fp16 P, where it is zero).
+__device__ __forceinline__ void exp2_fma2(uint64_t x2, float &r0, float &r1) {
+    float x0, x1;
+    up2(x2, x0, x1);
+    const uint64_t xc = pk2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+    const uint64_t t = add2(xc, pk2(12582912.0f, 12582912.0f));
+    const uint64_t nf = add2(t, pk2(-12582912.0f, -12582912.0f));
+    const uint64_t f = fma2(nf, pk2(-1.0f, -1.0f), xc);
+    uint64_t p = fma2(pk2(0.05517047643661499f, 0.05517047643661499f), f,
+                      pk2(0.2426084578037262f, 0.2426084578037262f));
+    p = fma2(p, f, pk2(0.6932609677314758f, 0.6932609677314758f));
+    p = fma2(p, f, pk2(0.9999282360076904f, 0.9999282360076904f));
+    float p0, p1, t0, t1;
+    up2(p, p0, p1);
+    up2(t, t0, t1);
+    r0 = __int_as_float(__float_as_int(p0) + (int)((uint32_t)__float_as_int(t0) << 23));
+    r1 = __int_as_float(__float_as_int(p1) + (int)((uint32_t)__float_as_int(t1) << 23));
+}
+
+// ---------------------------------------------------------------------------
+// Ping-pong kernel (D = 128): two 128-query tiles per work item, one softmax
+// warpgroup per tile, so the tensor pipe always has the other tile's MMAs to
+// run while a warpgroup does its exponentials.
+//
+// Per CTA, 320 threads: warp 0 TMA, warp 1 MMA, warps 2..5 softmax of tile
+// a, warps 6..9 softmax of tile b (one query row per thread, all 128 key
+// columns of the tile per thread, so the row max and sum need no exchange).
+// TMEM (512 columns): S_a [0,128), S_b [128,256), O_a [256,384), O_b
+// [384,512); P_x is written as fp16 pairs over S_x's first 64 columns once
+// the softmax has read them.  The MMA warp issues, per key tile j,
+//     P_a V_j -> S_a(j+1) = Q_a K_{j+1}^T -> P_b V_j -> S_b(j+1)
+// so each warpgroup's next score tile is computed right after its P V, while
+// the other warpgroup is busy.  The MMAs of one thread execute in issue order,
+// which is what lets S_x(j+1) reuse the columns P_x(j) was read from.
+constexpr int kPairQ = 256;
+
+struct PPSmem {
+    static constexpr int kTile = 128 * 128 * 2;     // 32 KB
+    static constexpr int kQ = 0;                    // Q_a, Q_b
+    static constexpr int kK = 2 * kTile;            // 2 stages
+    static constexpr int kV = kK + 2 * kTile;       // 2 stages
+    static constexpr int kBar = kV + 2 * kTile;
+    // q_full, q_empty, k_full[2], k_empty[2], v_full[2], v_empty[2],
+    // s_full[2], p_full[2], pv_done[2], o_free[2], drain
+    static constexpr int kNumBars = 19;
+    static constexpr int kTotal = kBar + kNumBars * 8 + 16 + 1024;
+};
+
+__device__ __forceinline__ void pp_item(int w, const AttnArgs &a, int &h, int &qp, int &nkv_a,
+                                        int &nkv_b) {
+    const int nq2 = a.nq;                       // pairs per head
+    const int per_group = kHeadGroup * nq2;
+    const int group = w / per_group;
+    const int first_h = group * kHeadGroup;
+    const int gs = min(kHeadGroup, a.BH - first_h);
+    const int r = w - group * per_group;
+    qp = nq2 - 1 - r / gs;
+    h = first_h + r % gs;
+    const int nk_all = (a.SK + kTK - 1) / kTK;
+    if (a.causal) {
+        nkv_a = min(a.SK - 1, qp * kPairQ + kTQ - 1) / kTK + 1;
+        nkv_b = min(a.SK - 1, qp * kPairQ + 2 * kTQ - 1) / kTK + 1;
+    } else {
+        nkv_a = nkv_b = nk_all;
+    }
+}
+
+__global__ void __launch_bounds__(320, 1)
+    attn_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
+    using L = PPSmem;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBar);
+    uint64_t *q_full = bars + 0, *q_empty = bars + 1;
+    uint64_t *k_full = bars + 2, *k_empty = bars + 4;
+    uint64_t *v_full = bars + 6, *v_empty = bars + 8;
+    uint64_t *s_full = bars + 10, *p_full = bars + 12, *pv_done = bars + 14, *o_free = bars + 16;
+    uint64_t *drain = bars + 18;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        tc::mbar_init(q_full, 1);
+        tc::mbar_init(q_empty, 1);
+        for (int x = 0; x < 2; x++) {
+            tc::mbar_init(&k_full[x], 1);
+            tc::mbar_init(&k_empty[x], 1);
+            tc::mbar_init(&v_full[x], 1);
+            tc::mbar_init(&v_empty[x], 1);
+            tc::mbar_init(&s_full[x], 1);
+            tc::mbar_init(&p_full[x], 4);      // the tile's four softmax warps
+            tc::mbar_init(&pv_done[x], 1);
+            tc::mbar_init(&o_free[x], 4);
+        }
+        tc::mbar_init(drain, 1);
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+        tc::tma_prefetch_desc(&tmQ);
+        tc::tma_prefetch_desc(&tmK);
+        tc::tma_prefetch_desc(&tmV);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ----------------------------------------------------------- TMA
+            uint32_t g = 0;
+            int item = 0;
+            uint32_t armed_q = 0, armed_k = 0, armed_v = 0;
+            uint32_t armed_k_ph[2] = {0, 0}, armed_v_ph[2] = {0, 0};
+            for (int w = blockIdx.x; w < args.nitems && !*abort_flag; w += gridDim.x, item++) {
+                int h, qp, nkv_a, nkv_b;
+                pp_item(w, args, h, qp, nkv_a, nkv_b);
+                if (!tc::mbar_wait(q_empty, (item & 1) ^ 1, abort_flag, args.err_word, kErrWaitEmpty))
+                    break;
+                tc::mbar_arrive_expect_tx(q_full, 2 * L::kTile);
+                for (int x = 0; x < 2; x++)
+                    for (int c = 0; c < 2; c++)
+                        tc::tma_load_3d(smem + L::kQ + x * L::kTile + c * kSub, &tmQ, q_full, c * 64,
+                                        qp * kPairQ + x * kTQ, h);
+                armed_q = (item & 1) + 1;
+                for (int j = 0; j < nkv_b; j++, g++) {
+                    const int st = g & 1;
+                    const uint32_t ph = (g >> 1) & 1;
+                    if (!tc::mbar_wait(&k_empty[st], ph ^ 1, abort_flag, args.err_word, kErrWaitEmpty))
+                        break;
+                    tc::mbar_arrive_expect_tx(&k_full[st], L::kTile);
+                    for (int c = 0; c < 2; c++)
+                        tc::tma_load_3d(smem + L::kK + st * L::kTile + c * kSub, &tmK, &k_full[st],
+                                        c * 64, j * kTK, h);
+                    armed_k |= 1u << st;
+                    armed_k_ph[st] = ph;
+                    if (!tc::mbar_wait(&v_empty[st], ph ^ 1, abort_flag, args.err_word, kErrWaitEmpty))
+                        break;
+                    tc::mbar_arrive_expect_tx(&v_full[st], L::kTile);
+                    for (int c = 0; c < 2; c++)
+                        tc::tma_load_3d(smem + L::kV + st * L::kTile + c * kSub, &tmV, &v_full[st],
+                                        c * 64, j * kTK, h);
+                    armed_v |= 1u << st;
+                    armed_v_ph[st] = ph;
+                }
+            }
+            const uint64_t t0 = tc::globaltimer();
+            auto drain_wait = [&](uint64_t *bar, uint32_t par) {
+                while (!tc::mbar_try_wait(bar, par) && tc::globaltimer() - t0 < kWaitBudgetNs) {
+                }
+            };
+            if (armed_q) drain_wait(q_full, armed_q - 1);
+            for (int x = 0; x < 2; x++) {
+                if (armed_k & (1u << x)) drain_wait(&k_full[x], armed_k_ph[x]);
+                if (armed_v & (1u << x)) drain_wait(&v_full[x], armed_v_ph[x]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ----------------------------------------------------------- MMA
+            constexpr uint32_t idesc_s = tc::idesc_f16_f32(kTQ, kTK, false);
+            constexpr uint32_t idesc_pv = tc::idesc_f16_f32(kTQ, 128, true);
+            const uint32_t sQ = tc::smem_u32(smem + L::kQ);
+            const uint32_t sK = tc::smem_u32(smem + L::kK);
+            const uint32_t sV = tc::smem_u32(smem + L::kV);
+            uint32_t g = 0, n[2] = {0, 0};      // key tiles so far; tiles per query tile so far
+            int item = 0;
+            bool issued = false, ok = true;
+            auto issue_s = [&](int x, uint32_t gk) {
+                const uint32_t kb = sK + (gk & 1) * L::kTile;
+                const uint32_t qb = sQ + x * L::kTile;
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const uint32_t off = (k >> 2) * kSub + (k & 3) * 32;
+                    tc::mma_ss<tc::MmaKind::F16>(tmem_base + x * 128, tc::sdesc_kmajor_sw128(qb + off),
+                                                 tc::sdesc_kmajor_sw128(kb + off), idesc_s,
+                                                 k > 0 ? 1u : 0u);
+                }
+                tc::mma_commit(&s_full[x]);
+                issued = true;
+            };
+            auto issue_pv = [&](int x, uint32_t gk, bool first) {
+                const uint32_t vb = sV + (gk & 1) * L::kTile;
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    tc::mma_ts_f16(tmem_base + 256 + x * 128, tmem_base + x * 128 + k * 8,
+                                   tc::sdesc_mnmajor_sw128(vb + k * 2048, kSub, 1024), idesc_pv,
+                                   (!first || k > 0) ? 1u : 0u);
+                tc::mma_commit(&pv_done[x]);
+            };
+            for (int w = blockIdx.x; w < args.nitems && ok && !*abort_flag; w += gridDim.x, item++) {
+                int h, qp, nkv_a, nkv_b;
+                pp_item(w, args, h, qp, nkv_a, nkv_b);
+                const int nkv[2] = {nkv_a, nkv_b};
+                ok = tc::mbar_wait(q_full, item & 1, abort_flag, args.err_word, kErrWaitFull) &&
+                     tc::mbar_wait(&k_full[g & 1], (g >> 1) & 1, abort_flag, args.err_word,
+                                   kErrWaitFull);
+                if (!ok) break;
+                tc::tc_fence_after();
+                issue_s(0, g);
+                issue_s(1, g);
+                tc::mma_commit(&k_empty[g & 1]);
+                if (nkv_b == 1) tc::mma_commit(q_empty);
+                for (int j = 0; j < nkv_b && ok; j++) {
+                    const uint32_t gj = g + j;
+                    ok = tc::mbar_wait(&v_full[gj & 1], (gj >> 1) & 1, abort_flag, args.err_word,
+                                       kErrWaitFull);
+                    const bool more = j + 1 < nkv_b;
+                    bool k_ready = false;
+                    for (int x = 0; x < 2 && ok; x++) {
+                        if (j >= nkv[x]) continue;
+                        const uint32_t c = n[x] + j;
+                        ok = tc::mbar_wait(&p_full[x], c & 1, abort_flag, args.err_word,
+                                           kErrWaitFull) &&
+                             (j > 0 || tc::mbar_wait(&o_free[x], (item & 1) ^ 1, abort_flag,
+                                                     args.err_word, kErrWaitAccum));
+                        if (!ok) break;
+                        tc::tc_fence_after();
+                        issue_pv(x, gj, j == 0);
+                        if (x == 1) tc::mma_commit(&v_empty[gj & 1]);
+                        if (more && j + 1 < nkv[x]) {
+                            if (!k_ready) {
+                                ok = tc::mbar_wait(&k_full[(gj + 1) & 1], ((gj + 1) >> 1) & 1,
+                                                   abort_flag, args.err_word, kErrWaitFull);
+                                if (!ok) break;
+                                tc::tc_fence_after();
+                                k_ready = true;
+                            }
+                            issue_s(x, gj + 1);
+                            if (x == 1) {
+                                tc::mma_commit(&k_empty[(gj + 1) & 1]);
+                                if (j + 1 == nkv_b - 1) tc::mma_commit(q_empty);
+                            }
+                        }
+                    }
+                }
+                n[0] += nkv_a;
+                n[1] += nkv_b;
+                g += nkv_b;
+            }
+            if (issued) {
+                tc::mma_commit(drain);
+                const uint64_t t0 = tc::globaltimer();
+                while (!tc::mbar_try_wait(drain, 0) && tc::globaltimer() - t0 < kWaitBudgetNs) {
+                }
+            }
+        }
+    } else {
+        // ----------------------------------------------------- softmax x
+        const int x = (warp - 2) >> 2;
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        const uint32_t s_addr = tmem_base + lane_base + x * 128;
+        const uint32_t o_addr = tmem_base + lane_base + 256 + x * 128;
+        uint32_t n = 0;
+        int item = 0;
+        for (int w = blockIdx.x; w < args.nitems; w += gridDim.x, item++) {
+            if (__any_sync(0xffffffffu, *abort_flag)) break;
+            int h, qp, nkv_a, nkv_b;
+            pp_item(w, args, h, qp, nkv_a, nkv_b);
+            const int nkv = x == 0 ? nkv_a : nkv_b;
+            const int q0 = qp * kPairQ + x * kTQ;
+            const int qi = q0 + row;
+            float m_ref = -INFINITY, l = 0.0f;
+            bool ok = true;
+            for (int j = 0; j < nkv; j++) {
+                const uint32_t c = n + j;
+                ok = tc::mbar_wait(&s_full[x], c & 1, abort_flag, args.err_word, kErrWaitAccum);
+                if (!__all_sync(0xffffffffu, ok)) break;
+                tc::tc_fence_after();
+                const int key0 = j * kTK;
+                const bool need_mask =
+                    (args.causal && key0 + kTK - 1 > q0) || key0 + kTK > args.SK;
+                auto mask_chunk = [&](uint32_t (&r)[32], int cc) {
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        const int kk = key0 + cc * 32 + e;
+                        if (kk >= args.SK || (args.causal && kk > qi))
+                            r[e] = __float_as_uint(-INFINITY);
+                    }
+                };
+                // pass 1: row max over the 128 raw scores (scale folded later)
+                float mx[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) mx[u] = -INFINITY;
+#pragma unroll
+                for (int cc = 0; cc < 4; cc++) {
+                    uint32_t r[32];
+                    tc::tmem_ld_32x32b_x32(s_addr + cc * 32, r);
+                    tc::tmem_ld_wait(r);
+                    if (need_mask) mask_chunk(r, cc);
+#pragma unroll
+                    for (int i = 0; i < 16; i++)
+                        mx[i & 7] = max3(mx[i & 7], __uint_as_float(r[2 * i]),
+                                         __uint_as_float(r[2 * i + 1]));
+                }
+                const float mt = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]),
+                                      fmaxf(mx[6], mx[7])) *
+                                 args.scale_log2;
+                const float m_new = fmaxf(m_ref, mt);
+                if (j == 0) {
+                    m_ref = m_new;
+                } else {
+                    const bool need = m_new > m_ref + 8.0f;
+                    if (__any_sync(0xffffffffu, need)) {
+                        // O_x is stable once P V of the previous key tile is done
+                        ok = tc::mbar_wait(&pv_done[x], (c - 1) & 1, abort_flag, args.err_word,
+                                           kErrWaitAccum);
+                        if (!__all_sync(0xffffffffu, ok)) break;
+                        tc::tc_fence_after();
+                        const float corr = need ? tc::ex2(m_ref - m_new) : 1.0f;
+#pragma unroll 1
+                        for (int cc = 0; cc < 4; cc++) {
+                            uint32_t o[32];
+                            tc::tmem_ld_32x32b_x32(o_addr + cc * 32, o);
+                            tc::tmem_ld_wait(o);
+#pragma unroll
+                            for (int e = 0; e < 32; e++)
+                                o[e] = __float_as_uint(__uint_as_float(o[e]) * corr);
+                            tc::tmem_st_32x32b_x32(o_addr + cc * 32, o);
+                        }
+                        tc::tmem_st_wait();
+                        if (need) {
+                            l *= corr;
+                            m_ref = m_new;
+                        }
+                    }
+                }
+                // pass 2: P = 2^(s*scale*log2e - m_ref), fp16 pairs written over
+                // S columns 16cc..16cc+15 (already read: chunk cc reads columns
+                // 32cc.. which are at or past the ones it overwrites).  Pairs of
+                // scores go through one f32x2 FMA; one pair in four takes the
+                // FMA-pipe exponential, the rest the MUFU ex2; the row sum is
+                // accumulated in four packed pairs.
+                uint64_t acc2[4] = {0, 0, 0, 0};
+                const uint64_t sl2 = pk2(args.scale_log2, args.scale_log2);
+                const uint64_t nm2 = pk2(-m_ref, -m_ref);
+#pragma unroll
+                for (int cc = 0; cc < 4; cc++) {
+                    uint32_t r[32];
+                    tc::tmem_ld_32x32b_x32(s_addr + cc * 32, r);
+                    tc::tmem_ld_wait(r);
+                    if (need_mask) mask_chunk(r, cc);
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int e2 = 0; e2 < 16; e2++) {
+                        const uint64_t x2 = fma2(pk2(__uint_as_float(r[2 * e2]),
+                                                     __uint_as_float(r[2 * e2 + 1])),
+                                                 sl2, nm2);
+                        float p0, p1;
+                        if ((e2 & 3) == 3) {
+                            exp2_fma2(x2, p0, p1);
+                        } else {
+                            float a0, a1;
+                            up2(x2, a0, a1);
+                            p0 = tc::ex2(a0);
+                            p1 = tc::ex2(a1);
+                        }
+                        acc2[e2 & 3] = add2(acc2[e2 & 3], pk2(p0, p1));
+                        __half2 hp = __floats2half2_rn(p0, p1);
+                        pk[e2] = *reinterpret_cast<uint32_t *>(&hp);
+                    }
+                    tc::tmem_st_32x32b_x16(s_addr + cc * 16, pk);
+                }
+                tc::tmem_st_wait();
+                {
+                    float s0, s1, s2, s3, s4, s5, s6, s7;
+                    up2(acc2[0], s0, s1);
+                    up2(acc2[1], s2, s3);
+                    up2(acc2[2], s4, s5);
+                    up2(acc2[3], s6, s7);
+                    l += ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7));
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&p_full[x]);
+            }
+            if (!__all_sync(0xffffffffu, ok)) break;
+            // epilogue: O_x / l -> fp16 rows
+            const uint32_t clast = n + nkv - 1;
+            ok = tc::mbar_wait(&pv_done[x], clast & 1, abort_flag, args.err_word, kErrWaitAccum);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc::tc_fence_after();
+            const float inv = 1.0f / l;
+            __half *orow = args.O + ((size_t)h * args.SQ + qi) * 128;
+#pragma unroll 1
+            for (int cc = 0; cc < 4; cc++) {
+                uint32_t o[32];
+                tc::tmem_ld_32x32b_x32(o_addr + cc * 32, o);
+                tc::tmem_ld_wait(o);
+                if (qi < args.SQ) {
+                    uint32_t w16[16];
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        __half2 hv = __floats2half2_rn(__uint_as_float(o[2 * e]) * inv,
+                                                       __uint_as_float(o[2 * e + 1]) * inv);
+                        w16[e] = *reinterpret_cast<uint32_t *>(&hv);
+                    }
+                    uint4 *dst = reinterpret_cast<uint4 *>(orow + cc * 32);
+#pragma unroll
+                    for (int e = 0; e < 4; e++)
+                        dst[e] = make_uint4(w16[4 * e], w16[4 * e + 1], w16[4 * e + 2], w16[4 * e + 3]);
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&o_free[x]);
+            n += nkv;
         }
     }
 
@@ -534,11 +1016,42 @@ int launch_attn_tc(Dev *d, const __half *Q, const __half *K, const __half *V, __
     a.O = O;
     a.err_word = d->err_word;
     const int grid = a.nitems < d->sms ? a.nitems : d->sms;
-    attn_tc_kernel<D><<<grid, kAT, L::kTotal, d->stream>>>(mq, mk, mv, a);
+    attn_tc_kernel<D><<<grid, AttnCfg<D>::kThreads, L::kTotal, d->stream>>>(mq, mk, mv, a);
     return HEXCUDA_OK;
 }
 
 }  // namespace
+
+int launch_attn_pp(Dev *d, const __half *Q, const __half *K, const __half *V, __half *O, int BH,
+                   int SQ, int SK, float scale, int causal) {
+    using L = PPSmem;
+    static bool attr_done[64] = {};
+    if (!attr_done[d->ordinal & 63]) {
+        if (int rc = check(cudaFuncSetAttribute(attn_pp_kernel,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                L::kTotal),
+                           "cudaFuncSetAttribute(attn_pp)"))
+            return rc;
+        attr_done[d->ordinal & 63] = true;
+    }
+    CUtensorMap mq, mk, mv;
+    if (int rc = make_head_map(&mq, Q, BH, SQ, 128)) return rc;
+    if (int rc = make_head_map(&mk, K, BH, SK, 128)) return rc;
+    if (int rc = make_head_map(&mv, V, BH, SK, 128)) return rc;
+    AttnArgs a;
+    a.BH = BH;
+    a.SQ = SQ;
+    a.SK = SK;
+    a.nq = (SQ + kPairQ - 1) / kPairQ;          // query-tile pairs per head
+    a.nitems = BH * a.nq;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.causal = causal;
+    a.O = O;
+    a.err_word = d->err_word;
+    const int grid = a.nitems < d->sms ? a.nitems : d->sms;
+    attn_pp_kernel<<<grid, 320, L::kTotal, d->stream>>>(mq, mk, mv, a);
+    return HEXCUDA_OK;
+}
 
 // The tcgen05 path takes D = 64 or 128 with 16-byte aligned tensors; other
 // shapes stay on the CUDA-core kernel in attn.cu.
@@ -549,6 +1062,8 @@ int attn_tc_launch(Dev *d, const __half *Q, const __half *K, const __half *V, __
     if (!(D == 64 || D == 128) || !al(Q) || !al(K) || !al(V) || !al(O)) return HEXCUDA_OK;
     if ((long long)BH * ((SQ + kTQ - 1) / kTQ) > 0x7fffffffLL) return HEXCUDA_OK;
     *handled = true;
+    if (D == 128 && SQ > kTQ)
+        return launch_attn_pp(d, Q, K, V, O, BH, SQ, SK, scale, causal);
     return D == 128 ? launch_attn_tc<128>(d, Q, K, V, O, BH, SQ, SK, scale, causal)
                     : launch_attn_tc<64>(d, Q, K, V, O, BH, SQ, SK, scale, causal);
 }

@@ -562,6 +562,10 @@ __device__ __forceinline__ void exp2_fma2(uint64_t x2, float &r0, float &r1) {
 // the other warpgroup is busy.  The MMAs of one thread execute in issue order,
 // which is what lets S_x(j+1) reuse the columns P_x(j) was read from.
 constexpr int kPairQ = 256;
+// One score pair in kPolyEvery takes the FMA-pipe exponential (0: none).
+// The MUFU unit is not the limiter of this kernel (issue slots are), and the
+// polynomial costs ~7 issue slots per score against 1 for ex2.
+constexpr int kPolyEvery = 0;
 
 struct PPSmem {
     static constexpr int kTile = 128 * 128 * 2;     // 32 KB
@@ -884,7 +888,8 @@ __global__ void __launch_bounds__(320, 1)
                                                      __uint_as_float(r[2 * e2 + 1])),
                                                  sl2, nm2);
                         float p0, p1;
-                        if ((e2 & 3) == 3) {
+                        if (kPolyEvery > 0 && (e2 % (kPolyEvery > 0 ? kPolyEvery : 1)) ==
+                                                  kPolyEvery - 1) {
                             exp2_fma2(x2, p0, p1);
                         } else {
                             float a0, a1;

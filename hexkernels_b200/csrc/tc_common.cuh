@@ -84,7 +84,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (true) {
-        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if (mbar_try_wait(bar, parity)) return true;
         if (*abort) return false;
         if (globaltimer() - t0 > budget_ns) {
             atomicOr(err_word, code);

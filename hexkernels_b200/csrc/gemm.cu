@@ -50,7 +50,7 @@ constexpr int kStages = 4;
 constexpr int kThreads = 320;      // TMA warp, MMA warp, 8 epilogue warps
 constexpr int kGroupM = 16;
 
-enum EpiKind { kEpiF16 = 0, kEpiRequant = 1 };
+enum EpiKind { kEpiF16 = 0, kEpiRequant = 1, kEpiHmx = 2 };
 
 struct EpiParams {
     void *out;
@@ -69,6 +69,10 @@ struct EpiParams {
     int shift;
     int zp;
     int lo, hi;
+    // HMX-convention epilogue (kEpiHmx): acc32 as above, then
+    //   r = sx12((acc32 * 17 + 8) >> 4)   (int32 wrap, arithmetic shift)
+    //   hmx_mode 0: int32 r; 1: int8 clamp(r); 2: uint8 clamp(max(r + bias[j], 0))
+    int hmx_mode;
 };
 
 struct GemmArgs {
@@ -126,6 +130,54 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             for (int i = 0; i < 4; i++) dst[i] = v[i];
         } else {
             for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = __float2half_rn(__uint_as_float(r[i]));
+        }
+    } else if constexpr (EPI == kEpiHmx) {
+        int32_t v[32];
+#pragma unroll
+        for (int i4 = 0; i4 < 8; i4++) {
+            const int4 c4 = *reinterpret_cast<const int4 *>(&cp->corr[4 * i4]);
+            const int4 b4 = *reinterpret_cast<const int4 *>(&cp->bias[4 * i4]);
+            const int cc[4] = {c4.x, c4.y, c4.z, c4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint32_t a32 = r[4 * i4 + u] - (uint32_t)cc[u];
+                const int32_t f = (int32_t)(a32 * 17u + 8u) >> 4;
+                int32_t x = (int32_t)((uint32_t)f << 20) >> 20;  // low 12 bits, sign-extended
+                if (ep.hmx_mode == 1) {
+                    x = min(max(x, -128), 127);
+                } else if (ep.hmx_mode == 2) {
+                    x = (int32_t)((uint32_t)x + (uint32_t)bb[u]);
+                    x = min(max(x, 0), 255);
+                }
+                v[4 * i4 + u] = x;
+            }
+        }
+        if (row >= ep.M) return;
+        if (ep.hmx_mode == 0) {
+            int32_t *o = reinterpret_cast<int32_t *>(ep.out) + (size_t)row * ep.ldo + col0;
+            if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
+                uint4 *dst = reinterpret_cast<uint4 *>(o);
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+                    dst[i] = make_uint4((uint32_t)v[4 * i], (uint32_t)v[4 * i + 1],
+                                        (uint32_t)v[4 * i + 2], (uint32_t)v[4 * i + 3]);
+            } else {
+                for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = v[i];
+            }
+        } else {
+            uint8_t *o = reinterpret_cast<uint8_t *>(ep.out) + (size_t)row * ep.ldo + col0;
+            uint32_t w[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                w[i] = ((uint32_t)v[4 * i] & 0xFFu) | (((uint32_t)v[4 * i + 1] & 0xFFu) << 8) |
+                       (((uint32_t)v[4 * i + 2] & 0xFFu) << 16) | ((uint32_t)v[4 * i + 3] << 24);
+            if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
+                uint4 *dst = reinterpret_cast<uint4 *>(o);
+                dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+                dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
+                for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = (uint8_t)v[i];
+            }
         }
     } else {
         // requant: the 32 columns' parameters were staged in `cp` by this warp
@@ -361,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
             for (int c = chalf * (BN / 2); c < (chalf + 1) * (BN / 2); c += 32) {
                 uint32_t r[32];
-                if constexpr (EPI == kEpiRequant) {
+                if constexpr (EPI != kEpiF16) {
                     stage_params(args.epi, cp, nb * BN + c, lane);
                 }
                 __syncwarp();
@@ -469,6 +521,33 @@ __global__ void __launch_bounds__(128) colsum_kernel(const int8_t *__restrict__ 
     for (int i = 0; i < 16 && n0 + i < N; i++) atomicAdd(colsum + n0 + i, acc[i]);
 }
 
+// colsum[n] = sum_k Bt[n][k] for a K-major int8 Bt [N, K] (pitch ldb): one
+// warp per row, 16-byte loads where the row allows them.
+__global__ void __launch_bounds__(256) rowsum_i8_kernel(const int8_t *__restrict__ Bt,
+                                                        int64_t ldb, int32_t *__restrict__ colsum,
+                                                        int N, int K, int vec) {
+    const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    const int8_t *row = Bt + (size_t)n * ldb;
+    int32_t s = 0;
+    int k0 = 0;
+    if (vec) {
+        const int kv = K & ~15;
+        for (int k = lane * 16; k < kv; k += 32 * 16) {
+            const int4 q = __ldg(reinterpret_cast<const int4 *>(row + k));
+            const int w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 16; i++) s += (int32_t)(int8_t)(w[i >> 2] >> (8 * (i & 3)));
+        }
+        k0 = kv;
+    }
+    for (int k = k0 + lane; k < K; k += 32) s += row[k];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) colsum[n] = s;
+}
+
 // ------------------------------------------------------------ host side
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -570,8 +649,6 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "%s: bad shape %dx%dx%d", name, M, N, K);
     if (M == 0 || N == 0) return HEXCUDA_OK;
     if ((K > 0 && (!A || !B)) || !ep.out) return fail(HEXCUDA_ERR_ARG, "%s: null pointer", name);
-    if (want_colsum && b_kmajor)
-        return fail(HEXCUDA_ERR_ARG, "%s: column sums need a row-major B", name);
     constexpr int esize = KIND == MmaKind::F16 ? 2 : 1;
     constexpr int kelems = kBKBytes / esize;
     constexpr CUtensorMapDataType dt =
@@ -592,6 +669,13 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
         if (int rc = check(cudaMemsetAsync(colsum, 0, sizeof(int32_t) * (size_t)N, d->stream),
                            "memset colsum"))
             return rc;
+    }
+    if (want_colsum && b_kmajor) {
+        // column sums of B = row sums of the K-major Bt, from the caller's copy
+        const bool vec = aligned16(B) && (K % 16) == 0;
+        rowsum_i8_kernel<<<(unsigned)((N + 7) / 8), 256, 0, d->stream>>>(
+            reinterpret_cast<const int8_t *>(B), K, colsum, N, K, vec ? 1 : 0);
+        nl++;
     }
     // row-major B that TMA can read in place: MN-major operand, no copy
     const bool b_mn = !b_kmajor && ((int64_t)N * esize) % 16 == 0 && aligned16(B) &&
@@ -742,6 +826,28 @@ HX_EXPORT int hexcuda_gemm_u8s8_pc(int dev, const uint8_t *A, const int8_t *B, c
     ep.shift_pc = shift;
     return run_gemm<MmaKind::I8, kEpiRequant, false, true>(dev, A, K, B, false, M, N, K, ep,
                                                            zpA != 0, "gemm_u8s8_pc");
+}
+
+// HMX-convention u8 x s8 GEMM (the corpus's hmx_matmul_i8_* family and
+// i8_gemm_bias_relu_requant_hmx): acc = A.B - zpA * colsum(B) in int32, then
+// sx12((acc * 17 + 8) >> 4) and, by out_kind, int32 / int8-clamp /
+// u8 bias-ReLU-clamp.  B is row-major [K, N] or, with b_transposed, K-major
+// Bt [N, K] (hmx_matmul_i8_transposeB).
+HX_EXPORT int hexcuda_gemm_hmx(int dev, const uint8_t *A, const int8_t *B, int b_transposed,
+                               const int32_t *bias, void *out, int out_kind, int M, int N, int K,
+                               int32_t zpA) {
+    if (out_kind < HEXCUDA_HMX_OUT_I32 || out_kind > HEXCUDA_HMX_OUT_U8_BIAS_RELU)
+        return fail(HEXCUDA_ERR_ARG, "gemm_hmx: out_kind %d", out_kind);
+    if (out_kind == HEXCUDA_HMX_OUT_U8_BIAS_RELU && !bias && N > 0)
+        return fail(HEXCUDA_ERR_ARG, "gemm_hmx: null bias");
+    EpiParams ep{};
+    ep.out = out;
+    ep.ldo = N;
+    ep.zpA = zpA;
+    ep.bias = out_kind == HEXCUDA_HMX_OUT_U8_BIAS_RELU ? bias : nullptr;
+    ep.hmx_mode = out_kind;
+    return run_gemm<MmaKind::I8, kEpiHmx, false, true>(dev, A, K, B, b_transposed != 0, M, N, K,
+                                                       ep, zpA != 0, "gemm_hmx");
 }
 
 // ------------------------------------------------ no-allocation u8 x s8 GEMM

@@ -389,6 +389,30 @@ HX_EXPORT int hexcuda_host_gemm_u8s8_pc(const uint8_t *A, const int8_t *B, const
     });
 }
 
+HX_EXPORT int hexcuda_host_gemm_hmx(const uint8_t *A, const int8_t *B, int b_transposed,
+                                    const int32_t *bias, void *out, int out_kind, int M, int N,
+                                    int K, int32_t zpA) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_hmx: bad shape");
+    if (out_kind < HEXCUDA_HMX_OUT_I32 || out_kind > HEXCUDA_HMX_OUT_U8_BIAS_RELU)
+        return fail(HEXCUDA_ERR_ARG, "host_gemm_hmx: out_kind %d", out_kind);
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    const bool has_bias = out_kind == HEXCUDA_HMX_OUT_U8_BIAS_RELU;
+    if (int rc = null_check("host_gemm_hmx", {A, B, out, has_bias ? bias : (const void *)A}))
+        return rc;
+    const size_t osize = out_kind == HEXCUDA_HMX_OUT_I32 ? 4 : 1;
+    return run_sharded(M, out, (size_t)N * osize, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const uint8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        const int32_t *dbias = has_bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
+        void *dout = scratch(p.d, kSlotOut, (size_t)(nr * N) * osize);
+        if (!dA || !dB || (has_bias && !dbias) || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_hmx(p.slot, dA, dB, b_transposed, dbias, dout, out_kind, (int)nr, N,
+                                K, zpA);
+    });
+}
+
 HX_EXPORT int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
                                        int M, int N, int K) {
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_f16_nt: bad shape");

@@ -86,6 +86,29 @@ def gemm_u8s8_pc(A, B, bias, zpA: int, mult, shift, zp_out: int) -> np.ndarray:
     return out
 
 
+HMX_OUT_I32, HMX_OUT_I8, HMX_OUT_U8_BIAS_RELU = 0, 1, 2
+
+
+def gemm_hmx(A, B, out_kind: int = HMX_OUT_I32, bias=None, zpA: int = 0,
+             b_transposed: bool = False) -> np.ndarray:
+    """HMX-convention u8 x s8 GEMM: sx12((acc * 17 + 8) >> 4) of
+    acc = (A - zpA) . B, then int32 / int8-clamp / u8 bias-ReLU by out_kind.
+    B is [K, N], or Bt [N, K] when b_transposed."""
+    A, B = _c(A, np.uint8), _c(B, np.int8)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    assert (B.shape[1] if b_transposed else B.shape[0]) == K
+    dt = {HMX_OUT_I32: np.int32, HMX_OUT_I8: np.int8, HMX_OUT_U8_BIAS_RELU: np.uint8}[out_kind]
+    out = np.empty((M, N), dt)
+    if out_kind == HMX_OUT_U8_BIAS_RELU:
+        bias = _c(bias, np.int32)
+        assert bias.shape == (N,)
+    check(load().hexcuda_host_gemm_hmx(_p(A), _p(B), int(b_transposed),
+                                       _p(bias) if bias is not None else None, _p(out), out_kind,
+                                       M, N, K, zpA))
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp: int) -> np.ndarray:
     a, mult, shift = _c(a, np.int32), _c(mult, np.int32), _c(shift, np.int32)
     R, Cc = a.shape

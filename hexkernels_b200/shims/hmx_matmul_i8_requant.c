@@ -1,0 +1,6 @@
+/* candidate_kernel for hmx_matmul_i8_requant on the B200 (libhexcuda). */
+#include "hexcuda.h"
+#include "kernel_api/hmx_matmul_i8_requant.h"
+void candidate_kernel(const uint8_t *A, const int8_t *B, int8_t *out, int n) {
+    hexcuda_host_gemm_hmx(A, B, 0, NULL, out, HEXCUDA_HMX_OUT_I8, n, n, n, 0);
+}

@@ -1,0 +1,6 @@
+/* candidate_kernel for hmx_matmul_i8_transposeB on the B200 (libhexcuda). */
+#include "hexcuda.h"
+#include "kernel_api/hmx_matmul_i8_transposeB.h"
+void candidate_kernel(const uint8_t *A, const int8_t *Bt, int32_t *out, int n) {
+    hexcuda_host_gemm_hmx(A, Bt, 1, NULL, out, HEXCUDA_HMX_OUT_I32, n, n, n, 0);
+}

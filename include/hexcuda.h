@@ -165,6 +165,26 @@ int hexcuda_gemm_u8s8_pc_noalloc(int dev, const uint8_t *A, const int8_t *B,
                                  int K, int32_t zpA, const int32_t *mult,
                                  const int *shift, uint8_t zp_out);
 
+/* HMX-convention u8 x s8 GEMM.  acc = sum_k (A[i][k] - zpA) * B[k][j] in
+ * int32 (two's-complement wrap), r = sx12((acc * 17 + 8) >> 4) -- the low 12
+ * bits of the matrix engine's 0x40-config requant field, sign-extended -- and
+ * by out_kind:
+ *   HEXCUDA_HMX_OUT_I32           out int32 [M,N] = r
+ *       (kernels/.../hmx_matmul_i8_64/kernel_api.h, hmx_matmul_i8_deepk,
+ *        hmx_matmul_i8_zp, hmx_matmul_i8_transposeB)
+ *   HEXCUDA_HMX_OUT_I8            out int8 = clamp(r, -128, 127)
+ *       (hmx_matmul_i8_requant/kernel_api.h)
+ *   HEXCUDA_HMX_OUT_U8_BIAS_RELU  out uint8 = clamp(max(r + bias[j], 0), 0, 255),
+ *       r + bias[j] in int32 with wrap (i8_gemm_bias_relu_requant_hmx/kernel_api.h)
+ * A uint8 [M,K] row-major.  B int8 [K,N] row-major, or with b_transposed
+ * Bt [N,K] (B column-major).  bias is read only for HEXCUDA_HMX_OUT_U8_BIAS_RELU. */
+#define HEXCUDA_HMX_OUT_I32 0
+#define HEXCUDA_HMX_OUT_I8 1
+#define HEXCUDA_HMX_OUT_U8_BIAS_RELU 2
+int hexcuda_gemm_hmx(int dev, const uint8_t *A, const int8_t *B, int b_transposed,
+                     const int32_t *bias, void *out, int out_kind, int M, int N, int K,
+                     int32_t zpA);
+
 /* fp16 GEMM, fp32 accumulate, one fp16 rounding: out[M,N] = A[M,K] . Bt[N,K]^T
  * (B column-major).  kernels/expert/fp16_attention_qkt_hmx/kernel_api.h:4-20. */
 int hexcuda_gemm_f16_nt(int dev, const uint16_t *A, const uint16_t *Bt,
@@ -232,6 +252,9 @@ int hexcuda_host_gemm_i8_zp(const int8_t *A, const int8_t *B, int8_t *out, int M
 int hexcuda_host_gemm_u8s8_pc(const uint8_t *A, const int8_t *B, const int32_t *bias,
                               uint8_t *out, int M, int N, int K, int32_t zpA,
                               const int32_t *mult, const int *shift, uint8_t zp_out);
+int hexcuda_host_gemm_hmx(const uint8_t *A, const int8_t *B, int b_transposed,
+                          const int32_t *bias, void *out, int out_kind, int M, int N,
+                          int K, int32_t zpA);
 int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
                              int M, int N, int K);
 int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uint16_t *out,

@@ -1,0 +1,7 @@
+/* candidate_kernel of kernels/expert/hmx_matmul_i8_zp/kernel_api.h:12
+ * acc = sum_k (A - zp) * B, out int32 = sx12((acc * 17 + 8) >> 4). */
+#ifndef HEXCUDA_KAPI_HMX_MATMUL_I8_ZP_H
+#define HEXCUDA_KAPI_HMX_MATMUL_I8_ZP_H
+#include <stdint.h>
+void candidate_kernel(const uint8_t *A, const int8_t *B, int zp, int32_t *out, int n);
+#endif

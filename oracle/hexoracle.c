@@ -153,6 +153,56 @@ void oracle_gemm_u8s8_pc_rows(const uint8_t *A, const int8_t *B,
     free(colsum);
 }
 
+/* sx12 of the HMX references (e.g. hmx_matmul_i8_64/reference.c:4):
+ * low 12 bits, sign-extended. */
+static inline int32_t sx12(int32_t f) {
+    int32_t v = f & 0xFFF;
+    if (v & 0x800) v -= 0x1000;
+    return v;
+}
+
+/* The six HMX-convention references (cited in hexoracle.h).  acc is the
+ * int32 sum of (A - zpA) * B in k order with two's-complement wrap; the
+ * (acc * 17 + 8) >> 4 step is the references' int arithmetic (gcc: wrap and
+ * arithmetic shift). */
+void oracle_gemm_hmx_rows(const uint8_t *A, const int8_t *B, int b_transposed,
+                          const int32_t *bias, void *out, int M, int N, int K,
+                          int32_t zpA, int mode, int r0, int r1) {
+    (void)M;
+    int32_t *acc = (int32_t *)malloc(sizeof(int32_t) * (size_t)(N > 0 ? N : 1));
+    for (int i = r0; i < r1; i++) {
+        memset(acc, 0, sizeof(int32_t) * (size_t)N);
+        for (int k = 0; k < K; k++) {
+            const uint32_t a = (uint32_t)((int32_t)A[(size_t)i * K + k] - zpA);
+            if (b_transposed) {
+                for (int j = 0; j < N; j++)
+                    acc[j] = (int32_t)((uint32_t)acc[j] + a * (uint32_t)(int32_t)B[(size_t)j * K + k]);
+            } else {
+                const int8_t *b = B + (size_t)k * N;
+                for (int j = 0; j < N; j++)
+                    acc[j] = (int32_t)((uint32_t)acc[j] + a * (uint32_t)(int32_t)b[j]);
+            }
+        }
+        for (int j = 0; j < N; j++) {
+            const int32_t f = (int32_t)((uint32_t)acc[j] * 17u + 8u) >> 4;
+            const int32_t r = sx12(f);
+            const size_t o = (size_t)i * N + j;
+            if (mode == 0) {
+                ((int32_t *)out)[o] = r;
+            } else if (mode == 1) {
+                ((int8_t *)out)[o] = (int8_t)(r > 127 ? 127 : (r < -128 ? -128 : r));
+            } else {
+                /* the reference's int add; two's-complement wrap where
+                 * r + bias[j] leaves the int32 range */
+                int32_t v = (int32_t)((uint32_t)r + (uint32_t)bias[j]);
+                v = v > 0 ? v : 0;
+                ((uint8_t *)out)[o] = (uint8_t)(v > 255 ? 255 : v);
+            }
+        }
+    }
+    free(acc);
+}
+
 /* kernels/expert/requant_per_channel/reference.c:4-16 */
 void oracle_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
                                 const int32_t *mult, const int *shift, int8_t zp) {

@@ -55,6 +55,21 @@ void oracle_gemm_u8s8_pc_rows(const uint8_t *A, const int8_t *B,
                               const int32_t *mult, const int *shift,
                               uint8_t zp_out, int r0, int r1);
 
+/* HMX-convention int8 GEMMs: acc = sum_k (A[i][k] - zpA) * B[k][j] (int32),
+ * r = sx12((acc * 17 + 8) >> 4) (the matrix engine's 0x40-config requant
+ * field, sign-extended from 12 bits), then by `mode`:
+ *   0: out int32 = r   (hmx_matmul_i8_64/reference.c:4-12,
+ *                       hmx_matmul_i8_deepk/reference.c:10-17,
+ *                       hmx_matmul_i8_zp/reference.c:14-22,
+ *                       hmx_matmul_i8_transposeB/reference.c:13-21)
+ *   1: out int8 = clamp(r, -128, 127)   (hmx_matmul_i8_requant/reference.c:4-13)
+ *   2: out uint8 = clamp(max(r + bias[j], 0), 0, 255)
+ *                       (i8_gemm_bias_relu_requant_hmx/reference.c:20-31)
+ * A uint8 [M][K]; B int8 [K][N], or Bt [N][K] when b_transposed. */
+void oracle_gemm_hmx_rows(const uint8_t *A, const int8_t *B, int b_transposed,
+                          const int32_t *bias, void *out, int M, int N, int K,
+                          int32_t zpA, int mode, int r0, int r1);
+
 /* kernels/expert/requant_per_channel/reference.c:2-17 (rows = channels) */
 void oracle_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
                                 const int32_t *mult, const int *shift, int8_t zp);

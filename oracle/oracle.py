@@ -95,6 +95,20 @@ def gemm_u8s8_pc(A, B, bias, zpA, mult, shift, zp_out, rows=None):
     return out
 
 
+def gemm_hmx(A, B, out_kind=0, bias=None, zpA=0, b_transposed=False):
+    """HMX-convention u8 x s8 GEMM: out_kind 0 int32, 1 int8, 2 uint8 bias-ReLU."""
+    A, B = np.ascontiguousarray(A, np.uint8), np.ascontiguousarray(B, np.int8)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    out = np.zeros((M, N), {0: np.int32, 1: np.int8, 2: np.uint8}[out_kind])
+    if out_kind == 2:
+        bias = np.ascontiguousarray(bias, np.int32)
+    lib().oracle_gemm_hmx_rows(_p(A), _p(B), int(b_transposed),
+                               _p(bias) if bias is not None else None, _p(out), M, N, K,
+                               C.c_int32(zpA), out_kind, 0, M)
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp):
     a = np.ascontiguousarray(a, np.int32)
     R, Cc = a.shape

@@ -252,6 +252,84 @@ def gen_gemm_u8s8_pc(ref):
     save("gemm_u8s8_pc_small", **arrays)
 
 
+def gen_hmx(ref):
+    # The six HMX-convention u8 x s8 bundles.  Harness cases regenerate each
+    # harness.c's inputs (hvx_lcg seed, value map, planted bias edges):
+    #   hmx_matmul_i8_requant/harness.c:14-18   N 32, seed 0xC4F8, A %16, B %9-4
+    #   hmx_matmul_i8_zp/harness.c:18-21        N 32, seed 0x2E90, A %8, B %7-3, zp 2
+    #   i8_gemm_bias_relu_requant_hmx/harness.c:24-31
+    #                                           N 64, seed 0xA6F7, A %8, B %7-3,
+    #                                           bias %4001-2000, bias[0..2] = -2000, 2000, 0
+    #   hmx_matmul_i8_64/harness.c:13-16        N 64, seed 0x8B22, A %8, B %7-3
+    #   hmx_matmul_i8_deepk/harness.c:14-17     N 32, K 128, seed 0xD5A9, A %4, B %3-1
+    #   hmx_matmul_i8_transposeB/harness.c:17-20 N 32, seed 0x7B21, A %8, Bt %7-3
+    # Wide cases use full-range u8 / s8 inputs (|acc| well past the 12-bit
+    # field, so the sx12 wrap is exercised) at n not a multiple of the GEMM
+    # tile; products stay inside int32 there, so the reference is well defined.
+    def lcg_mod(g, n, mod, off, dtype):
+        return np.array([(next(g) % mod) - off for _ in range(n)], np.int64).astype(dtype)
+
+    arrays = {}
+
+    def run(tag, fn, A, B, extra_pre, out, *tail):
+        getattr(ref, fn)(ptr(A), ptr(B), *extra_pre, ptr(out), *tail)
+        arrays[f"{tag}_A"], arrays[f"{tag}_B"], arrays[f"{tag}_out"] = A, B, out
+
+    n = 32
+    g = lcg_stream(0xC4F8)
+    A = lcg_mod(g, n * n, 16, 0, np.uint8); B = lcg_mod(g, n * n, 9, 4, np.int8)
+    run("requant", "ref_hmx_matmul_i8_requant", A, B, [], np.full(n * n, 0x5A, np.int8), n)
+    g = lcg_stream(0x2E90)
+    A = lcg_mod(g, n * n, 8, 0, np.uint8); B = lcg_mod(g, n * n, 7, 3, np.int8)
+    arrays["zp_zp"] = np.int32(2)
+    run("zp", "ref_hmx_matmul_i8_zp", A, B, [C.c_int(2)], np.zeros(n * n, np.int32), n)
+    n = 64
+    g = lcg_stream(0xA6F7)
+    A = lcg_mod(g, n * n, 8, 0, np.uint8); B = lcg_mod(g, n * n, 7, 3, np.int8)
+    bias = lcg_mod(g, n, 4001, 2000, np.int32)
+    bias[0], bias[1], bias[2] = -2000, 2000, 0
+    arrays["bias_relu_bias"] = bias
+    run("bias_relu", "ref_i8_gemm_bias_relu_requant_hmx", A, B, [ptr(bias)],
+        np.zeros(n * n, np.uint8), n)
+    g = lcg_stream(0x8B22)
+    A = lcg_mod(g, n * n, 8, 0, np.uint8); B = lcg_mod(g, n * n, 7, 3, np.int8)
+    run("i64", "ref_hmx_matmul_i8_64", A, B, [], np.zeros(n * n, np.int32), n)
+    n, K = 32, 128
+    g = lcg_stream(0xD5A9)
+    A = lcg_mod(g, n * K, 4, 0, np.uint8); B = lcg_mod(g, K * n, 3, 1, np.int8)
+    arrays["deepk_K"] = np.int32(K)
+    run("deepk", "ref_hmx_matmul_i8_deepk", A, B, [], np.zeros(n * n, np.int32), n, K)
+    n = 32
+    g = lcg_stream(0x7B21)
+    A = lcg_mod(g, n * n, 8, 0, np.uint8); B = lcg_mod(g, n * n, 7, 3, np.int8)
+    run("transposeB", "ref_hmx_matmul_i8_transposeB", A, B, [], np.zeros(n * n, np.int32), n)
+
+    # wide, full-range cases
+    rng = np.random.default_rng(11)
+    u8 = lambda k: rng.integers(0, 256, size=k, dtype=np.uint8)
+    s8 = lambda k: rng.integers(-128, 128, size=k, dtype=np.int8)
+    n = 160
+    run("w_requant", "ref_hmx_matmul_i8_requant", u8(n * n), s8(n * n), [],
+        np.zeros(n * n, np.int8), n)
+    n = 144
+    arrays["w_zp_zp"] = np.int32(131)
+    run("w_zp", "ref_hmx_matmul_i8_zp", u8(n * n), s8(n * n), [C.c_int(131)],
+        np.zeros(n * n, np.int32), n)
+    n = 200
+    wb = rng.integers(-3000, 3001, size=n, dtype=np.int32)
+    arrays["w_bias_relu_bias"] = wb
+    run("w_bias_relu", "ref_i8_gemm_bias_relu_requant_hmx", u8(n * n), s8(n * n), [ptr(wb)],
+        np.zeros(n * n, np.uint8), n)
+    n, K = 136, 1000
+    arrays["w_deepk_K"] = np.int32(K)
+    run("w_deepk", "ref_hmx_matmul_i8_deepk", u8(n * K), s8(K * n), [],
+        np.zeros(n * n, np.int32), n, K)
+    n = 130
+    run("w_transposeB", "ref_hmx_matmul_i8_transposeB", u8(n * n), s8(n * n), [],
+        np.zeros(n * n, np.int32), n)
+    save("hmx_gemm", **arrays)
+
+
 # ----------------------------------------------------------------- fp16
 
 def gen_hf_q(g, mod, off, step):
@@ -424,6 +502,7 @@ def main():
     gen_requant_per_channel(ref)
     gen_requantize_i32_u8(ref)
     gen_gemm_u8s8_pc(ref)
+    gen_hmx(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

@@ -85,3 +85,31 @@ def test_shim_attn_f16(hx, oracle):
     fn(p(Q), p(K), p(V), p(O), Bn, H, S, D, 1 / np.sqrt(D), 1)
     exp = oracle.attn_f16(Q, K, V, 1 / np.sqrt(D), True)
     assert np.all(np.abs(O.astype(np.float64) - exp) <= 1e-2 * np.abs(exp.astype(np.float64)) + 2e-3)
+
+
+def test_shim_hmx_bundles(hx, oracle):
+    """The six HMX-convention shims through candidate_kernel at a size that
+    spans several tiles (n = 200, full-range values)."""
+    rng = np.random.default_rng(3)
+    n, K = 200, 520
+    A = rng.integers(0, 256, (n, n), dtype=np.uint8)
+    B = rng.integers(-128, 128, (n, n), dtype=np.int8)
+    bias = rng.integers(-2000, 2000, n).astype(np.int32)
+    o32 = np.zeros((n, n), np.int32)
+    shim("hmx_matmul_i8_64")(p(A), p(B), p(o32), n)
+    np.testing.assert_array_equal(o32, oracle.gemm_hmx(A, B, 0))
+    shim("hmx_matmul_i8_zp")(p(A), p(B), 77, p(o32), n)
+    np.testing.assert_array_equal(o32, oracle.gemm_hmx(A, B, 0, None, 77))
+    Bt = np.ascontiguousarray(B.T)
+    shim("hmx_matmul_i8_transposeB")(p(A), p(Bt), p(o32), n)
+    np.testing.assert_array_equal(o32, oracle.gemm_hmx(A, B, 0))
+    o8 = np.zeros((n, n), np.int8)
+    shim("hmx_matmul_i8_requant")(p(A), p(B), p(o8), n)
+    np.testing.assert_array_equal(o8, oracle.gemm_hmx(A, B, 1))
+    u8 = np.zeros((n, n), np.uint8)
+    shim("i8_gemm_bias_relu_requant_hmx")(p(A), p(B), p(bias), p(u8), n)
+    np.testing.assert_array_equal(u8, oracle.gemm_hmx(A, B, 2, bias))
+    Ad = rng.integers(0, 256, (n, K), dtype=np.uint8)
+    Bd = rng.integers(-128, 128, (K, n), dtype=np.int8)
+    shim("hmx_matmul_i8_deepk")(p(Ad), p(Bd), p(o32), n, K)
+    np.testing.assert_array_equal(o32, oracle.gemm_hmx(Ad, Bd, 0))

@@ -130,6 +130,46 @@ def test_gemm_u8s8_extreme_values(hx, oracle):
                                   oracle.gemm_u8s8_pc(A, B, bias, 128, mult, shift, 128))
 
 
+# ------------------------------------------------- HMX-convention GEMMs
+
+from test_oracle_golden import HMX_CASES, hmx_case  # noqa: E402
+
+
+@pytest.mark.parametrize("tag,kind,bt", HMX_CASES)
+def test_hmx_gemm_golden(hx, tag, kind, bt):
+    A, B, out, K, N, zp, bias = hmx_case(golden("hmx_gemm"), tag)
+    B = B.reshape((N, K) if bt else (K, N))
+    np.testing.assert_array_equal(hx.gemm_hmx(A, B, kind, bias, zp, bt), out)
+
+
+@pytest.mark.parametrize("M,N,K", I8_SHAPES)
+def test_hmx_gemm_random(hx, oracle, M, N, K):
+    rng = np.random.default_rng(M * 5 + N * 11 + K)
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    Bt = np.ascontiguousarray(B.T)
+    bias = rng.integers(-3000, 3000, N).astype(np.int32)
+    for kind in (0, 1, 2):
+        for zpa in (0, 128, -5):
+            exp = oracle.gemm_hmx(A, B, kind, bias, zpa)
+            np.testing.assert_array_equal(hx.gemm_hmx(A, B, kind, bias, zpa), exp)
+            np.testing.assert_array_equal(hx.gemm_hmx(A, Bt, kind, bias, zpa, True), exp)
+
+
+def test_hmx_gemm_deep_k_wraps(hx, oracle):
+    """K = 8192 full-range operands: acc * 17 leaves int32, so the 12-bit
+    field wraps; the int32 two's-complement arithmetic must agree."""
+    M, N, K = 256, 384, 8192
+    rng = np.random.default_rng(7)
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    for zpa in (0, 128):
+        exp = oracle.gemm_hmx(A, B, 0, None, zpa)
+        np.testing.assert_array_equal(hx.gemm_hmx(A, B, 0, None, zpa), exp)
+        np.testing.assert_array_equal(
+            hx.gemm_hmx(A, np.ascontiguousarray(B.T), 0, None, zpa, True), exp)
+
+
 # --------------------------------------------------------------- fp16 GEMMs
 
 def assert_f16_gemm_close(got, exp):

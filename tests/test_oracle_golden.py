@@ -90,6 +90,35 @@ def test_gemm_u8s8_pc_small(oracle):
         np.testing.assert_array_equal(out, k("out"))
 
 
+# (fixture tag, out_kind, b_transposed) of the six HMX-convention bundles,
+# harness cases and wide full-range cases
+HMX_CASES = [("requant", 1, False), ("zp", 0, False), ("bias_relu", 2, False), ("i64", 0, False),
+             ("deepk", 0, False), ("transposeB", 0, True), ("w_requant", 1, False),
+             ("w_zp", 0, False), ("w_bias_relu", 2, False), ("w_deepk", 0, False),
+             ("w_transposeB", 0, True)]
+
+
+def hmx_case(g, tag):
+    A, B, out = g[f"{tag}_A"], g[f"{tag}_B"], g[f"{tag}_out"]
+    K = int(g[f"{tag}_K"]) if f"{tag}_K" in g else int(round(np.sqrt(A.size)))
+    M = A.size // K
+    N = out.size // M
+    zp = int(g[f"{tag}_zp"]) if f"{tag}_zp" in g else 0
+    bias = g[f"{tag}_bias"] if f"{tag}_bias" in g else None
+    return A.reshape(M, K), B, out.reshape(M, N), K, N, zp, bias
+
+
+@pytest.mark.parametrize("tag,kind,bt", HMX_CASES)
+def test_hmx_gemm_golden(oracle, tag, kind, bt):
+    A, B, out, K, N, zp, bias = hmx_case(golden("hmx_gemm"), tag)
+    B = B.reshape((N, K) if bt else (K, N))
+    got = oracle.gemm_hmx(A, B, kind, bias, zp, bt)
+    np.testing.assert_array_equal(got, out)
+    if tag.startswith("w_"):
+        # the wide cases leave the 12-bit field: outputs wrap / saturate
+        assert len(np.unique(got)) > 50
+
+
 @pytest.mark.parametrize("name,kind", [("gemm_f16_nt_harness", "nt"), ("gemm_f16_nn_harness", "nn"),
                                        ("attn_av_f16_harness", "nn_av")])
 def test_f16_gemm_harness(oracle, name, kind):

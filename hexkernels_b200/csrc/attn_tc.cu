@@ -551,9 +551,13 @@ __device__ __forceinline__ void exp2_fma2(uint64_t x2, float &r0, float &r1) {
 // warpgroup per tile, so the tensor pipe always has the other tile's MMAs to
 // run while a warpgroup does its exponentials.
 //
-// Per CTA, 320 threads: warp 0 TMA, warp 1 MMA, warps 2..5 softmax of tile
-// a, warps 6..9 softmax of tile b (one query row per thread, all 128 key
-// columns of the tile per thread, so the row max and sum need no exchange).
+// Per CTA, 384 threads in three warpgroups: warpgroup 0 = warp 0 TMA, warp 1
+// MMA (warps 2, 3 idle); warpgroup 1 = softmax of tile a, warpgroup 2 =
+// softmax of tile b (one query row per thread, all 128 key columns of the
+// tile per thread, so the row max and sum need no exchange).  The register
+// file is split with setmaxnreg: warpgroup 0 drops to kRegsCtl, the softmax
+// warpgroups rise to kRegsSoftmax, enough to hold a thread's whole score row
+// (128 fp32) so the row is read from TMEM once.
 // TMEM (512 columns): S_a [0,128), S_b [128,256), O_a [256,384), O_b
 // [384,512); P_x is written as fp16 pairs over S_x's first 64 columns once
 // the softmax has read them.  The MMA warp issues, per key tile j,
@@ -566,6 +570,16 @@ constexpr int kPairQ = 256;
 // The MUFU unit is not the limiter of this kernel (issue slots are), and the
 // polynomial costs ~7 issue slots per score against 1 for ex2.
 constexpr int kPolyEvery = 0;
+// Register split of the 384-thread CTA: launched at kRegsLaunch per thread
+// (ptxas's count for __launch_bounds__(384, 1)), 128 threads give up
+// registers, 256 take them: 128 * kRegsCtl + 256 * kRegsSoftmax must not
+// exceed 384 * kRegsLaunch, or setmaxnreg.inc would wait forever.  Per SM
+// sub-partition (warps w, w + 4, w + 8 share one) the same sum holds.
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsCtl = 104;
+constexpr int kRegsSoftmax = 200;
+static_assert(128 * kRegsCtl + 256 * kRegsSoftmax <= 384 * kRegsLaunch, "register split");
+static_assert(kRegsCtl % 8 == 0 && kRegsSoftmax % 8 == 0, "setmaxnreg takes multiples of 8");
 
 struct PPSmem {
     static constexpr int kTile = 128 * 128 * 2;     // 32 KB
@@ -598,7 +612,7 @@ __device__ __forceinline__ void pp_item(int w, const AttnArgs &a, int &h, int &q
     }
 }
 
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(384, 1)
     attn_pp_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                    const __grid_constant__ CUtensorMap tmV, const AttnArgs args) {
     using L = PPSmem;
@@ -644,7 +658,10 @@ __global__ void __launch_bounds__(320, 1)
     tc::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0) {
+    if (warp < 4) {
+      // warpgroup 0: one setmaxnreg for all four warps, then the roles
+      tc::setmaxnreg_dec<kRegsCtl>();
+      if (warp == 0) {
         if (lane == 0) {
             // ----------------------------------------------------------- TMA
             uint32_t g = 0;
@@ -725,7 +742,6 @@ __global__ void __launch_bounds__(320, 1)
                     tc::mma_ts_f16(tmem_base + 256 + x * 128, tmem_base + x * 128 + k * 8,
                                    tc::sdesc_mnmajor_sw128(vb + k * 2048, kSub, 1024), idesc_pv,
                                    (!first || k > 0) ? 1u : 0u);
-                tc::mma_commit(&pv_done[x]);
             };
             for (int w = blockIdx.x; w < args.nitems && ok && !*abort_flag; w += gridDim.x, item++) {
                 int h, qp, nkv_a, nkv_b;
@@ -756,6 +772,7 @@ __global__ void __launch_bounds__(320, 1)
                         if (!ok) break;
                         tc::tc_fence_after();
                         issue_pv(x, gj, j == 0);
+                        tc::mma_commit(&pv_done[x]);
                         if (x == 1) tc::mma_commit(&v_empty[gj & 1]);
                         if (more && j + 1 < nkv[x]) {
                             if (!k_ready) {
@@ -784,9 +801,11 @@ __global__ void __launch_bounds__(320, 1)
                 }
             }
         }
+      }
     } else {
         // ----------------------------------------------------- softmax x
-        const int x = (warp - 2) >> 2;
+        tc::setmaxnreg_inc<kRegsSoftmax>();
+        const int x = (warp - 4) >> 2;
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
@@ -819,20 +838,25 @@ __global__ void __launch_bounds__(320, 1)
                             r[e] = __float_as_uint(-INFINITY);
                     }
                 };
-                // pass 1: row max over the 128 raw scores (scale folded later)
+                // the whole score row into registers: four loads, one wait
+                uint32_t sr[4][32];
+#pragma unroll
+                for (int cc = 0; cc < 4; cc++) tc::tmem_ld_32x32b_x32(s_addr + cc * 32, sr[cc]);
+                tc::tmem_ld_wait(sr[0]);
+                tc::reg_fence(sr[1]);
+                tc::reg_fence(sr[2]);
+                tc::reg_fence(sr[3]);
+                // row max over the 128 raw scores (scale folded later)
                 float mx[8];
 #pragma unroll
                 for (int u = 0; u < 8; u++) mx[u] = -INFINITY;
 #pragma unroll
                 for (int cc = 0; cc < 4; cc++) {
-                    uint32_t r[32];
-                    tc::tmem_ld_32x32b_x32(s_addr + cc * 32, r);
-                    tc::tmem_ld_wait(r);
-                    if (need_mask) mask_chunk(r, cc);
+                    if (need_mask) mask_chunk(sr[cc], cc);
 #pragma unroll
                     for (int i = 0; i < 16; i++)
-                        mx[i & 7] = max3(mx[i & 7], __uint_as_float(r[2 * i]),
-                                         __uint_as_float(r[2 * i + 1]));
+                        mx[i & 7] = max3(mx[i & 7], __uint_as_float(sr[cc][2 * i]),
+                                         __uint_as_float(sr[cc][2 * i + 1]));
                 }
                 const float mt = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]),
                                       fmaxf(mx[6], mx[7])) *
@@ -841,6 +865,9 @@ __global__ void __launch_bounds__(320, 1)
                 if (j == 0) {
                     m_ref = m_new;
                 } else {
+                    // Lazy rescale: the reference max moves only when the row
+                    // max rose by more than 8 (P stays below 2^8 otherwise, well
+                    // inside fp16; O / l does not depend on the reference).
                     const bool need = m_new > m_ref + 8.0f;
                     if (__any_sync(0xffffffffu, need)) {
                         // O_x is stable once P V of the previous key tile is done
@@ -866,21 +893,17 @@ __global__ void __launch_bounds__(320, 1)
                         }
                     }
                 }
-                // pass 2: P = 2^(s*scale*log2e - m_ref), fp16 pairs written over
-                // S columns 16cc..16cc+15 (already read: chunk cc reads columns
-                // 32cc.. which are at or past the ones it overwrites).  Pairs of
-                // scores go through one f32x2 FMA; one pair in four takes the
-                // FMA-pipe exponential, the rest the MUFU ex2; the row sum is
-                // accumulated in four packed pairs.
+                // P = 2^(s*scale*log2e - m_ref) from the registers, fp16 pairs
+                // written over S columns 16cc..16cc+15.  Pairs of scores go
+                // through one f32x2 FMA; with kPolyEvery > 0 one pair in
+                // kPolyEvery takes the FMA-pipe exponential, the rest the MUFU
+                // ex2; the row sum is accumulated in four packed pairs.
                 uint64_t acc2[4] = {0, 0, 0, 0};
                 const uint64_t sl2 = pk2(args.scale_log2, args.scale_log2);
                 const uint64_t nm2 = pk2(-m_ref, -m_ref);
 #pragma unroll
                 for (int cc = 0; cc < 4; cc++) {
-                    uint32_t r[32];
-                    tc::tmem_ld_32x32b_x32(s_addr + cc * 32, r);
-                    tc::tmem_ld_wait(r);
-                    if (need_mask) mask_chunk(r, cc);
+                    const uint32_t (&r)[32] = sr[cc];
                     uint32_t pk[16];
 #pragma unroll
                     for (int e2 = 0; e2 < 16; e2++) {
@@ -1037,6 +1060,14 @@ int launch_attn_pp(Dev *d, const __half *Q, const __half *K, const __half *V, __
                                                 L::kTotal),
                            "cudaFuncSetAttribute(attn_pp)"))
             return rc;
+        // the register split assumes this launch count; a build with another
+        // count would leave setmaxnreg.inc short of registers, so refuse it
+        cudaFuncAttributes fa;
+        if (int rc = check(cudaFuncGetAttributes(&fa, attn_pp_kernel), "cudaFuncGetAttributes(attn_pp)"))
+            return rc;
+        if (fa.numRegs != kRegsLaunch)
+            return fail(HEXCUDA_ERR_CUDA, "attn_pp_kernel built with %d registers, expected %d",
+                        fa.numRegs, kRegsLaunch);
         attr_done[d->ordinal & 63] = true;
     }
     CUtensorMap mq, mk, mv;
@@ -1054,7 +1085,7 @@ int launch_attn_pp(Dev *d, const __half *Q, const __half *K, const __half *V, __
     a.O = O;
     a.err_word = d->err_word;
     const int grid = a.nitems < d->sms ? a.nitems : d->sms;
-    attn_pp_kernel<<<grid, 320, L::kTotal, d->stream>>>(mq, mk, mv, a);
+    attn_pp_kernel<<<grid, 384, L::kTotal, d->stream>>>(mq, mk, mv, a);
     return HEXCUDA_OK;
 }
 

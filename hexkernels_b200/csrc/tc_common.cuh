@@ -205,6 +205,14 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
                  :
                  : "memory");
 }
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
 // Ordering point for registers filled by a TMEM load that an earlier
 // tmem_ld_wait already completed.
 __device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
@@ -242,6 +250,18 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
         "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
         "r"(r[15])
         : "memory");
+}
+
+// Warpgroup-wide register reallocation (all 128 threads of the warpgroup
+// execute it): dec returns registers to the CTA's pool, inc waits until the
+// pool can grant the new per-thread count.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 __device__ __forceinline__ void tmem_st_wait() {

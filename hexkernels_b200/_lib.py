@@ -60,6 +60,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_gemm_i8_zp": (I, [I, P, P, P, I, I, I, I32, I32, I]),
     "hexcuda_gemm_u8s8_pc": (I, [I, P, P, P, P, I, I, I, I32, P, P, U8]),
     "hexcuda_gemm_hmx": (I, [I, P, P, I, P, P, I, I, I, I, I32]),
+    "hexcuda_gemm_hmx_ex": (I, [I, P, P, I, P, P, I, P, P, I, I, I, I, I, I, I32]),
     "hexcuda_gemm_u8s8_pc_noalloc": (I, [I, P, P, P, P, I, I, I, I32, P, P, U8]),
     "hexcuda_gemm_f16_nt": (I, [I, P, P, P, I, I, I]),
     "hexcuda_gemm_f16_nn": (I, [I, P, P, P, I, I, I]),
@@ -80,6 +81,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_gemm_i8_zp": (I, [P, P, P, I, I, I, I32, I32, I]),
     "hexcuda_host_gemm_u8s8_pc": (I, [P, P, P, P, I, I, I, I32, P, P, U8]),
     "hexcuda_host_gemm_hmx": (I, [P, P, I, P, P, I, I, I, I, I32]),
+    "hexcuda_host_gemm_hmx_ex": (I, [P, P, I, P, P, I, P, P, I, I, I, I, I, I, I32]),
     "hexcuda_host_gemm_f16_nt": (I, [P, P, P, I, I, I]),
     "hexcuda_host_gemm_f16_nn": (I, [P, P, P, I, I, I]),
     "hexcuda_host_attn_f16": (I, [P, P, P, P, I, I, I, I, F, I]),

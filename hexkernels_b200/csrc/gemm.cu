@@ -70,9 +70,13 @@ struct EpiParams {
     int zp;
     int lo, hi;
     // HMX-convention epilogue (kEpiHmx): acc32 as above, then
-    //   r = sx12((acc32 * 17 + 8) >> 4)   (int32 wrap, arithmetic shift)
-    //   hmx_mode 0: int32 r; 1: int8 clamp(r); 2: uint8 clamp(max(r + bias[j], 0))
-    int hmx_mode;
+    //   v = sx12((acc32 * 17 + 8) >> 4)    (int32 wrap, arithmetic shift)
+    //   v += bias[j] (null: 0); v += res[i][j] (res_kind 1 int32, 2 int8,
+    //   row-major [M, N]); activation; store (HEXCUDA_HMX_STORE_* of
+    //   hexcuda.h); col_major stores out[j * ldo + i].  All adds wrap.
+    int hmx_store, hmx_act, res_kind, col_major;
+    const void *res;
+    const void *lut;
 };
 
 struct GemmArgs {
@@ -132,6 +136,29 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = __float2half_rn(__uint_as_float(r[i]));
         }
     } else if constexpr (EPI == kEpiHmx) {
+        // residual of this row's 32 columns (rows past M are never stored)
+        int32_t rv[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) rv[i] = 0;
+        const bool full = col0 + 32 <= ep.N;
+        if (ep.res_kind != 0 && row < ep.M) {
+            const size_t base = (size_t)row * ep.N + col0;
+            if (ep.res_kind == 1) {
+                const int32_t *rp = reinterpret_cast<const int32_t *>(ep.res) + base;
+                if (full && (reinterpret_cast<uintptr_t>(rp) & 15u) == 0) {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int4 t = __ldg(reinterpret_cast<const int4 *>(rp) + i);
+                        rv[4 * i] = t.x, rv[4 * i + 1] = t.y, rv[4 * i + 2] = t.z, rv[4 * i + 3] = t.w;
+                    }
+                } else {
+                    for (int i = 0; i < 32 && col0 + i < ep.N; i++) rv[i] = __ldg(rp + i);
+                }
+            } else {
+                const int8_t *rp = reinterpret_cast<const int8_t *>(ep.res) + base;
+                for (int i = 0; i < 32 && col0 + i < ep.N; i++) rv[i] = __ldg(rp + i);
+            }
+        }
         int32_t v[32];
 #pragma unroll
         for (int i4 = 0; i4 < 8; i4++) {
@@ -142,20 +169,42 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             for (int u = 0; u < 4; u++) {
                 const uint32_t a32 = r[4 * i4 + u] - (uint32_t)cc[u];
                 const int32_t f = (int32_t)(a32 * 17u + 8u) >> 4;
-                int32_t x = (int32_t)((uint32_t)f << 20) >> 20;  // low 12 bits, sign-extended
-                if (ep.hmx_mode == 1) {
-                    x = min(max(x, -128), 127);
-                } else if (ep.hmx_mode == 2) {
-                    x = (int32_t)((uint32_t)x + (uint32_t)bb[u]);
-                    x = min(max(x, 0), 255);
+                uint32_t xu = (uint32_t)((int32_t)((uint32_t)f << 20) >> 20);  // sx12
+                xu += (uint32_t)bb[u] + (uint32_t)rv[4 * i4 + u];
+                int32_t x = (int32_t)xu;
+                if (ep.hmx_act == HEXCUDA_HMX_ACT_RELU) x = max(x, 0);
+                else if (ep.hmx_act == HEXCUDA_HMX_ACT_LEAKY_SHR3) x = x >= 0 ? x : (x >> 3);
+                switch (ep.hmx_store) {
+                case HEXCUDA_HMX_STORE_I8_SAT: x = min(max(x, -128), 127); break;
+                case HEXCUDA_HMX_STORE_U8_SAT: x = min(max(x, 0), 255); break;
+                case HEXCUDA_HMX_STORE_U16_FIELD: x &= 0xFFF; break;
+                case HEXCUDA_HMX_STORE_LUT_I32:
+                    x = __ldg(reinterpret_cast<const int32_t *>(ep.lut) + min(max(x + 128, 0), 255));
+                    break;
+                case HEXCUDA_HMX_STORE_LUT_I8:
+                    x = __ldg(reinterpret_cast<const int8_t *>(ep.lut) + (min(max(x, -128), 127) + 128));
+                    break;
+                default: break;  // I32; I8_LOW keeps the low byte at the store
                 }
                 v[4 * i4 + u] = x;
             }
         }
         if (row >= ep.M) return;
-        if (ep.hmx_mode == 0) {
+        const int es = (ep.hmx_store == HEXCUDA_HMX_STORE_I32 ||
+                        ep.hmx_store == HEXCUDA_HMX_STORE_LUT_I32) ? 4
+                       : ep.hmx_store == HEXCUDA_HMX_STORE_U16_FIELD ? 2 : 1;
+        if (ep.col_major) {
+            // lanes are consecutive rows: each column's store is one
+            // contiguous run across the warp
+            for (int i = 0; i < 32 && col0 + i < ep.N; i++) {
+                const size_t o = (size_t)(col0 + i) * ep.ldo + row;
+                if (es == 4) reinterpret_cast<int32_t *>(ep.out)[o] = v[i];
+                else if (es == 2) reinterpret_cast<uint16_t *>(ep.out)[o] = (uint16_t)v[i];
+                else reinterpret_cast<uint8_t *>(ep.out)[o] = (uint8_t)v[i];
+            }
+        } else if (es == 4) {
             int32_t *o = reinterpret_cast<int32_t *>(ep.out) + (size_t)row * ep.ldo + col0;
-            if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
+            if (full && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
                 uint4 *dst = reinterpret_cast<uint4 *>(o);
 #pragma unroll
                 for (int i = 0; i < 8; i++)
@@ -164,6 +213,22 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             } else {
                 for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = v[i];
             }
+        } else if (es == 2) {
+            uint16_t *o = reinterpret_cast<uint16_t *>(ep.out) + (size_t)row * ep.ldo + col0;
+            if (full && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
+                uint4 *dst = reinterpret_cast<uint4 *>(o);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+                        w[k] = ((uint32_t)v[8 * i + 2 * k] & 0xFFFFu) |
+                               ((uint32_t)v[8 * i + 2 * k + 1] << 16);
+                    dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            } else {
+                for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = (uint16_t)v[i];
+            }
         } else {
             uint8_t *o = reinterpret_cast<uint8_t *>(ep.out) + (size_t)row * ep.ldo + col0;
             uint32_t w[8];
@@ -171,7 +236,7 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             for (int i = 0; i < 8; i++)
                 w[i] = ((uint32_t)v[4 * i] & 0xFFu) | (((uint32_t)v[4 * i + 1] & 0xFFu) << 8) |
                        (((uint32_t)v[4 * i + 2] & 0xFFu) << 16) | ((uint32_t)v[4 * i + 3] << 24);
-            if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
+            if (full && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
                 uint4 *dst = reinterpret_cast<uint4 *>(o);
                 dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
                 dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
@@ -833,21 +898,51 @@ HX_EXPORT int hexcuda_gemm_u8s8_pc(int dev, const uint8_t *A, const int8_t *B, c
 // sx12((acc * 17 + 8) >> 4) and, by out_kind, int32 / int8-clamp /
 // u8 bias-ReLU-clamp.  B is row-major [K, N] or, with b_transposed, K-major
 // Bt [N, K] (hmx_matmul_i8_transposeB).
+HX_EXPORT int hexcuda_gemm_hmx_ex(int dev, const uint8_t *A, const int8_t *B, int b_transposed,
+                                  const int32_t *bias, const void *res, int res_kind,
+                                  const void *lut, void *out, int store, int act, int col_major,
+                                  int M, int N, int K, int32_t zpA) {
+    if (store < HEXCUDA_HMX_STORE_I32 || store > HEXCUDA_HMX_STORE_LUT_I8)
+        return fail(HEXCUDA_ERR_ARG, "gemm_hmx: store kind %d", store);
+    if (act < HEXCUDA_HMX_ACT_NONE || act > HEXCUDA_HMX_ACT_LEAKY_SHR3)
+        return fail(HEXCUDA_ERR_ARG, "gemm_hmx: activation %d", act);
+    if (res_kind < HEXCUDA_HMX_RES_NONE || res_kind > HEXCUDA_HMX_RES_I8)
+        return fail(HEXCUDA_ERR_ARG, "gemm_hmx: residual kind %d", res_kind);
+    if (M > 0 && N > 0 && ((res_kind != HEXCUDA_HMX_RES_NONE && !res) ||
+                           ((store == HEXCUDA_HMX_STORE_LUT_I32 || store == HEXCUDA_HMX_STORE_LUT_I8) &&
+                            !lut)))
+        return fail(HEXCUDA_ERR_ARG, "gemm_hmx: null residual or table");
+    EpiParams ep{};
+    ep.out = out;
+    ep.ldo = col_major ? M : N;
+    ep.zpA = zpA;
+    ep.bias = bias;
+    ep.hmx_store = store;
+    ep.hmx_act = act;
+    ep.res_kind = res_kind;
+    ep.res = res;
+    ep.lut = lut;
+    ep.col_major = col_major ? 1 : 0;
+    return run_gemm<MmaKind::I8, kEpiHmx, false, true>(dev, A, K, B, b_transposed != 0, M, N, K,
+                                                       ep, zpA != 0, "gemm_hmx");
+}
+
 HX_EXPORT int hexcuda_gemm_hmx(int dev, const uint8_t *A, const int8_t *B, int b_transposed,
                                const int32_t *bias, void *out, int out_kind, int M, int N, int K,
                                int32_t zpA) {
     if (out_kind < HEXCUDA_HMX_OUT_I32 || out_kind > HEXCUDA_HMX_OUT_U8_BIAS_RELU)
         return fail(HEXCUDA_ERR_ARG, "gemm_hmx: out_kind %d", out_kind);
-    if (out_kind == HEXCUDA_HMX_OUT_U8_BIAS_RELU && !bias && N > 0)
-        return fail(HEXCUDA_ERR_ARG, "gemm_hmx: null bias");
-    EpiParams ep{};
-    ep.out = out;
-    ep.ldo = N;
-    ep.zpA = zpA;
-    ep.bias = out_kind == HEXCUDA_HMX_OUT_U8_BIAS_RELU ? bias : nullptr;
-    ep.hmx_mode = out_kind;
-    return run_gemm<MmaKind::I8, kEpiHmx, false, true>(dev, A, K, B, b_transposed != 0, M, N, K,
-                                                       ep, zpA != 0, "gemm_hmx");
+    if (out_kind == HEXCUDA_HMX_OUT_U8_BIAS_RELU) {
+        if (!bias && N > 0) return fail(HEXCUDA_ERR_ARG, "gemm_hmx: null bias");
+        return hexcuda_gemm_hmx_ex(dev, A, B, b_transposed, bias, nullptr, HEXCUDA_HMX_RES_NONE,
+                                   nullptr, out, HEXCUDA_HMX_STORE_U8_SAT, HEXCUDA_HMX_ACT_RELU, 0,
+                                   M, N, K, zpA);
+    }
+    return hexcuda_gemm_hmx_ex(dev, A, B, b_transposed, nullptr, nullptr, HEXCUDA_HMX_RES_NONE,
+                               nullptr, out,
+                               out_kind == HEXCUDA_HMX_OUT_I32 ? HEXCUDA_HMX_STORE_I32
+                                                               : HEXCUDA_HMX_STORE_I8_SAT,
+                               HEXCUDA_HMX_ACT_NONE, 0, M, N, K, zpA);
 }
 
 // ------------------------------------------------ no-allocation u8 x s8 GEMM

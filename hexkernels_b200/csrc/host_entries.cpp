@@ -39,8 +39,11 @@ T *stage_in(Dev *d, int slot, const T *host, size_t count) {
 // Runs `enqueue(part)` on every shard (it stages inputs, launches and sets
 // part.dout), waits for all devices, then copies each shard's output rows
 // [r0, r1) (out_row_bytes each) back into `host_out`.
+// cm_cols > 0: the output is column-major [cm_cols][rows] with cm_esize-byte
+// elements, each shard's device output column-major [cm_cols][r1 - r0].
 int run_sharded(int64_t rows, void *host_out, size_t out_row_bytes,
-                const std::function<int(Part &)> &enqueue) {
+                const std::function<int(Part &)> &enqueue, int64_t cm_cols = 0,
+                size_t cm_esize = 0) {
     if (!ensure_init()) return HEXCUDA_ERR_NODEV;
     const int n = ndev();
     std::vector<Part> parts;
@@ -70,6 +73,17 @@ int run_sharded(int64_t rows, void *host_out, size_t out_row_bytes,
         size_t bytes = (size_t)(p.r1 - p.r0) * out_row_bytes;
         if (!bytes) continue;
         cudaSetDevice(p.d->ordinal);
+        if (cm_cols > 0) {
+            const size_t w = (size_t)(p.r1 - p.r0) * cm_esize;
+            if ((rc = check(cudaMemcpy2DAsync(reinterpret_cast<uint8_t *>(host_out) +
+                                                  (size_t)p.r0 * cm_esize,
+                                              (size_t)rows * cm_esize, p.dout, w, w,
+                                              (size_t)cm_cols, cudaMemcpyDeviceToHost,
+                                              p.d->stream),
+                            "d2h (column-major)")))
+                return rc;
+            continue;
+        }
         if ((rc = check(cudaMemcpyAsync(reinterpret_cast<uint8_t *>(host_out) + p.r0 * out_row_bytes,
                                         p.dout, bytes, cudaMemcpyDeviceToHost, p.d->stream),
                         "d2h")))
@@ -387,6 +401,48 @@ HX_EXPORT int hexcuda_host_gemm_u8s8_pc(const uint8_t *A, const int8_t *B, const
         return hexcuda_gemm_u8s8_pc(p.slot, dA, dB, dbias, dout, (int)nr, N, K, zpA, dm, ds,
                                     zp_out);
     });
+}
+
+HX_EXPORT int hexcuda_host_gemm_hmx_ex(const uint8_t *A, const int8_t *B, int b_transposed,
+                                       const int32_t *bias, const void *res, int res_kind,
+                                       const void *lut, void *out, int store, int act,
+                                       int col_major, int M, int N, int K, int32_t zpA) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_hmx: bad shape");
+    if (store < HEXCUDA_HMX_STORE_I32 || store > HEXCUDA_HMX_STORE_LUT_I8 ||
+        res_kind < HEXCUDA_HMX_RES_NONE || res_kind > HEXCUDA_HMX_RES_I8)
+        return fail(HEXCUDA_ERR_ARG, "host_gemm_hmx: store %d / residual %d", store, res_kind);
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    const bool has_lut = store == HEXCUDA_HMX_STORE_LUT_I32 || store == HEXCUDA_HMX_STORE_LUT_I8;
+    if (int rc = null_check("host_gemm_hmx", {A, B, out, res_kind ? res : (const void *)A,
+                                              has_lut ? lut : (const void *)A}))
+        return rc;
+    const size_t osize = (store == HEXCUDA_HMX_STORE_I32 || store == HEXCUDA_HMX_STORE_LUT_I32) ? 4
+                         : store == HEXCUDA_HMX_STORE_U16_FIELD ? 2 : 1;
+    const size_t rsize = res_kind == HEXCUDA_HMX_RES_I32 ? 4 : 1;
+    const size_t lsize = store == HEXCUDA_HMX_STORE_LUT_I32 ? 4 : 1;
+    return run_sharded(
+        M, out, (size_t)N * osize,
+        [&](Part &p) {
+            int64_t nr = p.r1 - p.r0;
+            const uint8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+            const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+            const int32_t *dbias = bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
+            const uint8_t *dres =
+                res_kind ? stage_in(p.d, kSlotIn3,
+                                    reinterpret_cast<const uint8_t *>(res) + p.r0 * N * rsize,
+                                    (size_t)(nr * N) * rsize)
+                         : nullptr;
+            const uint8_t *dlut =
+                has_lut ? stage_in(p.d, kSlotIn4, reinterpret_cast<const uint8_t *>(lut), 256 * lsize)
+                        : nullptr;
+            void *dout = scratch(p.d, kSlotOut, (size_t)(nr * N) * osize);
+            if (!dA || !dB || (bias && !dbias) || (res_kind && !dres) || (has_lut && !dlut) || !dout)
+                return hexcuda_last_error();
+            p.dout = dout;
+            return hexcuda_gemm_hmx_ex(p.slot, dA, dB, b_transposed, dbias, dres, res_kind, dlut,
+                                       dout, store, act, col_major, (int)nr, N, K, zpA);
+        },
+        col_major ? N : 0, osize);
 }
 
 HX_EXPORT int hexcuda_host_gemm_hmx(const uint8_t *A, const int8_t *B, int b_transposed,

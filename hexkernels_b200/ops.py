@@ -109,6 +109,40 @@ def gemm_hmx(A, B, out_kind: int = HMX_OUT_I32, bias=None, zpA: int = 0,
     return out
 
 
+HMX_STORE = {"i32": (0, np.int32), "i8_sat": (1, np.int8), "u8_sat": (2, np.uint8),
+             "i8_low": (3, np.int8), "u16_field": (4, np.uint16), "lut_i32": (5, np.int32),
+             "lut_i8": (6, np.int8)}
+HMX_ACT = {"none": 0, "relu": 1, "leaky_shr3": 2}
+
+
+def gemm_hmx_ex(A, B, store: str = "i32", act: str = "none", bias=None, res=None, lut=None,
+                zpA: int = 0, b_transposed: bool = False, col_major: bool = False) -> np.ndarray:
+    """HMX-convention u8 x s8 GEMM with the family's post-ops: sx12 field,
+    + bias[j], + res[i][j] (int32 or int8 [M, N]), activation, store kind
+    (keys of HMX_STORE).  Returns [M, N], or its transpose's memory [N, M]
+    when col_major."""
+    A, B = _c(A, np.uint8), _c(B, np.int8)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    kind, dt = HMX_STORE[store]
+    out = np.empty((N, M) if col_major else (M, N), dt)
+    res_kind = 0
+    if res is not None:
+        res = np.ascontiguousarray(res)
+        res_kind = {np.dtype(np.int32): 1, np.dtype(np.int8): 2}[res.dtype]
+        assert res.shape == (M, N)
+    if bias is not None:
+        bias = _c(bias, np.int32)
+    if lut is not None:
+        lut = _c(lut, np.int32 if store == "lut_i32" else np.int8)
+        assert lut.shape == (256,)
+    pp = lambda a: _p(a) if a is not None else None
+    check(load().hexcuda_host_gemm_hmx_ex(_p(A), _p(B), int(b_transposed), pp(bias), pp(res),
+                                          res_kind, pp(lut), _p(out), kind, HMX_ACT[act],
+                                          int(col_major), M, N, K, zpA))
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp: int) -> np.ndarray:
     a, mult, shift = _c(a, np.int32), _c(mult, np.int32), _c(shift, np.int32)
     R, Cc = a.shape

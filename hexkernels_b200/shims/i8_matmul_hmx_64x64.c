@@ -1,0 +1,7 @@
+/* candidate_kernel for i8_matmul_hmx_64x64 on the B200 (libhexcuda). */
+#include <stddef.h>
+#include "hexcuda.h"
+#include "kernel_api/i8_matmul_hmx_64x64.h"
+void candidate_kernel(const uint8_t *A, const int8_t *B, uint16_t *out, int n) {
+    hexcuda_host_gemm_hmx_ex(A, B, 0, NULL, NULL, HEXCUDA_HMX_RES_NONE, NULL, out, HEXCUDA_HMX_STORE_U16_FIELD, HEXCUDA_HMX_ACT_NONE, 0, n, n, n, 0);
+}

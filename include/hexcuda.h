@@ -185,6 +185,48 @@ int hexcuda_gemm_hmx(int dev, const uint8_t *A, const int8_t *B, int b_transpose
                      const int32_t *bias, void *out, int out_kind, int M, int N, int K,
                      int32_t zpA);
 
+/* The HMX-convention GEMM with the post-ops of the rest of that family:
+ * v = sx12((acc * 17 + 8) >> 4); v += bias[j] (bias may be NULL);
+ * v += res[i][j] (res_kind INT32 or INT8, row-major [M,N]); activation;
+ * then the store.  Adds wrap in int32 as the reference's int arithmetic.
+ *   store I32           out int32 = v
+ *         I8_SAT        out int8 = clamp(v, -128, 127)
+ *         U8_SAT        out uint8 = clamp(v, 0, 255)
+ *         I8_LOW        out int8 = low 8 bits of v (i8_matmul_hmx_requant)
+ *         U16_FIELD     out uint16 = v & 0xFFF, the unsigned 12-bit field
+ *                       (hvx_hmx_requant_0x40, env/harness/harness_common.h:127;
+ *                       i8_matmul_hmx_64x64, i8_matmul_hmx_96x96)
+ *         LUT_I32       out int32 = lut[clamp(v + 128, 0, 255)] (256 int32;
+ *                       hmx_matmul_i8_gelu_lut, whose reference is undefined
+ *                       outside the table)
+ *         LUT_I8        out int8 = lut[clamp(v, -128, 127) + 128] (256 int8;
+ *                       i8_matmul_bias_gelu_hmx)
+ *   act   RELU max(v, 0); LEAKY_SHR3 v >= 0 ? v : v >> 3 (i8_matmul_leaky_relu_hmx)
+ *   col_major  out[j * M + i] (hmx_matmul_i8_col_major)
+ * Bundles (kernels/expert/<name>/kernel_api.h): hmx_matmul_i8_{32, accum_chain,
+ * bias, bias_relu, col_major, gelu_lut, multi_n, rect_32x64, relu},
+ * i8_matmul_{bias, bias_relu, leaky_relu, residual, add_requant, bias_gelu}_hmx,
+ * i8_matmul_hmx_{64x64, 96x96, requant}, i8_gemm_relu_hmx_deepk,
+ * i8_linear_proj_hmx (W = Bt, b_transposed), hmx_kacc_i8_{2tile, 4tile},
+ * hmx_tile_mac_i8_32, hmx_gemv_i8 (N = 1). */
+#define HEXCUDA_HMX_STORE_I32 0
+#define HEXCUDA_HMX_STORE_I8_SAT 1
+#define HEXCUDA_HMX_STORE_U8_SAT 2
+#define HEXCUDA_HMX_STORE_I8_LOW 3
+#define HEXCUDA_HMX_STORE_U16_FIELD 4
+#define HEXCUDA_HMX_STORE_LUT_I32 5
+#define HEXCUDA_HMX_STORE_LUT_I8 6
+#define HEXCUDA_HMX_ACT_NONE 0
+#define HEXCUDA_HMX_ACT_RELU 1
+#define HEXCUDA_HMX_ACT_LEAKY_SHR3 2
+#define HEXCUDA_HMX_RES_NONE 0
+#define HEXCUDA_HMX_RES_I32 1
+#define HEXCUDA_HMX_RES_I8 2
+int hexcuda_gemm_hmx_ex(int dev, const uint8_t *A, const int8_t *B, int b_transposed,
+                        const int32_t *bias, const void *res, int res_kind,
+                        const void *lut, void *out, int store, int act, int col_major,
+                        int M, int N, int K, int32_t zpA);
+
 /* fp16 GEMM, fp32 accumulate, one fp16 rounding: out[M,N] = A[M,K] . Bt[N,K]^T
  * (B column-major).  kernels/expert/fp16_attention_qkt_hmx/kernel_api.h:4-20. */
 int hexcuda_gemm_f16_nt(int dev, const uint16_t *A, const uint16_t *Bt,
@@ -255,6 +297,10 @@ int hexcuda_host_gemm_u8s8_pc(const uint8_t *A, const int8_t *B, const int32_t *
 int hexcuda_host_gemm_hmx(const uint8_t *A, const int8_t *B, int b_transposed,
                           const int32_t *bias, void *out, int out_kind, int M, int N,
                           int K, int32_t zpA);
+int hexcuda_host_gemm_hmx_ex(const uint8_t *A, const int8_t *B, int b_transposed,
+                             const int32_t *bias, const void *res, int res_kind,
+                             const void *lut, void *out, int store, int act,
+                             int col_major, int M, int N, int K, int32_t zpA);
 int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
                              int M, int N, int K);
 int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uint16_t *out,

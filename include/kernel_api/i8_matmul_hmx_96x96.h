@@ -1,0 +1,7 @@
+/* candidate_kernel of kernels/expert/i8_matmul_hmx_96x96/kernel_api.h:20
+ * u8 x s8 GEMM, v = sx12((acc * 17 + 8) >> 4); uint16 out = unsigned 12-bit field. */
+#ifndef HEXCUDA_KAPI_I8_MATMUL_HMX_96X96_H
+#define HEXCUDA_KAPI_I8_MATMUL_HMX_96X96_H
+#include <stdint.h>
+void candidate_kernel(const uint8_t *A, const int8_t *B, uint16_t *out, int n);
+#endif

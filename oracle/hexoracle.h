@@ -70,6 +70,36 @@ void oracle_gemm_hmx_rows(const uint8_t *A, const int8_t *B, int b_transposed,
                           const int32_t *bias, void *out, int M, int N, int K,
                           int32_t zpA, int mode, int r0, int r1);
 
+/* General form of the HMX-convention family: v = sx12((acc * 17 + 8) >> 4),
+ * then v += bias[j] (if bias), v += res[i][j] (int32 or int8 [M][N] residual),
+ * the activation, and the store:
+ *   I32 v; I8_SAT clamp(v,-128,127); U8_SAT clamp(v,0,255); I8_LOW (int8)(v & 0xFF);
+ *   U16_FIELD v & 0xFFF; LUT_I32 lut32[clamp(v+128,0,255)];
+ *   LUT_I8 lut8[(uint8)(sat_i8(v)+128)]
+ * activation RELU max(v,0), LEAKY_SHR3 v >= 0 ? v : v >> 3.  col_major stores
+ * out[j*M + i].  References (kernels/expert/<bundle>/reference.c):
+ *   hmx_matmul_i8_32, _accum_chain, _multi_n, _rect_32x64, hmx_kacc_i8_2tile,
+ *   _4tile, hmx_tile_mac_i8_32, hmx_gemv_i8 (I32); hmx_matmul_i8_bias,
+ *   i8_matmul_bias_hmx (I32 + bias); hmx_matmul_i8_bias_relu,
+ *   i8_matmul_bias_relu_hmx (+ RELU); hmx_matmul_i8_relu, i8_gemm_relu_hmx_deepk
+ *   (RELU); i8_matmul_leaky_relu_hmx (LEAKY_SHR3); hmx_matmul_i8_col_major
+ *   (col_major); hmx_matmul_i8_gelu_lut (LUT_I32); i8_matmul_hmx_64x64, _96x96
+ *   (U16_FIELD, hvx_hmx_requant_0x40 of env/harness/harness_common.h:127);
+ *   i8_matmul_hmx_requant (I8_LOW); i8_matmul_residual_hmx (RES_I32);
+ *   i8_matmul_add_requant_hmx (RES_I8, I8_SAT); i8_matmul_bias_gelu_hmx
+ *   (bias, LUT_I8); i8_linear_proj_hmx (Bt, bias, I8_SAT). */
+enum {
+    ORACLE_HMX_STORE_I32 = 0, ORACLE_HMX_STORE_I8_SAT = 1, ORACLE_HMX_STORE_U8_SAT = 2,
+    ORACLE_HMX_STORE_I8_LOW = 3, ORACLE_HMX_STORE_U16_FIELD = 4, ORACLE_HMX_STORE_LUT_I32 = 5,
+    ORACLE_HMX_STORE_LUT_I8 = 6,
+    ORACLE_HMX_ACT_NONE = 0, ORACLE_HMX_ACT_RELU = 1, ORACLE_HMX_ACT_LEAKY_SHR3 = 2,
+    ORACLE_HMX_RES_NONE = 0, ORACLE_HMX_RES_I32 = 1, ORACLE_HMX_RES_I8 = 2,
+};
+void oracle_gemm_hmx_ex_rows(const uint8_t *A, const int8_t *B, int b_transposed,
+                             void *out, int M, int N, int K, int32_t zpA, int store,
+                             int act, const int32_t *bias, int res_kind, const void *res,
+                             const void *lut, int col_major, int r0, int r1);
+
 /* kernels/expert/requant_per_channel/reference.c:2-17 (rows = channels) */
 void oracle_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
                                 const int32_t *mult, const int *shift, int8_t zp);

@@ -109,6 +109,31 @@ def gemm_hmx(A, B, out_kind=0, bias=None, zpA=0, b_transposed=False):
     return out
 
 
+def gemm_hmx_ex(A, B, store="i32", act="none", bias=None, res=None, lut=None, zpA=0,
+                b_transposed=False, col_major=False):
+    stores = {"i32": (0, np.int32), "i8_sat": (1, np.int8), "u8_sat": (2, np.uint8),
+              "i8_low": (3, np.int8), "u16_field": (4, np.uint16), "lut_i32": (5, np.int32),
+              "lut_i8": (6, np.int8)}
+    A, B = np.ascontiguousarray(A, np.uint8), np.ascontiguousarray(B, np.int8)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    kind, dt = stores[store]
+    out = np.zeros((N, M) if col_major else (M, N), dt)
+    res_kind = 0
+    if res is not None:
+        res = np.ascontiguousarray(res)
+        res_kind = 1 if res.dtype == np.int32 else 2
+    if bias is not None:
+        bias = np.ascontiguousarray(bias, np.int32)
+    if lut is not None:
+        lut = np.ascontiguousarray(lut, np.int32 if store == "lut_i32" else np.int8)
+    pp = lambda a: _p(a) if a is not None else None
+    lib().oracle_gemm_hmx_ex_rows(_p(A), _p(B), int(b_transposed), _p(out), M, N, K,
+                                  C.c_int32(zpA), kind, {"none": 0, "relu": 1, "leaky_shr3": 2}[act],
+                                  pp(bias), res_kind, pp(res), pp(lut), int(col_major), 0, M)
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp):
     a = np.ascontiguousarray(a, np.int32)
     R, Cc = a.shape

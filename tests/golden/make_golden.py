@@ -330,6 +330,51 @@ def gen_hmx(ref):
     save("hmx_gemm", **arrays)
 
 
+def gen_hmx_family(ref):
+    # The 24 HMX-convention bundles of tests/hmx_family.py, each run through
+    # its own reference.c on seeded inputs: full-range u8 / s8 operands at
+    # sizes that are not multiples of the GEMM tile (products stay inside
+    # int32, so the references are well defined), small operands where a
+    # 256-entry table is indexed by the result.
+    sys.path.insert(0, str(HERE.parent))
+    from hmx_family import BUNDLES, OUT_DTYPE, shape_of
+    rng = np.random.default_rng(23)
+    arrays = {}
+    for b, (params, kw) in BUNDLES.items():
+        M, N, K = shape_of(b)
+        small = "lut" in kw["store"]
+        a = {
+            "A": (rng.integers(0, 4, M * K) if small else rng.integers(0, 256, M * K)).astype(np.uint8),
+            "bias": rng.integers(-200 if small else -3000, 201 if small else 3001, N).astype(np.int32),
+            "res32": rng.integers(-10**6, 10**6, M * N).astype(np.int32),
+            "res8": rng.integers(-128, 128, M * N).astype(np.int8),
+            "lut32": rng.integers(-10**5, 10**5, 256).astype(np.int32),
+            "lut8": rng.integers(-128, 128, 256).astype(np.int8),
+        }
+        bvals = rng.integers(-1, 2, K * N) if small else rng.integers(-128, 128, K * N)
+        a["B"] = a["Bt"] = a["x"] = bvals.astype(np.int8)
+        out = np.zeros(M * N, OUT_DTYPE[kw["store"]])
+        args = []
+        for prm in params:
+            if prm == "out":
+                args.append(ptr(out))
+            elif prm in ("n", "M"):
+                args.append(M)
+            elif prm == "N":
+                args.append(N)
+            elif prm == "K":
+                args.append(K)
+            else:
+                args.append(ptr(a[prm]))
+        getattr(ref, "ref_" + b)(*args)
+        for prm in params:
+            if prm in a:
+                arrays[f"{b}__{prm}"] = a[prm]
+        arrays[f"{b}__out"] = out
+        arrays[f"{b}__mnk"] = np.array([M, N, K], np.int32)
+    save("hmx_family", **arrays)
+
+
 # ----------------------------------------------------------------- fp16
 
 def gen_hf_q(g, mod, off, step):
@@ -503,6 +548,7 @@ def main():
     gen_requantize_i32_u8(ref)
     gen_gemm_u8s8_pc(ref)
     gen_hmx(ref)
+    gen_hmx_family(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

@@ -113,3 +113,29 @@ def test_shim_hmx_bundles(hx, oracle):
     Bd = rng.integers(-128, 128, (K, n), dtype=np.int8)
     shim("hmx_matmul_i8_deepk")(p(Ad), p(Bd), p(o32), n, K)
     np.testing.assert_array_equal(o32, oracle.gemm_hmx(Ad, Bd, 0))
+
+
+@pytest.mark.parametrize("bundle", sorted(__import__("hmx_family").BUNDLES))
+def test_shim_hmx_family(hx, bundle):
+    """Each HMX-family shim through candidate_kernel on its golden case."""
+    from conftest import golden
+    from hmx_family import BUNDLES
+    g = golden("hmx_family")
+    params, kw = BUNDLES[bundle]
+    arr = {k.split("__", 1)[1]: g[k] for k in g if k.startswith(bundle + "__")}
+    M, N, K = (int(v) for v in arr["mnk"])
+    out = np.zeros_like(arr["out"])
+    args = []
+    for prm in params:
+        if prm == "out":
+            args.append(p(out))
+        elif prm in ("n", "M"):
+            args.append(M)
+        elif prm == "N":
+            args.append(N)
+        elif prm == "K":
+            args.append(K)
+        else:
+            args.append(p(np.ascontiguousarray(arr[prm])))
+    shim(bundle)(*args)
+    np.testing.assert_array_equal(out, arr["out"])

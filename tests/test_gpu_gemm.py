@@ -170,6 +170,45 @@ def test_hmx_gemm_deep_k_wraps(hx, oracle):
             hx.gemm_hmx(A, np.ascontiguousarray(B.T), 0, None, zpa, True), exp)
 
 
+from hmx_family import BUNDLES as HMX_FAMILY, golden_case  # noqa: E402
+
+
+@pytest.mark.parametrize("bundle", sorted(HMX_FAMILY))
+def test_hmx_family_golden(hx, bundle):
+    A, B, out, kw = golden_case(golden("hmx_family"), bundle)
+    np.testing.assert_array_equal(hx.gemm_hmx_ex(A, B, **kw), out)
+
+
+HMX_EX_SHAPES = [(1, 1, 1), (129, 257, 130), (300, 520, 1000), (513, 129, 96), (256, 384, 4096)]
+
+
+@pytest.mark.parametrize("M,N,K", HMX_EX_SHAPES)
+def test_hmx_ex_random(hx, oracle, M, N, K):
+    """Every store kind and activation, with bias, int32 / int8 residuals,
+    column-major output, Bt operand and a zero point, against the oracle."""
+    rng = np.random.default_rng(M + 3 * N + 7 * K)
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    Bt = np.ascontiguousarray(B.T)
+    bias = rng.integers(-3000, 3000, N).astype(np.int32)
+    r32 = rng.integers(-10**6, 10**6, (M, N)).astype(np.int32)
+    r8 = rng.integers(-128, 128, (M, N)).astype(np.int8)
+    l32 = rng.integers(-10**5, 10**5, 256).astype(np.int32)
+    l8 = rng.integers(-128, 128, 256).astype(np.int8)
+    cases = [dict(store="i32", act="leaky_shr3", bias=bias, res=r32),
+             dict(store="i8_sat", res=r8, zpA=128),
+             dict(store="u8_sat", act="relu", bias=bias),
+             dict(store="i8_low", zpA=-3),
+             dict(store="u16_field", col_major=True),
+             dict(store="lut_i32", lut=l32, bias=bias),
+             dict(store="lut_i8", lut=l8, bias=bias, res=r8),
+             dict(store="i32", act="relu", col_major=True, res=r32, zpA=7)]
+    for kw in cases:
+        exp = oracle.gemm_hmx_ex(A, B, **kw)
+        np.testing.assert_array_equal(hx.gemm_hmx_ex(A, B, **kw), exp, err_msg=str(kw.keys()))
+        np.testing.assert_array_equal(hx.gemm_hmx_ex(A, Bt, b_transposed=True, **kw), exp)
+
+
 # --------------------------------------------------------------- fp16 GEMMs
 
 def assert_f16_gemm_close(got, exp):

@@ -203,3 +203,14 @@ def test_fp32_restatements_match_fp16_reference_formula(oracle):
     out = oracle.layernorm(g["x"].astype(np.float32).reshape(1, -1), g["gamma"].astype(np.float32),
                            g["beta"].astype(np.float32), 1e-3).astype(np.float16)
     np.testing.assert_array_equal(out.ravel().view(np.uint16), g["out"].view(np.uint16))
+
+
+from hmx_family import BUNDLES as HMX_FAMILY, golden_case  # noqa: E402
+
+
+@pytest.mark.parametrize("bundle", sorted(HMX_FAMILY))
+def test_hmx_family_golden(oracle, bundle):
+    """The generalised HMX epilogue (bias, residual, activation, store kind,
+    column-major) against each bundle's own reference.c."""
+    A, B, out, kw = golden_case(golden("hmx_family"), bundle)
+    np.testing.assert_array_equal(oracle.gemm_hmx_ex(A, B, **kw), out)

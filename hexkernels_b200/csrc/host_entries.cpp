@@ -403,6 +403,61 @@ HX_EXPORT int hexcuda_host_gemm_u8s8_pc(const uint8_t *A, const int8_t *B, const
     });
 }
 
+HX_EXPORT int hexcuda_host_requant_ew(const void *a, int a_i8, const void *b, int b_kind,
+                                      void *out, int64_t n, int pre, int64_t pre_c, int32_t mult,
+                                      int shift, int zp, int sign_of_a, int lo1, int hi1, int lo2,
+                                      int hi2, const int8_t *lut) {
+    if (n < 0 || b_kind < 0 || b_kind > 2) return fail(HEXCUDA_ERR_ARG, "host_requant_ew: bad size");
+    if (n == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_requant_ew", {a, out, b_kind ? b : a})) return rc;
+    const size_t ea = a_i8 ? 1 : 4, eb = b_kind == 2 ? 1 : 4;
+    return run_sharded(n, out, 1, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const uint8_t *da = stage_in(p.d, kSlotIn0, reinterpret_cast<const uint8_t *>(a) + p.r0 * ea,
+                                     (size_t)nr * ea);
+        const uint8_t *db = b_kind ? stage_in(p.d, kSlotIn1,
+                                              reinterpret_cast<const uint8_t *>(b) + p.r0 * eb,
+                                              (size_t)nr * eb)
+                                   : nullptr;
+        const int8_t *dl = lut ? stage_in(p.d, kSlotIn2, lut, 256) : nullptr;
+        void *dout = scratch(p.d, kSlotOut, (size_t)nr);
+        if (!da || (b_kind && !db) || (lut && !dl) || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_requant_ew(p.slot, da, a_i8, db, b_kind, dout, nr, pre, pre_c, mult, shift,
+                                  zp, sign_of_a, lo1, hi1, lo2, hi2, dl);
+    });
+}
+
+HX_EXPORT int hexcuda_host_epilogue_bias_i32(const int32_t *acc, const int32_t *bias,
+                                             int32_t *out, int R, int C) {
+    if (R < 0 || C < 0) return fail(HEXCUDA_ERR_ARG, "host_epilogue_bias_i32: bad shape");
+    if (R == 0 || C == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_epilogue_bias_i32", {acc, bias, out})) return rc;
+    return run_sharded(R, out, (size_t)C * 4, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int32_t *dacc = stage_in(p.d, kSlotIn0, acc + p.r0 * C, (size_t)(nr * C));
+        const int32_t *dbias = stage_in(p.d, kSlotIn1, bias, (size_t)C);
+        int32_t *dout = reinterpret_cast<int32_t *>(scratch(p.d, kSlotOut, (size_t)(nr * C) * 4));
+        if (!dacc || !dbias || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_epilogue_bias_i32(p.slot, dacc, dbias, dout, (int)nr, C);
+    });
+}
+
+HX_EXPORT int hexcuda_host_relu_i8(const int8_t *x, int8_t *out, int64_t n) {
+    if (n < 0) return fail(HEXCUDA_ERR_ARG, "host_relu_i8: n=%lld", (long long)n);
+    if (n == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_relu_i8", {x, out})) return rc;
+    return run_sharded(n, out, 1, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *dx = stage_in(p.d, kSlotIn0, x + p.r0, (size_t)nr);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)nr));
+        if (!dx || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_relu_i8(p.slot, dx, dout, nr);
+    });
+}
+
 HX_EXPORT int hexcuda_host_gemm_hmx_ex(const uint8_t *A, const int8_t *B, int b_transposed,
                                        const int32_t *bias, const void *res, int res_kind,
                                        const void *lut, void *out, int store, int act,

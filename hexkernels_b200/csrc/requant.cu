@@ -59,6 +59,154 @@ __global__ void __launch_bounds__(256) requant_per_channel_kernel(
     }
 }
 
+// ---------------------------------------------------------------------------
+// Elementwise requant family: x = pre(a, b); r = requant(x) + zp; two clamps;
+// out = lut ? lut[(uint8) r] : (uint8) r.  (The corpus bundles it covers are
+// listed with hexcuda_requant_ew in hexcuda.h.)
+struct RqEw {
+    int pre;            // HEXCUDA_RQ_PRE_*
+    int64_t c;          // MUL_ADD constant
+    int32_t mult;
+    int shift;          // 0..63
+    int zp;
+    int sign_of_a;      // sign(x) * ((|x| * mult + half) >> shift)
+    int lo1, hi1, lo2, hi2;
+    const int8_t *lut;  // 256 entries or null
+};
+
+__device__ __forceinline__ uint32_t rq_ew_one(int64_t a, int64_t b, const RqEw &p) {
+    int64_t x = a;
+    if (p.pre == HEXCUDA_RQ_PRE_ADD) {
+        x = a + b;
+    } else if (p.pre == HEXCUDA_RQ_PRE_ADD_RELU) {
+        x = a + b;
+        x = x > 0 ? x : 0;
+    } else if (p.pre == HEXCUDA_RQ_PRE_MUL_ADD) {
+        x = (int64_t)((uint64_t)a * (uint64_t)b + (uint64_t)p.c);
+    }
+    int64_t r;
+    if (p.sign_of_a) {
+        const int64_t half = p.shift > 0 ? ((int64_t)1 << (p.shift - 1)) : 0;
+        const int64_t am = (int64_t)((uint64_t)(x < 0 ? -x : x) * (uint64_t)(int64_t)p.mult);
+        const int64_t sh = (am + half) >> p.shift;
+        r = x < 0 ? -sh : sh;
+    } else {
+        r = rq_round((int64_t)((uint64_t)x * (uint64_t)(int64_t)p.mult), p.shift);
+    }
+    r += p.zp;
+    r = r > p.hi1 ? p.hi1 : r;
+    r = r < p.lo1 ? p.lo1 : r;
+    r = r > p.hi2 ? p.hi2 : r;
+    r = r < p.lo2 ? p.lo2 : r;
+    if (p.lut) return (uint32_t)(uint8_t)__ldg(p.lut + (uint8_t)r);
+    return (uint32_t)(uint8_t)r;
+}
+
+// 16 consecutive elements of one operand as int64 (int8 or int32 source)
+template <bool I8>
+__device__ __forceinline__ void load16(const void *src, int64_t v, int64_t (&x)[16]) {
+    if constexpr (I8) {
+        const uint4 q = __ldcs(reinterpret_cast<const uint4 *>(src) + v);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 16; i++) x[i] = (int8_t)(w[i >> 2] >> (8 * (i & 3)));
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int4 q = __ldcs(reinterpret_cast<const int4 *>(src) + v * 4 + k);
+            x[4 * k] = q.x, x[4 * k + 1] = q.y, x[4 * k + 2] = q.z, x[4 * k + 3] = q.w;
+        }
+    }
+}
+
+template <bool I8>
+__device__ __forceinline__ int64_t load1(const void *src, int64_t i) {
+    if constexpr (I8)
+        return reinterpret_cast<const int8_t *>(src)[i];
+    else
+        return reinterpret_cast<const int32_t *>(src)[i];
+}
+
+// Each thread turns 16 elements (one or two operands) into 16 output bytes
+// (one 128-bit store) per step; a scalar loop takes the tail and unaligned
+// buffers.  B_KIND: 0 none, 1 int32, 2 int8.
+template <bool A_I8, int B_KIND>
+__global__ void __launch_bounds__(256) requant_ew_kernel(const void *__restrict__ a,
+                                                          const void *__restrict__ b,
+                                                          uint8_t *__restrict__ out, int64_t n,
+                                                          const RqEw p, int vec) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t done = 0;
+    if (vec) {
+        const int64_t nv = n / 16;
+        for (int64_t v = t; v < nv; v += stride) {
+            int64_t xa[16], xb[16];
+            load16<A_I8>(a, v, xa);
+            if constexpr (B_KIND != 0) load16<B_KIND == 2>(b, v, xb);
+            uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                w[i >> 2] |= rq_ew_one(xa[i], B_KIND != 0 ? xb[i] : 0, p) << (8 * (i & 3));
+            __stcs(reinterpret_cast<uint4 *>(out) + v, make_uint4(w[0], w[1], w[2], w[3]));
+        }
+        done = nv * 16;
+    }
+    for (int64_t i = done + t; i < n; i += stride) {
+        const int64_t bi = B_KIND == 0 ? 0 : load1<B_KIND == 2>(b, i);
+        out[i] = (uint8_t)rq_ew_one(load1<A_I8>(a, i), bi, p);
+    }
+}
+
+// out[r][c] = acc[r][c] + bias[c] (int32, wrap): 4 columns per thread step
+__global__ void __launch_bounds__(256) epilogue_bias_i32_kernel(const int32_t *__restrict__ acc,
+                                                                 const int32_t *__restrict__ bias,
+                                                                 int32_t *__restrict__ out, int R,
+                                                                 int C, int vec) {
+    const int64_t total = (int64_t)R * C;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (vec) {  // C % 4 == 0 and 16-byte aligned buffers
+        for (int64_t v = t; v < total / 4; v += stride) {
+            const int c = (int)((v * 4) % C);
+            const int4 x = __ldcs(reinterpret_cast<const int4 *>(acc) + v);
+            const int4 bb = __ldg(reinterpret_cast<const int4 *>(bias + c));
+            __stcs(reinterpret_cast<int4 *>(out) + v,
+                   make_int4((int)((uint32_t)x.x + (uint32_t)bb.x), (int)((uint32_t)x.y + (uint32_t)bb.y),
+                             (int)((uint32_t)x.z + (uint32_t)bb.z), (int)((uint32_t)x.w + (uint32_t)bb.w)));
+        }
+    } else {
+        for (int64_t i = t; i < total; i += stride)
+            out[i] = (int32_t)((uint32_t)acc[i] + (uint32_t)bias[i % C]);
+    }
+}
+
+// out = max(x, 0) on int8, 16 per thread step
+__global__ void __launch_bounds__(256) relu_i8_kernel(const int8_t *__restrict__ x,
+                                                       int8_t *__restrict__ out, int64_t n, int vec) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t done = 0;
+    if (vec) {
+        for (int64_t v = t; v < n / 16; v += stride) {
+            const uint4 q = __ldcs(reinterpret_cast<const uint4 *>(x) + v);
+            uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) w[k] = __vmaxs4(w[k], 0u);
+            __stcs(reinterpret_cast<uint4 *>(out) + v, make_uint4(w[0], w[1], w[2], w[3]));
+        }
+        done = n / 16 * 16;
+    }
+    for (int64_t i = done + t; i < n; i += stride) out[i] = x[i] > 0 ? x[i] : 0;
+}
+
+int ew_blocks(const Dev *d, int64_t work) {
+    int64_t blocks = (work + 255) / 256;
+    const int64_t cap = (int64_t)d->sms * 8;
+    if (blocks > cap) blocks = cap;
+    return blocks < 1 ? 1 : (int)blocks;
+}
+
 }  // namespace
 }  // namespace hx
 
@@ -100,4 +248,68 @@ HX_EXPORT int hexcuda_requant_per_channel(int dev, const int32_t *a, int8_t *out
     requant_per_channel_kernel<<<dim3(gx, gy), 256, 0, d->stream>>>(a, out, R, C, mult, shift,
                                                                      (int)zp);
     return launch_end(d, "requant_per_channel");
+}
+
+HX_EXPORT int hexcuda_requant_ew(int dev, const void *a, int a_i8, const void *b, int b_kind,
+                                 void *out, int64_t n, int pre, int64_t pre_c, int32_t mult,
+                                 int shift, int zp, int sign_of_a, int lo1, int hi1, int lo2,
+                                 int hi2, const int8_t *lut) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (n < 0 || shift < 0 || shift > 63 || b_kind < 0 || b_kind > 2 ||
+        pre < HEXCUDA_RQ_PRE_A || pre > HEXCUDA_RQ_PRE_MUL_ADD || (pre != HEXCUDA_RQ_PRE_A && !b_kind))
+        return fail(HEXCUDA_ERR_ARG, "requant_ew: n=%lld shift=%d b_kind=%d pre=%d", (long long)n,
+                    shift, b_kind, pre);
+    if (n == 0) return HEXCUDA_OK;
+    if (!a || !out || (b_kind && !b)) return fail(HEXCUDA_ERR_ARG, "requant_ew: null pointer");
+    RqEw p{pre, pre_c, mult, shift, zp, sign_of_a ? 1 : 0, lo1, hi1, lo2, hi2, lut};
+    auto al = [](const void *q) { return q == nullptr || ((uintptr_t)q & 15u) == 0; };
+    const int vec = al(a) && al(b) && al(out);
+    const int blocks = ew_blocks(d, vec ? (n + 15) / 16 : n);
+    uint8_t *o = reinterpret_cast<uint8_t *>(out);
+    launch_begin(d);
+    if (a_i8) {
+        if (b_kind == 2)
+            requant_ew_kernel<true, 2><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+        else if (b_kind == 1)
+            requant_ew_kernel<true, 1><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+        else
+            requant_ew_kernel<true, 0><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+    } else {
+        if (b_kind == 2)
+            requant_ew_kernel<false, 2><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+        else if (b_kind == 1)
+            requant_ew_kernel<false, 1><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+        else
+            requant_ew_kernel<false, 0><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+    }
+    return launch_end(d, "requant_ew");
+}
+
+HX_EXPORT int hexcuda_epilogue_bias_i32(int dev, const int32_t *acc, const int32_t *bias,
+                                        int32_t *out, int R, int C) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (R < 0 || C < 0) return fail(HEXCUDA_ERR_ARG, "epilogue_bias_i32: R=%d C=%d", R, C);
+    if (R == 0 || C == 0) return HEXCUDA_OK;
+    if (!acc || !bias || !out) return fail(HEXCUDA_ERR_ARG, "epilogue_bias_i32: null pointer");
+    auto al = [](const void *q) { return ((uintptr_t)q & 15u) == 0; };
+    const int vec = (C % 4 == 0) && al(acc) && al(bias) && al(out);
+    const int64_t total = (int64_t)R * C;
+    launch_begin(d);
+    epilogue_bias_i32_kernel<<<ew_blocks(d, vec ? total / 4 : total), 256, 0, d->stream>>>(
+        acc, bias, out, R, C, vec);
+    return launch_end(d, "epilogue_bias_i32");
+}
+
+HX_EXPORT int hexcuda_relu_i8(int dev, const int8_t *x, int8_t *out, int64_t n) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (n < 0) return fail(HEXCUDA_ERR_ARG, "relu_i8: n=%lld", (long long)n);
+    if (n == 0) return HEXCUDA_OK;
+    if (!x || !out) return fail(HEXCUDA_ERR_ARG, "relu_i8: null pointer");
+    const int vec = (((uintptr_t)x | (uintptr_t)out) & 15u) == 0;
+    launch_begin(d);
+    relu_i8_kernel<<<ew_blocks(d, vec ? (n + 15) / 16 : n), 256, 0, d->stream>>>(x, out, n, vec);
+    return launch_end(d, "relu_i8");
 }

@@ -143,6 +143,47 @@ def gemm_hmx_ex(A, B, store: str = "i32", act: str = "none", bias=None, res=None
     return out
 
 
+RQ_PRE = {"a": 0, "add": 1, "add_relu": 2, "mul_add": 3}
+
+
+def requant_ew(a, b=None, pre: str = "a", pre_c: int = 0, mult: int = 1, shift: int = 0,
+               zp: int = 0, sign_of_a: bool = False, lo1: int = -128, hi1: int = 127,
+               lo2: int = -128, hi2: int = 127, lut=None, out_dtype=np.int8) -> np.ndarray:
+    """Elementwise requant family: pre-op of a (and b), round-half-away
+    requant, two clamps, optional 256-entry int8 table; one byte out."""
+    a = np.ascontiguousarray(a)
+    assert a.dtype in (np.int32, np.int8)
+    b_kind = 0
+    if b is not None:
+        b = np.ascontiguousarray(b)
+        assert b.shape == a.shape
+        b_kind = {np.dtype(np.int32): 1, np.dtype(np.int8): 2}[b.dtype]
+    if lut is not None:
+        lut = _c(lut, np.int8)
+        assert lut.shape == (256,)
+    out = np.empty(a.shape, out_dtype)
+    check(load().hexcuda_host_requant_ew(_p(a), int(a.dtype == np.int8),
+                                         _p(b) if b is not None else None, b_kind, _p(out), a.size,
+                                         RQ_PRE[pre], pre_c, mult, shift, zp, int(sign_of_a), lo1,
+                                         hi1, lo2, hi2, _p(lut) if lut is not None else None))
+    return out
+
+
+def epilogue_bias_i32(acc, bias) -> np.ndarray:
+    acc, bias = _c(acc, np.int32), _c(bias, np.int32)
+    R, Cc = acc.shape
+    out = np.empty_like(acc)
+    check(load().hexcuda_host_epilogue_bias_i32(_p(acc), _p(bias), _p(out), R, Cc))
+    return out
+
+
+def relu_i8(x) -> np.ndarray:
+    x = _c(x, np.int8)
+    out = np.empty_like(x)
+    check(load().hexcuda_host_relu_i8(_p(x), _p(out), x.size))
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp: int) -> np.ndarray:
     a, mult, shift = _c(a, np.int32), _c(mult, np.int32), _c(shift, np.int32)
     R, Cc = a.shape

@@ -1,0 +1,7 @@
+/* candidate_kernel for i8_skip_add_relu_requant on the B200 (libhexcuda). */
+#include <stddef.h>
+#include "hexcuda.h"
+#include "kernel_api/i8_skip_add_relu_requant.h"
+void candidate_kernel(const int8_t *a, const int8_t *b, int8_t *out, int n, int32_t mult, int shift, int8_t zp) {
+    hexcuda_host_requant_ew(a, 1, b, 2, out, n, HEXCUDA_RQ_PRE_ADD_RELU, 0, mult, shift, zp, 0, -128, 127, -128, 127, NULL);
+}

@@ -120,6 +120,37 @@ int hexcuda_requant_per_channel(int dev, const int32_t *a, int8_t *out, int R,
 int hexcuda_requantize_i32_u8(int dev, const int32_t *a, uint8_t *out, int64_t n,
                               int32_t mult, int shift, uint8_t zp);
 
+/* Elementwise requant family, n elements:
+ *   x = a (pre A) | a + b (ADD) | max(a + b, 0) (ADD_RELU) | a * b + pre_c (MUL_ADD)
+ *   r = round_half_away((int64) x * mult >> shift) + zp       (shift 0..63)
+ *       with sign_of_a: sign(x) * ((|x| * mult + half) >> shift)
+ *   r = max(min(r, hi1), lo1); r = max(min(r, hi2), lo2)
+ *   out byte = lut ? lut[(uint8) r] : (uint8) r
+ * a int32 (or int8 with a_i8), b none / int32 / int8 (b_kind 0 / 1 / 2).
+ * Products that leave int64 wrap (undefined in the C references).
+ * Bundles (kernels/expert/<name>/kernel_api.h): requantize_i32_i8_dma,
+ * epilogue_requant_i32_i8, requant_relu_dma (13, 3, clamp [0,127]),
+ * requant_relu6_dma (clamp [0,24]), i8_clip_requant_dma (second clamp
+ * [lo,hi]), dma_stream_requant_i32_i8 (sign_of_a), requant_sigmoid_lut and
+ * requant_tanh_lut (clamp [0,255], table), bias_add_requant,
+ * residual_add_requant, requant_add_dma (5, 3), add_relu_requant,
+ * i8_skip_add_relu_requant, mul_add_requant_dma (pre_c 50, 3, 1),
+ * i8_mul_requant_dma. */
+#define HEXCUDA_RQ_PRE_A 0
+#define HEXCUDA_RQ_PRE_ADD 1
+#define HEXCUDA_RQ_PRE_ADD_RELU 2
+#define HEXCUDA_RQ_PRE_MUL_ADD 3
+int hexcuda_requant_ew(int dev, const void *a, int a_i8, const void *b, int b_kind,
+                       void *out, int64_t n, int pre, int64_t pre_c, int32_t mult,
+                       int shift, int zp, int sign_of_a, int lo1, int hi1, int lo2,
+                       int hi2, const int8_t *lut);
+/* out[r][c] = acc[r][c] + bias[c], int32 (wrap).
+ * kernels/expert/epilogue_bias_i32/kernel_api.h:14. */
+int hexcuda_epilogue_bias_i32(int dev, const int32_t *acc, const int32_t *bias,
+                              int32_t *out, int R, int C);
+/* out = max(x, 0), int8.  kernels/expert/epilogue_relu_i8/kernel_api.h:13. */
+int hexcuda_relu_i8(int dev, const int8_t *x, int8_t *out, int64_t n);
+
 /* int8 GEMM + requant: A [M,K] s8, B [K,N] s8 row-major, out [M,N] s8.
  * kernels/expert/i8_gemm_requant/kernel_api.h:4-11. */
 int hexcuda_gemm_i8_requant(int dev, const int8_t *A, const int8_t *B, int8_t *out,
@@ -281,6 +312,13 @@ int hexcuda_host_requant_per_channel(const int32_t *a, int8_t *out, int R, int C
                                      const int32_t *mult, const int *shift, int8_t zp);
 int hexcuda_host_requantize_i32_u8(const int32_t *a, uint8_t *out, int64_t n,
                                    int32_t mult, int shift, uint8_t zp);
+int hexcuda_host_requant_ew(const void *a, int a_i8, const void *b, int b_kind, void *out,
+                            int64_t n, int pre, int64_t pre_c, int32_t mult, int shift,
+                            int zp, int sign_of_a, int lo1, int hi1, int lo2, int hi2,
+                            const int8_t *lut);
+int hexcuda_host_epilogue_bias_i32(const int32_t *acc, const int32_t *bias, int32_t *out,
+                                   int R, int C);
+int hexcuda_host_relu_i8(const int8_t *x, int8_t *out, int64_t n);
 int hexcuda_host_gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out,
                                  int M, int N, int K, int32_t mult, int shift,
                                  int8_t zp);

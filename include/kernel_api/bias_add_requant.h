@@ -1,0 +1,7 @@
+/* candidate_kernel of kernels/expert/bias_add_requant/kernel_api.h:9
+ * elementwise requant: pre add, round half away, clamp, int8 out. */
+#ifndef HEXCUDA_KAPI_BIAS_ADD_REQUANT_H
+#define HEXCUDA_KAPI_BIAS_ADD_REQUANT_H
+#include <stdint.h>
+void candidate_kernel(const int32_t *a, const int32_t *bias, int8_t *out, int n, int32_t mult, int shift, int8_t zp);
+#endif

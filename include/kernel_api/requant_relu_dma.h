@@ -1,0 +1,7 @@
+/* candidate_kernel of kernels/expert/requant_relu_dma/kernel_api.h:15
+ * elementwise requant: pre a, round half away, clamp, int8 out. */
+#ifndef HEXCUDA_KAPI_REQUANT_RELU_DMA_H
+#define HEXCUDA_KAPI_REQUANT_RELU_DMA_H
+#include <stdint.h>
+void candidate_kernel(const int32_t *a, int8_t *out, int n);
+#endif

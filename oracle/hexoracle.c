@@ -236,6 +236,52 @@ void oracle_gemm_hmx_rows(const uint8_t *A, const int8_t *B, int b_transposed,
                                 ORACLE_HMX_ACT_RELU, bias, 0, 0, 0, 0, r0, r1);
 }
 
+/* The elementwise requant family (cited in hexoracle.h).  Products that
+ * leave int64 are undefined in the references; here they wrap. */
+void oracle_requant_ew(const void *a, int a_i8, const void *b, int b_kind, int64_t n, int pre,
+                       int64_t pre_c, int32_t mult, int shift, int zp, int sign_of_a,
+                       int lo1, int hi1, int lo2, int hi2, const int8_t *lut, void *out) {
+    const int64_t half = shift > 0 ? ((int64_t)1 << (shift - 1)) : 0;
+    for (int64_t i = 0; i < n; i++) {
+        const int64_t ai = a_i8 ? (int64_t)((const int8_t *)a)[i] : (int64_t)((const int32_t *)a)[i];
+        int64_t bi = 0;
+        if (b_kind == 1) bi = ((const int32_t *)b)[i];
+        if (b_kind == 2) bi = ((const int8_t *)b)[i];
+        int64_t x = ai;
+        if (pre == ORACLE_RQ_PRE_ADD) x = ai + bi;
+        if (pre == ORACLE_RQ_PRE_ADD_RELU) x = ai + bi > 0 ? ai + bi : 0;
+        if (pre == ORACLE_RQ_PRE_MUL_ADD) x = (int64_t)((uint64_t)ai * (uint64_t)bi + (uint64_t)pre_c);
+        int64_t r;
+        if (sign_of_a) {
+            const int64_t am = (int64_t)((uint64_t)(x < 0 ? -x : x) * (uint64_t)(int64_t)mult);
+            const int64_t sh = (am + half) >> shift;
+            r = x < 0 ? -sh : sh;
+        } else {
+            const int64_t v = (int64_t)((uint64_t)x * (uint64_t)(int64_t)mult);
+            r = rq_round(v, shift);
+        }
+        r += zp;
+        if (r > hi1) r = hi1;
+        if (r < lo1) r = lo1;
+        if (r > hi2) r = hi2;
+        if (r < lo2) r = lo2;
+        if (lut)
+            ((int8_t *)out)[i] = lut[(uint8_t)r];
+        else
+            ((uint8_t *)out)[i] = (uint8_t)r;
+    }
+}
+
+void oracle_epilogue_bias_i32(const int32_t *acc, const int32_t *bias, int32_t *out, int R, int C) {
+    for (int r = 0; r < R; r++)
+        for (int c = 0; c < C; c++)
+            out[(size_t)r * C + c] = wrap_add(acc[(size_t)r * C + c], bias[c]);
+}
+
+void oracle_relu_i8(const int8_t *x, int8_t *out, int64_t n) {
+    for (int64_t i = 0; i < n; i++) out[i] = x[i] > 0 ? x[i] : 0;
+}
+
 /* kernels/expert/requant_per_channel/reference.c:4-16 */
 void oracle_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
                                 const int32_t *mult, const int *shift, int8_t zp) {

@@ -108,6 +108,30 @@ void oracle_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
 void oracle_requantize_i32_u8(const int32_t *a, uint8_t *out, int64_t n,
                               int32_t mult, int shift, uint8_t zp);
 
+/* Elementwise requant family (one restatement, parameters per bundle):
+ *   x = a                       (pre A)           requantize_i32_i8_dma, epilogue_requant_i32_i8,
+ *                                                 requant_relu_dma, requant_relu6_dma,
+ *                                                 i8_clip_requant_dma, requant_sigmoid_lut,
+ *                                                 requant_tanh_lut, dma_stream_requant_i32_i8
+ *   x = a + b                   (pre ADD)         bias_add_requant, residual_add_requant, requant_add_dma
+ *   x = max(a + b, 0)           (pre ADD_RELU)    add_relu_requant, i8_skip_add_relu_requant
+ *   x = a * b + c               (pre MUL_ADD)     mul_add_requant_dma (c = 50), i8_mul_requant_dma (c = 0)
+ *   r = round_half_away(x * mult, shift) + zp   (int64; sign_of_a: sign(a) *
+ *       ((|a| * mult + half) >> shift), dma_stream_requant_i32_i8/reference.c)
+ *   r = max(min(r, hi1), lo1); r = max(min(r, hi2), lo2)
+ *   out = lut ? lut[(uint8)r] : (uint8)r
+ * a and b are int32, or int8 when a_i8 / b_kind == 2 (b_kind 0: none,
+ * 1: int32).  (kernels/expert/<bundle>/reference.c) */
+enum { ORACLE_RQ_PRE_A = 0, ORACLE_RQ_PRE_ADD = 1, ORACLE_RQ_PRE_ADD_RELU = 2,
+       ORACLE_RQ_PRE_MUL_ADD = 3 };
+void oracle_requant_ew(const void *a, int a_i8, const void *b, int b_kind, int64_t n, int pre,
+                       int64_t pre_c, int32_t mult, int shift, int zp, int sign_of_a,
+                       int lo1, int hi1, int lo2, int hi2, const int8_t *lut, void *out);
+/* epilogue_bias_i32/reference.c: out[r][c] = acc[r][c] + bias[c] (int32, wrap) */
+void oracle_epilogue_bias_i32(const int32_t *acc, const int32_t *bias, int32_t *out, int R, int C);
+/* epilogue_relu_i8/reference.c: out = max(x, 0) */
+void oracle_relu_i8(const int8_t *x, int8_t *out, int64_t n);
+
 /* ---- fp16 GEMM ---- */
 
 /* kernels/expert/fp16_attention_qkt_hmx/reference.c:7-15 generalised to

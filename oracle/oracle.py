@@ -134,6 +134,39 @@ def gemm_hmx_ex(A, B, store="i32", act="none", bias=None, res=None, lut=None, zp
     return out
 
 
+def requant_ew(a, b=None, pre="a", pre_c=0, mult=1, shift=0, zp=0, sign_of_a=False,
+               lo1=-128, hi1=127, lo2=-128, hi2=127, lut=None, out_dtype=np.int8):
+    a = np.ascontiguousarray(a)
+    b_kind = 0
+    if b is not None:
+        b = np.ascontiguousarray(b)
+        b_kind = 1 if b.dtype == np.int32 else 2
+    if lut is not None:
+        lut = np.ascontiguousarray(lut, np.int8)
+    out = np.zeros(a.shape, out_dtype)
+    lib().oracle_requant_ew(_p(a), int(a.dtype == np.int8), _p(b) if b is not None else None,
+                            b_kind, C.c_int64(a.size),
+                            {"a": 0, "add": 1, "add_relu": 2, "mul_add": 3}[pre], C.c_int64(pre_c),
+                            C.c_int32(mult), shift, zp, int(sign_of_a), lo1, hi1, lo2, hi2,
+                            _p(lut) if lut is not None else None, _p(out))
+    return out
+
+
+def epilogue_bias_i32(acc, bias):
+    acc, bias = np.ascontiguousarray(acc, np.int32), np.ascontiguousarray(bias, np.int32)
+    R, Cc = acc.shape
+    out = np.zeros_like(acc)
+    lib().oracle_epilogue_bias_i32(_p(acc), _p(bias), _p(out), R, Cc)
+    return out
+
+
+def relu_i8(x):
+    x = np.ascontiguousarray(x, np.int8)
+    out = np.zeros_like(x)
+    lib().oracle_relu_i8(_p(x), _p(out), C.c_int64(x.size))
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp):
     a = np.ascontiguousarray(a, np.int32)
     R, Cc = a.shape

@@ -375,6 +375,71 @@ def gen_hmx_family(ref):
     save("hmx_family", **arrays)
 
 
+def gen_requant_family(ref):
+    # The elementwise requant bundles of tests/requant_family.py plus
+    # epilogue_bias_i32 / epilogue_relu_i8, run through their own reference.c
+    # on seeded inputs (n = 1037, not a multiple of the 16-element vector
+    # step), three parameter sets each where the bundle takes parameters
+    # (large mult / shift, a small mult, a negative mult).  Inputs are sized so
+    # every int64 product stays inside int64, where the references are defined.
+    sys.path.insert(0, str(HERE.parent))
+    from requant_family import RQ_BUNDLES
+    rng = np.random.default_rng(31)
+    n = 1037
+    arrays = {}
+    for b, (params, kw) in RQ_BUNDLES.items():
+        sets = [(int(rng.integers(2**30, 2**31)), int(rng.integers(30, 41)), int(rng.integers(-20, 21))),
+                (3, 4, -2), (-123457, 12, 3)] if "mult" in params else [(0, 0, 0), (0, 0, 0)]
+        for ci, (mult, shift, zp) in enumerate(sets):
+            big = 2**20 if kw.get("pre") == "mul_add" else 2**30
+            a = {"a32": rng.integers(-big, big, n).astype(np.int32),
+                 "b32": rng.integers(-big, big, n).astype(np.int32),
+                 "a8": rng.integers(-128, 128, n).astype(np.int8),
+                 "b8": rng.integers(-128, 128, n).astype(np.int8),
+                 "lut": rng.integers(-128, 128, 256).astype(np.int8)}
+            if "mult" not in params:
+                a["a32"] = rng.integers(-3000, 3000, n).astype(np.int32)
+            lo, hi = sorted(int(v) for v in rng.integers(-100, 100, 2))
+            out = np.zeros(n, np.int8)
+            args = []
+            for prm in params:
+                if prm == "out":
+                    args.append(ptr(out))
+                elif prm == "n":
+                    args.append(n)
+                elif prm == "mult":
+                    args.append(C.c_int32(mult))
+                elif prm == "shift":
+                    args.append(C.c_int(shift))
+                elif prm == "zp":
+                    args.append(C.c_int8(zp))
+                elif prm == "lo":
+                    args.append(C.c_int8(lo))
+                elif prm == "hi":
+                    args.append(C.c_int8(hi))
+                else:
+                    args.append(ptr(a[prm]))
+            getattr(ref, "ref_" + b)(*args)
+            key = f"{b}__c{ci}__"
+            for prm in params:
+                if prm in a:
+                    arrays[key + prm] = a[prm]
+            arrays.update({key + "out": out, key + "mult": np.int32(mult), key + "shift": np.int32(shift),
+                           key + "zp": np.int32(zp), key + "lo": np.int32(lo), key + "hi": np.int32(hi)})
+    R, Cc = 37, 300
+    acc = rng.integers(-2**31, 2**31, (R, Cc), dtype=np.int64).astype(np.int32)
+    bias = rng.integers(-2**31, 2**31, Cc, dtype=np.int64).astype(np.int32)
+    outb = np.zeros((R, Cc), np.int32)
+    ref.ref_epilogue_bias_i32(ptr(acc), ptr(bias), ptr(outb), R, Cc)
+    x8 = rng.integers(-128, 128, n).astype(np.int8)
+    outr = np.zeros(n, np.int8)
+    ref.ref_epilogue_relu_i8(ptr(x8), ptr(outr), n)
+    arrays.update({"epilogue_bias_i32__acc": acc, "epilogue_bias_i32__bias": bias,
+                   "epilogue_bias_i32__out": outb, "epilogue_relu_i8__x": x8,
+                   "epilogue_relu_i8__out": outr})
+    save("requant_family", **arrays)
+
+
 # ----------------------------------------------------------------- fp16
 
 def gen_hf_q(g, mod, off, step):
@@ -549,6 +614,7 @@ def main():
     gen_gemm_u8s8_pc(ref)
     gen_hmx(ref)
     gen_hmx_family(ref)
+    gen_requant_family(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

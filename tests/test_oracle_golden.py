@@ -214,3 +214,24 @@ def test_hmx_family_golden(oracle, bundle):
     column-major) against each bundle's own reference.c."""
     A, B, out, kw = golden_case(golden("hmx_family"), bundle)
     np.testing.assert_array_equal(oracle.gemm_hmx_ex(A, B, **kw), out)
+
+
+from requant_family import RQ_BUNDLES, case_arrays, ew_kwargs  # noqa: E402
+
+RQ_CASES = [(b, c) for b in sorted(RQ_BUNDLES) for c in ("c0", "c1", "c2")
+            if c != "c2" or "mult" in RQ_BUNDLES[b][0]]
+
+
+@pytest.mark.parametrize("bundle,case", RQ_CASES)
+def test_requant_family_golden(oracle, bundle, case):
+    arr = case_arrays(golden("requant_family"), bundle, case)
+    a = arr["a8"] if "a8" in arr else arr["a32"]
+    np.testing.assert_array_equal(oracle.requant_ew(a, **ew_kwargs(bundle, arr)), arr["out"])
+
+
+def test_epilogue_bias_relu_golden(oracle):
+    g = golden("requant_family")
+    np.testing.assert_array_equal(
+        oracle.epilogue_bias_i32(g["epilogue_bias_i32__acc"], g["epilogue_bias_i32__bias"]),
+        g["epilogue_bias_i32__out"])
+    np.testing.assert_array_equal(oracle.relu_i8(g["epilogue_relu_i8__x"]), g["epilogue_relu_i8__out"])

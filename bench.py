@@ -497,7 +497,131 @@ class GemmI8(Workload):
     cpu_what = "kernels/expert/i8_gemm_requant/reference.c (one thread)"
 
 
-WORKLOADS = {w.name: w for w in (Reduce, GemmU8S8, GemmF16, Attn, GemmI8)}
+def _threaded(fn, total, nthreads):
+    """Run fn(r0, r1) over [0, total) split across nthreads host threads (the
+    oracle's C calls release the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+    parts = [(total * i // nthreads, total * (i + 1) // nthreads) for i in range(nthreads)]
+    with ThreadPoolExecutor(nthreads) as ex:
+        list(ex.map(lambda p: fn(*p), [p for p in parts if p[1] > p[0]]))
+
+
+class RequantEw(Workload):
+    """residual_add_requant over 2^28 int32 pairs (the elementwise requant
+    kernel's two-input form): HBM-bound, 9 bytes per element."""
+    name = "requant"
+    unit = "GB/s"
+    dtype = "int64"
+    bound = "hbm"
+    N = 1 << 28
+    MULT, SHIFT, ZP = 1518500250, 38, 3
+
+    def config(self):
+        return {"workload": "residual_add_requant int32+int32 -> int8, 2^28 elements",
+                "n": self.N, "a": "U[-2^30,2^30)", "b": "U[-2^30,2^30)", "mult": self.MULT,
+                "shift": self.SHIFT, "zp": self.ZP, "seed": 0,
+                "l2": "inputs 2 GiB > L2, no flush", "sharding": "elements",
+                "parallelism": f"elements/{self.world}"}
+
+    def units_per_step(self):
+        return 9.0 * self.N
+
+    def setup_device(self, torch):
+        r0, r1 = shard(self.N, self.world, self.rank)
+        self.n = r1 - r0
+        g = torch.Generator(device="cuda").manual_seed(0)
+        self.a = torch.randint(-2**30, 2**30, (self.n,), dtype=torch.int32, device="cuda", generator=g)
+        self.b = torch.randint(-2**30, 2**30, (self.n,), dtype=torch.int32, device="cuda", generator=g)
+        self.out = torch.empty((self.n,), dtype=torch.int8, device="cuda")
+
+    def kernels(self):
+        return [("requant_ew", 9.0 * self.n)]
+
+    def launch(self, device, k):
+        device.launch("requant_ew", 0, self.a, 0, self.b, 1, self.out, self.n, 1, 0, self.MULT,
+                      self.SHIFT, self.ZP, 0, -128, 127, -128, 127, None)
+
+    def cpu_setup(self, rows):
+        rng = np.random.default_rng(0)
+        self.ca = rng.integers(-2**30, 2**30, rows).astype(np.int32)
+        self.cb = rng.integers(-2**30, 2**30, rows).astype(np.int32)
+        self.cout = np.empty(rows, np.int8)
+
+    def cpu_step(self, o, rows, nthreads):
+        import ctypes as C
+        lib = o.lib()
+
+        def part(r0, r1):
+            lib.oracle_requant_ew(C.c_void_p(self.ca.ctypes.data + 4 * r0), 0,
+                                  C.c_void_p(self.cb.ctypes.data + 4 * r0), 1, C.c_int64(r1 - r0),
+                                  1, C.c_int64(0), C.c_int32(self.MULT), self.SHIFT, self.ZP, 0,
+                                  -128, 127, -128, 127, None, C.c_void_p(self.cout.ctypes.data + r0))
+        _threaded(part, rows, nthreads)
+        return 9.0 * rows
+
+    cpu_kind = "port"
+    cpu_what = "oracle/hexoracle.c restatement of residual_add_requant/reference.c"
+
+
+class GemmHmx(Workload):
+    """HMX-convention u8 x s8 GEMM with bias and ReLU to int32
+    (i8_matmul_bias_relu_hmx's epilogue) at 16384 x 8192 x 8192."""
+    name = "gemm_hmx"
+    unit = "TOPS"
+    dtype = "u8*s8->s32"
+    bound = "tensor"
+    M, N, K = 16384, 8192, 8192
+
+    def config(self):
+        return {"workload": "HMX-convention u8 x s8 GEMM 16384x8192x8192, sx12 + bias + ReLU -> int32",
+                "M": self.M, "N": self.N, "K": self.K, "bias": "U[-3000,3000)", "seed": 0,
+                "l2": "inputs 192 MiB > L2, no flush", "sharding": "M rows",
+                "parallelism": f"M/{self.world}"}
+
+    def units_per_step(self):
+        return 2.0 * self.M * self.N * self.K
+
+    def setup_device(self, torch):
+        r0, r1 = shard(self.M, self.world, self.rank)
+        self.m = r1 - r0
+        g = torch.Generator(device="cuda").manual_seed(0)
+        self.A = torch.randint(0, 256, (self.m, self.K), dtype=torch.uint8, device="cuda", generator=g)
+        self.B = torch.randint(-128, 128, (self.K, self.N), dtype=torch.int8, device="cuda", generator=g)
+        self.bias = torch.randint(-3000, 3000, (self.N,), dtype=torch.int32, device="cuda", generator=g)
+        self.out = torch.empty((self.m, self.N), dtype=torch.int32, device="cuda")
+
+    def kernels(self):
+        return [("gemm_hmx_ex", 2.0 * self.m * self.N * self.K)]
+
+    def launch(self, device, k):
+        device.launch("gemm_hmx_ex", 0, self.A, self.B, 0, self.bias, None, 0, None, self.out, 0, 1,
+                      0, self.m, self.N, self.K, 0)
+
+    def cpu_setup(self, rows):
+        rng = np.random.default_rng(0)
+        self.cA = rng.integers(0, 256, (rows, self.K), dtype=np.uint8)
+        self.cB = rng.integers(-128, 128, (self.K, self.N), dtype=np.int8)
+        self.cbias = rng.integers(-3000, 3000, self.N).astype(np.int32)
+        self.cout = np.empty((rows, self.N), np.int32)
+
+    def cpu_step(self, o, rows, nthreads):
+        import ctypes as C
+        lib = o.lib()
+
+        def part(r0, r1):
+            lib.oracle_gemm_hmx_ex_rows(C.c_void_p(self.cA.ctypes.data), C.c_void_p(self.cB.ctypes.data),
+                                        0, C.c_void_p(self.cout.ctypes.data), rows, self.N, self.K,
+                                        C.c_int32(0), 0, 1, C.c_void_p(self.cbias.ctypes.data), 0,
+                                        None, None, 0, r0, r1)
+        _threaded(part, rows, nthreads)
+        return 2.0 * rows * self.N * self.K
+
+    cpu_kind = "port"
+    cpu_what = ("oracle/hexoracle.c restatement of the HMX-convention GEMMs "
+                "(i8_matmul_bias_relu_hmx/reference.c), rows split over host threads")
+
+
+WORKLOADS = {w.name: w for w in (Reduce, GemmU8S8, GemmF16, Attn, GemmI8, RequantEw, GemmHmx)}
 
 
 # ------------------------------------------------------------------- timing
@@ -555,7 +679,7 @@ def cpu_measure(wl, budget_s: float, nthreads: int, max_rows: int):
     then times repeated calls for about `budget_s` seconds."""
     from oracle import oracle as o
     o.lib()
-    rows = 8 if wl.name != "reduce" else 256
+    rows = {"reduce": 256, "requant": 1 << 16}.get(wl.name, 8)
     rows = min(rows, max_rows)
     while True:
         wl.cpu_setup(rows)
@@ -576,7 +700,7 @@ def cpu_measure(wl, budget_s: float, nthreads: int, max_rows: int):
 
 def cpu_rows_cap(wl):
     return {"reduce": wl.R if hasattr(wl, "R") else 0, "gemm_u8s8": 4096, "gemm_f16": 4096,
-            "attn": 4096, "gemm_i8": 256}[wl.name]
+            "attn": 4096, "gemm_i8": 256, "requant": 1 << 28, "gemm_hmx": 4096}[wl.name]
 
 
 def cpu_sample_text(wl, rows, reps, secs):
@@ -586,6 +710,8 @@ def cpu_sample_text(wl, rows, reps, secs):
         return f"last {rows} query rows of one causal head (S=4096, D=128), {reps} reps, {secs:.1f} s"
     if wl.name == "gemm_i8":
         return f"the full 256^3 GEMM, {reps} reps, {secs:.1f} s"
+    if wl.name == "requant":
+        return f"{rows} of 2^28 elements, {reps} reps, {secs:.1f} s"
     return f"{rows} rows of M with full N, K, {reps} reps, {secs:.1f} s"
 
 
@@ -662,7 +788,7 @@ def run_ours(args, dist):
     head = measure(WORKLOADS[args.workload], True, True)
     ops = {}
     if args.ops == "all":
-        for name in ("gemm_u8s8", "gemm_f16", "attn", "gemm_i8"):
+        for name in ("gemm_u8s8", "gemm_f16", "attn", "gemm_i8", "requant", "gemm_hmx"):
             if name == args.workload:
                 continue
             r = measure(WORKLOADS[name], False, args.cpu_all)
@@ -695,7 +821,7 @@ def run_reference(args, dist):
     nthreads = 1 if wl.name == "gemm_i8" else len(os.sched_getaffinity(0))
     # size the per-step sample so the whole run stays within ~2 minutes
     per_step_budget = max(0.2, 100.0 / max(1, args.steps + args.warmup))
-    rows = 8 if wl.name != "reduce" else 256
+    rows = {"reduce": 256, "requant": 1 << 16}.get(wl.name, 8)
     cap = cpu_rows_cap(wl)
     while True:
         wl.cpu_setup(rows)

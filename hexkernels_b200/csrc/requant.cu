@@ -72,39 +72,65 @@ struct RqEw {
     int sign_of_a;      // sign(x) * ((|x| * mult + half) >> shift)
     int lo1, hi1, lo2, hi2;
     const int8_t *lut;  // 256 entries or null
+    int lo, hi;         // the two clamps folded into one (set by the entry)
+    uint32_t amult;     // |mult|
+    bool mneg;          // mult < 0
 };
 
-__device__ __forceinline__ uint32_t rq_ew_one(int64_t a, int64_t b, const RqEw &p) {
+// One element.  PRE and SIGN_OF_A are compile-time so the per-element code
+// has no mode branches.  (A signed form of the rounding, (v + half - (v < 0))
+// >> shift with v from 32 x 32 multiplies, measured slower: it is the
+// integer ALU pipe that bounds this kernel.)  p.lo / p.hi are the two clamps folded into one
+// (the composition of two clamps is the clamp to [clamp(lo1, lo2, hi2),
+// clamp(hi1, lo2, hi2)]).
+template <int PRE, bool SIGN_OF_A>
+__device__ __forceinline__ uint32_t rq_ew_one(int32_t a, int32_t b, const RqEw &p, int64_t half) {
+    int32_t r32;
     int64_t x = a;
-    if (p.pre == HEXCUDA_RQ_PRE_ADD) {
-        x = a + b;
-    } else if (p.pre == HEXCUDA_RQ_PRE_ADD_RELU) {
-        x = a + b;
+    if constexpr (PRE == HEXCUDA_RQ_PRE_ADD) {
+        x = (int64_t)a + b;
+    } else if constexpr (PRE == HEXCUDA_RQ_PRE_ADD_RELU) {
+        x = (int64_t)a + b;
         x = x > 0 ? x : 0;
-    } else if (p.pre == HEXCUDA_RQ_PRE_MUL_ADD) {
-        x = (int64_t)((uint64_t)a * (uint64_t)b + (uint64_t)p.c);
+    } else if constexpr (PRE == HEXCUDA_RQ_PRE_MUL_ADD) {
+        x = (int64_t)((uint64_t)(int64_t)a * (uint64_t)(int64_t)b + (uint64_t)p.c);
     }
-    int64_t r;
-    if (p.sign_of_a) {
-        const int64_t half = p.shift > 0 ? ((int64_t)1 << (p.shift - 1)) : 0;
-        const int64_t am = (int64_t)((uint64_t)(x < 0 ? -x : x) * (uint64_t)(int64_t)p.mult);
-        const int64_t sh = (am + half) >> p.shift;
-        r = x < 0 ? -sh : sh;
+    const bool xneg = x < 0;
+    const uint64_t ax = xneg ? 0ull - (uint64_t)x : (uint64_t)x;
+    if (!SIGN_OF_A && ax < (1ull << 32)) {
+        // |x| < 2^32, |mult| <= 2^31: the exact |x * mult| < 2^63 from one
+        // 32 x 32 -> 64 multiply; round half away from zero on the magnitude
+        // (the reference's v >= 0 / v < 0 branches, including its int64 wrap
+        // of v + half at the largest shifts)
+        const int64_t ra = (int64_t)((uint64_t)(uint32_t)ax * p.amult + (uint64_t)half) >> p.shift;
+        const int32_t m = ra > (1 << 28) ? (1 << 28) : (ra < -(1 << 28) ? -(1 << 28) : (int32_t)ra);
+        r32 = (xneg != p.mneg) ? -m : m;
     } else {
-        r = rq_round((int64_t)((uint64_t)x * (uint64_t)(int64_t)p.mult), p.shift);
+        int64_t r;
+        if constexpr (SIGN_OF_A) {
+            const int64_t am = (int64_t)(ax * (uint64_t)(int64_t)p.mult);
+            const int64_t sh = (am + half) >> p.shift;
+            r = xneg ? -sh : sh;
+        } else {
+            r = rq_round((int64_t)((uint64_t)x * (uint64_t)(int64_t)p.mult), p.shift);
+        }
+        r32 = (int32_t)(r > (1 << 28) ? (1 << 28) : (r < -(1 << 28) ? -(1 << 28) : r));
     }
-    r += p.zp;
-    r = r > p.hi1 ? p.hi1 : r;
-    r = r < p.lo1 ? p.lo1 : r;
-    r = r > p.hi2 ? p.hi2 : r;
-    r = r < p.lo2 ? p.lo2 : r;
-    if (p.lut) return (uint32_t)(uint8_t)__ldg(p.lut + (uint8_t)r);
-    return (uint32_t)(uint8_t)r;
+    // zp, lo and hi are within +-2^24 (checked by the entry), so the magnitude
+    // cap at 2^28 above changes no clamped result
+    r32 = max(min(r32 + p.zp, p.hi), p.lo);
+    if (p.lut) return (uint32_t)(uint8_t)__ldg(p.lut + (uint8_t)r32);
+    return (uint32_t)r32 & 0xFFu;
+}
+
+// four results (low bytes) into one 32-bit word
+__device__ __forceinline__ uint32_t pack4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3) {
+    return __byte_perm(__byte_perm(x0, x1, 0x0040), __byte_perm(x2, x3, 0x0040), 0x5410);
 }
 
 // 16 consecutive elements of one operand as int64 (int8 or int32 source)
 template <bool I8>
-__device__ __forceinline__ void load16(const void *src, int64_t v, int64_t (&x)[16]) {
+__device__ __forceinline__ void load16(const void *src, int64_t v, int32_t (&x)[16]) {
     if constexpr (I8) {
         const uint4 q = __ldcs(reinterpret_cast<const uint4 *>(src) + v);
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
@@ -120,41 +146,89 @@ __device__ __forceinline__ void load16(const void *src, int64_t v, int64_t (&x)[
 }
 
 template <bool I8>
-__device__ __forceinline__ int64_t load1(const void *src, int64_t i) {
+__device__ __forceinline__ int32_t load1(const void *src, int64_t i) {
     if constexpr (I8)
         return reinterpret_cast<const int8_t *>(src)[i];
     else
         return reinterpret_cast<const int32_t *>(src)[i];
 }
 
-// Each thread turns 16 elements (one or two operands) into 16 output bytes
-// (one 128-bit store) per step; a scalar loop takes the tail and unaligned
-// buffers.  B_KIND: 0 none, 1 int32, 2 int8.
-template <bool A_I8, int B_KIND>
+// 4 consecutive elements of one operand (int32: one 16-byte load; int8:
+// one 4-byte load); consecutive lanes read consecutive 4-element groups, so
+// every load instruction of a warp is one contiguous run.
+template <bool I8>
+__device__ __forceinline__ void load4(const void *src, int64_t v, int32_t (&x)[4]) {
+    if constexpr (I8) {
+        const uint32_t w = __ldcs(reinterpret_cast<const unsigned int *>(src) + v);
+#pragma unroll
+        for (int i = 0; i < 4; i++) x[i] = (int8_t)(w >> (8 * i));
+    } else {
+        const int4 q = __ldcs(reinterpret_cast<const int4 *>(src) + v);
+        x[0] = q.x, x[1] = q.y, x[2] = q.z, x[3] = q.w;
+    }
+}
+
+template <bool A_I8, int B_KIND, int PRE, bool SIGN_OF_A>
 __global__ void __launch_bounds__(256) requant_ew_kernel(const void *__restrict__ a,
                                                           const void *__restrict__ b,
                                                           uint8_t *__restrict__ out, int64_t n,
                                                           const RqEw p, int vec) {
+    const int64_t half = p.shift > 0 ? ((int64_t)1 << (p.shift - 1)) : 0;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    constexpr bool kWide = A_I8 && B_KIND != 1;   // int8 data only: 16 per step
     int64_t done = 0;
-    if (vec) {
+    if (vec && kWide) {
         const int64_t nv = n / 16;
         for (int64_t v = t; v < nv; v += stride) {
-            int64_t xa[16], xb[16];
-            load16<A_I8>(a, v, xa);
-            if constexpr (B_KIND != 0) load16<B_KIND == 2>(b, v, xb);
-            uint32_t w[4] = {0, 0, 0, 0};
+            int32_t xa[16], xb[16];
+            load16<true>(a, v, xa);
+            if constexpr (B_KIND != 0) load16<true>(b, v, xb);
+            uint32_t y[16], w[4];
 #pragma unroll
             for (int i = 0; i < 16; i++)
-                w[i >> 2] |= rq_ew_one(xa[i], B_KIND != 0 ? xb[i] : 0, p) << (8 * (i & 3));
+                y[i] = rq_ew_one<PRE, SIGN_OF_A>(xa[i], B_KIND != 0 ? xb[i] : 0, p, half);
+#pragma unroll
+            for (int k = 0; k < 4; k++) w[k] = pack4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
             __stcs(reinterpret_cast<uint4 *>(out) + v, make_uint4(w[0], w[1], w[2], w[3]));
         }
         done = nv * 16;
+    } else if (vec) {
+        // two grid-stride steps per iteration: both steps' loads are issued
+        // before any result is needed (memory-level parallelism)
+        const int64_t nv = n / 4;
+        int64_t v = t;
+        for (; v + stride < nv; v += 2 * stride) {
+            int32_t xa[2][4], xb[2][4];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                load4<A_I8>(a, v + u * stride, xa[u]);
+                if constexpr (B_KIND != 0) load4<B_KIND == 2>(b, v + u * stride, xb[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                uint32_t y[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    y[i] = rq_ew_one<PRE, SIGN_OF_A>(xa[u][i], B_KIND != 0 ? xb[u][i] : 0, p, half);
+                __stcs(reinterpret_cast<unsigned int *>(out) + v + u * stride, pack4(y[0], y[1], y[2], y[3]));
+            }
+        }
+        for (; v < nv; v += stride) {
+            int32_t xa[4], xb[4];
+            load4<A_I8>(a, v, xa);
+            if constexpr (B_KIND != 0) load4<B_KIND == 2>(b, v, xb);
+            uint32_t y[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                y[i] = rq_ew_one<PRE, SIGN_OF_A>(xa[i], B_KIND != 0 ? xb[i] : 0, p, half);
+            __stcs(reinterpret_cast<unsigned int *>(out) + v, pack4(y[0], y[1], y[2], y[3]));
+        }
+        done = nv * 4;
     }
     for (int64_t i = done + t; i < n; i += stride) {
-        const int64_t bi = B_KIND == 0 ? 0 : load1<B_KIND == 2>(b, i);
-        out[i] = (uint8_t)rq_ew_one(load1<A_I8>(a, i), bi, p);
+        const int32_t bi = B_KIND == 0 ? 0 : load1<B_KIND == 2>(b, i);
+        out[i] = (uint8_t)rq_ew_one<PRE, SIGN_OF_A>(load1<A_I8>(a, i), bi, p, half);
     }
 }
 
@@ -256,32 +330,58 @@ HX_EXPORT int hexcuda_requant_ew(int dev, const void *a, int a_i8, const void *b
                                  int hi2, const int8_t *lut) {
     Dev *d = get_dev(dev);
     if (!d) return HEXCUDA_ERR_NODEV;
+    const int kLim = 1 << 24;
+    if (zp < -kLim || zp > kLim || lo1 < -kLim || lo1 > kLim || hi1 < -kLim || hi1 > kLim ||
+        lo2 < -kLim || lo2 > kLim || hi2 < -kLim || hi2 > kLim)
+        return fail(HEXCUDA_ERR_ARG, "requant_ew: zp / clamp bounds beyond +-2^24");
     if (n < 0 || shift < 0 || shift > 63 || b_kind < 0 || b_kind > 2 ||
         pre < HEXCUDA_RQ_PRE_A || pre > HEXCUDA_RQ_PRE_MUL_ADD || (pre != HEXCUDA_RQ_PRE_A && !b_kind))
         return fail(HEXCUDA_ERR_ARG, "requant_ew: n=%lld shift=%d b_kind=%d pre=%d", (long long)n,
                     shift, b_kind, pre);
     if (n == 0) return HEXCUDA_OK;
     if (!a || !out || (b_kind && !b)) return fail(HEXCUDA_ERR_ARG, "requant_ew: null pointer");
-    RqEw p{pre, pre_c, mult, shift, zp, sign_of_a ? 1 : 0, lo1, hi1, lo2, hi2, lut};
+    RqEw p{pre, pre_c, mult, shift, zp, sign_of_a ? 1 : 0, lo1, hi1, lo2, hi2, lut, 0, 0, 0, false};
+    {
+        auto clampi = [](int v, int lo, int hi) { return std::max(std::min(v, hi), lo); };
+        p.lo = clampi(lo1, lo2, hi2);
+        p.hi = clampi(hi1, lo2, hi2);
+        p.amult = mult < 0 ? 0u - (uint32_t)mult : (uint32_t)mult;
+        p.mneg = mult < 0;
+    }
     auto al = [](const void *q) { return q == nullptr || ((uintptr_t)q & 15u) == 0; };
     const int vec = al(a) && al(b) && al(out);
-    const int blocks = ew_blocks(d, vec ? (n + 15) / 16 : n);
+    const int per = (a_i8 && b_kind != 1) ? 16 : 4;
+    const int blocks = ew_blocks(d, vec ? (n + per - 1) / per : n);
     uint8_t *o = reinterpret_cast<uint8_t *>(out);
     launch_begin(d);
-    if (a_i8) {
-        if (b_kind == 2)
-            requant_ew_kernel<true, 2><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
-        else if (b_kind == 1)
-            requant_ew_kernel<true, 1><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+    if (sign_of_a) {
+        if (pre != HEXCUDA_RQ_PRE_A) return fail(HEXCUDA_ERR_ARG, "requant_ew: sign_of_a takes a alone");
+        if (a_i8)
+            requant_ew_kernel<true, 0, HEXCUDA_RQ_PRE_A, true><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
         else
-            requant_ew_kernel<true, 0><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+            requant_ew_kernel<false, 0, HEXCUDA_RQ_PRE_A, true><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+    } else if (pre == HEXCUDA_RQ_PRE_A) {
+        if (a_i8)
+            requant_ew_kernel<true, 0, HEXCUDA_RQ_PRE_A, false><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+        else
+            requant_ew_kernel<false, 0, HEXCUDA_RQ_PRE_A, false><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
     } else {
-        if (b_kind == 2)
-            requant_ew_kernel<false, 2><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
-        else if (b_kind == 1)
-            requant_ew_kernel<false, 1><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
-        else
-            requant_ew_kernel<false, 0><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+        // two-operand forms: int32 pairs or int8 pairs (the corpus's bundles)
+        if (a_i8 != (b_kind == 2))
+            return fail(HEXCUDA_ERR_ARG, "requant_ew: a and b must both be int32 or both int8");
+#define HX_RQ2(P)                                                                                 \
+    if (a_i8)                                                                                    \
+        requant_ew_kernel<true, 2, P, false><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec); \
+    else                                                                                         \
+        requant_ew_kernel<false, 1, P, false><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+        if (pre == HEXCUDA_RQ_PRE_ADD) {
+            HX_RQ2(HEXCUDA_RQ_PRE_ADD)
+        } else if (pre == HEXCUDA_RQ_PRE_ADD_RELU) {
+            HX_RQ2(HEXCUDA_RQ_PRE_ADD_RELU)
+        } else {
+            HX_RQ2(HEXCUDA_RQ_PRE_MUL_ADD)
+        }
+#undef HX_RQ2
     }
     return launch_end(d, "requant_ew");
 }

@@ -127,6 +127,8 @@ int hexcuda_requantize_i32_u8(int dev, const int32_t *a, uint8_t *out, int64_t n
  *   r = max(min(r, hi1), lo1); r = max(min(r, hi2), lo2)
  *   out byte = lut ? lut[(uint8) r] : (uint8) r
  * a int32 (or int8 with a_i8), b none / int32 / int8 (b_kind 0 / 1 / 2).
+ * zp, lo1, hi1, lo2, hi2 within +-2^24; the two-operand forms take a and b
+ * both int32 or both int8; sign_of_a only with pre A (HEXCUDA_ERR_ARG otherwise).
  * Products that leave int64 wrap (undefined in the C references).
  * Bundles (kernels/expert/<name>/kernel_api.h): requantize_i32_i8_dma,
  * epilogue_requant_i32_i8, requant_relu_dma (13, 3, clamp [0,127]),

@@ -10,7 +10,8 @@
  *    STMT (host CLOCK_MONOTONIC; the Hexagon pcycle counter does not exist
  *    here).  When libhexcuda is linked, the device time of the last launch,
  *    measured with a cudaEvent pair on the launching stream, is printed as
- *    "HEXCUDA_KERNEL_US kernel=<device us> wall=<call us>".
+ *    "HEXCUDA_KERNEL_US kernel=<device us> wall=<call us> launches=<n>" (n =
+ *    libhexcuda kernel launches made by STMT).
  *  - hvx_lcg, hvx_report, hvx_report_u16, hvx_close_f32, hvx_close_f16bits:
  *    same arithmetic and output line format (HVXENV_CORRECT / HVXENV_INCORRECT)
  *    as the corpus, so the corpus's evaluate.py result parser still applies.
@@ -32,6 +33,7 @@
 /* libhexcuda's device-time query; weak so a harness linked against the CPU
  * oracle (no libhexcuda) still links and simply prints no device time. */
 extern float hexcuda_last_kernel_ms(void) __attribute__((weak));
+extern uint64_t hexcuda_launch_count(void) __attribute__((weak));
 
 static inline void hvx_enable_pcycle(void) {}
 static inline unsigned long long hvx_rdpcyc(void) {
@@ -41,14 +43,16 @@ static inline unsigned long long hvx_rdpcyc(void) {
 }
 
 #define HVX_TIME_KERNEL(OUT, STMT) do {                                        \
+    unsigned long long _hx_l0 = hexcuda_launch_count ? hexcuda_launch_count() : 0; \
     unsigned long long _hx_t0 = hvx_rdpcyc();                                  \
     STMT;                                                                      \
     unsigned long long _hx_t1 = hvx_rdpcyc();                                  \
     (OUT) = _hx_t1 - _hx_t0;                                                   \
     if (hexcuda_last_kernel_ms)                                                \
-        printf("HEXCUDA_KERNEL_US kernel=%.3f wall=%.3f\n",                   \
+        printf("HEXCUDA_KERNEL_US kernel=%.3f wall=%.3f launches=%llu\n",     \
                1000.0 * (double)hexcuda_last_kernel_ms(),                      \
-               (double)(OUT) / 1000.0);                                        \
+               (double)(OUT) / 1000.0,                                         \
+               (hexcuda_launch_count ? hexcuda_launch_count() : 0) - _hx_l0);  \
 } while (0)
 
 /* LCG: s = s * 1664525 + 1013904223 (mod 2^32), as the corpus harnesses use. */

@@ -170,6 +170,7 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
                 const uint32_t a32 = r[4 * i4 + u] - (uint32_t)cc[u];
                 const int32_t f = (int32_t)(a32 * 17u + 8u) >> 4;
                 uint32_t xu = (uint32_t)((int32_t)((uint32_t)f << 20) >> 20);  // sx12
+                if (ep.hmx_store == HEXCUDA_HMX_STORE_ACC_I32) xu = a32;     // raw accumulator
                 xu += (uint32_t)bb[u] + (uint32_t)rv[4 * i4 + u];
                 int32_t x = (int32_t)xu;
                 if (ep.hmx_act == HEXCUDA_HMX_ACT_RELU) x = max(x, 0);
@@ -191,7 +192,8 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
         }
         if (row >= ep.M) return;
         const int es = (ep.hmx_store == HEXCUDA_HMX_STORE_I32 ||
-                        ep.hmx_store == HEXCUDA_HMX_STORE_LUT_I32) ? 4
+                        ep.hmx_store == HEXCUDA_HMX_STORE_LUT_I32 ||
+                        ep.hmx_store == HEXCUDA_HMX_STORE_ACC_I32) ? 4
                        : ep.hmx_store == HEXCUDA_HMX_STORE_U16_FIELD ? 2 : 1;
         if (ep.col_major) {
             // lanes are consecutive rows: each column's store is one
@@ -902,7 +904,7 @@ HX_EXPORT int hexcuda_gemm_hmx_ex(int dev, const uint8_t *A, const int8_t *B, in
                                   const int32_t *bias, const void *res, int res_kind,
                                   const void *lut, void *out, int store, int act, int col_major,
                                   int M, int N, int K, int32_t zpA) {
-    if (store < HEXCUDA_HMX_STORE_I32 || store > HEXCUDA_HMX_STORE_LUT_I8)
+    if (store < HEXCUDA_HMX_STORE_I32 || store > HEXCUDA_HMX_STORE_ACC_I32)
         return fail(HEXCUDA_ERR_ARG, "gemm_hmx: store kind %d", store);
     if (act < HEXCUDA_HMX_ACT_NONE || act > HEXCUDA_HMX_ACT_LEAKY_SHR3)
         return fail(HEXCUDA_ERR_ARG, "gemm_hmx: activation %d", act);

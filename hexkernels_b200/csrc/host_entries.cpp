@@ -463,7 +463,7 @@ HX_EXPORT int hexcuda_host_gemm_hmx_ex(const uint8_t *A, const int8_t *B, int b_
                                        const void *lut, void *out, int store, int act,
                                        int col_major, int M, int N, int K, int32_t zpA) {
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_hmx: bad shape");
-    if (store < HEXCUDA_HMX_STORE_I32 || store > HEXCUDA_HMX_STORE_LUT_I8 ||
+    if (store < HEXCUDA_HMX_STORE_I32 || store > HEXCUDA_HMX_STORE_ACC_I32 ||
         res_kind < HEXCUDA_HMX_RES_NONE || res_kind > HEXCUDA_HMX_RES_I8)
         return fail(HEXCUDA_ERR_ARG, "host_gemm_hmx: store %d / residual %d", store, res_kind);
     if (M == 0 || N == 0) return HEXCUDA_OK;
@@ -471,7 +471,8 @@ HX_EXPORT int hexcuda_host_gemm_hmx_ex(const uint8_t *A, const int8_t *B, int b_
     if (int rc = null_check("host_gemm_hmx", {A, B, out, res_kind ? res : (const void *)A,
                                               has_lut ? lut : (const void *)A}))
         return rc;
-    const size_t osize = (store == HEXCUDA_HMX_STORE_I32 || store == HEXCUDA_HMX_STORE_LUT_I32) ? 4
+    const size_t osize = (store == HEXCUDA_HMX_STORE_I32 || store == HEXCUDA_HMX_STORE_LUT_I32 ||
+                          store == HEXCUDA_HMX_STORE_ACC_I32) ? 4
                          : store == HEXCUDA_HMX_STORE_U16_FIELD ? 2 : 1;
     const size_t rsize = res_kind == HEXCUDA_HMX_RES_I32 ? 4 : 1;
     const size_t lsize = store == HEXCUDA_HMX_STORE_LUT_I32 ? 4 : 1;
@@ -521,6 +522,23 @@ HX_EXPORT int hexcuda_host_gemm_hmx(const uint8_t *A, const int8_t *B, int b_tra
         p.dout = dout;
         return hexcuda_gemm_hmx(p.slot, dA, dB, b_transposed, dbias, dout, out_kind, (int)nr, N,
                                 K, zpA);
+    });
+}
+
+HX_EXPORT int hexcuda_host_attn_qkt_av_hmx(const uint8_t *Q, const int8_t *K, const int8_t *V,
+                                           int32_t *out, int SQ, int SK, int D) {
+    if (SQ < 0 || SK < 0 || D < 0) return fail(HEXCUDA_ERR_ARG, "host_attn_qkt_av_hmx: bad shape");
+    if (SQ == 0 || D == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_attn_qkt_av_hmx", {Q, K, V, out})) return rc;
+    return run_sharded(SQ, out, (size_t)D * 4, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const uint8_t *dQ = stage_in(p.d, kSlotIn0, Q + p.r0 * D, (size_t)(nr * D));
+        const int8_t *dK = stage_in(p.d, kSlotIn1, K, (size_t)SK * D);
+        const int8_t *dV = stage_in(p.d, kSlotIn2, V, (size_t)SK * D);
+        int32_t *dout = reinterpret_cast<int32_t *>(scratch(p.d, kSlotOut, (size_t)(nr * D) * 4));
+        if (!dQ || !dK || !dV || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_attn_qkt_av_hmx(p.slot, dQ, dK, dV, dout, (int)nr, SK, D);
     });
 }
 

@@ -111,7 +111,7 @@ def gemm_hmx(A, B, out_kind: int = HMX_OUT_I32, bias=None, zpA: int = 0,
 
 HMX_STORE = {"i32": (0, np.int32), "i8_sat": (1, np.int8), "u8_sat": (2, np.uint8),
              "i8_low": (3, np.int8), "u16_field": (4, np.uint16), "lut_i32": (5, np.int32),
-             "lut_i8": (6, np.int8)}
+             "lut_i8": (6, np.int8), "acc_i32": (7, np.int32)}
 HMX_ACT = {"none": 0, "relu": 1, "leaky_shr3": 2}
 
 
@@ -181,6 +181,16 @@ def relu_i8(x) -> np.ndarray:
     x = _c(x, np.int8)
     out = np.empty_like(x)
     check(load().hexcuda_host_relu_i8(_p(x), _p(out), x.size))
+    return out
+
+
+def attn_qkt_av_hmx(Q, K, V) -> np.ndarray:
+    """sx12 field of (sx12 field of Q K^T) V; Q [SQ, D] u8, K / V [SK, D] s8."""
+    Q, K, V = _c(Q, np.uint8), _c(K, np.int8), _c(V, np.int8)
+    (SQ, D), (SK, D2) = Q.shape, K.shape
+    assert D == D2 and V.shape == K.shape
+    out = np.empty((SQ, D), np.int32)
+    check(load().hexcuda_host_attn_qkt_av_hmx(_p(Q), _p(K), _p(V), _p(out), SQ, SK, D))
     return out
 
 

@@ -249,6 +249,9 @@ int hexcuda_gemm_hmx(int dev, const uint8_t *A, const int8_t *B, int b_transpose
 #define HEXCUDA_HMX_STORE_U16_FIELD 4
 #define HEXCUDA_HMX_STORE_LUT_I32 5
 #define HEXCUDA_HMX_STORE_LUT_I8 6
+/* out int32 = the accumulator itself, without the 12-bit field (a building
+ * block for compositions such as hexcuda_attn_qkt_av_hmx) */
+#define HEXCUDA_HMX_STORE_ACC_I32 7
 #define HEXCUDA_HMX_ACT_NONE 0
 #define HEXCUDA_HMX_ACT_RELU 1
 #define HEXCUDA_HMX_ACT_LEAKY_SHR3 2
@@ -259,6 +262,15 @@ int hexcuda_gemm_hmx_ex(int dev, const uint8_t *A, const int8_t *B, int b_transp
                         const int32_t *bias, const void *res, int res_kind,
                         const void *lut, void *out, int store, int act, int col_major,
                         int M, int N, int K, int32_t zpA);
+
+/* HMX-convention QK^T -> AV block: Sc = sx12((Q K^T * 17 + 8) >> 4) (int,
+ * Q [SQ,D] u8, K [SK,D] s8), out [SQ,D] int32 = sx12((Sc V * 17 + 8) >> 4)
+ * (V [SK,D] s8).  kernels/expert/i8_attention_qkt_av_hmx/kernel_api.h
+ * (SQ = SK = S).  Four tcgen05 GEMM launches and two elementwise passes; the
+ * 12-bit Sc is split exactly into a u8 low byte and a zero-pointed u8 high
+ * byte for the second product. */
+int hexcuda_attn_qkt_av_hmx(int dev, const uint8_t *Q, const int8_t *K, const int8_t *V,
+                            int32_t *out, int SQ, int SK, int D);
 
 /* fp16 GEMM, fp32 accumulate, one fp16 rounding: out[M,N] = A[M,K] . Bt[N,K]^T
  * (B column-major).  kernels/expert/fp16_attention_qkt_hmx/kernel_api.h:4-20. */
@@ -341,6 +353,8 @@ int hexcuda_host_gemm_hmx_ex(const uint8_t *A, const int8_t *B, int b_transposed
                              const int32_t *bias, const void *res, int res_kind,
                              const void *lut, void *out, int store, int act,
                              int col_major, int M, int N, int K, int32_t zpA);
+int hexcuda_host_attn_qkt_av_hmx(const uint8_t *Q, const int8_t *K, const int8_t *V,
+                                 int32_t *out, int SQ, int SK, int D);
 int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
                              int M, int N, int K);
 int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uint16_t *out,

@@ -189,7 +189,7 @@ void oracle_gemm_hmx_ex_rows(const uint8_t *A, const int8_t *B, int b_transposed
         }
         for (int j = 0; j < N; j++) {
             const int32_t f = (int32_t)((uint32_t)acc[j] * 17u + 8u) >> 4;
-            int32_t v = sx12(f);
+            int32_t v = store == ORACLE_HMX_STORE_ACC_I32 ? acc[j] : sx12(f);
             const size_t rm = (size_t)i * N + j;
             if (bias) v = wrap_add(v, bias[j]);
             if (res_kind == ORACLE_HMX_RES_I32) v = wrap_add(v, ((const int32_t *)res)[rm]);
@@ -198,7 +198,8 @@ void oracle_gemm_hmx_ex_rows(const uint8_t *A, const int8_t *B, int b_transposed
             if (act == ORACLE_HMX_ACT_LEAKY_SHR3) v = v >= 0 ? v : (v >> 3);
             const size_t o = col_major ? (size_t)j * M + i : rm;
             switch (store) {
-            case ORACLE_HMX_STORE_I32: ((int32_t *)out)[o] = v; break;
+            case ORACLE_HMX_STORE_I32:
+            case ORACLE_HMX_STORE_ACC_I32: ((int32_t *)out)[o] = v; break;
             case ORACLE_HMX_STORE_I8_SAT: ((int8_t *)out)[o] = sat_i8(v); break;
             case ORACLE_HMX_STORE_U8_SAT: ((uint8_t *)out)[o] = sat_u8(v); break;
             case ORACLE_HMX_STORE_I8_LOW: ((int8_t *)out)[o] = (int8_t)(uint8_t)(v & 0xFF); break;
@@ -234,6 +235,25 @@ void oracle_gemm_hmx_rows(const uint8_t *A, const int8_t *B, int b_transposed,
     else
         oracle_gemm_hmx_ex_rows(A, B, b_transposed, out, M, N, K, zpA, ORACLE_HMX_STORE_U8_SAT,
                                 ORACLE_HMX_ACT_RELU, bias, 0, 0, 0, 0, r0, r1);
+}
+
+void oracle_attn_qkt_av_hmx(const uint8_t *Q, const int8_t *K, const int8_t *V, int32_t *out,
+                            int SQ, int SK, int D) {
+    int32_t *sc = (int32_t *)malloc(sizeof(int32_t) * (size_t)(SK > 0 ? SK : 1));
+    for (int i = 0; i < SQ; i++) {
+        for (int j = 0; j < SK; j++) {
+            uint32_t acc = 0;
+            for (int d = 0; d < D; d++)
+                acc += (uint32_t)((int32_t)Q[(size_t)i * D + d] * (int32_t)K[(size_t)j * D + d]);
+            sc[j] = sx12((int32_t)(acc * 17u + 8u) >> 4);
+        }
+        for (int d = 0; d < D; d++) {
+            uint32_t acc = 0;
+            for (int j = 0; j < SK; j++) acc += (uint32_t)(sc[j] * (int32_t)V[(size_t)j * D + d]);
+            out[(size_t)i * D + d] = sx12((int32_t)(acc * 17u + 8u) >> 4);
+        }
+    }
+    free(sc);
 }
 
 /* The elementwise requant family (cited in hexoracle.h).  Products that

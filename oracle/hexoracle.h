@@ -91,7 +91,7 @@ void oracle_gemm_hmx_rows(const uint8_t *A, const int8_t *B, int b_transposed,
 enum {
     ORACLE_HMX_STORE_I32 = 0, ORACLE_HMX_STORE_I8_SAT = 1, ORACLE_HMX_STORE_U8_SAT = 2,
     ORACLE_HMX_STORE_I8_LOW = 3, ORACLE_HMX_STORE_U16_FIELD = 4, ORACLE_HMX_STORE_LUT_I32 = 5,
-    ORACLE_HMX_STORE_LUT_I8 = 6,
+    ORACLE_HMX_STORE_LUT_I8 = 6, ORACLE_HMX_STORE_ACC_I32 = 7,
     ORACLE_HMX_ACT_NONE = 0, ORACLE_HMX_ACT_RELU = 1, ORACLE_HMX_ACT_LEAKY_SHR3 = 2,
     ORACLE_HMX_RES_NONE = 0, ORACLE_HMX_RES_I32 = 1, ORACLE_HMX_RES_I8 = 2,
 };
@@ -99,6 +99,12 @@ void oracle_gemm_hmx_ex_rows(const uint8_t *A, const int8_t *B, int b_transposed
                              void *out, int M, int N, int K, int32_t zpA, int store,
                              int act, const int32_t *bias, int res_kind, const void *res,
                              const void *lut, int col_major, int r0, int r1);
+
+/* kernels/expert/i8_attention_qkt_av_hmx/reference.c: Sc = sx12 field of
+ * Q K^T (Q [SQ][D] u8, K [SK][D] s8), out [SQ][D] = sx12 field of Sc V
+ * (V [SK][D] s8); int accumulation with wrap. */
+void oracle_attn_qkt_av_hmx(const uint8_t *Q, const int8_t *K, const int8_t *V, int32_t *out,
+                            int SQ, int SK, int D);
 
 /* kernels/expert/requant_per_channel/reference.c:2-17 (rows = channels) */
 void oracle_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,

@@ -113,7 +113,7 @@ def gemm_hmx_ex(A, B, store="i32", act="none", bias=None, res=None, lut=None, zp
                 b_transposed=False, col_major=False):
     stores = {"i32": (0, np.int32), "i8_sat": (1, np.int8), "u8_sat": (2, np.uint8),
               "i8_low": (3, np.int8), "u16_field": (4, np.uint16), "lut_i32": (5, np.int32),
-              "lut_i8": (6, np.int8)}
+              "lut_i8": (6, np.int8), "acc_i32": (7, np.int32)}
     A, B = np.ascontiguousarray(A, np.uint8), np.ascontiguousarray(B, np.int8)
     M, K = A.shape
     N = B.shape[0] if b_transposed else B.shape[1]
@@ -164,6 +164,15 @@ def relu_i8(x):
     x = np.ascontiguousarray(x, np.int8)
     out = np.zeros_like(x)
     lib().oracle_relu_i8(_p(x), _p(out), C.c_int64(x.size))
+    return out
+
+
+def attn_qkt_av_hmx(Q, K, V):
+    Q, K, V = (np.ascontiguousarray(Q, np.uint8), np.ascontiguousarray(K, np.int8),
+               np.ascontiguousarray(V, np.int8))
+    (SQ, D), (SK, _) = Q.shape, K.shape
+    out = np.zeros((SQ, D), np.int32)
+    lib().oracle_attn_qkt_av_hmx(_p(Q), _p(K), _p(V), _p(out), SQ, SK, D)
     return out
 
 

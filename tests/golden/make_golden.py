@@ -440,6 +440,36 @@ def gen_requant_family(ref):
     save("requant_family", **arrays)
 
 
+def gen_int8_attention_hmx(ref):
+    # i8_attention_qkt_hmx / _av_hmx at S = 72, D = 40 (off the tile grid),
+    # i8_attention_qkt_av_hmx at S = 32 (its reference keeps Sc in a 32x32
+    # array), D = 72, i8_gqa_qkt_hmx at its fixed shape (2 query heads, 1 KV
+    # head, S = D = 64); full-range u8 / s8 inputs, reference.c outputs.
+    rng = np.random.default_rng(41)
+    u8 = lambda k: rng.integers(0, 256, k, dtype=np.uint8)
+    s8 = lambda k: rng.integers(-128, 128, k, dtype=np.int8)
+    S, D = 72, 40
+    q, k = u8(S * D), s8(S * D)
+    o = np.zeros(S * S, np.uint16)
+    ref.ref_i8_attention_qkt_hmx(ptr(q), ptr(k), ptr(o), S, D)
+    arrays = {"qkt_Q": q, "qkt_K": k, "qkt_out": o, "qkt_SD": np.array([S, D], np.int32)}
+    pm, v = u8(S * S), s8(S * D)
+    o = np.zeros(S * D, np.uint16)
+    ref.ref_i8_attention_av_hmx(ptr(pm), ptr(v), ptr(o), S, D)
+    arrays.update({"av_P": pm, "av_V": v, "av_out": o, "av_SD": np.array([S, D], np.int32)})
+    S, D = 32, 72
+    q, k, v = u8(S * D), s8(S * D), s8(S * D)
+    o = np.zeros(S * D, np.int32)
+    ref.ref_i8_attention_qkt_av_hmx(ptr(q), ptr(k), ptr(v), ptr(o), S, D)
+    arrays.update({"qkav_Q": q, "qkav_K": k, "qkav_V": v, "qkav_out": o,
+                   "qkav_SD": np.array([S, D], np.int32)})
+    q, k = u8(2 * 64 * 64), s8(64 * 64)
+    o = np.zeros(2 * 64 * 64, np.uint16)
+    ref.ref_i8_gqa_qkt_hmx(ptr(q), ptr(k), ptr(o))
+    arrays.update({"gqa_Q": q, "gqa_K": k, "gqa_out": o})
+    save("int8_attention_hmx", **arrays)
+
+
 # ----------------------------------------------------------------- fp16
 
 def gen_hf_q(g, mod, off, step):
@@ -615,6 +645,7 @@ def main():
     gen_hmx(ref)
     gen_hmx_family(ref)
     gen_requant_family(ref)
+    gen_int8_attention_hmx(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

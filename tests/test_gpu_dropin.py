@@ -139,3 +139,22 @@ def test_shim_hmx_family(hx, bundle):
             args.append(p(np.ascontiguousarray(arr[prm])))
     shim(bundle)(*args)
     np.testing.assert_array_equal(out, arr["out"])
+
+
+def test_shim_int8_attention_hmx(hx):
+    from conftest import golden
+    g = golden("int8_attention_hmx")
+    S, D = (int(v) for v in g["qkt_SD"])
+    o16 = np.zeros(S * S, np.uint16)
+    shim("i8_attention_qkt_hmx")(p(g["qkt_Q"]), p(g["qkt_K"]), p(o16), S, D)
+    np.testing.assert_array_equal(o16, g["qkt_out"])
+    o16 = np.zeros(S * D, np.uint16)
+    shim("i8_attention_av_hmx")(p(g["av_P"]), p(g["av_V"]), p(o16), S, D)
+    np.testing.assert_array_equal(o16, g["av_out"])
+    S, D = (int(v) for v in g["qkav_SD"])
+    o32 = np.zeros(S * D, np.int32)
+    shim("i8_attention_qkt_av_hmx")(p(g["qkav_Q"]), p(g["qkav_K"]), p(g["qkav_V"]), p(o32), S, D)
+    np.testing.assert_array_equal(o32, g["qkav_out"])
+    og = np.zeros(2 * 64 * 64, np.uint16)
+    shim("i8_gqa_qkt_hmx")(p(g["gqa_Q"]), p(g["gqa_K"]), p(og))
+    np.testing.assert_array_equal(og, g["gqa_out"])

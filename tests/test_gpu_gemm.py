@@ -209,6 +209,33 @@ def test_hmx_ex_random(hx, oracle, M, N, K):
         np.testing.assert_array_equal(hx.gemm_hmx_ex(A, Bt, b_transposed=True, **kw), exp)
 
 
+def test_int8_attention_hmx_golden(hx):
+    g = golden("int8_attention_hmx")
+    S, D = g["qkt_SD"]
+    np.testing.assert_array_equal(
+        hx.gemm_hmx_ex(g["qkt_Q"].reshape(S, D), g["qkt_K"].reshape(S, D), "u16_field",
+                       b_transposed=True), g["qkt_out"].reshape(S, S))
+    np.testing.assert_array_equal(
+        hx.gemm_hmx_ex(g["av_P"].reshape(S, S), g["av_V"].reshape(S, D), "u16_field"),
+        g["av_out"].reshape(S, D))
+    S, D = g["qkav_SD"]
+    np.testing.assert_array_equal(
+        hx.attn_qkt_av_hmx(g["qkav_Q"].reshape(S, D), g["qkav_K"].reshape(S, D),
+                           g["qkav_V"].reshape(S, D)), g["qkav_out"].reshape(S, D))
+
+
+@pytest.mark.parametrize("SQ,SK,D", [(1, 1, 1), (32, 32, 32), (300, 200, 96), (129, 1000, 64),
+                                     (517, 384, 128)])
+def test_attn_qkt_av_hmx_random(hx, oracle, SQ, SK, D):
+    """The byte-split second product against the oracle's direct int sum,
+    full-range inputs (Sc spans the whole 12-bit field)."""
+    rng = np.random.default_rng(SQ + SK + D)
+    Q = rng.integers(0, 256, (SQ, D), dtype=np.uint8)
+    K = rng.integers(-128, 128, (SK, D), dtype=np.int8)
+    V = rng.integers(-128, 128, (SK, D), dtype=np.int8)
+    np.testing.assert_array_equal(hx.attn_qkt_av_hmx(Q, K, V), oracle.attn_qkt_av_hmx(Q, K, V))
+
+
 # --------------------------------------------------------------- fp16 GEMMs
 
 def assert_f16_gemm_close(got, exp):

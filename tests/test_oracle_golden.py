@@ -235,3 +235,22 @@ def test_epilogue_bias_relu_golden(oracle):
         oracle.epilogue_bias_i32(g["epilogue_bias_i32__acc"], g["epilogue_bias_i32__bias"]),
         g["epilogue_bias_i32__out"])
     np.testing.assert_array_equal(oracle.relu_i8(g["epilogue_relu_i8__x"]), g["epilogue_relu_i8__out"])
+
+
+def test_int8_attention_hmx_golden(oracle):
+    g = golden("int8_attention_hmx")
+    S, D = g["qkt_SD"]
+    np.testing.assert_array_equal(
+        oracle.gemm_hmx_ex(g["qkt_Q"].reshape(S, D), g["qkt_K"].reshape(S, D), "u16_field",
+                           b_transposed=True), g["qkt_out"].reshape(S, S))
+    np.testing.assert_array_equal(
+        oracle.gemm_hmx_ex(g["av_P"].reshape(S, S), g["av_V"].reshape(S, D), "u16_field"),
+        g["av_out"].reshape(S, D))
+    S, D = g["qkav_SD"]
+    np.testing.assert_array_equal(
+        oracle.attn_qkt_av_hmx(g["qkav_Q"].reshape(S, D), g["qkav_K"].reshape(S, D),
+                               g["qkav_V"].reshape(S, D)), g["qkav_out"].reshape(S, D))
+    Q, K = g["gqa_Q"].reshape(2, 64, 64), g["gqa_K"].reshape(64, 64)
+    for hq in range(2):
+        np.testing.assert_array_equal(oracle.gemm_hmx_ex(Q[hq], K, "u16_field", b_transposed=True),
+                                      g["gqa_out"].reshape(2, 64, 64)[hq])

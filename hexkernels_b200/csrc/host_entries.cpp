@@ -542,6 +542,69 @@ HX_EXPORT int hexcuda_host_attn_qkt_av_hmx(const uint8_t *Q, const int8_t *K, co
     });
 }
 
+HX_EXPORT int hexcuda_host_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int8_t *V,
+                                       const uint8_t *exp_lut, const int8_t *cos_lut,
+                                       const int8_t *sin_lut, int rot_shift, void *out, int HQ,
+                                       int HKV, int S, int D, int32_t scale_mult, int scale_shift,
+                                       int32_t av_mult, int av_shift) {
+    if (HQ < 1 || HKV < 1 || HQ % HKV != 0 || S < 0 || D < 0)
+        return fail(HEXCUDA_ERR_ARG, "host_attn_lut_i8: heads %d/%d S %d D %d", HQ, HKV, S, D);
+    if (S == 0 || D == 0) return HEXCUDA_OK;
+    const bool rope = mode == HEXCUDA_ATTN_LUT_HMX_ROPE;
+    const void *cl = rope ? (const void *)cos_lut : (const void *)exp_lut;
+    const void *sl = rope ? (const void *)sin_lut : (const void *)exp_lut;
+    if (int rc = null_check("host_attn_lut_i8", {Q, K, V, exp_lut, out, cl, sl}))
+        return rc;
+    const size_t osize = mode == HEXCUDA_ATTN_LUT_REQUANT ? 1 : 2;
+    const size_t hsd = (size_t)S * D;
+    // one device: the blocks are small (one CTA per query head)
+    return run_sharded(1, out, (size_t)HQ * hsd * osize, [&](Part &p) {
+        const uint8_t *dQ = stage_in(p.d, kSlotIn0, reinterpret_cast<const uint8_t *>(Q), HQ * hsd);
+        const int8_t *dK = stage_in(p.d, kSlotIn1, K, HKV * hsd);
+        const int8_t *dV = stage_in(p.d, kSlotIn2, V, HKV * hsd);
+        const uint8_t *dl = stage_in(p.d, kSlotIn3, exp_lut, 256);
+        const size_t tab = (size_t)S * (D / 2);
+        const int8_t *dc = rope ? stage_in(p.d, kSlotIn4, cos_lut, tab) : nullptr;
+        const int8_t *ds = rope ? stage_in(p.d, kSlotIn5, sin_lut, tab) : nullptr;
+        void *dout = scratch(p.d, kSlotOut, HQ * hsd * osize);
+        if (!dQ || !dK || !dV || !dl || (rope && (!dc || !ds)) || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_attn_lut_i8(p.slot, mode, dQ, dK, dV, dl, dc, ds, rot_shift, dout, HQ, HKV, S, D,
+                                   scale_mult, scale_shift, av_mult, av_shift);
+    });
+}
+
+HX_EXPORT int hexcuda_host_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                                            const int8_t *act_lut, const int8_t *W2,
+                                            const int32_t *b2, const uint8_t *exp_lut, int8_t *out,
+                                            int S, int D, int Dff) {
+    if (S < 0 || D < 0 || Dff < 0) return fail(HEXCUDA_ERR_ARG, "host_decoder_block_i8: bad shape");
+    if (S == 0 || D == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_decoder_block_i8", {X, W1, b1, act_lut, W2, b2, exp_lut, out}))
+        return rc;
+    return run_sharded(1, out, (size_t)S * D, [&](Part &p) {
+        const uint8_t *dX = stage_in(p.d, kSlotIn0, X, (size_t)S * D);
+        const int8_t *dW1 = stage_in(p.d, kSlotIn1, W1, (size_t)D * Dff);
+        const int8_t *dW2 = stage_in(p.d, kSlotIn2, W2, (size_t)Dff * D);
+        const int32_t *db1 = stage_in(p.d, kSlotIn3, b1, (size_t)Dff);
+        const int32_t *db2 = stage_in(p.d, kSlotIn4, b2, (size_t)D);
+        // the two 256-entry tables share one slot
+        uint8_t *tabs = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotIn5, 512));
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)S * D));
+        if (!dX || !dW1 || !dW2 || !db1 || !db2 || !tabs || !dout) return hexcuda_last_error();
+        if (int rc = check(cudaMemcpyAsync(tabs, act_lut, 256, cudaMemcpyHostToDevice, p.d->stream),
+                           "h2d"))
+            return rc;
+        if (int rc = check(cudaMemcpyAsync(tabs + 256, exp_lut, 256, cudaMemcpyHostToDevice,
+                                           p.d->stream),
+                           "h2d"))
+            return rc;
+        p.dout = dout;
+        return hexcuda_decoder_block_i8(p.slot, dX, dW1, db1, reinterpret_cast<const int8_t *>(tabs),
+                                        dW2, db2, tabs + 256, dout, S, D, Dff);
+    });
+}
+
 HX_EXPORT int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
                                        int M, int N, int K) {
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_f16_nt: bad shape");

@@ -194,6 +194,41 @@ def attn_qkt_av_hmx(Q, K, V) -> np.ndarray:
     return out
 
 
+ATTN_LUT = {"requant": 0, "hmx": 1, "hmx_rope": 2}
+
+
+def attn_lut_i8(mode: str, Q, K, V, exp_lut, cos_lut=None, sin_lut=None, rot_shift: int = 0,
+                scale_mult: int = 0, scale_shift: int = 0, av_mult: int = 0,
+                av_shift: int = 0) -> np.ndarray:
+    """int8 attention with the exp-table softmax; Q [HQ, S, D] (int8 for
+    "requant", u8 otherwise), K / V [HKV, S, D] int8."""
+    m = ATTN_LUT[mode]
+    Q = _c(Q, np.int8 if m == 0 else np.uint8)
+    K, V = _c(K, np.int8), _c(V, np.int8)
+    exp_lut = _c(exp_lut, np.uint8)
+    HQ, S, D = Q.shape
+    out = np.empty(Q.shape, np.int8 if m == 0 else np.uint16)
+    cs = _c(cos_lut, np.int8) if cos_lut is not None else None
+    sn = _c(sin_lut, np.int8) if sin_lut is not None else None
+    check(load().hexcuda_host_attn_lut_i8(m, _p(Q), _p(K), _p(V), _p(exp_lut),
+                                          _p(cs) if cs is not None else None,
+                                          _p(sn) if sn is not None else None, rot_shift, _p(out),
+                                          HQ, K.shape[0], S, D, scale_mult, scale_shift, av_mult,
+                                          av_shift))
+    return out
+
+
+def decoder_block_i8(X, W1, b1, act_lut, W2, b2, exp_lut) -> np.ndarray:
+    X, W1, W2 = _c(X, np.uint8), _c(W1, np.int8), _c(W2, np.int8)
+    b1, b2 = _c(b1, np.int32), _c(b2, np.int32)
+    act_lut, exp_lut = _c(act_lut, np.int8), _c(exp_lut, np.uint8)
+    S, D = X.shape
+    out = np.empty((S, D), np.int8)
+    check(load().hexcuda_host_decoder_block_i8(_p(X), _p(W1), _p(b1), _p(act_lut), _p(W2), _p(b2),
+                                               _p(exp_lut), _p(out), S, D, W1.shape[1]))
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp: int) -> np.ndarray:
     a, mult, shift = _c(a, np.int32), _c(mult, np.int32), _c(shift, np.int32)
     R, Cc = a.shape

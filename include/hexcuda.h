@@ -272,6 +272,37 @@ int hexcuda_gemm_hmx_ex(int dev, const uint8_t *A, const int8_t *B, int b_transp
 int hexcuda_attn_qkt_av_hmx(int dev, const uint8_t *Q, const int8_t *K, const int8_t *V,
                             int32_t *out, int SQ, int SK, int D);
 
+/* int8 attention with the corpus's LUT softmax (per score row: m = max;
+ * e_j = exp_lut[max(s_j - m, -255) + 255]; p_j = (e_j * 255 + S / 2) / S,
+ * S = sum e_j; a row whose S is 0 gets p = 0).  Q [HQ][S][D], K / V
+ * [HKV][S][D], query head h uses KV head h / (HQ / HKV); out [HQ][S][D].
+ *   REQUANT   Q int8; s = requant_i8(Q.K, scale_mult, scale_shift); out int8 =
+ *             requant_i8(P.V, av_mult, av_shift) (round half away, no zero
+ *             point).  kernels/expert/gqa_attention/kernel_api.h:40-46.
+ *   HMX       Q u8; s = clamp_i8(sx12(HMX field of Q.K) >> 4); out uint16 = HMX
+ *             field of P.V.  i8_attention_block/kernel_api.h:30,
+ *             i8_gqa_attention_block/kernel_api.h:40.
+ *   HMX_ROPE  HMX after rotating each (d, d + D/2) pair of Q and K by the
+ *             row's int8 cos / sin tables ([S][D/2]) with >> rot_shift
+ *             (clamped to u8 / int8).  i8_rope_attention_block/kernel_api.h:40.
+ * One CTA per query head, all operands in shared memory (HEXCUDA_ERR_ARG when
+ * S and D need more than 200 KB). */
+#define HEXCUDA_ATTN_LUT_REQUANT 0
+#define HEXCUDA_ATTN_LUT_HMX 1
+#define HEXCUDA_ATTN_LUT_HMX_ROPE 2
+int hexcuda_attn_lut_i8(int dev, int mode, const void *Q, const int8_t *K, const int8_t *V,
+                        const uint8_t *exp_lut, const int8_t *cos_lut, const int8_t *sin_lut,
+                        int rot_shift, void *out, int HQ, int HKV, int S, int D,
+                        int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift);
+/* int8 decoder block: causal LUT-softmax self-attention of X [S][D] (u8)
+ * with scores clamp_i8(X.X^T >> 2), h = clamp_u8(X + clamp_i8(P.X >> 8)),
+ * then out int8 = sat_i8(h + sat_i8((act_lut[clamp_i8((h.W1 >> 8) + b1) + 128]
+ * .W2 >> 7) + b2)); W1 [D][Dff], W2 [Dff][D] int8.
+ * kernels/expert/i8_decoder_block/kernel_api.h:53-58. */
+int hexcuda_decoder_block_i8(int dev, const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                             const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
+                             const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff);
+
 /* fp16 GEMM, fp32 accumulate, one fp16 rounding: out[M,N] = A[M,K] . Bt[N,K]^T
  * (B column-major).  kernels/expert/fp16_attention_qkt_hmx/kernel_api.h:4-20. */
 int hexcuda_gemm_f16_nt(int dev, const uint16_t *A, const uint16_t *Bt,
@@ -355,6 +386,14 @@ int hexcuda_host_gemm_hmx_ex(const uint8_t *A, const int8_t *B, int b_transposed
                              int col_major, int M, int N, int K, int32_t zpA);
 int hexcuda_host_attn_qkt_av_hmx(const uint8_t *Q, const int8_t *K, const int8_t *V,
                                  int32_t *out, int SQ, int SK, int D);
+int hexcuda_host_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int8_t *V,
+                             const uint8_t *exp_lut, const int8_t *cos_lut,
+                             const int8_t *sin_lut, int rot_shift, void *out, int HQ,
+                             int HKV, int S, int D, int32_t scale_mult, int scale_shift,
+                             int32_t av_mult, int av_shift);
+int hexcuda_host_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                                  const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
+                                  const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff);
 int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
                              int M, int N, int K);
 int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uint16_t *out,

@@ -256,6 +256,122 @@ void oracle_attn_qkt_av_hmx(const uint8_t *Q, const int8_t *K, const int8_t *V, 
     free(sc);
 }
 
+static int clamp_i8i(int v) { return v > 127 ? 127 : (v < -128 ? -128 : v); }
+static int clamp_u8i(int v) { return v > 255 ? 255 : (v < 0 ? 0 : v); }
+
+/* gqa_attention/reference.c: requant_i8 (round half away, no zero point) */
+static int requant_i8_att(int32_t raw, int32_t mult, int shift) {
+    int64_t v = (int64_t)raw * (int64_t)mult;
+    const int64_t q = rq_round(v, shift);
+    return q > 127 ? 127 : (q < -128 ? -128 : (int)q);
+}
+
+/* the LUT softmax shared by the attention blocks, over the first n entries of
+ * a row (entries n.. are set to 0) */
+static void lut_softmax_row(const int8_t *row, uint8_t *p, int n, int width, const uint8_t *lut) {
+    int m = row[0];
+    for (int j = 1; j < n; j++) if (row[j] > m) m = row[j];
+    int sum = 0;
+    for (int j = 0; j < n; j++) {
+        int diff = row[j] - m;
+        if (diff < -255) diff = -255;
+        p[j] = lut[diff + 255];
+        sum += p[j];
+    }
+    const int half = sum / 2;
+    for (int j = 0; j < n; j++) p[j] = sum > 0 ? (uint8_t)(((int)p[j] * 255 + half) / sum) : 0;
+    for (int j = n; j < width; j++) p[j] = 0;
+}
+
+static int hmx_field_i(int acc) { return ((int)((uint32_t)acc * 17u + 8u) >> 4) & 0xFFF; }
+
+void oracle_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int8_t *V,
+                        const uint8_t *exp_lut, const int8_t *cos_lut, const int8_t *sin_lut,
+                        int rot_shift, void *out, int HQ, int HKV, int S, int D,
+                        int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift) {
+    const int group = HQ / HKV, half_d = D / 2;
+    int8_t *sc = (int8_t *)malloc((size_t)S * S);
+    uint8_t *pr = (uint8_t *)malloc((size_t)S * S);
+    uint8_t *qr = (uint8_t *)malloc((size_t)S * D);
+    int8_t *kr = (int8_t *)malloc((size_t)S * D);
+    for (int hq = 0; hq < HQ; hq++) {
+        const int hkv = hq / group;
+        const uint8_t *Qh = (const uint8_t *)Q + (size_t)hq * S * D;
+        const int8_t *Qs = (const int8_t *)Q + (size_t)hq * S * D;
+        const int8_t *Kh = K + (size_t)hkv * S * D, *Vh = V + (size_t)hkv * S * D;
+        if (mode == 2) {
+            for (int i = 0; i < S; i++)
+                for (int d = 0; d < half_d; d++) {
+                    const int c = cos_lut[i * half_d + d], s = sin_lut[i * half_d + d];
+                    const int q0 = Qh[i * D + d], q1 = Qh[i * D + d + half_d];
+                    qr[i * D + d] = (uint8_t)clamp_u8i((q0 * c - q1 * s) >> rot_shift);
+                    qr[i * D + d + half_d] = (uint8_t)clamp_u8i((q0 * s + q1 * c) >> rot_shift);
+                    const int k0 = Kh[i * D + d], k1 = Kh[i * D + d + half_d];
+                    kr[i * D + d] = (int8_t)clamp_i8i((k0 * c - k1 * s) >> rot_shift);
+                    kr[i * D + d + half_d] = (int8_t)clamp_i8i((k0 * s + k1 * c) >> rot_shift);
+                }
+            Qh = qr;
+            Kh = kr;
+        }
+        for (int i = 0; i < S; i++)
+            for (int j = 0; j < S; j++) {
+                int acc = 0;
+                for (int d = 0; d < D; d++)
+                    acc += (mode == 0 ? (int)Qs[i * D + d] : (int)Qh[i * D + d]) * (int)Kh[j * D + d];
+                sc[i * S + j] = (int8_t)(mode == 0 ? requant_i8_att(acc, scale_mult, scale_shift)
+                                                   : clamp_i8i(sx12(hmx_field_i(acc)) >> 4));
+            }
+        for (int i = 0; i < S; i++) lut_softmax_row(sc + (size_t)i * S, pr + (size_t)i * S, S, S, exp_lut);
+        for (int i = 0; i < S; i++)
+            for (int d = 0; d < D; d++) {
+                int acc = 0;
+                for (int j = 0; j < S; j++) acc += (int)pr[i * S + j] * (int)Vh[j * D + d];
+                const size_t o = (size_t)hq * S * D + (size_t)i * D + d;
+                if (mode == 0)
+                    ((int8_t *)out)[o] = (int8_t)requant_i8_att(acc, av_mult, av_shift);
+                else
+                    ((uint16_t *)out)[o] = (uint16_t)hmx_field_i(acc);
+            }
+    }
+    free(sc); free(pr); free(qr); free(kr);
+}
+
+void oracle_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                             const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
+                             const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff) {
+    int8_t *sc = (int8_t *)calloc((size_t)S * S, 1);
+    uint8_t *pr = (uint8_t *)calloc((size_t)S * S, 1);
+    uint8_t *h = (uint8_t *)malloc((size_t)S * D);
+    int8_t *ha = (int8_t *)malloc((size_t)S * (Dff > 0 ? Dff : 1));
+    for (int i = 0; i < S; i++) {
+        for (int j = 0; j <= i; j++) {
+            int raw = 0;
+            for (int d = 0; d < D; d++) raw += (int)X[i * D + d] * (int)X[j * D + d];
+            sc[i * S + j] = (int8_t)clamp_i8i(raw >> 2);
+        }
+        lut_softmax_row(sc + (size_t)i * S, pr + (size_t)i * S, i + 1, S, exp_lut);
+        for (int d = 0; d < D; d++) {
+            int av = 0;
+            for (int j = 0; j <= i; j++) av += (int)pr[i * S + j] * (int)X[j * D + d];
+            h[i * D + d] = (uint8_t)clamp_u8i((int)X[i * D + d] + clamp_i8i(av >> 8));
+        }
+    }
+    for (int i = 0; i < S; i++)
+        for (int j = 0; j < Dff; j++) {
+            int acc = 0;
+            for (int k = 0; k < D; k++) acc += (int)h[i * D + k] * (int)W1[k * Dff + j];
+            ha[i * Dff + j] = act_lut[clamp_i8i((acc >> 8) + b1[j]) + 128];
+        }
+    for (int i = 0; i < S; i++)
+        for (int j = 0; j < D; j++) {
+            int acc = 0;
+            for (int k = 0; k < Dff; k++) acc += (int)ha[i * Dff + k] * (int)W2[k * D + j];
+            const int fv = clamp_i8i((acc >> 7) + b2[j]);
+            out[i * D + j] = (int8_t)clamp_i8i((int)h[i * D + j] + fv);
+        }
+    free(sc); free(pr); free(h); free(ha);
+}
+
 /* The elementwise requant family (cited in hexoracle.h).  Products that
  * leave int64 are undefined in the references; here they wrap. */
 void oracle_requant_ew(const void *a, int a_i8, const void *b, int b_kind, int64_t n, int pre,

@@ -106,6 +106,21 @@ void oracle_gemm_hmx_ex_rows(const uint8_t *A, const int8_t *B, int b_transposed
 void oracle_attn_qkt_av_hmx(const uint8_t *Q, const int8_t *K, const int8_t *V, int32_t *out,
                             int SQ, int SK, int D);
 
+/* int8 LUT-softmax attention, per query head hq (KV head hq / (HQ / HKV)):
+ *   mode 0  kernels/expert/gqa_attention/reference.c (Q int8, out int8)
+ *   mode 1  i8_attention_block/reference.c, i8_gqa_attention_block/reference.c
+ *           (Q u8, out uint16)
+ *   mode 2  i8_rope_attention_block/reference.c (mode 1 after the rotation)
+ * Q [HQ][S][D], K / V [HKV][S][D], out [HQ][S][D]. */
+void oracle_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int8_t *V,
+                        const uint8_t *exp_lut, const int8_t *cos_lut, const int8_t *sin_lut,
+                        int rot_shift, void *out, int HQ, int HKV, int S, int D,
+                        int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift);
+/* kernels/expert/i8_decoder_block/reference.c */
+void oracle_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                             const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
+                             const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff);
+
 /* kernels/expert/requant_per_channel/reference.c:2-17 (rows = channels) */
 void oracle_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
                                 const int32_t *mult, const int *shift, int8_t zp);

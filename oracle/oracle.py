@@ -176,6 +176,32 @@ def attn_qkt_av_hmx(Q, K, V):
     return out
 
 
+def attn_lut_i8(mode, Q, K, V, exp_lut, cos_lut=None, sin_lut=None, rot_shift=0,
+                scale_mult=0, scale_shift=0, av_mult=0, av_shift=0):
+    """Q [HQ, S, D], K / V [HKV, S, D]; mode 0 requant (int8 out), 1 HMX, 2 HMX + rotation."""
+    Q = np.ascontiguousarray(Q, np.int8 if mode == 0 else np.uint8)
+    K, V = np.ascontiguousarray(K, np.int8), np.ascontiguousarray(V, np.int8)
+    HQ, S, D = Q.shape
+    out = np.zeros(Q.shape, np.int8 if mode == 0 else np.uint16)
+    pp = lambda a: _p(np.ascontiguousarray(a)) if a is not None else None
+    lib().oracle_attn_lut_i8(mode, _p(Q), _p(K), _p(V), pp(np.asarray(exp_lut, np.uint8)),
+                             pp(cos_lut), pp(sin_lut), rot_shift, _p(out), HQ, K.shape[0], S, D,
+                             C.c_int32(scale_mult), scale_shift, C.c_int32(av_mult), av_shift)
+    return out
+
+
+def decoder_block_i8(X, W1, b1, act_lut, W2, b2, exp_lut):
+    X = np.ascontiguousarray(X, np.uint8)
+    W1, W2 = np.ascontiguousarray(W1, np.int8), np.ascontiguousarray(W2, np.int8)
+    b1, b2 = np.ascontiguousarray(b1, np.int32), np.ascontiguousarray(b2, np.int32)
+    act_lut, exp_lut = np.ascontiguousarray(act_lut, np.int8), np.ascontiguousarray(exp_lut, np.uint8)
+    S, D = X.shape
+    out = np.zeros((S, D), np.int8)
+    lib().oracle_decoder_block_i8(_p(X), _p(W1), _p(b1), _p(act_lut), _p(W2), _p(b2), _p(exp_lut),
+                                  _p(out), S, D, W1.shape[1])
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp):
     a = np.ascontiguousarray(a, np.int32)
     R, Cc = a.shape

@@ -470,6 +470,55 @@ def gen_int8_attention_hmx(ref):
     save("int8_attention_hmx", **arrays)
 
 
+def gen_int8_attention_blocks(ref):
+    # gqa_attention (fixed 4 query / 2 KV heads, SEQ 8, D 16), i8_attention_block
+    # (S 48, D 40), i8_gqa_attention_block (fixed 2 / 1 heads, S = D = 64),
+    # i8_rope_attention_block (S 40, D 56), i8_decoder_block (S 24, D 40,
+    # Dff 100), each through its reference.c on seeded inputs; the exp table is
+    # round(255 exp((i - 255) / 24)), the other tables are seeded int8.
+    rng = np.random.default_rng(53)
+    exp_lut = np.round(255 * np.exp((np.arange(256) - 255) / 24.0)).astype(np.uint8)
+    s8 = lambda *sh: rng.integers(-128, 128, sh, dtype=np.int8)
+    u8 = lambda *sh: rng.integers(0, 256, sh, dtype=np.uint8)
+    a = {"exp_lut": exp_lut}
+    q, k, v = s8(4, 8, 16), s8(2, 8, 16), s8(2, 8, 16)
+    o = np.zeros((4, 8, 16), np.int8)
+    ref.ref_gqa_attention(ptr(q), ptr(k), ptr(v), ptr(exp_lut), ptr(o), C.c_int32(1 << 30), 41,
+                          C.c_int32(1 << 30), 41)
+    a.update(gqa_Q=q, gqa_K=k, gqa_V=v, gqa_out=o)
+    S, D = 48, 40
+    q, k, v = u8(S, D), s8(S, D), s8(S, D)
+    o = np.zeros((S, D), np.uint16)
+    ref.ref_i8_attention_block(ptr(q), ptr(k), ptr(v), ptr(o), S, D, ptr(exp_lut))
+    a.update(blk_Q=q, blk_K=k, blk_V=v, blk_out=o)
+    q, k, v = u8(2, 64, 64), s8(1, 64, 64), s8(1, 64, 64)
+    o = np.zeros((2, 64, 64), np.uint16)
+    ref.ref_i8_gqa_attention_block(ptr(q), ptr(k), ptr(v), ptr(o), ptr(exp_lut))
+    a.update(gblk_Q=q, gblk_K=k, gblk_V=v, gblk_out=o)
+    S, D = 40, 56
+    q, k, v = u8(S, D), s8(S, D), s8(S, D)
+    cs = rng.integers(-64, 65, (S, D // 2)).astype(np.int8)
+    sn = rng.integers(-64, 65, (S, D // 2)).astype(np.int8)
+    o = np.zeros((S, D), np.uint16)
+    ref.ref_i8_rope_attention_block(ptr(q), ptr(k), ptr(v), ptr(cs), ptr(sn), ptr(o), S, D, 6,
+                                    ptr(exp_lut))
+    a.update(rope_Q=q, rope_K=k, rope_V=v, rope_cos=cs, rope_sin=sn, rope_out=o)
+    S, D, F = 24, 40, 100
+    x = rng.integers(0, 64, (S, D), dtype=np.uint8)
+    w1, w2 = s8(D, F), s8(F, D)
+    b1 = rng.integers(-200, 200, F).astype(np.int32)
+    b2 = rng.integers(-50, 50, D).astype(np.int32)
+    act = s8(256)
+    o = np.zeros((S, D), np.int8)
+    ref.ref_i8_decoder_block(ptr(x), ptr(w1), ptr(b1), ptr(act), ptr(w2), ptr(b2), ptr(exp_lut),
+                             ptr(o), S, D, F)
+    a.update(dec_X=x, dec_W1=w1, dec_b1=b1, dec_act=act, dec_W2=w2, dec_b2=b2, dec_out=o)
+    for key, val in a.items():
+        if key.endswith("_out"):
+            assert len(np.unique(val)) > 8, key   # not a degenerate case
+    save("int8_attention_blocks", **a)
+
+
 # ----------------------------------------------------------------- fp16
 
 def gen_hf_q(g, mod, off, step):
@@ -646,6 +695,7 @@ def main():
     gen_hmx_family(ref)
     gen_requant_family(ref)
     gen_int8_attention_hmx(ref)
+    gen_int8_attention_blocks(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

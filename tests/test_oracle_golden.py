@@ -254,3 +254,26 @@ def test_int8_attention_hmx_golden(oracle):
     for hq in range(2):
         np.testing.assert_array_equal(oracle.gemm_hmx_ex(Q[hq], K, "u16_field", b_transposed=True),
                                       g["gqa_out"].reshape(2, 64, 64)[hq])
+
+
+def blocks_calls(impl, g):
+    """(result, expected) of the five int8 LUT-attention blocks' golden cases
+    computed through `impl` (the oracle or the GPU ops module)."""
+    lut = g["exp_lut"]
+    yield (impl.attn_lut_i8(0 if impl.__name__.endswith("oracle") else "requant", g["gqa_Q"],
+                            g["gqa_K"], g["gqa_V"], lut, scale_mult=1 << 30, scale_shift=41,
+                            av_mult=1 << 30, av_shift=41), g["gqa_out"])
+    hmx = 1 if impl.__name__.endswith("oracle") else "hmx"
+    rope = 2 if impl.__name__.endswith("oracle") else "hmx_rope"
+    yield (impl.attn_lut_i8(hmx, g["blk_Q"][None], g["blk_K"][None], g["blk_V"][None], lut)[0],
+           g["blk_out"])
+    yield (impl.attn_lut_i8(hmx, g["gblk_Q"], g["gblk_K"], g["gblk_V"], lut), g["gblk_out"])
+    yield (impl.attn_lut_i8(rope, g["rope_Q"][None], g["rope_K"][None], g["rope_V"][None], lut,
+                            g["rope_cos"], g["rope_sin"], 6)[0], g["rope_out"])
+    yield (impl.decoder_block_i8(g["dec_X"], g["dec_W1"], g["dec_b1"], g["dec_act"], g["dec_W2"],
+                                 g["dec_b2"], lut), g["dec_out"])
+
+
+def test_int8_attention_blocks_golden(oracle):
+    for got, exp in blocks_calls(oracle, golden("int8_attention_blocks")):
+        np.testing.assert_array_equal(got, exp)

@@ -50,7 +50,7 @@ constexpr int kStages = 4;
 constexpr int kThreads = 320;      // TMA warp, MMA warp, 8 epilogue warps
 constexpr int kGroupM = 16;
 
-enum EpiKind { kEpiF16 = 0, kEpiRequant = 1, kEpiHmx = 2 };
+enum EpiKind { kEpiF16 = 0, kEpiRequant = 1, kEpiHmx = 2, kEpiF16Ex = 3 };
 
 struct EpiParams {
     void *out;
@@ -77,6 +77,12 @@ struct EpiParams {
     int hmx_store, hmx_act, res_kind, col_major;
     const void *res;
     const void *lut;
+    // fp16 post-ops (kEpiF16Ex), in the corpus's order: v = acc + res[i][j]
+    // (fp16 [M, N] or null) + bias[j] (fp16 or null); preround: v = fp16(v);
+    // activation (HEXCUDA_F16_ACT_*); v *= scale; out = fp16(v)
+    const __half *f16_bias, *f16_res;
+    int f16_act, f16_preround;
+    float f16_scale;
 };
 
 struct GemmArgs {
@@ -134,6 +140,38 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             for (int i = 0; i < 4; i++) dst[i] = v[i];
         } else {
             for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = __float2half_rn(__uint_as_float(r[i]));
+        }
+    } else if constexpr (EPI == kEpiF16Ex) {
+        if (row >= ep.M) return;
+        __half *o = reinterpret_cast<__half *>(ep.out) + (size_t)row * ep.ldo + col0;
+        const __half *rr = ep.f16_res ? ep.f16_res + (size_t)row * ep.N + col0 : nullptr;
+        __half hv[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const int j = col0 + i;
+            float v = __uint_as_float(r[i]);
+            if (j < ep.N) {
+                if (rr) v += __half2float(rr[i]);
+                if (ep.f16_bias) v += __half2float(ep.f16_bias[j]);
+            }
+            if (ep.f16_preround) v = __half2float(__float2half_rn(v));
+            if (ep.f16_act == HEXCUDA_F16_ACT_RELU) {
+                v = v > 0.0f ? v : 0.0f;
+            } else if (ep.f16_act == HEXCUDA_F16_ACT_LEAKY) {
+                v = v > 0.0f ? v : v * 0.125f;
+            } else if (ep.f16_act == HEXCUDA_F16_ACT_GELU) {
+                const float c = 0.7978845608f * (v + 0.044715f * v * v * v);
+                v = 0.5f * v * (1.0f + tanhf(c));
+            }
+            hv[i] = __float2half_rn(v * ep.f16_scale);
+        }
+        if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(hv);
+            uint4 *dst = reinterpret_cast<uint4 *>(o);
+#pragma unroll
+            for (int i = 0; i < 4; i++) dst[i] = src[i];
+        } else {
+            for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = hv[i];
         }
     } else if constexpr (EPI == kEpiHmx) {
         // residual of this row's 32 columns (rows past M are never stored)
@@ -480,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
             for (int c = chalf * (BN / 2); c < (chalf + 1) * (BN / 2); c += 32) {
                 uint32_t r[32];
-                if constexpr (EPI != kEpiF16) {
+                if constexpr (EPI == kEpiRequant || EPI == kEpiHmx) {
                     stage_params(args.epi, cp, nb * BN + c, lane);
                 }
                 __syncwarp();
@@ -900,6 +938,23 @@ HX_EXPORT int hexcuda_gemm_u8s8_pc(int dev, const uint8_t *A, const int8_t *B, c
 // sx12((acc * 17 + 8) >> 4) and, by out_kind, int32 / int8-clamp /
 // u8 bias-ReLU-clamp.  B is row-major [K, N] or, with b_transposed, K-major
 // Bt [N, K] (hmx_matmul_i8_transposeB).
+HX_EXPORT int hexcuda_gemm_f16_ex(int dev, const uint16_t *A, const uint16_t *B, int b_transposed,
+                                  const uint16_t *bias, const uint16_t *res, uint16_t *out, int act,
+                                  int preround, float scale, int M, int N, int K) {
+    if (act < HEXCUDA_F16_ACT_NONE || act > HEXCUDA_F16_ACT_GELU)
+        return fail(HEXCUDA_ERR_ARG, "gemm_f16_ex: activation %d", act);
+    EpiParams ep{};
+    ep.out = out;
+    ep.ldo = N;
+    ep.f16_bias = reinterpret_cast<const __half *>(bias);
+    ep.f16_res = reinterpret_cast<const __half *>(res);
+    ep.f16_act = act;
+    ep.f16_preround = preround ? 1 : 0;
+    ep.f16_scale = scale;
+    return run_gemm<MmaKind::F16, kEpiF16Ex, false, false>(dev, A, K, B, b_transposed != 0, M, N, K,
+                                                           ep, false, "gemm_f16_ex");
+}
+
 HX_EXPORT int hexcuda_gemm_hmx_ex(int dev, const uint8_t *A, const int8_t *B, int b_transposed,
                                   const int32_t *bias, const void *res, int res_kind,
                                   const void *lut, void *out, int store, int act, int col_major,

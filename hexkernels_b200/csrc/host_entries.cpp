@@ -605,6 +605,26 @@ HX_EXPORT int hexcuda_host_decoder_block_i8(const uint8_t *X, const int8_t *W1, 
     });
 }
 
+HX_EXPORT int hexcuda_host_gemm_f16_ex(const uint16_t *A, const uint16_t *B, int b_transposed,
+                                       const uint16_t *bias, const uint16_t *res, uint16_t *out,
+                                       int act, int preround, float scale, int M, int N, int K) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_f16_ex: bad shape");
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_f16_ex", {A, B, out})) return rc;
+    return run_sharded(M, out, (size_t)N * 2, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const uint16_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const uint16_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        const uint16_t *dbias = bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
+        const uint16_t *dres = res ? stage_in(p.d, kSlotIn3, res + p.r0 * N, (size_t)(nr * N)) : nullptr;
+        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, (size_t)(nr * N) * 2));
+        if (!dA || !dB || (bias && !dbias) || (res && !dres) || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_f16_ex(p.slot, dA, dB, b_transposed, dbias, dres, dout, act, preround,
+                                   scale, (int)nr, N, K);
+    });
+}
+
 HX_EXPORT int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
                                        int M, int N, int K) {
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_f16_nt: bad shape");

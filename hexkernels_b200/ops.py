@@ -229,6 +229,26 @@ def decoder_block_i8(X, W1, b1, act_lut, W2, b2, exp_lut) -> np.ndarray:
     return out
 
 
+F16_ACT = {"none": 0, "relu": 1, "leaky": 2, "gelu": 3}
+
+
+def gemm_f16_ex(A, B, act: str = "none", preround: bool = False, scale: float = 1.0, bias=None,
+                res=None, b_transposed: bool = False) -> np.ndarray:
+    """fp16 GEMM with the corpus's fp16 post-ops (residual, bias, rounding,
+    activation, scale); B [K, N] or Bt [N, K]."""
+    A, B = _c(A, np.float16), _c(B, np.float16)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    bias = _c(bias, np.float16) if bias is not None else None
+    res = _c(res, np.float16) if res is not None else None
+    out = np.empty((M, N), np.float16)
+    check(load().hexcuda_host_gemm_f16_ex(_p(A), _p(B), int(b_transposed),
+                                          _p(bias) if bias is not None else None,
+                                          _p(res) if res is not None else None, _p(out),
+                                          F16_ACT[act], int(preround), float(scale), M, N, K))
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp: int) -> np.ndarray:
     a, mult, shift = _c(a, np.int32), _c(mult, np.int32), _c(shift, np.int32)
     R, Cc = a.shape

@@ -307,6 +307,25 @@ int hexcuda_decoder_block_i8(int dev, const uint8_t *X, const int8_t *W1, const 
  * (B column-major).  kernels/expert/fp16_attention_qkt_hmx/kernel_api.h:4-20. */
 int hexcuda_gemm_f16_nt(int dev, const uint16_t *A, const uint16_t *Bt,
                         uint16_t *out, int M, int N, int K);
+/* fp16 GEMM with the corpus's fp16 post-ops, fp32 accumulate:
+ *   v = acc + res[i][j] (fp16 [M,N], may be NULL) + bias[j] (fp16, may be NULL);
+ *   preround: v = (fp16) v; activation; v *= scale; out = (fp16) v.
+ * B row-major [K,N], or Bt [N,K] with b_transposed.  Bundles
+ * (kernels/expert/<name>/kernel_api.h): hmx_matmul_fp16_bias (bias),
+ * hmx_matmul_fp16_relu (RELU), fp16_matmul_leaky_relu_hmx (preround, LEAKY:
+ * v > 0 ? v : v * 0.125), fp16_matmul_gelu_hmx (preround, GELU: 0.5 v (1 +
+ * tanh(0.7978845608 (v + 0.044715 v^3)))), hmx_tile_mac_fp16_32 (res = the
+ * output's previous contents), qkt_tile_fp16 (preround, scale),
+ * hmx_matmul_fp16_32, fp16_matmul_hmx_32x32, fp16_matmul_hmx_deepk,
+ * av_tile_fp16 and hmx_conv1x1_fp16 (plain; the last two with Bt). */
+#define HEXCUDA_F16_ACT_NONE 0
+#define HEXCUDA_F16_ACT_RELU 1
+#define HEXCUDA_F16_ACT_LEAKY 2
+#define HEXCUDA_F16_ACT_GELU 3
+int hexcuda_gemm_f16_ex(int dev, const uint16_t *A, const uint16_t *B, int b_transposed,
+                        const uint16_t *bias, const uint16_t *res, uint16_t *out, int act,
+                        int preround, float scale, int M, int N, int K);
+
 /* Same with row-major B[K,N].  kernels/expert/hmx_matmul_fp16_deepk/
  * kernel_api.h:4-10 and fp16_attention_av_hmx/kernel_api.h. */
 int hexcuda_gemm_f16_nn(int dev, const uint16_t *A, const uint16_t *B,
@@ -394,6 +413,9 @@ int hexcuda_host_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int
 int hexcuda_host_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
                                   const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
                                   const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff);
+int hexcuda_host_gemm_f16_ex(const uint16_t *A, const uint16_t *B, int b_transposed,
+                             const uint16_t *bias, const uint16_t *res, uint16_t *out, int act,
+                             int preround, float scale, int M, int N, int K);
 int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
                              int M, int N, int K);
 int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uint16_t *out,

@@ -372,6 +372,29 @@ void oracle_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *
     free(sc); free(pr); free(h); free(ha);
 }
 
+void oracle_gemm_f16_ex_rows(const uint16_t *A, const uint16_t *B, int b_transposed,
+                             const uint16_t *bias, const uint16_t *res, uint16_t *out, int M,
+                             int N, int K, int act, int preround, float scale, int r0, int r1) {
+    (void)M;
+    for (int i = r0; i < r1; i++)
+        for (int j = 0; j < N; j++) {
+            float acc = res ? h2f(res[(size_t)i * N + j]) : 0.0f;
+            for (int k = 0; k < K; k++)
+                acc += h2f(A[(size_t)i * K + k]) *
+                       h2f(b_transposed ? B[(size_t)j * K + k] : B[(size_t)k * N + j]);
+            float v = acc;
+            if (bias) v = acc + h2f(bias[j]);
+            if (preround) v = h2f(f2h(v));
+            if (act == 1) v = v > 0.0f ? v : 0.0f;
+            if (act == 2) v = v > 0.0f ? v : v * 0.125f;
+            if (act == 3) {
+                const float c = 0.7978845608f * (v + 0.044715f * v * v * v);
+                v = 0.5f * v * (1.0f + tanhf(c));
+            }
+            out[(size_t)i * N + j] = f2h(v * scale);
+        }
+}
+
 /* The elementwise requant family (cited in hexoracle.h).  Products that
  * leave int64 are undefined in the references; here they wrap. */
 void oracle_requant_ew(const void *a, int a_i8, const void *b, int b_kind, int64_t n, int pre,

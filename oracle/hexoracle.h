@@ -166,6 +166,17 @@ void oracle_gemm_f16_nt_rows(const uint16_t *A, const uint16_t *Bt, uint16_t *ou
 void oracle_gemm_f16_nn_rows(const uint16_t *A, const uint16_t *B, uint16_t *out,
                              int M, int N, int K, int r0, int r1);
 
+/* fp16 GEMM with post-ops, fp32 accumulation in k order starting from
+ * res[i][j] (hmx_tile_mac_fp16_32/reference.c) or 0, then + bias[j]
+ * (hmx_matmul_fp16_bias), optional rounding to fp16 (preround), the
+ * activation act (0 none, 1 relu: hmx_matmul_fp16_relu, 2 leaky x0.125:
+ * fp16_matmul_leaky_relu_hmx, 3 tanh gelu: fp16_matmul_gelu_hmx), * scale
+ * (qkt_tile_fp16), one final fp16 rounding.  B [K][N], or Bt [N][K] when
+ * b_transposed (av_tile_fp16, hmx_conv1x1_fp16). */
+void oracle_gemm_f16_ex_rows(const uint16_t *A, const uint16_t *B, int b_transposed,
+                             const uint16_t *bias, const uint16_t *res, uint16_t *out, int M,
+                             int N, int K, int act, int preround, float scale, int r0, int r1);
+
 /* ---- fp16 attention ---- */
 
 /* kernels/expert/fp16_flash_attention_tile/reference.c:9-28 with the scale

@@ -202,6 +202,22 @@ def decoder_block_i8(X, W1, b1, act_lut, W2, b2, exp_lut):
     return out
 
 
+def gemm_f16_ex(A, B, act="none", preround=False, scale=1.0, bias=None, res=None,
+                b_transposed=False):
+    A, B = np.ascontiguousarray(A, np.float16), np.ascontiguousarray(B, np.float16)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    out = np.zeros((M, N), np.float16)
+    pp = lambda a: _p(np.ascontiguousarray(a, np.float16)) if a is not None else None
+    keep = [np.ascontiguousarray(x, np.float16) for x in (bias, res) if x is not None]
+    lib().oracle_gemm_f16_ex_rows(_p(A), _p(B), int(b_transposed),
+                                  _p(keep[0]) if bias is not None else None,
+                                  _p(keep[-1]) if res is not None else None, _p(out), M, N, K,
+                                  {"none": 0, "relu": 1, "leaky": 2, "gelu": 3}[act], int(preround),
+                                  C.c_float(scale), 0, M)
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp):
     a = np.ascontiguousarray(a, np.int32)
     R, Cc = a.shape

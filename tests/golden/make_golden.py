@@ -519,6 +519,51 @@ def gen_int8_attention_blocks(ref):
     save("int8_attention_blocks", **a)
 
 
+def gen_f16_family(ref):
+    # The fp16 post-op GEMM bundles through their reference.c at sizes off the
+    # tile grid, inputs N(0,1)/sqrt(K) in fp16 (outputs of order 1; the GELU
+    # and leaky cases see both signs).
+    rng = np.random.default_rng(61)
+    f16 = lambda *sh, k=1: (rng.standard_normal(sh) / np.sqrt(k)).astype(np.float16)
+    a = {}
+    n, kd = 72, 136
+
+    def run(tag, fn, *args):
+        getattr(ref, "ref_" + fn)(*args)
+
+    for name, k in (("fp16_matmul_gelu_hmx", n), ("fp16_matmul_hmx_32x32", n), ("hmx_matmul_fp16_32", n),
+                    ("hmx_matmul_fp16_relu", n), ("hmx_conv1x1_fp16", n)):
+        A, B = f16(n, n, k=n), f16(n, n)
+        o = np.zeros((n, n), np.float16)
+        run(name, name, ptr(A), ptr(B), ptr(o), n)
+        a.update({f"{name}__A": A, f"{name}__B": B, f"{name}__out": o})
+    for name in ("fp16_matmul_hmx_deepk", "fp16_matmul_leaky_relu_hmx"):
+        A, B = f16(n, kd, k=kd), f16(kd, n)
+        o = np.zeros((n, n), np.float16)
+        run(name, name, ptr(A), ptr(B), ptr(o), n, kd)
+        a.update({f"{name}__A": A, f"{name}__B": B, f"{name}__out": o})
+    A, B, bias = f16(n, n, k=n), f16(n, n), f16(n)
+    o = np.zeros((n, n), np.float16)
+    run("b", "hmx_matmul_fp16_bias", ptr(A), ptr(B), ptr(bias), ptr(o), n)
+    a.update({"hmx_matmul_fp16_bias__A": A, "hmx_matmul_fp16_bias__B": B,
+              "hmx_matmul_fp16_bias__bias": bias, "hmx_matmul_fp16_bias__out": o})
+    A, B, c0 = f16(n, n, k=n), f16(n, n), f16(n, n)
+    o = c0.copy()
+    run("m", "hmx_tile_mac_fp16_32", ptr(A), ptr(B), ptr(o), n)
+    a.update({"hmx_tile_mac_fp16_32__A": A, "hmx_tile_mac_fp16_32__B": B,
+              "hmx_tile_mac_fp16_32__C": c0, "hmx_tile_mac_fp16_32__out": o})
+    M, N, D = 60, 100, 40
+    Q, K = f16(M, D, k=D), f16(D, N)
+    o = np.zeros((M, N), np.float16)
+    ref.ref_qkt_tile_fp16(ptr(Q), ptr(K), ptr(o), M, N, D, C.c_uint16(np.float16(0.125).view(np.uint16)))
+    a.update({"qkt_tile_fp16__Q": Q, "qkt_tile_fp16__K": K, "qkt_tile_fp16__out": o})
+    Am, V = f16(M, N, k=N), f16(D, N)
+    o = np.zeros((M, D), np.float16)
+    ref.ref_av_tile_fp16(ptr(Am), ptr(V), ptr(o), M, N, D)
+    a.update({"av_tile_fp16__A": Am, "av_tile_fp16__V": V, "av_tile_fp16__out": o})
+    save("f16_family", **a)
+
+
 # ----------------------------------------------------------------- fp16
 
 def gen_hf_q(g, mod, off, step):
@@ -696,6 +741,7 @@ def main():
     gen_requant_family(ref)
     gen_int8_attention_hmx(ref)
     gen_int8_attention_blocks(ref)
+    gen_f16_family(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

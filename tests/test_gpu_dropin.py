@@ -158,3 +158,34 @@ def test_shim_int8_attention_hmx(hx):
     og = np.zeros(2 * 64 * 64, np.uint16)
     shim("i8_gqa_qkt_hmx")(p(g["gqa_Q"]), p(g["gqa_K"]), p(og))
     np.testing.assert_array_equal(og, g["gqa_out"])
+
+
+def test_shim_f16_family(hx):
+    """The fp16 post-op shims through candidate_kernel on their golden cases
+    (fp16 GEMM tolerance; hmx_tile_mac accumulates into its output)."""
+    from conftest import golden
+    from test_gpu_gemm import assert_f16_gemm_close
+    g = golden("f16_family")
+    arr = lambda b, k: np.ascontiguousarray(g[f"{b}__{k}"])
+    for b in ("fp16_matmul_gelu_hmx", "fp16_matmul_hmx_32x32", "hmx_matmul_fp16_32",
+              "hmx_matmul_fp16_relu", "hmx_conv1x1_fp16"):
+        o = np.zeros_like(arr(b, "out"))
+        shim(b)(p(arr(b, "A")), p(arr(b, "B")), p(o), o.shape[0])
+        assert_f16_gemm_close(o, arr(b, "out"))
+    for b in ("fp16_matmul_hmx_deepk", "fp16_matmul_leaky_relu_hmx"):
+        o = np.zeros_like(arr(b, "out"))
+        shim(b)(p(arr(b, "A")), p(arr(b, "B")), p(o), o.shape[0], arr(b, "A").shape[1])
+        assert_f16_gemm_close(o, arr(b, "out"))
+    b = "hmx_matmul_fp16_bias"
+    o = np.zeros_like(arr(b, "out"))
+    shim(b)(p(arr(b, "A")), p(arr(b, "B")), p(arr(b, "bias")), p(o), o.shape[0])
+    assert_f16_gemm_close(o, arr(b, "out"))
+    b = "hmx_tile_mac_fp16_32"
+    o = arr(b, "C").copy()
+    shim(b)(p(arr(b, "A")), p(arr(b, "B")), p(o), o.shape[0])
+    assert_f16_gemm_close(o, arr(b, "out"))
+    b = "av_tile_fp16"
+    (M, N), D = arr(b, "A").shape, arr(b, "V").shape[0]
+    o = np.zeros_like(arr(b, "out"))
+    shim(b)(p(arr(b, "A")), p(arr(b, "V")), p(o), M, N, D)
+    assert_f16_gemm_close(o, arr(b, "out"))

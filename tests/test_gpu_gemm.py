@@ -317,3 +317,30 @@ def test_f16_benchmark_shape(hx, oracle):
     got = hx.gemm_f16_nt(A, Bt)
     rows = np.sort(rng.choice(M, 24, replace=False))
     assert_f16_gemm_close(got[rows], oracle.gemm_f16_nt(A[rows], Bt))
+
+
+from f16_family import F16_BUNDLES, f16_case  # noqa: E402
+
+
+@pytest.mark.parametrize("bundle", sorted(F16_BUNDLES))
+def test_f16_family_golden(hx, bundle):
+    A, B, out, kw = f16_case(golden("f16_family"), bundle)
+    assert_f16_gemm_close(hx.gemm_f16_ex(A, B, **kw), out)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (130, 257, 200), (512, 384, 1024), (300, 72, 4096)])
+def test_f16_ex_random(hx, oracle, M, N, K):
+    """Every post-op against the oracle: residual, bias, relu, leaky and GELU
+    on the fp16-rounded sum, scaling; B row-major and transposed."""
+    rng = np.random.default_rng(M + 7 * N + K)
+    A = (rng.standard_normal((M, K)) / np.sqrt(K)).astype(np.float16)
+    B = rng.standard_normal((K, N)).astype(np.float16)
+    Bt = np.ascontiguousarray(B.T)
+    bias = rng.standard_normal(N).astype(np.float16)
+    res = rng.standard_normal((M, N)).astype(np.float16)
+    for kw in (dict(act="gelu", preround=True), dict(act="leaky", preround=True, bias=bias),
+               dict(act="relu", res=res), dict(preround=True, scale=0.0883883476),
+               dict(res=res, bias=bias, act="none")):
+        exp = oracle.gemm_f16_ex(A, B, **kw)
+        assert_f16_gemm_close(hx.gemm_f16_ex(A, B, **kw), exp)
+        assert_f16_gemm_close(hx.gemm_f16_ex(A, Bt, b_transposed=True, **kw), exp)

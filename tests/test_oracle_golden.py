@@ -277,3 +277,14 @@ def blocks_calls(impl, g):
 def test_int8_attention_blocks_golden(oracle):
     for got, exp in blocks_calls(oracle, golden("int8_attention_blocks")):
         np.testing.assert_array_equal(got, exp)
+
+
+from f16_family import F16_BUNDLES, f16_case  # noqa: E402
+
+
+@pytest.mark.parametrize("bundle", sorted(F16_BUNDLES))
+def test_f16_family_golden(oracle, bundle):
+    """The oracle's fp16 post-op GEMM reproduces each bundle's reference.c
+    (same fp32 accumulation order, same libm tanh) bit for bit."""
+    A, B, out, kw = f16_case(golden("f16_family"), bundle)
+    np.testing.assert_array_equal(oracle.gemm_f16_ex(A, B, **kw).view(np.uint16), out.view(np.uint16))

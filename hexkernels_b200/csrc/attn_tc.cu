@@ -34,6 +34,9 @@
 #include <cuda_fp16.h>
 #include <math.h>
 
+#include <queue>
+#include <vector>
+
 #include "hx_internal.h"
 #include "tc_common.cuh"
 
@@ -75,6 +78,8 @@ struct AttnArgs {
     int causal;
     __half *O;
     int *err_word;
+    // ping-pong kernel: CTA c runs items sched[sched_off[c] .. sched_off[c+1])
+    const int *sched, *sched_off;
 };
 
 // Items are walked in groups of kHeadGroup heads: inside a group the last
@@ -668,7 +673,9 @@ __global__ void __launch_bounds__(384, 1)
             int item = 0;
             uint32_t armed_q = 0, armed_k = 0, armed_v = 0;
             uint32_t armed_k_ph[2] = {0, 0}, armed_v_ph[2] = {0, 0};
-            for (int w = blockIdx.x; w < args.nitems && !*abort_flag; w += gridDim.x, item++) {
+            for (int k = args.sched_off[blockIdx.x];
+                 k < args.sched_off[blockIdx.x + 1] && !*abort_flag; k++, item++) {
+                const int w = args.sched[k];
                 int h, qp, nkv_a, nkv_b;
                 pp_item(w, args, h, qp, nkv_a, nkv_b);
                 if (!tc::mbar_wait(q_empty, (item & 1) ^ 1, abort_flag, args.err_word, kErrWaitEmpty))
@@ -743,7 +750,9 @@ __global__ void __launch_bounds__(384, 1)
                                    tc::sdesc_mnmajor_sw128(vb + k * 2048, kSub, 1024), idesc_pv,
                                    (!first || k > 0) ? 1u : 0u);
             };
-            for (int w = blockIdx.x; w < args.nitems && ok && !*abort_flag; w += gridDim.x, item++) {
+            for (int k = args.sched_off[blockIdx.x];
+                 k < args.sched_off[blockIdx.x + 1] && ok && !*abort_flag; k++, item++) {
+                const int w = args.sched[k];
                 int h, qp, nkv_a, nkv_b;
                 pp_item(w, args, h, qp, nkv_a, nkv_b);
                 const int nkv[2] = {nkv_a, nkv_b};
@@ -813,8 +822,9 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t o_addr = tmem_base + lane_base + 256 + x * 128;
         uint32_t n = 0;
         int item = 0;
-        for (int w = blockIdx.x; w < args.nitems; w += gridDim.x, item++) {
+        for (int k = args.sched_off[blockIdx.x]; k < args.sched_off[blockIdx.x + 1]; k++, item++) {
             if (__any_sync(0xffffffffu, *abort_flag)) break;
+            const int w = args.sched[k];
             int h, qp, nkv_a, nkv_b;
             pp_item(w, args, h, qp, nkv_a, nkv_b);
             const int nkv = x == 0 ? nkv_a : nkv_b;
@@ -1050,6 +1060,62 @@ int launch_attn_tc(Dev *d, const __half *Q, const __half *K, const __half *V, __
 
 }  // namespace
 
+// Item lists of the ping-pong kernel's CTAs: greedy list scheduling in the
+// head-group order (each item, in that order, goes to the CTA with the least
+// work so far; an item costs its key tiles plus two for its set-up and
+// epilogue).  Items keep their group order inside every CTA's list, so the
+// heads in flight stay few (K / V reuse from L2), and the CTAs finish within
+// about one item of each other instead of the several that a fixed stride
+// leaves for the causal triangle.  Built on the host once per shape and kept
+// on the device: [grid + 1 offsets][nitems item ids].
+constexpr int kSlotSched = 15;
+
+const int *pp_schedule(Dev *d, const AttnArgs &a, int grid) {
+    struct Cache {
+        int bh = -1, sq = -1, sk = -1, causal = -1, grid = -1;
+        const int *ptr = nullptr;
+    };
+    static Cache cache[64];
+    Cache &c = cache[d->ordinal & 63];
+    const size_t bytes = sizeof(int) * (size_t)(grid + 1 + a.nitems);
+    int *dev = reinterpret_cast<int *>(scratch(d, kSlotSched, bytes));
+    if (!dev) return nullptr;
+    if (c.ptr == dev && c.bh == a.BH && c.sq == a.SQ && c.sk == a.SK && c.causal == a.causal &&
+        c.grid == grid)
+        return dev;
+    std::vector<std::vector<int>> lists((size_t)grid);
+    typedef std::pair<long long, int> Load;
+    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+    for (int i = 0; i < grid; i++) heap.push(Load(0, i));
+    const int nk_all = (a.SK + kTK - 1) / kTK;
+    for (int w = 0; w < a.nitems; w++) {
+        // the item's key-tile count, as pp_item computes it on the device
+        const int per_group = kHeadGroup * a.nq, group = w / per_group;
+        const int gs = std::min(kHeadGroup, a.BH - group * kHeadGroup);
+        const int qp = a.nq - 1 - (w - group * per_group) / gs;
+        const int nkv = a.causal ? std::min(a.SK - 1, qp * kPairQ + 2 * kTQ - 1) / kTK + 1 : nk_all;
+        Load l = heap.top();
+        heap.pop();
+        lists[(size_t)l.second].push_back(w);
+        heap.push(Load(l.first + nkv + 2, l.second));
+    }
+    std::vector<int> host;
+    host.reserve((size_t)grid + 1 + (size_t)a.nitems);
+    int off = 0;
+    for (int i = 0; i < grid; i++) {
+        host.push_back(off);
+        off += (int)lists[(size_t)i].size();
+    }
+    host.push_back(off);
+    for (auto &l : lists) host.insert(host.end(), l.begin(), l.end());
+    // (from pageable memory: the call returns once `host` has been staged)
+    if (check(cudaMemcpyAsync(dev, host.data(), bytes, cudaMemcpyHostToDevice, d->stream),
+              "h2d attention schedule"))
+        return nullptr;
+    c = Cache{a.BH, a.SQ, a.SK, a.causal, grid, dev};
+    return dev;
+}
+
 int launch_attn_pp(Dev *d, const __half *Q, const __half *K, const __half *V, __half *O, int BH,
                    int SQ, int SK, float scale, int causal) {
     using L = PPSmem;
@@ -1085,6 +1151,10 @@ int launch_attn_pp(Dev *d, const __half *Q, const __half *K, const __half *V, __
     a.O = O;
     a.err_word = d->err_word;
     const int grid = a.nitems < d->sms ? a.nitems : d->sms;
+    const int *sched = pp_schedule(d, a, grid);
+    if (!sched) return hexcuda_last_error();
+    a.sched_off = sched;
+    a.sched = sched + grid + 1;
     attn_pp_kernel<<<grid, 384, L::kTotal, d->stream>>>(mq, mk, mv, a);
     return HEXCUDA_OK;
 }

@@ -69,6 +69,7 @@ struct EpiParams {
     int shift;
     int zp;
     int lo, hi;
+    int relu_pre;              // requant: x = max(x, 0) after the bias add
     // HMX-convention epilogue (kEpiHmx): acc32 as above, then
     //   v = sx12((acc32 * 17 + 8) >> 4)    (int32 wrap, arithmetic shift)
     //   v += bias[j] (null: 0); v += res[i][j] (res_kind 1 int32, 2 int8,
@@ -302,7 +303,9 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
                 // acc32 = rawdot - zpA * colsum[j] with int32 wrap, then the
                 // int64 bias add, multiply and round-half-away shift
                 const int32_t a32 = (int32_t)(r[4 * i4 + u] - (uint32_t)cc[u]);
-                const int64_t v = ((int64_t)a32 + bb[u]) * (int64_t)mm[u];
+                int64_t xb = (int64_t)a32 + bb[u];
+                if (ep.relu_pre && xb < 0) xb = 0;
+                const int64_t v = xb * (int64_t)mm[u];
                 const int sh = ss[u];
                 const uint64_t half = sh > 0 ? (1ull << (sh - 1)) : 0ull;
                 const uint64_t av = v < 0 ? (uint64_t)(-v) : (uint64_t)v;
@@ -953,6 +956,30 @@ HX_EXPORT int hexcuda_gemm_f16_ex(int dev, const uint16_t *A, const uint16_t *B,
     ep.f16_scale = scale;
     return run_gemm<MmaKind::F16, kEpiF16Ex, false, false>(dev, A, K, B, b_transposed != 0, M, N, K,
                                                            ep, false, "gemm_f16_ex");
+}
+
+HX_EXPORT int hexcuda_gemm_i8_rq_ex(int dev, const int8_t *A, const int8_t *B, int b_transposed,
+                                    const int32_t *bias, int8_t *out, int M, int N, int K,
+                                    int32_t mult, int shift, int8_t zp, int relu) {
+    if (shift < 0 || shift > 63) return fail(HEXCUDA_ERR_ARG, "gemm_i8_rq_ex: shift %d", shift);
+    EpiParams ep = requant_epi(out, N, mult, shift, zp, -128, 127);
+    ep.bias = bias;
+    ep.relu_pre = relu ? 1 : 0;
+    return run_gemm<MmaKind::I8, kEpiRequant, true, true>(dev, A, K, B, b_transposed != 0, M, N, K,
+                                                          ep, false, "gemm_i8_rq_ex");
+}
+
+HX_EXPORT int hexcuda_gemm_hmx_s8u8(int dev, const int8_t *A, const uint8_t *B, void *out, int store,
+                                    int M, int N, int K) {
+    if (store < HEXCUDA_HMX_STORE_I32 || store > HEXCUDA_HMX_STORE_ACC_I32 ||
+        store == HEXCUDA_HMX_STORE_LUT_I32 || store == HEXCUDA_HMX_STORE_LUT_I8)
+        return fail(HEXCUDA_ERR_ARG, "gemm_hmx_s8u8: store kind %d", store);
+    EpiParams ep{};
+    ep.out = out;
+    ep.ldo = N;
+    ep.hmx_store = store;
+    return run_gemm<MmaKind::I8, kEpiHmx, true, false>(dev, A, K, B, false, M, N, K, ep, false,
+                                                       "gemm_hmx_s8u8");
 }
 
 HX_EXPORT int hexcuda_gemm_hmx_ex(int dev, const uint8_t *A, const int8_t *B, int b_transposed,

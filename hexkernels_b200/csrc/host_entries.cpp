@@ -625,6 +625,43 @@ HX_EXPORT int hexcuda_host_gemm_f16_ex(const uint16_t *A, const uint16_t *B, int
     });
 }
 
+HX_EXPORT int hexcuda_host_gemm_i8_rq_ex(const int8_t *A, const int8_t *B, int b_transposed,
+                                         const int32_t *bias, int8_t *out, int M, int N, int K,
+                                         int32_t mult, int shift, int8_t zp, int relu) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_i8_rq_ex: bad shape");
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_i8_rq_ex", {A, B, out})) return rc;
+    return run_sharded(M, out, (size_t)N, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        const int32_t *db = bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * N)));
+        if (!dA || !dB || (bias && !db) || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_i8_rq_ex(p.slot, dA, dB, b_transposed, db, dout, (int)nr, N, K, mult,
+                                     shift, zp, relu);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gemm_hmx_s8u8(const int8_t *A, const uint8_t *B, void *out, int store,
+                                         int M, int N, int K) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_hmx_s8u8: bad shape");
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_hmx_s8u8", {A, B, out})) return rc;
+    const size_t osize = store == HEXCUDA_HMX_STORE_U16_FIELD ? 2
+                         : (store == HEXCUDA_HMX_STORE_I32 || store == HEXCUDA_HMX_STORE_ACC_I32) ? 4 : 1;
+    return run_sharded(M, out, (size_t)N * osize, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const uint8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        void *dout = scratch(p.d, kSlotOut, (size_t)(nr * N) * osize);
+        if (!dA || !dB || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_hmx_s8u8(p.slot, dA, dB, dout, store, (int)nr, N, K);
+    });
+}
+
 HX_EXPORT int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
                                        int M, int N, int K) {
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_f16_nt: bad shape");

@@ -249,6 +249,30 @@ def gemm_f16_ex(A, B, act: str = "none", preround: bool = False, scale: float = 
     return out
 
 
+def gemm_i8_rq_ex(A, B, mult: int, shift: int, zp: int, bias=None, relu: bool = False,
+                  b_transposed: bool = False) -> np.ndarray:
+    """s8 x s8 GEMM + requant, optional bias and ReLU before the requant."""
+    A, B = _c(A, np.int8), _c(B, np.int8)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    bias = _c(bias, np.int32) if bias is not None else None
+    out = np.empty((M, N), np.int8)
+    check(load().hexcuda_host_gemm_i8_rq_ex(_p(A), _p(B), int(b_transposed),
+                                            _p(bias) if bias is not None else None, _p(out), M, N,
+                                            K, mult, shift, zp, int(relu)))
+    return out
+
+
+def gemm_hmx_s8u8(A, B, store: str = "i32") -> np.ndarray:
+    """HMX-field GEMM with s8 A [M, K] and u8 B [K, N]."""
+    A, B = _c(A, np.int8), _c(B, np.uint8)
+    kind, dt = {"i32": (0, np.int32), "u16_field": (4, np.uint16), "acc_i32": (7, np.int32)}[store]
+    M, K = A.shape
+    out = np.empty((M, B.shape[1]), dt)
+    check(load().hexcuda_host_gemm_hmx_s8u8(_p(A), _p(B), _p(out), kind, M, B.shape[1], K))
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp: int) -> np.ndarray:
     a, mult, shift = _c(a, np.int32), _c(mult, np.int32), _c(shift, np.int32)
     R, Cc = a.shape

@@ -303,6 +303,21 @@ int hexcuda_decoder_block_i8(int dev, const uint8_t *X, const int8_t *W1, const 
                              const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
                              const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff);
 
+/* s8 x s8 GEMM + fixed-point requant with an optional bias (NULL: none) and an
+ * optional ReLU between the bias add and the requant; B row-major [K,N] or
+ * Bt [N,K].  kernels/expert/gemm_bias_relu_requant/kernel_api.h:14; with
+ * A = x [1,K] and Bt = the matrix [M,K] it is the matrix-vector form of
+ * i8_linear_relu_requant/kernel_api.h:18 and i8_matvec_bias_requant/kernel_api.h:15. */
+int hexcuda_gemm_i8_rq_ex(int dev, const int8_t *A, const int8_t *B, int b_transposed,
+                          const int32_t *bias, int8_t *out, int M, int N, int K, int32_t mult,
+                          int shift, int8_t zp, int relu);
+/* HMX-convention GEMM with s8 A [M,K] and u8 B [K,N] (the weights-by-
+ * activations form of the 1x1 convolutions, i8_conv2d_1x1_hmx/kernel_api.h:17,
+ * i8_pointwise_conv_hmx/kernel_api.h:16); store kinds as hexcuda_gemm_hmx_ex
+ * without the tables. */
+int hexcuda_gemm_hmx_s8u8(int dev, const int8_t *A, const uint8_t *B, void *out, int store,
+                          int M, int N, int K);
+
 /* fp16 GEMM, fp32 accumulate, one fp16 rounding: out[M,N] = A[M,K] . Bt[N,K]^T
  * (B column-major).  kernels/expert/fp16_attention_qkt_hmx/kernel_api.h:4-20. */
 int hexcuda_gemm_f16_nt(int dev, const uint16_t *A, const uint16_t *Bt,
@@ -416,6 +431,11 @@ int hexcuda_host_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int3
 int hexcuda_host_gemm_f16_ex(const uint16_t *A, const uint16_t *B, int b_transposed,
                              const uint16_t *bias, const uint16_t *res, uint16_t *out, int act,
                              int preround, float scale, int M, int N, int K);
+int hexcuda_host_gemm_i8_rq_ex(const int8_t *A, const int8_t *B, int b_transposed,
+                               const int32_t *bias, int8_t *out, int M, int N, int K,
+                               int32_t mult, int shift, int8_t zp, int relu);
+int hexcuda_host_gemm_hmx_s8u8(const int8_t *A, const uint8_t *B, void *out, int store, int M,
+                               int N, int K);
 int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,
                              int M, int N, int K);
 int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uint16_t *out,

@@ -395,6 +395,41 @@ void oracle_gemm_f16_ex_rows(const uint16_t *A, const uint16_t *B, int b_transpo
         }
 }
 
+void oracle_gemm_i8_rq_ex_rows(const int8_t *A, const int8_t *B, int b_transposed,
+                               const int32_t *bias, int8_t *out, int M, int N, int K,
+                               int32_t mult, int shift, int zp, int relu, int r0, int r1) {
+    (void)M;
+    for (int i = r0; i < r1; i++)
+        for (int j = 0; j < N; j++) {
+            uint32_t acc = 0;
+            for (int k = 0; k < K; k++)
+                acc += (uint32_t)((int32_t)A[(size_t)i * K + k] *
+                                  (int32_t)(b_transposed ? B[(size_t)j * K + k] : B[(size_t)k * N + j]));
+            int64_t x = (int64_t)(int32_t)acc + (bias ? (int64_t)bias[j] : 0);
+            if (relu && x < 0) x = 0;
+            out[(size_t)i * N + j] = sat_i8(rq_round(x * (int64_t)mult, shift) + zp);
+        }
+}
+
+void oracle_gemm_hmx_s8u8_rows(const int8_t *A, const uint8_t *B, void *out, int store, int M,
+                               int N, int K, int r0, int r1) {
+    (void)M;
+    for (int i = r0; i < r1; i++)
+        for (int j = 0; j < N; j++) {
+            uint32_t acc = 0;
+            for (int k = 0; k < K; k++)
+                acc += (uint32_t)((int32_t)A[(size_t)i * K + k] * (int32_t)B[(size_t)k * N + j]);
+            const int32_t f = (int32_t)(acc * 17u + 8u) >> 4;
+            const size_t o = (size_t)i * N + j;
+            if (store == ORACLE_HMX_STORE_U16_FIELD)
+                ((uint16_t *)out)[o] = (uint16_t)(f & 0xFFF);
+            else if (store == ORACLE_HMX_STORE_ACC_I32)
+                ((int32_t *)out)[o] = (int32_t)acc;
+            else
+                ((int32_t *)out)[o] = sx12(f);
+        }
+}
+
 /* The elementwise requant family (cited in hexoracle.h).  Products that
  * leave int64 are undefined in the references; here they wrap. */
 void oracle_requant_ew(const void *a, int a_i8, const void *b, int b_kind, int64_t n, int pre,

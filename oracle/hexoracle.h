@@ -121,6 +121,18 @@ void oracle_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *
                              const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
                              const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff);
 
+/* s8 x s8 GEMM + requant with optional bias and a ReLU between bias add and
+ * requant (kernels/expert/gemm_bias_relu_requant/reference.c; the matrix-
+ * vector i8_linear_relu_requant / i8_matvec_bias_requant as A = x, Bt = matrix). */
+void oracle_gemm_i8_rq_ex_rows(const int8_t *A, const int8_t *B, int b_transposed,
+                               const int32_t *bias, int8_t *out, int M, int N, int K,
+                               int32_t mult, int shift, int zp, int relu, int r0, int r1);
+/* s8 A x u8 B HMX-field GEMM (i8_conv2d_1x1_hmx/reference.c,
+ * i8_pointwise_conv_hmx/reference.c): store ORACLE_HMX_STORE_I32 (sx12),
+ * _U16_FIELD or _ACC_I32. */
+void oracle_gemm_hmx_s8u8_rows(const int8_t *A, const uint8_t *B, void *out, int store, int M,
+                               int N, int K, int r0, int r1);
+
 /* kernels/expert/requant_per_channel/reference.c:2-17 (rows = channels) */
 void oracle_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
                                 const int32_t *mult, const int *shift, int8_t zp);

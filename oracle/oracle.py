@@ -218,6 +218,28 @@ def gemm_f16_ex(A, B, act="none", preround=False, scale=1.0, bias=None, res=None
     return out
 
 
+def gemm_i8_rq_ex(A, B, mult, shift, zp, bias=None, relu=False, b_transposed=False):
+    A, B = np.ascontiguousarray(A, np.int8), np.ascontiguousarray(B, np.int8)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    out = np.zeros((M, N), np.int8)
+    bias = np.ascontiguousarray(bias, np.int32) if bias is not None else None
+    lib().oracle_gemm_i8_rq_ex_rows(_p(A), _p(B), int(b_transposed),
+                                    _p(bias) if bias is not None else None, _p(out), M, N, K,
+                                    C.c_int32(mult), shift, zp, int(relu), 0, M)
+    return out
+
+
+def gemm_hmx_s8u8(A, B, store="i32"):
+    A, B = np.ascontiguousarray(A, np.int8), np.ascontiguousarray(B, np.uint8)
+    M, K = A.shape
+    N = B.shape[1]
+    kind, dt = {"i32": (0, np.int32), "u16_field": (4, np.uint16), "acc_i32": (7, np.int32)}[store]
+    out = np.zeros((M, N), dt)
+    lib().oracle_gemm_hmx_s8u8_rows(_p(A), _p(B), _p(out), kind, M, N, K, 0, M)
+    return out
+
+
 def requant_per_channel(a, mult, shift, zp):
     a = np.ascontiguousarray(a, np.int32)
     R, Cc = a.shape

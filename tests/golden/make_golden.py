@@ -564,6 +564,52 @@ def gen_f16_family(ref):
     save("f16_family", **a)
 
 
+def gen_i8_callers(ref):
+    # Callers of the int8 GEMM + requant and HMX paths through their
+    # reference.c: gemm_bias_relu_requant (70 x 90 x 150), i8_linear_relu_requant
+    # and i8_matvec_bias_requant (300 x 520), hmx_conv1x1_i8 (n 72),
+    # i8_gemm_tiled_bias_relu_requant (60 x 100 x 130), i8_conv2d_1x1_hmx and
+    # i8_pointwise_conv_hmx (their fixed shapes); full-range operands.
+    rng = np.random.default_rng(71)
+    s8 = lambda *sh: rng.integers(-128, 128, sh, dtype=np.int8)
+    u8 = lambda *sh: rng.integers(0, 256, sh, dtype=np.uint8)
+    a = {}
+    M, N, K = 70, 90, 150
+    A, B = s8(M, K), s8(K, N)
+    bias = rng.integers(-40000, 40000, N).astype(np.int32)
+    o = np.zeros((M, N), np.int8)
+    ref.ref_gemm_bias_relu_requant(ptr(A), ptr(B), ptr(bias), ptr(o), M, N, K, C.c_int32(1 << 30), 38,
+                                   C.c_int8(3))
+    a.update(gbr_A=A, gbr_B=B, gbr_bias=bias, gbr_out=o)
+    M, K = 300, 520
+    A, x = s8(M, K), s8(K)
+    bias = rng.integers(-40000, 40000, M).astype(np.int32)
+    for name in ("i8_linear_relu_requant", "i8_matvec_bias_requant"):
+        o = np.zeros(M, np.int8)
+        getattr(ref, "ref_" + name)(ptr(A), ptr(x), ptr(bias), ptr(o), M, K, C.c_int32(1 << 30), 38,
+                                    C.c_int8(-2))
+        a[name + "_out"] = o
+    a.update(mv_A=A, mv_x=x, mv_bias=bias)
+    n = 72
+    In, W = u8(n, n), s8(n, n)
+    bias = rng.integers(-3000, 3000, n).astype(np.int32)
+    o = np.zeros((n, n), np.int32)
+    ref.ref_hmx_conv1x1_i8(ptr(In), ptr(W), ptr(bias), ptr(o), n)
+    a.update(c11_In=In, c11_W=W, c11_bias=bias, c11_out=o)
+    M, N, K = 60, 100, 130
+    A, B = u8(M, K), s8(K, N)
+    bias = rng.integers(-3000, 3000, N).astype(np.int32)
+    o = np.zeros((M, N), np.uint8)
+    ref.ref_i8_gemm_tiled_bias_relu_requant(ptr(A), ptr(B), ptr(bias), ptr(o), M, N, K)
+    a.update(tbr_A=A, tbr_B=B, tbr_bias=bias, tbr_out=o)
+    for name, cin in (("i8_conv2d_1x1_hmx", 64), ("i8_pointwise_conv_hmx", 96)):
+        inp, W = u8(cin, 64), s8(64, cin)
+        o = np.zeros((64, 64), np.uint16)
+        getattr(ref, "ref_" + name)(ptr(inp), ptr(W), ptr(o), 64)
+        a.update({name + "_in": inp, name + "_W": W, name + "_out": o})
+    save("i8_callers", **a)
+
+
 # ----------------------------------------------------------------- fp16
 
 def gen_hf_q(g, mod, off, step):
@@ -742,6 +788,7 @@ def main():
     gen_int8_attention_hmx(ref)
     gen_int8_attention_blocks(ref)
     gen_f16_family(ref)
+    gen_i8_callers(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

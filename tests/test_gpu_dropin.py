@@ -189,3 +189,35 @@ def test_shim_f16_family(hx):
     o = np.zeros_like(arr(b, "out"))
     shim(b)(p(arr(b, "A")), p(arr(b, "V")), p(o), M, N, D)
     assert_f16_gemm_close(o, arr(b, "out"))
+
+
+def test_shim_i8_callers(hx):
+    from conftest import golden
+    g = golden("i8_callers")
+    c = lambda a: np.ascontiguousarray(a)
+    M, N = g["gbr_out"].shape
+    K = g["gbr_A"].shape[1]
+    o = np.zeros((M, N), np.int8)
+    shim("gemm_bias_relu_requant")(p(c(g["gbr_A"])), p(c(g["gbr_B"])), p(c(g["gbr_bias"])), p(o), M, N, K,
+                                   C.c_int32(1 << 30), 38, C.c_int8(3))
+    np.testing.assert_array_equal(o, g["gbr_out"])
+    M, K = g["mv_A"].shape
+    for name in ("i8_linear_relu_requant", "i8_matvec_bias_requant"):
+        o = np.zeros(M, np.int8)
+        shim(name)(p(c(g["mv_A"])), p(c(g["mv_x"])), p(c(g["mv_bias"])), p(o), M, K, C.c_int32(1 << 30), 38,
+                   C.c_int8(-2))
+        np.testing.assert_array_equal(o, g[name + "_out"])
+    n = g["c11_out"].shape[0]
+    o = np.zeros((n, n), np.int32)
+    shim("hmx_conv1x1_i8")(p(c(g["c11_In"])), p(c(g["c11_W"])), p(c(g["c11_bias"])), p(o), n)
+    np.testing.assert_array_equal(o, g["c11_out"])
+    M, N = g["tbr_out"].shape
+    K = g["tbr_A"].shape[1]
+    o = np.zeros((M, N), np.uint8)
+    shim("i8_gemm_tiled_bias_relu_requant")(p(c(g["tbr_A"])), p(c(g["tbr_B"])), p(c(g["tbr_bias"])), p(o),
+                                            M, N, K)
+    np.testing.assert_array_equal(o, g["tbr_out"])
+    for name in ("i8_conv2d_1x1_hmx", "i8_pointwise_conv_hmx"):
+        o = np.zeros((64, 64), np.uint16)
+        shim(name)(p(c(g[name + "_in"])), p(c(g[name + "_W"])), p(o), 64)
+        np.testing.assert_array_equal(o, g[name + "_out"])

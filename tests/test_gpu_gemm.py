@@ -344,3 +344,29 @@ def test_f16_ex_random(hx, oracle, M, N, K):
         exp = oracle.gemm_f16_ex(A, B, **kw)
         assert_f16_gemm_close(hx.gemm_f16_ex(A, B, **kw), exp)
         assert_f16_gemm_close(hx.gemm_f16_ex(A, Bt, b_transposed=True, **kw), exp)
+
+
+from test_oracle_golden import i8_callers_calls  # noqa: E402
+
+
+def test_i8_callers_golden(hx):
+    for got, exp in i8_callers_calls(hx, golden("i8_callers")):
+        np.testing.assert_array_equal(got, exp)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (1, 4097, 3000), (129, 257, 130), (300, 520, 1000)])
+def test_i8_rq_ex_and_s8u8_random(hx, oracle, M, N, K):
+    """ReLU-before-requant GEMM (both B layouts, with and without bias) and the
+    s8 x u8 HMX field GEMM against the oracle."""
+    rng = np.random.default_rng(M + 3 * N + K)
+    A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    bias = rng.integers(-40000, 40000, N).astype(np.int32)
+    for kw in (dict(bias=bias, relu=True), dict(relu=False), dict(bias=bias, relu=False)):
+        exp = oracle.gemm_i8_rq_ex(A, B, 1234567, 30, 4, **kw)
+        np.testing.assert_array_equal(hx.gemm_i8_rq_ex(A, B, 1234567, 30, 4, **kw), exp)
+        np.testing.assert_array_equal(
+            hx.gemm_i8_rq_ex(A, np.ascontiguousarray(B.T), 1234567, 30, 4, b_transposed=True, **kw), exp)
+    Bu = rng.integers(0, 256, (K, N), dtype=np.uint8)
+    for store in ("i32", "u16_field", "acc_i32"):
+        np.testing.assert_array_equal(hx.gemm_hmx_s8u8(A, Bu, store), oracle.gemm_hmx_s8u8(A, Bu, store))

@@ -288,3 +288,25 @@ def test_f16_family_golden(oracle, bundle):
     (same fp32 accumulation order, same libm tanh) bit for bit."""
     A, B, out, kw = f16_case(golden("f16_family"), bundle)
     np.testing.assert_array_equal(oracle.gemm_f16_ex(A, B, **kw).view(np.uint16), out.view(np.uint16))
+
+
+def i8_callers_calls(impl, g):
+    """(result, expected) of the int8 GEMM callers' golden cases through
+    `impl` (the oracle or the GPU ops module)."""
+    yield (impl.gemm_i8_rq_ex(g["gbr_A"], g["gbr_B"], 1 << 30, 38, 3, bias=g["gbr_bias"], relu=True),
+           g["gbr_out"])
+    x = g["mv_x"][None]
+    yield (impl.gemm_i8_rq_ex(x, g["mv_A"], 1 << 30, 38, -2, bias=g["mv_bias"], relu=True,
+                              b_transposed=True)[0], g["i8_linear_relu_requant_out"])
+    yield (impl.gemm_i8_rq_ex(x, g["mv_A"], 1 << 30, 38, -2, bias=g["mv_bias"], b_transposed=True)[0],
+           g["i8_matvec_bias_requant_out"])
+    yield (impl.gemm_hmx_ex(g["c11_In"], g["c11_W"], "i32", bias=g["c11_bias"], b_transposed=True),
+           g["c11_out"])
+    yield (impl.gemm_hmx_ex(g["tbr_A"], g["tbr_B"], "u8_sat", "relu", bias=g["tbr_bias"]), g["tbr_out"])
+    for name in ("i8_conv2d_1x1_hmx", "i8_pointwise_conv_hmx"):
+        yield impl.gemm_hmx_s8u8(g[name + "_W"], g[name + "_in"], "u16_field"), g[name + "_out"]
+
+
+def test_i8_callers_golden(oracle):
+    for got, exp in i8_callers_calls(oracle, golden("i8_callers")):
+        np.testing.assert_array_equal(got, exp)

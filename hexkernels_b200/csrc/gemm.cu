@@ -49,6 +49,7 @@ constexpr int kBKBytes = 128;        // K extent of one stage, in bytes
 constexpr int kStages = 4;
 constexpr int kThreads = 320;      // TMA warp, MMA warp, 8 epilogue warps
 constexpr int kGroupM = 16;
+constexpr int kColParamBytes = 6 * 32 * 4;   // one epilogue warp's ColParams
 
 enum EpiKind { kEpiF16 = 0, kEpiRequant = 1, kEpiHmx = 2, kEpiF16Ex = 3 };
 
@@ -103,7 +104,7 @@ struct Smem {
     // per epilogue warp: the requant parameters of its current 32 columns,
     // read with 16-byte loads, so the region starts on a 128-byte boundary
     static constexpr int kParamOffset = (kBarOffset + kNumBars * 8 + 16 + 127) / 128 * 128;
-    static constexpr int kParamBytes = 8 * 512;
+    static constexpr int kParamBytes = 8 * kColParamBytes;
     static constexpr int kTotal = kParamOffset + kParamBytes + 1024;  // + align slack
 };
 
@@ -117,10 +118,55 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
     nb = r / gsize;
 }
 
-// Requant parameters of one epilogue warp's current 32 columns.
+// Requant parameters of one epilogue warp's current 32 columns; half is the
+// rounding term 2^(shift-1) (0 for shift 0) as two 32-bit words.
 struct ColParams {
     int32_t corr[32], bias[32], mult[32], shift[32];
+    uint32_t half_lo[32], half_hi[32];
 };
+static_assert(sizeof(ColParams) == kColParamBytes, "per-warp parameter slice");
+
+// Rounded magnitudes at or above kMagCap saturate every clamp of the requant
+// epilogue (the host keeps |zp|, |lo|, |hi| below 2^19), so the magnitude is
+// capped there and the zero point and clamps run in 32 bits.
+constexpr uint32_t kMagCap = 1u << 20;
+
+// 32 requantised columns of one row -> 8 words of packed 8-bit outputs:
+//   x = (int64)(acc32 - corr_j) + bias_j; RELU: x = max(x, 0)
+//   v = x * mult_j (int64 wrap); q = sign(v) ((|v| + half_j) >> shift_j)
+//   out = clamp(q + zp, lo, hi)   (upper clamp first, as the reference)
+template <bool RELU>
+__device__ __forceinline__ void requant_chunk(const EpiParams &ep, const uint32_t (&r)[32],
+                                              const ColParams *cp, uint32_t (&w)[8]) {
+#pragma unroll
+    for (int i4 = 0; i4 < 8; i4++) {
+        const int4 c4 = *reinterpret_cast<const int4 *>(&cp->corr[4 * i4]);
+        const int4 b4 = *reinterpret_cast<const int4 *>(&cp->bias[4 * i4]);
+        const int4 m4 = *reinterpret_cast<const int4 *>(&cp->mult[4 * i4]);
+        const int4 s4 = *reinterpret_cast<const int4 *>(&cp->shift[4 * i4]);
+        const uint4 hl4 = *reinterpret_cast<const uint4 *>(&cp->half_lo[4 * i4]);
+        const uint4 hh4 = *reinterpret_cast<const uint4 *>(&cp->half_hi[4 * i4]);
+        const int cc[4] = {c4.x, c4.y, c4.z, c4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
+        const int mm[4] = {m4.x, m4.y, m4.z, m4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+        const uint32_t hl[4] = {hl4.x, hl4.y, hl4.z, hl4.w}, hh[4] = {hh4.x, hh4.y, hh4.z, hh4.w};
+        uint32_t q[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int32_t a32 = (int32_t)(r[4 * i4 + u] - (uint32_t)cc[u]);
+            int64_t xb = (int64_t)a32 + bb[u];
+            if (RELU && xb < 0) xb = 0;
+            const int64_t v = (int64_t)((uint64_t)xb * (uint64_t)(int64_t)mm[u]);
+            const uint64_t av = v < 0 ? 0ull - (uint64_t)v : (uint64_t)v;
+            const uint64_t mag = (av + (((uint64_t)hh[u] << 32) | hl[u])) >> ss[u];
+            const int32_t m32 = mag >= kMagCap ? (int32_t)kMagCap : (int32_t)mag;
+            int32_t x = (v < 0 ? -m32 : m32) + ep.zp;
+            x = x > ep.hi ? ep.hi : x;
+            x = x < ep.lo ? ep.lo : x;
+            q[u] = (uint32_t)x;
+        }
+        w[i4] = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+    }
+}
 
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32_t (&r)[32],
@@ -289,34 +335,10 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
         // requant: the 32 columns' parameters were staged in `cp` by this warp
         uint8_t *o = reinterpret_cast<uint8_t *>(ep.out) + (size_t)row * ep.ldo + col0;
         uint32_t w[8];
-#pragma unroll
-        for (int i4 = 0; i4 < 8; i4++) {
-            const int4 c4 = *reinterpret_cast<const int4 *>(&cp->corr[4 * i4]);
-            const int4 b4 = *reinterpret_cast<const int4 *>(&cp->bias[4 * i4]);
-            const int4 m4 = *reinterpret_cast<const int4 *>(&cp->mult[4 * i4]);
-            const int4 s4 = *reinterpret_cast<const int4 *>(&cp->shift[4 * i4]);
-            const int cc[4] = {c4.x, c4.y, c4.z, c4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
-            const int mm[4] = {m4.x, m4.y, m4.z, m4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
-            uint32_t packed = 0;
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                // acc32 = rawdot - zpA * colsum[j] with int32 wrap, then the
-                // int64 bias add, multiply and round-half-away shift
-                const int32_t a32 = (int32_t)(r[4 * i4 + u] - (uint32_t)cc[u]);
-                int64_t xb = (int64_t)a32 + bb[u];
-                if (ep.relu_pre && xb < 0) xb = 0;
-                const int64_t v = xb * (int64_t)mm[u];
-                const int sh = ss[u];
-                const uint64_t half = sh > 0 ? (1ull << (sh - 1)) : 0ull;
-                const uint64_t av = v < 0 ? (uint64_t)(-v) : (uint64_t)v;
-                int64_t q = (int64_t)((av + half) >> sh);
-                q = (v < 0 ? -q : q) + ep.zp;
-                q = q > ep.hi ? ep.hi : q;
-                q = q < ep.lo ? ep.lo : q;
-                packed |= ((uint32_t)q & 0xFFu) << (8 * u);
-            }
-            w[i4] = packed;
-        }
+        if (ep.relu_pre)
+            requant_chunk<true>(ep, r, cp, w);
+        else
+            requant_chunk<false>(ep, r, cp, w);
         if (row >= ep.M) return;
         if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
             uint4 *dst = reinterpret_cast<uint4 *>(o);
@@ -330,7 +352,8 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
 
 // Stage the requant parameters of columns col0..col0+31 (lane = column) into
 // the warp's shared-memory slice: zpA * colsum[j] (int32 wrap), bias[j],
-// mult[j], shift[j] clamped to 0..63 (the C reference is undefined beyond).
+// mult[j], shift[j] clamped to 0..63 (the C reference is undefined beyond)
+// and its rounding term.
 __device__ __forceinline__ void stage_params(const EpiParams &ep, ColParams *cp, int col0,
                                              int lane) {
     const int j = col0 + lane;
@@ -341,10 +364,14 @@ __device__ __forceinline__ void stage_params(const EpiParams &ep, ColParams *cp,
         if (ep.mult_pc) m = __ldg(ep.mult_pc + j);
         if (ep.shift_pc) sh = __ldg(ep.shift_pc + j);
     }
+    sh = sh < 0 ? 0 : (sh > 63 ? 63 : sh);
+    const uint64_t half = sh > 0 ? 1ull << (sh - 1) : 0ull;
     cp->corr[lane] = c;
     cp->bias[lane] = b;
     cp->mult[lane] = m;
-    cp->shift[lane] = sh < 0 ? 0 : (sh > 63 ? 63 : sh);
+    cp->shift[lane] = sh;
+    cp->half_lo[lane] = (uint32_t)half;
+    cp->half_hi[lane] = (uint32_t)(half >> 32);
 }
 
 template <MmaKind KIND, int BN, int EPI, bool A_SIGNED, bool B_SIGNED, bool B_MN = false>
@@ -542,6 +569,259 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         __syncwarp();
         tc::tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ------------------------------------------- CTA-pair kernel (cta_group::2)
+//
+// Same roles and epilogues as gemm_tc_kernel, on 256 x 256 output tiles
+// computed by a cluster of two CTAs on two SMs.  CTA r of the pair stages
+// rows [256 mb + 128 r, +128) of A and columns [256 nb + 128 r, +128) of B;
+// the even CTA's MMA thread issues M = 256, N = 256 MMAs that read both
+// CTAs' stages and leave rows 128 r.. of the tile in CTA r's tensor memory.
+// Per SM a stage is 32 KB for the same MMA time that a 48 KB stage of the
+// 128 x 256 tile feeds, so operand traffic per SM drops by a third and six
+// stages fit in shared memory.
+//
+// Barriers: full[s] lives in the even CTA (both CTAs' TMA loads count their
+// bytes there; its producer arms it with both halves); empty[s] and tfull[b]
+// live in both CTAs and are signalled by the even CTA's MMA commits;
+// tempty[b] lives in the even CTA and collects one arrival per epilogue warp
+// of both CTAs.
+constexpr int kStages2 = 6;
+constexpr int kGroupM2 = 8;        // pair tiles of 256 rows per rasterisation group
+
+struct Smem2 {
+    static constexpr int kABytes = 128 * kBKBytes;        // this CTA's 128 rows of A
+    static constexpr int kBBytes = 128 * kBKBytes;        // this CTA's 128 columns of B
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBarOffset = kStages2 * kStageBytes;
+    // full[S], empty[S], tfull[2], tempty[2], drain
+    static constexpr int kNumBars = 2 * kStages2 + 5;
+    static constexpr int kParamOffset = (kBarOffset + kNumBars * 8 + 16 + 127) / 128 * 128;
+    static constexpr int kParamBytes = 8 * kColParamBytes;
+    static constexpr int kTotal = kParamOffset + kParamBytes + 1024;
+};
+static_assert(Smem2::kTotal <= 227 * 1024, "pair-kernel shared memory");
+
+__device__ __forceinline__ void tile_coords2(int t, int tiles_m, int tiles_n, int &mb, int &nb) {
+    const int per_group = kGroupM2 * tiles_n;
+    const int group = t / per_group;
+    const int first_m = group * kGroupM2;
+    const int gsize = min(tiles_m - first_m, kGroupM2);
+    const int r = t - group * per_group;
+    mb = first_m + r % gsize;
+    nb = r / gsize;
+}
+
+template <MmaKind KIND, int EPI, bool A_SIGNED, bool B_SIGNED, bool B_MN = false>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmArgs args) {
+    constexpr int kEsize = KIND == MmaKind::F16 ? 2 : 1;
+    constexpr int kKElems = kBKBytes / kEsize;
+    constexpr int kNBox = 128 / kEsize;
+    constexpr int kBoxBytes = kKElems * 128;
+    constexpr int kTileN = 256;
+    constexpr uint32_t kTmemCols = 512;               // two 256-column accumulators
+    using L = Smem2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBarOffset);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + kStages2;
+    uint64_t *tfull = bars + 2 * kStages2;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + L::kNumBars);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = tc::cluster_ctarank();
+    const bool even = rank == 0;
+    const int pair = blockIdx.x >> 1;
+    const int npairs = gridDim.x >> 1;
+    const int num_tiles = args.tiles_m * args.tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages2; s++) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            tc::mbar_init(&tfull[b], 1);
+            tc::mbar_init(&tempty[b], 16);   // one arrive per epilogue warp of the pair
+        }
+        tc::mbar_init(drain, 1);
+        *abort_flag = 0;
+        tc::fence_mbar_init();
+        tc::tma_prefetch_desc(&tmA);
+        tc::tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc_pair(tmem_slot, kTmemCols);
+        tc::tmem_relinquish_pair();
+    }
+    // barriers of both CTAs initialised and the allocation visible before
+    // any load, commit or remote arrive of the pair
+    tc::tc_fence_before();
+    tc::cluster_sync_all();
+    tc::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs)
+            const uint32_t full_even = tc::mapa_shared(tc::smem_u32(full), 0);
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0, armed_phase = 0;
+            for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
+                int mb, nb;
+                tile_coords2(t, args.tiles_m, args.tiles_n, mb, nb);
+                const int row0 = mb * 256 + (int)rank * 128;
+                const int col0 = nb * kTileN + (int)rank * 128;
+                for (int kb = 0; kb < args.num_kb; kb++) {
+                    if (!tc::mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.err_word,
+                                       kErrWaitEmpty))
+                        break;
+                    uint8_t *sa = smem + stage * L::kStageBytes;
+                    uint8_t *sb = sa + L::kABytes;
+                    if (even) tc::mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+                    const uint32_t fb = full_even + (uint32_t)stage * 8u;
+                    const int kx = kb * kKElems;
+                    tc::tma_load_2d_pair(sa, &tmA, fb, kx, row0);
+                    if constexpr (B_MN) {
+#pragma unroll
+                        for (int c = 0; c < 128 / kNBox; c++)
+                            tc::tma_load_2d_pair(sb + c * kBoxBytes, &tmB, fb, col0 + c * kNBox, kx);
+                    } else {
+                        tc::tma_load_2d_pair(sb, &tmB, fb, kx, col0);
+                    }
+                    armed |= 1u << stage;
+                    armed_phase = (armed_phase & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kStages2) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Drain (even CTA): the full barriers count both CTAs' bytes, so
+            // once the armed phases complete no load of the pair is in flight.
+            if (even)
+                for (int s = 0; s < kStages2; s++)
+                    if (armed & (1u << s)) {
+                        const uint64_t t0 = tc::globaltimer();
+                        while (!tc::mbar_try_wait(&full[s], (armed_phase >> s) & 1u) &&
+                               tc::globaltimer() - t0 < kWaitBudgetNs) {
+                        }
+                    }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && even) {
+            // ---------------- MMA issuer (even CTA only)
+            constexpr uint32_t idesc = (KIND == MmaKind::F16)
+                                           ? tc::idesc_f16_f32(256, kTileN, B_MN)
+                                           : tc::idesc_i8_s32(256, kTileN, A_SIGNED, B_SIGNED, B_MN);
+            const uint32_t empty_own = tc::smem_u32(empty);
+            const uint32_t empty_odd = tc::mapa_shared(empty_own, 1);
+            const uint32_t tfull_own = tc::smem_u32(tfull);
+            const uint32_t tfull_odd = tc::mapa_shared(tfull_own, 1);
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool issued = false;
+            for (int t = pair; t < num_tiles && !*abort_flag; t += npairs, local++) {
+                const int buf = local & 1;
+                const uint32_t aphase = (local >> 1) & 1;
+                if (!tc::mbar_wait_cluster(&tempty[buf], aphase ^ 1, abort_flag, args.err_word,
+                                           kErrWaitAccum))
+                    break;
+                tc::tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kTileN);
+                for (int kb = 0; kb < args.num_kb; kb++) {
+                    if (!tc::mbar_wait(&full[stage], phase, abort_flag, args.err_word,
+                                       kErrWaitFull))
+                        break;
+                    tc::tc_fence_after();
+                    const uint32_t sa = tc::smem_u32(smem + stage * L::kStageBytes);
+                    const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+                    for (int k = 0; k < kBKBytes / 32; k++) {
+                        const uint64_t ad = tc::sdesc_kmajor_sw128(sa + k * 32);
+                        const uint64_t bd =
+                            B_MN ? tc::sdesc_mnmajor_sw128(sb + k * (32 / kEsize) * 128, kBoxBytes, 1024)
+                                 : tc::sdesc_kmajor_sw128(sb + k * 32);
+                        tc::mma_ss_pair<KIND>(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    issued = true;
+                    tc::mma_commit_pair(empty_own + (uint32_t)stage * 8u);
+                    tc::mma_commit_pair(empty_odd + (uint32_t)stage * 8u);
+                    if (++stage == kStages2) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                tc::mma_commit_pair(tfull_own + (uint32_t)buf * 8u);
+                tc::mma_commit_pair(tfull_odd + (uint32_t)buf * 8u);
+            }
+            if (issued) {
+                tc::mma_commit_pair(tc::smem_u32(drain));
+                const uint64_t t0 = tc::globaltimer();
+                while (!tc::mbar_try_wait(drain, 0) && tc::globaltimer() - t0 < kWaitBudgetNs) {
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 2..9 of both CTAs: this CTA's 128
+        // rows of the tile, all 256 columns (warp halves as gemm_tc_kernel)
+        const int q = warp & 3;
+        const int chalf = (warp - 2) >> 2;
+        ColParams *cp = reinterpret_cast<ColParams *>(smem + L::kParamOffset) + (warp - 2);
+        const uint32_t tempty_even = tc::mapa_shared(tc::smem_u32(tempty), 0);
+        int local = 0;
+        for (int t = pair; t < num_tiles && !__any_sync(0xffffffffu, *abort_flag);
+             t += npairs, local++) {
+            int mb, nb;
+            tile_coords2(t, args.tiles_m, args.tiles_n, mb, nb);
+            const int buf = local & 1;
+            const uint32_t aphase = (local >> 1) & 1;
+            const bool ok =
+                tc::mbar_wait(&tfull[buf], aphase, abort_flag, args.err_word, kErrWaitAccum);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            tc::tc_fence_after();
+            const int row = mb * 256 + (int)rank * 128 + q * 32 + lane;
+            const uint32_t taddr =
+                tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kTileN);
+#pragma unroll 1
+            for (int c = chalf * (kTileN / 2); c < (chalf + 1) * (kTileN / 2); c += 32) {
+                uint32_t r[32];
+                if constexpr (EPI == kEpiRequant || EPI == kEpiHmx) {
+                    stage_params(args.epi, cp, nb * kTileN + c, lane);
+                }
+                __syncwarp();
+                tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
+                tc::tmem_ld_wait(r);
+                epilogue_chunk<EPI>(args.epi, r, row, nb * kTileN + c, cp);
+                __syncwarp();
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive_remote(tempty_even + (uint32_t)buf * 8u);
+        }
+    }
+
+    // Both CTAs stay resident until the pair's last MMA, commit and remote
+    // arrive are done; then each frees its half of the allocation.
+    __syncwarp();
+    tc::tc_fence_before();
+    tc::cluster_sync_all();
+    tc::tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tc::tmem_dealloc_pair(tmem_base, kTmemCols);
     }
 }
 
@@ -744,6 +1024,73 @@ int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int
     return HEXCUDA_OK;
 }
 
+// The CTA-pair kernel, persistent over as many pairs as the device keeps
+// resident at once.  Returns HEXCUDA_OK with *launched = false (nothing
+// launched) when the device reports no resident pair, so the caller takes
+// the one-SM kernel.
+template <MmaKind KIND, int EPI, bool AS, bool BS, bool BMN = false>
+int launch_gemm2_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K,
+                        const EpiParams &ep, bool *launched) {
+    using L = Smem2;
+    auto kern = gemm_tc2_kernel<KIND, EPI, AS, BS, BMN>;
+    static int pairs_resident[64] = {};     // 0: not queried yet, -1: none
+    const int dev_slot = d->ordinal & 63;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = L::kTotal;
+    cfg.stream = d->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    *launched = false;
+    if (pairs_resident[dev_slot] == 0) {
+        if (int rc = check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                L::kTotal),
+                           "cudaFuncSetAttribute(gemm pair smem)"))
+            return rc;
+        cfg.gridDim = dim3(2, 1, 1);
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+            cudaGetLastError();
+            n = -1;
+        }
+        pairs_resident[dev_slot] = n;
+    }
+    if (pairs_resident[dev_slot] < 0) return HEXCUDA_OK;
+    GemmArgs args;
+    args.tiles_m = (M + 255) / 256;
+    args.tiles_n = (N + 255) / 256;
+    const int kelems = KIND == MmaKind::F16 ? kBKBytes / 2 : kBKBytes;
+    args.num_kb = (K + kelems - 1) / kelems;
+    args.err_word = d->err_word;
+    args.epi = ep;
+    const int tiles = args.tiles_m * args.tiles_n;
+    const int pairs = tiles < pairs_resident[dev_slot] ? tiles : pairs_resident[dev_slot];
+    cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+    if (int rc = check(cudaLaunchKernelEx(&cfg, kern, ta, tb, args), "launch gemm pair kernel"))
+        return rc;
+    *launched = true;
+    return HEXCUDA_OK;
+}
+
+// The CTA-pair kernel serves the 256-column launches with at least two row
+// tiles of the fp16 and HMX-convention epilogues (measured 0-5 % faster than
+// the one-SM kernel there); the per-channel requant epilogue measured ~3 %
+// faster on the one-SM kernel (u8 x s8 16384 x 8192 x 8192), so it stays
+// there.  HEXCUDA_GEMM_PAIR=0 / =1 in the environment forces either kernel.
+template <int EPI>
+bool gemm_pair_enabled(int M, int N) {
+    if (M <= kBM || N <= 128) return false;
+    const char *e = getenv("HEXCUDA_GEMM_PAIR");
+    if (e && e[0] == '0') return false;
+    if (e && e[0] == '1') return true;
+    return EPI != kEpiRequant;
+}
+
 // Common driver: A [M,K] K-major (pitch lda elements), B given either as
 // Bt [N,K] K-major (b_kmajor) or as row-major B [K,N] (transposed here).
 // Operands whose rows are not 16-byte aligned, or shorter than one 128-byte
@@ -757,6 +1104,9 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "%s: bad shape %dx%dx%d", name, M, N, K);
     if (M == 0 || N == 0) return HEXCUDA_OK;
     if ((K > 0 && (!A || !B)) || !ep.out) return fail(HEXCUDA_ERR_ARG, "%s: null pointer", name);
+    if (EPI == kEpiRequant &&
+        (ep.zp <= -(1 << 19) || ep.zp >= (1 << 19) || ep.lo <= -(1 << 19) || ep.hi >= (1 << 19)))
+        return fail(HEXCUDA_ERR_ARG, "%s: zero point / clamp out of range", name);
     constexpr int esize = KIND == MmaKind::F16 ? 2 : 1;
     constexpr int kelems = kBKBytes / esize;
     constexpr CUtensorMapDataType dt =
@@ -840,6 +1190,18 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
     ep.N = N;
     const int kdim = (int)std::max(a_kdim, b_kdim);
     int rc;
+    if (gemm_pair_enabled<EPI>(M, N)) {
+        bool launched = false;
+        if (b_mn) {
+            if ((rc = make_mnmajor_map(&tb, B, dt, esize, N, K, kelems))) return rc;
+            rc = launch_gemm2_kernel<KIND, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep, &launched);
+        } else {
+            if ((rc = make_kmajor_map(&tb, bt, dt, esize, b_kdim, N, bt_pitch, 128))) return rc;
+            rc = launch_gemm2_kernel<KIND, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep, &launched);
+        }
+        if (rc) return rc;
+        if (launched) return launch_end(d, name, nl + 1);
+    }
     if (b_mn) {
         if ((rc = make_mnmajor_map(&tb, B, dt, esize, N, K, kelems))) return rc;
         if (N <= 128)

@@ -68,14 +68,18 @@ def test_kernel_sources_are_sm100a_native():
                    "tcgen05.alloc", "tcgen05.ld.sync.aligned", "cp.async.bulk.tensor.2d"):
         assert needle in allsrc, needle
     assert "float4" in src["rows.cu"] and "uint4" in src["rows.cu"]
-    # every TMA load is one of the two plain per-CTA forms (each CTA loads its
-    # own tiles; the package runs on several GPUs)
+    # every TMA load is a plain per-CTA form or the CTA-pair form whose bytes
+    # are counted on the pair's barrier; none is a cluster-wide broadcast
+    # (each CTA loads its own tiles; the package runs on several GPUs)
     allowed = {
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes",
         "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes",
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes",
     }
     forms = set(re.findall(r"cp\.async\.bulk\.tensor[\w.:]*", allsrc))
     assert forms == allowed, forms
+    assert "multi" + "cast" not in allsrc
+    assert "tcgen05.mma.cta_group::2" in src["tc_common.cuh"]
     # no legacy tensor-core paths
     for legacy in ("mma.sync", "wmma::", "wgmma"):
         assert legacy not in allsrc, legacy

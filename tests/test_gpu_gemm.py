@@ -370,3 +370,44 @@ def test_i8_rq_ex_and_s8u8_random(hx, oracle, M, N, K):
     Bu = rng.integers(0, 256, (K, N), dtype=np.uint8)
     for store in ("i32", "u16_field", "acc_i32"):
         np.testing.assert_array_equal(hx.gemm_hmx_s8u8(A, Bu, store), oracle.gemm_hmx_s8u8(A, Bu, store))
+
+
+# ------------------------------------------- CTA-pair vs one-SM GEMM kernel
+
+@pytest.mark.parametrize("M,N,K", [(4096, 2304, 256), (1000, 1800, 520)])
+def test_gemm_pair_kernel_matches_single_sm(hx, oracle, monkeypatch, M, N, K):
+    """The 256 x 256 CTA-pair kernel (HEXCUDA_GEMM_PAIR=1; the default for
+    the fp16 and HMX epilogues when M, N > 128) and the 128-row one-SM kernel
+    (HEXCUDA_GEMM_PAIR=0) give identical integer results for every epilogue
+    kind, several tiles per pair (accumulator double buffer, ragged edges);
+    sampled rows against the oracle."""
+    rng = np.random.default_rng(M + N + K)
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    bias = np.round(rng.normal(0, 1000, N)).astype(np.int32)
+    mult = rng.integers(2**30, 2**31, N, dtype=np.int64).astype(np.int32)
+    shift = rng.integers(36, 44, N).astype(np.int32)
+    As = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    Bt = np.ascontiguousarray(B.T)
+    Af = (rng.standard_normal((M, K)) / np.sqrt(K)).astype(np.float16)
+    Btf = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float16)
+
+    def run():
+        return (hx.gemm_u8s8_pc(A, B, bias, 128, mult, shift, 128),
+                hx.gemm_i8_requant(As, B, 1234567, 30, 3),
+                hx.gemm_hmx_ex(A, Bt, store="i32", act="relu", bias=bias, b_transposed=True),
+                hx.gemm_f16_nt(Af, Btf),
+                hx.gemm_f16_nn(Af, np.ascontiguousarray(Btf.T)))
+
+    monkeypatch.setenv("HEXCUDA_GEMM_PAIR", "1")
+    pair = run()
+    monkeypatch.setenv("HEXCUDA_GEMM_PAIR", "0")
+    single = run()
+    for p, s in zip(pair[:3], single[:3]):
+        np.testing.assert_array_equal(p, s)
+    rows = np.sort(rng.choice(M, 16, replace=False))
+    np.testing.assert_array_equal(
+        pair[0][rows], oracle.gemm_u8s8_pc(A[rows], B, bias, 128, mult, shift, 128))
+    np.testing.assert_array_equal(pair[1][rows], oracle.gemm_i8_requant(As[rows], B, 1234567, 30, 3))
+    for f in pair[3:]:
+        assert_f16_gemm_close(f[rows], oracle.gemm_f16_nt(Af[rows], Btf))

@@ -75,50 +75,76 @@ struct RqEw {
     int lo, hi;         // the two clamps folded into one (set by the entry)
     uint32_t amult;     // |mult|
     bool mneg;          // mult < 0
+    int lo_z, hi_z;     // lo - zp, hi - zp
 };
 
-// One element.  PRE and SIGN_OF_A are compile-time so the per-element code
-// has no mode branches.  (A signed form of the rounding, (v + half - (v < 0))
-// >> shift with v from 32 x 32 multiplies, measured slower: it is the
-// integer ALU pipe that bounds this kernel.)  p.lo / p.hi are the two clamps folded into one
-// (the composition of two clamps is the clamp to [clamp(lo1, lo2, hi2),
-// clamp(hi1, lo2, hi2)]).
-template <int PRE, bool SIGN_OF_A>
+// One element.  PRE, SIGN_OF_A and SHIFT_HI (shift >= 32) are compile-time
+// so the per-element code has no mode branches; the kernel is bound by the
+// integer ALU pipe, so the common forms work on 32-bit words:
+//  * pre(a, b) for A / ADD / ADD_RELU is at most 33 bits; its magnitude fits
+//    32 bits except x = -2^32, which takes the general path;
+//  * |x| * |mult| + half is one 32 x 32 -> 64 multiply-add, and with shift
+//    >= 32 the reference's arithmetic shift of that int64 (including its
+//    wrap past 2^63 at the largest shifts) is a 32-bit shift of the high word;
+//  * magnitudes beyond 2^28 (or below -2^28 after a wrap) saturate every
+//    clamp (zp, lo and hi are within +-2^24, checked by the entry), so only
+//    the lower cap is applied before the sign and the clamp runs as
+//    clamp(r, lo - zp, hi - zp) + zp.
+// p.lo / p.hi are the two clamps folded into one (the composition of two
+// clamps is the clamp to [clamp(lo1, lo2, hi2), clamp(hi1, lo2, hi2)]).
+template <int PRE, bool SIGN_OF_A, bool SHIFT_HI>
 __device__ __forceinline__ uint32_t rq_ew_one(int32_t a, int32_t b, const RqEw &p, int64_t half) {
+    constexpr int kCap = 1 << 28;
     int32_t r32;
-    int64_t x = a;
-    if constexpr (PRE == HEXCUDA_RQ_PRE_ADD) {
-        x = (int64_t)a + b;
-    } else if constexpr (PRE == HEXCUDA_RQ_PRE_ADD_RELU) {
-        x = (int64_t)a + b;
-        x = x > 0 ? x : 0;
-    } else if constexpr (PRE == HEXCUDA_RQ_PRE_MUL_ADD) {
-        x = (int64_t)((uint64_t)(int64_t)a * (uint64_t)(int64_t)b + (uint64_t)p.c);
+    bool general = SIGN_OF_A || PRE == HEXCUDA_RQ_PRE_MUL_ADD;
+    if constexpr (!SIGN_OF_A && PRE != HEXCUDA_RQ_PRE_MUL_ADD) {
+        uint32_t lo;
+        bool xneg;
+        if constexpr (PRE == HEXCUDA_RQ_PRE_A) {
+            xneg = a < 0;
+            lo = (uint32_t)a;
+        } else {
+            const int64_t x = (int64_t)a + b;
+            lo = (uint32_t)x;
+            xneg = x < 0;
+            if constexpr (PRE == HEXCUDA_RQ_PRE_ADD_RELU) {
+                if (xneg) lo = 0;
+                xneg = false;
+            } else {
+                general = xneg && lo == 0;      // x = -2^32
+            }
+        }
+        const uint32_t ax = xneg ? 0u - lo : lo;
+        const uint64_t t = (uint64_t)ax * p.amult + (uint64_t)half;
+        int32_t ra;
+        if constexpr (SHIFT_HI) {
+            ra = max((int32_t)(uint32_t)(t >> 32) >> (p.shift - 32), -kCap);
+        } else {
+            const int64_t r = (int64_t)t >> p.shift;
+            ra = (int32_t)(r > kCap ? kCap : (r < -kCap ? -kCap : r));
+        }
+        r32 = (xneg != p.mneg) ? -ra : ra;
     }
-    const bool xneg = x < 0;
-    const uint64_t ax = xneg ? 0ull - (uint64_t)x : (uint64_t)x;
-    if (!SIGN_OF_A && ax < (1ull << 32)) {
-        // |x| < 2^32, |mult| <= 2^31: the exact |x * mult| < 2^63 from one
-        // 32 x 32 -> 64 multiply; round half away from zero on the magnitude
-        // (the reference's v >= 0 / v < 0 branches, including its int64 wrap
-        // of v + half at the largest shifts)
-        const int64_t ra = (int64_t)((uint64_t)(uint32_t)ax * p.amult + (uint64_t)half) >> p.shift;
-        const int32_t m = ra > (1 << 28) ? (1 << 28) : (ra < -(1 << 28) ? -(1 << 28) : (int32_t)ra);
-        r32 = (xneg != p.mneg) ? -m : m;
-    } else {
+    if (general) {
+        int64_t x = a;
+        if constexpr (PRE == HEXCUDA_RQ_PRE_ADD || PRE == HEXCUDA_RQ_PRE_ADD_RELU) {
+            x = (int64_t)a + b;
+        } else if constexpr (PRE == HEXCUDA_RQ_PRE_MUL_ADD) {
+            x = (int64_t)((uint64_t)(int64_t)a * (uint64_t)(int64_t)b + (uint64_t)p.c);
+        }
         int64_t r;
-        if constexpr (SIGN_OF_A) {
+        if (SIGN_OF_A) {
+            const bool xneg = x < 0;
+            const uint64_t ax = xneg ? 0ull - (uint64_t)x : (uint64_t)x;
             const int64_t am = (int64_t)(ax * (uint64_t)(int64_t)p.mult);
             const int64_t sh = (am + half) >> p.shift;
             r = xneg ? -sh : sh;
         } else {
             r = rq_round((int64_t)((uint64_t)x * (uint64_t)(int64_t)p.mult), p.shift);
         }
-        r32 = (int32_t)(r > (1 << 28) ? (1 << 28) : (r < -(1 << 28) ? -(1 << 28) : r));
+        r32 = (int32_t)(r > kCap ? kCap : (r < -kCap ? -kCap : r));
     }
-    // zp, lo and hi are within +-2^24 (checked by the entry), so the magnitude
-    // cap at 2^28 above changes no clamped result
-    r32 = max(min(r32 + p.zp, p.hi), p.lo);
+    r32 = max(min(r32, p.hi_z), p.lo_z) + p.zp;
     if (p.lut) return (uint32_t)(uint8_t)__ldg(p.lut + (uint8_t)r32);
     return (uint32_t)r32 & 0xFFu;
 }
@@ -168,7 +194,7 @@ __device__ __forceinline__ void load4(const void *src, int64_t v, int32_t (&x)[4
     }
 }
 
-template <bool A_I8, int B_KIND, int PRE, bool SIGN_OF_A>
+template <bool A_I8, int B_KIND, int PRE, bool SIGN_OF_A, bool SHIFT_HI>
 __global__ void __launch_bounds__(256) requant_ew_kernel(const void *__restrict__ a,
                                                           const void *__restrict__ b,
                                                           uint8_t *__restrict__ out, int64_t n,
@@ -187,7 +213,7 @@ __global__ void __launch_bounds__(256) requant_ew_kernel(const void *__restrict_
             uint32_t y[16], w[4];
 #pragma unroll
             for (int i = 0; i < 16; i++)
-                y[i] = rq_ew_one<PRE, SIGN_OF_A>(xa[i], B_KIND != 0 ? xb[i] : 0, p, half);
+                y[i] = rq_ew_one<PRE, SIGN_OF_A, SHIFT_HI>(xa[i], B_KIND != 0 ? xb[i] : 0, p, half);
 #pragma unroll
             for (int k = 0; k < 4; k++) w[k] = pack4(y[4 * k], y[4 * k + 1], y[4 * k + 2], y[4 * k + 3]);
             __stcs(reinterpret_cast<uint4 *>(out) + v, make_uint4(w[0], w[1], w[2], w[3]));
@@ -210,7 +236,7 @@ __global__ void __launch_bounds__(256) requant_ew_kernel(const void *__restrict_
                 uint32_t y[4];
 #pragma unroll
                 for (int i = 0; i < 4; i++)
-                    y[i] = rq_ew_one<PRE, SIGN_OF_A>(xa[u][i], B_KIND != 0 ? xb[u][i] : 0, p, half);
+                    y[i] = rq_ew_one<PRE, SIGN_OF_A, SHIFT_HI>(xa[u][i], B_KIND != 0 ? xb[u][i] : 0, p, half);
                 __stcs(reinterpret_cast<unsigned int *>(out) + v + u * stride, pack4(y[0], y[1], y[2], y[3]));
             }
         }
@@ -221,14 +247,14 @@ __global__ void __launch_bounds__(256) requant_ew_kernel(const void *__restrict_
             uint32_t y[4];
 #pragma unroll
             for (int i = 0; i < 4; i++)
-                y[i] = rq_ew_one<PRE, SIGN_OF_A>(xa[i], B_KIND != 0 ? xb[i] : 0, p, half);
+                y[i] = rq_ew_one<PRE, SIGN_OF_A, SHIFT_HI>(xa[i], B_KIND != 0 ? xb[i] : 0, p, half);
             __stcs(reinterpret_cast<unsigned int *>(out) + v, pack4(y[0], y[1], y[2], y[3]));
         }
         done = nv * 4;
     }
     for (int64_t i = done + t; i < n; i += stride) {
         const int32_t bi = B_KIND == 0 ? 0 : load1<B_KIND == 2>(b, i);
-        out[i] = (uint8_t)rq_ew_one<PRE, SIGN_OF_A>(load1<A_I8>(a, i), bi, p, half);
+        out[i] = (uint8_t)rq_ew_one<PRE, SIGN_OF_A, SHIFT_HI>(load1<A_I8>(a, i), bi, p, half);
     }
 }
 
@@ -272,6 +298,41 @@ __global__ void __launch_bounds__(256) relu_i8_kernel(const int8_t *__restrict__
         done = n / 16 * 16;
     }
     for (int64_t i = done + t; i < n; i += stride) out[i] = x[i] > 0 ? x[i] : 0;
+}
+
+// Grid of a grid-stride kernel: enough 256-thread blocks for `work` thread
+// steps, capped at what the device keeps resident at once (blocks per SM from
+// the kernel's register and shared-memory use, cached per kernel and device),
+// so every block runs in the first and only wave.
+template <auto KERN>
+int resident_blocks(const Dev *d, int64_t work) {
+    static int per_sm[64] = {};
+    const int slot = d->ordinal & 63;
+    if (per_sm[slot] == 0) {
+        int nb = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, KERN, 256, 0) != cudaSuccess || nb < 1) {
+            cudaGetLastError();
+            nb = 1;
+        }
+        per_sm[slot] = nb;
+    }
+    int64_t blocks = (work + 255) / 256;
+    const int64_t cap = (int64_t)d->sms * per_sm[slot];
+    if (blocks > cap) blocks = cap;
+    return blocks < 1 ? 1 : (int)blocks;
+}
+
+template <bool A_I8, int B_KIND, int PRE, bool SIGN_OF_A>
+void launch_rq_ew(const Dev *d, int64_t work, const void *a, const void *b, uint8_t *o, int64_t n,
+                  const RqEw &p, int vec) {
+    constexpr bool kFast = !SIGN_OF_A && PRE != HEXCUDA_RQ_PRE_MUL_ADD;
+    if (kFast && p.shift >= 32) {
+        constexpr auto kern = requant_ew_kernel<A_I8, B_KIND, PRE, SIGN_OF_A, kFast>;
+        kern<<<resident_blocks<kern>(d, work), 256, 0, d->stream>>>(a, b, o, n, p, vec);
+    } else {
+        constexpr auto kern = requant_ew_kernel<A_I8, B_KIND, PRE, SIGN_OF_A, false>;
+        kern<<<resident_blocks<kern>(d, work), 256, 0, d->stream>>>(a, b, o, n, p, vec);
+    }
 }
 
 int ew_blocks(const Dev *d, int64_t work) {
@@ -340,40 +401,42 @@ HX_EXPORT int hexcuda_requant_ew(int dev, const void *a, int a_i8, const void *b
                     shift, b_kind, pre);
     if (n == 0) return HEXCUDA_OK;
     if (!a || !out || (b_kind && !b)) return fail(HEXCUDA_ERR_ARG, "requant_ew: null pointer");
-    RqEw p{pre, pre_c, mult, shift, zp, sign_of_a ? 1 : 0, lo1, hi1, lo2, hi2, lut, 0, 0, 0, false};
+    RqEw p{pre, pre_c, mult, shift, zp, sign_of_a ? 1 : 0, lo1, hi1, lo2, hi2, lut, 0, 0, 0, false, 0, 0};
     {
         auto clampi = [](int v, int lo, int hi) { return std::max(std::min(v, hi), lo); };
         p.lo = clampi(lo1, lo2, hi2);
         p.hi = clampi(hi1, lo2, hi2);
         p.amult = mult < 0 ? 0u - (uint32_t)mult : (uint32_t)mult;
         p.mneg = mult < 0;
+        p.lo_z = p.lo - zp;
+        p.hi_z = p.hi - zp;
     }
     auto al = [](const void *q) { return q == nullptr || ((uintptr_t)q & 15u) == 0; };
     const int vec = al(a) && al(b) && al(out);
     const int per = (a_i8 && b_kind != 1) ? 16 : 4;
-    const int blocks = ew_blocks(d, vec ? (n + per - 1) / per : n);
+    const int64_t work = vec ? (n + per - 1) / per : n;
     uint8_t *o = reinterpret_cast<uint8_t *>(out);
     launch_begin(d);
     if (sign_of_a) {
         if (pre != HEXCUDA_RQ_PRE_A) return fail(HEXCUDA_ERR_ARG, "requant_ew: sign_of_a takes a alone");
         if (a_i8)
-            requant_ew_kernel<true, 0, HEXCUDA_RQ_PRE_A, true><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+            launch_rq_ew<true, 0, HEXCUDA_RQ_PRE_A, true>(d, work, a, b, o, n, p, vec);
         else
-            requant_ew_kernel<false, 0, HEXCUDA_RQ_PRE_A, true><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+            launch_rq_ew<false, 0, HEXCUDA_RQ_PRE_A, true>(d, work, a, b, o, n, p, vec);
     } else if (pre == HEXCUDA_RQ_PRE_A) {
         if (a_i8)
-            requant_ew_kernel<true, 0, HEXCUDA_RQ_PRE_A, false><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+            launch_rq_ew<true, 0, HEXCUDA_RQ_PRE_A, false>(d, work, a, b, o, n, p, vec);
         else
-            requant_ew_kernel<false, 0, HEXCUDA_RQ_PRE_A, false><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+            launch_rq_ew<false, 0, HEXCUDA_RQ_PRE_A, false>(d, work, a, b, o, n, p, vec);
     } else {
         // two-operand forms: int32 pairs or int8 pairs (the corpus's bundles)
         if (a_i8 != (b_kind == 2))
             return fail(HEXCUDA_ERR_ARG, "requant_ew: a and b must both be int32 or both int8");
 #define HX_RQ2(P)                                                                                 \
     if (a_i8)                                                                                    \
-        requant_ew_kernel<true, 2, P, false><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec); \
+        launch_rq_ew<true, 2, P, false>(d, work, a, b, o, n, p, vec); \
     else                                                                                         \
-        requant_ew_kernel<false, 1, P, false><<<blocks, 256, 0, d->stream>>>(a, b, o, n, p, vec);
+        launch_rq_ew<false, 1, P, false>(d, work, a, b, o, n, p, vec);
         if (pre == HEXCUDA_RQ_PRE_ADD) {
             HX_RQ2(HEXCUDA_RQ_PRE_ADD)
         } else if (pre == HEXCUDA_RQ_PRE_ADD_RELU) {

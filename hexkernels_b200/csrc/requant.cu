@@ -194,8 +194,11 @@ __device__ __forceinline__ void load4(const void *src, int64_t v, int32_t (&x)[4
     }
 }
 
+// Six blocks per SM (at most 40 registers a thread): the loads in flight of
+// 48 warps, against 40 at the register count ptxas picks unbounded; eight
+// blocks (32 registers) spill.
 template <bool A_I8, int B_KIND, int PRE, bool SIGN_OF_A, bool SHIFT_HI>
-__global__ void __launch_bounds__(256) requant_ew_kernel(const void *__restrict__ a,
+__global__ void __launch_bounds__(256, 6) requant_ew_kernel(const void *__restrict__ a,
                                                           const void *__restrict__ b,
                                                           uint8_t *__restrict__ out, int64_t n,
                                                           const RqEw p, int vec) {

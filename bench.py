@@ -563,6 +563,56 @@ class RequantEw(Workload):
     cpu_what = "oracle/hexoracle.c restatement of residual_add_requant/reference.c"
 
 
+class ReduceI8(Workload):
+    """i8_sum_dma at scale: the int32 sum of 2^31 int8 (2 GiB read once) on
+    the integer whole-array reduction kernel; HBM-bound, 1 byte per element."""
+    name = "reduce_i8"
+    unit = "GB/s"
+    dtype = "int32"
+    bound = "hbm"
+    N = 1 << 31
+
+    def config(self):
+        return {"workload": "i8_sum_dma: int32 sum of 2^31 int8", "n": self.N,
+                "a": "U[-128,128)", "seed": 0, "l2": "input 2 GiB > L2, no flush",
+                "sharding": "elements", "parallelism": f"elements/{self.world}"}
+
+    def units_per_step(self):
+        return float(self.N)
+
+    def setup_device(self, torch):
+        r0, r1 = shard(self.N, self.world, self.rank)
+        self.n = r1 - r0
+        g = torch.Generator(device="cuda").manual_seed(0)
+        self.a = torch.randint(-128, 128, (self.n,), dtype=torch.int8, device="cuda", generator=g)
+        self.out = torch.zeros(2, dtype=torch.int32, device="cuda")
+
+    def kernels(self):
+        return [("reduce_int", float(self.n))]
+
+    def launch(self, device, k):
+        device.launch("reduce_int", 0, self.a, None, 0, self.n, 0, self.out)
+
+    def cpu_setup(self, rows):
+        self.ca = np.random.default_rng(0).integers(-128, 128, rows, dtype=np.int8)
+        self.cout = np.zeros(256, np.int32)
+
+    def cpu_step(self, o, rows, nthreads):
+        import ctypes as C
+        lib = o.lib()
+
+        def part(r0, r1):
+            slot = min(255, r0 * max(1, nthreads) // max(1, rows))
+            lib.oracle_reduce_int(C.c_void_p(self.ca.ctypes.data + r0), None, 0,
+                                  C.c_int64(r1 - r0), 0,
+                                  C.c_void_p(self.cout.ctypes.data + 4 * slot))
+        _threaded(part, rows, nthreads)
+        return float(rows)
+
+    cpu_kind = "port"
+    cpu_what = "oracle/hexoracle.c restatement of i8_sum_dma/reference.c (int32 sum)"
+
+
 class GemmHmx(Workload):
     """HMX-convention u8 x s8 GEMM with bias and ReLU to int32
     (i8_matmul_bias_relu_hmx's epilogue) at 16384 x 8192 x 8192."""
@@ -621,7 +671,8 @@ class GemmHmx(Workload):
                 "(i8_matmul_bias_relu_hmx/reference.c), rows split over host threads")
 
 
-WORKLOADS = {w.name: w for w in (Reduce, GemmU8S8, GemmF16, Attn, GemmI8, RequantEw, GemmHmx)}
+WORKLOADS = {w.name: w for w in (Reduce, GemmU8S8, GemmF16, Attn, GemmI8, RequantEw, GemmHmx,
+                                  ReduceI8)}
 
 
 # ------------------------------------------------------------------- timing
@@ -679,7 +730,7 @@ def cpu_measure(wl, budget_s: float, nthreads: int, max_rows: int):
     then times repeated calls for about `budget_s` seconds."""
     from oracle import oracle as o
     o.lib()
-    rows = {"reduce": 256, "requant": 1 << 16}.get(wl.name, 8)
+    rows = {"reduce": 256, "requant": 1 << 16, "reduce_i8": 1 << 22}.get(wl.name, 8)
     rows = min(rows, max_rows)
     while True:
         wl.cpu_setup(rows)
@@ -700,7 +751,8 @@ def cpu_measure(wl, budget_s: float, nthreads: int, max_rows: int):
 
 def cpu_rows_cap(wl):
     return {"reduce": wl.R if hasattr(wl, "R") else 0, "gemm_u8s8": 4096, "gemm_f16": 4096,
-            "attn": 4096, "gemm_i8": 256, "requant": 1 << 28, "gemm_hmx": 4096}[wl.name]
+            "attn": 4096, "gemm_i8": 256, "requant": 1 << 28, "gemm_hmx": 4096,
+            "reduce_i8": 1 << 28}[wl.name]
 
 
 def cpu_sample_text(wl, rows, reps, secs):
@@ -712,6 +764,8 @@ def cpu_sample_text(wl, rows, reps, secs):
         return f"the full 256^3 GEMM, {reps} reps, {secs:.1f} s"
     if wl.name == "requant":
         return f"{rows} of 2^28 elements, {reps} reps, {secs:.1f} s"
+    if wl.name == "reduce_i8":
+        return f"{rows} of 2^31 elements, {reps} reps, {secs:.1f} s"
     return f"{rows} rows of M with full N, K, {reps} reps, {secs:.1f} s"
 
 
@@ -788,7 +842,8 @@ def run_ours(args, dist):
     head = measure(WORKLOADS[args.workload], True, True)
     ops = {}
     if args.ops == "all":
-        for name in ("gemm_u8s8", "gemm_f16", "attn", "gemm_i8", "requant", "gemm_hmx"):
+        for name in ("gemm_u8s8", "gemm_f16", "attn", "gemm_i8", "requant", "gemm_hmx",
+                     "reduce_i8"):
             if name == args.workload:
                 continue
             r = measure(WORKLOADS[name], False, args.cpu_all)
@@ -821,7 +876,7 @@ def run_reference(args, dist):
     nthreads = 1 if wl.name == "gemm_i8" else len(os.sched_getaffinity(0))
     # size the per-step sample so the whole run stays within ~2 minutes
     per_step_budget = max(0.2, 100.0 / max(1, args.steps + args.warmup))
-    rows = {"reduce": 256, "requant": 1 << 16}.get(wl.name, 8)
+    rows = {"reduce": 256, "requant": 1 << 16, "reduce_i8": 1 << 22}.get(wl.name, 8)
     cap = cpu_rows_cap(wl)
     while True:
         wl.cpu_setup(rows)

@@ -69,6 +69,11 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_requant_ew": (I, [I, P, I, P, I, P, I64, I, I64, I32, I, I, I, I, I, I, I, P]),
     "hexcuda_epilogue_bias_i32": (I, [I, P, P, P, I, I]),
     "hexcuda_relu_i8": (I, [I, P, P, I64]),
+    "hexcuda_reduce_int": (I, [I, P, P, I, I64, I, P]),
+    "hexcuda_minmax_ew": (I, [I, P, P, I32, I, I, P, I64]),
+    "hexcuda_group_sum_i8": (I, [I, P, P, I64, I]),
+    "hexcuda_scan_max_i8": (I, [I, P, P, I64]),
+    "hexcuda_head_group_reduce_i8": (I, [I, P, P, I, I, I64, I32, I]),
     "hexcuda_gemm_hmx_ex": (I, [I, P, P, I, P, P, I, P, P, I, I, I, I, I, I, I32]),
     "hexcuda_gemm_u8s8_pc_noalloc": (I, [I, P, P, P, P, I, I, I, I32, P, P, U8]),
     "hexcuda_gemm_f16_nt": (I, [I, P, P, P, I, I, I]),
@@ -99,6 +104,11 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_requant_ew": (I, [P, I, P, I, P, I64, I, I64, I32, I, I, I, I, I, I, I, P]),
     "hexcuda_host_epilogue_bias_i32": (I, [P, P, P, I, I]),
     "hexcuda_host_relu_i8": (I, [P, P, I64]),
+    "hexcuda_host_reduce_int": (I, [P, P, I, I64, I, P]),
+    "hexcuda_host_minmax_ew": (I, [P, P, I32, I, I, P, I64]),
+    "hexcuda_host_group_sum_i8": (I, [P, P, I64, I]),
+    "hexcuda_host_scan_max_i8": (I, [P, P, I64]),
+    "hexcuda_host_head_group_reduce_i8": (I, [P, P, I, I, I64, I32, I]),
     "hexcuda_host_gemm_hmx_ex": (I, [P, P, I, P, P, I, P, P, I, I, I, I, I, I, I32]),
     "hexcuda_host_gemm_f16_nt": (I, [P, P, P, I, I, I]),
     "hexcuda_host_gemm_f16_nn": (I, [P, P, P, I, I, I]),

@@ -742,3 +742,74 @@ HX_EXPORT int hexcuda_host_online_softmax_step_f16(const uint16_t *scores, const
     std::copy(result.begin() + 2, result.end(), acc);
     return HEXCUDA_OK;
 }
+
+HX_EXPORT int hexcuda_host_minmax_ew(const void *a, const void *b, int32_t c, int elem, int op,
+                                     void *out, int64_t n) {
+    if (n < 0 || (elem != HEXCUDA_ELEM_I8 && elem != HEXCUDA_ELEM_U8 && elem != HEXCUDA_ELEM_I16))
+        return fail(HEXCUDA_ERR_ARG, "host_minmax_ew: elem %d n %lld", elem, (long long)n);
+    if (n == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_minmax_ew", {a, out})) return rc;
+    const size_t es = elem == HEXCUDA_ELEM_I16 ? 2 : 1;
+    return run_sharded(n, out, es, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const uint8_t *da = stage_in(p.d, kSlotIn0, reinterpret_cast<const uint8_t *>(a) + p.r0 * es,
+                                     (size_t)nr * es);
+        const uint8_t *db = b ? stage_in(p.d, kSlotIn1, reinterpret_cast<const uint8_t *>(b) + p.r0 * es,
+                                         (size_t)nr * es)
+                              : nullptr;
+        void *dout = scratch(p.d, kSlotOut, (size_t)nr * es);
+        if (!da || (b && !db) || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_minmax_ew(p.slot, da, db, c, elem, op, dout, nr);
+    });
+}
+
+HX_EXPORT int hexcuda_host_group_sum_i8(const int8_t *a, int32_t *out, int64_t g, int w) {
+    if (g < 0 || w < 1) return fail(HEXCUDA_ERR_ARG, "host_group_sum_i8: g %lld w %d", (long long)g, w);
+    if (g == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_group_sum_i8", {a, out})) return rc;
+    return run_sharded(g, out, 4, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *da = stage_in(p.d, kSlotIn0, a + p.r0 * w, (size_t)(nr * w));
+        int32_t *dout = reinterpret_cast<int32_t *>(scratch(p.d, kSlotOut, (size_t)nr * 4));
+        if (!da || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_group_sum_i8(p.slot, da, dout, nr, w);
+    });
+}
+
+// a prefix scan: one device (the array as a single row)
+HX_EXPORT int hexcuda_host_scan_max_i8(const int8_t *in, int8_t *out, int64_t n) {
+    if (n < 0) return fail(HEXCUDA_ERR_ARG, "host_scan_max_i8: n %lld", (long long)n);
+    if (n == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_scan_max_i8", {in, out})) return rc;
+    return run_sharded(1, out, (size_t)n, [&](Part &p) {
+        const int8_t *din = stage_in(p.d, kSlotIn0, in, (size_t)n);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)n));
+        if (!din || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_scan_max_i8(p.slot, din, dout, n);
+    });
+}
+
+// groups (each with its H/G head planes) sharded over the devices
+HX_EXPORT int hexcuda_host_head_group_reduce_i8(const int8_t *X, int8_t *Y, int H, int G,
+                                                int64_t MN, int32_t mult, int shift) {
+    if (H < 0 || G < 1 || MN < 0)
+        return fail(HEXCUDA_ERR_ARG, "host_head_group_reduce_i8: H %d G %d MN %lld", H, G,
+                    (long long)MN);
+    if (MN == 0) return HEXCUDA_OK;
+    const int HPG = H / G;
+    if (int rc = null_check("host_head_group_reduce_i8", {HPG ? (const void *)X : Y, Y})) return rc;
+    return run_sharded(G, Y, (size_t)MN, [&](Part &p) {
+        const int64_t ng = p.r1 - p.r0;
+        const int8_t *dx = HPG ? stage_in(p.d, kSlotIn0, X + p.r0 * HPG * MN, (size_t)(ng * HPG * MN))
+                               : nullptr;
+        int8_t *dy = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(ng * MN)));
+        if ((HPG && !dx) || !dy) return hexcuda_last_error();
+        p.dout = dy;
+        // the shard's groups: H' = ng * HPG heads in ng groups
+        return hexcuda_head_group_reduce_i8(p.slot, dx, dy, (int)(ng * HPG), (int)ng, MN, mult,
+                                            shift);
+    });
+}

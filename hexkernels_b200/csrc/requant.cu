@@ -10,6 +10,7 @@
 // All integer, so the device result is bit-identical to the reference.
 #include "hx_internal.h"
 #include "requant.cuh"
+#include "ew_launch.cuh"
 
 namespace hx {
 namespace {
@@ -301,28 +302,6 @@ __global__ void __launch_bounds__(256) relu_i8_kernel(const int8_t *__restrict__
         done = n / 16 * 16;
     }
     for (int64_t i = done + t; i < n; i += stride) out[i] = x[i] > 0 ? x[i] : 0;
-}
-
-// Grid of a grid-stride kernel: enough 256-thread blocks for `work` thread
-// steps, capped at what the device keeps resident at once (blocks per SM from
-// the kernel's register and shared-memory use, cached per kernel and device),
-// so every block runs in the first and only wave.
-template <auto KERN>
-int resident_blocks(const Dev *d, int64_t work) {
-    static int per_sm[64] = {};
-    const int slot = d->ordinal & 63;
-    if (per_sm[slot] == 0) {
-        int nb = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, KERN, 256, 0) != cudaSuccess || nb < 1) {
-            cudaGetLastError();
-            nb = 1;
-        }
-        per_sm[slot] = nb;
-    }
-    int64_t blocks = (work + 255) / 256;
-    const int64_t cap = (int64_t)d->sms * per_sm[slot];
-    if (blocks > cap) blocks = cap;
-    return blocks < 1 ? 1 : (int)blocks;
 }
 
 template <bool A_I8, int B_KIND, int PRE, bool SIGN_OF_A>

@@ -184,6 +184,66 @@ def relu_i8(x) -> np.ndarray:
     return out
 
 
+ELEM = {np.dtype(np.int8): 0, np.dtype(np.uint8): 1, np.dtype(np.int16): 2,
+        np.dtype(np.int32): 3}
+RED_OPS = {"sum": 0, "sum64": 1, "sumsq": 2, "sumsq_diff": 3, "dot": 4, "l1": 5, "absmax": 6,
+           "max": 7, "min": 8, "argmax": 9, "argmin": 10, "top1": 11, "mean": 12}
+
+
+def reduce_int(a, op: str, b=None):
+    """Whole-array integer reduction (hexcuda_host_reduce_int) of an int8,
+    uint8, int16 or int32 array; returns an int, or (max, first index) for
+    "top1"."""
+    a = np.ascontiguousarray(a).ravel()
+    if b is not None:
+        b = _c(b, a.dtype).ravel()
+        assert b.size == a.size
+    out = np.zeros(2, np.int64 if op == "sum64" else np.int32)
+    check(load().hexcuda_host_reduce_int(_p(a), None if b is None else _p(b), ELEM[a.dtype],
+                                         a.size, RED_OPS[op], _p(out)))
+    return (int(out[0]), int(out[1])) if op == "top1" else int(out[0])
+
+
+def minmax_ew(a, b=None, c: int = 0, op: str = "max") -> np.ndarray:
+    """Elementwise max / min of a and b, or of a and the scalar c (b None)."""
+    a = np.ascontiguousarray(a)
+    if b is not None:
+        b = _c(b, a.dtype)
+        assert b.shape == a.shape
+    out = np.empty_like(a)
+    check(load().hexcuda_host_minmax_ew(_p(a), None if b is None else _p(b), int(c), ELEM[a.dtype],
+                                        {"max": 0, "min": 1}[op], _p(out), a.size))
+    return out
+
+
+def group_sum_i8(a, w: int = 4) -> np.ndarray:
+    """out[k] = sum of a[w k : w k + w] (int8 -> int32)."""
+    a = _c(a, np.int8).ravel()
+    g = a.size // w
+    out = np.empty(g, np.int32)
+    check(load().hexcuda_host_group_sum_i8(_p(a), _p(out), g, w))
+    return out
+
+
+def scan_max_i8(x) -> np.ndarray:
+    """Inclusive prefix maximum of an int8 array."""
+    x = _c(x, np.int8).ravel()
+    out = np.empty_like(x)
+    check(load().hexcuda_host_scan_max_i8(_p(x), _p(out), x.size))
+    return out
+
+
+def head_group_reduce_i8(X, G: int, mult: int, shift: int) -> np.ndarray:
+    """Y[g] = sat_i8(round_half_away(sum of the H/G head planes of group g
+    * mult >> shift)); X [H, ...] int8 -> Y [G, ...]."""
+    X = _c(X, np.int8)
+    H = X.shape[0]
+    MN = int(np.prod(X.shape[1:]))
+    Y = np.empty((G,) + X.shape[1:], np.int8)
+    check(load().hexcuda_host_head_group_reduce_i8(_p(X), _p(Y), H, G, MN, int(mult), shift))
+    return Y
+
+
 def attn_qkt_av_hmx(Q, K, V) -> np.ndarray:
     """sx12 field of (sx12 field of Q K^T) V; Q [SQ, D] u8, K / V [SK, D] s8."""
     Q, K, V = _c(Q, np.uint8), _c(K, np.int8), _c(V, np.int8)

@@ -1,0 +1,7 @@
+/* candidate_kernel for i8_sumsq_i32 on the B200 (libhexcuda). */
+#include <stddef.h>
+#include "hexcuda.h"
+#include "kernel_api/i8_sumsq_i32.h"
+void candidate_kernel(const int8_t *a, int n, int32_t *out) {
+    hexcuda_host_reduce_int(a, NULL, HEXCUDA_ELEM_I8, n, HEXCUDA_RED_SUMSQ, out);
+}

@@ -153,6 +153,61 @@ int hexcuda_epilogue_bias_i32(int dev, const int32_t *acc, const int32_t *bias,
 /* out = max(x, 0), int8.  kernels/expert/epilogue_relu_i8/kernel_api.h:13. */
 int hexcuda_relu_i8(int dev, const int8_t *x, int8_t *out, int64_t n);
 
+/* Whole-array integer reductions over n elements of a (and b), one scalar
+ * result.  elem: HEXCUDA_ELEM_I8 / _U8 / _I16 / _I32.  Sums wrap modulo 2^32
+ * like the references' int32 accumulators, SUM64 accumulates in int64:
+ *   SUM       out i32 = sum a[i]             vtcm_reduce_i32 (i32), i8_sum_dma
+ *   SUM64     out i64 = sum a[i]             dma_double_buffer_reduce_i32
+ *   SUMSQ     out i32 = sum a[i]^2           i8_sumsq_i32
+ *   SUMSQ_DIFF out i32 = sum (a[i]-b[i])^2   i8_sumsq_diff_i32
+ *   DOT       out i32 = sum a[i]*b[i]        i8_weighted_sum
+ *   L1        out i32 = sum |a[i]|           i8_l1norm_dma
+ *   ABSMAX    out i32 = max(0, max |a[i]|)   i8_absmax_dma
+ *   MAX / MIN out i32 = max / min a[i]       dma_stream_max_u8 (u8, 0 when n = 0)
+ *   ARGMAX / ARGMIN out i32 = first index of the max / min   i8_argmax_dma, i8_argmin_dma
+ *   TOP1      out i32[2] = {max, first index of it}          i8_top1_reduce_dma
+ *   MEAN      out i32 = (int32 sum) / n, truncated (C /)     i8_mean_dma
+ * (kernels/expert/<bundle>/reference.c).  ARGMAX, ARGMIN, TOP1 and MEAN need
+ * n >= 1 (the references read a[0] / divide by n).  out is a device pointer. */
+#define HEXCUDA_ELEM_I8 0
+#define HEXCUDA_ELEM_U8 1
+#define HEXCUDA_ELEM_I16 2
+#define HEXCUDA_ELEM_I32 3
+#define HEXCUDA_RED_SUM 0
+#define HEXCUDA_RED_SUM64 1
+#define HEXCUDA_RED_SUMSQ 2
+#define HEXCUDA_RED_SUMSQ_DIFF 3
+#define HEXCUDA_RED_DOT 4
+#define HEXCUDA_RED_L1 5
+#define HEXCUDA_RED_ABSMAX 6
+#define HEXCUDA_RED_MAX 7
+#define HEXCUDA_RED_MIN 8
+#define HEXCUDA_RED_ARGMAX 9
+#define HEXCUDA_RED_ARGMIN 10
+#define HEXCUDA_RED_TOP1 11
+#define HEXCUDA_RED_MEAN 12
+int hexcuda_reduce_int(int dev, const void *a, const void *b, int elem, int64_t n, int op,
+                       void *out);
+
+/* Elementwise max (op 0) or min (op 1) of a[i] and b[i], or of a[i] and the
+ * scalar c when b is null: hvx_vmax_i8, hvx_vmax_u8, hvx_vmin_i16,
+ * hvx_vmin_u8, i8_max_scalar_dma, i8_min_scalar_dma.  elem I8, U8 or I16. */
+int hexcuda_minmax_ew(int dev, const void *a, const void *b, int32_t c, int elem, int op,
+                      void *out, int64_t n);
+
+/* out[k] = sum_{j < w} a[w k + j] for k < g (int8 -> int32), w >= 1:
+ * hvx_vradd_i8_reduce (w = 4). */
+int hexcuda_group_sum_i8(int dev, const int8_t *a, int32_t *out, int64_t g, int w);
+
+/* Inclusive prefix maximum, out[i] = max(-128, in[0..i]): i8_scan_max. */
+int hexcuda_scan_max_i8(int dev, const int8_t *in, int8_t *out, int64_t n);
+
+/* Head-group reduce: Y[g][i] = sat_i8(round_half_away(sum_{t < H/G}
+ * X[g H/G + t][i] * mult >> shift)) for g < G, i < MN: gqa_group_reduce_i8
+ * (reference.c: sum of the group's head planes, requant, clamp). */
+int hexcuda_head_group_reduce_i8(int dev, const int8_t *X, int8_t *Y, int H, int G,
+                                 int64_t MN, int32_t mult, int shift);
+
 /* int8 GEMM + requant: A [M,K] s8, B [K,N] s8 row-major, out [M,N] s8.
  * kernels/expert/i8_gemm_requant/kernel_api.h:4-11. */
 int hexcuda_gemm_i8_requant(int dev, const int8_t *A, const int8_t *B, int8_t *out,
@@ -398,6 +453,17 @@ int hexcuda_host_requant_ew(const void *a, int a_i8, const void *b, int b_kind, 
 int hexcuda_host_epilogue_bias_i32(const int32_t *acc, const int32_t *bias, int32_t *out,
                                    int R, int C);
 int hexcuda_host_relu_i8(const int8_t *x, int8_t *out, int64_t n);
+/* out is a HOST pointer here (the result type of the op, as above); the
+ * array is split over the devices and the partial results combined. */
+int hexcuda_host_reduce_int(const void *a, const void *b, int elem, int64_t n, int op,
+                            void *out);
+int hexcuda_host_minmax_ew(const void *a, const void *b, int32_t c, int elem, int op,
+                           void *out, int64_t n);
+int hexcuda_host_group_sum_i8(const int8_t *a, int32_t *out, int64_t g, int w);
+/* on the first device only (a prefix scan) */
+int hexcuda_host_scan_max_i8(const int8_t *in, int8_t *out, int64_t n);
+int hexcuda_host_head_group_reduce_i8(const int8_t *X, int8_t *Y, int H, int G, int64_t MN,
+                                      int32_t mult, int shift);
 int hexcuda_host_gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out,
                                  int M, int N, int K, int32_t mult, int shift,
                                  int8_t zp);

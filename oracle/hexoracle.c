@@ -868,3 +868,129 @@ int oracle_parallel(int op, const void *args, int r0, int r1, int nthreads) {
     free(jobs);
     return rc;
 }
+
+/* ------------------------------------------------ integer reductions
+ * One left-to-right pass per op, as the references:
+ *   SUM    vtcm_reduce_i32/reference.c:5-9, i8_sum_dma/reference.c:4-8
+ *   SUM64  dma_double_buffer_reduce_i32/reference.c:5-9
+ *   SUMSQ  i8_sumsq_i32/reference.c:2-4;  SUMSQ_DIFF i8_sumsq_diff_i32/reference.c:2-9
+ *   DOT    i8_weighted_sum/reference.c:2-6;  L1 i8_l1norm_dma/reference.c:6-10
+ *   ABSMAX i8_absmax_dma/reference.c:6-13;  MAX dma_stream_max_u8/reference.c:5-9
+ *   ARGMAX / ARGMIN i8_argmax_dma/reference.c:6-13, i8_argmin_dma/reference.c:6-13
+ *   TOP1   i8_top1_reduce_dma/reference.c:8-16;  MEAN i8_mean_dma/reference.c:6-10
+ * The int32 accumulations are done on uint32 (the references' signed int32
+ * overflow, defined here as the two's-complement wrap). */
+static int64_t red_elem_at(const void *a, int elem, int64_t i) {
+    switch (elem) {
+    case ORACLE_ELEM_I8: return ((const int8_t *)a)[i];
+    case ORACLE_ELEM_U8: return ((const uint8_t *)a)[i];
+    case ORACLE_ELEM_I16: return ((const int16_t *)a)[i];
+    default: return ((const int32_t *)a)[i];
+    }
+}
+
+void oracle_reduce_int(const void *a, const void *b, int elem, int64_t n, int op, void *out) {
+    int32_t *o32 = (int32_t *)out;
+    uint32_t s = 0;
+    int64_t s64 = 0;
+    if (op == ORACLE_RED_ARGMAX || op == ORACLE_RED_ARGMIN || op == ORACLE_RED_TOP1) {
+        int64_t bv = red_elem_at(a, elem, 0), bi = 0;
+        for (int64_t i = 1; i < n; i++) {
+            const int64_t x = red_elem_at(a, elem, i);
+            if (op == ORACLE_RED_ARGMIN ? x < bv : x > bv) {
+                bv = x;
+                bi = i;
+            }
+        }
+        if (op == ORACLE_RED_TOP1) {
+            o32[0] = (int32_t)bv;
+            o32[1] = (int32_t)bi;
+        } else {
+            o32[0] = (int32_t)bi;
+        }
+        return;
+    }
+    if (op == ORACLE_RED_MAX || op == ORACLE_RED_MIN || op == ORACLE_RED_ABSMAX) {
+        int64_t m = 0;
+        for (int64_t i = 0; i < n; i++) {
+            int64_t x = red_elem_at(a, elem, i);
+            if (op == ORACLE_RED_ABSMAX) x = x < 0 ? -x : x;
+            if (i == 0 && op != ORACLE_RED_ABSMAX) m = x;
+            else if (op == ORACLE_RED_MIN ? x < m : x > m) m = x;
+        }
+        o32[0] = (int32_t)m;
+        return;
+    }
+    for (int64_t i = 0; i < n; i++) {
+        const int64_t x = red_elem_at(a, elem, i);
+        const int64_t y = (op == ORACLE_RED_SUMSQ_DIFF || op == ORACLE_RED_DOT)
+                              ? red_elem_at(b, elem, i) : 0;
+        switch (op) {
+        case ORACLE_RED_SUM64: s64 += x; break;
+        case ORACLE_RED_SUMSQ: s += (uint32_t)x * (uint32_t)x; break;
+        case ORACLE_RED_SUMSQ_DIFF: {
+            const uint32_t d = (uint32_t)(x - y);
+            s += d * d;
+            break;
+        }
+        case ORACLE_RED_DOT: s += (uint32_t)x * (uint32_t)y; break;
+        case ORACLE_RED_L1: s += (uint32_t)(x < 0 ? -x : x); break;
+        default: s += (uint32_t)x; break;   /* SUM, MEAN */
+        }
+    }
+    if (op == ORACLE_RED_SUM64) *(int64_t *)out = s64;
+    else if (op == ORACLE_RED_MEAN) o32[0] = (int32_t)((int64_t)(int32_t)s / n);
+    else o32[0] = (int32_t)s;
+}
+
+/* hvx_vmax_i8/reference.c:3-6, hvx_vmax_u8/reference.c:3-6,
+ * hvx_vmin_i16/reference.c:3-6, hvx_vmin_u8/reference.c:3-6,
+ * i8_max_scalar_dma/reference.c:6-11, i8_min_scalar_dma/reference.c:6-11 */
+void oracle_minmax_ew(const void *a, const void *b, int32_t c, int elem, int op, void *out,
+                      int64_t n) {
+    for (int64_t i = 0; i < n; i++) {
+        const int64_t x = red_elem_at(a, elem, i);
+        int64_t y = b ? red_elem_at(b, elem, i) : 0;
+        if (!b) {   /* the scalar in the element's own type */
+            if (elem == ORACLE_ELEM_I8) y = (int8_t)c;
+            else if (elem == ORACLE_ELEM_U8) y = (uint8_t)c;
+            else y = (int16_t)c;
+        }
+        const int64_t r = op ? (x < y ? x : y) : (x > y ? x : y);
+        if (elem == ORACLE_ELEM_I16) ((int16_t *)out)[i] = (int16_t)r;
+        else ((uint8_t *)out)[i] = (uint8_t)r;
+    }
+}
+
+/* hvx_vradd_i8_reduce/reference.c:3-10 with the group width a parameter */
+void oracle_group_sum_i8(const int8_t *a, int32_t *out, int64_t g, int w) {
+    for (int64_t k = 0; k < g; k++) {
+        uint32_t s = 0;
+        for (int j = 0; j < w; j++) s += (uint32_t)(int32_t)a[k * w + j];
+        out[k] = (int32_t)s;
+    }
+}
+
+/* i8_scan_max/reference.c:2-8 */
+void oracle_scan_max_i8(const int8_t *in, int8_t *out, int64_t n) {
+    int8_t cur = -128;
+    for (int64_t i = 0; i < n; i++) {
+        if (in[i] > cur) cur = in[i];
+        out[i] = cur;
+    }
+}
+
+/* gqa_group_reduce_i8/reference.c:6-26 */
+void oracle_head_group_reduce_i8(const int8_t *X, int8_t *Y, int H, int G, int64_t MN,
+                                 int32_t mult, int shift) {
+    const int hpg = H / G;
+    for (int g = 0; g < G; g++)
+        for (int64_t i = 0; i < MN; i++) {
+            int32_t acc = 0;
+            for (int t = 0; t < hpg; t++) acc += X[(int64_t)(g * hpg + t) * MN + i];
+            int64_t q = rq_round((int64_t)acc * (int64_t)mult, shift);
+            if (q > 127) q = 127;
+            if (q < -128) q = -128;
+            Y[(int64_t)g * MN + i] = (int8_t)q;
+        }
+}

@@ -245,6 +245,30 @@ void oracle_rowreduce_f32_rows(const float *x, float *out, int R, int C,
                                int op, int r0, int r1);
 
 /* ---- threaded drivers: split [0, rows) into nthreads contiguous blocks ---- */
+/* Whole-array integer reductions, each a plain left-to-right scan as in
+ * kernels/expert/<bundle>/reference.c (int32 sums wrap modulo 2^32, the
+ * references' signed int32 accumulators on a two's-complement machine):
+ * elem ORACLE_ELEM_*, op ORACLE_RED_* (same numbering as hexcuda.h's
+ * HEXCUDA_ELEM_* / HEXCUDA_RED_*).  out: int32[1], int64[1] (SUM64) or
+ * int32[2] (TOP1). */
+enum { ORACLE_ELEM_I8 = 0, ORACLE_ELEM_U8 = 1, ORACLE_ELEM_I16 = 2, ORACLE_ELEM_I32 = 3 };
+enum {
+    ORACLE_RED_SUM = 0, ORACLE_RED_SUM64, ORACLE_RED_SUMSQ, ORACLE_RED_SUMSQ_DIFF, ORACLE_RED_DOT,
+    ORACLE_RED_L1, ORACLE_RED_ABSMAX, ORACLE_RED_MAX, ORACLE_RED_MIN, ORACLE_RED_ARGMAX,
+    ORACLE_RED_ARGMIN, ORACLE_RED_TOP1, ORACLE_RED_MEAN
+};
+void oracle_reduce_int(const void *a, const void *b, int elem, int64_t n, int op, void *out);
+/* out[i] = max / min (op 0 / 1) of a[i] and b[i], or of a[i] and c (b null). */
+void oracle_minmax_ew(const void *a, const void *b, int32_t c, int elem, int op, void *out,
+                      int64_t n);
+/* out[k] = sum_{j < w} a[w k + j] (hvx_vradd_i8_reduce/reference.c, w = 4). */
+void oracle_group_sum_i8(const int8_t *a, int32_t *out, int64_t g, int w);
+/* inclusive prefix max from -128 (i8_scan_max/reference.c). */
+void oracle_scan_max_i8(const int8_t *in, int8_t *out, int64_t n);
+/* gqa_group_reduce_i8/reference.c: sum of a group's H/G head planes, requant. */
+void oracle_head_group_reduce_i8(const int8_t *X, int8_t *Y, int H, int G, int64_t MN,
+                                 int32_t mult, int shift);
+
 enum {
     ORACLE_OP_I8_GEMM_REQUANT = 1,
     ORACLE_OP_GEMM_U8S8_PC = 2,

@@ -392,3 +392,53 @@ def rows_args(**kw) -> _RowsArgs:
     for k, v in kw.items():
         setattr(a, k, _p(v) if isinstance(v, np.ndarray) else v)
     return a
+
+
+ELEM = {np.dtype(np.int8): 0, np.dtype(np.uint8): 1, np.dtype(np.int16): 2,
+        np.dtype(np.int32): 3}
+RED_OPS = {"sum": 0, "sum64": 1, "sumsq": 2, "sumsq_diff": 3, "dot": 4, "l1": 5, "absmax": 6,
+           "max": 7, "min": 8, "argmax": 9, "argmin": 10, "top1": 11, "mean": 12}
+
+
+def reduce_int(a, op, b=None):
+    a = np.ascontiguousarray(a).ravel()
+    if b is not None:
+        b = np.ascontiguousarray(b, a.dtype).ravel()
+    out = np.zeros(2, np.int64 if op == "sum64" else np.int32)
+    lib().oracle_reduce_int(_p(a), _p(b) if b is not None else None, ELEM[a.dtype],
+                            C.c_int64(a.size), RED_OPS[op], _p(out))
+    return (int(out[0]), int(out[1])) if op == "top1" else int(out[0])
+
+
+def minmax_ew(a, b=None, c=0, op="max"):
+    a = np.ascontiguousarray(a)
+    out = np.zeros_like(a)
+    lib().oracle_minmax_ew(_p(a), _p(np.ascontiguousarray(b, a.dtype)) if b is not None else None,
+                           C.c_int32(int(c)), ELEM[a.dtype], {"max": 0, "min": 1}[op], _p(out),
+                           C.c_int64(a.size))
+    return out
+
+
+def group_sum_i8(a, w=4):
+    a = np.ascontiguousarray(a, np.int8).ravel()
+    g = a.size // w
+    out = np.zeros(g, np.int32)
+    lib().oracle_group_sum_i8(_p(a), _p(out), C.c_int64(g), w)
+    return out
+
+
+def scan_max_i8(x):
+    x = np.ascontiguousarray(x, np.int8).ravel()
+    out = np.zeros_like(x)
+    lib().oracle_scan_max_i8(_p(x), _p(out), C.c_int64(x.size))
+    return out
+
+
+def head_group_reduce_i8(X, G, mult, shift):
+    X = np.ascontiguousarray(X, np.int8)
+    H = X.shape[0]
+    MN = int(np.prod(X.shape[1:]))
+    Y = np.zeros((G,) + X.shape[1:], np.int8)
+    lib().oracle_head_group_reduce_i8(_p(X), _p(Y), H, G, C.c_int64(MN), C.c_int32(int(mult)),
+                                      shift)
+    return Y

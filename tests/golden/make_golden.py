@@ -771,6 +771,39 @@ def gen_mined_fp32_sum():
          knu=np.array([float.fromhex(knu.strip().rstrip("f"))], np.float32))
 
 
+def gen_reduce_family(ref):
+    # The integer reduction bundles of tests/reduce_family.py run through
+    # their own reference.c on seeded full-range inputs (vtcm_reduce_i32:
+    # |a| < 2^18, so the reference's signed int32 sum stays defined), four
+    # sizes each (1, 17, 1000 and 4099 elements; g = 1, 17, 250 and 1025
+    # groups for the 4-wide group sum), the arg reductions with their
+    # extreme planted at three positions; gqa_group_reduce_i8 on three
+    # shapes (H, G, M, N) = (8, 2, 5, 33), (12, 3, 4, 16), (7, 2, 3, 3).
+    sys.path.insert(0, str(HERE.parent))
+    from reduce_family import RD_BUNDLES, ctypes_args, make_inputs, out_buffer
+    rng = np.random.default_rng(83)
+    arrays = {}
+    for b, (params, dt, kind) in RD_BUNDLES.items():
+        if kind[0] == "gqa":
+            cases = []
+            for H, G, M, N in ((8, 2, 5, 33), (12, 3, 4, 16), (7, 2, 3, 3)):
+                arr = make_inputs(b, rng, 0)
+                arr.update(H=H, G=G, M=M, N=N,
+                           X=rng.integers(-128, 128, H * M * N).astype(np.int8))
+                cases.append(arr)
+        else:
+            sizes = (4, 68, 1000, 4100) if kind[0] == "group_sum" else (1, 17, 1000, 4099)
+            cases = [make_inputs(b, rng, n) for n in sizes]
+        for ci, arr in enumerate(cases):
+            out = out_buffer(b, arr)
+            getattr(ref, "ref_" + b)(*ctypes_args(b, arr, out))
+            key = f"{b}__c{ci}__"
+            for k, v in arr.items():
+                arrays[key + k] = np.asarray(v)
+            arrays[key + "out"] = out
+    save("reduce_family", **arrays)
+
+
 def main():
     if not (REF_ROOT / "kernels").is_dir():
         sys.exit(f"reference tree not found at {REF_ROOT}")
@@ -789,6 +822,7 @@ def main():
     gen_int8_attention_blocks(ref)
     gen_f16_family(ref)
     gen_i8_callers(ref)
+    gen_reduce_family(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

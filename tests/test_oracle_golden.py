@@ -310,3 +310,21 @@ def i8_callers_calls(impl, g):
 def test_i8_callers_golden(oracle):
     for got, exp in i8_callers_calls(oracle, golden("i8_callers")):
         np.testing.assert_array_equal(got, exp)
+
+
+from reduce_family import golden_case as rd_case, golden_cases as rd_cases, library_call  # noqa: E402
+
+RD_CASES = rd_cases(golden("reduce_family"))
+
+
+@pytest.mark.parametrize("bundle,case", RD_CASES)
+def test_reduce_family_golden(oracle, bundle, case):
+    """The oracle's integer reductions, elementwise max / min, group sums,
+    prefix max and head-group reduce reproduce each bundle's reference.c."""
+    arr = rd_case(golden("reduce_family"), bundle, case)
+    np.testing.assert_array_equal(library_call(oracle, bundle, arr), arr["out"])
+
+
+def test_reduce_family_covers_every_bundle():
+    from reduce_family import RD_BUNDLES
+    assert {b for b, _ in RD_CASES} == set(RD_BUNDLES)

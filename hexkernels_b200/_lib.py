@@ -60,7 +60,9 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_gemm_i8_zp": (I, [I, P, P, P, I, I, I, I32, I32, I]),
     "hexcuda_gemm_u8s8_pc": (I, [I, P, P, P, P, I, I, I, I32, P, P, U8]),
     "hexcuda_gemm_hmx": (I, [I, P, P, I, P, P, I, I, I, I, I32]),
-    "hexcuda_gemm_i8_rq_ex": (I, [I, P, P, I, P, P, I, I, I, I32, I, I8, I]),
+    "hexcuda_gemm_i8_rq_ex": (I, [I, P, P, I, P, P, P, I, I, I, I32, I, I8, I]),
+    "hexcuda_gemm_i8_acc": (I, [I, P, I, P, I, P, P, I, P, P, I, I, I, I, I]),
+    "hexcuda_ffn_relu_i8": (I, [I, P, P, P, P, P, P, I, I, I, I, I32, I, I8]),
     "hexcuda_gemm_hmx_s8u8": (I, [I, P, P, P, I, I, I, I]),
     "hexcuda_gemm_f16_ex": (I, [I, P, P, I, P, P, P, I, I, F, I, I, I]),
     "hexcuda_attn_lut_i8": (I, [I, I, P, P, P, P, P, P, I, P, I, I, I, I, I32, I, I32, I]),
@@ -95,7 +97,9 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_gemm_i8_zp": (I, [P, P, P, I, I, I, I32, I32, I]),
     "hexcuda_host_gemm_u8s8_pc": (I, [P, P, P, P, I, I, I, I32, P, P, U8]),
     "hexcuda_host_gemm_hmx": (I, [P, P, I, P, P, I, I, I, I, I32]),
-    "hexcuda_host_gemm_i8_rq_ex": (I, [P, P, I, P, P, I, I, I, I32, I, I8, I]),
+    "hexcuda_host_gemm_i8_rq_ex": (I, [P, P, I, P, P, P, I, I, I, I32, I, I8, I]),
+    "hexcuda_host_gemm_i8_acc": (I, [P, I, P, I, P, P, I, P, P, I, I, I, I, I]),
+    "hexcuda_host_ffn_relu_i8": (I, [P, P, P, P, P, P, I, I, I, I, I32, I, I8]),
     "hexcuda_host_gemm_hmx_s8u8": (I, [P, P, P, I, I, I, I]),
     "hexcuda_host_gemm_f16_ex": (I, [P, P, I, P, P, P, I, I, F, I, I, I]),
     "hexcuda_host_attn_lut_i8": (I, [I, P, P, P, P, P, P, I, P, I, I, I, I, I32, I, I32, I]),

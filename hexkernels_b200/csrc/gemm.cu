@@ -79,6 +79,13 @@ struct EpiParams {
     int hmx_store, hmx_act, res_kind, col_major;
     const void *res;
     const void *lut;
+    // hmx_raw: the raw accumulator instead of the sx12 field, with the bias,
+    // residual and activation in int64 before the store's saturation (the
+    // int8 GEMM callers that widen to int64 before they saturate)
+    int hmx_raw;
+    // requant epilogue: int8 residual [M, N] added with int8 saturation
+    // after the requant's clamp (null: none)
+    const int8_t *rq_res;
     // fp16 post-ops (kEpiF16Ex), in the corpus's order: v = acc + res[i][j]
     // (fp16 [M, N] or null) + bias[j] (fp16 or null); preround: v = fp16(v);
     // activation (HEXCUDA_F16_ACT_*); v *= scale; out = fp16(v)
@@ -197,11 +204,12 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
         for (int i = 0; i < 32; i++) {
             const int j = col0 + i;
             float v = __uint_as_float(r[i]);
+            if (ep.f16_preround == HEXCUDA_F16_PREROUND_ACC) v = __half2float(__float2half_rn(v));
             if (j < ep.N) {
                 if (rr) v += __half2float(rr[i]);
                 if (ep.f16_bias) v += __half2float(ep.f16_bias[j]);
             }
-            if (ep.f16_preround) v = __half2float(__float2half_rn(v));
+            if (ep.f16_preround == HEXCUDA_F16_PREROUND_SUM) v = __half2float(__float2half_rn(v));
             if (ep.f16_act == HEXCUDA_F16_ACT_RELU) {
                 v = v > 0.0f ? v : 0.0f;
             } else if (ep.f16_act == HEXCUDA_F16_ACT_LEAKY) {
@@ -209,6 +217,10 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             } else if (ep.f16_act == HEXCUDA_F16_ACT_GELU) {
                 const float c = 0.7978845608f * (v + 0.044715f * v * v * v);
                 v = 0.5f * v * (1.0f + tanhf(c));
+            } else if (ep.f16_act == HEXCUDA_F16_ACT_SIGMOID) {
+                v = 1.0f / (1.0f + expf(-v));
+            } else if (ep.f16_act == HEXCUDA_F16_ACT_TANH) {
+                v = tanhf(v);
             }
             hv[i] = __float2half_rn(v * ep.f16_scale);
         }
@@ -253,6 +265,27 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
 #pragma unroll
             for (int u = 0; u < 4; u++) {
                 const uint32_t a32 = r[4 * i4 + u] - (uint32_t)cc[u];
+                if (ep.hmx_raw) {
+                    int64_t x = (int64_t)(int32_t)a32 + bb[u] + rv[4 * i4 + u];
+                    if (ep.hmx_act == HEXCUDA_HMX_ACT_RELU) x = x > 0 ? x : 0;
+                    else if (ep.hmx_act == HEXCUDA_HMX_ACT_LEAKY_SHR3) x = x >= 0 ? x : (x >> 3);
+                    switch (ep.hmx_store) {
+                    case HEXCUDA_HMX_STORE_I8_SAT: x = x > 127 ? 127 : (x < -128 ? -128 : x); break;
+                    case HEXCUDA_HMX_STORE_U8_SAT: x = x > 255 ? 255 : (x < 0 ? 0 : x); break;
+                    case HEXCUDA_HMX_STORE_U16_FIELD: x &= 0xFFF; break;
+                    case HEXCUDA_HMX_STORE_LUT_I32:
+                        x = __ldg(reinterpret_cast<const int32_t *>(ep.lut) +
+                                  (x + 128 > 255 ? 255 : (x + 128 < 0 ? 0 : x + 128)));
+                        break;
+                    case HEXCUDA_HMX_STORE_LUT_I8:
+                        x = __ldg(reinterpret_cast<const int8_t *>(ep.lut) +
+                                  ((x > 127 ? 127 : (x < -128 ? -128 : x)) + 128));
+                        break;
+                    default: break;
+                    }
+                    v[4 * i4 + u] = (int32_t)x;
+                    continue;
+                }
                 const int32_t f = (int32_t)(a32 * 17u + 8u) >> 4;
                 uint32_t xu = (uint32_t)((int32_t)((uint32_t)f << 20) >> 20);  // sx12
                 if (ep.hmx_store == HEXCUDA_HMX_STORE_ACC_I32) xu = a32;     // raw accumulator
@@ -340,6 +373,17 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
         else
             requant_chunk<false>(ep, r, cp, w);
         if (row >= ep.M) return;
+        if (ep.rq_res) {
+            // q = sat8(q + res[i][j]): one signed saturating byte add per 4
+            const int8_t *rp = ep.rq_res + (size_t)row * ep.N + col0;
+#pragma unroll
+            for (int i4 = 0; i4 < 8; i4++) {
+                uint32_t rw = 0;
+                for (int u = 0; u < 4 && col0 + 4 * i4 + u < ep.N; u++)
+                    rw |= (uint32_t)(uint8_t)__ldg(rp + 4 * i4 + u) << (8 * u);
+                w[i4] = __vaddss4(w[i4], rw);
+            }
+        }
         if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
             uint4 *dst = reinterpret_cast<uint4 *>(o);
             dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -1306,29 +1350,81 @@ HX_EXPORT int hexcuda_gemm_u8s8_pc(int dev, const uint8_t *A, const int8_t *B, c
 HX_EXPORT int hexcuda_gemm_f16_ex(int dev, const uint16_t *A, const uint16_t *B, int b_transposed,
                                   const uint16_t *bias, const uint16_t *res, uint16_t *out, int act,
                                   int preround, float scale, int M, int N, int K) {
-    if (act < HEXCUDA_F16_ACT_NONE || act > HEXCUDA_F16_ACT_GELU)
+    if (act < HEXCUDA_F16_ACT_NONE || act > HEXCUDA_F16_ACT_TANH)
         return fail(HEXCUDA_ERR_ARG, "gemm_f16_ex: activation %d", act);
+    if (preround < HEXCUDA_F16_PREROUND_NONE || preround > HEXCUDA_F16_PREROUND_ACC)
+        return fail(HEXCUDA_ERR_ARG, "gemm_f16_ex: preround %d", preround);
     EpiParams ep{};
     ep.out = out;
     ep.ldo = N;
     ep.f16_bias = reinterpret_cast<const __half *>(bias);
     ep.f16_res = reinterpret_cast<const __half *>(res);
     ep.f16_act = act;
-    ep.f16_preround = preround ? 1 : 0;
+    ep.f16_preround = preround;
     ep.f16_scale = scale;
     return run_gemm<MmaKind::F16, kEpiF16Ex, false, false>(dev, A, K, B, b_transposed != 0, M, N, K,
                                                            ep, false, "gemm_f16_ex");
 }
 
 HX_EXPORT int hexcuda_gemm_i8_rq_ex(int dev, const int8_t *A, const int8_t *B, int b_transposed,
-                                    const int32_t *bias, int8_t *out, int M, int N, int K,
-                                    int32_t mult, int shift, int8_t zp, int relu) {
+                                    const int32_t *bias, const int8_t *res, int8_t *out, int M,
+                                    int N, int K, int32_t mult, int shift, int8_t zp, int relu) {
     if (shift < 0 || shift > 63) return fail(HEXCUDA_ERR_ARG, "gemm_i8_rq_ex: shift %d", shift);
     EpiParams ep = requant_epi(out, N, mult, shift, zp, -128, 127);
     ep.bias = bias;
     ep.relu_pre = relu ? 1 : 0;
+    ep.rq_res = res;
     return run_gemm<MmaKind::I8, kEpiRequant, true, true>(dev, A, K, B, b_transposed != 0, M, N, K,
                                                           ep, false, "gemm_i8_rq_ex");
+}
+
+HX_EXPORT int hexcuda_gemm_i8_acc(int dev, const void *A, int a_signed, const int8_t *B,
+                                  int b_transposed, const int32_t *bias, const void *res,
+                                  int res_kind, const void *lut, void *out, int store, int act,
+                                  int M, int N, int K) {
+    if (store < HEXCUDA_HMX_STORE_I32 || store > HEXCUDA_HMX_STORE_ACC_I32)
+        return fail(HEXCUDA_ERR_ARG, "gemm_i8_acc: store kind %d", store);
+    if (act < HEXCUDA_HMX_ACT_NONE || act > HEXCUDA_HMX_ACT_LEAKY_SHR3)
+        return fail(HEXCUDA_ERR_ARG, "gemm_i8_acc: activation %d", act);
+    if (res_kind < HEXCUDA_HMX_RES_NONE || res_kind > HEXCUDA_HMX_RES_I8 || (res_kind && !res))
+        return fail(HEXCUDA_ERR_ARG, "gemm_i8_acc: residual kind %d", res_kind);
+    if ((store == HEXCUDA_HMX_STORE_LUT_I32 || store == HEXCUDA_HMX_STORE_LUT_I8) && !lut)
+        return fail(HEXCUDA_ERR_ARG, "gemm_i8_acc: table store without a table");
+    EpiParams ep{};
+    ep.out = out;
+    ep.ldo = N;
+    ep.bias = bias;
+    ep.res = res;
+    ep.res_kind = res_kind;
+    ep.lut = lut;
+    ep.hmx_store = store;
+    ep.hmx_act = act;
+    ep.hmx_raw = 1;
+    if (a_signed)
+        return run_gemm<MmaKind::I8, kEpiHmx, true, true>(dev, A, K, B, b_transposed != 0, M, N, K,
+                                                          ep, false, "gemm_i8_acc");
+    return run_gemm<MmaKind::I8, kEpiHmx, false, true>(dev, A, K, B, b_transposed != 0, M, N, K, ep,
+                                                       false, "gemm_i8_acc");
+}
+
+// scratch slot of the FFN's hidden activations (device entries own 0..7)
+constexpr int kSlotFfnHidden = 19;
+
+HX_EXPORT int hexcuda_ffn_relu_i8(int dev, const int8_t *A, const int8_t *W1, const int32_t *b1,
+                                  const int8_t *W2, const int32_t *b2, int8_t *out, int M, int K,
+                                  int V, int D, int32_t mult, int shift, int8_t zp) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (M < 0 || K < 0 || V < 0 || D < 0) return fail(HEXCUDA_ERR_ARG, "ffn_relu_i8: bad shape");
+    if (M == 0 || D == 0) return HEXCUDA_OK;
+    int8_t *hid = reinterpret_cast<int8_t *>(scratch(d, kSlotFfnHidden, (size_t)M * (V > 0 ? V : 1)));
+    if (!hid) return HEXCUDA_ERR_OOM;
+    if (V > 0) {
+        if (int rc = hexcuda_gemm_i8_acc(dev, A, 1, W1, 0, b1, nullptr, HEXCUDA_HMX_RES_NONE, nullptr,
+                                         hid, HEXCUDA_HMX_STORE_I8_SAT, HEXCUDA_HMX_ACT_RELU, M, V, K))
+            return rc;
+    }
+    return hexcuda_gemm_i8_rq_ex(dev, hid, W2, 0, b2, nullptr, out, M, D, V, mult, shift, zp, 0);
 }
 
 HX_EXPORT int hexcuda_gemm_hmx_s8u8(int dev, const int8_t *A, const uint8_t *B, void *out, int store,

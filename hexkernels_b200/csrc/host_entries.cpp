@@ -626,8 +626,9 @@ HX_EXPORT int hexcuda_host_gemm_f16_ex(const uint16_t *A, const uint16_t *B, int
 }
 
 HX_EXPORT int hexcuda_host_gemm_i8_rq_ex(const int8_t *A, const int8_t *B, int b_transposed,
-                                         const int32_t *bias, int8_t *out, int M, int N, int K,
-                                         int32_t mult, int shift, int8_t zp, int relu) {
+                                         const int32_t *bias, const int8_t *res, int8_t *out,
+                                         int M, int N, int K, int32_t mult, int shift, int8_t zp,
+                                         int relu) {
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_i8_rq_ex: bad shape");
     if (M == 0 || N == 0) return HEXCUDA_OK;
     if (int rc = null_check("host_gemm_i8_rq_ex", {A, B, out})) return rc;
@@ -636,11 +637,71 @@ HX_EXPORT int hexcuda_host_gemm_i8_rq_ex(const int8_t *A, const int8_t *B, int b
         const int8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
         const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
         const int32_t *db = bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
+        const int8_t *dr = res ? stage_in(p.d, kSlotIn3, res + p.r0 * N, (size_t)(nr * N)) : nullptr;
         int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * N)));
-        if (!dA || !dB || (bias && !db) || !dout) return hexcuda_last_error();
+        if (!dA || !dB || (bias && !db) || (res && !dr) || !dout) return hexcuda_last_error();
         p.dout = dout;
-        return hexcuda_gemm_i8_rq_ex(p.slot, dA, dB, b_transposed, db, dout, (int)nr, N, K, mult,
-                                     shift, zp, relu);
+        return hexcuda_gemm_i8_rq_ex(p.slot, dA, dB, b_transposed, db, dr, dout, (int)nr, N, K,
+                                     mult, shift, zp, relu);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gemm_i8_acc(const void *A, int a_signed, const int8_t *B,
+                                      int b_transposed, const int32_t *bias, const void *res,
+                                      int res_kind, const void *lut, void *out, int store, int act,
+                                      int M, int N, int K) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_i8_acc: bad shape");
+    if (store < HEXCUDA_HMX_STORE_I32 || store > HEXCUDA_HMX_STORE_ACC_I32 ||
+        res_kind < HEXCUDA_HMX_RES_NONE || res_kind > HEXCUDA_HMX_RES_I8)
+        return fail(HEXCUDA_ERR_ARG, "host_gemm_i8_acc: store %d / residual %d", store, res_kind);
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_i8_acc", {A, B, out})) return rc;
+    const bool has_lut = store == HEXCUDA_HMX_STORE_LUT_I32 || store == HEXCUDA_HMX_STORE_LUT_I8;
+    const size_t osize = (store == HEXCUDA_HMX_STORE_I32 || store == HEXCUDA_HMX_STORE_LUT_I32 ||
+                          store == HEXCUDA_HMX_STORE_ACC_I32) ? 4
+                         : store == HEXCUDA_HMX_STORE_U16_FIELD ? 2 : 1;
+    const size_t rsize = res_kind == HEXCUDA_HMX_RES_I32 ? 4 : 1;
+    return run_sharded(M, out, (size_t)N * osize, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const uint8_t *dA = stage_in(p.d, kSlotIn0, reinterpret_cast<const uint8_t *>(A) + p.r0 * K,
+                                     (size_t)(nr * K));
+        const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        const int32_t *db = bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
+        const uint8_t *dr = res_kind ? stage_in(p.d, kSlotIn3,
+                                                reinterpret_cast<const uint8_t *>(res) +
+                                                    (size_t)p.r0 * N * rsize,
+                                                (size_t)(nr * N) * rsize)
+                                     : nullptr;
+        const uint8_t *dl = has_lut ? stage_in(p.d, kSlotIn4, reinterpret_cast<const uint8_t *>(lut),
+                                               store == HEXCUDA_HMX_STORE_LUT_I32 ? 1024 : 256)
+                                    : nullptr;
+        void *dout = scratch(p.d, kSlotOut, (size_t)(nr * N) * osize);
+        if (!dA || !dB || (bias && !db) || (res_kind && !dr) || (has_lut && !dl) || !dout)
+            return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_i8_acc(p.slot, dA, a_signed, dB, b_transposed, db, dr, res_kind, dl,
+                                   dout, store, act, (int)nr, N, K);
+    });
+}
+
+HX_EXPORT int hexcuda_host_ffn_relu_i8(const int8_t *A, const int8_t *W1, const int32_t *b1,
+                                      const int8_t *W2, const int32_t *b2, int8_t *out, int M,
+                                      int K, int V, int D, int32_t mult, int shift, int8_t zp) {
+    if (M < 0 || K < 0 || V < 0 || D < 0) return fail(HEXCUDA_ERR_ARG, "host_ffn_relu_i8: bad shape");
+    if (M == 0 || D == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_ffn_relu_i8", {A, W1, b1, W2, b2, out})) return rc;
+    return run_sharded(M, out, (size_t)D, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const int8_t *dW1 = stage_in(p.d, kSlotIn1, W1, (size_t)K * V);
+        const int32_t *db1 = stage_in(p.d, kSlotIn2, b1, (size_t)V);
+        const int8_t *dW2 = stage_in(p.d, kSlotIn3, W2, (size_t)V * D);
+        const int32_t *db2 = stage_in(p.d, kSlotIn4, b2, (size_t)D);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * D)));
+        if (!dA || !dW1 || !db1 || !dW2 || !db2 || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_ffn_relu_i8(p.slot, dA, dW1, db1, dW2, db2, dout, (int)nr, K, V, D, mult,
+                                   shift, zp);
     });
 }
 

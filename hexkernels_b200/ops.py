@@ -289,7 +289,8 @@ def decoder_block_i8(X, W1, b1, act_lut, W2, b2, exp_lut) -> np.ndarray:
     return out
 
 
-F16_ACT = {"none": 0, "relu": 1, "leaky": 2, "gelu": 3}
+F16_ACT = {"none": 0, "relu": 1, "leaky": 2, "gelu": 3, "sigmoid": 4, "tanh": 5}
+F16_PREROUND = {False: 0, True: 1, "sum": 1, "acc": 2}
 
 
 def gemm_f16_ex(A, B, act: str = "none", preround: bool = False, scale: float = 1.0, bias=None,
@@ -305,21 +306,62 @@ def gemm_f16_ex(A, B, act: str = "none", preround: bool = False, scale: float = 
     check(load().hexcuda_host_gemm_f16_ex(_p(A), _p(B), int(b_transposed),
                                           _p(bias) if bias is not None else None,
                                           _p(res) if res is not None else None, _p(out),
-                                          F16_ACT[act], int(preround), float(scale), M, N, K))
+                                          F16_ACT[act], F16_PREROUND[preround], float(scale), M, N, K))
     return out
 
 
 def gemm_i8_rq_ex(A, B, mult: int, shift: int, zp: int, bias=None, relu: bool = False,
-                  b_transposed: bool = False) -> np.ndarray:
-    """s8 x s8 GEMM + requant, optional bias and ReLU before the requant."""
+                  b_transposed: bool = False, res=None) -> np.ndarray:
+    """s8 x s8 GEMM + requant, optional bias and ReLU before the requant, and
+    an optional int8 residual [M, N] added with saturation after it."""
     A, B = _c(A, np.int8), _c(B, np.int8)
     M, K = A.shape
     N = B.shape[0] if b_transposed else B.shape[1]
     bias = _c(bias, np.int32) if bias is not None else None
+    res = _c(res, np.int8) if res is not None else None
     out = np.empty((M, N), np.int8)
     check(load().hexcuda_host_gemm_i8_rq_ex(_p(A), _p(B), int(b_transposed),
-                                            _p(bias) if bias is not None else None, _p(out), M, N,
+                                            _p(bias) if bias is not None else None,
+                                            _p(res) if res is not None else None, _p(out), M, N,
                                             K, mult, shift, zp, int(relu)))
+    return out
+
+
+def gemm_i8_acc(A, B, store: str = "i32", act: str = "none", bias=None, res=None, lut=None,
+                b_transposed: bool = False) -> np.ndarray:
+    """s8 (or u8) x s8 GEMM on the raw int32 accumulator with int64 post-ops:
+    + bias[j] + res[i][j], activation, store (keys of HMX_STORE)."""
+    A = np.ascontiguousarray(A)
+    a_signed = {np.dtype(np.int8): 1, np.dtype(np.uint8): 0}[A.dtype]
+    B = _c(B, np.int8)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    kind, dt = HMX_STORE[store]
+    out = np.empty((M, N), dt)
+    res_kind = 0
+    if res is not None:
+        res = np.ascontiguousarray(res)
+        res_kind = {np.dtype(np.int32): 1, np.dtype(np.int8): 2}[res.dtype]
+    if bias is not None:
+        bias = _c(bias, np.int32)
+    if lut is not None:
+        lut = _c(lut, np.int32 if store == "lut_i32" else np.int8)
+    pp = lambda a: _p(a) if a is not None else None
+    check(load().hexcuda_host_gemm_i8_acc(_p(A), a_signed, _p(B), int(b_transposed), pp(bias),
+                                          pp(res), res_kind, pp(lut), _p(out), kind, HMX_ACT[act],
+                                          M, N, K))
+    return out
+
+
+def ffn_relu_i8(A, W1, b1, W2, b2, mult: int, shift: int, zp: int) -> np.ndarray:
+    """Two-layer int8 FFN (GEMM + b1 + ReLU + sat8, GEMM + b2 + requant)."""
+    A, W1, W2 = _c(A, np.int8), _c(W1, np.int8), _c(W2, np.int8)
+    b1, b2 = _c(b1, np.int32), _c(b2, np.int32)
+    (M, K), (K2, V), (V2, D) = A.shape, W1.shape, W2.shape
+    assert K == K2 and V == V2
+    out = np.empty((M, D), np.int8)
+    check(load().hexcuda_host_ffn_relu_i8(_p(A), _p(W1), _p(b1), _p(W2), _p(b2), _p(out), M, K,
+                                          V, D, mult, shift, zp))
     return out
 
 

@@ -1,0 +1,7 @@
+/* candidate_kernel for i8_gemm_bias on the B200 (libhexcuda). */
+#include <stddef.h>
+#include "hexcuda.h"
+#include "kernel_api/i8_gemm_bias.h"
+void candidate_kernel(const int8_t *A, const int8_t *B, const int32_t *bias, int32_t *C, int M, int N, int K) {
+    hexcuda_host_gemm_i8_acc(A, 1, B, 0, bias, NULL, HEXCUDA_HMX_RES_NONE, NULL, C, HEXCUDA_HMX_STORE_I32, HEXCUDA_HMX_ACT_NONE, M, N, K);
+}

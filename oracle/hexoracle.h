@@ -125,8 +125,20 @@ void oracle_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *
  * requant (kernels/expert/gemm_bias_relu_requant/reference.c; the matrix-
  * vector i8_linear_relu_requant / i8_matvec_bias_requant as A = x, Bt = matrix). */
 void oracle_gemm_i8_rq_ex_rows(const int8_t *A, const int8_t *B, int b_transposed,
-                               const int32_t *bias, int8_t *out, int M, int N, int K,
-                               int32_t mult, int shift, int zp, int relu, int r0, int r1);
+                               const int32_t *bias, const int8_t *res, int8_t *out, int M, int N,
+                               int K, int32_t mult, int shift, int zp, int relu, int r0, int r1);
+/* s8 (a_signed) / u8 A x s8 B on the raw int32 accumulator, int64 post-ops:
+ * x = acc + bias[j] + res[i][j]; activation; store (ORACLE_HMX_STORE_*).
+ * kernels/expert/{gemm_tile_i8,gemm_tile_deepk_i8,i8_gemm_tile,i8_gemm_bias,
+ * gemm_tile_bias_relu_i8,gemm_bias_gelu,i8_gemm_gelu_lut,ffn_up_gelu_i8}/reference.c */
+void oracle_gemm_i8_acc_rows(const void *A, int a_signed, const int8_t *B, int b_transposed,
+                             const int32_t *bias, const void *res, int res_kind, const void *lut,
+                             void *out, int store, int act, int M, int N, int K, int r0, int r1);
+/* kernels/expert/ffn_relu_block/reference.c: two GEMM layers, ReLU + sat8
+ * between, requant after. */
+void oracle_ffn_relu_i8(const int8_t *A, const int8_t *W1, const int32_t *b1, const int8_t *W2,
+                        const int32_t *b2, int8_t *out, int M, int K, int V, int D, int32_t mult,
+                        int shift, int zp);
 /* s8 A x u8 B HMX-field GEMM (i8_conv2d_1x1_hmx/reference.c,
  * i8_pointwise_conv_hmx/reference.c): store ORACLE_HMX_STORE_I32 (sx12),
  * _U16_FIELD or _ACC_I32. */

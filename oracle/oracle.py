@@ -213,20 +213,61 @@ def gemm_f16_ex(A, B, act="none", preround=False, scale=1.0, bias=None, res=None
     lib().oracle_gemm_f16_ex_rows(_p(A), _p(B), int(b_transposed),
                                   _p(keep[0]) if bias is not None else None,
                                   _p(keep[-1]) if res is not None else None, _p(out), M, N, K,
-                                  {"none": 0, "relu": 1, "leaky": 2, "gelu": 3}[act], int(preround),
+                                  {"none": 0, "relu": 1, "leaky": 2, "gelu": 3, "sigmoid": 4,
+                                   "tanh": 5}[act], {False: 0, True: 1, "sum": 1, "acc": 2}[preround],
                                   C.c_float(scale), 0, M)
     return out
 
 
-def gemm_i8_rq_ex(A, B, mult, shift, zp, bias=None, relu=False, b_transposed=False):
+def gemm_i8_rq_ex(A, B, mult, shift, zp, bias=None, relu=False, b_transposed=False, res=None):
     A, B = np.ascontiguousarray(A, np.int8), np.ascontiguousarray(B, np.int8)
     M, K = A.shape
     N = B.shape[0] if b_transposed else B.shape[1]
     out = np.zeros((M, N), np.int8)
     bias = np.ascontiguousarray(bias, np.int32) if bias is not None else None
+    res = np.ascontiguousarray(res, np.int8) if res is not None else None
     lib().oracle_gemm_i8_rq_ex_rows(_p(A), _p(B), int(b_transposed),
-                                    _p(bias) if bias is not None else None, _p(out), M, N, K,
+                                    _p(bias) if bias is not None else None,
+                                    _p(res) if res is not None else None, _p(out), M, N, K,
                                     C.c_int32(mult), shift, zp, int(relu), 0, M)
+    return out
+
+
+HMX_STORE = {"i32": (0, np.int32), "i8_sat": (1, np.int8), "u8_sat": (2, np.uint8),
+             "i8_low": (3, np.int8), "u16_field": (4, np.uint16), "lut_i32": (5, np.int32),
+             "lut_i8": (6, np.int8), "acc_i32": (7, np.int32)}
+HMX_ACT = {"none": 0, "relu": 1, "leaky_shr3": 2}
+
+
+def gemm_i8_acc(A, B, store="i32", act="none", bias=None, res=None, lut=None, b_transposed=False):
+    A = np.ascontiguousarray(A)
+    a_signed = int(A.dtype == np.int8)
+    B = np.ascontiguousarray(B, np.int8)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    kind, dt = HMX_STORE[store]
+    out = np.zeros((M, N), dt)
+    res_kind = 0
+    if res is not None:
+        res = np.ascontiguousarray(res)
+        res_kind = 1 if res.dtype == np.int32 else 2
+    if bias is not None:
+        bias = np.ascontiguousarray(bias, np.int32)
+    if lut is not None:
+        lut = np.ascontiguousarray(lut, np.int32 if store == "lut_i32" else np.int8)
+    pp = lambda a: _p(a) if a is not None else None
+    lib().oracle_gemm_i8_acc_rows(_p(A), a_signed, _p(B), int(b_transposed), pp(bias), pp(res),
+                                  res_kind, pp(lut), _p(out), kind, HMX_ACT[act], M, N, K, 0, M)
+    return out
+
+
+def ffn_relu_i8(A, W1, b1, W2, b2, mult, shift, zp):
+    A, W1, W2 = (np.ascontiguousarray(x, np.int8) for x in (A, W1, W2))
+    b1, b2 = np.ascontiguousarray(b1, np.int32), np.ascontiguousarray(b2, np.int32)
+    (M, K), (_, V), (_, D) = A.shape, W1.shape, W2.shape
+    out = np.zeros((M, D), np.int8)
+    lib().oracle_ffn_relu_i8(_p(A), _p(W1), _p(b1), _p(W2), _p(b2), _p(out), M, K, V, D,
+                             C.c_int32(mult), shift, zp)
     return out
 
 

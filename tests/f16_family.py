@@ -3,7 +3,7 @@ gemm_f16_ex arguments that compute it (kernels/expert/<bundle>/reference.c).
 Used by the CPU and GPU tests."""
 import numpy as np
 
-ACT = {"none": 0, "relu": 1, "leaky": 2, "gelu": 3}
+ACT = {"none": 0, "relu": 1, "leaky": 2, "gelu": 3, "sigmoid": 4, "tanh": 5}
 
 # bundle -> (A key, B key, b_transposed, extra kwargs)
 F16_BUNDLES = {
@@ -18,6 +18,13 @@ F16_BUNDLES = {
     "hmx_tile_mac_fp16_32": ("A", "B", False, dict(res="C")),
     "qkt_tile_fp16": ("Q", "K", False, dict(preround=True, scale=0.125)),
     "av_tile_fp16": ("A", "V", True, dict()),
+    # the accumulator rounded to fp16 before the adds and the activation
+    "fp16_matmul_bias_gelu": ("A", "B", False, dict(bias="bias", act="gelu", preround="acc")),
+    "fp16_matmul_bias_relu": ("A", "B", False, dict(bias="bias", act="relu", preround="acc")),
+    "fp16_matmul_residual": ("A", "B", False, dict(res="C", preround="acc")),
+    "fp16_matmul_sigmoid": ("A", "B", False, dict(act="sigmoid", preround="acc")),
+    "fp16_matmul_tanh": ("A", "B", False, dict(act="tanh", preround="acc")),
+    "ai_fp16_matmul_gelu": ("A", "B", False, dict(act="gelu", preround="acc")),
 }
 
 

@@ -561,6 +561,26 @@ def gen_f16_family(ref):
     o = np.zeros((M, D), np.float16)
     ref.ref_av_tile_fp16(ptr(Am), ptr(V), ptr(o), M, N, D)
     a.update({"av_tile_fp16__A": Am, "av_tile_fp16__V": V, "av_tile_fp16__out": o})
+    # the callers that round the accumulator before their post-op
+    for name in ("fp16_matmul_bias_gelu", "fp16_matmul_bias_relu"):
+        A, B, bias = f16(n, kd, k=kd), f16(kd, n), f16(n)
+        o = np.zeros((n, n), np.float16)
+        run(name, name, ptr(A), ptr(B), ptr(bias), ptr(o), n, kd)
+        a.update({f"{name}__A": A, f"{name}__B": B, f"{name}__bias": bias, f"{name}__out": o})
+    A, B, c0 = f16(n, kd, k=kd), f16(kd, n), f16(n, n)
+    o = np.zeros((n, n), np.float16)
+    run("r", "fp16_matmul_residual", ptr(A), ptr(B), ptr(c0), ptr(o), n, kd)
+    a.update({"fp16_matmul_residual__A": A, "fp16_matmul_residual__B": B,
+              "fp16_matmul_residual__C": c0, "fp16_matmul_residual__out": o})
+    for name in ("fp16_matmul_sigmoid", "fp16_matmul_tanh"):
+        A, B = f16(n, kd, k=kd), f16(kd, n)
+        o = np.zeros((n, n), np.float16)
+        run(name, name, ptr(A), ptr(B), ptr(o), n, kd)
+        a.update({f"{name}__A": A, f"{name}__B": B, f"{name}__out": o})
+    A, B = f16(n, n, k=n), f16(n, n)
+    o = np.zeros((n, n), np.float16)
+    run("g", "ai_fp16_matmul_gelu", ptr(A), ptr(B), ptr(o), n)
+    a.update({"ai_fp16_matmul_gelu__A": A, "ai_fp16_matmul_gelu__B": B, "ai_fp16_matmul_gelu__out": o})
     save("f16_family", **a)
 
 
@@ -804,6 +824,77 @@ def gen_reduce_family(ref):
     save("reduce_family", **arrays)
 
 
+def gen_i8_acc_callers(ref):
+    # The raw-accumulator int8 GEMM callers, the requant + residual GEMM and
+    # the two-layer FFN through their reference.c at shapes off the tile
+    # grid: full-range operands where the bundle saturates or keeps int32,
+    # small-range operands (|x| <= 4) where a table or the int8 range must be
+    # hit inside its range; ffn_relu_block at its reference's fixed hidden
+    # buffer (M * V <= 256).
+    rng = np.random.default_rng(97)
+    s8 = lambda lo, hi, *sh: rng.integers(lo, hi, sh, dtype=np.int8)
+    a = {}
+
+    def run(name, args, **arrs):
+        getattr(ref, "ref_" + name)(*args)
+        for k, v in arrs.items():
+            a[f"{name}__{k}"] = v
+
+    for name, (M, N, K), bt in (("gemm_tile_i8", (70, 130, 200), True),
+                                ("gemm_tile_deepk_i8", (40, 70, 1100), False),
+                                ("i8_gemm_tile", (129, 65, 77), False)):
+        A, B = s8(-128, 128, M, K), s8(-128, 128, *((N, K) if bt else (K, N)))
+        C_ = np.zeros((M, N), np.int32)
+        run(name, (ptr(A), ptr(B), ptr(C_), M, N, K), A=A, B=B, out=C_)
+    M, N, K = 100, 90, 300
+    A, B = s8(-128, 128, M, K), s8(-128, 128, K, N)
+    bias = rng.integers(-2**20, 2**20, N).astype(np.int32)
+    C_ = np.zeros((M, N), np.int32)
+    run("i8_gemm_bias", (ptr(A), ptr(B), ptr(bias), ptr(C_), M, N, K), A=A, B=B, bias=bias, out=C_)
+    M, N, K = 33, 40, 50
+    A, B = s8(-128, 128, 4, M, K), s8(-128, 128, 4, K, N)
+    bias = rng.integers(-50000, 50000, (4, N)).astype(np.int32)
+    C0, C1 = np.zeros((4, M, N), np.int32), np.zeros((4, M, N), np.int32)
+    run("i8_batch_matmul", (ptr(A), ptr(B), ptr(C0), M, N, K), A=A, B=B, out=C0)
+    run("i8_batch_matmul_bias", (ptr(A), ptr(B), ptr(bias), ptr(C1), M, N, K), bias=bias, out=C1)
+    M, N, K = 64, 80, 96
+    A, B = s8(-4, 5, M, K), s8(-4, 5, N, K)
+    bias = rng.integers(-200, 200, N).astype(np.int32)
+    C8 = np.zeros((M, N), np.int8)
+    run("gemm_tile_bias_relu_i8", (ptr(A), ptr(B), ptr(bias), ptr(C8), M, N, K), A=A, B=B, bias=bias,
+        out=C8)
+    lut = s8(-128, 128, 256)
+    a["gelu_lut"] = lut
+    M, N, K = 50, 60, 64
+    A, B = s8(-4, 5, M, K), s8(-4, 5, K, N)
+    bias = rng.integers(-150, 150, N).astype(np.int32)
+    o = np.zeros((M, N), np.int8)
+    run("gemm_bias_gelu", (ptr(A), ptr(B), ptr(bias), ptr(lut), ptr(o), M, N, K), A=A, B=B,
+        bias=bias, out=o)
+    o = np.zeros((M, N), np.int8)
+    run("i8_gemm_gelu_lut", (ptr(A), ptr(B), ptr(lut), ptr(o), M, N, K), out=o)
+    M, N, K = 32, 48, 40
+    A, Bt = s8(-4, 5, M, K), s8(-4, 5, N, K)
+    bias = rng.integers(-150, 150, N).astype(np.int32)
+    o = np.zeros((M, N), np.int8)
+    run("ffn_up_gelu_i8", (ptr(A), ptr(Bt), ptr(bias), ptr(lut), ptr(o), M, N, K), A=A, B=Bt,
+        bias=bias, out=o)
+    M, N, K = 60, 70, 90
+    A, B, res = s8(-128, 128, M, K), s8(-128, 128, K, N), s8(-128, 128, M, N)
+    o = np.zeros((M, N), np.int8)
+    run("matmul_residual_add_i8", (ptr(A), ptr(B), ptr(res), ptr(o), M, N, K, C.c_int32(1 << 30), 42),
+        A=A, B=B, res=res, out=o)
+    M, K, V, D = 8, 16, 32, 16
+    A, W1, W2 = s8(-128, 128, M, K), s8(-128, 128, K, V), s8(-128, 128, V, D)
+    b1 = rng.integers(-20000, 20000, V).astype(np.int32)
+    b2 = rng.integers(-2000, 2000, D).astype(np.int32)
+    o = np.zeros((M, D), np.int8)
+    run("ffn_relu_block", (ptr(A), ptr(W1), ptr(b1), ptr(W2), ptr(b2), ptr(o), M, K, V, D,
+                           C.c_int32(1 << 24), 30, C.c_int8(-3)),
+        A=A, W1=W1, b1=b1, W2=W2, b2=b2, out=o)
+    save("i8_acc_callers", **a)
+
+
 def main():
     if not (REF_ROOT / "kernels").is_dir():
         sys.exit(f"reference tree not found at {REF_ROOT}")
@@ -823,6 +914,7 @@ def main():
     gen_f16_family(ref)
     gen_i8_callers(ref)
     gen_reduce_family(ref)
+    gen_i8_acc_callers(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

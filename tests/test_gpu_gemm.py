@@ -411,3 +411,52 @@ def test_gemm_pair_kernel_matches_single_sm(hx, oracle, monkeypatch, M, N, K):
     np.testing.assert_array_equal(pair[1][rows], oracle.gemm_i8_requant(As[rows], B, 1234567, 30, 3))
     for f in pair[3:]:
         assert_f16_gemm_close(f[rows], oracle.gemm_f16_nt(Af[rows], Btf))
+
+
+from test_oracle_golden import i8_acc_calls  # noqa: E402
+
+
+def test_i8_acc_callers_golden(hx):
+    for got, exp in i8_acc_calls(hx, golden("i8_acc_callers")):
+        np.testing.assert_array_equal(got, exp)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (129, 257, 130), (300, 520, 1000), (640, 384, 4096)])
+def test_i8_acc_random(hx, oracle, M, N, K):
+    """Raw-accumulator epilogue (int64 post-ops) on both GEMM kernels,
+    signed and unsigned A, every store kind, against the oracle; and the
+    requant + int8 residual form."""
+    rng = np.random.default_rng(M + N + K)
+    A8 = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    U8 = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    Bt = np.ascontiguousarray(B.T)
+    bias = rng.integers(-2**31, 2**31, N, dtype=np.int64).astype(np.int32)
+    res32 = rng.integers(-2**31, 2**31, (M, N), dtype=np.int64).astype(np.int32)
+    res8 = rng.integers(-128, 128, (M, N), dtype=np.int8)
+    lut8 = rng.integers(-128, 128, 256, dtype=np.int8)
+    lut32 = rng.integers(-2**31, 2**31, 256, dtype=np.int64).astype(np.int32)
+    cases = [dict(store="i32"), dict(store="i8_sat", act="relu", bias=bias),
+             dict(store="u8_sat", res=res8), dict(store="lut_i8", bias=bias, lut=lut8),
+             dict(store="lut_i32", act="leaky_shr3", res=res32, lut=lut32),
+             dict(store="i8_low", bias=bias, res=res8), dict(store="u16_field", act="relu")]
+    for A in (A8, U8):
+        for kw in cases:
+            exp = oracle.gemm_i8_acc(A, B, **kw)
+            np.testing.assert_array_equal(hx.gemm_i8_acc(A, B, **kw), exp, err_msg=str(kw))
+            np.testing.assert_array_equal(hx.gemm_i8_acc(A, Bt, b_transposed=True, **kw), exp)
+    for mult, shift in ((1 << 30, 44), (-1234567, 20)):
+        np.testing.assert_array_equal(hx.gemm_i8_rq_ex(A8, B, mult, shift, 3, bias=bias, res=res8),
+                                      oracle.gemm_i8_rq_ex(A8, B, mult, shift, 3, bias=bias, res=res8))
+
+
+def test_ffn_relu_i8_random(hx, oracle):
+    rng = np.random.default_rng(5)
+    M, K, V, D = 300, 256, 512, 200
+    A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    W1 = rng.integers(-128, 128, (K, V), dtype=np.int8)
+    W2 = rng.integers(-128, 128, (V, D), dtype=np.int8)
+    b1 = rng.integers(-50000, 50000, V).astype(np.int32)
+    b2 = rng.integers(-50000, 50000, D).astype(np.int32)
+    np.testing.assert_array_equal(hx.ffn_relu_i8(A, W1, b1, W2, b2, 1 << 28, 36, 5),
+                                  oracle.ffn_relu_i8(A, W1, b1, W2, b2, 1 << 28, 36, 5))

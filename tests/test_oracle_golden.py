@@ -328,3 +328,40 @@ def test_reduce_family_golden(oracle, bundle, case):
 def test_reduce_family_covers_every_bundle():
     from reduce_family import RD_BUNDLES
     assert {b for b, _ in RD_CASES} == set(RD_BUNDLES)
+
+
+def i8_acc_calls(impl, g):
+    """(result, expected) of the raw-accumulator int8 GEMM callers, the
+    requant + residual GEMM and the two-layer FFN (golden i8_acc_callers)
+    through `impl` (the oracle or the GPU ops module)."""
+    yield impl.gemm_i8_acc(g["gemm_tile_i8__A"], g["gemm_tile_i8__B"], b_transposed=True), g["gemm_tile_i8__out"]
+    for name in ("gemm_tile_deepk_i8", "i8_gemm_tile"):
+        yield impl.gemm_i8_acc(g[name + "__A"], g[name + "__B"]), g[name + "__out"]
+    yield (impl.gemm_i8_acc(g["i8_gemm_bias__A"], g["i8_gemm_bias__B"], bias=g["i8_gemm_bias__bias"]),
+           g["i8_gemm_bias__out"])
+    A, B, bias = g["i8_batch_matmul__A"], g["i8_batch_matmul__B"], g["i8_batch_matmul_bias__bias"]
+    yield np.stack([impl.gemm_i8_acc(A[b], B[b]) for b in range(4)]), g["i8_batch_matmul__out"]
+    yield (np.stack([impl.gemm_i8_acc(A[b], B[b], bias=bias[b]) for b in range(4)]),
+           g["i8_batch_matmul_bias__out"])
+    n = "gemm_tile_bias_relu_i8"
+    yield (impl.gemm_i8_acc(g[n + "__A"], g[n + "__B"], "i8_sat", "relu", bias=g[n + "__bias"],
+                            b_transposed=True), g[n + "__out"])
+    lut = g["gelu_lut"]
+    n = "gemm_bias_gelu"
+    yield (impl.gemm_i8_acc(g[n + "__A"], g[n + "__B"], "lut_i8", bias=g[n + "__bias"], lut=lut),
+           g[n + "__out"])
+    yield impl.gemm_i8_acc(g[n + "__A"], g[n + "__B"], "lut_i8", lut=lut), g["i8_gemm_gelu_lut__out"]
+    n = "ffn_up_gelu_i8"
+    yield (impl.gemm_i8_acc(g[n + "__A"], g[n + "__B"], "lut_i8", bias=g[n + "__bias"], lut=lut,
+                            b_transposed=True), g[n + "__out"])
+    n = "matmul_residual_add_i8"
+    yield (impl.gemm_i8_rq_ex(g[n + "__A"], g[n + "__B"], 1 << 30, 42, 0, res=g[n + "__res"]),
+           g[n + "__out"])
+    n = "ffn_relu_block"
+    yield (impl.ffn_relu_i8(g[n + "__A"], g[n + "__W1"], g[n + "__b1"], g[n + "__W2"], g[n + "__b2"],
+                            1 << 24, 30, -3), g[n + "__out"])
+
+
+def test_i8_acc_callers_golden(oracle):
+    for got, exp in i8_acc_calls(oracle, golden("i8_acc_callers")):
+        np.testing.assert_array_equal(got, exp)

@@ -76,6 +76,14 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_group_sum_i8": (I, [I, P, P, I64, I]),
     "hexcuda_scan_max_i8": (I, [I, P, P, I64]),
     "hexcuda_head_group_reduce_i8": (I, [I, P, P, I, I, I64, I32, I]),
+    "hexcuda_layernorm_lut_i8": (I, [I, P, P, P, P, I, I, P, P, P, I]),
+    "hexcuda_layernorm_lut_i16": (I, [I, P, P, I, I, P, P, P, I]),
+    "hexcuda_lut_softmax_u8": (I, [I, P, P, I, I, P]),
+    "hexcuda_lut_softmax_i16": (I, [I, P, P, I, I, P]),
+    "hexcuda_requant_i16": (I, [I, P, P, I64, I32, I]),
+    "hexcuda_norm_requant_i8": (I, [I, P, P, I64, I, P, P, I32, I, I]),
+    "hexcuda_gemm_softmax_u8": (I, [I, P, P, I, P, P, I, I, I, I, I32, I]),
+    "hexcuda_gelu_ffn_residual_i8": (I, [I, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I]),
     "hexcuda_gemm_hmx_ex": (I, [I, P, P, I, P, P, I, P, P, I, I, I, I, I, I, I32]),
     "hexcuda_gemm_u8s8_pc_noalloc": (I, [I, P, P, P, P, I, I, I, I32, P, P, U8]),
     "hexcuda_gemm_f16_nt": (I, [I, P, P, P, I, I, I]),
@@ -113,6 +121,14 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_group_sum_i8": (I, [P, P, I64, I]),
     "hexcuda_host_scan_max_i8": (I, [P, P, I64]),
     "hexcuda_host_head_group_reduce_i8": (I, [P, P, I, I, I64, I32, I]),
+    "hexcuda_host_layernorm_lut_i8": (I, [P, I, P, P, P, I, I, P, P, P, I]),
+    "hexcuda_host_layernorm_lut_i16": (I, [P, P, I, I, P, P, P, I]),
+    "hexcuda_host_lut_softmax_u8": (I, [P, P, I, I, P]),
+    "hexcuda_host_lut_softmax_i16": (I, [P, P, I, I, P]),
+    "hexcuda_host_requant_i16": (I, [P, P, I64, I32, I]),
+    "hexcuda_host_norm_requant_i8": (I, [P, P, I64, I, P, P, I32, I, I]),
+    "hexcuda_host_gemm_softmax_u8": (I, [P, P, I, P, P, I, I, I, I, I32, I]),
+    "hexcuda_host_gelu_ffn_residual_i8": (I, [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I]),
     "hexcuda_host_gemm_hmx_ex": (I, [P, P, I, P, P, I, P, P, I, I, I, I, I, I, I32]),
     "hexcuda_host_gemm_f16_nt": (I, [P, P, P, I, I, I]),
     "hexcuda_host_gemm_f16_nn": (I, [P, P, P, I, I, I]),

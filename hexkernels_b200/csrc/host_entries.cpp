@@ -874,3 +874,190 @@ HX_EXPORT int hexcuda_host_head_group_reduce_i8(const int8_t *X, int8_t *Y, int 
                                             shift);
     });
 }
+
+// Rows sharded over the devices; a gathered layernorm (idx) replicates the
+// table x (xrows rows) and shards idx; per-row affine operands are sharded
+// with their rows, shared ones replicated.
+HX_EXPORT int hexcuda_host_layernorm_lut_i8(const int8_t *x, int xrows, const int32_t *idx,
+                                            const int8_t *res, int8_t *out, int R, int W,
+                                            const int8_t *gamma, const int8_t *beta,
+                                            const uint8_t *inv_lut, int affine) {
+    if (R < 0 || W < 1 || (idx && xrows < 1) || affine < HEXCUDA_LN_AFFINE_SHARED ||
+        affine > HEXCUDA_LN_AFFINE_PER_ROW)
+        return fail(HEXCUDA_ERR_ARG, "host_layernorm_lut_i8: R %d W %d affine %d", R, W, affine);
+    if (R == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_layernorm_lut_i8", {x, out, gamma, beta, inv_lut})) return rc;
+    return run_sharded(R, out, (size_t)W, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *dx = idx ? stage_in(p.d, kSlotIn0, x, (size_t)xrows * W)
+                               : stage_in(p.d, kSlotIn0, x + p.r0 * W, (size_t)(nr * W));
+        const int32_t *di = idx ? stage_in(p.d, kSlotIn1, idx + p.r0, (size_t)nr) : nullptr;
+        const int8_t *dr = res ? stage_in(p.d, kSlotIn2, res + p.r0 * W, (size_t)(nr * W)) : nullptr;
+        int64_t g0 = 0, gn = W, l0 = 0, ln = 256;
+        if (affine == HEXCUDA_LN_AFFINE_ROWWISE) g0 = p.r0 * W, gn = nr * W;
+        if (affine == HEXCUDA_LN_AFFINE_PER_ROW) g0 = p.r0, gn = nr, l0 = p.r0 * 256, ln = nr * 256;
+        const int8_t *dg = stage_in(p.d, kSlotIn3, gamma + g0, (size_t)gn);
+        const int8_t *db = stage_in(p.d, kSlotIn4, beta + g0, (size_t)gn);
+        const uint8_t *dl = stage_in(p.d, kSlotIn5, inv_lut + l0, (size_t)ln);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * W)));
+        if (!dx || (idx && !di) || (res && !dr) || !dg || !db || !dl || !dout)
+            return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_layernorm_lut_i8(p.slot, dx, di, dr, dout, (int)nr, W, dg, db, dl, affine);
+    });
+}
+
+HX_EXPORT int hexcuda_host_layernorm_lut_i16(const int16_t *x, int16_t *out, int R, int C,
+                                             const int16_t *gamma, const int16_t *beta,
+                                             const uint16_t *inv_lut, int order) {
+    if (R < 0 || C < 1 || (order != 0 && order != 1))
+        return fail(HEXCUDA_ERR_ARG, "host_layernorm_lut_i16: R %d C %d order %d", R, C, order);
+    if (R == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_layernorm_lut_i16", {x, out, gamma, beta, inv_lut})) return rc;
+    return run_sharded(R, out, (size_t)C * 2, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int16_t *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
+        const int64_t g0 = order ? p.r0 : 0, gn = order ? nr : C;
+        const int16_t *dg = stage_in(p.d, kSlotIn1, gamma + g0, (size_t)gn);
+        const int16_t *db = stage_in(p.d, kSlotIn2, beta + g0, (size_t)gn);
+        const uint16_t *dl = stage_in(p.d, kSlotIn3, inv_lut, 256);
+        int16_t *dout = reinterpret_cast<int16_t *>(scratch(p.d, kSlotOut, (size_t)(nr * C) * 2));
+        if (!dx || !dg || !db || !dl || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_layernorm_lut_i16(p.slot, dx, dout, (int)nr, C, dg, db, dl, order);
+    });
+}
+
+HX_EXPORT int hexcuda_host_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C,
+                                          const uint8_t *exp_lut) {
+    if (R < 0 || C < 1) return fail(HEXCUDA_ERR_ARG, "host_lut_softmax_u8: R %d C %d", R, C);
+    if (R == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_lut_softmax_u8", {x, out, exp_lut})) return rc;
+    return run_sharded(R, out, (size_t)C, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
+        const uint8_t *dl = stage_in(p.d, kSlotIn1, exp_lut, 256);
+        uint8_t *dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * C)));
+        if (!dx || !dl || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_lut_softmax_u8(p.slot, dx, dout, (int)nr, C, dl);
+    });
+}
+
+HX_EXPORT int hexcuda_host_lut_softmax_i16(const int16_t *x, int16_t *out, int R, int C,
+                                           const uint16_t *exp_lut) {
+    if (R < 0 || C < 1) return fail(HEXCUDA_ERR_ARG, "host_lut_softmax_i16: R %d C %d", R, C);
+    if (R == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_lut_softmax_i16", {x, out, exp_lut})) return rc;
+    return run_sharded(R, out, (size_t)C * 2, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int16_t *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
+        const uint16_t *dl = stage_in(p.d, kSlotIn1, exp_lut, 256);
+        int16_t *dout = reinterpret_cast<int16_t *>(scratch(p.d, kSlotOut, (size_t)(nr * C) * 2));
+        if (!dx || !dl || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_lut_softmax_i16(p.slot, dx, dout, (int)nr, C, dl);
+    });
+}
+
+HX_EXPORT int hexcuda_host_requant_i16(const int32_t *a, int16_t *out, int64_t n, int32_t mult,
+                                       int shift) {
+    if (n < 0) return fail(HEXCUDA_ERR_ARG, "host_requant_i16: n %lld", (long long)n);
+    if (n == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_requant_i16", {a, out})) return rc;
+    return run_sharded(n, out, 2, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int32_t *da = stage_in(p.d, kSlotIn0, a + p.r0, (size_t)nr);
+        int16_t *dout = reinterpret_cast<int16_t *>(scratch(p.d, kSlotOut, (size_t)nr * 2));
+        if (!da || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_requant_i16(p.slot, da, dout, nr, mult, shift);
+    });
+}
+
+// channels are fixed fractions of n: one device
+HX_EXPORT int hexcuda_host_norm_requant_i8(const int8_t *a, int8_t *out, int64_t n, int nch,
+                                           const int32_t *nmult, const int *nshift, int32_t mult,
+                                           int shift, int zp) {
+    if (n < 0 || nch < 1) return fail(HEXCUDA_ERR_ARG, "host_norm_requant_i8: n %lld", (long long)n);
+    const int64_t used = n / nch * nch;
+    if (used == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_norm_requant_i8", {a, out, nmult, nshift})) return rc;
+    return run_sharded(1, out, (size_t)used, [&](Part &p) {
+        const int8_t *da = stage_in(p.d, kSlotIn0, a, (size_t)used);
+        const int32_t *dm = stage_in(p.d, kSlotIn1, nmult, (size_t)nch);
+        const int *ds = stage_in(p.d, kSlotIn2, nshift, (size_t)nch);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)used));
+        if (!da || !dm || !ds || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_norm_requant_i8(p.slot, da, dout, used, nch, dm, ds, mult, shift, zp);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gemm_softmax_u8(const int8_t *A, const int8_t *B, int b_transposed,
+                                           const uint8_t *exp_lut, uint8_t *out, int M, int N,
+                                           int K, int requant, int32_t mult, int shift) {
+    if (M < 0 || N < 1 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_softmax_u8: bad shape");
+    if (M == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_softmax_u8", {A, B, exp_lut, out})) return rc;
+    return run_sharded(M, out, (size_t)N, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        const uint8_t *dl = stage_in(p.d, kSlotIn2, exp_lut, 256);
+        uint8_t *dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * N)));
+        if (!dA || !dB || !dl || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gemm_softmax_u8(p.slot, dA, dB, b_transposed, dl, dout, (int)nr, N, K,
+                                       requant, mult, shift);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gelu_ffn_residual_i8(const int8_t *x, const int8_t *W1, const int32_t *b1,
+                                                const int8_t *gelu_lut, const int8_t *W2,
+                                                const int32_t *b2, const int8_t *x_res,
+                                                const int8_t *gamma, const int8_t *beta,
+                                                const uint8_t *inv_lut, int8_t *out, int M, int K,
+                                                int V, int D) {
+    if (M < 0 || K < 0 || V < 0 || D < 1) return fail(HEXCUDA_ERR_ARG, "host_gelu_ffn_residual_i8: bad shape");
+    if (M == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gelu_ffn_residual_i8",
+                            {x, W1, b1, gelu_lut, W2, b2, x_res, gamma, beta, inv_lut, out}))
+        return rc;
+    return run_sharded(M, out, (size_t)D, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        // 8 staged operands: the weights and tables share the input slots
+        // with the row-sharded activations through one packed buffer
+        const size_t nx = (size_t)(nr * K), nw1 = (size_t)K * V, nw2 = (size_t)V * D,
+                     nres = (size_t)(nr * D);
+        auto r16 = [](size_t b) { return (b + 15) / 16 * 16; };
+        uint8_t *pk = reinterpret_cast<uint8_t *>(
+            scratch(p.d, kSlotIn0, r16(nx) + r16(nw1) + r16(nw2) + r16(nres) + 2 * r16((size_t)D) + 512));
+        int32_t *dbias = reinterpret_cast<int32_t *>(scratch(p.d, kSlotIn1, 4 * ((size_t)V + D)));
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, nres));
+        if (!pk || !dbias || !dout) return hexcuda_last_error();
+        size_t off = 0;
+        auto put = [&](const void *src, size_t bytes) -> uint8_t * {
+            uint8_t *dst = pk + off;
+            off += (bytes + 15) / 16 * 16;
+            if (bytes && check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, p.d->stream), "h2d"))
+                return nullptr;
+            return dst;
+        };
+        const int8_t *dx = reinterpret_cast<const int8_t *>(put(x + p.r0 * K, nx));
+        const int8_t *dw1 = reinterpret_cast<const int8_t *>(put(W1, nw1));
+        const int8_t *dw2 = reinterpret_cast<const int8_t *>(put(W2, nw2));
+        const int8_t *dres = reinterpret_cast<const int8_t *>(put(x_res + p.r0 * D, nres));
+        const int8_t *dg = reinterpret_cast<const int8_t *>(put(gamma, (size_t)D));
+        const int8_t *dbt = reinterpret_cast<const int8_t *>(put(beta, (size_t)D));
+        const int8_t *dgl = reinterpret_cast<const int8_t *>(put(gelu_lut, 256));
+        const uint8_t *dil = put(inv_lut, 256);
+        if (check(cudaMemcpyAsync(dbias, b1, 4 * (size_t)V, cudaMemcpyHostToDevice, p.d->stream), "h2d") ||
+            check(cudaMemcpyAsync(dbias + V, b2, 4 * (size_t)D, cudaMemcpyHostToDevice, p.d->stream), "h2d"))
+            return hexcuda_last_error();
+        if (!dx || !dw1 || !dw2 || !dres || !dg || !dbt || !dgl || !dil) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gelu_ffn_residual_i8(p.slot, dx, dw1, dbias, dgl, dw2, dbias + V, dres, dg, dbt,
+                                            dil, dout, (int)nr, K, V, D);
+    });
+}

@@ -11,7 +11,7 @@
 
 namespace hx {
 
-constexpr int kScratchSlots = 20;
+constexpr int kScratchSlots = 24;
 constexpr int kPipeChunks = 64;     // max chunks in flight per pipelined host call
 
 // Per-device state.  `stream` is where every launcher enqueues work; it is the

@@ -244,6 +244,92 @@ def head_group_reduce_i8(X, G: int, mult: int, shift: int) -> np.ndarray:
     return Y
 
 
+LN_AFFINE = {"shared": 0, "rowwise": 1, "per_row": 2}
+
+
+def layernorm_lut_i8(x, gamma, beta, inv_lut, affine: str = "shared", res=None, idx=None):
+    """int8 layernorm with an inverse-variance table (hexcuda_layernorm_lut_i8)
+    over the rows of x [R, W]; with idx, the rows x[idx[r]] (x is the table)."""
+    x = _c(x, np.int8)
+    xrows, W = x.shape
+    idx = _c(idx, np.int32) if idx is not None else None
+    R = idx.size if idx is not None else xrows
+    res = _c(res, np.int8) if res is not None else None
+    gamma, beta, inv_lut = _c(gamma, np.int8), _c(beta, np.int8), _c(inv_lut, np.uint8)
+    out = np.empty((R, W), np.int8)
+    check(load().hexcuda_host_layernorm_lut_i8(_p(x), xrows, None if idx is None else _p(idx),
+                                               None if res is None else _p(res), _p(out), R, W,
+                                               _p(gamma), _p(beta), _p(inv_lut), LN_AFFINE[affine]))
+    return out
+
+
+def layernorm_lut_i16(x, gamma, beta, inv_lut, order: int = 0) -> np.ndarray:
+    x = _c(x, np.int16)
+    R, Cc = x.shape
+    out = np.empty_like(x)
+    check(load().hexcuda_host_layernorm_lut_i16(_p(x), _p(out), R, Cc, _p(_c(gamma, np.int16)),
+                                                _p(_c(beta, np.int16)), _p(_c(inv_lut, np.uint16)),
+                                                order))
+    return out
+
+
+def lut_softmax_u8(x, exp_lut) -> np.ndarray:
+    x = _c(x, np.int8)
+    R, Cc = x.shape
+    out = np.empty((R, Cc), np.uint8)
+    check(load().hexcuda_host_lut_softmax_u8(_p(x), _p(out), R, Cc, _p(_c(exp_lut, np.uint8))))
+    return out
+
+
+def lut_softmax_i16(x, exp_lut) -> np.ndarray:
+    x = _c(x, np.int16)
+    R, Cc = x.shape
+    out = np.empty_like(x)
+    check(load().hexcuda_host_lut_softmax_i16(_p(x), _p(out), R, Cc, _p(_c(exp_lut, np.uint16))))
+    return out
+
+
+def requant_i16(a, mult: int, shift: int) -> np.ndarray:
+    a = _c(a, np.int32)
+    out = np.empty(a.shape, np.int16)
+    check(load().hexcuda_host_requant_i16(_p(a), _p(out), a.size, mult, shift))
+    return out
+
+
+def norm_requant_i8(a, nmult, nshift, mult: int, shift: int, zp: int = 0) -> np.ndarray:
+    """Per-channel requant (channels = equal parts of a) then a second one;
+    elements past the channels' last whole part are returned as zero."""
+    a = _c(a, np.int8).ravel()
+    nmult, nshift = _c(nmult, np.int32), _c(nshift, np.int32)
+    out = np.zeros_like(a)
+    check(load().hexcuda_host_norm_requant_i8(_p(a), _p(out), a.size, nmult.size, _p(nmult),
+                                              _p(nshift), mult, shift, zp))
+    return out
+
+
+def gemm_softmax_u8(A, B, exp_lut, b_transposed: bool = False, requant: bool = False,
+                    mult: int = 1, shift: int = 0) -> np.ndarray:
+    A, B = _c(A, np.int8), _c(B, np.int8)
+    M, K = A.shape
+    N = B.shape[0] if b_transposed else B.shape[1]
+    out = np.empty((M, N), np.uint8)
+    check(load().hexcuda_host_gemm_softmax_u8(_p(A), _p(B), int(b_transposed),
+                                              _p(_c(exp_lut, np.uint8)), _p(out), M, N, K,
+                                              int(requant), mult, shift))
+    return out
+
+
+def gelu_ffn_residual_i8(x, W1, b1, gelu_lut, W2, b2, x_res, gamma, beta, inv_lut) -> np.ndarray:
+    x, W1, W2, x_res = (_c(t, np.int8) for t in (x, W1, W2, x_res))
+    (M, K), (_, V), (_, D) = x.shape, W1.shape, W2.shape
+    out = np.empty((M, D), np.int8)
+    check(load().hexcuda_host_gelu_ffn_residual_i8(
+        _p(x), _p(W1), _p(_c(b1, np.int32)), _p(_c(gelu_lut, np.int8)), _p(W2),
+        _p(_c(b2, np.int32)), _p(x_res), _p(_c(gamma, np.int8)), _p(_c(beta, np.int8)),
+        _p(_c(inv_lut, np.uint8)), _p(out), M, K, V, D))
+    return out
+
+
 def attn_qkt_av_hmx(Q, K, V) -> np.ndarray:
     """sx12 field of (sx12 field of Q K^T) V; Q [SQ, D] u8, K / V [SK, D] s8."""
     Q, K, V = _c(Q, np.uint8), _c(K, np.int8), _c(V, np.int8)

@@ -189,6 +189,60 @@ int hexcuda_relu_i8(int dev, const int8_t *x, int8_t *out, int64_t n);
 int hexcuda_reduce_int(int dev, const void *a, const void *b, int elem, int64_t n, int op,
                        void *out);
 
+/* int8 layernorm with an inverse-variance table, one row of W elements per
+ * output row r < R:  t = x row (row idx[r] of x when idx is not NULL; t =
+ * sat8(t + res[r][j]) when res is not NULL); mu = sum t / W; var = sum (t -
+ * mu)^2 / W (int32, C division); inv = lut[clamp(var, 0, 255)];
+ * out = sat8(((((t - mu) g + 64) >> 7) inv + 128) >> 8) + b).
+ * affine SHARED: g = gamma[j], b = beta[j] (i8_layernorm_dma, layernorm_residual,
+ * embedding_layer_norm); ROWWISE: gamma[r W + j] (i8_chunk_norm); PER_ROW:
+ * gamma[r], beta[r] and the table inv_lut + 256 r (i8_instance_norm). */
+#define HEXCUDA_LN_AFFINE_SHARED 0
+#define HEXCUDA_LN_AFFINE_ROWWISE 1
+#define HEXCUDA_LN_AFFINE_PER_ROW 2
+int hexcuda_layernorm_lut_i8(int dev, const int8_t *x, const int32_t *idx, const int8_t *res,
+                             int8_t *out, int R, int W, const int8_t *gamma, const int8_t *beta,
+                             const uint8_t *inv_lut, int affine);
+/* int16 forms: mu = (int32)(sum / C), var = sum (x - mu)^2 / C (int64),
+ * inv = inv_lut[clamp(var >> 5, 0, 255)]; order 0 (layernorm_row_i16):
+ * sat16(((((x - mu) gamma[c] + 32) >> 6) inv + 512) >> 10) + beta[c]);
+ * order 1 (layernorm_affine_i16): sat16(((((x - mu) inv + 512) >> 10)
+ * gamma[r] + 32) >> 6) + beta[r]). */
+int hexcuda_layernorm_lut_i16(int dev, const int16_t *x, int16_t *out, int R, int C,
+                              const int16_t *gamma, const int16_t *beta, const uint16_t *inv_lut,
+                              int order);
+/* Row softmax by an exp table: m = row max, e = lut[max(x - m, -255) + 255],
+ * S = sum e, p = (e 255 + S / 2) / S as uint8 (i8_gemm_softmax_tile,
+ * matmul_softmax_tile step B); the int16 form with a uint16 table, int64 S
+ * and (e 32767 + S / 2) / S (vtcm_softmax_row_i16). */
+int hexcuda_lut_softmax_u8(int dev, const int8_t *x, uint8_t *out, int R, int C,
+                           const uint8_t *exp_lut);
+int hexcuda_lut_softmax_i16(int dev, const int16_t *x, int16_t *out, int R, int C,
+                            const uint16_t *exp_lut);
+/* out = sat16(round_half_away(a * mult >> shift)): attention_scale_i16. */
+int hexcuda_requant_i16(int dev, const int32_t *a, int16_t *out, int64_t n, int32_t mult,
+                        int shift);
+/* Channel c = i / (n / nch) of the first nch (n / nch) elements:
+ * v = round_half_away(a * nmult[c] >> nshift[c]) (int64, unclamped),
+ * out = sat8(round_half_away(v * mult >> shift) + zp): i8_norm_requant_dma
+ * (16 channels, its fixed tables, 5 / 4 / 0). */
+int hexcuda_norm_requant_i8(int dev, const int8_t *a, int8_t *out, int64_t n, int nch,
+                            const int32_t *nmult, const int *nshift, int32_t mult, int shift,
+                            int zp);
+/* s8 GEMM -> int8 scores (sat8 of the accumulator, or with requant the
+ * round-half-away requant by mult / shift) -> hexcuda_lut_softmax_u8:
+ * i8_gemm_softmax_tile (B row-major), matmul_softmax_tile (K as Bt, requant). */
+int hexcuda_gemm_softmax_u8(int dev, const int8_t *A, const int8_t *B, int b_transposed,
+                            const uint8_t *exp_lut, uint8_t *out, int M, int N, int K,
+                            int requant, int32_t mult, int shift);
+/* gelu_ffn_residual: hid = gelu_lut[sat8(x W1 + b1) + 128]; s = sat8(hid W2 +
+ * b2 + x_res); out = hexcuda_layernorm_lut_i8(s, gamma, beta, inv_lut)
+ * (W1 [K,V], W2 [V,D] row-major; the intermediates stay in HBM). */
+int hexcuda_gelu_ffn_residual_i8(int dev, const int8_t *x, const int8_t *W1, const int32_t *b1,
+                                 const int8_t *gelu_lut, const int8_t *W2, const int32_t *b2,
+                                 const int8_t *x_res, const int8_t *gamma, const int8_t *beta,
+                                 const uint8_t *inv_lut, int8_t *out, int M, int K, int V, int D);
+
 /* Elementwise max (op 0) or min (op 1) of a[i] and b[i], or of a[i] and the
  * scalar c when b is null: hvx_vmax_i8, hvx_vmax_u8, hvx_vmin_i16,
  * hvx_vmin_u8, i8_max_scalar_dma, i8_min_scalar_dma.  elem I8, U8 or I16. */
@@ -495,6 +549,31 @@ int hexcuda_host_group_sum_i8(const int8_t *a, int32_t *out, int64_t g, int w);
 int hexcuda_host_scan_max_i8(const int8_t *in, int8_t *out, int64_t n);
 int hexcuda_host_head_group_reduce_i8(const int8_t *X, int8_t *Y, int H, int G, int64_t MN,
                                       int32_t mult, int shift);
+/* x has R rows, or xrows rows gathered through idx (idx not NULL) */
+int hexcuda_host_layernorm_lut_i8(const int8_t *x, int xrows, const int32_t *idx,
+                                  const int8_t *res, int8_t *out, int R, int W,
+                                  const int8_t *gamma, const int8_t *beta, const uint8_t *inv_lut,
+                                  int affine);
+int hexcuda_host_layernorm_lut_i16(const int16_t *x, int16_t *out, int R, int C,
+                                   const int16_t *gamma, const int16_t *beta,
+                                   const uint16_t *inv_lut, int order);
+int hexcuda_host_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C,
+                                const uint8_t *exp_lut);
+int hexcuda_host_lut_softmax_i16(const int16_t *x, int16_t *out, int R, int C,
+                                 const uint16_t *exp_lut);
+int hexcuda_host_requant_i16(const int32_t *a, int16_t *out, int64_t n, int32_t mult, int shift);
+/* one device */
+int hexcuda_host_norm_requant_i8(const int8_t *a, int8_t *out, int64_t n, int nch,
+                                 const int32_t *nmult, const int *nshift, int32_t mult, int shift,
+                                 int zp);
+int hexcuda_host_gemm_softmax_u8(const int8_t *A, const int8_t *B, int b_transposed,
+                                 const uint8_t *exp_lut, uint8_t *out, int M, int N, int K,
+                                 int requant, int32_t mult, int shift);
+int hexcuda_host_gelu_ffn_residual_i8(const int8_t *x, const int8_t *W1, const int32_t *b1,
+                                      const int8_t *gelu_lut, const int8_t *W2, const int32_t *b2,
+                                      const int8_t *x_res, const int8_t *gamma, const int8_t *beta,
+                                      const uint8_t *inv_lut, int8_t *out, int M, int K, int V,
+                                      int D);
 int hexcuda_host_gemm_i8_requant(const int8_t *A, const int8_t *B, int8_t *out,
                                  int M, int N, int K, int32_t mult, int shift,
                                  int8_t zp);

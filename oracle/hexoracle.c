@@ -1054,3 +1054,135 @@ void oracle_head_group_reduce_i8(const int8_t *X, int8_t *Y, int H, int G, int64
             Y[(int64_t)g * MN + i] = (int8_t)q;
         }
 }
+
+/* ---------------------------------- integer rows with the table arithmetic */
+static int32_t sat8i(int32_t v) { return v > 127 ? 127 : (v < -128 ? -128 : v); }
+
+/* i8_layernorm_dma/reference.c:4-28 (layernorm_row), i8_instance_norm/
+ * reference.c:4-40 (per channel: gamma[c], beta[c], table inv_lut + 256 c),
+ * i8_chunk_norm/reference.c:4-38 (chunk c: gamma + c chunk), layernorm_residual/
+ * reference.c:4-40 (saturating residual add first), embedding_layer_norm/
+ * reference.c:4-35 (rows gathered by idx) */
+void oracle_layernorm_lut_i8(const int8_t *x, const int32_t *idx, const int8_t *res, int8_t *out,
+                             int R, int W, const int8_t *gamma, const int8_t *beta,
+                             const uint8_t *inv_lut, int affine) {
+    int32_t *t = (int32_t *)malloc(sizeof(int32_t) * (size_t)W);
+    for (int r = 0; r < R; r++) {
+        const int8_t *xr = x + (size_t)(idx ? idx[r] : r) * W;
+        for (int j = 0; j < W; j++) t[j] = res ? sat8i((int32_t)xr[j] + res[(size_t)r * W + j]) : xr[j];
+        uint32_t sum = 0;
+        for (int j = 0; j < W; j++) sum += (uint32_t)t[j];
+        const int32_t mu = (int32_t)sum / W;
+        uint32_t vs = 0;
+        for (int j = 0; j < W; j++) {
+            const int32_t d = t[j] - mu;
+            vs += (uint32_t)(d * d);
+        }
+        const int32_t var = (int32_t)vs / W;
+        const int vi = var < 0 ? 0 : (var > 255 ? 255 : var);
+        const int32_t inv = (affine == 2 ? inv_lut + 256 * (size_t)r : inv_lut)[vi];
+        for (int j = 0; j < W; j++) {
+            const size_t gj = affine == 1 ? (size_t)r * W + j : (size_t)j;
+            const int32_t g = affine == 2 ? gamma[r] : gamma[gj];
+            const int32_t b = affine == 2 ? beta[r] : beta[gj];
+            const int32_t d = t[j] - mu;
+            const int32_t scaled = (d * g + 64) >> 7;
+            const int32_t normed = (scaled * inv + 128) >> 8;
+            out[(size_t)r * W + j] = (int8_t)sat8i(normed + b);
+        }
+    }
+    free(t);
+}
+
+/* layernorm_row_i16/reference.c:6-35, layernorm_affine_i16/reference.c:6-37 */
+void oracle_layernorm_lut_i16(const int16_t *x, int16_t *out, int R, int C, const int16_t *gamma,
+                              const int16_t *beta, const uint16_t *inv_lut, int order) {
+    for (int r = 0; r < R; r++) {
+        const int16_t *xr = x + (size_t)r * C;
+        int64_t sum = 0;
+        for (int c = 0; c < C; c++) sum += xr[c];
+        const int32_t mu = (int32_t)(sum / C);
+        int64_t vs = 0;
+        for (int c = 0; c < C; c++) {
+            const int64_t d = (int64_t)xr[c] - mu;
+            vs += d * d;
+        }
+        int32_t vi = (int32_t)((vs / C) >> 5);
+        vi = vi < 0 ? 0 : (vi > 255 ? 255 : vi);
+        const int32_t inv = inv_lut[vi];
+        for (int c = 0; c < C; c++) {
+            const int32_t d = (int32_t)xr[c] - mu;
+            int32_t v;
+            if (order == 0) {
+                const int32_t scaled = (d * (int32_t)gamma[c] + 32) >> 6;
+                v = ((scaled * inv + 512) >> 10) + beta[c];
+            } else {
+                const int32_t normed = (d * inv + 512) >> 10;
+                v = ((normed * (int32_t)gamma[r] + 32) >> 6) + beta[r];
+            }
+            out[(size_t)r * C + c] = (int16_t)(v > 32767 ? 32767 : (v < -32768 ? -32768 : v));
+        }
+    }
+}
+
+/* i8_gemm_softmax_tile/reference.c:28-48 */
+void oracle_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C, const uint8_t *exp_lut) {
+    for (int r = 0; r < R; r++) {
+        const int8_t *row = x + (size_t)r * C;
+        int8_t m = row[0];
+        for (int j = 1; j < C; j++) if (row[j] > m) m = row[j];
+        int32_t S = 0;
+        for (int j = 0; j < C; j++) {
+            int diff = (int)row[j] - (int)m;
+            if (diff < -255) diff = -255;
+            S += exp_lut[diff + 255];
+        }
+        const int32_t half = S / 2;
+        for (int j = 0; j < C; j++) {
+            int diff = (int)row[j] - (int)m;
+            if (diff < -255) diff = -255;
+            out[(size_t)r * C + j] = (uint8_t)(S > 0 ? (exp_lut[diff + 255] * 255 + half) / S : 0);
+        }
+    }
+}
+
+/* vtcm_softmax_row_i16/reference.c:6-30 */
+void oracle_lut_softmax_i16(const int16_t *x, int16_t *out, int R, int C, const uint16_t *exp_lut) {
+    for (int r = 0; r < R; r++) {
+        const int16_t *row = x + (size_t)r * C;
+        int16_t m = row[0];
+        for (int j = 1; j < C; j++) if (row[j] > m) m = row[j];
+        int64_t S = 0;
+        for (int j = 0; j < C; j++) {
+            int32_t diff = (int32_t)row[j] - (int32_t)m;
+            if (diff < -255) diff = -255;
+            S += exp_lut[diff + 255];
+        }
+        const int64_t half = S / 2;
+        for (int j = 0; j < C; j++) {
+            int32_t diff = (int32_t)row[j] - (int32_t)m;
+            if (diff < -255) diff = -255;
+            out[(size_t)r * C + j] = (int16_t)(S > 0 ? ((int64_t)exp_lut[diff + 255] * 32767 + half) / S : 0);
+        }
+    }
+}
+
+/* attention_scale_i16/reference.c:4-16 */
+void oracle_requant_i16(const int32_t *a, int16_t *out, int64_t n, int32_t mult, int shift) {
+    for (int64_t i = 0; i < n; i++) {
+        const int64_t q = rq_round((int64_t)a[i] * (int64_t)mult, shift);
+        out[i] = (int16_t)(q > 32767 ? 32767 : (q < -32768 ? -32768 : q));
+    }
+}
+
+/* i8_norm_requant_dma/reference.c:11-32 */
+void oracle_norm_requant_i8(const int8_t *a, int8_t *out, int64_t n, int nch, const int32_t *nmult,
+                            const int *nshift, int32_t mult, int shift, int zp) {
+    const int64_t per = n / nch;
+    for (int c = 0; c < nch; c++)
+        for (int64_t i = 0; i < per; i++) {
+            const int64_t v = rq_round((int64_t)a[c * per + i] * nmult[c], nshift[c]);
+            const int64_t r = rq_round(v * (int64_t)mult, shift) + zp;
+            out[c * per + i] = (int8_t)(r > 127 ? 127 : (r < -128 ? -128 : r));
+        }
+}

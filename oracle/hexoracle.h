@@ -281,6 +281,28 @@ void oracle_scan_max_i8(const int8_t *in, int8_t *out, int64_t n);
 void oracle_head_group_reduce_i8(const int8_t *X, int8_t *Y, int H, int G, int64_t MN,
                                  int32_t mult, int shift);
 
+/* int8 layernorm with an inverse-variance table (affine 0 shared gamma[j],
+ * 1 rowwise gamma[r W + j], 2 per-row gamma[r] with the table inv_lut + 256 r;
+ * idx: gathered rows; res: saturating residual first).
+ * kernels/expert/{i8_layernorm_dma,i8_instance_norm,i8_chunk_norm,
+ * layernorm_residual,embedding_layer_norm}/reference.c */
+void oracle_layernorm_lut_i8(const int8_t *x, const int32_t *idx, const int8_t *res, int8_t *out,
+                             int R, int W, const int8_t *gamma, const int8_t *beta,
+                             const uint8_t *inv_lut, int affine);
+/* layernorm_row_i16/reference.c (order 0), layernorm_affine_i16/reference.c (1) */
+void oracle_layernorm_lut_i16(const int16_t *x, int16_t *out, int R, int C, const int16_t *gamma,
+                              const int16_t *beta, const uint16_t *inv_lut, int order);
+/* row softmax by an exp table: i8_gemm_softmax_tile/reference.c step C (u8),
+ * vtcm_softmax_row_i16/reference.c (i16) */
+void oracle_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C, const uint8_t *exp_lut);
+void oracle_lut_softmax_i16(const int16_t *x, int16_t *out, int R, int C, const uint16_t *exp_lut);
+/* attention_scale_i16/reference.c */
+void oracle_requant_i16(const int32_t *a, int16_t *out, int64_t n, int32_t mult, int shift);
+/* i8_norm_requant_dma/reference.c:11-32 with the channel count and tables as
+ * parameters */
+void oracle_norm_requant_i8(const int8_t *a, int8_t *out, int64_t n, int nch, const int32_t *nmult,
+                            const int *nshift, int32_t mult, int shift, int zp);
+
 enum {
     ORACLE_OP_I8_GEMM_REQUANT = 1,
     ORACLE_OP_GEMM_U8S8_PC = 2,

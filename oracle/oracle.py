@@ -483,3 +483,75 @@ def head_group_reduce_i8(X, G, mult, shift):
     lib().oracle_head_group_reduce_i8(_p(X), _p(Y), H, G, C.c_int64(MN), C.c_int32(int(mult)),
                                       shift)
     return Y
+
+
+LN_AFFINE = {"shared": 0, "rowwise": 1, "per_row": 2}
+
+
+def layernorm_lut_i8(x, gamma, beta, inv_lut, affine="shared", res=None, idx=None):
+    x = np.ascontiguousarray(x, np.int8)
+    W = x.shape[1]
+    idx = np.ascontiguousarray(idx, np.int32) if idx is not None else None
+    R = idx.size if idx is not None else x.shape[0]
+    res = np.ascontiguousarray(res, np.int8) if res is not None else None
+    g, b, lut = (np.ascontiguousarray(gamma, np.int8), np.ascontiguousarray(beta, np.int8),
+                 np.ascontiguousarray(inv_lut, np.uint8))
+    out = np.zeros((R, W), np.int8)
+    lib().oracle_layernorm_lut_i8(_p(x), None if idx is None else _p(idx),
+                                  None if res is None else _p(res), _p(out), R, W, _p(g), _p(b),
+                                  _p(lut), LN_AFFINE[affine])
+    return out
+
+
+def layernorm_lut_i16(x, gamma, beta, inv_lut, order=0):
+    x = np.ascontiguousarray(x, np.int16)
+    R, Cc = x.shape
+    out = np.zeros_like(x)
+    g, b, lut = (np.ascontiguousarray(gamma, np.int16), np.ascontiguousarray(beta, np.int16),
+                 np.ascontiguousarray(inv_lut, np.uint16))
+    lib().oracle_layernorm_lut_i16(_p(x), _p(out), R, Cc, _p(g), _p(b), _p(lut), order)
+    return out
+
+
+def lut_softmax_u8(x, exp_lut):
+    x = np.ascontiguousarray(x, np.int8)
+    out = np.zeros(x.shape, np.uint8)
+    lut = np.ascontiguousarray(exp_lut, np.uint8)
+    lib().oracle_lut_softmax_u8(_p(x), _p(out), x.shape[0], x.shape[1], _p(lut))
+    return out
+
+
+def lut_softmax_i16(x, exp_lut):
+    x = np.ascontiguousarray(x, np.int16)
+    out = np.zeros_like(x)
+    lut = np.ascontiguousarray(exp_lut, np.uint16)
+    lib().oracle_lut_softmax_i16(_p(x), _p(out), x.shape[0], x.shape[1], _p(lut))
+    return out
+
+
+def requant_i16(a, mult, shift):
+    a = np.ascontiguousarray(a, np.int32)
+    out = np.zeros(a.shape, np.int16)
+    lib().oracle_requant_i16(_p(a), _p(out), C.c_int64(a.size), C.c_int32(mult), shift)
+    return out
+
+
+def norm_requant_i8(a, nmult, nshift, mult, shift, zp=0):
+    a = np.ascontiguousarray(a, np.int8).ravel()
+    nm, ns = np.ascontiguousarray(nmult, np.int32), np.ascontiguousarray(nshift, np.int32)
+    out = np.zeros_like(a)
+    lib().oracle_norm_requant_i8(_p(a), _p(out), C.c_int64(a.size), nm.size, _p(nm), _p(ns),
+                                 C.c_int32(mult), shift, zp)
+    return out
+
+
+def gemm_softmax_u8(A, B, exp_lut, b_transposed=False, requant=False, mult=1, shift=0):
+    sc = (gemm_i8_rq_ex(A, B, mult, shift, 0, b_transposed=b_transposed) if requant
+          else gemm_i8_acc(A, B, "i8_sat", b_transposed=b_transposed))
+    return lut_softmax_u8(sc, exp_lut)
+
+
+def gelu_ffn_residual_i8(x, W1, b1, gelu_lut, W2, b2, x_res, gamma, beta, inv_lut):
+    hid = gemm_i8_acc(x, W1, "lut_i8", bias=b1, lut=gelu_lut)
+    s = gemm_i8_acc(hid, W2, "i8_sat", bias=b2, res=np.ascontiguousarray(x_res, np.int8))
+    return layernorm_lut_i8(s, gamma, beta, inv_lut)

@@ -895,6 +895,94 @@ def gen_i8_acc_callers(ref):
     save("i8_acc_callers", **a)
 
 
+def gen_int_rows(ref):
+    # The attention-tile callers, the integer layernorms with an inverse-
+    # variance table, the exp-table softmax tiles, the int16 requant, the
+    # per-channel double requant and the GELU FFN block through their
+    # reference.c: full-range int8 operands; int16 layernorms with |gamma| <=
+    # 1024 (the reference's int32 products stay defined); the fixed shapes of
+    # the tile and FFN references.
+    rng = np.random.default_rng(113)
+    s8 = lambda *sh: rng.integers(-128, 128, sh, dtype=np.int8)
+    u8 = lambda *sh: rng.integers(0, 256, sh, dtype=np.uint8)
+    a = {}
+
+    def run(name, args, **arrs):
+        getattr(ref, "ref_" + name)(*args)
+        for k, v in arrs.items():
+            a[f"{name}__{k}"] = v
+
+    M, N, D = 40, 50, 64
+    for name, kshape in (("attention_qkt_tile", (N, D)), ("qkt_tile_i8", (D, N))):
+        Q, K = s8(M, D), s8(*kshape)
+        S = np.zeros((M, N), np.int8)
+        run(name, (ptr(Q), ptr(K), ptr(S), M, N, D, C.c_int32(1 << 20), 26), Q=Q, K=K, out=S)
+    for name, vshape in (("attention_av_tile", (N, D)), ("av_tile_i8", (D, N))):
+        A, V = s8(M, N), s8(*vshape)
+        O = np.zeros((M, D), np.int32)
+        run(name, (ptr(A), ptr(V), ptr(O), M, N, D), A=A, V=V, out=O)
+    raw = rng.integers(-2**31, 2**31, (33, 47), dtype=np.int64).astype(np.int32)
+    o16 = np.zeros((33, 47), np.int16)
+    run("attention_scale_i16", (ptr(raw), ptr(o16), 33, 47, C.c_int32(1 << 20), 30), raw=raw, out=o16)
+    lut_e = u8(511)
+    lut_e[255] = max(int(lut_e[255]), 1)
+    a["exp_lut"] = lut_e
+    A, B = s8(16, 16), s8(16, 16)
+    o = np.zeros((16, 16), np.uint8)
+    run("i8_gemm_softmax_tile", (ptr(A), ptr(B), ptr(o), ptr(lut_e)), A=A, B=B, out=o)
+    Q, K = s8(16, 32), s8(16, 32)
+    o = np.zeros((16, 16), np.uint8)
+    run("matmul_softmax_tile", (ptr(Q), ptr(K), ptr(o), ptr(lut_e), C.c_int32(3000), 12), Q=Q, K=K, out=o)
+    inv = u8(256)
+    a["inv_lut"] = inv
+    R, W = 37, 200
+    x, g, b = s8(R, W), s8(W), s8(W)
+    o = np.zeros((R, W), np.int8)
+    run("i8_layernorm_dma", (ptr(x), ptr(o), R, W, ptr(g), ptr(b), ptr(inv)), x=x, gamma=g, beta=b, out=o)
+    H, Wd, Cc = 9, 11, 5
+    x, g, b, cl = s8(Cc, H * Wd), s8(Cc), s8(Cc), u8(Cc, 256)
+    o = np.zeros((Cc, H * Wd), np.int8)
+    run("i8_instance_norm", (ptr(x), ptr(o), H, Wd, Cc, ptr(g), ptr(b), ptr(cl)), x=x, gamma=g, beta=b,
+        lut=cl, out=o)
+    n, G = 7 * 60 + 3, 7
+    x, g, b = s8(n), s8(n), s8(n)
+    o = np.zeros(n, np.int8)
+    run("i8_chunk_norm", (ptr(x), ptr(o), n, G, ptr(g), ptr(b), ptr(inv)), x=x, gamma=g, beta=b, out=o)
+    n = 256
+    x, r, g, b = s8(n), s8(n), s8(n), s8(n)
+    o = np.zeros(n, np.int8)
+    run("layernorm_residual", (ptr(x), ptr(r), ptr(o), n, ptr(g), ptr(b), ptr(inv)), x=x, res=r, gamma=g,
+        beta=b, out=o)
+    tab, idx = s8(50, 64), rng.integers(0, 50, 40).astype(np.int32)
+    g, b = s8(64), s8(64)
+    o = np.zeros((40, 64), np.int8)
+    run("embedding_layer_norm", (ptr(tab), ptr(idx), ptr(o), 40, 64, ptr(g), ptr(b), ptr(inv)), table=tab,
+        idx=idx, gamma=g, beta=b, out=o)
+    R, Cc = 9, 300
+    inv16 = rng.integers(0, 65536, 256).astype(np.uint16)
+    a["inv_lut16"] = inv16
+    x = rng.integers(-32768, 32768, (R, Cc)).astype(np.int16)
+    for name, gn in (("layernorm_row_i16", Cc), ("layernorm_affine_i16", R)):
+        g = rng.integers(-1024, 1025, gn).astype(np.int16)
+        b = rng.integers(-32768, 32768, gn).astype(np.int16)
+        o = np.zeros((R, Cc), np.int16)
+        run(name, (ptr(x), ptr(o), R, Cc, ptr(g), ptr(b), ptr(inv16)), x=x, gamma=g, beta=b, out=o)
+    n = 16 * 130 + 5
+    x = s8(n)
+    o = np.zeros(n, np.int8)
+    run("i8_norm_requant_dma", (ptr(x), ptr(o), n), x=x, out=o)
+    M, K, V, D = 8, 16, 32, 16
+    x, W1, W2, xr = s8(M, K), s8(K, V), s8(V, D), s8(M, D)
+    b1 = rng.integers(-3000, 3000, V).astype(np.int32)
+    b2 = rng.integers(-3000, 3000, D).astype(np.int32)
+    gl, g, b = s8(256), s8(D), s8(D)
+    o = np.zeros((M, D), np.int8)
+    run("gelu_ffn_residual", (ptr(x), ptr(W1), ptr(b1), ptr(gl), ptr(W2), ptr(b2), ptr(xr), ptr(g), ptr(b),
+                              ptr(inv), ptr(o), M, K, V, D),
+        x=x, W1=W1, b1=b1, gelu_lut=gl, W2=W2, b2=b2, x_res=xr, gamma=g, beta=b, out=o)
+    save("int_rows", **a)
+
+
 def main():
     if not (REF_ROOT / "kernels").is_dir():
         sys.exit(f"reference tree not found at {REF_ROOT}")
@@ -915,6 +1003,7 @@ def main():
     gen_i8_callers(ref)
     gen_reduce_family(ref)
     gen_i8_acc_callers(ref)
+    gen_int_rows(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

@@ -1,0 +1,118 @@
+"""Integer row operators on the B200 (table layernorms, exp-table softmaxes,
+int16 and double requants, GEMM + softmax tiles, the GELU FFN block),
+bit-exact against the reference's outputs (golden int_rows) and the oracle
+on larger and ragged shapes; the shims of the bundles whose harnesses need
+the Hexagon SDK on their golden cases."""
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from conftest import golden
+from test_oracle_golden import NORM_MULT, NORM_SHIFT, int_rows_calls
+
+pytestmark = pytest.mark.gpu
+
+SHIMS = Path(__file__).resolve().parent.parent / "hexkernels_b200" / "shims"
+
+
+def test_int_rows_golden(hx):
+    for k, (got, exp) in enumerate(int_rows_calls(hx, golden("int_rows"))):
+        np.testing.assert_array_equal(got, exp, err_msg=str(k))
+
+
+def shim(name):
+    so = SHIMS / f"libcand_{name}.so"
+    if not so.exists():
+        subprocess.run(["make", "-s", "-C", str(SHIMS)], check=True)
+    fn = C.CDLL(str(so)).candidate_kernel
+    fn.restype = None
+    return fn
+
+
+def p(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def test_sdk_harness_bundles_through_shims(hx, oracle):
+    g = golden("int_rows")
+    n = "i8_layernorm_dma"
+    x = g[n + "__x"]
+    out = np.zeros_like(x)
+    shim(n)(p(x), p(out), x.shape[0], x.shape[1], p(g[n + "__gamma"]), p(g[n + "__beta"]), p(g["inv_lut"]))
+    np.testing.assert_array_equal(out, g[n + "__out"])
+    n = "i8_norm_requant_dma"
+    x = g[n + "__x"]
+    out = np.zeros_like(x)
+    shim(n)(p(x), p(out), x.size)
+    np.testing.assert_array_equal(out, g[n + "__out"])
+    rng = np.random.default_rng(9)
+    x16 = rng.integers(-20000, 20000, (33, 517)).astype(np.int16)
+    lut16 = rng.integers(0, 65536, 256).astype(np.uint16)
+    out16 = np.zeros_like(x16)
+    shim("vtcm_softmax_row_i16")(p(x16), p(out16), 33, 517, p(lut16))
+    np.testing.assert_array_equal(out16, oracle.lut_softmax_i16(x16, lut16))
+
+
+@pytest.mark.parametrize("R,W", [(1, 1), (7, 33), (300, 200), (4096, 64), (65, 4099)])
+def test_layernorm_lut_i8_random(hx, oracle, R, W):
+    rng = np.random.default_rng(R * 3 + W)
+    s8 = lambda *sh: rng.integers(-128, 128, sh, dtype=np.int8)
+    x, res = s8(R, W), s8(R, W)
+    inv = rng.integers(0, 256, 256, dtype=np.uint8)
+    g, b = s8(W), s8(W)
+    for kw in (dict(), dict(res=res)):
+        np.testing.assert_array_equal(hx.layernorm_lut_i8(x, g, b, inv, **kw),
+                                      oracle.layernorm_lut_i8(x, g, b, inv, **kw))
+    gr, br = s8(R * W), s8(R * W)
+    np.testing.assert_array_equal(hx.layernorm_lut_i8(x, gr, br, inv, "rowwise"),
+                                  oracle.layernorm_lut_i8(x, gr, br, inv, "rowwise"))
+    gp, bp, lp = s8(R), s8(R), rng.integers(0, 256, (R, 256), dtype=np.uint8)
+    np.testing.assert_array_equal(hx.layernorm_lut_i8(x, gp, bp, lp, "per_row"),
+                                  oracle.layernorm_lut_i8(x, gp, bp, lp, "per_row"))
+    idx = rng.integers(0, R, 3 * R + 1).astype(np.int32)
+    np.testing.assert_array_equal(hx.layernorm_lut_i8(x, g, b, inv, idx=idx),
+                                  oracle.layernorm_lut_i8(x, g, b, inv, idx=idx))
+
+
+@pytest.mark.parametrize("R,C", [(1, 1), (9, 300), (2048, 256), (3, 10000)])
+def test_layernorm_lut_i16_and_softmaxes(hx, oracle, R, C):
+    rng = np.random.default_rng(R + C)
+    x = rng.integers(-32768, 32768, (R, C)).astype(np.int16)
+    inv = rng.integers(0, 65536, 256).astype(np.uint16)
+    gc, bc = (rng.integers(-1024, 1025, C).astype(np.int16), rng.integers(-32768, 32768, C).astype(np.int16))
+    gr, br = (rng.integers(-1024, 1025, R).astype(np.int16), rng.integers(-32768, 32768, R).astype(np.int16))
+    np.testing.assert_array_equal(hx.layernorm_lut_i16(x, gc, bc, inv, 0), oracle.layernorm_lut_i16(x, gc, bc, inv, 0))
+    np.testing.assert_array_equal(hx.layernorm_lut_i16(x, gr, br, inv, 1), oracle.layernorm_lut_i16(x, gr, br, inv, 1))
+    lut16 = rng.integers(0, 65536, 256).astype(np.uint16)
+    lut16[255] |= 1
+    np.testing.assert_array_equal(hx.lut_softmax_i16(x, lut16), oracle.lut_softmax_i16(x, lut16))
+    x8 = rng.integers(-128, 128, (R, C), dtype=np.int8)
+    lut8 = rng.integers(0, 256, 256, dtype=np.uint8)
+    lut8[255] |= 1
+    np.testing.assert_array_equal(hx.lut_softmax_u8(x8, lut8), oracle.lut_softmax_u8(x8, lut8))
+
+
+def test_requants_and_compositions(hx, oracle):
+    rng = np.random.default_rng(17)
+    a = rng.integers(-2**31, 2**31, (1 << 22) + 7, dtype=np.int64).astype(np.int32)
+    for mult, shift in ((1 << 20, 30), (-77777, 9), (1, 0), (2**31 - 1, 63)):
+        np.testing.assert_array_equal(hx.requant_i16(a, mult, shift), oracle.requant_i16(a, mult, shift))
+    x = rng.integers(-128, 128, 16 * 100003 + 11, dtype=np.int8)
+    np.testing.assert_array_equal(hx.norm_requant_i8(x, NORM_MULT, NORM_SHIFT, 5, 4, 0),
+                                  oracle.norm_requant_i8(x, NORM_MULT, NORM_SHIFT, 5, 4, 0))
+    A, B = (rng.integers(-128, 128, (300, 256), dtype=np.int8), rng.integers(-128, 128, (256, 520), dtype=np.int8))
+    lut = rng.integers(0, 256, 256, dtype=np.uint8)
+    lut[255] |= 1
+    np.testing.assert_array_equal(hx.gemm_softmax_u8(A, B, lut), oracle.gemm_softmax_u8(A, B, lut))
+    Bt = np.ascontiguousarray(B.T)
+    np.testing.assert_array_equal(hx.gemm_softmax_u8(A, Bt, lut, True, True, 3000, 14),
+                                  oracle.gemm_softmax_u8(A, Bt, lut, True, True, 3000, 14))
+    M, K, V, D = 200, 128, 256, 96
+    s8 = lambda *sh: rng.integers(-128, 128, sh, dtype=np.int8)
+    args = (s8(M, K), s8(K, V), rng.integers(-3000, 3000, V).astype(np.int32), s8(256), s8(V, D),
+            rng.integers(-3000, 3000, D).astype(np.int32), s8(M, D), s8(D), s8(D),
+            rng.integers(0, 256, 256, dtype=np.uint8))
+    np.testing.assert_array_equal(hx.gelu_ffn_residual_i8(*args), oracle.gelu_ffn_residual_i8(*args))

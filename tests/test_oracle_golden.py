@@ -365,3 +365,71 @@ def i8_acc_calls(impl, g):
 def test_i8_acc_callers_golden(oracle):
     for got, exp in i8_acc_calls(oracle, golden("i8_acc_callers")):
         np.testing.assert_array_equal(got, exp)
+
+
+NORM_MULT = np.array([3, 5, 7, 9, 11, 13, 15, 17, 3, 5, 7, 9, 11, 13, 15, 17], np.int32)
+NORM_SHIFT = np.array([2, 3, 4, 5, 3, 4, 5, 6, 2, 3, 4, 5, 3, 4, 5, 6], np.int32)
+
+
+def int_rows_calls(impl, g):
+    """(result, expected) of the attention-tile callers, the table layernorms
+    and softmaxes, the int16 requant, the double requant and the GELU FFN
+    block (golden int_rows) through `impl` (the oracle or the GPU ops)."""
+    c = lambda n, k: g[f"{n}__{k}"]
+    yield (impl.gemm_i8_rq_ex(c("attention_qkt_tile", "Q"), c("attention_qkt_tile", "K"), 1 << 20, 26, 0,
+                              b_transposed=True), c("attention_qkt_tile", "out"))
+    yield (impl.gemm_i8_rq_ex(c("qkt_tile_i8", "Q"), c("qkt_tile_i8", "K"), 1 << 20, 26, 0),
+           c("qkt_tile_i8", "out"))
+    yield impl.gemm_i8_acc(c("attention_av_tile", "A"), c("attention_av_tile", "V")), c("attention_av_tile", "out")
+    yield (impl.gemm_i8_acc(c("av_tile_i8", "A"), c("av_tile_i8", "V"), b_transposed=True),
+           c("av_tile_i8", "out"))
+    yield impl.requant_i16(c("attention_scale_i16", "raw"), 1 << 20, 30), c("attention_scale_i16", "out")
+    lut = g["exp_lut"][:256]
+    yield (impl.gemm_softmax_u8(c("i8_gemm_softmax_tile", "A"), c("i8_gemm_softmax_tile", "B"), lut),
+           c("i8_gemm_softmax_tile", "out"))
+    yield (impl.gemm_softmax_u8(c("matmul_softmax_tile", "Q"), c("matmul_softmax_tile", "K"), lut,
+                                b_transposed=True, requant=True, mult=3000, shift=12),
+           c("matmul_softmax_tile", "out"))
+    inv = g["inv_lut"]
+    n = "i8_layernorm_dma"
+    yield impl.layernorm_lut_i8(c(n, "x"), c(n, "gamma"), c(n, "beta"), inv), c(n, "out")
+    n = "i8_instance_norm"
+    yield (impl.layernorm_lut_i8(c(n, "x"), c(n, "gamma"), c(n, "beta"), c(n, "lut"), "per_row"),
+           c(n, "out"))
+    n = "i8_chunk_norm"
+    ch = c(n, "x").size // 7
+    got = impl.layernorm_lut_i8(c(n, "x")[:7 * ch].reshape(7, ch), c(n, "gamma")[:7 * ch],
+                                c(n, "beta")[:7 * ch], inv, "rowwise").ravel()
+    yield got, c(n, "out")[:7 * ch]
+    n = "layernorm_residual"
+    yield (impl.layernorm_lut_i8(c(n, "x")[None], c(n, "gamma"), c(n, "beta"), inv,
+                                 res=c(n, "res")[None])[0], c(n, "out"))
+    n = "embedding_layer_norm"
+    yield (impl.layernorm_lut_i8(c(n, "table"), c(n, "gamma"), c(n, "beta"), inv, idx=c(n, "idx")),
+           c(n, "out"))
+    for n, order in (("layernorm_row_i16", 0), ("layernorm_affine_i16", 1)):
+        yield impl.layernorm_lut_i16(c(n, "x"), c(n, "gamma"), c(n, "beta"), g["inv_lut16"], order), c(n, "out")
+    n = "i8_norm_requant_dma"
+    yield impl.norm_requant_i8(c(n, "x"), NORM_MULT, NORM_SHIFT, 5, 4, 0), c(n, "out")
+    n = "gelu_ffn_residual"
+    yield (impl.gelu_ffn_residual_i8(*(c(n, k) for k in ("x", "W1", "b1", "gelu_lut", "W2", "b2", "x_res",
+                                                          "gamma", "beta")), inv), c(n, "out"))
+
+
+def test_int_rows_golden(oracle):
+    for k, (got, exp) in enumerate(int_rows_calls(oracle, golden("int_rows"))):
+        np.testing.assert_array_equal(got, exp, err_msg=str(k))
+
+
+def test_lut_softmax_i16_properties(oracle):
+    """vtcm_softmax_row_i16 (its reference needs the Hexagon SDK headers and
+    is not built): the restatement's rows are non-negative, the row maximum
+    maps to the largest value, and a constant row gives equal values."""
+    rng = np.random.default_rng(4)
+    lut = np.sort(rng.integers(1, 65536, 256).astype(np.uint16))
+    x = rng.integers(-3000, 3000, (20, 300)).astype(np.int16)
+    p = oracle.lut_softmax_i16(x, lut)
+    assert (p >= 0).all()
+    assert (p[np.arange(20), x.argmax(1)] == p.max(1)).all()
+    flat = oracle.lut_softmax_i16(np.full((2, 64), 7, np.int16), lut)
+    assert (flat == flat[0, 0]).all()

@@ -52,6 +52,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_layernorm_f16": (I, [I, P, P, P, P, I, I, F]),
     "hexcuda_rmsnorm_f32": (I, [I, P, P, P, I, I, F]),
     "hexcuda_rmsnorm_f16": (I, [I, P, P, P, I, I, F]),
+    "hexcuda_rmsnorm_gain_f16": (I, [I, P, P, P, I, I, F]),
     "hexcuda_rowreduce_f32": (I, [I, P, P, I, I, I]),
     "hexcuda_requant_per_channel": (I, [I, P, P, I, I, P, P, I8]),
     "hexcuda_requantize_i32_u8": (I, [I, P, P, I64, I32, I, U8]),
@@ -78,7 +79,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_head_group_reduce_i8": (I, [I, P, P, I, I, I64, I32, I]),
     "hexcuda_layernorm_lut_i8": (I, [I, P, P, P, P, I, I, P, P, P, I]),
     "hexcuda_layernorm_lut_i16": (I, [I, P, P, I, I, P, P, P, I]),
-    "hexcuda_lut_softmax_u8": (I, [I, P, P, I, I, P]),
+    "hexcuda_lut_softmax_u8": (I, [I, P, P, I, I, P, P]),
     "hexcuda_lut_softmax_i16": (I, [I, P, P, I, I, P]),
     "hexcuda_requant_i16": (I, [I, P, P, I64, I32, I]),
     "hexcuda_norm_requant_i8": (I, [I, P, P, I64, I, P, P, I32, I, I]),
@@ -97,6 +98,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_layernorm_f32": (I, [P, P, P, P, I, I, F]),
     "hexcuda_host_layernorm_f16": (I, [P, P, P, P, I, I, F]),
     "hexcuda_host_rmsnorm_f16": (I, [P, P, P, I, I, F]),
+    "hexcuda_host_rmsnorm_gain_f16": (I, [P, P, P, I, I, F]),
     "hexcuda_host_rowreduce_f32": (I, [P, P, I, I, I]),
     "hexcuda_host_requant_per_channel": (I, [P, P, I, I, P, P, I8]),
     "hexcuda_host_requantize_i32_u8": (I, [P, P, I64, I32, I, U8]),
@@ -123,7 +125,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_head_group_reduce_i8": (I, [P, P, I, I, I64, I32, I]),
     "hexcuda_host_layernorm_lut_i8": (I, [P, I, P, P, P, I, I, P, P, P, I]),
     "hexcuda_host_layernorm_lut_i16": (I, [P, P, I, I, P, P, P, I]),
-    "hexcuda_host_lut_softmax_u8": (I, [P, P, I, I, P]),
+    "hexcuda_host_lut_softmax_u8": (I, [P, P, I, I, P, P]),
     "hexcuda_host_lut_softmax_i16": (I, [P, P, I, I, P]),
     "hexcuda_host_requant_i16": (I, [P, P, I64, I32, I]),
     "hexcuda_host_norm_requant_i8": (I, [P, P, I64, I, P, P, I32, I, I]),

@@ -262,6 +262,22 @@ HX_EXPORT int hexcuda_host_layernorm_f16(const uint16_t *x, const uint16_t *gamm
     });
 }
 
+HX_EXPORT int hexcuda_host_rmsnorm_gain_f16(const uint16_t *x, const uint16_t *gain, uint16_t *out,
+                                            int R, int C, float eps) {
+    if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_rmsnorm_gain_f16: R=%d C=%d", R, C);
+    if (R == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_rmsnorm_gain_f16", {x, gain, out})) return rc;
+    return run_sharded(R, out, 2 * (size_t)C, [&](Part &p) {
+        int64_t nr = p.r1 - p.r0;
+        const uint16_t *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
+        const uint16_t *dg = stage_in(p.d, kSlotIn1, gain + p.r0, (size_t)nr);
+        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * nr * C));
+        if (!dx || !dg || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_rmsnorm_gain_f16(p.slot, dx, dg, dout, (int)nr, C, eps);
+    });
+}
+
 HX_EXPORT int hexcuda_host_rmsnorm_f16(const uint16_t *x, const uint16_t *gamma, uint16_t *out,
                                        int R, int C, float eps) {
     if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_rmsnorm_f16: R=%d C=%d", R, C);
@@ -883,10 +899,12 @@ HX_EXPORT int hexcuda_host_layernorm_lut_i8(const int8_t *x, int xrows, const in
                                             const int8_t *gamma, const int8_t *beta,
                                             const uint8_t *inv_lut, int affine) {
     if (R < 0 || W < 1 || (idx && xrows < 1) || affine < HEXCUDA_LN_AFFINE_SHARED ||
-        affine > HEXCUDA_LN_AFFINE_PER_ROW)
+        affine > HEXCUDA_LN_RMS_SHARED)
         return fail(HEXCUDA_ERR_ARG, "host_layernorm_lut_i8: R %d W %d affine %d", R, W, affine);
     if (R == 0) return HEXCUDA_OK;
-    if (int rc = null_check("host_layernorm_lut_i8", {x, out, gamma, beta, inv_lut})) return rc;
+    const bool rms = affine == HEXCUDA_LN_RMS_SHARED;
+    if (int rc = null_check("host_layernorm_lut_i8", {x, out, gamma, rms ? gamma : beta, inv_lut}))
+        return rc;
     return run_sharded(R, out, (size_t)W, [&](Part &p) {
         const int64_t nr = p.r1 - p.r0;
         const int8_t *dx = idx ? stage_in(p.d, kSlotIn0, x, (size_t)xrows * W)
@@ -897,10 +915,10 @@ HX_EXPORT int hexcuda_host_layernorm_lut_i8(const int8_t *x, int xrows, const in
         if (affine == HEXCUDA_LN_AFFINE_ROWWISE) g0 = p.r0 * W, gn = nr * W;
         if (affine == HEXCUDA_LN_AFFINE_PER_ROW) g0 = p.r0, gn = nr, l0 = p.r0 * 256, ln = nr * 256;
         const int8_t *dg = stage_in(p.d, kSlotIn3, gamma + g0, (size_t)gn);
-        const int8_t *db = stage_in(p.d, kSlotIn4, beta + g0, (size_t)gn);
+        const int8_t *db = rms ? nullptr : stage_in(p.d, kSlotIn4, beta + g0, (size_t)gn);
         const uint8_t *dl = stage_in(p.d, kSlotIn5, inv_lut + l0, (size_t)ln);
         int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * W)));
-        if (!dx || (idx && !di) || (res && !dr) || !dg || !db || !dl || !dout)
+        if (!dx || (idx && !di) || (res && !dr) || !dg || (!rms && !db) || !dl || !dout)
             return hexcuda_last_error();
         p.dout = dout;
         return hexcuda_layernorm_lut_i8(p.slot, dx, di, dr, dout, (int)nr, W, dg, db, dl, affine);
@@ -929,7 +947,7 @@ HX_EXPORT int hexcuda_host_layernorm_lut_i16(const int16_t *x, int16_t *out, int
 }
 
 HX_EXPORT int hexcuda_host_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C,
-                                          const uint8_t *exp_lut) {
+                                          const uint8_t *exp_lut, const uint16_t *recip_lut) {
     if (R < 0 || C < 1) return fail(HEXCUDA_ERR_ARG, "host_lut_softmax_u8: R %d C %d", R, C);
     if (R == 0) return HEXCUDA_OK;
     if (int rc = null_check("host_lut_softmax_u8", {x, out, exp_lut})) return rc;
@@ -937,10 +955,11 @@ HX_EXPORT int hexcuda_host_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, 
         const int64_t nr = p.r1 - p.r0;
         const int8_t *dx = stage_in(p.d, kSlotIn0, x + p.r0 * C, (size_t)(nr * C));
         const uint8_t *dl = stage_in(p.d, kSlotIn1, exp_lut, 256);
+        const uint16_t *dr = recip_lut ? stage_in(p.d, kSlotIn2, recip_lut, 256) : nullptr;
         uint8_t *dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * C)));
-        if (!dx || !dl || !dout) return hexcuda_last_error();
+        if (!dx || !dl || (recip_lut && !dr) || !dout) return hexcuda_last_error();
         p.dout = dout;
-        return hexcuda_lut_softmax_u8(p.slot, dx, dout, (int)nr, C, dl);
+        return hexcuda_lut_softmax_u8(p.slot, dx, dout, (int)nr, C, dl, dr);
     });
 }
 

@@ -50,7 +50,8 @@ __device__ __forceinline__ int sat16(int v) { return v > 32767 ? 32767 : (v < -3
 // residual); mu = sum / W; var = sum (t - mu)^2 / W (int32, C division);
 // inv = lut[clamp(var, 0, 255)]; out = sat8((((t - mu) g + 64) >> 7) inv + 128)
 // >> 8) + b).  affine: SHARED g[j], b[j]; ROWWISE g[r W + j], b[r W + j];
-// PER_ROW g[r], b[r] and the table lut + 256 r.
+// PER_ROW g[r], b[r] and the table lut + 256 r.  RMS_SHARED: mu = 0, no b
+// (rmsnorm_residual/reference.c: var = sum t^2 / W, out = sat8(normed)).
 __global__ void __launch_bounds__(256) layernorm_lut_i8_kernel(
     const int8_t *__restrict__ x, const int32_t *__restrict__ idx, const int8_t *__restrict__ res,
     int8_t *__restrict__ out, int R, int W, const int8_t *__restrict__ gamma,
@@ -64,9 +65,11 @@ __global__ void __launch_bounds__(256) layernorm_lut_i8_kernel(
             if (rr) t = sat8(t + rr[j]);
             return t;
         };
+        const bool rms = affine == HEXCUDA_LN_RMS_SHARED;
         int32_t s = 0;
-        for (int j = lane; j < W; j += 32) s += load(j);
-        const int32_t mu = warp_sum_i32(s) / W;
+        if (!rms)
+            for (int j = lane; j < W; j += 32) s += load(j);
+        const int32_t mu = rms ? 0 : warp_sum_i32(s) / W;
         uint32_t vs = 0;
         for (int j = lane; j < W; j += 32) {
             const int32_t d = load(j) - mu;
@@ -78,8 +81,10 @@ __global__ void __launch_bounds__(256) layernorm_lut_i8_kernel(
         const int32_t inv = tl[vi];
         int8_t *orow = out + (size_t)r * W;
         for (int j = lane; j < W; j += 32) {
-            int32_t g, b;
-            if (affine == HEXCUDA_LN_AFFINE_PER_ROW) {
+            int32_t g, b = 0;
+            if (rms) {
+                g = gamma[j];
+            } else if (affine == HEXCUDA_LN_AFFINE_PER_ROW) {
                 g = gamma[r];
                 b = beta[r];
             } else {
@@ -90,7 +95,7 @@ __global__ void __launch_bounds__(256) layernorm_lut_i8_kernel(
             const int32_t d = load(j) - mu;
             const int32_t scaled = (d * g + 64) >> 7;
             const int32_t normed = (scaled * inv + 128) >> 8;
-            orow[j] = (int8_t)sat8(normed + b);
+            orow[j] = (int8_t)sat8(rms ? normed : normed + b);
         }
     }
 }
@@ -139,10 +144,13 @@ __global__ void __launch_bounds__(256) layernorm_lut_i16_kernel(
 // ------------------------------------------------------------ LUT softmaxes
 // u8: m = row max; e_j = lut[max(x_j - m, -255) + 255]; S = sum e;
 // p_j = (e_j 255 + S / 2) / S  (i8_gemm_softmax_tile/reference.c, step C)
+// With a reciprocal table (softmax_row_i8/reference.c): recip =
+// recip_lut[clamp(S >> 6, 0, 255)], p_j = clamp((e_j recip + 32768) >> 16, 0, 255).
 __global__ void __launch_bounds__(256) lut_softmax_u8_kernel(const int8_t *__restrict__ x,
                                                              uint8_t *__restrict__ out, int R,
                                                              int C,
-                                                             const uint8_t *__restrict__ lut) {
+                                                             const uint8_t *__restrict__ lut,
+                                                             const uint16_t *__restrict__ recip_lut) {
     const int lane = threadIdx.x & 31;
     for (int r = blockIdx.x * kRowWarps + (threadIdx.x >> 5); r < R; r += gridDim.x * kRowWarps) {
         const int8_t *xr = x + (size_t)r * C;
@@ -153,10 +161,17 @@ __global__ void __launch_bounds__(256) lut_softmax_u8_kernel(const int8_t *__res
         for (int j = lane; j < C; j += 32) s += lut[max((int)xr[j] - m, -255) + 255];
         s = warp_sum_i32(s);
         const int32_t half = s / 2;
+        const int32_t si = s >> 6;
+        const int32_t recip = recip_lut ? recip_lut[si < 0 ? 0 : (si > 255 ? 255 : si)] : 0;
         uint8_t *orow = out + (size_t)r * C;
         for (int j = lane; j < C; j += 32) {
             const int32_t e = lut[max((int)xr[j] - m, -255) + 255];
-            orow[j] = (uint8_t)(s > 0 ? (e * 255 + half) / s : 0);
+            if (recip_lut) {
+                const int32_t v = (e * recip + 32768) >> 16;
+                orow[j] = (uint8_t)(v < 0 ? 0 : (v > 255 ? 255 : v));
+            } else {
+                orow[j] = (uint8_t)(s > 0 ? (e * 255 + half) / s : 0);
+            }
         }
     }
 }
@@ -231,10 +246,10 @@ HX_EXPORT int hexcuda_layernorm_lut_i8(int dev, const int8_t *x, const int32_t *
                                       const uint8_t *inv_lut, int affine) {
     Dev *d = get_dev(dev);
     if (!d) return HEXCUDA_ERR_NODEV;
-    if (R < 0 || W < 1 || affine < HEXCUDA_LN_AFFINE_SHARED || affine > HEXCUDA_LN_AFFINE_PER_ROW)
+    if (R < 0 || W < 1 || affine < HEXCUDA_LN_AFFINE_SHARED || affine > HEXCUDA_LN_RMS_SHARED)
         return fail(HEXCUDA_ERR_ARG, "layernorm_lut_i8: R %d W %d affine %d", R, W, affine);
     if (R == 0) return HEXCUDA_OK;
-    if (!x || !out || !gamma || !beta || !inv_lut)
+    if (!x || !out || !gamma || (!beta && affine != HEXCUDA_LN_RMS_SHARED) || !inv_lut)
         return fail(HEXCUDA_ERR_ARG, "layernorm_lut_i8: null pointer");
     launch_begin(d);
     layernorm_lut_i8_kernel<<<row_blocks(d, R), 256, 0, d->stream>>>(x, idx, res, out, R, W, gamma,
@@ -259,14 +274,14 @@ HX_EXPORT int hexcuda_layernorm_lut_i16(int dev, const int16_t *x, int16_t *out,
 }
 
 HX_EXPORT int hexcuda_lut_softmax_u8(int dev, const int8_t *x, uint8_t *out, int R, int C,
-                                    const uint8_t *exp_lut) {
+                                    const uint8_t *exp_lut, const uint16_t *recip_lut) {
     Dev *d = get_dev(dev);
     if (!d) return HEXCUDA_ERR_NODEV;
     if (R < 0 || C < 1) return fail(HEXCUDA_ERR_ARG, "lut_softmax_u8: R %d C %d", R, C);
     if (R == 0) return HEXCUDA_OK;
     if (!x || !out || !exp_lut) return fail(HEXCUDA_ERR_ARG, "lut_softmax_u8: null pointer");
     launch_begin(d);
-    lut_softmax_u8_kernel<<<row_blocks(d, R), 256, 0, d->stream>>>(x, out, R, C, exp_lut);
+    lut_softmax_u8_kernel<<<row_blocks(d, R), 256, 0, d->stream>>>(x, out, R, C, exp_lut, recip_lut);
     return launch_end(d, "lut_softmax_u8");
 }
 
@@ -337,7 +352,7 @@ HX_EXPORT int hexcuda_gemm_softmax_u8(int dev, const int8_t *A, const int8_t *B,
                                            HEXCUDA_HMX_RES_NONE, nullptr, sc,
                                            HEXCUDA_HMX_STORE_I8_SAT, HEXCUDA_HMX_ACT_NONE, M, N, K);
     if (rc) return rc;
-    return hexcuda_lut_softmax_u8(dev, sc, out, M, N, exp_lut);
+    return hexcuda_lut_softmax_u8(dev, sc, out, M, N, exp_lut, nullptr);
 }
 
 HX_EXPORT int hexcuda_gelu_ffn_residual_i8(int dev, const int8_t *x, const int8_t *W1,

@@ -263,6 +263,28 @@ __global__ void __launch_bounds__(kNT) row_generic_kernel(const T *__restrict__ 
     }
 }
 
+// RMS norm with one gain per row (rmsnorm_gain_fp16/reference.c:6-19):
+// inv = 1 / sqrt(sum x^2 / C + eps), out = (fp16)((x inv) gain[row]).
+__global__ void __launch_bounds__(kNT) rmsnorm_gain_f16_kernel(const __half *__restrict__ x,
+                                                               const __half *__restrict__ gain,
+                                                               __half *__restrict__ out, int C,
+                                                               float eps) {
+    __shared__ float sh[kWarps];
+    const int row = blockIdx.x;
+    const __half *xr = x + (size_t)row * C;
+    float s2 = 0.0f;
+    for (int j = threadIdx.x; j < C; j += kNT) {
+        const float v = __half2float(xr[j]);
+        s2 += v * v;
+    }
+    s2 = block_sum(s2, sh);
+    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(s2, (float)C), eps)));
+    const float g = __half2float(gain[row]);
+    __half *orow = out + (size_t)row * C;
+    for (int j = threadIdx.x; j < C; j += kNT)
+        orow[j] = __float2half_rn(__fmul_rn(__fmul_rn(__half2float(xr[j]), inv), g));
+}
+
 template <typename T, int OP, int NV>
 void launch_reg(Dev *d, const T *x, const T *g, const T *b, T *o, float *ro, int R, int C,
                 float eps) {
@@ -380,6 +402,18 @@ HX_EXPORT int hexcuda_rmsnorm_f16(int dev, const uint16_t *x, const uint16_t *ga
                                   uint16_t *out, int R, int C, float eps) {
     return launch_rows<__half, kRmsNorm>(dev, (const __half *)x, (const __half *)gamma, nullptr,
                                          (__half *)out, nullptr, R, C, eps, "rmsnorm_f16");
+}
+HX_EXPORT int hexcuda_rmsnorm_gain_f16(int dev, const uint16_t *x, const uint16_t *gain,
+                                       uint16_t *out, int R, int C, float eps) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "rmsnorm_gain_f16: R=%d C=%d", R, C);
+    if (R == 0) return HEXCUDA_OK;
+    if (!x || !gain || !out) return fail(HEXCUDA_ERR_ARG, "rmsnorm_gain_f16: null pointer");
+    launch_begin(d);
+    rmsnorm_gain_f16_kernel<<<R, kNT, 0, d->stream>>>((const __half *)x, (const __half *)gain,
+                                                      (__half *)out, C, eps);
+    return launch_end(d, "rmsnorm_gain_f16");
 }
 HX_EXPORT int hexcuda_rowreduce_f32(int dev, const float *x, float *out, int R, int C, int op) {
     if (op == 0)

@@ -244,7 +244,7 @@ def head_group_reduce_i8(X, G: int, mult: int, shift: int) -> np.ndarray:
     return Y
 
 
-LN_AFFINE = {"shared": 0, "rowwise": 1, "per_row": 2}
+LN_AFFINE = {"shared": 0, "rowwise": 1, "per_row": 2, "rms": 3}
 
 
 def layernorm_lut_i8(x, gamma, beta, inv_lut, affine: str = "shared", res=None, idx=None):
@@ -255,11 +255,13 @@ def layernorm_lut_i8(x, gamma, beta, inv_lut, affine: str = "shared", res=None, 
     idx = _c(idx, np.int32) if idx is not None else None
     R = idx.size if idx is not None else xrows
     res = _c(res, np.int8) if res is not None else None
-    gamma, beta, inv_lut = _c(gamma, np.int8), _c(beta, np.int8), _c(inv_lut, np.uint8)
+    gamma, inv_lut = _c(gamma, np.int8), _c(inv_lut, np.uint8)
+    beta = _c(beta, np.int8) if beta is not None else None
     out = np.empty((R, W), np.int8)
     check(load().hexcuda_host_layernorm_lut_i8(_p(x), xrows, None if idx is None else _p(idx),
                                                None if res is None else _p(res), _p(out), R, W,
-                                               _p(gamma), _p(beta), _p(inv_lut), LN_AFFINE[affine]))
+                                               _p(gamma), None if beta is None else _p(beta),
+                                               _p(inv_lut), LN_AFFINE[affine]))
     return out
 
 
@@ -273,11 +275,13 @@ def layernorm_lut_i16(x, gamma, beta, inv_lut, order: int = 0) -> np.ndarray:
     return out
 
 
-def lut_softmax_u8(x, exp_lut) -> np.ndarray:
+def lut_softmax_u8(x, exp_lut, recip_lut=None) -> np.ndarray:
     x = _c(x, np.int8)
     R, Cc = x.shape
     out = np.empty((R, Cc), np.uint8)
-    check(load().hexcuda_host_lut_softmax_u8(_p(x), _p(out), R, Cc, _p(_c(exp_lut, np.uint8))))
+    rl = _c(recip_lut, np.uint16) if recip_lut is not None else None
+    check(load().hexcuda_host_lut_softmax_u8(_p(x), _p(out), R, Cc, _p(_c(exp_lut, np.uint8)),
+                                             None if rl is None else _p(rl)))
     return out
 
 
@@ -555,6 +559,15 @@ def rmsnorm_f16(x, gamma, eps: float) -> np.ndarray:
     R, Cc = x.reshape(-1, x.shape[-1]).shape
     out = np.empty_like(x)
     check(load().hexcuda_host_rmsnorm_f16(_p(x), _p(gamma), _p(out), R, Cc, eps))
+    return out
+
+
+def rmsnorm_gain_f16(x, gain, eps: float) -> np.ndarray:
+    """RMS norm of each row of x [R, C] times one gain per row (fp16)."""
+    x, gain = _c(x, np.float16), _c(gain, np.float16)
+    R, Cc = x.shape
+    out = np.empty_like(x)
+    check(load().hexcuda_host_rmsnorm_gain_f16(_p(x), _p(gain), _p(out), R, Cc, eps))
     return out
 
 

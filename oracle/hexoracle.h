@@ -294,7 +294,11 @@ void oracle_layernorm_lut_i16(const int16_t *x, int16_t *out, int R, int C, cons
                               const int16_t *beta, const uint16_t *inv_lut, int order);
 /* row softmax by an exp table: i8_gemm_softmax_tile/reference.c step C (u8),
  * vtcm_softmax_row_i16/reference.c (i16) */
-void oracle_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C, const uint8_t *exp_lut);
+void oracle_lut_softmax_u8(const int8_t *x, uint8_t *out, int R, int C, const uint8_t *exp_lut,
+                           const uint16_t *recip_lut);
+/* rmsnorm_gain_fp16/reference.c: one gain per row */
+void oracle_rmsnorm_gain_f16(const uint16_t *x, const uint16_t *gain, uint16_t *out, int R, int C,
+                             float eps);
 void oracle_lut_softmax_i16(const int16_t *x, int16_t *out, int R, int C, const uint16_t *exp_lut);
 /* attention_scale_i16/reference.c */
 void oracle_requant_i16(const int32_t *a, int16_t *out, int64_t n, int32_t mult, int shift);

@@ -485,7 +485,7 @@ def head_group_reduce_i8(X, G, mult, shift):
     return Y
 
 
-LN_AFFINE = {"shared": 0, "rowwise": 1, "per_row": 2}
+LN_AFFINE = {"shared": 0, "rowwise": 1, "per_row": 2, "rms": 3}
 
 
 def layernorm_lut_i8(x, gamma, beta, inv_lut, affine="shared", res=None, idx=None):
@@ -494,12 +494,12 @@ def layernorm_lut_i8(x, gamma, beta, inv_lut, affine="shared", res=None, idx=Non
     idx = np.ascontiguousarray(idx, np.int32) if idx is not None else None
     R = idx.size if idx is not None else x.shape[0]
     res = np.ascontiguousarray(res, np.int8) if res is not None else None
-    g, b, lut = (np.ascontiguousarray(gamma, np.int8), np.ascontiguousarray(beta, np.int8),
-                 np.ascontiguousarray(inv_lut, np.uint8))
+    g, lut = np.ascontiguousarray(gamma, np.int8), np.ascontiguousarray(inv_lut, np.uint8)
+    b = np.ascontiguousarray(beta, np.int8) if beta is not None else None
     out = np.zeros((R, W), np.int8)
     lib().oracle_layernorm_lut_i8(_p(x), None if idx is None else _p(idx),
-                                  None if res is None else _p(res), _p(out), R, W, _p(g), _p(b),
-                                  _p(lut), LN_AFFINE[affine])
+                                  None if res is None else _p(res), _p(out), R, W, _p(g),
+                                  _p(b) if b is not None else None, _p(lut), LN_AFFINE[affine])
     return out
 
 
@@ -513,11 +513,21 @@ def layernorm_lut_i16(x, gamma, beta, inv_lut, order=0):
     return out
 
 
-def lut_softmax_u8(x, exp_lut):
+def lut_softmax_u8(x, exp_lut, recip_lut=None):
     x = np.ascontiguousarray(x, np.int8)
     out = np.zeros(x.shape, np.uint8)
     lut = np.ascontiguousarray(exp_lut, np.uint8)
-    lib().oracle_lut_softmax_u8(_p(x), _p(out), x.shape[0], x.shape[1], _p(lut))
+    rl = np.ascontiguousarray(recip_lut, np.uint16) if recip_lut is not None else None
+    lib().oracle_lut_softmax_u8(_p(x), _p(out), x.shape[0], x.shape[1], _p(lut),
+                                _p(rl) if rl is not None else None)
+    return out
+
+
+def rmsnorm_gain_f16(x, gain, eps):
+    x = np.ascontiguousarray(x, np.float16)
+    g = np.ascontiguousarray(gain, np.float16)
+    out = np.zeros_like(x)
+    lib().oracle_rmsnorm_gain_f16(_p(x), _p(g), _p(out), x.shape[0], x.shape[1], C.c_float(eps))
     return out
 
 
@@ -555,3 +565,12 @@ def gelu_ffn_residual_i8(x, W1, b1, gelu_lut, W2, b2, x_res, gamma, beta, inv_lu
     hid = gemm_i8_acc(x, W1, "lut_i8", bias=b1, lut=gelu_lut)
     s = gemm_i8_acc(hid, W2, "i8_sat", bias=b2, res=np.ascontiguousarray(x_res, np.int8))
     return layernorm_lut_i8(s, gamma, beta, inv_lut)
+
+
+def rmsnorm_f16(x, gamma, eps):
+    x = np.ascontiguousarray(x, np.float16)
+    g = np.ascontiguousarray(gamma, np.float16)
+    out = np.zeros_like(x)
+    R, Cc = x.shape
+    lib().oracle_rmsnorm_f16_rows(_p(x), _p(g), _p(out), R, Cc, C.c_float(eps), 0, R)
+    return out

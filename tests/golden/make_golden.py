@@ -983,6 +983,50 @@ def gen_int_rows(ref):
     save("int_rows", **a)
 
 
+def gen_softmax_rms(ref):
+    # The exp-table row softmaxes (division, reciprocal table, int16) and the
+    # RMS norms (int8 residual + table, fp16 per-row gain, fp16 per-column
+    # gamma) through their reference.c at ragged shapes; int16 softmax rows
+    # of <= 8000 values so the reference's int32 sum stays defined.
+    rng = np.random.default_rng(127)
+    a = {}
+
+    def run(name, args, **arrs):
+        getattr(ref, "ref_" + name)(*args)
+        for k, v in arrs.items():
+            a[f"{name}__{k}"] = v
+
+    R, Cc = 37, 301
+    x = rng.integers(-128, 128, (R, Cc), dtype=np.int8)
+    lut = rng.integers(0, 256, 256, dtype=np.uint8)
+    lut[255] |= 1
+    rl = rng.integers(0, 65536, 256, dtype=np.uint16)
+    a.update(exp_lut=lut, recip_lut=rl, x8=x)
+    o = np.zeros((R, Cc), np.uint8)
+    run("softmax_rowwise", (ptr(x), ptr(o), R, Cc, ptr(lut)), out=o)
+    o = np.zeros((R, Cc), np.uint8)
+    run("softmax_row_i8", (ptr(x), ptr(o), R, Cc, ptr(lut), ptr(rl)), out=o)
+    x16 = rng.integers(-3000, 3000, (9, 4000)).astype(np.int16)
+    l16 = rng.integers(0, 65536, 256).astype(np.uint16)
+    l16[255] |= 1
+    o = np.zeros_like(x16)
+    run("softmax_row_lut_i16", (ptr(x16), ptr(o), 9, 4000, ptr(l16)), x=x16, lut=l16, out=o)
+    n = 256
+    xi, ri, g = (rng.integers(-128, 128, n, dtype=np.int8) for _ in range(3))
+    inv = rng.integers(0, 256, 256, dtype=np.uint8)
+    o = np.zeros(n, np.int8)
+    run("rmsnorm_residual", (ptr(xi), ptr(ri), ptr(o), n, ptr(g), ptr(inv)), x=xi, res=ri, gamma=g, inv=inv,
+        out=o)
+    xf = rng.standard_normal((33, 520)).astype(np.float16)
+    gain = rng.standard_normal(33).astype(np.float16)
+    o = np.zeros_like(xf)
+    run("rmsnorm_gain_fp16", (ptr(xf), ptr(gain), ptr(o), 33, 520), x=xf, gain=gain, out=o)
+    gam = rng.standard_normal(520).astype(np.float16)
+    o = np.zeros_like(xf)
+    run("rmsnorm_row_fp16", (ptr(xf), ptr(gam), ptr(o), 33, 520), gamma=gam, out=o)
+    save("softmax_rms", **a)
+
+
 def main():
     if not (REF_ROOT / "kernels").is_dir():
         sys.exit(f"reference tree not found at {REF_ROOT}")
@@ -1004,6 +1048,7 @@ def main():
     gen_reduce_family(ref)
     gen_i8_acc_callers(ref)
     gen_int_rows(ref)
+    gen_softmax_rms(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

@@ -116,3 +116,39 @@ def test_requants_and_compositions(hx, oracle):
             rng.integers(-3000, 3000, D).astype(np.int32), s8(M, D), s8(D), s8(D),
             rng.integers(0, 256, 256, dtype=np.uint8))
     np.testing.assert_array_equal(hx.gelu_ffn_residual_i8(*args), oracle.gelu_ffn_residual_i8(*args))
+
+
+from test_oracle_golden import check_softmax_rms  # noqa: E402
+
+
+def test_softmax_rms_golden(hx):
+    check_softmax_rms(hx, golden("softmax_rms"))
+
+
+def test_softmax_recip_and_rms_random(hx, oracle):
+    rng = np.random.default_rng(21)
+    x = rng.integers(-128, 128, (1000, 777), dtype=np.int8)
+    lut = rng.integers(0, 256, 256, dtype=np.uint8)
+    rl = rng.integers(0, 65536, 256, dtype=np.uint16)
+    np.testing.assert_array_equal(hx.lut_softmax_u8(x, lut, rl), oracle.lut_softmax_u8(x, lut, rl))
+    g = rng.integers(-128, 128, 777, dtype=np.int8)
+    inv = rng.integers(0, 256, 256, dtype=np.uint8)
+    np.testing.assert_array_equal(hx.layernorm_lut_i8(x, g, None, inv, "rms", res=x[::-1].copy()),
+                                  oracle.layernorm_lut_i8(x, g, None, inv, "rms", res=x[::-1].copy()))
+    xf = rng.standard_normal((300, 4096)).astype(np.float16)
+    gain = rng.standard_normal(300).astype(np.float16)
+    got = hx.rmsnorm_gain_f16(xf, gain, 1e-3).astype(np.float64)
+    exp = oracle.rmsnorm_gain_f16(xf, gain, 1e-3).astype(np.float64)
+    assert np.all(np.abs(got - exp) <= 1e-2 * np.abs(exp) + 1e-3 * np.abs(exp).max())
+
+
+def test_attention_qkt_tile_shim(hx):
+    """attention_qkt_tile's own harness reads past its parameter tables, so
+    its shim is checked here on the golden case (valid scale parameters)."""
+    g = golden("int_rows")
+    Q, K, exp = (g["attention_qkt_tile__" + k] for k in ("Q", "K", "out"))
+    out = np.zeros_like(exp)
+    fn = shim("attention_qkt_tile")
+    fn.argtypes = [C.c_void_p] * 3 + [C.c_int] * 3 + [C.c_int32, C.c_int]
+    fn(p(Q), p(K), p(out), Q.shape[0], K.shape[0], Q.shape[1], 1 << 20, 26)
+    np.testing.assert_array_equal(out, exp)

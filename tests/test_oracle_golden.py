@@ -433,3 +433,32 @@ def test_lut_softmax_i16_properties(oracle):
     assert (p[np.arange(20), x.argmax(1)] == p.max(1)).all()
     flat = oracle.lut_softmax_i16(np.full((2, 64), 7, np.int16), lut)
     assert (flat == flat[0, 0]).all()
+
+
+def softmax_rms_calls(impl, g):
+    """(result, expected, tolerance) of the softmax / RMS-norm bundles
+    (golden softmax_rms); tolerance None = bit-exact, else the fp16 bar."""
+    yield impl.lut_softmax_u8(g["x8"], g["exp_lut"]), g["softmax_rowwise__out"], None
+    yield impl.lut_softmax_u8(g["x8"], g["exp_lut"], g["recip_lut"]), g["softmax_row_i8__out"], None
+    n = "softmax_row_lut_i16"
+    yield impl.lut_softmax_i16(g[n + "__x"], g[n + "__lut"]), g[n + "__out"], None
+    n = "rmsnorm_residual"
+    yield (impl.layernorm_lut_i8(g[n + "__x"][None], g[n + "__gamma"], None, g[n + "__inv"], "rms",
+                                 res=g[n + "__res"][None])[0], g[n + "__out"], None)
+    n = "rmsnorm_gain_fp16"
+    yield impl.rmsnorm_gain_f16(g[n + "__x"], g[n + "__gain"], 1e-3), g[n + "__out"], 1e-2
+    yield (impl.rmsnorm_f16(g["rmsnorm_gain_fp16__x"], g["rmsnorm_row_fp16__gamma"], 1e-3),
+           g["rmsnorm_row_fp16__out"], 1e-2)
+
+
+def check_softmax_rms(impl, g):
+    for k, (got, exp, tol) in enumerate(softmax_rms_calls(impl, g)):
+        if tol is None:
+            np.testing.assert_array_equal(got, exp, err_msg=str(k))
+        else:
+            e = exp.astype(np.float64)
+            assert np.all(np.abs(got.astype(np.float64) - e) <= tol * np.abs(e) + 1e-3 * np.abs(e).max()), k
+
+
+def test_softmax_rms_golden(oracle):
+    check_softmax_rms(oracle, golden("softmax_rms"))

@@ -67,6 +67,9 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_gemm_hmx_s8u8": (I, [I, P, P, P, I, I, I, I]),
     "hexcuda_gemm_f16_ex": (I, [I, P, P, I, P, P, P, I, I, F, I, I, I]),
     "hexcuda_attn_lut_i8": (I, [I, I, P, P, P, P, P, P, I, P, I, I, I, I, I32, I, I32, I]),
+    "hexcuda_attn_lut_i8_window": (I, [I, P, P, P, P, P, I, I, I, I, I32, I, I32, I]),
+    "hexcuda_kv_cache_update_i8": (I, [I, P, P, P, P, I, I, I, I]),
+    "hexcuda_rope_pair_f16": (I, [I, P, P, P, P, I64]),
     "hexcuda_decoder_block_i8": (I, [I, P, P, P, P, P, P, P, P, I, I, I]),
     "hexcuda_attn_qkt_av_hmx": (I, [I, P, P, P, P, I, I, I]),
     "hexcuda_requant_ew": (I, [I, P, I, P, I, P, I64, I, I64, I32, I, I, I, I, I, I, I, P]),
@@ -75,6 +78,9 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_reduce_int": (I, [I, P, P, I, I64, I, P]),
     "hexcuda_minmax_ew": (I, [I, P, P, I32, I, I, P, I64]),
     "hexcuda_group_sum_i8": (I, [I, P, P, I64, I]),
+    "hexcuda_group_dot_i8": (I, [I, P, P, P, I64, I]),
+    "hexcuda_gate_mul_requant_i8": (I, [I, P, P, P, P, I64, I32, I]),
+    "hexcuda_ffn_lut_i8": (I, [I, P, P, P, P, P, P, P, I, I, I, I, I32, I, I8]),
     "hexcuda_scan_max_i8": (I, [I, P, P, I64]),
     "hexcuda_head_group_reduce_i8": (I, [I, P, P, I, I, I64, I32, I]),
     "hexcuda_layernorm_lut_i8": (I, [I, P, P, P, P, I, I, P, P, P, I]),
@@ -113,6 +119,9 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_gemm_hmx_s8u8": (I, [P, P, P, I, I, I, I]),
     "hexcuda_host_gemm_f16_ex": (I, [P, P, I, P, P, P, I, I, F, I, I, I]),
     "hexcuda_host_attn_lut_i8": (I, [I, P, P, P, P, P, P, I, P, I, I, I, I, I32, I, I32, I]),
+    "hexcuda_host_attn_lut_i8_window": (I, [P, P, P, P, P, I, I, I, I, I32, I, I32, I]),
+    "hexcuda_host_kv_cache_update_i8": (I, [P, P, P, P, I, I, I, I]),
+    "hexcuda_host_rope_pair_f16": (I, [P, P, P, P, I64]),
     "hexcuda_host_decoder_block_i8": (I, [P, P, P, P, P, P, P, P, I, I, I]),
     "hexcuda_host_attn_qkt_av_hmx": (I, [P, P, P, P, I, I, I]),
     "hexcuda_host_requant_ew": (I, [P, I, P, I, P, I64, I, I64, I32, I, I, I, I, I, I, I, P]),
@@ -121,6 +130,9 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_reduce_int": (I, [P, P, I, I64, I, P]),
     "hexcuda_host_minmax_ew": (I, [P, P, I32, I, I, P, I64]),
     "hexcuda_host_group_sum_i8": (I, [P, P, I64, I]),
+    "hexcuda_host_group_dot_i8": (I, [P, P, P, I64, I]),
+    "hexcuda_host_gate_mul_requant_i8": (I, [P, P, P, P, I64, I32, I]),
+    "hexcuda_host_ffn_lut_i8": (I, [P, P, P, P, P, P, P, I, I, I, I, I32, I, I8]),
     "hexcuda_host_scan_max_i8": (I, [P, P, I64]),
     "hexcuda_host_head_group_reduce_i8": (I, [P, P, I, I, I64, I32, I]),
     "hexcuda_host_layernorm_lut_i8": (I, [P, I, P, P, P, I, I, P, P, P, I]),

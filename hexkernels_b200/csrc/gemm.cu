@@ -1427,6 +1427,25 @@ HX_EXPORT int hexcuda_ffn_relu_i8(int dev, const int8_t *A, const int8_t *W1, co
     return hexcuda_gemm_i8_rq_ex(dev, hid, W2, 0, b2, nullptr, out, M, D, V, mult, shift, zp, 0);
 }
 
+HX_EXPORT int hexcuda_ffn_lut_i8(int dev, const int8_t *A, const int8_t *W1, const int32_t *b1,
+                                 const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
+                                 int8_t *out, int M, int K, int V, int D, int32_t mult, int shift,
+                                 int8_t zp) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (M < 0 || K < 0 || V < 0 || D < 0) return fail(HEXCUDA_ERR_ARG, "ffn_lut_i8: bad shape");
+    if (M == 0 || D == 0) return HEXCUDA_OK;
+    if (!act_lut) return fail(HEXCUDA_ERR_ARG, "ffn_lut_i8: null table");
+    int8_t *hid = reinterpret_cast<int8_t *>(scratch(d, kSlotFfnHidden, (size_t)M * (V > 0 ? V : 1)));
+    if (!hid) return HEXCUDA_ERR_OOM;
+    if (V > 0) {
+        if (int rc = hexcuda_gemm_i8_acc(dev, A, 1, W1, 0, b1, nullptr, HEXCUDA_HMX_RES_NONE, act_lut,
+                                         hid, HEXCUDA_HMX_STORE_LUT_I8, HEXCUDA_HMX_ACT_NONE, M, V, K))
+            return rc;
+    }
+    return hexcuda_gemm_i8_rq_ex(dev, hid, W2, 0, b2, nullptr, out, M, D, V, mult, shift, zp, 0);
+}
+
 HX_EXPORT int hexcuda_gemm_hmx_s8u8(int dev, const int8_t *A, const uint8_t *B, void *out, int store,
                                     int M, int N, int K) {
     if (store < HEXCUDA_HMX_STORE_I32 || store > HEXCUDA_HMX_STORE_ACC_I32 ||

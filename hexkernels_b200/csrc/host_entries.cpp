@@ -590,6 +590,29 @@ HX_EXPORT int hexcuda_host_attn_lut_i8(int mode, const void *Q, const int8_t *K,
     });
 }
 
+HX_EXPORT int hexcuda_host_attn_lut_i8_window(const int8_t *Q, const int8_t *K, const int8_t *V,
+                                              const uint8_t *exp_lut, int8_t *out, int H, int S,
+                                              int D, int window, int32_t scale_mult,
+                                              int scale_shift, int32_t av_mult, int av_shift) {
+    if (H < 1 || S < 0 || D < 0 || window < 0)
+        return fail(HEXCUDA_ERR_ARG, "host_attn_lut_i8_window: H %d S %d D %d window %d", H, S, D,
+                    window);
+    if (S == 0 || D == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_attn_lut_i8_window", {Q, K, V, exp_lut, out})) return rc;
+    const size_t n = (size_t)H * S * D;
+    return run_sharded(1, out, n, [&](Part &p) {
+        const int8_t *dQ = stage_in(p.d, kSlotIn0, Q, n);
+        const int8_t *dK = stage_in(p.d, kSlotIn1, K, n);
+        const int8_t *dV = stage_in(p.d, kSlotIn2, V, n);
+        const uint8_t *dl = stage_in(p.d, kSlotIn3, exp_lut, 256);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, n));
+        if (!dQ || !dK || !dV || !dl || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_attn_lut_i8_window(p.slot, dQ, dK, dV, dl, dout, H, S, D, window, scale_mult,
+                                          scale_shift, av_mult, av_shift);
+    });
+}
+
 HX_EXPORT int hexcuda_host_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
                                             const int8_t *act_lut, const int8_t *W2,
                                             const int32_t *b2, const uint8_t *exp_lut, int8_t *out,
@@ -1078,5 +1101,108 @@ HX_EXPORT int hexcuda_host_gelu_ffn_residual_i8(const int8_t *x, const int8_t *W
         p.dout = dout;
         return hexcuda_gelu_ffn_residual_i8(p.slot, dx, dw1, dbias, dgl, dw2, dbias + V, dres, dg, dbt,
                                             dil, dout, (int)nr, K, V, D);
+    });
+}
+
+HX_EXPORT int hexcuda_host_group_dot_i8(const int8_t *a, const int8_t *b, int32_t *out, int64_t g,
+                                        int w) {
+    if (g < 0 || w < 1) return fail(HEXCUDA_ERR_ARG, "host_group_dot_i8: g %lld w %d", (long long)g, w);
+    if (g == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_group_dot_i8", {a, b, out})) return rc;
+    return run_sharded(g, out, 4, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *da = stage_in(p.d, kSlotIn0, a + p.r0 * w, (size_t)(nr * w));
+        const int8_t *db = stage_in(p.d, kSlotIn1, b + p.r0 * w, (size_t)(nr * w));
+        int32_t *dout = reinterpret_cast<int32_t *>(scratch(p.d, kSlotOut, (size_t)nr * 4));
+        if (!da || !db || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_group_dot_i8(p.slot, da, db, dout, nr, w);
+    });
+}
+
+HX_EXPORT int hexcuda_host_gate_mul_requant_i8(const int8_t *gate, const int8_t *up,
+                                               const int8_t *lut, int8_t *out, int64_t n,
+                                               int32_t mult, int shift) {
+    if (n < 0) return fail(HEXCUDA_ERR_ARG, "host_gate_mul_requant_i8: n %lld", (long long)n);
+    if (n == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gate_mul_requant_i8", {gate, up, lut, out})) return rc;
+    return run_sharded(n, out, 1, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *dg = stage_in(p.d, kSlotIn0, gate + p.r0, (size_t)nr);
+        const int8_t *du = stage_in(p.d, kSlotIn1, up + p.r0, (size_t)nr);
+        const int8_t *dl = stage_in(p.d, kSlotIn2, lut, 256);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)nr));
+        if (!dg || !du || !dl || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_gate_mul_requant_i8(p.slot, dg, du, dl, dout, nr, mult, shift);
+    });
+}
+
+HX_EXPORT int hexcuda_host_ffn_lut_i8(const int8_t *A, const int8_t *W1, const int32_t *b1,
+                                      const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
+                                      int8_t *out, int M, int K, int V, int D, int32_t mult,
+                                      int shift, int8_t zp) {
+    if (M < 0 || K < 0 || V < 0 || D < 0) return fail(HEXCUDA_ERR_ARG, "host_ffn_lut_i8: bad shape");
+    if (M == 0 || D == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_ffn_lut_i8", {A, W1, b1, act_lut, W2, b2, out})) return rc;
+    return run_sharded(M, out, (size_t)D, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const int8_t *dW1 = stage_in(p.d, kSlotIn1, W1, (size_t)K * V);
+        const int32_t *db1 = stage_in(p.d, kSlotIn2, b1, (size_t)V);
+        const int8_t *dW2 = stage_in(p.d, kSlotIn3, W2, (size_t)V * D);
+        const int32_t *db2 = stage_in(p.d, kSlotIn4, b2, (size_t)D);
+        const int8_t *dl = stage_in(p.d, kSlotIn5, act_lut, 256);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * D)));
+        if (!dA || !dW1 || !db1 || !dW2 || !db2 || !dl || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_ffn_lut_i8(p.slot, dA, dW1, db1, dl, dW2, db2, dout, (int)nr, K, V, D, mult,
+                                  shift, zp);
+    });
+}
+
+// Heads are split over the devices; each shard's K cache rows come back
+// through run_sharded, its V cache rows by a copy queued after the kernel.
+HX_EXPORT int hexcuda_host_kv_cache_update_i8(int8_t *k_cache, int8_t *v_cache,
+                                              const int8_t *k_new, const int8_t *v_new, int pos,
+                                              int heads, int cache_len, int head_dim) {
+    if (heads < 0 || cache_len < 1 || head_dim < 0 || pos < 0 || pos >= cache_len)
+        return fail(HEXCUDA_ERR_ARG, "host_kv_cache_update_i8: pos %d heads %d cache_len %d head_dim %d",
+                    pos, heads, cache_len, head_dim);
+    if (heads == 0 || head_dim == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_kv_cache_update_i8", {k_cache, v_cache, k_new, v_new})) return rc;
+    const size_t plane = (size_t)cache_len * head_dim;
+    return run_sharded(heads, k_cache, plane, [&](Part &p) {
+        const int64_t nh = p.r1 - p.r0;
+        int8_t *dk = stage_in(p.d, kSlotIn0, k_cache + p.r0 * plane, (size_t)nh * plane);
+        int8_t *dv = stage_in(p.d, kSlotIn1, v_cache + p.r0 * plane, (size_t)nh * plane);
+        const int8_t *dkn = stage_in(p.d, kSlotIn2, k_new + p.r0 * head_dim, (size_t)(nh * head_dim));
+        const int8_t *dvn = stage_in(p.d, kSlotIn3, v_new + p.r0 * head_dim, (size_t)(nh * head_dim));
+        if (!dk || !dv || !dkn || !dvn) return hexcuda_last_error();
+        if (int rc = hexcuda_kv_cache_update_i8(p.slot, dk, dv, dkn, dvn, pos, (int)nh, cache_len,
+                                                head_dim))
+            return rc;
+        p.dout = dk;
+        return check(cudaMemcpyAsync(v_cache + p.r0 * plane, dv, (size_t)nh * plane,
+                                     cudaMemcpyDeviceToHost, p.d->stream),
+                     "d2h (V cache)");
+    });
+}
+
+HX_EXPORT int hexcuda_host_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t,
+                                         const uint16_t *sin_t, uint16_t *out, int64_t n_pairs) {
+    if (n_pairs < 0)
+        return fail(HEXCUDA_ERR_ARG, "host_rope_pair_f16: n_pairs %lld", (long long)n_pairs);
+    if (n_pairs == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_rope_pair_f16", {x, cos_t, sin_t, out})) return rc;
+    return run_sharded(n_pairs, out, 4, [&](Part &p) {
+        const int64_t np = p.r1 - p.r0;
+        const uint16_t *dx = stage_in(p.d, kSlotIn0, x + 2 * p.r0, (size_t)(2 * np));
+        const uint16_t *dc = stage_in(p.d, kSlotIn1, cos_t + p.r0, (size_t)np);
+        const uint16_t *ds = stage_in(p.d, kSlotIn2, sin_t + p.r0, (size_t)np);
+        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, (size_t)np * 4));
+        if (!dx || !dc || !ds || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_rope_pair_f16(p.slot, dx, dc, ds, dout, np);
     });
 }

@@ -39,6 +39,7 @@ struct AttnI8Args {
     int HQ, HKV, S, D;
     int32_t smult, amult;
     int sshift, ashift;
+    int window;   // REQUANT mode: scores with |i - j| > window become -128 (< 0: none)
 };
 
 // 4-byte dot products: d = c + sum a_i * b_i over the bytes of a and b
@@ -184,6 +185,9 @@ __global__ void __launch_bounds__(kThreads) attn_lut_i8_kernel(const AttnI8Args 
                 acc = MODE == kModeRq ? dot_ss(qr[w], kr[w], acc) : dot_us(qr[w], kr[w], acc);
             v = MODE == kModeRq ? requant_i8(acc, a.smult, a.sshift)
                                 : clamp_i8(sx12(hmx_field(acc)) >> 4);
+            // banded mask of i8_sparse_attn_block/reference.c:33-42: the
+            // masked scores stay in the softmax at the int8 minimum
+            if (MODE == kModeRq && a.window >= 0 && abs(i - j) > a.window) v = -128;
         }
         sc[idx] = (int8_t)v;
     }
@@ -339,11 +343,12 @@ int set_smem(K kern, int dev_ordinal, bool *done) {
 
 using namespace hx;
 
-HX_EXPORT int hexcuda_attn_lut_i8(int dev, int mode, const void *Q, const int8_t *K, const int8_t *V,
-                                  const uint8_t *exp_lut, const int8_t *cos_lut,
-                                  const int8_t *sin_lut, int rot_shift, void *out, int HQ, int HKV,
-                                  int S, int D, int32_t scale_mult, int scale_shift, int32_t av_mult,
-                                  int av_shift) {
+namespace hx {
+namespace {
+int attn_lut_i8_run(int dev, int mode, const void *Q, const int8_t *K, const int8_t *V,
+                    const uint8_t *exp_lut, const int8_t *cos_lut, const int8_t *sin_lut,
+                    int rot_shift, void *out, int HQ, int HKV, int S, int D, int32_t scale_mult,
+                    int scale_shift, int32_t av_mult, int av_shift, int window) {
     Dev *d = get_dev(dev);
     if (!d) return HEXCUDA_ERR_NODEV;
     if (mode < HEXCUDA_ATTN_LUT_REQUANT || mode > HEXCUDA_ATTN_LUT_HMX_ROPE || HQ < 1 || HKV < 1 ||
@@ -363,7 +368,7 @@ HX_EXPORT int hexcuda_attn_lut_i8(int dev, int mode, const void *Q, const int8_t
         return fail(HEXCUDA_ERR_ARG, "attn_lut_i8: S=%d D=%d need %d B of shared memory (max %d)", S,
                     D, L.total, kMaxSmem);
     AttnI8Args a{Q, K, V, exp_lut, cos_lut, sin_lut, rot_shift, out, HQ, HKV, S, D,
-                 scale_mult, av_mult, scale_shift, av_shift};
+                 scale_mult, av_mult, scale_shift, av_shift, window};
     static bool done[3][64] = {};
     launch_begin(d);
     int rc;
@@ -379,6 +384,26 @@ HX_EXPORT int hexcuda_attn_lut_i8(int dev, int mode, const void *Q, const int8_t
     }
     if (rc) return rc;
     return launch_end(d, "attn_lut_i8");
+}
+}  // namespace
+}  // namespace hx
+
+HX_EXPORT int hexcuda_attn_lut_i8(int dev, int mode, const void *Q, const int8_t *K, const int8_t *V,
+                                  const uint8_t *exp_lut, const int8_t *cos_lut,
+                                  const int8_t *sin_lut, int rot_shift, void *out, int HQ, int HKV,
+                                  int S, int D, int32_t scale_mult, int scale_shift, int32_t av_mult,
+                                  int av_shift) {
+    return attn_lut_i8_run(dev, mode, Q, K, V, exp_lut, cos_lut, sin_lut, rot_shift, out, HQ, HKV, S,
+                           D, scale_mult, scale_shift, av_mult, av_shift, -1);
+}
+
+HX_EXPORT int hexcuda_attn_lut_i8_window(int dev, const int8_t *Q, const int8_t *K, const int8_t *V,
+                                         const uint8_t *exp_lut, int8_t *out, int H, int S, int D,
+                                         int window, int32_t scale_mult, int scale_shift,
+                                         int32_t av_mult, int av_shift) {
+    if (window < 0) return fail(HEXCUDA_ERR_ARG, "attn_lut_i8_window: window %d", window);
+    return attn_lut_i8_run(dev, HEXCUDA_ATTN_LUT_REQUANT, Q, K, V, exp_lut, nullptr, nullptr, 0, out,
+                           H, H, S, D, scale_mult, scale_shift, av_mult, av_shift, window);
 }
 
 HX_EXPORT int hexcuda_decoder_block_i8(int dev, const uint8_t *X, const int8_t *W1, const int32_t *b1,

@@ -229,6 +229,19 @@ __global__ void __launch_bounds__(256) norm_requant_i8_kernel(
     }
 }
 
+// out = sat8(round_half_away((lut[gate + 128] up) * mult >> shift))
+// (mlp_gate_silu_i8/reference.c:4-17)
+__global__ void __launch_bounds__(256) gate_mul_requant_i8_kernel(
+    const int8_t *__restrict__ gate, const int8_t *__restrict__ up, const int8_t *__restrict__ lut,
+    int8_t *__restrict__ out, int64_t n, int32_t mult, int shift) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const int32_t g = lut[(int)gate[i] + 128];
+        const int64_t q = rq_round((int64_t)(g * (int32_t)up[i]) * (int64_t)mult, shift);
+        out[i] = (int8_t)(q > 127 ? 127 : (q < -128 ? -128 : q));
+    }
+}
+
 int row_blocks(const Dev *d, int R) {
     const int64_t b = ((int64_t)R + kRowWarps - 1) / kRowWarps;
     const int64_t cap = (int64_t)d->sms * 8;
@@ -309,6 +322,21 @@ HX_EXPORT int hexcuda_requant_i16(int dev, const int32_t *a, int16_t *out, int64
     constexpr auto kern = requant_i16_kernel;
     kern<<<resident_blocks<kern>(d, n), 256, 0, d->stream>>>(a, out, n, mult, shift);
     return launch_end(d, "requant_i16");
+}
+
+HX_EXPORT int hexcuda_gate_mul_requant_i8(int dev, const int8_t *gate, const int8_t *up,
+                                         const int8_t *lut, int8_t *out, int64_t n, int32_t mult,
+                                         int shift) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (n < 0 || shift < 0 || shift > 63)
+        return fail(HEXCUDA_ERR_ARG, "gate_mul_requant_i8: n %lld shift %d", (long long)n, shift);
+    if (n == 0) return HEXCUDA_OK;
+    if (!gate || !up || !lut || !out) return fail(HEXCUDA_ERR_ARG, "gate_mul_requant_i8: null pointer");
+    launch_begin(d);
+    constexpr auto kern = gate_mul_requant_i8_kernel;
+    kern<<<resident_blocks<kern>(d, n), 256, 0, d->stream>>>(gate, up, lut, out, n, mult, shift);
+    return launch_end(d, "gate_mul_requant_i8");
 }
 
 HX_EXPORT int hexcuda_norm_requant_i8(int dev, const int8_t *a, int8_t *out, int64_t n, int nch,

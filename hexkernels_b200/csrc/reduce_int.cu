@@ -484,29 +484,39 @@ int minmax_launch(Dev *d, const void *a, const void *b, int32_t c, void *out, in
 // --------------------------------------------------------------- group sums
 // w = 4 with 16-byte aligned operands: four outputs per 16-byte load (dp4a
 // against ones), one 16-byte store.
+// With b: out[k] = sum_j a[4k + j] b[4k + j] (hvx_vrmpy_i8_dot), dp4a against b.
+template <bool DOT>
 __global__ void __launch_bounds__(256) group_sum4_kernel(const int8_t *__restrict__ a,
+                                                         const int8_t *__restrict__ b,
                                                          int32_t *__restrict__ out, int64_t g) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t nv = g / 4;
     for (int64_t v = t; v < nv; v += stride) {
         const uint4 x = __ldcs(reinterpret_cast<const uint4 *>(a) + v);
+        const uint4 y = DOT ? __ldcs(reinterpret_cast<const uint4 *>(b) + v)
+                            : make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
         __stcs(reinterpret_cast<int4 *>(out) + v,
-               make_int4(__dp4a((int)x.x, 0x01010101, 0), __dp4a((int)x.y, 0x01010101, 0),
-                         __dp4a((int)x.z, 0x01010101, 0), __dp4a((int)x.w, 0x01010101, 0)));
+               make_int4(__dp4a((int)x.x, (int)y.x, 0), __dp4a((int)x.y, (int)y.y, 0),
+                         __dp4a((int)x.z, (int)y.z, 0), __dp4a((int)x.w, (int)y.w, 0)));
     }
-    for (int64_t k = nv * 4 + t; k < g; k += stride)
-        out[k] = (int32_t)a[4 * k] + a[4 * k + 1] + a[4 * k + 2] + a[4 * k + 3];
+    for (int64_t k = nv * 4 + t; k < g; k += stride) {
+        int32_t s = 0;
+        for (int j = 0; j < 4; j++) s += (int32_t)a[4 * k + j] * (DOT ? (int32_t)b[4 * k + j] : 1);
+        out[k] = s;
+    }
 }
 
+template <bool DOT>
 __global__ void __launch_bounds__(256) group_sum_kernel(const int8_t *__restrict__ a,
+                                                        const int8_t *__restrict__ b,
                                                         int32_t *__restrict__ out, int64_t g,
                                                         int w) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < g; k += stride) {
         uint32_t s = 0;
-        const int8_t *src = a + k * w;
-        for (int j = 0; j < w; j++) s += (uint32_t)(int32_t)src[j];
+        for (int j = 0; j < w; j++)
+            s += (uint32_t)((int32_t)a[k * w + j] * (DOT ? (int32_t)b[k * w + j] : 1));
         out[k] = (int32_t)s;
     }
 }
@@ -755,21 +765,40 @@ HX_EXPORT int hexcuda_minmax_ew(int dev, const void *a, const void *b, int32_t c
               : minmax_launch<HEXCUDA_ELEM_I16, false>(d, a, b, c, out, n);
 }
 
+namespace hx {
+namespace {
+template <bool DOT>
+int group_launch(Dev *d, const int8_t *a, const int8_t *b, int32_t *out, int64_t g, int w) {
+    launch_begin(d);
+    if (w == 4 && al16(a) && al16(out) && (!DOT || al16(b))) {
+        constexpr auto kern = group_sum4_kernel<DOT>;
+        kern<<<resident_blocks<kern>(d, std::max<int64_t>(1, g / 4)), 256, 0, d->stream>>>(a, b, out, g);
+    } else {
+        constexpr auto kern = group_sum_kernel<DOT>;
+        kern<<<resident_blocks<kern>(d, g), 256, 0, d->stream>>>(a, b, out, g, w);
+    }
+    return launch_end(d, DOT ? "group_dot_i8" : "group_sum_i8");
+}
+}  // namespace
+}  // namespace hx
+
 HX_EXPORT int hexcuda_group_sum_i8(int dev, const int8_t *a, int32_t *out, int64_t g, int w) {
     Dev *d = get_dev(dev);
     if (!d) return HEXCUDA_ERR_NODEV;
     if (g < 0 || w < 1) return fail(HEXCUDA_ERR_ARG, "group_sum_i8: g %lld w %d", (long long)g, w);
     if (g == 0) return HEXCUDA_OK;
     if (!a || !out) return fail(HEXCUDA_ERR_ARG, "group_sum_i8: null pointer");
-    launch_begin(d);
-    if (w == 4 && al16(a) && al16(out)) {
-        constexpr auto kern = group_sum4_kernel;
-        kern<<<resident_blocks<kern>(d, std::max<int64_t>(1, g / 4)), 256, 0, d->stream>>>(a, out, g);
-    } else {
-        constexpr auto kern = group_sum_kernel;
-        kern<<<resident_blocks<kern>(d, g), 256, 0, d->stream>>>(a, out, g, w);
-    }
-    return launch_end(d, "group_sum_i8");
+    return group_launch<false>(d, a, nullptr, out, g, w);
+}
+
+HX_EXPORT int hexcuda_group_dot_i8(int dev, const int8_t *a, const int8_t *b, int32_t *out,
+                                   int64_t g, int w) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (g < 0 || w < 1) return fail(HEXCUDA_ERR_ARG, "group_dot_i8: g %lld w %d", (long long)g, w);
+    if (g == 0) return HEXCUDA_OK;
+    if (!a || !b || !out) return fail(HEXCUDA_ERR_ARG, "group_dot_i8: null pointer");
+    return group_launch<true>(d, a, b, out, g, w);
 }
 
 HX_EXPORT int hexcuda_scan_max_i8(int dev, const int8_t *in, int8_t *out, int64_t n) {

@@ -225,6 +225,27 @@ def group_sum_i8(a, w: int = 4) -> np.ndarray:
     return out
 
 
+def group_dot_i8(a, b, w: int = 4) -> np.ndarray:
+    """out[k] = sum_j a[w k + j] b[w k + j] (int8 x int8 -> int32)."""
+    a = _c(a, np.int8).ravel()
+    b = _c(b, np.int8).ravel()
+    assert a.size == b.size
+    g = a.size // w
+    out = np.empty(g, np.int32)
+    check(load().hexcuda_host_group_dot_i8(_p(a), _p(b), _p(out), g, w))
+    return out
+
+
+def gate_mul_requant_i8(gate, up, lut, mult: int, shift: int) -> np.ndarray:
+    """SiLU-gated product: sat8(round_half_away(lut[gate + 128] up * mult >> shift))."""
+    gate, up, lut = _c(gate, np.int8), _c(up, np.int8), _c(lut, np.int8)
+    assert gate.shape == up.shape and lut.shape == (256,)
+    out = np.empty(gate.shape, np.int8)
+    check(load().hexcuda_host_gate_mul_requant_i8(_p(gate), _p(up), _p(lut), _p(out), gate.size,
+                                                  mult, shift))
+    return out
+
+
 def scan_max_i8(x) -> np.ndarray:
     """Inclusive prefix maximum of an int8 array."""
     x = _c(x, np.int8).ravel()
@@ -368,6 +389,44 @@ def attn_lut_i8(mode: str, Q, K, V, exp_lut, cos_lut=None, sin_lut=None, rot_shi
     return out
 
 
+def attn_lut_i8_window(Q, K, V, exp_lut, window: int, scale_mult: int, scale_shift: int,
+                       av_mult: int, av_shift: int) -> np.ndarray:
+    """int8 LUT-softmax attention (requant scores and output) with a banded
+    mask: scores of keys with |i - j| > window are -128.  Q / K / V [H, S, D]."""
+    Q, K, V = _c(Q, np.int8), _c(K, np.int8), _c(V, np.int8)
+    assert Q.shape == K.shape == V.shape and Q.ndim == 3
+    H, S, D = Q.shape
+    out = np.empty(Q.shape, np.int8)
+    check(load().hexcuda_host_attn_lut_i8_window(_p(Q), _p(K), _p(V), _p(_c(exp_lut, np.uint8)),
+                                                 _p(out), H, S, D, window, scale_mult, scale_shift,
+                                                 av_mult, av_shift))
+    return out
+
+
+def kv_cache_update_i8(k_cache, v_cache, k_new, v_new, pos: int):
+    """Writes k_new / v_new [heads, head_dim] into row pos of the caches
+    [heads, cache_len, head_dim] (in place on the host arrays, which are
+    returned)."""
+    assert k_cache.dtype == v_cache.dtype == np.int8 and k_cache.flags.c_contiguous
+    assert v_cache.flags.c_contiguous and k_cache.shape == v_cache.shape
+    heads, cache_len, head_dim = k_cache.shape
+    k_new, v_new = _c(k_new, np.int8), _c(v_new, np.int8)
+    assert k_new.shape == v_new.shape == (heads, head_dim)
+    check(load().hexcuda_host_kv_cache_update_i8(_p(k_cache), _p(v_cache), _p(k_new), _p(v_new), pos,
+                                                 heads, cache_len, head_dim))
+    return k_cache, v_cache
+
+
+def rope_pair_f16(x, cos_t, sin_t) -> np.ndarray:
+    """Rotary embedding of interleaved fp16 pairs (x [2 n], cos / sin [n])."""
+    x, cos_t, sin_t = _c(x, np.float16).ravel(), _c(cos_t, np.float16), _c(sin_t, np.float16)
+    n = x.size // 2
+    assert x.size == 2 * n and cos_t.size == sin_t.size == n
+    out = np.empty_like(x)
+    check(load().hexcuda_host_rope_pair_f16(_p(x), _p(cos_t), _p(sin_t), _p(out), n))
+    return out
+
+
 def decoder_block_i8(X, W1, b1, act_lut, W2, b2, exp_lut) -> np.ndarray:
     X, W1, W2 = _c(X, np.uint8), _c(W1, np.int8), _c(W2, np.int8)
     b1, b2 = _c(b1, np.int32), _c(b2, np.int32)
@@ -452,6 +511,19 @@ def ffn_relu_i8(A, W1, b1, W2, b2, mult: int, shift: int, zp: int) -> np.ndarray
     out = np.empty((M, D), np.int8)
     check(load().hexcuda_host_ffn_relu_i8(_p(A), _p(W1), _p(b1), _p(W2), _p(b2), _p(out), M, K,
                                           V, D, mult, shift, zp))
+    return out
+
+
+def ffn_lut_i8(A, W1, b1, act_lut, W2, b2, mult: int, shift: int, zp: int) -> np.ndarray:
+    """Two-layer int8 FFN with a table activation (GEMM + b1 + sat8 + table,
+    GEMM + b2 + requant)."""
+    A, W1, W2, act_lut = _c(A, np.int8), _c(W1, np.int8), _c(W2, np.int8), _c(act_lut, np.int8)
+    b1, b2 = _c(b1, np.int32), _c(b2, np.int32)
+    (M, K), (K2, V), (V2, D) = A.shape, W1.shape, W2.shape
+    assert K == K2 and V == V2 and act_lut.shape == (256,)
+    out = np.empty((M, D), np.int8)
+    check(load().hexcuda_host_ffn_lut_i8(_p(A), _p(W1), _p(b1), _p(act_lut), _p(W2), _p(b2), _p(out),
+                                         M, K, V, D, mult, shift, zp))
     return out
 
 

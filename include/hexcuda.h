@@ -262,14 +262,22 @@ int hexcuda_minmax_ew(int dev, const void *a, const void *b, int32_t c, int elem
 /* out[k] = sum_{j < w} a[w k + j] for k < g (int8 -> int32), w >= 1:
  * hvx_vradd_i8_reduce (w = 4). */
 int hexcuda_group_sum_i8(int dev, const int8_t *a, int32_t *out, int64_t g, int w);
+/* out[k] = sum_{j < w} a[w k + j] b[w k + j] (int32, modulo 2^32):
+ * kernels/expert/hvx_vrmpy_i8_dot/reference.c:3-9 (w = 4). */
+int hexcuda_group_dot_i8(int dev, const int8_t *a, const int8_t *b, int32_t *out, int64_t g, int w);
+/* out = sat8(round_half_away((lut[gate + 128] up) * mult >> shift)), n
+ * elements: the SiLU-gated product of kernels/expert/mlp_gate_silu_i8/
+ * reference.c:4-15. */
+int hexcuda_gate_mul_requant_i8(int dev, const int8_t *gate, const int8_t *up, const int8_t *lut,
+                                int8_t *out, int64_t n, int32_t mult, int shift);
 
 /* Inclusive prefix maximum, out[i] = max(-128, in[0..i]): i8_scan_max. */
 int hexcuda_scan_max_i8(int dev, const int8_t *in, int8_t *out, int64_t n);
 
-/* Head-group reduce: Y[g][i] = sat_i8(round_half_away(sum_{t < H/G}
- * X[g H/G + t][i] * mult >> shift)) for g < G, i < MN: gqa_group_reduce_i8
+/* Head-group reduce: Y[g][i] = sat_i8(round_half_away(sum_{t < heads/G}
+ * X[g heads/G + t][i] * mult >> shift)) for g < G, i < MN: gqa_group_reduce_i8
  * (reference.c: sum of the group's head planes, requant, clamp). */
-int hexcuda_head_group_reduce_i8(int dev, const int8_t *X, int8_t *Y, int H, int G,
+int hexcuda_head_group_reduce_i8(int dev, const int8_t *X, int8_t *Y, int heads, int G,
                                  int64_t MN, int32_t mult, int shift);
 
 /* int8 GEMM + requant: A [M,K] s8, B [K,N] s8 row-major, out [M,N] s8.
@@ -413,6 +421,25 @@ int hexcuda_attn_lut_i8(int dev, int mode, const void *Q, const int8_t *K, const
                         const uint8_t *exp_lut, const int8_t *cos_lut, const int8_t *sin_lut,
                         int rot_shift, void *out, int HQ, int HKV, int S, int D,
                         int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift);
+/* The REQUANT form (H query heads, one KV head each) with a banded mask:
+ * scores of keys with |i - j| > window are set to -128 and stay in the
+ * softmax.  kernels/expert/i8_sparse_attn_block/reference.c:33-42. */
+int hexcuda_attn_lut_i8_window(int dev, const int8_t *Q, const int8_t *K, const int8_t *V,
+                               const uint8_t *exp_lut, int8_t *out, int heads, int S, int D, int window,
+                               int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift);
+/* KV-cache write: for h < heads, k_cache[h][pos][:] = k_new[h][:] and
+ * v_cache[h][pos][:] = v_new[h][:], caches [heads][cache_len][head_dim] int8
+ * (kernels/expert/kv_cache_update/reference.c:14-25); 0 <= pos < cache_len. */
+int hexcuda_kv_cache_update_i8(int dev, int8_t *k_cache, int8_t *v_cache, const int8_t *k_new,
+                               const int8_t *v_new, int pos, int heads, int cache_len,
+                               int head_dim);
+/* Rotary embedding of interleaved fp16 pairs: out[2p] = x[2p] c - x[2p+1] s,
+ * out[2p+1] = x[2p] s + x[2p+1] c with c = cos_t[p], s = sin_t[p], in fp32
+ * without fused multiply-adds, one fp16 rounding per output
+ * (kernels/expert/rope_pair_fp16/reference.c:5-13).  x and out 4-byte
+ * aligned. */
+int hexcuda_rope_pair_f16(int dev, const uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
+                          uint16_t *out, int64_t n_pairs);
 /* int8 decoder block: causal LUT-softmax self-attention of X [S][D] (u8)
  * with scores clamp_i8(X.X^T >> 2), h = clamp_u8(X + clamp_i8(P.X >> 8)),
  * then out int8 = sat_i8(h + sat_i8((act_lut[clamp_i8((h.W1 >> 8) + b1) + 128]
@@ -451,6 +478,12 @@ int hexcuda_gemm_i8_acc(int dev, const void *A, int a_signed, const int8_t *B, i
 int hexcuda_ffn_relu_i8(int dev, const int8_t *A, const int8_t *W1, const int32_t *b1,
                         const int8_t *W2, const int32_t *b2, int8_t *out, int M, int K, int V,
                         int D, int32_t mult, int shift, int8_t zp);
+/* Same with a table activation between the layers: hid = act_lut[sat8(A W1 +
+ * b1) + 128] (kernels/expert/mlp_block/reference.c:19-30); the second layer
+ * and its requant are hexcuda_ffn_relu_i8's. */
+int hexcuda_ffn_lut_i8(int dev, const int8_t *A, const int8_t *W1, const int32_t *b1,
+                       const int8_t *act_lut, const int8_t *W2, const int32_t *b2, int8_t *out,
+                       int M, int K, int V, int D, int32_t mult, int shift, int8_t zp);
 /* HMX-convention GEMM with s8 A [M,K] and u8 B [K,N] (the weights-by-
  * activations form of the 1x1 convolutions, i8_conv2d_1x1_hmx/kernel_api.h:17,
  * i8_pointwise_conv_hmx/kernel_api.h:16); store kinds as hexcuda_gemm_hmx_ex
@@ -557,9 +590,15 @@ int hexcuda_host_reduce_int(const void *a, const void *b, int elem, int64_t n, i
 int hexcuda_host_minmax_ew(const void *a, const void *b, int32_t c, int elem, int op,
                            void *out, int64_t n);
 int hexcuda_host_group_sum_i8(const int8_t *a, int32_t *out, int64_t g, int w);
+int hexcuda_host_group_dot_i8(const int8_t *a, const int8_t *b, int32_t *out, int64_t g, int w);
+int hexcuda_host_gate_mul_requant_i8(const int8_t *gate, const int8_t *up, const int8_t *lut,
+                                     int8_t *out, int64_t n, int32_t mult, int shift);
+int hexcuda_host_ffn_lut_i8(const int8_t *A, const int8_t *W1, const int32_t *b1,
+                            const int8_t *act_lut, const int8_t *W2, const int32_t *b2, int8_t *out,
+                            int M, int K, int V, int D, int32_t mult, int shift, int8_t zp);
 /* on the first device only (a prefix scan) */
 int hexcuda_host_scan_max_i8(const int8_t *in, int8_t *out, int64_t n);
-int hexcuda_host_head_group_reduce_i8(const int8_t *X, int8_t *Y, int H, int G, int64_t MN,
+int hexcuda_host_head_group_reduce_i8(const int8_t *X, int8_t *Y, int heads, int G, int64_t MN,
                                       int32_t mult, int shift);
 /* x has R rows, or xrows rows gathered through idx (idx not NULL) */
 int hexcuda_host_layernorm_lut_i8(const int8_t *x, int xrows, const int32_t *idx,
@@ -613,6 +652,15 @@ int hexcuda_host_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int
                              const int8_t *sin_lut, int rot_shift, void *out, int HQ,
                              int HKV, int S, int D, int32_t scale_mult, int scale_shift,
                              int32_t av_mult, int av_shift);
+int hexcuda_host_attn_lut_i8_window(const int8_t *Q, const int8_t *K, const int8_t *V,
+                                    const uint8_t *exp_lut, int8_t *out, int heads, int S, int D,
+                                    int window, int32_t scale_mult, int scale_shift,
+                                    int32_t av_mult, int av_shift);
+int hexcuda_host_kv_cache_update_i8(int8_t *k_cache, int8_t *v_cache, const int8_t *k_new,
+                                    const int8_t *v_new, int pos, int heads, int cache_len,
+                                    int head_dim);
+int hexcuda_host_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
+                               uint16_t *out, int64_t n_pairs);
 int hexcuda_host_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
                                   const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
                                   const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff);

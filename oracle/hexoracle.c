@@ -285,10 +285,11 @@ static void lut_softmax_row(const int8_t *row, uint8_t *p, int n, int width, con
 
 static int hmx_field_i(int acc) { return ((int)((uint32_t)acc * 17u + 8u) >> 4) & 0xFFF; }
 
-void oracle_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int8_t *V,
-                        const uint8_t *exp_lut, const int8_t *cos_lut, const int8_t *sin_lut,
-                        int rot_shift, void *out, int HQ, int HKV, int S, int D,
-                        int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift) {
+static void attn_lut_i8_impl(int mode, const void *Q, const int8_t *K, const int8_t *V,
+                             const uint8_t *exp_lut, const int8_t *cos_lut, const int8_t *sin_lut,
+                             int rot_shift, void *out, int HQ, int HKV, int S, int D,
+                             int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift,
+                             int window) {
     const int group = HQ / HKV, half_d = D / 2;
     int8_t *sc = (int8_t *)malloc((size_t)S * S);
     uint8_t *pr = (uint8_t *)malloc((size_t)S * S);
@@ -320,6 +321,9 @@ void oracle_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int8_t *
                     acc += (mode == 0 ? (int)Qs[i * D + d] : (int)Qh[i * D + d]) * (int)Kh[j * D + d];
                 sc[i * S + j] = (int8_t)(mode == 0 ? requant_i8_att(acc, scale_mult, scale_shift)
                                                    : clamp_i8i(sx12(hmx_field_i(acc)) >> 4));
+                /* i8_sparse_attn_block/reference.c:33-42: outside the band
+                 * the score is MASK_VAL (-128) and stays in the softmax */
+                if (window >= 0 && abs(i - j) > window) sc[i * S + j] = -128;
             }
         for (int i = 0; i < S; i++) lut_softmax_row(sc + (size_t)i * S, pr + (size_t)i * S, S, S, exp_lut);
         for (int i = 0; i < S; i++)
@@ -334,6 +338,22 @@ void oracle_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int8_t *
             }
     }
     free(sc); free(pr); free(qr); free(kr);
+}
+
+void oracle_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int8_t *V,
+                        const uint8_t *exp_lut, const int8_t *cos_lut, const int8_t *sin_lut,
+                        int rot_shift, void *out, int HQ, int HKV, int S, int D,
+                        int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift) {
+    attn_lut_i8_impl(mode, Q, K, V, exp_lut, cos_lut, sin_lut, rot_shift, out, HQ, HKV, S, D,
+                     scale_mult, scale_shift, av_mult, av_shift, -1);
+}
+
+/* i8_sparse_attn_block/reference.c:14-62 (H heads of SEQ x HEAD_DIM) */
+void oracle_attn_lut_i8_window(const int8_t *Q, const int8_t *K, const int8_t *V,
+                               const uint8_t *exp_lut, int8_t *out, int H, int S, int D, int window,
+                               int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift) {
+    attn_lut_i8_impl(0, Q, K, V, exp_lut, NULL, NULL, 0, out, H, H, S, D, scale_mult, scale_shift,
+                     av_mult, av_shift, window);
 }
 
 void oracle_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
@@ -467,6 +487,18 @@ void oracle_ffn_relu_i8(const int8_t *A, const int8_t *W1, const int32_t *b1, co
     int8_t *hid = (int8_t *)malloc((size_t)M * (V > 0 ? V : 1));
     oracle_gemm_i8_acc_rows(A, 1, W1, 0, b1, NULL, 0, NULL, hid, ORACLE_HMX_STORE_I8_SAT,
                             ORACLE_HMX_ACT_RELU, M, V, K, 0, M);
+    oracle_gemm_i8_rq_ex_rows(hid, W2, 0, b2, NULL, out, M, D, V, mult, shift, zp, 0, 0, M);
+    free(hid);
+}
+
+/* mlp_block/reference.c:19-47: the first layer through the table, the second
+ * as ffn_relu_block's. */
+void oracle_ffn_lut_i8(const int8_t *A, const int8_t *W1, const int32_t *b1, const int8_t *act_lut,
+                       const int8_t *W2, const int32_t *b2, int8_t *out, int M, int K, int V, int D,
+                       int32_t mult, int shift, int zp) {
+    int8_t *hid = (int8_t *)malloc((size_t)M * (V > 0 ? V : 1));
+    oracle_gemm_i8_acc_rows(A, 1, W1, 0, b1, NULL, 0, act_lut, hid, ORACLE_HMX_STORE_LUT_I8,
+                            ORACLE_HMX_ACT_NONE, M, V, K, 0, M);
     oracle_gemm_i8_rq_ex_rows(hid, W2, 0, b2, NULL, out, M, D, V, mult, shift, zp, 0, 0, M);
     free(hid);
 }
@@ -1031,6 +1063,25 @@ void oracle_group_sum_i8(const int8_t *a, int32_t *out, int64_t g, int w) {
     }
 }
 
+/* hvx_vrmpy_i8_dot/reference.c:3-9 (w = 4) */
+void oracle_group_dot_i8(const int8_t *a, const int8_t *b, int32_t *out, int64_t g, int w) {
+    for (int64_t k = 0; k < g; k++) {
+        uint32_t s = 0;
+        for (int j = 0; j < w; j++) s += (uint32_t)((int32_t)a[k * w + j] * (int32_t)b[k * w + j]);
+        out[k] = (int32_t)s;
+    }
+}
+
+/* mlp_gate_silu_i8/reference.c:4-15 */
+void oracle_gate_mul_requant_i8(const int8_t *gate, const int8_t *up, const int8_t *lut,
+                                int8_t *out, int64_t n, int32_t mult, int shift) {
+    for (int64_t i = 0; i < n; i++) {
+        const int32_t g = lut[(uint8_t)((int)gate[i] + 128)];
+        const int64_t q = rq_round((int64_t)(g * (int32_t)up[i]) * (int64_t)mult, shift);
+        out[i] = (int8_t)(q > 127 ? 127 : (q < -128 ? -128 : q));
+    }
+}
+
 /* i8_scan_max/reference.c:2-8 */
 void oracle_scan_max_i8(const int8_t *in, int8_t *out, int64_t n) {
     int8_t cur = -128;
@@ -1214,5 +1265,30 @@ void oracle_rmsnorm_gain_f16(const uint16_t *x, const uint16_t *gain, uint16_t *
         const float inv_rms = 1.0f / sqrtf(ms + eps);
         const float g = h2f(gain[r]);
         for (int c = 0; c < C; c++) out[(size_t)r * C + c] = f2h(h2f(xr[c]) * inv_rms * g);
+    }
+}
+
+/* kv_cache_update/reference.c:14-25 */
+void oracle_kv_cache_update_i8(int8_t *k_cache, int8_t *v_cache, const int8_t *k_new,
+                               const int8_t *v_new, int pos, int heads, int cache_len,
+                               int head_dim) {
+    for (int h = 0; h < heads; h++) {
+        const size_t base = ((size_t)h * cache_len + pos) * head_dim;
+        for (int d = 0; d < head_dim; d++) {
+            k_cache[base + d] = k_new[(size_t)h * head_dim + d];
+            v_cache[base + d] = v_new[(size_t)h * head_dim + d];
+        }
+    }
+}
+
+/* rope_pair_fp16/reference.c:5-13 (built with -ffp-contract=off: each
+ * product and sum is rounded to fp32) */
+void oracle_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
+                          uint16_t *out, int64_t n_pairs) {
+    for (int64_t p = 0; p < n_pairs; p++) {
+        const float xr = h2f(x[2 * p]), xi = h2f(x[2 * p + 1]);
+        const float c = h2f(cos_t[p]), s = h2f(sin_t[p]);
+        out[2 * p] = f2h(xr * c - xi * s);
+        out[2 * p + 1] = f2h(xr * s + xi * c);
     }
 }

@@ -116,6 +116,11 @@ void oracle_attn_lut_i8(int mode, const void *Q, const int8_t *K, const int8_t *
                         const uint8_t *exp_lut, const int8_t *cos_lut, const int8_t *sin_lut,
                         int rot_shift, void *out, int HQ, int HKV, int S, int D,
                         int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift);
+/* mode 0 with the banded mask of kernels/expert/i8_sparse_attn_block/
+ * reference.c: scores with |i - j| > window are -128 (still in the softmax). */
+void oracle_attn_lut_i8_window(const int8_t *Q, const int8_t *K, const int8_t *V,
+                               const uint8_t *exp_lut, int8_t *out, int heads, int S, int D, int window,
+                               int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift);
 /* kernels/expert/i8_decoder_block/reference.c */
 void oracle_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
                              const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
@@ -139,6 +144,11 @@ void oracle_gemm_i8_acc_rows(const void *A, int a_signed, const int8_t *B, int b
 void oracle_ffn_relu_i8(const int8_t *A, const int8_t *W1, const int32_t *b1, const int8_t *W2,
                         const int32_t *b2, int8_t *out, int M, int K, int V, int D, int32_t mult,
                         int shift, int zp);
+/* kernels/expert/mlp_block/reference.c: the first layer's activation is
+ * act_lut[sat8(acc + b1) + 128]. */
+void oracle_ffn_lut_i8(const int8_t *A, const int8_t *W1, const int32_t *b1, const int8_t *act_lut,
+                       const int8_t *W2, const int32_t *b2, int8_t *out, int M, int K, int V, int D,
+                       int32_t mult, int shift, int zp);
 /* s8 A x u8 B HMX-field GEMM (i8_conv2d_1x1_hmx/reference.c,
  * i8_pointwise_conv_hmx/reference.c): store ORACLE_HMX_STORE_I32 (sx12),
  * _U16_FIELD or _ACC_I32. */
@@ -275,6 +285,12 @@ void oracle_minmax_ew(const void *a, const void *b, int32_t c, int elem, int op,
                       int64_t n);
 /* out[k] = sum_{j < w} a[w k + j] (hvx_vradd_i8_reduce/reference.c, w = 4). */
 void oracle_group_sum_i8(const int8_t *a, int32_t *out, int64_t g, int w);
+/* out[k] = sum_{j < w} a[w k + j] b[w k + j] (hvx_vrmpy_i8_dot/reference.c). */
+void oracle_group_dot_i8(const int8_t *a, const int8_t *b, int32_t *out, int64_t g, int w);
+/* sat8(round_half_away(lut[gate + 128] up * mult >> shift))
+ * (mlp_gate_silu_i8/reference.c). */
+void oracle_gate_mul_requant_i8(const int8_t *gate, const int8_t *up, const int8_t *lut,
+                                int8_t *out, int64_t n, int32_t mult, int shift);
 /* inclusive prefix max from -128 (i8_scan_max/reference.c). */
 void oracle_scan_max_i8(const int8_t *in, int8_t *out, int64_t n);
 /* gqa_group_reduce_i8/reference.c: sum of a group's H/G head planes, requant. */
@@ -332,6 +348,14 @@ typedef struct {
 typedef struct {
     const float *x, *gamma, *beta; float *out; int R, C; float eps; int op;
 } oracle_rows_args;
+
+/* kernels/expert/kv_cache_update/reference.c: row pos of each head's caches. */
+void oracle_kv_cache_update_i8(int8_t *k_cache, int8_t *v_cache, const int8_t *k_new,
+                               const int8_t *v_new, int pos, int heads, int cache_len,
+                               int head_dim);
+/* kernels/expert/rope_pair_fp16/reference.c: interleaved-pair rotation. */
+void oracle_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
+                          uint16_t *out, int64_t n_pairs);
 
 #ifdef __cplusplus
 }

@@ -190,6 +190,17 @@ def attn_lut_i8(mode, Q, K, V, exp_lut, cos_lut=None, sin_lut=None, rot_shift=0,
     return out
 
 
+def attn_lut_i8_window(Q, K, V, exp_lut, window, scale_mult, scale_shift, av_mult, av_shift):
+    """Q / K / V [H, S, D] int8; requant scores outside |i - j| <= window set to -128."""
+    Q, K, V = (np.ascontiguousarray(x, np.int8) for x in (Q, K, V))
+    H, S, D = Q.shape
+    out = np.zeros(Q.shape, np.int8)
+    lib().oracle_attn_lut_i8_window(_p(Q), _p(K), _p(V), _p(np.ascontiguousarray(exp_lut, np.uint8)),
+                                    _p(out), H, S, D, window, C.c_int32(scale_mult), scale_shift,
+                                    C.c_int32(av_mult), av_shift)
+    return out
+
+
 def decoder_block_i8(X, W1, b1, act_lut, W2, b2, exp_lut):
     X = np.ascontiguousarray(X, np.uint8)
     W1, W2 = np.ascontiguousarray(W1, np.int8), np.ascontiguousarray(W2, np.int8)
@@ -268,6 +279,16 @@ def ffn_relu_i8(A, W1, b1, W2, b2, mult, shift, zp):
     out = np.zeros((M, D), np.int8)
     lib().oracle_ffn_relu_i8(_p(A), _p(W1), _p(b1), _p(W2), _p(b2), _p(out), M, K, V, D,
                              C.c_int32(mult), shift, zp)
+    return out
+
+
+def ffn_lut_i8(A, W1, b1, act_lut, W2, b2, mult, shift, zp):
+    A, W1, W2, act_lut = (np.ascontiguousarray(x, np.int8) for x in (A, W1, W2, act_lut))
+    b1, b2 = np.ascontiguousarray(b1, np.int32), np.ascontiguousarray(b2, np.int32)
+    (M, K), (_, V), (_, D) = A.shape, W1.shape, W2.shape
+    out = np.zeros((M, D), np.int8)
+    lib().oracle_ffn_lut_i8(_p(A), _p(W1), _p(b1), _p(act_lut), _p(W2), _p(b2), _p(out), M, K, V,
+                            D, C.c_int32(mult), shift, zp)
     return out
 
 
@@ -468,6 +489,24 @@ def group_sum_i8(a, w=4):
     return out
 
 
+def group_dot_i8(a, b, w=4):
+    a = np.ascontiguousarray(a, np.int8).ravel()
+    b = np.ascontiguousarray(b, np.int8).ravel()
+    g = a.size // w
+    out = np.zeros(g, np.int32)
+    lib().oracle_group_dot_i8(_p(a), _p(b), _p(out), C.c_int64(g), w)
+    return out
+
+
+def gate_mul_requant_i8(gate, up, lut, mult, shift):
+    gate, up = np.ascontiguousarray(gate, np.int8), np.ascontiguousarray(up, np.int8)
+    lut = np.ascontiguousarray(lut, np.int8)
+    out = np.zeros(gate.shape, np.int8)
+    lib().oracle_gate_mul_requant_i8(_p(gate), _p(up), _p(lut), _p(out), C.c_int64(gate.size),
+                                     C.c_int32(int(mult)), shift)
+    return out
+
+
 def scan_max_i8(x):
     x = np.ascontiguousarray(x, np.int8).ravel()
     out = np.zeros_like(x)
@@ -573,4 +612,21 @@ def rmsnorm_f16(x, gamma, eps):
     out = np.zeros_like(x)
     R, Cc = x.shape
     lib().oracle_rmsnorm_f16_rows(_p(x), _p(g), _p(out), R, Cc, C.c_float(eps), 0, R)
+    return out
+
+
+def kv_cache_update_i8(k_cache, v_cache, k_new, v_new, pos):
+    k_cache, v_cache = np.array(k_cache, np.int8), np.array(v_cache, np.int8)
+    heads, cache_len, head_dim = k_cache.shape
+    k_new, v_new = np.ascontiguousarray(k_new, np.int8), np.ascontiguousarray(v_new, np.int8)
+    lib().oracle_kv_cache_update_i8(_p(k_cache), _p(v_cache), _p(k_new), _p(v_new), pos, heads,
+                                    cache_len, head_dim)
+    return k_cache, v_cache
+
+
+def rope_pair_f16(x, cos_t, sin_t):
+    x = np.ascontiguousarray(x, np.float16).ravel()
+    cos_t, sin_t = np.ascontiguousarray(cos_t, np.float16), np.ascontiguousarray(sin_t, np.float16)
+    out = np.zeros_like(x)
+    lib().oracle_rope_pair_f16(_p(x), _p(cos_t), _p(sin_t), _p(out), C.c_int64(x.size // 2))
     return out

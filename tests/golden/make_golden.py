@@ -895,6 +895,123 @@ def gen_i8_acc_callers(ref):
     save("i8_acc_callers", **a)
 
 
+def gen_dot_callers(ref):
+    # The matrix-vector, dot-product, narrow-GEMM, outer-product, FFN-down,
+    # table-activation MLP and SiLU-gate bundles through their reference.c:
+    # full-range operands where the reference's int32 sums stay defined
+    # (i8_dot_i32_dma also in its harness's [-16, 16] range;
+    # i16_dot_i32_dma accumulates in int64 and keeps the low 32 bits, so its
+    # full-range case wraps); small-range operands where a table must be hit
+    # inside its range; mlp_block at its reference's fixed hidden buffer
+    # (M * V <= 256).
+    rng = np.random.default_rng(131)
+    s8 = lambda lo, hi, *sh: rng.integers(lo, hi, sh, dtype=np.int8)
+    a = {}
+
+    def run(name, args, **arrs):
+        getattr(ref, "ref_" + name)(*args)
+        for k, v in arrs.items():
+            a[f"{name}__{k}"] = v
+
+    for t, (M, K) in enumerate(((256, 130), (300, 1000))):
+        A, x = s8(-128, 128, M, K), s8(-128, 128, K)
+        y = np.zeros(M, np.int32)
+        run("i8_matvec", (ptr(A), ptr(x), ptr(y), M, K), **{f"A{t}": A, f"x{t}": x, f"out{t}": y})
+    M, N, K = 70, 90, 110
+    A, Bt = s8(-128, 128, M, K), s8(-128, 128, N, K)
+    bias = rng.integers(-2**20, 2**20, N).astype(np.int32)
+    for t, (mult, shift) in enumerate(((1 << 10, 25), (-7, 17), (3, 0))):
+        o = np.zeros((M, N), np.int8)
+        run("ffn_down_i8", (ptr(A), ptr(Bt), ptr(bias), ptr(o), M, N, K, C.c_int32(mult), shift),
+            **{f"out{t}": o})
+    a.update(ffn_down_i8__A=A, ffn_down_i8__B=Bt, ffn_down_i8__bias=bias)
+    for t, (n, lo, hi) in enumerate(((65549, -16, 17), (100003, -128, 128))):
+        x, y = s8(lo, hi, n), s8(lo, hi, n)
+        o = np.zeros(1, np.int32)
+        run("i8_dot_i32_dma", (ptr(x), ptr(y), n, ptr(o)), **{f"a{t}": x, f"b{t}": y, f"out{t}": o})
+    for t, n in enumerate((65543, 1000)):
+        x = rng.integers(-32768, 32768, n).astype(np.int16)
+        y = rng.integers(-32768, 32768, n).astype(np.int16)
+        o = np.zeros(1, np.int32)
+        run("i16_dot_i32_dma", (ptr(x), ptr(y), n, ptr(o)), **{f"a{t}": x, f"b{t}": y, f"out{t}": o})
+    for t, g in enumerate((261, 1000)):
+        x, y = s8(-128, 128, 4 * g), s8(-128, 128, 4 * g)
+        o = np.zeros(g, np.int32)
+        run("hvx_vrmpy_i8_dot", (ptr(x), ptr(y), ptr(o), g), **{f"a{t}": x, f"b{t}": y, f"out{t}": o})
+    M, K, N = 161, 8101, 4
+    A, X = s8(-128, 128, M, K), s8(-128, 128, K, N)
+    o = np.zeros((M, N), np.int32)
+    run("vtcm_stage_matmul_i8", (ptr(A), ptr(X), ptr(o), M, K, N), A=A, X=X, out=o)
+    for t, (M, N) in enumerate(((128, 128), (33, 200))):
+        x, y = s8(-128, 128, M), s8(-128, 128, N)
+        o = np.zeros((M, N), np.int32)
+        run("i8_outer_product", (ptr(x), ptr(y), ptr(o), M, N), **{f"a{t}": x, f"b{t}": y, f"out{t}": o})
+    M, K, V, D = 8, 16, 32, 16
+    A, W1, W2 = s8(-4, 5, M, K), s8(-4, 5, K, V), s8(-8, 9, V, D)
+    b1 = rng.integers(-150, 150, V).astype(np.int32)
+    b2 = rng.integers(-2000, 2000, D).astype(np.int32)
+    lut = s8(-128, 128, 256)
+    a.update(mlp_block__A=A, mlp_block__W1=W1, mlp_block__W2=W2, mlp_block__b1=b1, mlp_block__b2=b2,
+             mlp_block__lut=lut)
+    for t, (mult, shift, zp) in enumerate(((3, 10, 0), (7, 11, -3))):
+        o = np.zeros((M, D), np.int8)
+        run("mlp_block", (ptr(A), ptr(W1), ptr(b1), ptr(lut), ptr(W2), ptr(b2), ptr(o), M, K, V, D,
+                          C.c_int32(mult), shift, C.c_int8(zp)), **{f"out{t}": o})
+    silu = s8(-128, 128, 256)
+    a["mlp_gate_silu_i8__lut"] = silu
+    for t, (n, mult, shift) in enumerate(((150, 3, 7), (150, 5, 3), (100003, 1 << 20, 27))):
+        gate, up = s8(-128, 128, n), s8(-128, 128, n)
+        o = np.zeros(n, np.int8)
+        run("mlp_gate_silu_i8", (ptr(gate), ptr(up), ptr(silu), ptr(o), n, C.c_int32(mult), shift),
+            **{f"gate{t}": gate, f"up{t}": up, f"out{t}": o})
+    save("dot_callers", **a)
+
+
+def gen_sparse_attn(ref):
+    # i8_sparse_attn_block through its reference.c (fixed H 1, SEQ 8,
+    # HEAD_DIM 16): full-range Q / K / V, random exp tables, the band widths
+    # 0 (diagonal only), 1, 2 and 7 (no key masked) and two requant sets.
+    rng = np.random.default_rng(137)
+    a = {}
+    t = 0
+    for window in (0, 1, 2, 7):
+        for smult, sshift, amult, ashift in ((3, 7, 5, 8), (1 << 12, 17, 77, 14)):
+            Q, K, V = (rng.integers(-128, 128, (1, 8, 16), dtype=np.int8) for _ in range(3))
+            lut = rng.integers(0, 256, 256, dtype=np.uint8)
+            lut[255] = 255
+            o = np.zeros((1, 8, 16), np.int8)
+            ref.ref_i8_sparse_attn_block(ptr(Q), ptr(K), ptr(V), ptr(lut), ptr(o), window,
+                                         C.c_int32(smult), sshift, C.c_int32(amult), ashift)
+            a.update({f"Q{t}": Q, f"K{t}": K, f"V{t}": V, f"lut{t}": lut, f"out{t}": o,
+                      f"params{t}": np.array([window, smult, sshift, amult, ashift], np.int64)})
+            t += 1
+    save("sparse_attn", **a)
+
+
+def gen_cache_rope(ref):
+    # kv_cache_update and rope_pair_fp16 through their reference.c: caches at
+    # the harness's shape (positions 0 and 63) and a ragged one (head_dim
+    # 20); rotations of N(0, 4) fp16 pairs by random angles at the harness's
+    # n (100) and a longer odd n.
+    rng = np.random.default_rng(139)
+    a = {}
+    for t, (heads, cl, hd, pos) in enumerate(((4, 64, 32, 0), (4, 64, 32, 63), (3, 50, 20, 17))):
+        kc, vc = (rng.integers(-128, 128, (heads, cl, hd), dtype=np.int8) for _ in range(2))
+        kn, vn = (rng.integers(-128, 128, (heads, hd), dtype=np.int8) for _ in range(2))
+        a.update({f"kc{t}": kc.copy(), f"vc{t}": vc.copy(), f"kn{t}": kn, f"vn{t}": vn,
+                  f"pos{t}": np.array(pos)})
+        ref.ref_kv_cache_update(ptr(kc), ptr(vc), ptr(kn), ptr(vn), pos, heads, cl, hd)
+        a.update({f"kout{t}": kc, f"vout{t}": vc})
+    for t, n in enumerate((100, 4099)):
+        x = (rng.standard_normal(2 * n) * 4).astype(np.float16)
+        th = rng.uniform(-np.pi, np.pi, n)
+        c, sn = np.cos(th).astype(np.float16), np.sin(th).astype(np.float16)
+        o = np.zeros(2 * n, np.float16)
+        ref.ref_rope_pair_fp16(ptr(x), ptr(c), ptr(sn), ptr(o), n)
+        a.update({f"x{t}": x, f"cos{t}": c, f"sin{t}": sn, f"rope{t}": o})
+    save("cache_rope", **a)
+
+
 def gen_int_rows(ref):
     # The attention-tile callers, the integer layernorms with an inverse-
     # variance table, the exp-table softmax tiles, the int16 requant, the
@@ -1031,6 +1148,11 @@ def main():
     if not (REF_ROOT / "kernels").is_dir():
         sys.exit(f"reference tree not found at {REF_ROOT}")
     ref = load_ref()
+    if len(sys.argv) > 1:                       # named generators only
+        for name in sys.argv[1:]:
+            fn = globals()[name]
+            fn() if name == "gen_mined_fp32_sum" else fn(ref)
+        return
     gen_i8_gemm_requant(ref)
     gen_i8_gemm_requant_256(ref)
     gen_i8_gemm_bias_requant(ref)
@@ -1049,6 +1171,9 @@ def main():
     gen_i8_acc_callers(ref)
     gen_int_rows(ref)
     gen_softmax_rms(ref)
+    gen_dot_callers(ref)
+    gen_sparse_attn(ref)
+    gen_cache_rope(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

@@ -460,3 +460,85 @@ def test_ffn_relu_i8_random(hx, oracle):
     b2 = rng.integers(-50000, 50000, D).astype(np.int32)
     np.testing.assert_array_equal(hx.ffn_relu_i8(A, W1, b1, W2, b2, 1 << 28, 36, 5),
                                   oracle.ffn_relu_i8(A, W1, b1, W2, b2, 1 << 28, 36, 5))
+
+
+# ------------------------------------------- dot, narrow-GEMM and MLP callers
+
+from test_oracle_golden import dot_calls  # noqa: E402
+
+
+def test_dot_callers_golden(hx):
+    for k, (got, exp) in enumerate(dot_calls(hx, golden("dot_callers"))):
+        np.testing.assert_array_equal(got, exp, err_msg=str(k))
+
+
+def _shim(name):
+    import ctypes as C
+    import subprocess
+    from pathlib import Path
+    shims = Path(__file__).resolve().parent.parent / "hexkernels_b200" / "shims"
+    so = shims / f"libcand_{name}.so"
+    if not so.exists():
+        subprocess.run(["make", "-s", "-C", str(shims)], check=True)
+    fn = C.CDLL(str(so)).candidate_kernel
+    fn.restype = None
+    return fn
+
+
+def test_dot_callers_sdk_shims(hx):
+    """The three bundles whose harnesses need the Hexagon SDK, through their
+    candidate_kernel shims on the golden cases."""
+    import ctypes as C
+    p = lambda a: a.ctypes.data_as(C.c_void_p)
+    g = golden("dot_callers")
+    for n in ("i8_dot_i32_dma", "i16_dot_i32_dma"):
+        for t in range(2):
+            a, b = g[f"{n}__a{t}"], g[f"{n}__b{t}"]
+            out = np.zeros(1, np.int32)
+            _shim(n)(p(a), p(b), a.size, p(out))
+            np.testing.assert_array_equal(out, g[f"{n}__out{t}"])
+    n = "vtcm_stage_matmul_i8"
+    A, X = g[n + "__A"], g[n + "__X"]
+    out = np.zeros((A.shape[0], X.shape[1]), np.int32)
+    _shim(n)(p(A), p(X), p(out), A.shape[0], A.shape[1], X.shape[1])
+    np.testing.assert_array_equal(out, g[n + "__out"])
+
+
+@pytest.mark.parametrize("M,K", [(1, 1), (4097, 8101), (20000, 4096)])
+def test_matvec_and_narrow_random(hx, oracle, M, K):
+    rng = np.random.default_rng(M + K)
+    A = rng.integers(-128, 128, (M, K), dtype=np.int8)
+    x = rng.integers(-128, 128, (1, K), dtype=np.int8)
+    np.testing.assert_array_equal(hx.gemm_i8_acc(x, A, b_transposed=True),
+                                  oracle.gemm_i8_acc(x, A, b_transposed=True))
+    X = rng.integers(-128, 128, (K, 4), dtype=np.int8)
+    np.testing.assert_array_equal(hx.gemm_i8_acc(A, X), oracle.gemm_i8_acc(A, X))
+
+
+def test_outer_product_and_group_dot_random(hx, oracle):
+    rng = np.random.default_rng(29)
+    a, b = rng.integers(-128, 128, (3000, 1), dtype=np.int8), rng.integers(-128, 128, (1, 5001), dtype=np.int8)
+    np.testing.assert_array_equal(hx.gemm_i8_acc(a, b), oracle.gemm_i8_acc(a, b))
+    x = rng.integers(-128, 128, (1 << 22) + 44, dtype=np.int8)
+    y = rng.integers(-128, 128, (1 << 22) + 44, dtype=np.int8)
+    for w in (4, 3, 1, 64):
+        np.testing.assert_array_equal(hx.group_dot_i8(x, y, w), oracle.group_dot_i8(x, y, w))
+    np.testing.assert_array_equal(hx.group_dot_i8(x[1:], y[1:], 4), oracle.group_dot_i8(x[1:], y[1:], 4))
+
+
+def test_gate_mul_requant_and_ffn_lut_random(hx, oracle):
+    rng = np.random.default_rng(31)
+    n = (1 << 22) + 3
+    gate, up = rng.integers(-128, 128, n, dtype=np.int8), rng.integers(-128, 128, n, dtype=np.int8)
+    lut = rng.integers(-128, 128, 256, dtype=np.int8)
+    for mult, shift in ((3, 7), (5, 0), (-(1 << 20), 27), (2**31 - 1, 63), (1 << 30, 40)):
+        np.testing.assert_array_equal(hx.gate_mul_requant_i8(gate, up, lut, mult, shift),
+                                      oracle.gate_mul_requant_i8(gate, up, lut, mult, shift))
+    M, K, V, D = 300, 256, 512, 200
+    A = rng.integers(-8, 9, (M, K), dtype=np.int8)
+    W1 = rng.integers(-8, 9, (K, V), dtype=np.int8)
+    W2 = rng.integers(-128, 128, (V, D), dtype=np.int8)
+    b1 = rng.integers(-300, 300, V).astype(np.int32)
+    b2 = rng.integers(-50000, 50000, D).astype(np.int32)
+    np.testing.assert_array_equal(hx.ffn_lut_i8(A, W1, b1, lut, W2, b2, 1 << 28, 36, 5),
+                                  oracle.ffn_lut_i8(A, W1, b1, lut, W2, b2, 1 << 28, 36, 5))

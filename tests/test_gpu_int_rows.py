@@ -152,3 +152,78 @@ def test_attention_qkt_tile_shim(hx):
     fn.argtypes = [C.c_void_p] * 3 + [C.c_int] * 3 + [C.c_int32, C.c_int]
     fn(p(Q), p(K), p(out), Q.shape[0], K.shape[0], Q.shape[1], 1 << 20, 26)
     np.testing.assert_array_equal(out, exp)
+
+
+from test_oracle_golden import sparse_attn_calls  # noqa: E402
+
+
+def test_sparse_attn_golden_and_shim(hx):
+    g = golden("sparse_attn")
+    for got, exp in sparse_attn_calls(hx, g):
+        np.testing.assert_array_equal(got, exp)
+    fn = shim("i8_sparse_attn_block")
+    fn.argtypes = [C.c_void_p] * 5 + [C.c_int, C.c_int32, C.c_int, C.c_int32, C.c_int]
+    for t in range(8):
+        w, sm, ss, am, ash = (int(v) for v in g[f"params{t}"])
+        out = np.zeros((1, 8, 16), np.int8)
+        fn(p(g[f"Q{t}"]), p(g[f"K{t}"]), p(g[f"V{t}"]), p(g[f"lut{t}"]), p(out), w, sm, ss, am, ash)
+        np.testing.assert_array_equal(out, g[f"out{t}"])
+
+
+@pytest.mark.parametrize("H,S,D", [(1, 1, 1), (4, 33, 20), (16, 128, 64)])
+def test_sparse_attn_random(hx, oracle, H, S, D):
+    rng = np.random.default_rng(H * S + D)
+    Q, K, V = (rng.integers(-128, 128, (H, S, D), dtype=np.int8) for _ in range(3))
+    lut = rng.integers(0, 256, 256, dtype=np.uint8)
+    lut[255] = 255
+    for w in (0, 1, 5, S):
+        for sm, ss, am, ash in ((3, 7, 5, 8), (1 << 12, 17, 77, 14)):
+            np.testing.assert_array_equal(hx.attn_lut_i8_window(Q, K, V, lut, w, sm, ss, am, ash),
+                                          oracle.attn_lut_i8_window(Q, K, V, lut, w, sm, ss, am, ash))
+
+
+from test_oracle_golden import cache_rope_calls  # noqa: E402
+
+
+def test_cache_rope_golden_and_shims(hx):
+    g = golden("cache_rope")
+    for got, exp in cache_rope_calls(hx, g):
+        np.testing.assert_array_equal(got.view(np.uint8), exp.view(np.uint8))
+    fn = shim("kv_cache_update")
+    fn.argtypes = [C.c_void_p] * 4 + [C.c_int] * 4
+    for t in range(3):
+        kc, vc = g[f"kc{t}"].copy(), g[f"vc{t}"].copy()
+        heads, cl, hd = kc.shape
+        fn(p(kc), p(vc), p(g[f"kn{t}"]), p(g[f"vn{t}"]), int(g[f"pos{t}"]), heads, cl, hd)
+        np.testing.assert_array_equal(kc, g[f"kout{t}"])
+        np.testing.assert_array_equal(vc, g[f"vout{t}"])
+    fn = shim("rope_pair_fp16")
+    fn.argtypes = [C.c_void_p] * 4 + [C.c_int]
+    for t in range(2):
+        x = g[f"x{t}"]
+        out = np.zeros_like(x)
+        fn(p(x), p(g[f"cos{t}"]), p(g[f"sin{t}"]), p(out), x.size // 2)
+        np.testing.assert_array_equal(out.view(np.uint16), g[f"rope{t}"].view(np.uint16))
+
+
+@pytest.mark.parametrize("heads,cl,hd,pos", [(1, 1, 1, 0), (32, 4096, 128, 4095), (7, 300, 20, 123)])
+def test_kv_cache_update_random(hx, oracle, heads, cl, hd, pos):
+    rng = np.random.default_rng(heads + hd)
+    kc, vc = (rng.integers(-128, 128, (heads, cl, hd), dtype=np.int8) for _ in range(2))
+    kn, vn = (rng.integers(-128, 128, (heads, hd), dtype=np.int8) for _ in range(2))
+    ek, ev = oracle.kv_cache_update_i8(kc, vc, kn, vn, pos)
+    gk, gv = hx.kv_cache_update_i8(kc.copy(), vc.copy(), kn, vn, pos)
+    np.testing.assert_array_equal(gk, ek)
+    np.testing.assert_array_equal(gv, ev)
+    with pytest.raises(RuntimeError):
+        hx.kv_cache_update_i8(kc, vc, kn, vn, cl)
+
+
+def test_rope_pair_random(hx, oracle):
+    rng = np.random.default_rng(41)
+    n = (1 << 22) + 3
+    x = (rng.standard_normal(2 * n) * 30).astype(np.float16)
+    th = rng.uniform(-np.pi, np.pi, n)
+    c, s = np.cos(th).astype(np.float16), np.sin(th).astype(np.float16)
+    np.testing.assert_array_equal(hx.rope_pair_f16(x, c, s).view(np.uint16),
+                                  oracle.rope_pair_f16(x, c, s).view(np.uint16))

@@ -367,6 +367,83 @@ def test_i8_acc_callers_golden(oracle):
         np.testing.assert_array_equal(got, exp)
 
 
+def dot_calls(impl, g):
+    """(result, expected) of the matrix-vector, dot-product, narrow-GEMM,
+    outer-product, FFN-down, table-MLP and SiLU-gate bundles (golden
+    dot_callers) through `impl` (the oracle or the GPU ops module)."""
+    c = lambda n, k: g[f"{n}__{k}"]
+    for t in range(2):
+        x = c("i8_matvec", f"x{t}")
+        yield (impl.gemm_i8_acc(x[None, :], c("i8_matvec", f"A{t}"), b_transposed=True)[0],
+               c("i8_matvec", f"out{t}"))
+    for t, (mult, shift) in enumerate(((1 << 10, 25), (-7, 17), (3, 0))):
+        yield (impl.gemm_i8_rq_ex(c("ffn_down_i8", "A"), c("ffn_down_i8", "B"), mult, shift, 0,
+                                  bias=c("ffn_down_i8", "bias"), b_transposed=True),
+               c("ffn_down_i8", f"out{t}"))
+    for n in ("i8_dot_i32_dma", "i16_dot_i32_dma"):
+        for t in range(2):
+            yield (np.array([impl.reduce_int(c(n, f"a{t}"), "dot", c(n, f"b{t}"))], np.int32),
+                   c(n, f"out{t}"))
+    for t in range(2):
+        n = "hvx_vrmpy_i8_dot"
+        yield impl.group_dot_i8(c(n, f"a{t}"), c(n, f"b{t}")), c(n, f"out{t}")
+    n = "vtcm_stage_matmul_i8"
+    yield impl.gemm_i8_acc(c(n, "A"), c(n, "X")), c(n, "out")
+    for t in range(2):
+        n = "i8_outer_product"
+        yield impl.gemm_i8_acc(c(n, f"a{t}")[:, None], c(n, f"b{t}")[None, :]), c(n, f"out{t}")
+    n = "mlp_block"
+    for t, (mult, shift, zp) in enumerate(((3, 10, 0), (7, 11, -3))):
+        yield (impl.ffn_lut_i8(c(n, "A"), c(n, "W1"), c(n, "b1"), c(n, "lut"), c(n, "W2"), c(n, "b2"),
+                               mult, shift, zp), c(n, f"out{t}"))
+    n = "mlp_gate_silu_i8"
+    for t, (mult, shift) in enumerate(((3, 7), (5, 3), (1 << 20, 27))):
+        yield (impl.gate_mul_requant_i8(c(n, f"gate{t}"), c(n, f"up{t}"), c(n, "lut"), mult, shift),
+               c(n, f"out{t}"))
+
+
+def test_dot_callers_golden(oracle):
+    for k, (got, exp) in enumerate(dot_calls(oracle, golden("dot_callers"))):
+        np.testing.assert_array_equal(got, exp, err_msg=str(k))
+
+
+def sparse_attn_calls(impl, g):
+    """(result, expected) of i8_sparse_attn_block's golden cases through
+    `impl` (the oracle or the GPU ops module)."""
+    t = 0
+    while f"out{t}" in g:
+        w, sm, ss, am, ash = (int(v) for v in g[f"params{t}"])
+        yield (impl.attn_lut_i8_window(g[f"Q{t}"], g[f"K{t}"], g[f"V{t}"], g[f"lut{t}"], w, sm, ss, am,
+                                       ash), g[f"out{t}"])
+        t += 1
+
+
+def test_sparse_attn_golden(oracle):
+    n = 0
+    for got, exp in sparse_attn_calls(oracle, golden("sparse_attn")):
+        np.testing.assert_array_equal(got, exp)
+        n += 1
+    assert n == 8
+
+
+def cache_rope_calls(impl, g):
+    """(result, expected) of kv_cache_update's and rope_pair_fp16's golden
+    cases through `impl` (the oracle or the GPU ops module); the caches are
+    updated on copies."""
+    for t in range(3):
+        kc, vc = g[f"kc{t}"].copy(), g[f"vc{t}"].copy()
+        kc, vc = impl.kv_cache_update_i8(kc, vc, g[f"kn{t}"], g[f"vn{t}"], int(g[f"pos{t}"]))
+        yield kc, g[f"kout{t}"]
+        yield vc, g[f"vout{t}"]
+    for t in range(2):
+        yield impl.rope_pair_f16(g[f"x{t}"], g[f"cos{t}"], g[f"sin{t}"]), g[f"rope{t}"]
+
+
+def test_cache_rope_golden(oracle):
+    for got, exp in cache_rope_calls(oracle, golden("cache_rope")):
+        np.testing.assert_array_equal(got.view(np.uint8), exp.view(np.uint8))
+
+
 NORM_MULT = np.array([3, 5, 7, 9, 11, 13, 15, 17, 3, 5, 7, 9, 11, 13, 15, 17], np.int32)
 NORM_SHIFT = np.array([2, 3, 4, 5, 3, 4, 5, 6, 2, 3, 4, 5, 3, 4, 5, 6], np.int32)
 

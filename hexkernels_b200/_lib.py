@@ -70,6 +70,9 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_attn_lut_i8_window": (I, [I, P, P, P, P, P, I, I, I, I, I32, I, I32, I]),
     "hexcuda_kv_cache_update_i8": (I, [I, P, P, P, P, I, I, I, I]),
     "hexcuda_rope_pair_f16": (I, [I, P, P, P, P, I64]),
+    "hexcuda_ffn_hmx_i8": (I, [I, P, P, P, P, P, P, I, I, I, I, I]),
+    "hexcuda_ffn_swiglu_hmx_i8": (I, [I, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I]),
+    "hexcuda_encoder_block_i8": (I, [I, P, P, P, P, P, P, P, I, I, I]),
     "hexcuda_decoder_block_i8": (I, [I, P, P, P, P, P, P, P, P, I, I, I]),
     "hexcuda_attn_qkt_av_hmx": (I, [I, P, P, P, P, I, I, I]),
     "hexcuda_requant_ew": (I, [I, P, I, P, I, P, I64, I, I64, I32, I, I, I, I, I, I, I, P]),
@@ -122,6 +125,9 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_attn_lut_i8_window": (I, [P, P, P, P, P, I, I, I, I, I32, I, I32, I]),
     "hexcuda_host_kv_cache_update_i8": (I, [P, P, P, P, I, I, I, I]),
     "hexcuda_host_rope_pair_f16": (I, [P, P, P, P, I64]),
+    "hexcuda_host_ffn_hmx_i8": (I, [P, P, P, P, P, P, I, I, I, I, I]),
+    "hexcuda_host_ffn_swiglu_hmx_i8": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, I]),
+    "hexcuda_host_encoder_block_i8": (I, [P, P, P, P, P, P, P, I, I, I]),
     "hexcuda_host_decoder_block_i8": (I, [P, P, P, P, P, P, P, P, I, I, I]),
     "hexcuda_host_attn_qkt_av_hmx": (I, [P, P, P, P, I, I, I]),
     "hexcuda_host_requant_ew": (I, [P, I, P, I, P, I64, I, I64, I32, I, I, I, I, I, I, I, P]),

@@ -35,6 +35,7 @@
 #include <algorithm>
 #include <type_traits>
 
+#include "ew_launch.cuh"
 #include "hx_internal.h"
 #include "requant.cuh"
 #include "tc_common.cuh"
@@ -52,6 +53,12 @@ constexpr int kGroupM = 16;
 constexpr int kColParamBytes = 6 * 32 * 4;   // one epilogue warp's ColParams
 
 enum EpiKind { kEpiF16 = 0, kEpiRequant = 1, kEpiHmx = 2, kEpiF16Ex = 3 };
+
+// Activations of the HMX epilogue used only by the FFN compositions below
+// (the public entries accept HEXCUDA_HMX_ACT_* only): an arithmetic right
+// shift by post_shift after the bias, with ReLU (v > 0 ? v >> s : 0) or
+// without it.
+constexpr int kActReluShr = 16, kActShr = 17;
 
 struct EpiParams {
     void *out;
@@ -77,6 +84,7 @@ struct EpiParams {
     //   row-major [M, N]); activation; store (HEXCUDA_HMX_STORE_* of
     //   hexcuda.h); col_major stores out[j * ldo + i].  All adds wrap.
     int hmx_store, hmx_act, res_kind, col_major;
+    int post_shift;            // kActReluShr / kActShr
     const void *res;
     const void *lut;
     // hmx_raw: the raw accumulator instead of the sx12 field, with the bias,
@@ -293,6 +301,8 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
                 int32_t x = (int32_t)xu;
                 if (ep.hmx_act == HEXCUDA_HMX_ACT_RELU) x = max(x, 0);
                 else if (ep.hmx_act == HEXCUDA_HMX_ACT_LEAKY_SHR3) x = x >= 0 ? x : (x >> 3);
+                else if (ep.hmx_act == kActReluShr) x = x > 0 ? (x >> ep.post_shift) : 0;
+                else if (ep.hmx_act == kActShr) x >>= ep.post_shift;
                 switch (ep.hmx_store) {
                 case HEXCUDA_HMX_STORE_I8_SAT: x = min(max(x, -128), 127); break;
                 case HEXCUDA_HMX_STORE_U8_SAT: x = min(max(x, 0), 255); break;
@@ -1486,6 +1496,89 @@ HX_EXPORT int hexcuda_gemm_hmx_ex(int dev, const uint8_t *A, const int8_t *B, in
     ep.col_major = col_major ? 1 : 0;
     return run_gemm<MmaKind::I8, kEpiHmx, false, true>(dev, A, K, B, b_transposed != 0, M, N, K,
                                                        ep, zpA != 0, "gemm_hmx");
+}
+
+namespace hx {
+namespace {
+// u8 A x s8 B [K,N] HMX-field GEMM + bias, shift activation, int8 saturation
+int hmx_shift_gemm(int dev, const uint8_t *A, const int8_t *B, const int32_t *bias, int8_t *out,
+                   int M, int N, int K, int act, int shift, const char *name) {
+    EpiParams ep{};
+    ep.out = out;
+    ep.ldo = N;
+    ep.bias = bias;
+    ep.hmx_store = HEXCUDA_HMX_STORE_I8_SAT;
+    ep.hmx_act = act;
+    ep.post_shift = shift;
+    return run_gemm<MmaKind::I8, kEpiHmx, false, true>(dev, A, K, B, false, M, N, K, ep, false, name);
+}
+
+// Hu = (u8)(clamp((lut[g + 128] u) >> sh, -zp, zp - 1) + zp), lut read as int8
+// (i8_ffn_swiglu_block/kernel_api.h: sw_gate, sw_hu)
+__global__ void __launch_bounds__(256) swiglu_gate_kernel(const int8_t *__restrict__ g,
+                                                          const int8_t *__restrict__ u,
+                                                          const uint8_t *__restrict__ lut,
+                                                          uint8_t *__restrict__ hu, int64_t n,
+                                                          int sh, int zp) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        const int s = (int)(int8_t)__ldg(lut + (int)g[i] + 128);
+        int h = (s * (int)u[i]) >> sh;
+        h = h > zp - 1 ? zp - 1 : (h < -zp ? -zp : h);
+        hu[i] = (uint8_t)(h + zp);
+    }
+}
+}  // namespace
+}  // namespace hx
+
+HX_EXPORT int hexcuda_ffn_hmx_i8(int dev, const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                                 const int8_t *W2, const int32_t *b2, int8_t *out, int M, int D,
+                                 int Dff, int sh1, int sh2) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (M < 0 || D < 0 || Dff < 0 || sh1 < 0 || sh1 > 31 || sh2 < 0 || sh2 > 31)
+        return fail(HEXCUDA_ERR_ARG, "ffn_hmx_i8: M %d D %d Dff %d shifts %d / %d", M, D, Dff, sh1, sh2);
+    if (M == 0 || D == 0) return HEXCUDA_OK;
+    if (!X || !W1 || !b1 || !W2 || !b2 || !out) return fail(HEXCUDA_ERR_ARG, "ffn_hmx_i8: null pointer");
+    int8_t *hid = reinterpret_cast<int8_t *>(scratch(d, kSlotFfnHidden, (size_t)M * (Dff > 0 ? Dff : 1)));
+    if (!hid) return HEXCUDA_ERR_OOM;
+    if (int rc = hmx_shift_gemm(dev, X, W1, b1, hid, M, Dff, D, kActReluShr, sh1, "ffn_hmx_i8 (up)"))
+        return rc;
+    // hid is in [0, 127]: its bytes read the same as u8
+    return hmx_shift_gemm(dev, reinterpret_cast<const uint8_t *>(hid), W2, b2, out, M, D, Dff, kActShr,
+                          sh2, "ffn_hmx_i8 (down)");
+}
+
+HX_EXPORT int hexcuda_ffn_swiglu_hmx_i8(int dev, const uint8_t *X, const int8_t *Wg,
+                                        const int8_t *Wu, const int8_t *Wd, const int32_t *bd,
+                                        const uint8_t *silu_lut, int8_t *out, int M, int D, int Dff,
+                                        int sg, int su, int sh, int zp, int so) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (M < 0 || D < 0 || Dff < 0 || sg < 0 || sg > 31 || su < 0 || su > 31 || sh < 0 || sh > 31 ||
+        so < 0 || so > 31 || zp < 1 || zp > 128)
+        return fail(HEXCUDA_ERR_ARG, "ffn_swiglu_hmx_i8: M %d D %d Dff %d sg %d su %d sh %d zp %d so %d",
+                    M, D, Dff, sg, su, sh, zp, so);
+    if (M == 0 || D == 0) return HEXCUDA_OK;
+    if (!X || !Wg || !Wu || !Wd || !bd || !silu_lut || !out)
+        return fail(HEXCUDA_ERR_ARG, "ffn_swiglu_hmx_i8: null pointer");
+    const size_t n = (size_t)M * (Dff > 0 ? Dff : 1);
+    int8_t *g = reinterpret_cast<int8_t *>(scratch(d, kSlotFfnHidden, n));
+    int8_t *u = reinterpret_cast<int8_t *>(scratch(d, kSlotFfnHidden + 1, n));
+    uint8_t *hu = reinterpret_cast<uint8_t *>(scratch(d, kSlotFfnHidden + 2, n));
+    if (!g || !u || !hu) return HEXCUDA_ERR_OOM;
+    if (Dff > 0) {
+        if (int rc = hmx_shift_gemm(dev, X, Wg, nullptr, g, M, Dff, D, kActShr, sg, "ffn_swiglu (gate)"))
+            return rc;
+        if (int rc = hmx_shift_gemm(dev, X, Wu, nullptr, u, M, Dff, D, kActShr, su, "ffn_swiglu (up)"))
+            return rc;
+        launch_begin(d);
+        constexpr auto kern = swiglu_gate_kernel;
+        kern<<<resident_blocks<kern>(d, (int64_t)M * Dff), 256, 0, d->stream>>>(
+            g, u, silu_lut, hu, (int64_t)M * Dff, sh, zp);
+        if (int rc = launch_end(d, "ffn_swiglu (gate x up)")) return rc;
+    }
+    return hmx_shift_gemm(dev, hu, Wd, bd, out, M, D, Dff, kActShr, so, "ffn_swiglu (down)");
 }
 
 HX_EXPORT int hexcuda_gemm_hmx(int dev, const uint8_t *A, const int8_t *B, int b_transposed,

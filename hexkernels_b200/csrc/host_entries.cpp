@@ -1206,3 +1206,75 @@ HX_EXPORT int hexcuda_host_rope_pair_f16(const uint16_t *x, const uint16_t *cos_
         return hexcuda_rope_pair_f16(p.slot, dx, dc, ds, dout, np);
     });
 }
+
+HX_EXPORT int hexcuda_host_ffn_hmx_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                                      const int8_t *W2, const int32_t *b2, int8_t *out, int M,
+                                      int D, int Dff, int sh1, int sh2) {
+    if (M < 0 || D < 0 || Dff < 0) return fail(HEXCUDA_ERR_ARG, "host_ffn_hmx_i8: bad shape");
+    if (M == 0 || D == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_ffn_hmx_i8", {X, W1, b1, W2, b2, out})) return rc;
+    return run_sharded(M, out, (size_t)D, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const uint8_t *dX = stage_in(p.d, kSlotIn0, X + p.r0 * D, (size_t)(nr * D));
+        const int8_t *dW1 = stage_in(p.d, kSlotIn1, W1, (size_t)D * Dff);
+        const int32_t *db1 = stage_in(p.d, kSlotIn2, b1, (size_t)Dff);
+        const int8_t *dW2 = stage_in(p.d, kSlotIn3, W2, (size_t)Dff * D);
+        const int32_t *db2 = stage_in(p.d, kSlotIn4, b2, (size_t)D);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * D)));
+        if (!dX || !dW1 || !db1 || !dW2 || !db2 || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_ffn_hmx_i8(p.slot, dX, dW1, db1, dW2, db2, dout, (int)nr, D, Dff, sh1, sh2);
+    });
+}
+
+// The gate and up weights share one staging slot (two halves).
+HX_EXPORT int hexcuda_host_ffn_swiglu_hmx_i8(const uint8_t *X, const int8_t *Wg, const int8_t *Wu,
+                                             const int8_t *Wd, const int32_t *bd,
+                                             const uint8_t *silu_lut, int8_t *out, int M, int D,
+                                             int Dff, int sg, int su, int sh, int zp, int so) {
+    if (M < 0 || D < 0 || Dff < 0) return fail(HEXCUDA_ERR_ARG, "host_ffn_swiglu_hmx_i8: bad shape");
+    if (M == 0 || D == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_ffn_swiglu_hmx_i8", {X, Wg, Wu, Wd, bd, silu_lut, out})) return rc;
+    const size_t wsz = (size_t)D * Dff, wpad = (wsz + 15) & ~(size_t)15;
+    return run_sharded(M, out, (size_t)D, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const uint8_t *dX = stage_in(p.d, kSlotIn0, X + p.r0 * D, (size_t)(nr * D));
+        int8_t *dW = reinterpret_cast<int8_t *>(scratch(p.d, kSlotIn1, 2 * wpad + 16));
+        const int8_t *dWd = stage_in(p.d, kSlotIn2, Wd, wsz);
+        const int32_t *dbd = stage_in(p.d, kSlotIn3, bd, (size_t)D);
+        const uint8_t *dl = stage_in(p.d, kSlotIn4, silu_lut, 256);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * D)));
+        if (!dX || !dW || !dWd || !dbd || !dl || !dout) return hexcuda_last_error();
+        if (wsz) {
+            if (int rc = check(cudaMemcpyAsync(dW, Wg, wsz, cudaMemcpyHostToDevice, p.d->stream), "h2d"))
+                return rc;
+            if (int rc = check(cudaMemcpyAsync(dW + wpad, Wu, wsz, cudaMemcpyHostToDevice, p.d->stream),
+                               "h2d"))
+                return rc;
+        }
+        p.dout = dout;
+        return hexcuda_ffn_swiglu_hmx_i8(p.slot, dX, dW, dW + wpad, dWd, dbd, dl, dout, (int)nr, D, Dff,
+                                         sg, su, sh, zp, so);
+    });
+}
+
+HX_EXPORT int hexcuda_host_encoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                                            const int8_t *W2, const int32_t *b2,
+                                            const uint8_t *exp_lut, int8_t *out, int S, int D,
+                                            int Dff) {
+    if (S < 0 || D < 0 || Dff < 0) return fail(HEXCUDA_ERR_ARG, "host_encoder_block_i8: bad shape");
+    if (S == 0 || D == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_encoder_block_i8", {X, W1, b1, W2, b2, exp_lut, out})) return rc;
+    return run_sharded(1, out, (size_t)S * D, [&](Part &p) {
+        const uint8_t *dX = stage_in(p.d, kSlotIn0, X, (size_t)S * D);
+        const int8_t *dW1 = stage_in(p.d, kSlotIn1, W1, (size_t)D * Dff);
+        const int8_t *dW2 = stage_in(p.d, kSlotIn2, W2, (size_t)Dff * D);
+        const int32_t *db1 = stage_in(p.d, kSlotIn3, b1, (size_t)Dff);
+        const int32_t *db2 = stage_in(p.d, kSlotIn4, b2, (size_t)D);
+        const uint8_t *dl = stage_in(p.d, kSlotIn5, exp_lut, 256);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)S * D));
+        if (!dX || !dW1 || !dW2 || !db1 || !db2 || !dl || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_encoder_block_i8(p.slot, dX, dW1, db1, dW2, db2, dl, dout, S, D, Dff);
+    });
+}

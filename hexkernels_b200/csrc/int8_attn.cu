@@ -239,8 +239,16 @@ struct DecArgs {
 
 // i8_decoder_block/kernel_api.h:48-51
 constexpr int kAttnScaleShift = 2, kAttnOutShift = 8, kFfnSh1 = 8, kFfnSh2 = 7;
+// i8_transformer_encoder_block/kernel_api.h:45-48
+constexpr int kEncScaleShift = 4, kEncOutShift = 8, kEncSh1 = 8, kEncSh2 = 4;
 
-__global__ void __launch_bounds__(kThreads) decoder_block_i8_kernel(const DecArgs a) {
+// ENC false: i8_decoder_block (causal, plain shifts, table activation).
+// ENC true: i8_transformer_encoder_block (reference.c:18-78): every key,
+// X read as u8 on the query side and as int8 on the key / value side, HMX
+// 12-bit fields after each product, ReLU + shift between the FFN layers,
+// and the second residual added after the shift without saturating first.
+template <bool ENC>
+__global__ void __launch_bounds__(kThreads) block_i8_kernel(const DecArgs a) {
     extern __shared__ __align__(16) uint8_t sm[];
     const int S = a.S, D = a.D, F = a.Dff;
     const DecSmem L(S, D, F);
@@ -267,21 +275,26 @@ __global__ void __launch_bounds__(kThreads) decoder_block_i8_kernel(const DecArg
         W2t[idx] = k < F ? a.W2[k * D + j] : (int8_t)0;
     }
     __syncthreads();
-    // causal scores: key j <= query i
+    // scores: causal (key j <= query i) for the decoder, every key for the encoder
     for (int idx = threadIdx.x; idx < S * Sp; idx += blockDim.x) {
         const int i = idx / Sp, j = idx % Sp;
         int v = 0;
-        if (j <= i) {
+        if (ENC ? j < S : j <= i) {
             const uint32_t *xi = reinterpret_cast<const uint32_t *>(Xs + i * Dp);
             const uint32_t *xj = reinterpret_cast<const uint32_t *>(Xs + j * Dp);
             int raw = 0;
-            for (int w = 0; w < Dp / 4; w++) raw = dot_uu(xi[w], xj[w], raw);
-            v = clamp_i8(raw >> kAttnScaleShift);
+            if constexpr (ENC) {
+                for (int w = 0; w < Dp / 4; w++) raw = dot_us(xi[w], xj[w], raw);
+                v = clamp_i8(sx12(hmx_field(raw)) >> kEncScaleShift);
+            } else {
+                for (int w = 0; w < Dp / 4; w++) raw = dot_uu(xi[w], xj[w], raw);
+                v = clamp_i8(raw >> kAttnScaleShift);
+            }
         }
         sc[idx] = (int8_t)v;
     }
     __syncthreads();
-    lut_softmax_rows(sc, pr, S, Sp, 1, a.exp_lut);
+    lut_softmax_rows(sc, pr, S, Sp, ENC ? 0 : 1, a.exp_lut);
     __syncthreads();
     // attention output and residual: h = clamp_u8(X + clamp_i8(P X >> 8))
     for (int idx = threadIdx.x; idx < S * Dp; idx += blockDim.x) {
@@ -291,8 +304,15 @@ __global__ void __launch_bounds__(kThreads) decoder_block_i8_kernel(const DecArg
             const uint32_t *pp = reinterpret_cast<const uint32_t *>(pr + i * Sp);
             const uint32_t *xx = reinterpret_cast<const uint32_t *>(Xt + d * Sp);
             int av = 0;
-            for (int w = 0; w < Sp / 4; w++) av = dot_uu(pp[w], xx[w], av);
-            h = (uint8_t)clamp_u8((int)Xs[i * Dp + d] + clamp_i8(av >> kAttnOutShift));
+            int at;
+            if constexpr (ENC) {
+                for (int w = 0; w < Sp / 4; w++) av = dot_us(pp[w], xx[w], av);
+                at = clamp_i8(sx12(hmx_field(av)) >> kEncOutShift);
+            } else {
+                for (int w = 0; w < Sp / 4; w++) av = dot_uu(pp[w], xx[w], av);
+                at = clamp_i8(av >> kAttnOutShift);
+            }
+            h = (uint8_t)clamp_u8((int)Xs[i * Dp + d] + at);
         }
         hs[idx] = h;
     }
@@ -306,8 +326,13 @@ __global__ void __launch_bounds__(kThreads) decoder_block_i8_kernel(const DecArg
             const uint32_t *ww = reinterpret_cast<const uint32_t *>(W1t + j * Dp);
             int acc = 0;
             for (int w = 0; w < Dp / 4; w++) acc = dot_us(hh[w], ww[w], acc);
-            const int p1 = (acc >> kFfnSh1) + a.b1[j];
-            v = __ldg(a.act_lut + clamp_i8(p1) + 128);
+            if constexpr (ENC) {
+                const int p1 = sx12(hmx_field(acc)) + a.b1[j];
+                v = (int8_t)(p1 > 0 ? min(p1 >> kEncSh1, 127) : 0);
+            } else {
+                const int p1 = (acc >> kFfnSh1) + a.b1[j];
+                v = __ldg(a.act_lut + clamp_i8(p1) + 128);
+            }
         }
         Ha[idx] = v;
     }
@@ -319,7 +344,10 @@ __global__ void __launch_bounds__(kThreads) decoder_block_i8_kernel(const DecArg
         const uint32_t *ww = reinterpret_cast<const uint32_t *>(W2t + j * Fp);
         int acc = 0;
         for (int w = 0; w < Fp / 4; w++) acc = dot_ss(hh[w], ww[w], acc);
-        const int fv = clamp_i8((acc >> kFfnSh2) + a.b2[j]);
+        // (the encoder's hidden values are in [0, 127]: signed and unsigned
+        // bytes agree)
+        const int fv = ENC ? (sx12(hmx_field(acc)) + a.b2[j]) >> kEncSh2
+                           : clamp_i8((acc >> kFfnSh2) + a.b2[j]);
         a.out[idx] = (int8_t)clamp_i8((int)hs[i * Dp + j] + fv);
     }
 }
@@ -423,7 +451,29 @@ HX_EXPORT int hexcuda_decoder_block_i8(int dev, const uint8_t *X, const int8_t *
     DecArgs a{X, W1, W2, act_lut, b1, b2, exp_lut, out, S, D, Dff};
     static bool done[64] = {};
     launch_begin(d);
-    if (int rc = set_smem(decoder_block_i8_kernel, d->ordinal, done)) return rc;
-    decoder_block_i8_kernel<<<1, kThreads, L.total, d->stream>>>(a);
+    if (int rc = set_smem(block_i8_kernel<false>, d->ordinal, done)) return rc;
+    block_i8_kernel<false><<<1, kThreads, L.total, d->stream>>>(a);
     return launch_end(d, "decoder_block_i8");
+}
+
+HX_EXPORT int hexcuda_encoder_block_i8(int dev, const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                                       const int8_t *W2, const int32_t *b2, const uint8_t *exp_lut,
+                                       int8_t *out, int S, int D, int Dff) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (S < 0 || D < 0 || Dff < 0)
+        return fail(HEXCUDA_ERR_ARG, "encoder_block_i8: S %d D %d Dff %d", S, D, Dff);
+    if (S == 0 || D == 0) return HEXCUDA_OK;
+    if (!X || !W1 || !b1 || !W2 || !b2 || !exp_lut || !out)
+        return fail(HEXCUDA_ERR_ARG, "encoder_block_i8: null pointer");
+    const DecSmem L(S, D, Dff);
+    if (L.total > kMaxSmem)
+        return fail(HEXCUDA_ERR_ARG, "encoder_block_i8: S=%d D=%d Dff=%d need %d B of shared memory",
+                    S, D, Dff, L.total);
+    DecArgs a{X, W1, W2, nullptr, b1, b2, exp_lut, out, S, D, Dff};
+    static bool done[64] = {};
+    launch_begin(d);
+    if (int rc = set_smem(block_i8_kernel<true>, d->ordinal, done)) return rc;
+    block_i8_kernel<true><<<1, kThreads, L.total, d->stream>>>(a);
+    return launch_end(d, "encoder_block_i8");
 }

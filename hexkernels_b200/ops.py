@@ -427,6 +427,46 @@ def rope_pair_f16(x, cos_t, sin_t) -> np.ndarray:
     return out
 
 
+def ffn_hmx_i8(X, W1, b1, W2, b2, sh1: int = 8, sh2: int = 3) -> np.ndarray:
+    """HMX-convention two-layer FFN (ReLU + shift between, shift + saturate
+    after); X u8 [M, D], W1 [D, Dff], W2 [Dff, D]."""
+    X, W1, W2 = _c(X, np.uint8), _c(W1, np.int8), _c(W2, np.int8)
+    b1, b2 = _c(b1, np.int32), _c(b2, np.int32)
+    (M, D), (D2, F), (F2, D3) = X.shape, W1.shape, W2.shape
+    assert D == D2 == D3 and F == F2 and b1.size == F and b2.size == D
+    out = np.empty((M, D), np.int8)
+    check(load().hexcuda_host_ffn_hmx_i8(_p(X), _p(W1), _p(b1), _p(W2), _p(b2), _p(out), M, D, F,
+                                         sh1, sh2))
+    return out
+
+
+def ffn_swiglu_hmx_i8(X, Wg, Wu, Wd, bd, silu_lut, sg: int = 2, su: int = 2, sh: int = 10,
+                      zp: int = 8, so: int = 3) -> np.ndarray:
+    """HMX-convention SwiGLU FFN (gate / up projections, SiLU-table gate x up
+    with a zero point, down projection + bias + shift + saturate)."""
+    X, Wg, Wu, Wd = _c(X, np.uint8), _c(Wg, np.int8), _c(Wu, np.int8), _c(Wd, np.int8)
+    bd, silu_lut = _c(bd, np.int32), _c(silu_lut, np.uint8)
+    (M, D), (D2, F) = X.shape, Wg.shape
+    assert D == D2 and Wu.shape == Wg.shape and Wd.shape == (F, D) and bd.size == D
+    out = np.empty((M, D), np.int8)
+    check(load().hexcuda_host_ffn_swiglu_hmx_i8(_p(X), _p(Wg), _p(Wu), _p(Wd), _p(bd), _p(silu_lut),
+                                                _p(out), M, D, F, sg, su, sh, zp, so))
+    return out
+
+
+def encoder_block_i8(X, W1, b1, W2, b2, exp_lut) -> np.ndarray:
+    """int8 encoder block: HMX-field self-attention of X with itself over
+    every key, residual, HMX-field FFN, residual."""
+    X, W1, W2 = _c(X, np.uint8), _c(W1, np.int8), _c(W2, np.int8)
+    b1, b2, exp_lut = _c(b1, np.int32), _c(b2, np.int32), _c(exp_lut, np.uint8)
+    S, D = X.shape
+    F = W1.shape[1]
+    out = np.empty((S, D), np.int8)
+    check(load().hexcuda_host_encoder_block_i8(_p(X), _p(W1), _p(b1), _p(W2), _p(b2), _p(exp_lut),
+                                               _p(out), S, D, F))
+    return out
+
+
 def decoder_block_i8(X, W1, b1, act_lut, W2, b2, exp_lut) -> np.ndarray:
     X, W1, W2 = _c(X, np.uint8), _c(W1, np.int8), _c(W2, np.int8)
     b1, b2 = _c(b1, np.int32), _c(b2, np.int32)

@@ -445,6 +445,15 @@ int hexcuda_rope_pair_f16(int dev, const uint16_t *x, const uint16_t *cos_t, con
  * then out int8 = sat_i8(h + sat_i8((act_lut[clamp_i8((h.W1 >> 8) + b1) + 128]
  * .W2 >> 7) + b2)); W1 [D][Dff], W2 [Dff][D] int8.
  * kernels/expert/i8_decoder_block/kernel_api.h:53-58. */
+/* int8 encoder block (kernels/expert/i8_transformer_encoder_block/
+ * reference.c:18-78): self-attention of X [S][D] with itself over every key
+ * (query side u8, key / value side the same bytes as int8), scores
+ * clamp_i8(sx12 field >> 4), exp-table softmax, h = clamp_u8(X +
+ * clamp_i8(sx12 field of P X >> 8)), FFN with H = relu(sx12 field + b1) >> 8
+ * (<= 127), out = sat_i8(h + ((sx12 field of H W2 + b2) >> 4)).  One CTA. */
+int hexcuda_encoder_block_i8(int dev, const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                             const int8_t *W2, const int32_t *b2, const uint8_t *exp_lut,
+                             int8_t *out, int S, int D, int Dff);
 int hexcuda_decoder_block_i8(int dev, const uint8_t *X, const int8_t *W1, const int32_t *b1,
                              const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
                              const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff);
@@ -484,6 +493,23 @@ int hexcuda_ffn_relu_i8(int dev, const int8_t *A, const int8_t *W1, const int32_
 int hexcuda_ffn_lut_i8(int dev, const int8_t *A, const int8_t *W1, const int32_t *b1,
                        const int8_t *act_lut, const int8_t *W2, const int32_t *b2, int8_t *out,
                        int M, int K, int V, int D, int32_t mult, int shift, int8_t zp);
+/* HMX-convention two-layer FFN: X u8 [M,D], W1 [D,Dff], W2 [Dff,D] int8
+ * row-major; r = sx12 field of each product;
+ * H = (r1 + b1 > 0) ? min((r1 + b1) >> sh1, 127) : 0 (kept on the device),
+ * out = sat_i8((r2 + b2) >> sh2).  kernels/expert/i8_ffn_block/
+ * reference.c:8-27 (sh1 8, sh2 3). */
+int hexcuda_ffn_hmx_i8(int dev, const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                       const int8_t *W2, const int32_t *b2, int8_t *out, int M, int D, int Dff,
+                       int sh1, int sh2);
+/* HMX-convention SwiGLU FFN: g = clamp_i8(sx12 field of X Wg >> sg), u the
+ * same with Wu and su, Hu = u8(clamp((silu_lut[g + 128] (as int8) u) >> sh,
+ * -zp, zp - 1) + zp), out = sat_i8((sx12 field of Hu Wd + bd) >> so).
+ * kernels/expert/i8_ffn_swiglu_block/reference.c:10-34 (sg 2, su 2, sh 10,
+ * zp 8, so 3). */
+int hexcuda_ffn_swiglu_hmx_i8(int dev, const uint8_t *X, const int8_t *Wg, const int8_t *Wu,
+                              const int8_t *Wd, const int32_t *bd, const uint8_t *silu_lut,
+                              int8_t *out, int M, int D, int Dff, int sg, int su, int sh, int zp,
+                              int so);
 /* HMX-convention GEMM with s8 A [M,K] and u8 B [K,N] (the weights-by-
  * activations form of the 1x1 convolutions, i8_conv2d_1x1_hmx/kernel_api.h:17,
  * i8_pointwise_conv_hmx/kernel_api.h:16); store kinds as hexcuda_gemm_hmx_ex
@@ -661,6 +687,15 @@ int hexcuda_host_kv_cache_update_i8(int8_t *k_cache, int8_t *v_cache, const int8
                                     int head_dim);
 int hexcuda_host_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
                                uint16_t *out, int64_t n_pairs);
+int hexcuda_host_ffn_hmx_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1, const int8_t *W2,
+                            const int32_t *b2, int8_t *out, int M, int D, int Dff, int sh1, int sh2);
+int hexcuda_host_ffn_swiglu_hmx_i8(const uint8_t *X, const int8_t *Wg, const int8_t *Wu,
+                                   const int8_t *Wd, const int32_t *bd, const uint8_t *silu_lut,
+                                   int8_t *out, int M, int D, int Dff, int sg, int su, int sh,
+                                   int zp, int so);
+int hexcuda_host_encoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                                  const int8_t *W2, const int32_t *b2, const uint8_t *exp_lut,
+                                  int8_t *out, int S, int D, int Dff);
 int hexcuda_host_decoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
                                   const int8_t *act_lut, const int8_t *W2, const int32_t *b2,
                                   const uint8_t *exp_lut, int8_t *out, int S, int D, int Dff);

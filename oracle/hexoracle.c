@@ -1292,3 +1292,96 @@ void oracle_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t, const uint16
         out[2 * p + 1] = f2h(xr * s + xi * c);
     }
 }
+
+/* i8_ffn_block/reference.c:8-27 (FFN_SH1 / FFN_SH2 as sh1 / sh2) */
+void oracle_ffn_hmx_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1, const int8_t *W2,
+                       const int32_t *b2, int8_t *out, int M, int D, int Dff, int sh1, int sh2) {
+    int8_t *H = (int8_t *)malloc((size_t)M * (Dff > 0 ? Dff : 1));
+    for (int i = 0; i < M; i++)
+        for (int j = 0; j < Dff; j++) {
+            int acc = 0;
+            for (int k = 0; k < D; k++) acc += (int)X[(size_t)i * D + k] * (int)W1[(size_t)k * Dff + j];
+            const int p1 = sx12(hmx_field_i(acc)) + b1[j];
+            int h = p1 > 0 ? (p1 >> sh1) : 0;
+            H[(size_t)i * Dff + j] = (int8_t)(h > 127 ? 127 : h);
+        }
+    for (int i = 0; i < M; i++)
+        for (int j = 0; j < D; j++) {
+            int acc = 0;
+            for (int k = 0; k < Dff; k++) acc += (int)H[(size_t)i * Dff + k] * (int)W2[(size_t)k * D + j];
+            out[(size_t)i * D + j] = (int8_t)clamp_i8i((sx12(hmx_field_i(acc)) + b2[j]) >> sh2);
+        }
+    free(H);
+}
+
+/* i8_ffn_swiglu_block/reference.c:10-34 with kernel_api.h's sw_scale,
+ * sw_gate and sw_hu (SW_SG, SW_SU, SW_SH, SW_ZP, SW_SO as sg, su, sh, zp, so) */
+void oracle_ffn_swiglu_hmx_i8(const uint8_t *X, const int8_t *Wg, const int8_t *Wu,
+                              const int8_t *Wd, const int32_t *bd, const uint8_t *silu_lut,
+                              int8_t *out, int M, int D, int Dff, int sg, int su, int sh, int zp,
+                              int so) {
+    uint8_t *Hu = (uint8_t *)malloc((size_t)M * (Dff > 0 ? Dff : 1));
+    for (int i = 0; i < M; i++)
+        for (int j = 0; j < Dff; j++) {
+            int gacc = 0, uacc = 0;
+            for (int k = 0; k < D; k++) {
+                gacc += (int)X[(size_t)i * D + k] * (int)Wg[(size_t)k * Dff + j];
+                uacc += (int)X[(size_t)i * D + k] * (int)Wu[(size_t)k * Dff + j];
+            }
+            const int gq = clamp_i8i(sx12(hmx_field_i(gacc)) >> sg);
+            const int uq = clamp_i8i(sx12(hmx_field_i(uacc)) >> su);
+            const int silu_g = (signed char)silu_lut[gq + 128];
+            int h = (silu_g * uq) >> sh;
+            if (h > zp - 1) h = zp - 1;
+            if (h < -zp) h = -zp;
+            Hu[(size_t)i * Dff + j] = (uint8_t)(h + zp);
+        }
+    for (int i = 0; i < M; i++)
+        for (int m = 0; m < D; m++) {
+            int acc = 0;
+            for (int j = 0; j < Dff; j++) acc += (int)Hu[(size_t)i * Dff + j] * (int)Wd[(size_t)j * D + m];
+            out[(size_t)i * D + m] = (int8_t)clamp_i8i((sx12(hmx_field_i(acc)) + bd[m]) >> so);
+        }
+    free(Hu);
+}
+
+/* i8_transformer_encoder_block/reference.c:18-78 (ATTN_SCALE_SHIFT 4,
+ * ATTN_OUT_SHIFT 8, FFN_SH1 8, FFN_SH2 4) */
+void oracle_encoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                             const int8_t *W2, const int32_t *b2, const uint8_t *exp_lut,
+                             int8_t *out, int S, int D, int Dff) {
+    int8_t *sc = (int8_t *)malloc((size_t)S * S);
+    uint8_t *pr = (uint8_t *)malloc((size_t)S * S);
+    uint8_t *h = (uint8_t *)malloc((size_t)S * D);
+    uint8_t *Hb = (uint8_t *)malloc((size_t)S * (Dff > 0 ? Dff : 1));
+    for (int i = 0; i < S; i++)
+        for (int j = 0; j < S; j++) {
+            int acc = 0;
+            for (int d = 0; d < D; d++) acc += (int)X[(size_t)i * D + d] * (int)(int8_t)X[(size_t)j * D + d];
+            sc[(size_t)i * S + j] = (int8_t)clamp_i8i(sx12(hmx_field_i(acc)) >> 4);
+        }
+    for (int i = 0; i < S; i++) lut_softmax_row(sc + (size_t)i * S, pr + (size_t)i * S, S, S, exp_lut);
+    for (int i = 0; i < S; i++)
+        for (int d = 0; d < D; d++) {
+            int acc = 0;
+            for (int j = 0; j < S; j++) acc += (int)pr[(size_t)i * S + j] * (int)(int8_t)X[(size_t)j * D + d];
+            const int a = clamp_i8i(sx12(hmx_field_i(acc)) >> 8);
+            h[(size_t)i * D + d] = (uint8_t)clamp_u8i((int)X[(size_t)i * D + d] + a);
+        }
+    for (int i = 0; i < S; i++)
+        for (int j = 0; j < Dff; j++) {
+            int acc = 0;
+            for (int k = 0; k < D; k++) acc += (int)h[(size_t)i * D + k] * (int)W1[(size_t)k * Dff + j];
+            const int p1 = sx12(hmx_field_i(acc)) + b1[j];
+            const int hh = p1 > 0 ? (p1 >> 8) : 0;
+            Hb[(size_t)i * Dff + j] = (uint8_t)(hh > 127 ? 127 : hh);
+        }
+    for (int i = 0; i < S; i++)
+        for (int j = 0; j < D; j++) {
+            int acc = 0;
+            for (int k = 0; k < Dff; k++) acc += (int)Hb[(size_t)i * Dff + k] * (int)W2[(size_t)k * D + j];
+            const int fv = (sx12(hmx_field_i(acc)) + b2[j]) >> 4;
+            out[(size_t)i * D + j] = (int8_t)clamp_i8i((int)h[(size_t)i * D + j] + fv);
+        }
+    free(sc); free(pr); free(h); free(Hb);
+}

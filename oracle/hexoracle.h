@@ -357,6 +357,19 @@ void oracle_kv_cache_update_i8(int8_t *k_cache, int8_t *v_cache, const int8_t *k
 void oracle_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
                           uint16_t *out, int64_t n_pairs);
 
+/* kernels/expert/i8_ffn_block/reference.c: HMX-field FFN, ReLU + shift. */
+void oracle_ffn_hmx_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1, const int8_t *W2,
+                       const int32_t *b2, int8_t *out, int M, int D, int Dff, int sh1, int sh2);
+/* kernels/expert/i8_ffn_swiglu_block/reference.c: HMX-field SwiGLU FFN. */
+void oracle_ffn_swiglu_hmx_i8(const uint8_t *X, const int8_t *Wg, const int8_t *Wu,
+                              const int8_t *Wd, const int32_t *bd, const uint8_t *silu_lut,
+                              int8_t *out, int M, int D, int Dff, int sg, int su, int sh, int zp,
+                              int so);
+/* kernels/expert/i8_transformer_encoder_block/reference.c. */
+void oracle_encoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1,
+                             const int8_t *W2, const int32_t *b2, const uint8_t *exp_lut,
+                             int8_t *out, int S, int D, int Dff);
+
 #ifdef __cplusplus
 }
 #endif

@@ -630,3 +630,36 @@ def rope_pair_f16(x, cos_t, sin_t):
     out = np.zeros_like(x)
     lib().oracle_rope_pair_f16(_p(x), _p(cos_t), _p(sin_t), _p(out), C.c_int64(x.size // 2))
     return out
+
+
+def ffn_hmx_i8(X, W1, b1, W2, b2, sh1=8, sh2=3):
+    X = np.ascontiguousarray(X, np.uint8)
+    W1, W2 = np.ascontiguousarray(W1, np.int8), np.ascontiguousarray(W2, np.int8)
+    b1, b2 = np.ascontiguousarray(b1, np.int32), np.ascontiguousarray(b2, np.int32)
+    (M, D), F = X.shape, W1.shape[1]
+    out = np.zeros((M, D), np.int8)
+    lib().oracle_ffn_hmx_i8(_p(X), _p(W1), _p(b1), _p(W2), _p(b2), _p(out), M, D, F, sh1, sh2)
+    return out
+
+
+def ffn_swiglu_hmx_i8(X, Wg, Wu, Wd, bd, silu_lut, sg=2, su=2, sh=10, zp=8, so=3):
+    X = np.ascontiguousarray(X, np.uint8)
+    Wg, Wu, Wd = (np.ascontiguousarray(w, np.int8) for w in (Wg, Wu, Wd))
+    bd, silu_lut = np.ascontiguousarray(bd, np.int32), np.ascontiguousarray(silu_lut, np.uint8)
+    (M, D), F = X.shape, Wg.shape[1]
+    out = np.zeros((M, D), np.int8)
+    lib().oracle_ffn_swiglu_hmx_i8(_p(X), _p(Wg), _p(Wu), _p(Wd), _p(bd), _p(silu_lut), _p(out), M,
+                                   D, F, sg, su, sh, zp, so)
+    return out
+
+
+def encoder_block_i8(X, W1, b1, W2, b2, exp_lut):
+    X = np.ascontiguousarray(X, np.uint8)
+    W1, W2 = np.ascontiguousarray(W1, np.int8), np.ascontiguousarray(W2, np.int8)
+    b1, b2 = np.ascontiguousarray(b1, np.int32), np.ascontiguousarray(b2, np.int32)
+    exp_lut = np.ascontiguousarray(exp_lut, np.uint8)
+    S, D = X.shape
+    F = W1.shape[1]
+    out = np.zeros((S, D), np.int8)
+    lib().oracle_encoder_block_i8(_p(X), _p(W1), _p(b1), _p(W2), _p(b2), _p(exp_lut), _p(out), S, D, F)
+    return out

@@ -1012,6 +1012,57 @@ def gen_cache_rope(ref):
     save("cache_rope", **a)
 
 
+def gen_blocks(ref):
+    # i8_ffn_block, i8_ffn_swiglu_block and i8_transformer_encoder_block
+    # through their reference.c: the harnesses' shapes and value ranges (X in
+    # 0..3, small weights, +-4000 bias columns that kill / saturate) and
+    # full-range operands at ragged shapes, where the 12-bit fields wrap;
+    # within each reference's fixed scratch arrays (S * Dff <= 65536; the
+    # encoder's S, D <= 64, Dff <= 128).
+    rng = np.random.default_rng(149)
+    a = {}
+
+    def ints(lo, hi, *sh, dt=np.int8):
+        return rng.integers(lo, hi, sh).astype(dt)
+
+    for t, (S, D, F, small) in enumerate(((64, 128, 128, True), (37, 72, 100, False))):
+        X = ints(0, 4 if small else 256, S, D, dt=np.uint8)
+        W1, W2 = (ints(-3, 4, D, F), ints(-2, 3, F, D)) if small else (ints(-128, 128, D, F), ints(-128, 128, F, D))
+        b1, b2 = ints(-64, 65, F, dt=np.int32), ints(-256, 257, D, dt=np.int32)
+        b1[:2], b2[:2] = (-4000, 4000), (-4000, 4000)
+        o = np.zeros((S, D), np.int8)
+        ref.ref_i8_ffn_block(ptr(X), ptr(W1), ptr(b1), ptr(W2), ptr(b2), ptr(o), S, D, F)
+        a.update({f"ffn_X{t}": X, f"ffn_W1{t}": W1, f"ffn_b1{t}": b1, f"ffn_W2{t}": W2, f"ffn_b2{t}": b2,
+                  f"ffn_out{t}": o})
+    for t, (S, D, F, small) in enumerate(((64, 64, 128, True), (50, 40, 96, False))):
+        X = ints(0, 4 if small else 256, S, D, dt=np.uint8)
+        if small:
+            Wg, Wu, Wd = ints(-3, 4, D, F), ints(-3, 4, D, F), ints(-1, 2, F, D)
+        else:
+            Wg, Wu, Wd = ints(-128, 128, D, F), ints(-128, 128, D, F), ints(-128, 128, F, D)
+        bd = ints(-256, 257, D, dt=np.int32)
+        lut = ints(0, 256, 256, dt=np.uint8)
+        o = np.zeros((S, D), np.int8)
+        ref.ref_i8_ffn_swiglu_block(ptr(X), ptr(Wg), ptr(Wu), ptr(Wd), ptr(bd), ptr(lut), ptr(o), S, D, F)
+        a.update({f"sw_X{t}": X, f"sw_Wg{t}": Wg, f"sw_Wu{t}": Wu, f"sw_Wd{t}": Wd, f"sw_bd{t}": bd,
+                  f"sw_lut{t}": lut, f"sw_out{t}": o})
+    for t, (S, D, F, small) in enumerate(((64, 64, 128, True), (40, 48, 100, False))):
+        X = ints(0, 4 if small else 256, S, D, dt=np.uint8)
+        W1, W2 = (ints(-3, 4, D, F), ints(-2, 3, F, D)) if small else (ints(-128, 128, D, F), ints(-128, 128, F, D))
+        b1, b2 = ints(-64, 65, F, dt=np.int32), ints(-256, 257, D, dt=np.int32)
+        b1[:2], b2[:2] = (-4000, 4000), (-4000, 4000)
+        lut = np.round(255 * np.exp((np.arange(256) - 255) / 16.0)).astype(np.uint8)
+        if not small:
+            lut = ints(0, 256, 256, dt=np.uint8)
+            lut[255] = 255
+        o = np.zeros((S, D), np.int8)
+        ref.ref_i8_transformer_encoder_block(ptr(X), ptr(W1), ptr(b1), ptr(W2), ptr(b2), ptr(lut), ptr(o),
+                                             S, D, F)
+        a.update({f"enc_X{t}": X, f"enc_W1{t}": W1, f"enc_b1{t}": b1, f"enc_W2{t}": W2, f"enc_b2{t}": b2,
+                  f"enc_lut{t}": lut, f"enc_out{t}": o})
+    save("blocks", **a)
+
+
 def gen_int_rows(ref):
     # The attention-tile callers, the integer layernorms with an inverse-
     # variance table, the exp-table softmax tiles, the int16 requant, the
@@ -1174,6 +1225,7 @@ def main():
     gen_dot_callers(ref)
     gen_sparse_attn(ref)
     gen_cache_rope(ref)
+    gen_blocks(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

@@ -227,3 +227,63 @@ def test_rope_pair_random(hx, oracle):
     c, s = np.cos(th).astype(np.float16), np.sin(th).astype(np.float16)
     np.testing.assert_array_equal(hx.rope_pair_f16(x, c, s).view(np.uint16),
                                   oracle.rope_pair_f16(x, c, s).view(np.uint16))
+
+
+from test_oracle_golden import block_calls  # noqa: E402
+
+
+def test_blocks_golden_and_shims(hx):
+    g = golden("blocks")
+    for k, (got, exp) in enumerate(block_calls(hx, g)):
+        np.testing.assert_array_equal(got, exp, err_msg=str(k))
+    for t in range(2):
+        c = lambda k: g[f"ffn_{k}{t}"]
+        S, D = c("X").shape
+        out = np.zeros((S, D), np.int8)
+        shim("i8_ffn_block")(p(c("X")), p(c("W1")), p(c("b1")), p(c("W2")), p(c("b2")), p(out), S, D,
+                             c("W1").shape[1])
+        np.testing.assert_array_equal(out, c("out"))
+        c = lambda k: g[f"sw_{k}{t}"]
+        S, D = c("X").shape
+        out = np.zeros((S, D), np.int8)
+        shim("i8_ffn_swiglu_block")(p(c("X")), p(c("Wg")), p(c("Wu")), p(c("Wd")), p(c("bd")), p(c("lut")),
+                                    p(out), S, D, c("Wg").shape[1])
+        np.testing.assert_array_equal(out, c("out"))
+        c = lambda k: g[f"enc_{k}{t}"]
+        S, D = c("X").shape
+        out = np.zeros((S, D), np.int8)
+        shim("i8_transformer_encoder_block")(p(c("X")), p(c("W1")), p(c("b1")), p(c("W2")), p(c("b2")),
+                                             p(c("lut")), p(out), S, D, c("W1").shape[1])
+        np.testing.assert_array_equal(out, c("out"))
+
+
+@pytest.mark.parametrize("M,D,F", [(1, 1, 1), (1000, 256, 512), (333, 130, 70)])
+def test_hmx_ffns_random(hx, oracle, M, D, F):
+    rng = np.random.default_rng(M + D + F)
+    X = rng.integers(0, 256, (M, D), dtype=np.uint8)
+    s8 = lambda *sh: rng.integers(-128, 128, sh, dtype=np.int8)
+    W1, W2, Wu = s8(D, F), s8(F, D), s8(D, F)
+    b1 = rng.integers(-3000, 3000, F).astype(np.int32)
+    b2 = rng.integers(-3000, 3000, D).astype(np.int32)
+    np.testing.assert_array_equal(hx.ffn_hmx_i8(X, W1, b1, W2, b2), oracle.ffn_hmx_i8(X, W1, b1, W2, b2))
+    np.testing.assert_array_equal(hx.ffn_hmx_i8(X, W1, b1, W2, b2, 5, 7),
+                                  oracle.ffn_hmx_i8(X, W1, b1, W2, b2, 5, 7))
+    lut = rng.integers(0, 256, 256, dtype=np.uint8)
+    args = (X, W1, Wu, W2, b2, lut)
+    np.testing.assert_array_equal(hx.ffn_swiglu_hmx_i8(*args), oracle.ffn_swiglu_hmx_i8(*args))
+    np.testing.assert_array_equal(hx.ffn_swiglu_hmx_i8(*args, 3, 1, 6, 100, 2),
+                                  oracle.ffn_swiglu_hmx_i8(*args, 3, 1, 6, 100, 2))
+
+
+@pytest.mark.parametrize("S,D,F", [(1, 1, 1), (64, 64, 128), (31, 45, 77), (96, 128, 192)])
+def test_encoder_block_random(hx, oracle, S, D, F):
+    rng = np.random.default_rng(S * D + F)
+    X = rng.integers(0, 256, (S, D), dtype=np.uint8)
+    W1 = rng.integers(-128, 128, (D, F), dtype=np.int8)
+    W2 = rng.integers(-128, 128, (F, D), dtype=np.int8)
+    b1 = rng.integers(-3000, 3000, F).astype(np.int32)
+    b2 = rng.integers(-3000, 3000, D).astype(np.int32)
+    lut = rng.integers(0, 256, 256, dtype=np.uint8)
+    lut[255] = 255
+    np.testing.assert_array_equal(hx.encoder_block_i8(X, W1, b1, W2, b2, lut),
+                                  oracle.encoder_block_i8(X, W1, b1, W2, b2, lut))

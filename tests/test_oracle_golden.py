@@ -444,6 +444,27 @@ def test_cache_rope_golden(oracle):
         np.testing.assert_array_equal(got.view(np.uint8), exp.view(np.uint8))
 
 
+def block_calls(impl, g):
+    """(result, expected) of i8_ffn_block, i8_ffn_swiglu_block and
+    i8_transformer_encoder_block's golden cases through `impl` (the oracle
+    or the GPU ops module)."""
+    for t in range(2):
+        c = lambda k: g[f"ffn_{k}{t}"]
+        yield impl.ffn_hmx_i8(c("X"), c("W1"), c("b1"), c("W2"), c("b2"), 8, 3), c("out")
+    for t in range(2):
+        c = lambda k: g[f"sw_{k}{t}"]
+        yield (impl.ffn_swiglu_hmx_i8(c("X"), c("Wg"), c("Wu"), c("Wd"), c("bd"), c("lut"), 2, 2, 10, 8, 3),
+               c("out"))
+    for t in range(2):
+        c = lambda k: g[f"enc_{k}{t}"]
+        yield impl.encoder_block_i8(c("X"), c("W1"), c("b1"), c("W2"), c("b2"), c("lut")), c("out")
+
+
+def test_blocks_golden(oracle):
+    for k, (got, exp) in enumerate(block_calls(oracle, golden("blocks"))):
+        np.testing.assert_array_equal(got, exp, err_msg=str(k))
+
+
 NORM_MULT = np.array([3, 5, 7, 9, 11, 13, 15, 17, 3, 5, 7, 9, 11, 13, 15, 17], np.int32)
 NORM_SHIFT = np.array([2, 3, 4, 5, 3, 4, 5, 6, 2, 3, 4, 5, 3, 4, 5, 6], np.int32)
 

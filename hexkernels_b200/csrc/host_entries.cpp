@@ -1278,3 +1278,26 @@ HX_EXPORT int hexcuda_host_encoder_block_i8(const uint8_t *X, const int8_t *W1, 
         return hexcuda_encoder_block_i8(p.slot, dX, dW1, db1, dW2, db2, dl, dout, S, D, Dff);
     });
 }
+
+HX_EXPORT int hexcuda_host_affine_ew(const void *in, int elem_in, void *out, int elem_out, int64_t n,
+                                     int32_t zp_in, int32_t mult, int64_t add, int shift, int round,
+                                     int wrap32, int zp_out, int32_t lo, int32_t hi) {
+    if (elem_in < HEXCUDA_ELEM_I8 || elem_in > HEXCUDA_ELEM_I32 || elem_out < HEXCUDA_ELEM_I8 ||
+        elem_out > HEXCUDA_ELEM_I32 || n < 0)
+        return fail(HEXCUDA_ERR_ARG, "host_affine_ew: elem %d -> %d n %lld", elem_in, elem_out,
+                    (long long)n);
+    if (n == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_affine_ew", {in, out})) return rc;
+    auto esz = [](int e) { return e == HEXCUDA_ELEM_I32 ? (size_t)4 : (e == HEXCUDA_ELEM_I16 ? (size_t)2 : (size_t)1); };
+    const size_t ei = esz(elem_in), eo = esz(elem_out);
+    return run_sharded(n, out, eo, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const uint8_t *din = stage_in(p.d, kSlotIn0, reinterpret_cast<const uint8_t *>(in) + p.r0 * ei,
+                                      (size_t)nr * ei);
+        void *dout = scratch(p.d, kSlotOut, (size_t)nr * eo);
+        if (!din || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_affine_ew(p.slot, din, elem_in, dout, elem_out, nr, zp_in, mult, add, shift,
+                                 round, wrap32, zp_out, lo, hi);
+    });
+}

@@ -403,6 +403,25 @@ def attn_lut_i8_window(Q, K, V, exp_lut, window: int, scale_mult: int, scale_shi
     return out
 
 
+ROUND = {"half_away": 0, "floor": 1}
+
+
+def affine_ew(x, out_dtype, zp_in: int = 0, mult: int = 1, add: int = 0, shift: int = 0,
+              round: str = "half_away", wrap32: bool = False, zp_out: int = 0, lo=None,
+              hi=None) -> np.ndarray:
+    """clamp(round((x - zp_in) * mult + add, shift) + zp_out, lo, hi) in the
+    integer type out_dtype (lo / hi default to its range)."""
+    x = np.ascontiguousarray(x)
+    info = np.iinfo(out_dtype)
+    lo = info.min if lo is None else lo
+    hi = info.max if hi is None else hi
+    out = np.empty(x.shape, out_dtype)
+    check(load().hexcuda_host_affine_ew(_p(x), ELEM[x.dtype], _p(out), ELEM[np.dtype(out_dtype)],
+                                        x.size, zp_in, mult, add, shift, ROUND[round], int(wrap32),
+                                        zp_out, lo, hi))
+    return out
+
+
 def kv_cache_update_i8(k_cache, v_cache, k_new, v_new, pos: int):
     """Writes k_new / v_new [heads, head_dim] into row pos of the caches
     [heads, cache_len, head_dim] (in place on the host arrays, which are

@@ -427,6 +427,19 @@ int hexcuda_attn_lut_i8(int dev, int mode, const void *Q, const int8_t *K, const
 int hexcuda_attn_lut_i8_window(int dev, const int8_t *Q, const int8_t *K, const int8_t *V,
                                const uint8_t *exp_lut, int8_t *out, int heads, int S, int D, int window,
                                int32_t scale_mult, int scale_shift, int32_t av_mult, int av_shift);
+/* Integer affine elementwise requant: out[i] = clamp(round((x[i] - zp_in) *
+ * mult + add, shift) + zp_out, lo, hi), x and out of the HEXCUDA_ELEM_*
+ * types; round HEXCUDA_ROUND_HALF_AWAY (sign-magnitude, half away from zero)
+ * or HEXCUDA_ROUND_FLOOR (arithmetic right shift); wrap32 != 0 takes the
+ * product and sum modulo 2^32 first (the references' int32 arithmetic;
+ * shift 0..31), else exactly in int64 (shift 0..62).  kernels/expert/
+ * rescale_i16_i8_dma, dequant_i8_i16_dma, hmx_requant_store_i8,
+ * i8_add_bias_sat_dma, i8_element_affine_dma (reference.c of each). */
+#define HEXCUDA_ROUND_HALF_AWAY 0
+#define HEXCUDA_ROUND_FLOOR 1
+int hexcuda_affine_ew(int dev, const void *in, int elem_in, void *out, int elem_out, int64_t n,
+                      int32_t zp_in, int32_t mult, int64_t add, int shift, int round, int wrap32,
+                      int zp_out, int32_t lo, int32_t hi);
 /* KV-cache write: for h < heads, k_cache[h][pos][:] = k_new[h][:] and
  * v_cache[h][pos][:] = v_new[h][:], caches [heads][cache_len][head_dim] int8
  * (kernels/expert/kv_cache_update/reference.c:14-25); 0 <= pos < cache_len. */
@@ -687,6 +700,9 @@ int hexcuda_host_kv_cache_update_i8(int8_t *k_cache, int8_t *v_cache, const int8
                                     int head_dim);
 int hexcuda_host_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
                                uint16_t *out, int64_t n_pairs);
+int hexcuda_host_affine_ew(const void *in, int elem_in, void *out, int elem_out, int64_t n,
+                           int32_t zp_in, int32_t mult, int64_t add, int shift, int round,
+                           int wrap32, int zp_out, int32_t lo, int32_t hi);
 int hexcuda_host_ffn_hmx_i8(const uint8_t *X, const int8_t *W1, const int32_t *b1, const int8_t *W2,
                             const int32_t *b2, int8_t *out, int M, int D, int Dff, int sh1, int sh2);
 int hexcuda_host_ffn_swiglu_hmx_i8(const uint8_t *X, const int8_t *Wg, const int8_t *Wu,

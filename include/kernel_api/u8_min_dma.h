@@ -1,0 +1,7 @@
+/* candidate_kernel of kernels/expert/u8_min_dma/kernel_api.h:7
+ * minimum of a uint8 array (255 when empty). */
+#ifndef HEXCUDA_KAPI_U8_MIN_DMA_H
+#define HEXCUDA_KAPI_U8_MIN_DMA_H
+#include <stdint.h>
+void candidate_kernel(const uint8_t *a, int n, uint8_t *out);
+#endif

@@ -1385,3 +1385,34 @@ void oracle_encoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *
         }
     free(sc); free(pr); free(h); free(Hb);
 }
+
+/* rescale_i16_i8_dma/reference.c:5-15, dequant_i8_i16_dma/reference.c:5-12,
+ * hmx_requant_store_i8/reference.c:3-8, i8_add_bias_sat_dma/reference.c:3-9,
+ * i8_element_affine_dma/reference.c:5-16: one affine form with their
+ * int32 (wrap32) or int64 arithmetic and their rounding */
+void oracle_affine_ew(const void *in, int elem_in, void *out, int elem_out, int64_t n, int32_t zp_in,
+                      int32_t mult, int64_t add, int shift, int round, int wrap32, int zp_out,
+                      int32_t lo, int32_t hi) {
+    for (int64_t i = 0; i < n; i++) {
+        int64_t x;
+        switch (elem_in) {
+        case 0: x = ((const int8_t *)in)[i]; break;
+        case 1: x = ((const uint8_t *)in)[i]; break;
+        case 2: x = ((const int16_t *)in)[i]; break;
+        default: x = ((const int32_t *)in)[i]; break;
+        }
+        int64_t v = wrap32 ? (int64_t)(int32_t)(((uint32_t)(int32_t)x - (uint32_t)zp_in) * (uint32_t)mult +
+                                                (uint32_t)add)
+                           : (x - zp_in) * (int64_t)mult + add;
+        int64_t r = round ? (v >> shift) : rq_round(v, shift);
+        r += zp_out;
+        if (r < lo) r = lo;
+        if (r > hi) r = hi;
+        switch (elem_out) {
+        case 0: ((int8_t *)out)[i] = (int8_t)r; break;
+        case 1: ((uint8_t *)out)[i] = (uint8_t)r; break;
+        case 2: ((int16_t *)out)[i] = (int16_t)r; break;
+        default: ((int32_t *)out)[i] = (int32_t)r; break;
+        }
+    }
+}

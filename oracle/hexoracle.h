@@ -370,6 +370,13 @@ void oracle_encoder_block_i8(const uint8_t *X, const int8_t *W1, const int32_t *
                              const int8_t *W2, const int32_t *b2, const uint8_t *exp_lut,
                              int8_t *out, int S, int D, int Dff);
 
+/* clamp(round((x - zp_in) * mult + add, shift) + zp_out, lo, hi); round 0
+ * half away from zero, 1 floor; wrap32: int32 product and sum (the
+ * rescale / dequant / HMX-store / bias-add / affine bundles' reference.c). */
+void oracle_affine_ew(const void *in, int elem_in, void *out, int elem_out, int64_t n, int32_t zp_in,
+                      int32_t mult, int64_t add, int shift, int round, int wrap32, int zp_out,
+                      int32_t lo, int32_t hi);
+
 #ifdef __cplusplus
 }
 #endif

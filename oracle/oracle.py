@@ -663,3 +663,17 @@ def encoder_block_i8(X, W1, b1, W2, b2, exp_lut):
     out = np.zeros((S, D), np.int8)
     lib().oracle_encoder_block_i8(_p(X), _p(W1), _p(b1), _p(W2), _p(b2), _p(exp_lut), _p(out), S, D, F)
     return out
+
+
+def affine_ew(x, out_dtype, zp_in=0, mult=1, add=0, shift=0, round="half_away", wrap32=False,
+              zp_out=0, lo=None, hi=None):
+    x = np.ascontiguousarray(x)
+    info = np.iinfo(out_dtype)
+    lo = info.min if lo is None else lo
+    hi = info.max if hi is None else hi
+    out = np.zeros(x.shape, out_dtype)
+    lib().oracle_affine_ew(_p(x), ELEM[x.dtype], _p(out), ELEM[np.dtype(out_dtype)],
+                           C.c_int64(x.size), C.c_int32(zp_in), C.c_int32(mult), C.c_int64(add),
+                           shift, {"half_away": 0, "floor": 1}[round], int(wrap32), zp_out,
+                           C.c_int32(lo), C.c_int32(hi))
+    return out

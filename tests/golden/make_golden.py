@@ -1063,6 +1063,47 @@ def gen_blocks(ref):
     save("blocks", **a)
 
 
+def gen_affine(ref):
+    # The integer affine requant bundles and the uint8 extremes through their
+    # reference.c: full-range inputs (int16, int8, int32 accumulators within
+    # the range where the reference's int32 products stay defined) at a
+    # length off every vector width, each bundle's runtime parameters swept.
+    rng = np.random.default_rng(151)
+    a = {}
+    n = 4099
+
+    def run(name, t, args, **arrs):
+        getattr(ref, "ref_" + name)(*args)
+        for k, v in arrs.items():
+            a[f"{name}__{k}{t}"] = v
+
+    x16 = rng.integers(-32768, 32768, n).astype(np.int16)
+    o = np.zeros(n, np.int8)
+    run("rescale_i16_i8_dma", 0, (ptr(x16), ptr(o), n), a=x16, out=o)
+    x8 = rng.integers(-128, 128, n).astype(np.int8)
+    a["x8"] = x8
+    for t, (zp, scale, shift) in enumerate(((0, 1, 0), (-7, 300, 3), (100, -77777, 11), (-128, 2**22, 31))):
+        o = np.zeros(n, np.int16)
+        run("dequant_i8_i16_dma", t, (ptr(x8), ptr(o), n, C.c_int8(zp), C.c_int32(scale), shift), out=o)
+    acc = rng.integers(-(2**26), 2**26, n).astype(np.int32)
+    acc[:4] = (0, -1, 7, -8)
+    o = np.zeros(n, np.int8)
+    run("hmx_requant_store_i8", 0, (ptr(acc), ptr(o), n), a=acc, out=o)
+    for t, bias in enumerate((0, 77, -200, 100000)):
+        o = np.zeros(n, np.int8)
+        run("i8_add_bias_sat_dma", t, (ptr(x8), ptr(o), n, C.c_int32(bias)), out=o)
+    for t, (scale, sh, s) in enumerate(((1, 0, 0), (3, 5, 2), (-1000, 333, 9), (2**31 - 1, -(2**31), 40))):
+        o = np.zeros(n, np.int8)
+        run("i8_element_affine_dma", t, (ptr(x8), ptr(o), n, C.c_int32(scale), C.c_int32(sh), s), out=o)
+    u8 = rng.integers(0, 256, n).astype(np.uint8)
+    a["u8"] = u8
+    for name in ("u8_max_dma", "u8_min_dma"):
+        for t, m in enumerate((n, 1, 0)):
+            o = np.zeros(1, np.uint8)
+            run(name, t, (ptr(u8), m, ptr(o)), out=o)
+    save("affine", **a)
+
+
 def gen_int_rows(ref):
     # The attention-tile callers, the integer layernorms with an inverse-
     # variance table, the exp-table softmax tiles, the int16 requant, the
@@ -1226,6 +1267,7 @@ def main():
     gen_sparse_attn(ref)
     gen_cache_rope(ref)
     gen_blocks(ref)
+    gen_affine(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

@@ -465,6 +465,36 @@ def test_blocks_golden(oracle):
         np.testing.assert_array_equal(got, exp, err_msg=str(k))
 
 
+def affine_calls(impl, g):
+    """(result, expected) of the affine requant bundles and the uint8
+    extremes (golden affine) through `impl` (the oracle or the GPU ops)."""
+    c = lambda k: g[k]
+    x8 = c("x8")
+    yield (impl.affine_ew(c("rescale_i16_i8_dma__a0"), np.int8, mult=3, shift=4, wrap32=True),
+           c("rescale_i16_i8_dma__out0"))
+    for t, (zp, scale, shift) in enumerate(((0, 1, 0), (-7, 300, 3), (100, -77777, 11), (-128, 2**22, 31))):
+        yield (impl.affine_ew(x8, np.int16, zp_in=zp, mult=scale, shift=shift, round="floor", wrap32=True),
+               c(f"dequant_i8_i16_dma__out{t}"))
+    yield (impl.affine_ew(c("hmx_requant_store_i8__a0"), np.int8, mult=17, add=8, shift=4, round="floor",
+                          wrap32=True), c("hmx_requant_store_i8__out0"))
+    for t, bias in enumerate((0, 77, -200, 100000)):
+        yield (impl.affine_ew(x8, np.int8, add=bias, round="floor", wrap32=True),
+               c(f"i8_add_bias_sat_dma__out{t}"))
+    for t, (scale, sh, s) in enumerate(((1, 0, 0), (3, 5, 2), (-1000, 333, 9), (2**31 - 1, -(2**31), 40))):
+        yield impl.affine_ew(x8, np.int8, mult=scale, add=sh, shift=s), c(f"i8_element_affine_dma__out{t}")
+    u8 = c("u8")
+    for t, m in enumerate((u8.size, 1)):
+        yield np.array([impl.reduce_int(u8[:m], "max")], np.uint8), c(f"u8_max_dma__out{t}")
+        yield np.array([impl.reduce_int(u8[:m], "min")], np.uint8), c(f"u8_min_dma__out{t}")
+
+
+def test_affine_golden(oracle):
+    for k, (got, exp) in enumerate(affine_calls(oracle, golden("affine"))):
+        np.testing.assert_array_equal(got, exp, err_msg=str(k))
+    g = golden("affine")
+    assert g["u8_max_dma__out2"][0] == 0 and g["u8_min_dma__out2"][0] == 255
+
+
 NORM_MULT = np.array([3, 5, 7, 9, 11, 13, 15, 17, 3, 5, 7, 9, 11, 13, 15, 17], np.int32)
 NORM_SHIFT = np.array([2, 3, 4, 5, 3, 4, 5, 6, 2, 3, 4, 5, 3, 4, 5, 6], np.int32)
 

@@ -1,0 +1,7 @@
+/* candidate_kernel of kernels/expert/i8_add_stream_dma/kernel_api.h:7
+ * int8 saturating add. */
+#ifndef HEXCUDA_KAPI_I8_ADD_STREAM_DMA_H
+#define HEXCUDA_KAPI_I8_ADD_STREAM_DMA_H
+#include <stdint.h>
+void candidate_kernel(const int8_t *a, const int8_t *b, int8_t *out, int n);
+#endif

@@ -1101,6 +1101,31 @@ def gen_affine(ref):
         for t, m in enumerate((n, 1, 0)):
             o = np.zeros(1, np.uint8)
             run(name, t, (ptr(u8), m, ptr(o)), out=o)
+    for name in ("i8_relu_dma", "i8_relu_stream_dma"):
+        o = np.zeros(n, np.int8)
+        run(name, 0, (ptr(x8), ptr(o), n), out=o)
+    for t, scale in enumerate((10, 0, 21, 22, 100, -3)):
+        o = np.zeros(n, np.int8)
+        run("i8_relu6_dma", t, (ptr(x8), ptr(o), n, C.c_int8(scale)), out=o)
+    for name in ("u8_clamp_range_dma", "dma_double_buffer_relu_u8"):
+        o = np.zeros(n, np.uint8)
+        run(name, 0, (ptr(u8), ptr(o), n), out=o)
+    for t, m in enumerate((n, 1, 77)):
+        for name, src, dt in (("i8_global_avgpool_dma", x8, np.int8), ("u8_global_avgpool_dma", u8, np.uint8),
+                              ("i8_global_maxpool_dma", x8, np.int8)):
+            o = np.zeros(1, dt)
+            run(name, t, (ptr(src), m, ptr(o)), out=o)
+    o = np.zeros(1, np.int8)
+    run("i8_global_maxpool_dma", 3, (ptr(x8), 0, ptr(o)), out=o)
+    o = np.zeros(n, np.uint8)
+    run("u8_threshold_dma", 0, (ptr(u8), ptr(o), n), out=o)
+    o = np.zeros(n, np.int8)
+    run("i8_sign_dma", 0, (ptr(x8), ptr(o), n), out=o)
+    y8 = rng.integers(-128, 128, n).astype(np.int8)
+    a["y8"] = y8
+    for name in ("i8_add_dma", "i8_add_stream_dma", "i8_vadd_dma"):
+        o = np.zeros(n, np.int8)
+        run(name, 0, (ptr(x8), ptr(y8), ptr(o), n), out=o)
     save("affine", **a)
 
 

@@ -94,3 +94,51 @@ def test_affine_rejects_bad_arguments(hx):
     for kw in (dict(shift=32, wrap32=True), dict(shift=63), dict(round="floor", lo=5, hi=4)):
         with pytest.raises(RuntimeError):
             hx.affine_ew(x, np.int8, **kw)
+
+
+from test_oracle_golden import RELU6_SCALES, clamp_calls  # noqa: E402
+
+
+def test_clamp_and_pool_golden_and_shims(hx):
+    g = golden("affine")
+    for k, (got, exp) in enumerate(clamp_calls(hx, g)):
+        np.testing.assert_array_equal(got, exp, err_msg=str(k))
+    x8, u8, n = g["x8"], g["u8"], g["x8"].size
+    for name in ("i8_relu_dma", "i8_relu_stream_dma"):
+        out = np.zeros(n, np.int8)
+        shim(name)(p(x8), p(out), n)
+        np.testing.assert_array_equal(out, g[name + "__out0"])
+    fn = shim("i8_relu6_dma")
+    fn.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int8]
+    for t, scale in enumerate(RELU6_SCALES):
+        out = np.zeros(n, np.int8)
+        fn(p(x8), p(out), n, scale)
+        np.testing.assert_array_equal(out, g[f"i8_relu6_dma__out{t}"], err_msg=str(scale))
+    for name in ("u8_clamp_range_dma", "dma_double_buffer_relu_u8"):
+        out = np.zeros(n, np.uint8)
+        shim(name)(p(u8), p(out), n)
+        np.testing.assert_array_equal(out, g[name + "__out0"])
+    for t, m in enumerate((n, 1, 77)):
+        for name, src, dt in (("i8_global_avgpool_dma", x8, np.int8), ("u8_global_avgpool_dma", u8, np.uint8),
+                              ("i8_global_maxpool_dma", x8, np.int8)):
+            o = np.zeros(1, dt)
+            shim(name)(p(src), m, p(o))
+            np.testing.assert_array_equal(o, g[f"{name}__out{t}"], err_msg=f"{name} {m}")
+    o = np.zeros(1, np.int8)
+    shim("i8_global_maxpool_dma")(p(x8), 0, p(o))
+    np.testing.assert_array_equal(o, g["i8_global_maxpool_dma__out3"])
+
+
+def test_ew_shims(hx):
+    g = golden("affine")
+    x8, y8, u8, n = g["x8"], g["y8"], g["u8"], g["x8"].size
+    out = np.zeros(n, np.uint8)
+    shim("u8_threshold_dma")(p(u8), p(out), n)
+    np.testing.assert_array_equal(out, g["u8_threshold_dma__out0"])
+    out = np.zeros(n, np.int8)
+    shim("i8_sign_dma")(p(x8), p(out), n)
+    np.testing.assert_array_equal(out, g["i8_sign_dma__out0"])
+    for name in ("i8_add_dma", "i8_add_stream_dma", "i8_vadd_dma"):
+        out = np.zeros(n, np.int8)
+        shim(name)(p(x8), p(y8), p(out), n)
+        np.testing.assert_array_equal(out, g[name + "__out0"], err_msg=name)

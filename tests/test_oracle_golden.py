@@ -488,7 +488,38 @@ def affine_calls(impl, g):
         yield np.array([impl.reduce_int(u8[:m], "min")], np.uint8), c(f"u8_min_dma__out{t}")
 
 
+RELU6_SCALES = (10, 0, 21, 22, 100, -3)
+
+
+def clamp_calls(impl, g):
+    """(result, expected) of the ReLU / clamp bundles and the global pools
+    (golden affine) through `impl`, with the shims' parameter mapping."""
+    x8, u8 = g["x8"], g["u8"]
+    for name in ("i8_relu_dma", "i8_relu_stream_dma"):
+        yield impl.affine_ew(x8, np.int8, round="floor", wrap32=True, lo=0, hi=127), g[name + "__out0"]
+    for t, scale in enumerate(RELU6_SCALES):
+        cap = int(np.int8(np.int32(6 * scale).astype(np.int8)))
+        kw = dict(lo=0, hi=cap) if cap >= 0 else dict(mult=-1000, add=cap, lo=cap, hi=0)
+        yield impl.affine_ew(x8, np.int8, round="floor", wrap32=True, **kw), g[f"i8_relu6_dma__out{t}"]
+    yield impl.affine_ew(u8, np.uint8, round="floor", wrap32=True, lo=64, hi=191), g["u8_clamp_range_dma__out0"]
+    yield (impl.affine_ew(u8, np.uint8, zp_in=128, round="floor", wrap32=True, lo=0, hi=255),
+           g["dma_double_buffer_relu_u8__out0"])
+    for t, m in enumerate((x8.size, 1, 77)):
+        yield np.array([impl.reduce_int(x8[:m], "mean")]).astype(np.int8), g[f"i8_global_avgpool_dma__out{t}"]
+        yield np.array([impl.reduce_int(u8[:m], "mean")]).astype(np.uint8), g[f"u8_global_avgpool_dma__out{t}"]
+        yield np.array([impl.reduce_int(x8[:m], "max")], np.int8), g[f"i8_global_maxpool_dma__out{t}"]
+    yield (impl.affine_ew(u8, np.uint8, zp_in=127, mult=255, round="floor", wrap32=True, lo=0, hi=255),
+           g["u8_threshold_dma__out0"])
+    yield impl.affine_ew(x8, np.int8, mult=1000, round="floor", wrap32=True, lo=-1, hi=1), g["i8_sign_dma__out0"]
+    y8 = g["y8"]
+    for name, (lo, hi) in (("i8_add_dma", (-128, 127)), ("i8_add_stream_dma", (-128, 127)),
+                           ("i8_vadd_dma", (-256, 255))):
+        yield impl.requant_ew(x8, y8, pre="add", lo1=lo, hi1=hi, lo2=lo, hi2=hi), g[name + "__out0"]
+
+
 def test_affine_golden(oracle):
+    for k, (got, exp) in enumerate(clamp_calls(oracle, golden("affine"))):
+        np.testing.assert_array_equal(got, exp, err_msg=f"clamp {k}")
     for k, (got, exp) in enumerate(affine_calls(oracle, golden("affine"))):
         np.testing.assert_array_equal(got, exp, err_msg=str(k))
     g = golden("affine")

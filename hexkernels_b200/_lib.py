@@ -70,6 +70,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_attn_lut_i8_window": (I, [I, P, P, P, P, P, I, I, I, I, I32, I, I32, I]),
     "hexcuda_kv_cache_update_i8": (I, [I, P, P, P, P, I, I, I, I]),
     "hexcuda_rope_pair_f16": (I, [I, P, P, P, P, I64]),
+    "hexcuda_gemm_i16": (I, [I, P, P, P, I, I, I]),
     "hexcuda_affine_ew": (I, [I, P, I, P, I, I64, I32, I32, I64, I, I, I, I, I32, I32]),
     "hexcuda_ffn_hmx_i8": (I, [I, P, P, P, P, P, P, I, I, I, I, I]),
     "hexcuda_ffn_swiglu_hmx_i8": (I, [I, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I]),
@@ -126,6 +127,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_attn_lut_i8_window": (I, [P, P, P, P, P, I, I, I, I, I32, I, I32, I]),
     "hexcuda_host_kv_cache_update_i8": (I, [P, P, P, P, I, I, I, I]),
     "hexcuda_host_rope_pair_f16": (I, [P, P, P, P, I64]),
+    "hexcuda_host_gemm_i16": (I, [P, P, P, I, I, I]),
     "hexcuda_host_affine_ew": (I, [P, I, P, I, I64, I32, I32, I64, I, I, I, I, I32, I32]),
     "hexcuda_host_ffn_hmx_i8": (I, [P, P, P, P, P, P, I, I, I, I, I]),
     "hexcuda_host_ffn_swiglu_hmx_i8": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, I]),

@@ -1531,6 +1531,113 @@ __global__ void __launch_bounds__(256) swiglu_gate_kernel(const int8_t *__restri
 }  // namespace
 }  // namespace hx
 
+// ---------------------------------------------------------------- int16 GEMM
+//
+// i16_gemm/reference.c:2-11: C = A B with int16 operands and an int32
+// accumulator (modulo 2^32).  Each operand is split into a signed high byte
+// and a signed low byte, x - 128 = 256 xh + xl' (xh = x >> 8, xl' =
+// (x & 255) - 128), so one kind::i8 GEMM of [Ah; Al'] (2M x K) by
+// [Bh | Bl'] (K x 2N) gives the four byte products, and
+//   sum a b = 65536 hh + 256 (hl + lh) + ll + 128 rowsum(A - 128)
+//             + 128 colsum(B - 128) + 16384 K            (all modulo 2^32).
+namespace hx {
+namespace {
+constexpr int kSlotI16A = 19, kSlotI16B = 20, kSlotI16T = 21, kSlotI16Sums = 22;
+
+__global__ void __launch_bounds__(256) i16_split_a_kernel(const int16_t *__restrict__ A,
+                                                          int8_t *__restrict__ As,
+                                                          int32_t *__restrict__ rs, int M, int K) {
+    __shared__ uint32_t part[8];
+    const int i = blockIdx.x;
+    uint32_t s = 0;
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const int x = A[(size_t)i * K + k];
+        As[(size_t)i * K + k] = (int8_t)(x >> 8);
+        As[(size_t)(M + i) * K + k] = (int8_t)((x & 255) - 128);
+        s += (uint32_t)(x - 128);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t t = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += part[w];
+        rs[i] = (int32_t)t;
+    }
+}
+
+// one thread per column j and chunk of 64 rows; column sums by atomic adds
+// (integer, so the order does not matter)
+__global__ void __launch_bounds__(256) i16_split_b_kernel(const int16_t *__restrict__ B,
+                                                          int8_t *__restrict__ Bs,
+                                                          int32_t *__restrict__ cs, int K, int N) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const int k0 = blockIdx.y * 64;
+    if (j >= N) return;
+    uint32_t s = 0;
+    for (int k = k0; k < min(k0 + 64, K); k++) {
+        const int x = B[(size_t)k * N + j];
+        Bs[(size_t)k * 2 * N + j] = (int8_t)(x >> 8);
+        Bs[(size_t)k * 2 * N + N + j] = (int8_t)((x & 255) - 128);
+        s += (uint32_t)(x - 128);
+    }
+    atomicAdd(reinterpret_cast<unsigned *>(cs) + j, s);
+}
+
+__global__ void __launch_bounds__(256) i16_combine_kernel(const int32_t *__restrict__ T,
+                                                          const int32_t *__restrict__ rs,
+                                                          const int32_t *__restrict__ cs,
+                                                          int32_t *__restrict__ C, int M, int N,
+                                                          uint32_t kterm) {
+    const int64_t n = (int64_t)M * N;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += stride) {
+        const int i = (int)(t / N), j = (int)(t % N);
+        const size_t r0 = (size_t)i * 2 * N, r1 = (size_t)(M + i) * 2 * N;
+        const uint32_t hh = (uint32_t)T[r0 + j], hl = (uint32_t)T[r0 + N + j];
+        const uint32_t lh = (uint32_t)T[r1 + j], ll = (uint32_t)T[r1 + N + j];
+        C[t] = (int32_t)((hh << 16) + ((hl + lh) << 8) + ll + 128u * (uint32_t)rs[i] +
+                         128u * (uint32_t)cs[j] + kterm);
+    }
+}
+}  // namespace
+}  // namespace hx
+
+HX_EXPORT int hexcuda_gemm_i16(int dev, const int16_t *A, const int16_t *B, int32_t *C, int M, int N,
+                               int K) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (M < 0 || N < 0 || K < 0 || (int64_t)M * 2 > INT32_MAX || (int64_t)N * 2 > INT32_MAX)
+        return fail(HEXCUDA_ERR_ARG, "gemm_i16: bad shape %dx%dx%d", M, N, K);
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if ((K > 0 && (!A || !B)) || !C) return fail(HEXCUDA_ERR_ARG, "gemm_i16: null pointer");
+    const size_t kk = (size_t)(K > 0 ? K : 1);
+    int8_t *As = reinterpret_cast<int8_t *>(scratch(d, kSlotI16A, 2 * (size_t)M * kk));
+    int8_t *Bs = reinterpret_cast<int8_t *>(scratch(d, kSlotI16B, 2 * (size_t)N * kk));
+    int32_t *T = reinterpret_cast<int32_t *>(scratch(d, kSlotI16T, 16 * (size_t)M * N));
+    int32_t *sums = reinterpret_cast<int32_t *>(scratch(d, kSlotI16Sums, 4 * ((size_t)M + N)));
+    if (!As || !Bs || !T || !sums) return HEXCUDA_ERR_OOM;
+    int32_t *rs = sums, *cs = sums + M;
+    launch_begin(d);
+    if (int rc = check(cudaMemsetAsync(sums, 0, 4 * ((size_t)M + N), d->stream), "memset i16 sums"))
+        return rc;
+    if (K > 0) {
+        i16_split_a_kernel<<<M, 256, 0, d->stream>>>(A, As, rs, M, K);
+        i16_split_b_kernel<<<dim3((unsigned)((N + 255) / 256), (unsigned)((K + 63) / 64)), 256, 0,
+                             d->stream>>>(B, Bs, cs, K, N);
+    }
+    if (int rc = launch_end(d, "gemm_i16 (split)")) return rc;
+    if (int rc = hexcuda_gemm_i8_acc(dev, As, 1, Bs, 0, nullptr, nullptr, HEXCUDA_HMX_RES_NONE, nullptr,
+                                     T, HEXCUDA_HMX_STORE_I32, HEXCUDA_HMX_ACT_NONE, 2 * M, 2 * N, K))
+        return rc;
+    launch_begin(d);
+    constexpr auto kern = i16_combine_kernel;
+    kern<<<resident_blocks<kern>(d, (int64_t)M * N), 256, 0, d->stream>>>(
+        T, rs, cs, C, M, N, 16384u * (uint32_t)K);
+    return launch_end(d, "gemm_i16 (combine)");
+}
+
 HX_EXPORT int hexcuda_ffn_hmx_i8(int dev, const uint8_t *X, const int8_t *W1, const int32_t *b1,
                                  const int8_t *W2, const int32_t *b2, int8_t *out, int M, int D,
                                  int Dff, int sh1, int sh2) {

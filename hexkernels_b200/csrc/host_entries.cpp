@@ -1301,3 +1301,19 @@ HX_EXPORT int hexcuda_host_affine_ew(const void *in, int elem_in, void *out, int
                                  round, wrap32, zp_out, lo, hi);
     });
 }
+
+HX_EXPORT int hexcuda_host_gemm_i16(const int16_t *A, const int16_t *B, int32_t *C, int M, int N,
+                                    int K) {
+    if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_i16: bad shape");
+    if (M == 0 || N == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_gemm_i16", {A, B, C})) return rc;
+    return run_sharded(M, C, (size_t)N * 4, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int16_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
+        const int16_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+        int32_t *dC = reinterpret_cast<int32_t *>(scratch(p.d, kSlotOut, (size_t)nr * N * 4));
+        if ((K && (!dA || !dB)) || !dC) return hexcuda_last_error();
+        p.dout = dC;
+        return hexcuda_gemm_i16(p.slot, dA, dB, dC, (int)nr, N, K);
+    });
+}

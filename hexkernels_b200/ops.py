@@ -446,6 +446,16 @@ def rope_pair_f16(x, cos_t, sin_t) -> np.ndarray:
     return out
 
 
+def gemm_i16(A, B) -> np.ndarray:
+    """int16 GEMM, int32 accumulator (modulo 2^32): A [M, K], B [K, N]."""
+    A, B = _c(A, np.int16), _c(B, np.int16)
+    (M, K), (K2, N) = A.shape, B.shape
+    assert K == K2
+    C = np.empty((M, N), np.int32)
+    check(load().hexcuda_host_gemm_i16(_p(A), _p(B), _p(C), M, N, K))
+    return C
+
+
 def ffn_hmx_i8(X, W1, b1, W2, b2, sh1: int = 8, sh2: int = 3) -> np.ndarray:
     """HMX-convention two-layer FFN (ReLU + shift between, shift + saturate
     after); X u8 [M, D], W1 [D, Dff], W2 [Dff, D]."""

@@ -506,6 +506,11 @@ int hexcuda_ffn_relu_i8(int dev, const int8_t *A, const int8_t *W1, const int32_
 int hexcuda_ffn_lut_i8(int dev, const int8_t *A, const int8_t *W1, const int32_t *b1,
                        const int8_t *act_lut, const int8_t *W2, const int32_t *b2, int8_t *out,
                        int M, int K, int V, int D, int32_t mult, int shift, int8_t zp);
+/* int16 GEMM: C [M,N] int32 = A [M,K] B [K,N] (int16 row-major), the
+ * accumulator modulo 2^32 (kernels/expert/i16_gemm/reference.c:2-11).  The
+ * operands are split into signed bytes and multiplied by one tcgen05
+ * kind::i8 GEMM of twice the rows and columns; 16 M N bytes of scratch. */
+int hexcuda_gemm_i16(int dev, const int16_t *A, const int16_t *B, int32_t *C, int M, int N, int K);
 /* HMX-convention two-layer FFN: X u8 [M,D], W1 [D,Dff], W2 [Dff,D] int8
  * row-major; r = sx12 field of each product;
  * H = (r1 + b1 > 0) ? min((r1 + b1) >> sh1, 127) : 0 (kept on the device),
@@ -700,6 +705,7 @@ int hexcuda_host_kv_cache_update_i8(int8_t *k_cache, int8_t *v_cache, const int8
                                     int head_dim);
 int hexcuda_host_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
                                uint16_t *out, int64_t n_pairs);
+int hexcuda_host_gemm_i16(const int16_t *A, const int16_t *B, int32_t *C, int M, int N, int K);
 int hexcuda_host_affine_ew(const void *in, int elem_in, void *out, int elem_out, int64_t n,
                            int32_t zp_in, int32_t mult, int64_t add, int shift, int round,
                            int wrap32, int zp_out, int32_t lo, int32_t hi);

@@ -1416,3 +1416,14 @@ void oracle_affine_ew(const void *in, int elem_in, void *out, int elem_out, int6
         }
     }
 }
+
+/* i16_gemm/reference.c:2-11 (int32 accumulator, modulo 2^32) */
+void oracle_gemm_i16(const int16_t *A, const int16_t *B, int32_t *C, int M, int N, int K) {
+    for (int i = 0; i < M; i++)
+        for (int j = 0; j < N; j++) {
+            uint32_t acc = 0;
+            for (int k = 0; k < K; k++)
+                acc += (uint32_t)((int32_t)A[(size_t)i * K + k] * (int32_t)B[(size_t)k * N + j]);
+            C[(size_t)i * N + j] = (int32_t)acc;
+        }
+}

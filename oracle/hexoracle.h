@@ -377,6 +377,9 @@ void oracle_affine_ew(const void *in, int elem_in, void *out, int elem_out, int6
                       int32_t mult, int64_t add, int shift, int round, int wrap32, int zp_out,
                       int32_t lo, int32_t hi);
 
+/* kernels/expert/i16_gemm/reference.c: int16 GEMM, int32 accumulator. */
+void oracle_gemm_i16(const int16_t *A, const int16_t *B, int32_t *C, int M, int N, int K);
+
 #ifdef __cplusplus
 }
 #endif

@@ -677,3 +677,11 @@ def affine_ew(x, out_dtype, zp_in=0, mult=1, add=0, shift=0, round="half_away", 
                            shift, {"half_away": 0, "floor": 1}[round], int(wrap32), zp_out,
                            C.c_int32(lo), C.c_int32(hi))
     return out
+
+
+def gemm_i16(A, B):
+    A, B = np.ascontiguousarray(A, np.int16), np.ascontiguousarray(B, np.int16)
+    (M, K), N = A.shape, B.shape[1]
+    C_ = np.zeros((M, N), np.int32)
+    lib().oracle_gemm_i16(_p(A), _p(B), _p(C_), M, N, K)
+    return C_

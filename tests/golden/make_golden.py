@@ -1121,6 +1121,11 @@ def gen_affine(ref):
     run("u8_threshold_dma", 0, (ptr(u8), ptr(o), n), out=o)
     o = np.zeros(n, np.int8)
     run("i8_sign_dma", 0, (ptr(x8), ptr(o), n), out=o)
+    for t, (M, N, K) in enumerate(((32, 32, 66), (70, 90, 130))):
+        A16 = rng.integers(-32768, 32768, (M, K)).astype(np.int16)
+        B16 = rng.integers(-32768, 32768, (K, N)).astype(np.int16)
+        o = np.zeros((M, N), np.int32)
+        run("i16_gemm", t, (ptr(A16), ptr(B16), ptr(o), M, N, K), A=A16, B=B16, out=o)
     y8 = rng.integers(-128, 128, n).astype(np.int8)
     a["y8"] = y8
     for name in ("i8_add_dma", "i8_add_stream_dma", "i8_vadd_dma"):

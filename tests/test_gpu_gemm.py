@@ -542,3 +542,28 @@ def test_gate_mul_requant_and_ffn_lut_random(hx, oracle):
     b2 = rng.integers(-50000, 50000, D).astype(np.int32)
     np.testing.assert_array_equal(hx.ffn_lut_i8(A, W1, b1, lut, W2, b2, 1 << 28, 36, 5),
                                   oracle.ffn_lut_i8(A, W1, b1, lut, W2, b2, 1 << 28, 36, 5))
+
+
+# ---------------------------------------------------------------- int16 GEMM
+
+def test_i16_gemm_golden_and_shim(hx):
+    import ctypes as C
+    g = golden("affine")
+    fn = _shim("i16_gemm")
+    for t in range(2):
+        A, B, exp = g[f"i16_gemm__A{t}"], g[f"i16_gemm__B{t}"], g[f"i16_gemm__out{t}"]
+        np.testing.assert_array_equal(hx.gemm_i16(A, B), exp)
+        out = np.zeros_like(exp)
+        p = lambda a: a.ctypes.data_as(C.c_void_p)
+        fn(p(A), p(B), p(out), A.shape[0], B.shape[1], A.shape[1])
+        np.testing.assert_array_equal(out, exp)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (129, 257, 130), (512, 384, 4099), (1000, 70, 33)])
+def test_i16_gemm_random(hx, oracle, M, N, K):
+    rng = np.random.default_rng(M + N + K)
+    A = rng.integers(-32768, 32768, (M, K)).astype(np.int16)
+    B = rng.integers(-32768, 32768, (K, N)).astype(np.int16)
+    np.testing.assert_array_equal(hx.gemm_i16(A, B), oracle.gemm_i16(A, B))
+    ext = np.full((M, K), -32768, np.int16), np.full((K, N), 32767, np.int16)
+    np.testing.assert_array_equal(hx.gemm_i16(*ext), oracle.gemm_i16(*ext))

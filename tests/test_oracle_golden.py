@@ -517,6 +517,13 @@ def clamp_calls(impl, g):
         yield impl.requant_ew(x8, y8, pre="add", lo1=lo, hi1=hi, lo2=lo, hi2=hi), g[name + "__out0"]
 
 
+def test_i16_gemm_golden(oracle):
+    g = golden("affine")
+    for t in range(2):
+        np.testing.assert_array_equal(oracle.gemm_i16(g[f"i16_gemm__A{t}"], g[f"i16_gemm__B{t}"]),
+                                      g[f"i16_gemm__out{t}"])
+
+
 def test_affine_golden(oracle):
     for k, (got, exp) in enumerate(clamp_calls(oracle, golden("affine"))):
         np.testing.assert_array_equal(got, exp, err_msg=f"clamp {k}")

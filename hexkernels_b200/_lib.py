@@ -71,6 +71,9 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_kv_cache_update_i8": (I, [I, P, P, P, P, I, I, I, I]),
     "hexcuda_rope_pair_f16": (I, [I, P, P, P, P, I64]),
     "hexcuda_gemm_i16": (I, [I, P, P, P, I, I, I]),
+    "hexcuda_mix_mlp_i8": (I, [I, P, P, P, P, P, P, P, I, I, I, I, I32, I, I32, I]),
+    "hexcuda_token_mix_i8": (I, [I, P, P, P, P, P, P, I, I, I, I32, I, I32, I]),
+    "hexcuda_rnn_cell_i8": (I, [I, P, P, P, P, P, P, I, I, I32, I, I8, P]),
     "hexcuda_affine_ew": (I, [I, P, I, P, I, I64, I32, I32, I64, I, I, I, I, I32, I32]),
     "hexcuda_ffn_hmx_i8": (I, [I, P, P, P, P, P, P, I, I, I, I, I]),
     "hexcuda_ffn_swiglu_hmx_i8": (I, [I, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I]),
@@ -128,6 +131,9 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_kv_cache_update_i8": (I, [P, P, P, P, I, I, I, I]),
     "hexcuda_host_rope_pair_f16": (I, [P, P, P, P, I64]),
     "hexcuda_host_gemm_i16": (I, [P, P, P, I, I, I]),
+    "hexcuda_host_mix_mlp_i8": (I, [P, P, P, P, P, P, P, I, I, I, I, I32, I, I32, I]),
+    "hexcuda_host_token_mix_i8": (I, [P, P, P, P, P, P, I, I, I, I32, I, I32, I]),
+    "hexcuda_host_rnn_cell_i8": (I, [P, P, P, P, P, P, I, I, I32, I, I8, P]),
     "hexcuda_host_affine_ew": (I, [P, I, P, I, I64, I32, I32, I64, I, I, I, I, I32, I32]),
     "hexcuda_host_ffn_hmx_i8": (I, [P, P, P, P, P, P, I, I, I, I, I]),
     "hexcuda_host_ffn_swiglu_hmx_i8": (I, [P, P, P, P, P, P, P, I, I, I, I, I, I, I, I]),

@@ -1638,6 +1638,116 @@ HX_EXPORT int hexcuda_gemm_i16(int dev, const int16_t *A, const int16_t *B, int3
     return launch_end(d, "gemm_i16 (combine)");
 }
 
+// ------------------------------------------------- mixer blocks and RNN cell
+namespace hx {
+namespace {
+constexpr int kSlotMixQ = 19, kSlotMixY = 20, kSlotMixT = 21, kSlotMixX = 22, kSlotMixXt = 23;
+
+// out [C][R] = in [R][C] (int8), 32 x 32 tiles through shared memory
+__global__ void __launch_bounds__(256) transpose_i8_kernel(const int8_t *__restrict__ in,
+                                                           int8_t *__restrict__ out, int R, int C) {
+    __shared__ int8_t t[32][33];
+    const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+    for (int k = threadIdx.x; k < 32 * 32; k += blockDim.x) {
+        const int r = k / 32, c = k % 32;
+        if (r0 + r < R && c0 + c < C) t[r][c] = in[(size_t)(r0 + r) * C + c0 + c];
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < 32 * 32; k += blockDim.x) {
+        const int c = k / 32, r = k % 32;
+        if (r0 + r < R && c0 + c < C) out[(size_t)(c0 + c) * R + r0 + r] = t[r][c];
+    }
+}
+
+int transpose_i8(Dev *d, const int8_t *in, int8_t *out, int R, int C) {
+    launch_begin(d);
+    transpose_i8_kernel<<<dim3((unsigned)((C + 31) / 32), (unsigned)((R + 31) / 32)), 256, 0,
+                          d->stream>>>(in, out, R, C);
+    return launch_end(d, "transpose_i8");
+}
+}  // namespace
+}  // namespace hx
+
+HX_EXPORT int hexcuda_mix_mlp_i8(int dev, const int8_t *X, const int8_t *W1, const int32_t *b1,
+                                 const int8_t *lut, const int8_t *W2, const int32_t *b2, int8_t *out,
+                                 int M, int K, int V, int D, int32_t mult1, int shift1,
+                                 int32_t mult2, int shift2) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (M < 0 || K < 0 || V < 0 || D < 0) return fail(HEXCUDA_ERR_ARG, "mix_mlp_i8: bad shape");
+    if (M == 0 || D == 0) return HEXCUDA_OK;
+    const size_t n = (size_t)M * (V > 0 ? V : 1);
+    int8_t *q = reinterpret_cast<int8_t *>(scratch(d, kSlotMixQ, n));
+    int8_t *y = reinterpret_cast<int8_t *>(scratch(d, kSlotMixY, n));
+    if (!q || !y) return HEXCUDA_ERR_OOM;
+    if (V > 0) {
+        if (int rc = hexcuda_gemm_i8_rq_ex(dev, X, W1, 1, b1, nullptr, q, M, V, K, mult1, shift1, 0, 0))
+            return rc;
+        if (lut) {
+            // y = lut[(uint8)(q + 128)]: q + 128 lies in [0, 255]
+            if (int rc = hexcuda_requant_ew(dev, q, 1, nullptr, 0, y, (int64_t)M * V, HEXCUDA_RQ_PRE_A, 0,
+                                            1, 0, 128, 0, 0, 255, 0, 255, lut))
+                return rc;
+        } else {
+            y = q;
+        }
+    }
+    return hexcuda_gemm_i8_rq_ex(dev, y, W2, 1, b2, nullptr, out, M, D, V, mult2, shift2, 0, 0);
+}
+
+HX_EXPORT int hexcuda_token_mix_i8(int dev, const int8_t *X, const int8_t *W, const int32_t *b,
+                                   const int8_t *W2, const int32_t *b2, int8_t *out, int T, int C,
+                                   int DM, int32_t mult1, int shift1, int32_t mult2, int shift2) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (T < 0 || C < 0 || DM < 0) return fail(HEXCUDA_ERR_ARG, "token_mix_i8: bad shape");
+    if (T == 0 || C == 0) return HEXCUDA_OK;
+    if (!X || !out) return fail(HEXCUDA_ERR_ARG, "token_mix_i8: null pointer");
+    int8_t *xt = reinterpret_cast<int8_t *>(scratch(d, kSlotMixXt, (size_t)T * C));
+    int8_t *ot = reinterpret_cast<int8_t *>(scratch(d, kSlotMixT, (size_t)T * C));
+    if (!xt || !ot) return HEXCUDA_ERR_OOM;
+    // mixing along the tokens is the channel MLP of X^T (channels as rows)
+    if (int rc = transpose_i8(d, X, xt, T, C)) return rc;
+    if (int rc = hexcuda_mix_mlp_i8(dev, xt, W, b, nullptr, W2, b2, ot, C, T, DM, T, mult1, shift1,
+                                    mult2, shift2))
+        return rc;
+    return transpose_i8(d, ot, out, C, T);
+}
+
+HX_EXPORT int hexcuda_rnn_cell_i8(int dev, const int8_t *Wx, const int8_t *Wh, const int32_t *b,
+                                  const int8_t *x, const int8_t *h_prev, int8_t *h_t, int H, int I,
+                                  int32_t mult, int shift, int8_t zp, const int8_t *tanh_lut) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (H < 0 || I < 0) return fail(HEXCUDA_ERR_ARG, "rnn_cell_i8: H %d I %d", H, I);
+    if (H == 0) return HEXCUDA_OK;
+    if (!Wh || !b || !h_prev || !h_t || !tanh_lut || (I > 0 && (!Wx || !x)))
+        return fail(HEXCUDA_ERR_ARG, "rnn_cell_i8: null pointer");
+    const int KK = I + H;
+    int8_t *W = reinterpret_cast<int8_t *>(scratch(d, kSlotMixT, (size_t)H * KK));
+    int8_t *xh = reinterpret_cast<int8_t *>(scratch(d, kSlotMixX, (size_t)KK));
+    int8_t *q = reinterpret_cast<int8_t *>(scratch(d, kSlotMixQ, (size_t)H));
+    if (!W || !xh || !q) return HEXCUDA_ERR_OOM;
+    // [Wx | Wh] (H x (I + H)) and [x, h_prev]: one matrix-vector product
+    launch_begin(d);
+    int rc = HEXCUDA_OK;
+    if (I > 0) {
+        rc = check(cudaMemcpy2DAsync(W, KK, Wx, I, I, H, cudaMemcpyDeviceToDevice, d->stream), "copy Wx");
+        if (!rc) rc = check(cudaMemcpyAsync(xh, x, I, cudaMemcpyDeviceToDevice, d->stream), "copy x");
+    }
+    if (!rc) rc = check(cudaMemcpy2DAsync(W + I, KK, Wh, H, H, H, cudaMemcpyDeviceToDevice, d->stream),
+                        "copy Wh");
+    if (!rc) rc = check(cudaMemcpyAsync(xh + I, h_prev, H, cudaMemcpyDeviceToDevice, d->stream),
+                        "copy h_prev");
+    if (rc) return rc;
+    if ((rc = launch_end(d, "rnn_cell_i8 (pack)", 0))) return rc;
+    if ((rc = hexcuda_gemm_i8_rq_ex(dev, xh, W, 1, b, nullptr, q, 1, H, KK, mult, shift, zp, 0)))
+        return rc;
+    // h_t = tanh_lut[(uint8) q]
+    return hexcuda_requant_ew(dev, q, 1, nullptr, 0, h_t, H, HEXCUDA_RQ_PRE_A, 0, 1, 0, 0, 0,
+                              -128, 127, -128, 127, tanh_lut);
+}
+
 HX_EXPORT int hexcuda_ffn_hmx_i8(int dev, const uint8_t *X, const int8_t *W1, const int32_t *b1,
                                  const int8_t *W2, const int32_t *b2, int8_t *out, int M, int D,
                                  int Dff, int sh1, int sh2) {

@@ -1317,3 +1317,69 @@ HX_EXPORT int hexcuda_host_gemm_i16(const int16_t *A, const int16_t *B, int32_t 
         return hexcuda_gemm_i16(p.slot, dA, dB, dC, (int)nr, N, K);
     });
 }
+
+HX_EXPORT int hexcuda_host_mix_mlp_i8(const int8_t *X, const int8_t *W1, const int32_t *b1,
+                                      const int8_t *lut, const int8_t *W2, const int32_t *b2,
+                                      int8_t *out, int M, int K, int V, int D, int32_t mult1,
+                                      int shift1, int32_t mult2, int shift2) {
+    if (M < 0 || K < 0 || V < 0 || D < 0) return fail(HEXCUDA_ERR_ARG, "host_mix_mlp_i8: bad shape");
+    if (M == 0 || D == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_mix_mlp_i8", {X, W1, b1, W2, b2, out})) return rc;
+    return run_sharded(M, out, (size_t)D, [&](Part &p) {
+        const int64_t nr = p.r1 - p.r0;
+        const int8_t *dX = stage_in(p.d, kSlotIn0, X + p.r0 * K, (size_t)(nr * K));
+        const int8_t *dW1 = stage_in(p.d, kSlotIn1, W1, (size_t)V * K);
+        const int32_t *db1 = stage_in(p.d, kSlotIn2, b1, (size_t)V);
+        const int8_t *dW2 = stage_in(p.d, kSlotIn3, W2, (size_t)D * V);
+        const int32_t *db2 = stage_in(p.d, kSlotIn4, b2, (size_t)D);
+        const int8_t *dl = lut ? stage_in(p.d, kSlotIn5, lut, 256) : nullptr;
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * D)));
+        if (!dX || !dW1 || !db1 || !dW2 || !db2 || (lut && !dl) || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_mix_mlp_i8(p.slot, dX, dW1, db1, dl, dW2, db2, dout, (int)nr, K, V, D, mult1,
+                                  shift1, mult2, shift2);
+    });
+}
+
+HX_EXPORT int hexcuda_host_token_mix_i8(const int8_t *X, const int8_t *W, const int32_t *b,
+                                        const int8_t *W2, const int32_t *b2, int8_t *out, int T,
+                                        int C, int DM, int32_t mult1, int shift1, int32_t mult2,
+                                        int shift2) {
+    if (T < 0 || C < 0 || DM < 0) return fail(HEXCUDA_ERR_ARG, "host_token_mix_i8: bad shape");
+    if (T == 0 || C == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_token_mix_i8", {X, W, b, W2, b2, out})) return rc;
+    return run_sharded(1, out, (size_t)T * C, [&](Part &p) {
+        const int8_t *dX = stage_in(p.d, kSlotIn0, X, (size_t)T * C);
+        const int8_t *dW = stage_in(p.d, kSlotIn1, W, (size_t)DM * T);
+        const int32_t *db = stage_in(p.d, kSlotIn2, b, (size_t)DM);
+        const int8_t *dW2 = stage_in(p.d, kSlotIn3, W2, (size_t)T * DM);
+        const int32_t *db2 = stage_in(p.d, kSlotIn4, b2, (size_t)T);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)T * C));
+        if (!dX || !dW || !db || !dW2 || !db2 || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_token_mix_i8(p.slot, dX, dW, db, dW2, db2, dout, T, C, DM, mult1, shift1, mult2,
+                                    shift2);
+    });
+}
+
+HX_EXPORT int hexcuda_host_rnn_cell_i8(const int8_t *Wx, const int8_t *Wh, const int32_t *b,
+                                       const int8_t *x, const int8_t *h_prev, int8_t *h_t, int H,
+                                       int I, int32_t mult, int shift, int8_t zp,
+                                       const int8_t *tanh_lut) {
+    if (H < 0 || I < 0) return fail(HEXCUDA_ERR_ARG, "host_rnn_cell_i8: H %d I %d", H, I);
+    if (H == 0) return HEXCUDA_OK;
+    if (int rc = null_check("host_rnn_cell_i8", {Wh, b, h_prev, h_t, tanh_lut})) return rc;
+    if (I > 0 && (!Wx || !x)) return fail(HEXCUDA_ERR_ARG, "host_rnn_cell_i8: null pointer");
+    return run_sharded(1, h_t, (size_t)H, [&](Part &p) {
+        const int8_t *dWx = I ? stage_in(p.d, kSlotIn0, Wx, (size_t)H * I) : nullptr;
+        const int8_t *dWh = stage_in(p.d, kSlotIn1, Wh, (size_t)H * H);
+        const int32_t *db = stage_in(p.d, kSlotIn2, b, (size_t)H);
+        const int8_t *dx = I ? stage_in(p.d, kSlotIn3, x, (size_t)I) : nullptr;
+        const int8_t *dh = stage_in(p.d, kSlotIn4, h_prev, (size_t)H);
+        const int8_t *dl = stage_in(p.d, kSlotIn5, tanh_lut, 256);
+        int8_t *dout = reinterpret_cast<int8_t *>(scratch(p.d, kSlotOut, (size_t)H));
+        if ((I && (!dWx || !dx)) || !dWh || !db || !dh || !dl || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_rnn_cell_i8(p.slot, dWx, dWh, db, dx, dh, dout, H, I, mult, shift, zp, dl);
+    });
+}

@@ -456,6 +456,43 @@ def gemm_i16(A, B) -> np.ndarray:
     return C
 
 
+def mix_mlp_i8(X, W1, b1, W2, b2, mult1: int, shift1: int, mult2: int, shift2: int,
+               lut=None) -> np.ndarray:
+    """Channel-mixing MLP: two requantised products with Bt weights (W1
+    [V, K], W2 [D, V]) and an optional int8 table between them."""
+    X, W1, W2 = _c(X, np.int8), _c(W1, np.int8), _c(W2, np.int8)
+    b1, b2 = _c(b1, np.int32), _c(b2, np.int32)
+    (M, K), (V, K2), (D, V2) = X.shape, W1.shape, W2.shape
+    assert K == K2 and V == V2
+    lp = _p(_c(lut, np.int8)) if lut is not None else None
+    out = np.empty((M, D), np.int8)
+    check(load().hexcuda_host_mix_mlp_i8(_p(X), _p(W1), _p(b1), lp, _p(W2), _p(b2), _p(out), M, K, V,
+                                         D, mult1, shift1, mult2, shift2))
+    return out
+
+
+def token_mix_i8(X, W, b, W2, b2, mult1: int, shift1: int, mult2: int, shift2: int) -> np.ndarray:
+    """Token-mixing MLP of X [T, C]: W [DM, T], W2 [T, DM]."""
+    X, W, W2 = _c(X, np.int8), _c(W, np.int8), _c(W2, np.int8)
+    b, b2 = _c(b, np.int32), _c(b2, np.int32)
+    (T, Cc), DM = X.shape, W.shape[0]
+    out = np.empty((T, Cc), np.int8)
+    check(load().hexcuda_host_token_mix_i8(_p(X), _p(W), _p(b), _p(W2), _p(b2), _p(out), T, Cc, DM,
+                                           mult1, shift1, mult2, shift2))
+    return out
+
+
+def rnn_cell_i8(Wx, Wh, b, x, h_prev, mult: int, shift: int, zp: int, tanh_lut) -> np.ndarray:
+    """One int8 RNN step: tanh table of the requantised b + Wx x + Wh h."""
+    Wx, Wh, x, h_prev = _c(Wx, np.int8), _c(Wh, np.int8), _c(x, np.int8), _c(h_prev, np.int8)
+    b, tanh_lut = _c(b, np.int32), _c(tanh_lut, np.int8)
+    H, I = Wx.shape
+    out = np.empty(H, np.int8)
+    check(load().hexcuda_host_rnn_cell_i8(_p(Wx), _p(Wh), _p(b), _p(x), _p(h_prev), _p(out), H, I,
+                                          mult, shift, zp, _p(tanh_lut)))
+    return out
+
+
 def ffn_hmx_i8(X, W1, b1, W2, b2, sh1: int = 8, sh2: int = 3) -> np.ndarray:
     """HMX-convention two-layer FFN (ReLU + shift between, shift + saturate
     after); X u8 [M, D], W1 [D, Dff], W2 [Dff, D]."""

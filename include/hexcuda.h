@@ -511,6 +511,27 @@ int hexcuda_ffn_lut_i8(int dev, const int8_t *A, const int8_t *W1, const int32_t
  * operands are split into signed bytes and multiplied by one tcgen05
  * kind::i8 GEMM of twice the rows and columns; 16 M N bytes of scratch. */
 int hexcuda_gemm_i16(int dev, const int16_t *A, const int16_t *B, int32_t *C, int M, int N, int K);
+/* Channel-mixing MLP: q = sat_i8(round_half_away((X W1^T + b1) mult1 >>
+ * shift1)), y = lut ? lut[q + 128] : q, out = sat_i8(round_half_away((y W2^T
+ * + b2) mult2 >> shift2)); X [M,K], W1 [V,K], W2 [D,V] int8 row-major.
+ * kernels/expert/i8_channel_mix_block/reference.c:17-40. */
+int hexcuda_mix_mlp_i8(int dev, const int8_t *X, const int8_t *W1, const int32_t *b1,
+                       const int8_t *lut, const int8_t *W2, const int32_t *b2, int8_t *out, int M,
+                       int K, int V, int D, int32_t mult1, int shift1, int32_t mult2, int shift2);
+/* Token-mixing MLP of X [T,C]: the same two requantised products along the
+ * token axis, W [DM,T], b [DM], W2 [T,DM], b2 [T] (computed as the channel
+ * MLP of X^T, transposed back).  kernels/expert/i8_token_mix_block/
+ * reference.c:17-41. */
+int hexcuda_token_mix_i8(int dev, const int8_t *X, const int8_t *W, const int32_t *b,
+                         const int8_t *W2, const int32_t *b2, int8_t *out, int T, int C, int DM,
+                         int32_t mult1, int shift1, int32_t mult2, int shift2);
+/* int8 RNN cell: h_t = tanh_lut[(uint8) sat_i8(round_half_away((b + Wx x +
+ * Wh h_prev) mult >> shift) + zp)], Wx [hidden,in_dim], Wh [hidden,hidden]; one
+ * matrix-vector product of [Wx | Wh] by [x, h_prev].
+ * kernels/expert/rnn_cell_i8/reference.c. */
+int hexcuda_rnn_cell_i8(int dev, const int8_t *Wx, const int8_t *Wh, const int32_t *b,
+                        const int8_t *x, const int8_t *h_prev, int8_t *h_t, int hidden, int in_dim,
+                        int32_t mult, int shift, int8_t zp, const int8_t *tanh_lut);
 /* HMX-convention two-layer FFN: X u8 [M,D], W1 [D,Dff], W2 [Dff,D] int8
  * row-major; r = sx12 field of each product;
  * H = (r1 + b1 > 0) ? min((r1 + b1) >> sh1, 127) : 0 (kept on the device),
@@ -706,6 +727,15 @@ int hexcuda_host_kv_cache_update_i8(int8_t *k_cache, int8_t *v_cache, const int8
 int hexcuda_host_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
                                uint16_t *out, int64_t n_pairs);
 int hexcuda_host_gemm_i16(const int16_t *A, const int16_t *B, int32_t *C, int M, int N, int K);
+int hexcuda_host_mix_mlp_i8(const int8_t *X, const int8_t *W1, const int32_t *b1, const int8_t *lut,
+                            const int8_t *W2, const int32_t *b2, int8_t *out, int M, int K, int V,
+                            int D, int32_t mult1, int shift1, int32_t mult2, int shift2);
+int hexcuda_host_token_mix_i8(const int8_t *X, const int8_t *W, const int32_t *b, const int8_t *W2,
+                              const int32_t *b2, int8_t *out, int T, int C, int DM, int32_t mult1,
+                              int shift1, int32_t mult2, int shift2);
+int hexcuda_host_rnn_cell_i8(const int8_t *Wx, const int8_t *Wh, const int32_t *b, const int8_t *x,
+                             const int8_t *h_prev, int8_t *h_t, int hidden, int in_dim, int32_t mult,
+                             int shift, int8_t zp, const int8_t *tanh_lut);
 int hexcuda_host_affine_ew(const void *in, int elem_in, void *out, int elem_out, int64_t n,
                            int32_t zp_in, int32_t mult, int64_t add, int shift, int round,
                            int wrap32, int zp_out, int32_t lo, int32_t hi);

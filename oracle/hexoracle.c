@@ -1427,3 +1427,63 @@ void oracle_gemm_i16(const int16_t *A, const int16_t *B, int32_t *C, int M, int 
             C[(size_t)i * N + j] = (int32_t)acc;
         }
 }
+
+static int8_t rq_biased_i8(int32_t acc, int32_t bias, int32_t mult, int shift, int zp) {
+    return sat_i8(rq_round(((int64_t)acc + bias) * (int64_t)mult, shift) + zp);
+}
+
+/* i8_channel_mix_block/reference.c:17-40 (TOKENS x CHANNELS as M x K,
+ * D_FF as V, CHANNELS out as D; lut NULL: no table) */
+void oracle_mix_mlp_i8(const int8_t *X, const int8_t *W1, const int32_t *b1, const int8_t *lut,
+                       const int8_t *W2, const int32_t *b2, int8_t *out, int M, int K, int V, int D,
+                       int32_t mult1, int shift1, int32_t mult2, int shift2) {
+    int8_t *y = (int8_t *)malloc((size_t)(V > 0 ? V : 1));
+    for (int t = 0; t < M; t++) {
+        for (int m = 0; m < V; m++) {
+            uint32_t acc = 0;
+            for (int c = 0; c < K; c++) acc += (uint32_t)((int32_t)W1[(size_t)m * K + c] * X[(size_t)t * K + c]);
+            const int8_t q = rq_biased_i8((int32_t)acc, b1[m], mult1, shift1, 0);
+            y[m] = lut ? lut[(uint8_t)((int)q + 128)] : q;
+        }
+        for (int c = 0; c < D; c++) {
+            uint32_t acc = 0;
+            for (int m = 0; m < V; m++) acc += (uint32_t)((int32_t)W2[(size_t)c * V + m] * y[m]);
+            out[(size_t)t * D + c] = rq_biased_i8((int32_t)acc, b2[c], mult2, shift2, 0);
+        }
+    }
+    free(y);
+}
+
+/* i8_token_mix_block/reference.c:17-41 */
+void oracle_token_mix_i8(const int8_t *X, const int8_t *W, const int32_t *b, const int8_t *W2,
+                         const int32_t *b2, int8_t *out, int T, int C, int DM, int32_t mult1,
+                         int shift1, int32_t mult2, int shift2) {
+    int8_t *y = (int8_t *)malloc((size_t)(DM > 0 ? DM : 1));
+    for (int c = 0; c < C; c++) {
+        for (int m = 0; m < DM; m++) {
+            uint32_t acc = 0;
+            for (int t = 0; t < T; t++) acc += (uint32_t)((int32_t)W[(size_t)m * T + t] * X[(size_t)t * C + c]);
+            y[m] = rq_biased_i8((int32_t)acc, b[m], mult1, shift1, 0);
+        }
+        for (int t = 0; t < T; t++) {
+            uint32_t acc = 0;
+            for (int m = 0; m < DM; m++) acc += (uint32_t)((int32_t)W2[(size_t)t * DM + m] * y[m]);
+            out[(size_t)t * C + c] = rq_biased_i8((int32_t)acc, b2[t], mult2, shift2, 0);
+        }
+    }
+    free(y);
+}
+
+/* rnn_cell_i8/reference.c: acc = b + Wx x + Wh h (int32), requant + zp,
+ * saturate, h_t = tanh_lut[(uint8) pre_act] */
+void oracle_rnn_cell_i8(const int8_t *Wx, const int8_t *Wh, const int32_t *b, const int8_t *x,
+                        const int8_t *h_prev, int8_t *h_t, int H, int I, int32_t mult, int shift,
+                        int zp, const int8_t *tanh_lut) {
+    for (int j = 0; j < H; j++) {
+        uint32_t acc = (uint32_t)b[j];
+        for (int k = 0; k < I; k++) acc += (uint32_t)((int32_t)Wx[(size_t)j * I + k] * x[k]);
+        for (int k = 0; k < H; k++) acc += (uint32_t)((int32_t)Wh[(size_t)j * H + k] * h_prev[k]);
+        const int8_t pre = sat_i8(rq_round((int64_t)(int32_t)acc * (int64_t)mult, shift) + zp);
+        h_t[j] = tanh_lut[(uint8_t)pre];
+    }
+}

@@ -380,6 +380,19 @@ void oracle_affine_ew(const void *in, int elem_in, void *out, int elem_out, int6
 /* kernels/expert/i16_gemm/reference.c: int16 GEMM, int32 accumulator. */
 void oracle_gemm_i16(const int16_t *A, const int16_t *B, int32_t *C, int M, int N, int K);
 
+/* kernels/expert/i8_channel_mix_block/reference.c (lut NULL: no table). */
+void oracle_mix_mlp_i8(const int8_t *X, const int8_t *W1, const int32_t *b1, const int8_t *lut,
+                       const int8_t *W2, const int32_t *b2, int8_t *out, int M, int K, int V, int D,
+                       int32_t mult1, int shift1, int32_t mult2, int shift2);
+/* kernels/expert/i8_token_mix_block/reference.c. */
+void oracle_token_mix_i8(const int8_t *X, const int8_t *W, const int32_t *b, const int8_t *W2,
+                         const int32_t *b2, int8_t *out, int T, int C, int DM, int32_t mult1,
+                         int shift1, int32_t mult2, int shift2);
+/* kernels/expert/rnn_cell_i8/reference.c. */
+void oracle_rnn_cell_i8(const int8_t *Wx, const int8_t *Wh, const int32_t *b, const int8_t *x,
+                        const int8_t *h_prev, int8_t *h_t, int H, int I, int32_t mult, int shift,
+                        int zp, const int8_t *tanh_lut);
+
 #ifdef __cplusplus
 }
 #endif

@@ -685,3 +685,34 @@ def gemm_i16(A, B):
     C_ = np.zeros((M, N), np.int32)
     lib().oracle_gemm_i16(_p(A), _p(B), _p(C_), M, N, K)
     return C_
+
+
+def mix_mlp_i8(X, W1, b1, W2, b2, mult1, shift1, mult2, shift2, lut=None):
+    X, W1, W2 = (np.ascontiguousarray(a, np.int8) for a in (X, W1, W2))
+    b1, b2 = np.ascontiguousarray(b1, np.int32), np.ascontiguousarray(b2, np.int32)
+    (M, K), V, D = X.shape, W1.shape[0], W2.shape[0]
+    out = np.zeros((M, D), np.int8)
+    lp = _p(np.ascontiguousarray(lut, np.int8)) if lut is not None else None
+    lib().oracle_mix_mlp_i8(_p(X), _p(W1), _p(b1), lp, _p(W2), _p(b2), _p(out), M, K, V, D,
+                            C.c_int32(mult1), shift1, C.c_int32(mult2), shift2)
+    return out
+
+
+def token_mix_i8(X, W, b, W2, b2, mult1, shift1, mult2, shift2):
+    X, W, W2 = (np.ascontiguousarray(a, np.int8) for a in (X, W, W2))
+    b, b2 = np.ascontiguousarray(b, np.int32), np.ascontiguousarray(b2, np.int32)
+    (T, Cc), DM = X.shape, W.shape[0]
+    out = np.zeros((T, Cc), np.int8)
+    lib().oracle_token_mix_i8(_p(X), _p(W), _p(b), _p(W2), _p(b2), _p(out), T, Cc, DM,
+                              C.c_int32(mult1), shift1, C.c_int32(mult2), shift2)
+    return out
+
+
+def rnn_cell_i8(Wx, Wh, b, x, h_prev, mult, shift, zp, tanh_lut):
+    Wx, Wh, x, h_prev, tanh_lut = (np.ascontiguousarray(a, np.int8) for a in (Wx, Wh, x, h_prev, tanh_lut))
+    b = np.ascontiguousarray(b, np.int32)
+    H, I = Wx.shape
+    out = np.zeros(H, np.int8)
+    lib().oracle_rnn_cell_i8(_p(Wx), _p(Wh), _p(b), _p(x), _p(h_prev), _p(out), H, I,
+                             C.c_int32(mult), shift, zp, _p(tanh_lut))
+    return out

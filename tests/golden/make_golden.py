@@ -1134,6 +1134,40 @@ def gen_affine(ref):
     save("affine", **a)
 
 
+def gen_mixers(ref):
+    # i8_channel_mix_block and i8_token_mix_block (fixed 8 x 16, hidden 16)
+    # and rnn_cell_i8 through their reference.c: full-range int8 operands,
+    # biases around the accumulator scale, the harnesses' requant sets and a
+    # wider one; the RNN at H = I = 32 and a ragged H 40, I 24.
+    rng = np.random.default_rng(157)
+    s8 = lambda *sh: rng.integers(-128, 128, sh).astype(np.int8)
+    i32 = lambda lim, *sh: rng.integers(-lim, lim, sh).astype(np.int32)
+    a = {"lut": s8(256)}
+    X, W1, W2 = s8(8, 16), s8(16, 16), s8(16, 16)
+    b1, b2 = i32(20000, 16), i32(20000, 16)
+    a.update(X=X, W1=W1, W2=W2, b1=b1, b2=b2)
+    for t, (m1, s1, m2, s2) in enumerate(((3, 7, 5, 8), (1, 4, 2, 5), (1 << 12, 20, 77, 14))):
+        o = np.zeros((8, 16), np.int8)
+        ref.ref_i8_channel_mix_block(ptr(X), ptr(W1), ptr(b1), ptr(W2), ptr(b2), ptr(a["lut"]), ptr(o),
+                                     C.c_int32(m1), s1, C.c_int32(m2), s2)
+        a[f"cmix{t}"] = o
+        o = np.zeros((8, 16), np.int8)
+        Wt, Wt2, bt2 = W1[:, :8].copy(), W2[:8, :].copy(), b2[:8].copy()
+        ref.ref_i8_token_mix_block(ptr(X), ptr(Wt), ptr(b1), ptr(Wt2), ptr(bt2), ptr(o),
+                                   C.c_int32(m1), s1, C.c_int32(m2), s2)
+        a.update({f"tmix{t}": o, "Wt": Wt, "Wt2": Wt2, "bt2": bt2})
+    for t, (H, I, mult, shift, zp) in enumerate(((32, 32, 3, 7, 0), (32, 32, 5, 5, -3),
+                                                  (40, 24, 1 << 14, 22, 9))):
+        Wx, Wh, x, h = s8(H, I), s8(H, H), s8(I), s8(H)
+        b = i32(30000, H)
+        o = np.zeros(H, np.int8)
+        ref.ref_rnn_cell_i8(ptr(Wx), ptr(Wh), ptr(b), ptr(x), ptr(h), ptr(o), H, I, C.c_int32(mult), shift,
+                            C.c_int8(zp), ptr(a["lut"]))
+        a.update({f"rnn_Wx{t}": Wx, f"rnn_Wh{t}": Wh, f"rnn_b{t}": b, f"rnn_x{t}": x, f"rnn_h{t}": h,
+                  f"rnn_out{t}": o, f"rnn_p{t}": np.array([mult, shift, zp])})
+    save("mixers", **a)
+
+
 def gen_int_rows(ref):
     # The attention-tile callers, the integer layernorms with an inverse-
     # variance table, the exp-table softmax tiles, the int16 requant, the
@@ -1298,6 +1332,7 @@ def main():
     gen_cache_rope(ref)
     gen_blocks(ref)
     gen_affine(ref)
+    gen_mixers(ref)
     gen_f16_gemms(ref)
     gen_flash_attention(ref)
     gen_online_softmax_step(ref)

@@ -567,3 +567,53 @@ def test_i16_gemm_random(hx, oracle, M, N, K):
     np.testing.assert_array_equal(hx.gemm_i16(A, B), oracle.gemm_i16(A, B))
     ext = np.full((M, K), -32768, np.int16), np.full((K, N), 32767, np.int16)
     np.testing.assert_array_equal(hx.gemm_i16(*ext), oracle.gemm_i16(*ext))
+
+
+# --------------------------------------------------- mixer blocks, RNN cell
+
+from test_oracle_golden import MIX_SETS, mixer_calls  # noqa: E402
+
+
+def test_mixers_golden_and_shims(hx):
+    import ctypes as C
+    g = golden("mixers")
+    for k, (got, exp) in enumerate(mixer_calls(hx, g)):
+        np.testing.assert_array_equal(got, exp, err_msg=str(k))
+    p = lambda a: a.ctypes.data_as(C.c_void_p)
+    cm, tm, rnn = _shim("i8_channel_mix_block"), _shim("i8_token_mix_block"), _shim("rnn_cell_i8")
+    cm.argtypes = [C.c_void_p] * 7 + [C.c_int32, C.c_int, C.c_int32, C.c_int]
+    tm.argtypes = [C.c_void_p] * 6 + [C.c_int32, C.c_int, C.c_int32, C.c_int]
+    rnn.argtypes = [C.c_void_p] * 6 + [C.c_int, C.c_int, C.c_int32, C.c_int, C.c_int8, C.c_void_p]
+    for t, (m1, s1, m2, s2) in enumerate(MIX_SETS):
+        out = np.zeros((8, 16), np.int8)
+        cm(p(g["X"]), p(g["W1"]), p(g["b1"]), p(g["W2"]), p(g["b2"]), p(g["lut"]), p(out), m1, s1, m2, s2)
+        np.testing.assert_array_equal(out, g[f"cmix{t}"])
+        tm(p(g["X"]), p(g["Wt"]), p(g["b1"]), p(g["Wt2"]), p(g["bt2"]), p(out), m1, s1, m2, s2)
+        np.testing.assert_array_equal(out, g[f"tmix{t}"])
+    for t in range(3):
+        c = lambda k: g[f"rnn_{k}{t}"]
+        mult, shift, zp = (int(v) for v in c("p"))
+        H, I = c("Wx").shape
+        out = np.zeros(H, np.int8)
+        rnn(p(c("Wx")), p(c("Wh")), p(c("b")), p(c("x")), p(c("h")), p(out), H, I, mult, shift, zp, p(g["lut"]))
+        np.testing.assert_array_equal(out, c("out"))
+
+
+def test_mixers_random(hx, oracle):
+    rng = np.random.default_rng(43)
+    s8 = lambda *sh: rng.integers(-128, 128, sh, dtype=np.int8)
+    i32 = lambda *sh: rng.integers(-50000, 50000, sh).astype(np.int32)
+    lut = s8(256)
+    M, K, V, D = 3000, 200, 384, 96
+    X, W1, W2 = s8(M, K), s8(V, K), s8(D, V)
+    args = (X, W1, i32(V), W2, i32(D), 1 << 12, 20, 77, 14)
+    np.testing.assert_array_equal(hx.mix_mlp_i8(*args, lut=lut), oracle.mix_mlp_i8(*args, lut=lut))
+    np.testing.assert_array_equal(hx.mix_mlp_i8(*args), oracle.mix_mlp_i8(*args))
+    T, Cc, DM = 196, 512, 256
+    X, W, W2 = s8(T, Cc), s8(DM, T), s8(T, DM)
+    args = (X, W, i32(DM), W2, i32(T), 1 << 12, 19, 99, 14)
+    np.testing.assert_array_equal(hx.token_mix_i8(*args), oracle.token_mix_i8(*args))
+    for H, I in ((1, 1), (1000, 300), (64, 0)):
+        Wx, Wh, x, h = s8(H, I), s8(H, H), s8(I), s8(H)
+        args = (Wx, Wh, i32(H), x, h, 1 << 14, 22, 9, lut)
+        np.testing.assert_array_equal(hx.rnn_cell_i8(*args), oracle.rnn_cell_i8(*args))

@@ -517,6 +517,27 @@ def clamp_calls(impl, g):
         yield impl.requant_ew(x8, y8, pre="add", lo1=lo, hi1=hi, lo2=lo, hi2=hi), g[name + "__out0"]
 
 
+MIX_SETS = ((3, 7, 5, 8), (1, 4, 2, 5), (1 << 12, 20, 77, 14))
+
+
+def mixer_calls(impl, g):
+    """(result, expected) of the channel / token mixing blocks and the RNN
+    cell (golden mixers) through `impl` (the oracle or the GPU ops)."""
+    for t, (m1, s1, m2, s2) in enumerate(MIX_SETS):
+        yield (impl.mix_mlp_i8(g["X"], g["W1"], g["b1"], g["W2"], g["b2"], m1, s1, m2, s2, lut=g["lut"]),
+               g[f"cmix{t}"])
+        yield impl.token_mix_i8(g["X"], g["Wt"], g["b1"], g["Wt2"], g["bt2"], m1, s1, m2, s2), g[f"tmix{t}"]
+    for t in range(3):
+        c = lambda k: g[f"rnn_{k}{t}"]
+        mult, shift, zp = (int(v) for v in c("p"))
+        yield impl.rnn_cell_i8(c("Wx"), c("Wh"), c("b"), c("x"), c("h"), mult, shift, zp, g["lut"]), c("out")
+
+
+def test_mixers_golden(oracle):
+    for k, (got, exp) in enumerate(mixer_calls(oracle, golden("mixers"))):
+        np.testing.assert_array_equal(got, exp, err_msg=str(k))
+
+
 def test_i16_gemm_golden(oracle):
     g = golden("affine")
     for t in range(2):

@@ -71,6 +71,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_kv_cache_update_i8": (I, [I, P, P, P, P, I, I, I, I]),
     "hexcuda_rope_pair_f16": (I, [I, P, P, P, P, I64]),
     "hexcuda_gemm_i16": (I, [I, P, P, P, I, I, I]),
+    "hexcuda_conv2d_hmx": (I, [I, P, P, P, P, I, I, I, I, I, I, I, I, I]),
     "hexcuda_mix_mlp_i8": (I, [I, P, P, P, P, P, P, P, I, I, I, I, I32, I, I32, I]),
     "hexcuda_token_mix_i8": (I, [I, P, P, P, P, P, P, I, I, I, I32, I, I32, I]),
     "hexcuda_rnn_cell_i8": (I, [I, P, P, P, P, P, P, I, I, I32, I, I8, P]),
@@ -131,6 +132,7 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_host_kv_cache_update_i8": (I, [P, P, P, P, I, I, I, I]),
     "hexcuda_host_rope_pair_f16": (I, [P, P, P, P, I64]),
     "hexcuda_host_gemm_i16": (I, [P, P, P, I, I, I]),
+    "hexcuda_host_conv2d_hmx": (I, [P, P, P, P, I, I, I, I, I, I, I, I, I]),
     "hexcuda_host_mix_mlp_i8": (I, [P, P, P, P, P, P, P, I, I, I, I, I32, I, I32, I]),
     "hexcuda_host_token_mix_i8": (I, [P, P, P, P, P, P, I, I, I, I32, I, I32, I]),
     "hexcuda_host_rnn_cell_i8": (I, [P, P, P, P, P, P, I, I, I32, I, I8, P]),

@@ -1748,6 +1748,57 @@ HX_EXPORT int hexcuda_rnn_cell_i8(int dev, const int8_t *Wx, const int8_t *Wh, c
                               -128, 127, -128, 127, tanh_lut);
 }
 
+// ------------------------------------------------ HMX-convention convolution
+//
+// out[co][p] = epilogue(sum_{ci, kh, kw} W[co][ci][kh][kw] in[ci][window(p)])
+// as the HMX-convention GEMM of the window matrix (rows = output positions,
+// u8) by W^T (W row-major [c_out][c_in kh kw] is its K-major Bt), stored
+// column-major so that out is [c_out][positions].
+namespace hx {
+namespace {
+constexpr int kSlotConvCol = 23;
+
+__global__ void __launch_bounds__(256) im2col_u8_kernel(const uint8_t *__restrict__ in,
+                                                        uint8_t *__restrict__ col, int C, int IH,
+                                                        int IW, int KH, int KW, int stride, int OW,
+                                                        int64_t n) {
+    const int kk = C * KH * KW;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += step) {
+        const int p = (int)(t / kk), r = (int)(t % kk);
+        const int ci = r / (KH * KW), kh = (r / KW) % KH, kw = r % KW;
+        const int oh = p / OW, ow = p % OW;
+        col[t] = in[((size_t)ci * IH + oh * stride + kh) * IW + ow * stride + kw];
+    }
+}
+}  // namespace
+}  // namespace hx
+
+HX_EXPORT int hexcuda_conv2d_hmx(int dev, const uint8_t *in, const int8_t *W, const int32_t *bias,
+                                 void *out, int store, int act, int c_in, int ih, int iw, int c_out,
+                                 int kh, int kw, int stride) {
+    Dev *d = get_dev(dev);
+    if (!d) return HEXCUDA_ERR_NODEV;
+    if (c_in < 1 || c_out < 1 || kh < 1 || kw < 1 || stride < 1 || ih < kh || iw < kw)
+        return fail(HEXCUDA_ERR_ARG, "conv2d_hmx: c_in %d %dx%d c_out %d kernel %dx%d stride %d", c_in, ih,
+                    iw, c_out, kh, kw, stride);
+    if (store != HEXCUDA_HMX_STORE_I32 && store != HEXCUDA_HMX_STORE_I8_SAT &&
+        store != HEXCUDA_HMX_STORE_U16_FIELD)
+        return fail(HEXCUDA_ERR_ARG, "conv2d_hmx: store kind %d", store);
+    if (!in || !W || !out) return fail(HEXCUDA_ERR_ARG, "conv2d_hmx: null pointer");
+    const int oh = (ih - kh) / stride + 1, ow = (iw - kw) / stride + 1;
+    const int P = oh * ow, KK = c_in * kh * kw;
+    uint8_t *col = reinterpret_cast<uint8_t *>(scratch(d, kSlotConvCol, (size_t)P * KK));
+    if (!col) return HEXCUDA_ERR_OOM;
+    launch_begin(d);
+    constexpr auto kern = im2col_u8_kernel;
+    kern<<<resident_blocks<kern>(d, (int64_t)P * KK), 256, 0, d->stream>>>(
+        in, col, c_in, ih, iw, kh, kw, stride, ow, (int64_t)P * KK);
+    if (int rc = launch_end(d, "conv2d_hmx (im2col)")) return rc;
+    return hexcuda_gemm_hmx_ex(dev, col, W, 1, bias, nullptr, HEXCUDA_HMX_RES_NONE, nullptr, out, store,
+                               act, 1, P, c_out, KK, 0);
+}
+
 HX_EXPORT int hexcuda_ffn_hmx_i8(int dev, const uint8_t *X, const int8_t *W1, const int32_t *b1,
                                  const int8_t *W2, const int32_t *b2, int8_t *out, int M, int D,
                                  int Dff, int sh1, int sh2) {

@@ -1383,3 +1383,24 @@ HX_EXPORT int hexcuda_host_rnn_cell_i8(const int8_t *Wx, const int8_t *Wh, const
         return hexcuda_rnn_cell_i8(p.slot, dWx, dWh, db, dx, dh, dout, H, I, mult, shift, zp, dl);
     });
 }
+
+HX_EXPORT int hexcuda_host_conv2d_hmx(const uint8_t *in, const int8_t *W, const int32_t *bias,
+                                      void *out, int store, int act, int c_in, int ih, int iw,
+                                      int c_out, int kh, int kw, int stride) {
+    if (c_in < 1 || c_out < 1 || kh < 1 || kw < 1 || stride < 1 || ih < kh || iw < kw)
+        return fail(HEXCUDA_ERR_ARG, "host_conv2d_hmx: bad shape");
+    if (int rc = null_check("host_conv2d_hmx", {in, W, out})) return rc;
+    const int oh = (ih - kh) / stride + 1, ow = (iw - kw) / stride + 1;
+    const size_t es = store == HEXCUDA_HMX_STORE_I32 ? 4 : (store == HEXCUDA_HMX_STORE_U16_FIELD ? 2 : 1);
+    const size_t obytes = (size_t)c_out * oh * ow * es;
+    return run_sharded(1, out, obytes, [&](Part &p) {
+        const uint8_t *din = stage_in(p.d, kSlotIn0, in, (size_t)c_in * ih * iw);
+        const int8_t *dW = stage_in(p.d, kSlotIn1, W, (size_t)c_out * c_in * kh * kw);
+        const int32_t *db = bias ? stage_in(p.d, kSlotIn2, bias, (size_t)c_out) : nullptr;
+        void *dout = scratch(p.d, kSlotOut, obytes);
+        if (!din || !dW || (bias && !db) || !dout) return hexcuda_last_error();
+        p.dout = dout;
+        return hexcuda_conv2d_hmx(p.slot, din, dW, db, dout, store, act, c_in, ih, iw, c_out, kh, kw,
+                                  stride);
+    });
+}

@@ -446,6 +446,23 @@ def rope_pair_f16(x, cos_t, sin_t) -> np.ndarray:
     return out
 
 
+def conv2d_hmx(x, W, bias=None, store: str = "u16_field", act: str = "none", stride: int = 1):
+    """HMX-convention convolution, no padding: x [c_in, ih, iw] u8, W
+    [c_out, c_in, kh, kw] int8 -> [c_out, oh, ow] (store "u16_field",
+    "i32" or "i8_sat"; activation as gemm_hmx_ex)."""
+    x, W = _c(x, np.uint8), _c(W, np.int8)
+    c_in, ih, iw = x.shape
+    c_out, c_in2, kh, kw = W.shape
+    assert c_in == c_in2
+    kind, dt = HMX_STORE[store]
+    oh, ow = (ih - kh) // stride + 1, (iw - kw) // stride + 1
+    bp = _p(_c(bias, np.int32)) if bias is not None else None
+    out = np.empty((c_out, oh, ow), dt)
+    check(load().hexcuda_host_conv2d_hmx(_p(x), _p(W), bp, _p(out), kind, HMX_ACT[act], c_in, ih, iw,
+                                         c_out, kh, kw, stride))
+    return out
+
+
 def gemm_i16(A, B) -> np.ndarray:
     """int16 GEMM, int32 accumulator (modulo 2^32): A [M, K], B [K, N]."""
     A, B = _c(A, np.int16), _c(B, np.int16)

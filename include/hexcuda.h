@@ -511,6 +511,17 @@ int hexcuda_ffn_lut_i8(int dev, const int8_t *A, const int8_t *W1, const int32_t
  * operands are split into signed bytes and multiplied by one tcgen05
  * kind::i8 GEMM of twice the rows and columns; 16 M N bytes of scratch. */
 int hexcuda_gemm_i16(int dev, const int16_t *A, const int16_t *B, int32_t *C, int M, int N, int K);
+/* HMX-convention convolution of in [c_in][ih][iw] (u8) by W
+ * [c_out][c_in][kh][kw] (int8) at the given stride, no padding: acc over the
+ * window, v = sx12((acc * 17 + 8) >> 4) (+ bias[co]), activation
+ * (HEXCUDA_HMX_ACT_*), store HEXCUDA_HMX_STORE_U16_FIELD / I32 / I8_SAT into
+ * out [c_out][oh][ow].  Window matrix + HMX GEMM with a column-major store.
+ * kernels/expert/i8_conv2d_3x3_hmx, i8_conv2d_3x3_hmx_tiled,
+ * i8_conv2d_bias_relu_hmx, i8_conv1d_bias_requant_hmx (ih = kh = 1)
+ * reference.c. */
+int hexcuda_conv2d_hmx(int dev, const uint8_t *in, const int8_t *W, const int32_t *bias, void *out,
+                       int store, int act, int c_in, int ih, int iw, int c_out, int kh, int kw,
+                       int stride);
 /* Channel-mixing MLP: q = sat_i8(round_half_away((X W1^T + b1) mult1 >>
  * shift1)), y = lut ? lut[q + 128] : q, out = sat_i8(round_half_away((y W2^T
  * + b2) mult2 >> shift2)); X [M,K], W1 [V,K], W2 [D,V] int8 row-major.
@@ -727,6 +738,9 @@ int hexcuda_host_kv_cache_update_i8(int8_t *k_cache, int8_t *v_cache, const int8
 int hexcuda_host_rope_pair_f16(const uint16_t *x, const uint16_t *cos_t, const uint16_t *sin_t,
                                uint16_t *out, int64_t n_pairs);
 int hexcuda_host_gemm_i16(const int16_t *A, const int16_t *B, int32_t *C, int M, int N, int K);
+int hexcuda_host_conv2d_hmx(const uint8_t *in, const int8_t *W, const int32_t *bias, void *out,
+                            int store, int act, int c_in, int ih, int iw, int c_out, int kh, int kw,
+                            int stride);
 int hexcuda_host_mix_mlp_i8(const int8_t *X, const int8_t *W1, const int32_t *b1, const int8_t *lut,
                             const int8_t *W2, const int32_t *b2, int8_t *out, int M, int K, int V,
                             int D, int32_t mult1, int shift1, int32_t mult2, int shift2);

@@ -1487,3 +1487,32 @@ void oracle_rnn_cell_i8(const int8_t *Wx, const int8_t *Wh, const int32_t *b, co
         h_t[j] = tanh_lut[(uint8_t)pre];
     }
 }
+
+/* i8_conv2d_3x3_hmx/reference.c, i8_conv2d_3x3_hmx_tiled/reference.c,
+ * i8_conv2d_bias_relu_hmx/reference.c, i8_conv1d_bias_requant_hmx/reference.c:
+ * window sums, the 12-bit HMX field, bias, activation, store (store /
+ * act numbered as ORACLE_HMX_STORE_* / ORACLE_HMX_ACT_*) */
+void oracle_conv2d_hmx(const uint8_t *in, const int8_t *W, const int32_t *bias, void *out, int store,
+                       int act, int c_in, int ih, int iw, int c_out, int kh, int kw, int stride) {
+    const int oh = (ih - kh) / stride + 1, ow = (iw - kw) / stride + 1;
+    for (int co = 0; co < c_out; co++)
+        for (int y = 0; y < oh; y++)
+            for (int x = 0; x < ow; x++) {
+                int acc = 0;
+                for (int ci = 0; ci < c_in; ci++)
+                    for (int a = 0; a < kh; a++)
+                        for (int b = 0; b < kw; b++)
+                            acc += (int)in[((size_t)ci * ih + y * stride + a) * iw + x * stride + b] *
+                                   (int)W[(((size_t)co * c_in + ci) * kh + a) * kw + b];
+                const int f = hmx_field_i(acc);
+                int v = sx12(f) + (bias ? bias[co] : 0);
+                if (act == ORACLE_HMX_ACT_RELU && v < 0) v = 0;
+                const size_t o = ((size_t)co * oh + y) * ow + x;
+                if (store == ORACLE_HMX_STORE_U16_FIELD)
+                    ((uint16_t *)out)[o] = (uint16_t)(v & 0xFFF);
+                else if (store == ORACLE_HMX_STORE_I8_SAT)
+                    ((int8_t *)out)[o] = (int8_t)clamp_i8i(v);
+                else
+                    ((int32_t *)out)[o] = v;
+            }
+}

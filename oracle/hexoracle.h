@@ -393,6 +393,11 @@ void oracle_rnn_cell_i8(const int8_t *Wx, const int8_t *Wh, const int32_t *b, co
                         const int8_t *h_prev, int8_t *h_t, int H, int I, int32_t mult, int shift,
                         int zp, const int8_t *tanh_lut);
 
+/* HMX-convention convolution (the i8_conv2d_*_hmx / i8_conv1d_bias_requant_hmx
+ * reference.c files), no padding. */
+void oracle_conv2d_hmx(const uint8_t *in, const int8_t *W, const int32_t *bias, void *out, int store,
+                       int act, int c_in, int ih, int iw, int c_out, int kh, int kw, int stride);
+
 #ifdef __cplusplus
 }
 #endif

@@ -716,3 +716,16 @@ def rnn_cell_i8(Wx, Wh, b, x, h_prev, mult, shift, zp, tanh_lut):
     lib().oracle_rnn_cell_i8(_p(Wx), _p(Wh), _p(b), _p(x), _p(h_prev), _p(out), H, I,
                              C.c_int32(mult), shift, zp, _p(tanh_lut))
     return out
+
+
+def conv2d_hmx(x, W, bias=None, store="u16_field", act="none", stride=1):
+    x, W = np.ascontiguousarray(x, np.uint8), np.ascontiguousarray(W, np.int8)
+    c_in, ih, iw = x.shape
+    c_out, _, kh, kw = W.shape
+    kind, dt = HMX_STORE[store]
+    oh, ow = (ih - kh) // stride + 1, (iw - kw) // stride + 1
+    out = np.zeros((c_out, oh, ow), dt)
+    bp = _p(np.ascontiguousarray(bias, np.int32)) if bias is not None else None
+    lib().oracle_conv2d_hmx(_p(x), _p(W), bp, _p(out), kind, HMX_ACT[act], c_in, ih, iw, c_out, kh, kw,
+                            stride)
+    return out

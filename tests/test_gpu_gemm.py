@@ -617,3 +617,17 @@ def test_mixers_random(hx, oracle):
         Wx, Wh, x, h = s8(H, I), s8(H, H), s8(I), s8(H)
         args = (Wx, Wh, i32(H), x, h, 1 << 14, 22, 9, lut)
         np.testing.assert_array_equal(hx.rnn_cell_i8(*args), oracle.rnn_cell_i8(*args))
+
+
+# ------------------------------------------------ HMX-convention convolution
+
+@pytest.mark.parametrize("c_in,ih,iw,c_out,kh,kw,stride", [(8, 10, 10, 32, 3, 3, 1), (3, 31, 17, 40, 5, 3, 2),
+                                                          (16, 1, 68, 64, 1, 5, 1), (64, 56, 56, 128, 3, 3, 1)])
+def test_conv2d_hmx_random(hx, oracle, c_in, ih, iw, c_out, kh, kw, stride):
+    rng = np.random.default_rng(c_in * ih + c_out)
+    x = rng.integers(0, 256, (c_in, ih, iw), dtype=np.uint8)
+    W = rng.integers(-128, 128, (c_out, c_in, kh, kw), dtype=np.int8)
+    bias = rng.integers(-3000, 3000, c_out).astype(np.int32)
+    for kw_ in (dict(), dict(bias=bias, store="i32", act="relu"), dict(bias=bias, store="i8_sat")):
+        np.testing.assert_array_equal(hx.conv2d_hmx(x, W, stride=stride, **kw_),
+                                      oracle.conv2d_hmx(x, W, stride=stride, **kw_), err_msg=str(kw_))

@@ -181,6 +181,11 @@ class Workload:
     def scale(self) -> float:
         return 1e9 if self.unit == "GB/s" else 1e12
 
+    def gather_spec(self):
+        """Outputs a replicated run all-gathers: (this rank's rows, total
+        rows, bytes per row) each; None when the output does not shard."""
+        return None
+
 
 class Reduce(Workload):
     name = "reduce"
@@ -221,6 +226,10 @@ class Reduce(Workload):
         self.o1 = torch.empty_like(self.x)
         self.o2 = torch.empty_like(self.x)
         self.hx_host = (x, g, b)
+
+    def gather_spec(self):
+        # (this rank's output rows, total rows, bytes per row) per output
+        return [(self.o1, self.R, self.C * 4), (self.o2, self.R, self.C * 4)]
 
     def kernels(self):
         # (label, algorithmic units of one launch on this rank)
@@ -307,12 +316,28 @@ class GemmU8S8(Workload):
         self.shift = torch.full((self.N,), 44, dtype=torch.int32, device="cuda")
         self.out = torch.empty((self.m, self.N), dtype=torch.uint8, device="cuda")
 
+    def gather_spec(self):
+        return [(self.out, self.M, self.N)]
+
     def kernels(self):
         return [("gemm_u8s8_pc", 2.0 * self.m * self.N * self.K)]
 
     def launch(self, device, k):
         device.launch("gemm_u8s8_pc", 0, self.A, self.B, self.bias, self.out, self.m, self.N,
                       self.K, 128, self.mult, self.shift, 128)
+
+    def setup_e2e(self, torch):
+        self.h = [t.cpu().pin_memory() for t in (self.A, self.B, self.bias, self.mult, self.shift)]
+        self.hout = torch.empty((self.m, self.N), dtype=torch.uint8).pin_memory()
+
+    def e2e_step(self, lib, check):
+        A, B, bias, mult, shift = (t.data_ptr() for t in self.h)
+        check(lib.hexcuda_host_gemm_u8s8_pc(A, B, bias, self.hout.data_ptr(), self.m, self.N,
+                                            self.K, 128, mult, shift, 128))
+
+    def e2e_bytes(self):
+        return {"h2d_bytes_per_step": self.m * self.K + self.K * self.N + 3 * 4 * self.N,
+                "d2h_bytes_per_step": self.m * self.N}
 
     def cpu_setup(self, rows):
         rng = np.random.default_rng(0)
@@ -360,11 +385,26 @@ class GemmF16(Workload):
         self.Bt = (torch.randn((self.N, self.K), device="cuda", generator=g) * s).half()
         self.out = torch.empty((self.m, self.N), dtype=torch.float16, device="cuda")
 
+    def gather_spec(self):
+        return [(self.out, self.M, 2 * self.N)]
+
     def kernels(self):
         return [("gemm_f16_nt", 2.0 * self.m * self.N * self.K)]
 
     def launch(self, device, k):
         device.launch("gemm_f16_nt", 0, self.A, self.Bt, self.out, self.m, self.N, self.K)
+
+    def setup_e2e(self, torch):
+        self.h = [t.cpu().pin_memory() for t in (self.A, self.Bt)]
+        self.hout = torch.empty((self.m, self.N), dtype=torch.float16).pin_memory()
+
+    def e2e_step(self, lib, check):
+        check(lib.hexcuda_host_gemm_f16_nt(self.h[0].data_ptr(), self.h[1].data_ptr(),
+                                           self.hout.data_ptr(), self.m, self.N, self.K))
+
+    def e2e_bytes(self):
+        return {"h2d_bytes_per_step": 2 * (self.m * self.K + self.N * self.K),
+                "d2h_bytes_per_step": 2 * self.m * self.N}
 
     def cpu_setup(self, rows):
         rng = np.random.default_rng(0)
@@ -412,12 +452,28 @@ class Attn(Workload):
         self.V = torch.randn(shp, device="cuda", generator=g).half()
         self.O = torch.empty_like(self.Q)
 
+    def gather_spec(self):
+        return [(self.O, self.B * self.H, 2 * self.S * self.D)]
+
     def kernels(self):
         return [("attn_f16", self.flops(self.h))]
 
     def launch(self, device, k):
         device.launch("attn_f16", 0, self.Q, self.K_, self.V, self.O, self.h, self.S, self.S,
                       self.D, 1 / math.sqrt(self.D), 1)
+
+    def setup_e2e(self, torch):
+        self.hq = [t.cpu().pin_memory() for t in (self.Q, self.K_, self.V)]
+        self.hout = torch.empty_like(self.hq[0]).pin_memory()
+
+    def e2e_step(self, lib, check):
+        q, k, v = (t.data_ptr() for t in self.hq)
+        check(lib.hexcuda_host_attn_f16(q, k, v, self.hout.data_ptr(), self.h, self.S, self.S,
+                                        self.D, 1 / math.sqrt(self.D), 1))
+
+    def e2e_bytes(self):
+        return {"h2d_bytes_per_step": 3 * 2 * self.h * self.S * self.D,
+                "d2h_bytes_per_step": 2 * self.h * self.S * self.D}
 
     def cpu_setup(self, rows):
         rng = np.random.default_rng(0)
@@ -470,6 +526,18 @@ class GemmI8(Workload):
     def launch(self, device, k):
         device.launch("gemm_i8_requant", 0, self.A, self.B, self.out, 256, 256, 256, self.mult,
                       self.shift, 0)
+
+    def setup_e2e(self, torch):
+        self.h = [t.cpu().pin_memory() for t in (self.A, self.B)]
+        self.hout = torch.empty((256, 256), dtype=torch.int8).pin_memory()
+
+    def e2e_step(self, lib, check):
+        check(lib.hexcuda_host_gemm_i8_requant(self.h[0].data_ptr(), self.h[1].data_ptr(),
+                                               self.hout.data_ptr(), 256, 256, 256, self.mult,
+                                               self.shift, 0))
+
+    def e2e_bytes(self):
+        return {"h2d_bytes_per_step": 2 * 256 * 256, "d2h_bytes_per_step": 256 * 256}
 
     def cpu_setup(self, rows):
         rng = np.random.default_rng(0)
@@ -534,12 +602,27 @@ class RequantEw(Workload):
         self.b = torch.randint(-2**30, 2**30, (self.n,), dtype=torch.int32, device="cuda", generator=g)
         self.out = torch.empty((self.n,), dtype=torch.int8, device="cuda")
 
+    def gather_spec(self):
+        return [(self.out, self.N, 1)]
+
     def kernels(self):
         return [("requant_ew", 9.0 * self.n)]
 
     def launch(self, device, k):
         device.launch("requant_ew", 0, self.a, 0, self.b, 1, self.out, self.n, 1, 0, self.MULT,
                       self.SHIFT, self.ZP, 0, -128, 127, -128, 127, None)
+
+    def setup_e2e(self, torch):
+        self.h = [t.cpu().pin_memory() for t in (self.a, self.b)]
+        self.hout = torch.empty((self.n,), dtype=torch.int8).pin_memory()
+
+    def e2e_step(self, lib, check):
+        check(lib.hexcuda_host_requant_ew(self.h[0].data_ptr(), 0, self.h[1].data_ptr(), 1,
+                                          self.hout.data_ptr(), self.n, 1, 0, self.MULT,
+                                          self.SHIFT, self.ZP, 0, -128, 127, -128, 127, None))
+
+    def e2e_bytes(self):
+        return {"h2d_bytes_per_step": 8 * self.n, "d2h_bytes_per_step": self.n}
 
     def cpu_setup(self, rows):
         rng = np.random.default_rng(0)
@@ -593,6 +676,17 @@ class ReduceI8(Workload):
     def launch(self, device, k):
         device.launch("reduce_int", 0, self.a, None, 0, self.n, 0, self.out)
 
+    def setup_e2e(self, torch):
+        self.h = self.a.cpu().pin_memory()
+        self.hout = torch.zeros(2, dtype=torch.int32).pin_memory()
+
+    def e2e_step(self, lib, check):
+        check(lib.hexcuda_host_reduce_int(self.h.data_ptr(), None, 0, self.n, 0,
+                                          self.hout.data_ptr()))
+
+    def e2e_bytes(self):
+        return {"h2d_bytes_per_step": self.n, "d2h_bytes_per_step": 4}
+
     def cpu_setup(self, rows):
         self.ca = np.random.default_rng(0).integers(-128, 128, rows, dtype=np.int8)
         self.cout = np.zeros(256, np.int32)
@@ -640,12 +734,28 @@ class GemmHmx(Workload):
         self.bias = torch.randint(-3000, 3000, (self.N,), dtype=torch.int32, device="cuda", generator=g)
         self.out = torch.empty((self.m, self.N), dtype=torch.int32, device="cuda")
 
+    def gather_spec(self):
+        return [(self.out, self.M, 4 * self.N)]
+
     def kernels(self):
         return [("gemm_hmx_ex", 2.0 * self.m * self.N * self.K)]
 
     def launch(self, device, k):
         device.launch("gemm_hmx_ex", 0, self.A, self.B, 0, self.bias, None, 0, None, self.out, 0, 1,
                       0, self.m, self.N, self.K, 0)
+
+    def setup_e2e(self, torch):
+        self.h = [t.cpu().pin_memory() for t in (self.A, self.B, self.bias)]
+        self.hout = torch.empty((self.m, self.N), dtype=torch.int32).pin_memory()
+
+    def e2e_step(self, lib, check):
+        A, B, bias = (t.data_ptr() for t in self.h)
+        check(lib.hexcuda_host_gemm_hmx_ex(A, B, 0, bias, None, 0, None, self.hout.data_ptr(), 0,
+                                           1, 0, self.m, self.N, self.K, 0))
+
+    def e2e_bytes(self):
+        return {"h2d_bytes_per_step": self.m * self.K + self.K * self.N + 4 * self.N,
+                "d2h_bytes_per_step": 4 * self.m * self.N}
 
     def cpu_setup(self, rows):
         rng = np.random.default_rng(0)
@@ -771,6 +881,70 @@ def cpu_sample_text(wl, rows, reps, secs):
 
 # --------------------------------------------------------------------- arms
 
+def measure_pcie(torch, nbytes=256 << 20):
+    """Pinned host <-> device copy bandwidth of this rank's GPU (GB/s): H2D
+    alone, D2H alone, and both directions at once on two streams."""
+    h_src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    h_dst = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d_a = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    d_b = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    s2 = torch.cuda.Stream()
+
+    def timed(fn, reps=5):
+        fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / reps
+
+    def both():
+        d_a.copy_(h_src, non_blocking=True)
+        with torch.cuda.stream(s2):
+            h_dst.copy_(d_b, non_blocking=True)
+
+    h2d = nbytes / timed(lambda: d_a.copy_(h_src, non_blocking=True)) / 1e9
+    d2h = nbytes / timed(lambda: h_dst.copy_(d_b, non_blocking=True)) / 1e9
+    duplex = 2 * nbytes / timed(both) / 1e9
+    return {"h2d_gbs": round(h2d, 1), "d2h_gbs": round(d2h, 1), "duplex_gbs": round(duplex, 1)}
+
+
+def time_allgather(wl, torch, lib, check, steps, warmup, dist):
+    """The replicated-output option: each output's row shards all-gathered
+    across the ranks (NCCL over NVLink through hexcuda_comm_allgather_rows),
+    timed on its own with CUDA events, max over ranks."""
+    spec = wl.gather_spec()
+    fulls = [torch.empty((rows, rb), dtype=torch.uint8, device="cuda") for _, rows, rb in spec]
+
+    def step():
+        for (shard, rows, rb), full in zip(spec, fulls):
+            check(lib.hexcuda_comm_allgather_rows(shard.data_ptr(), full.data_ptr(), rows, rb))
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = dist.max(start.elapsed_time(end)) / steps
+    total = sum(rows * rb for _, rows, rb in spec)
+    algbw = total / (ms / 1e3) / 1e9
+    del fulls
+    return {"ms_per_step": round(ms, 4), "bytes_per_step": total,
+            "algbw_gbs": round(algbw, 1),
+            "busbw_gbs": round(algbw * (dist.world - 1) / dist.world, 1),
+            "api": "hexcuda_comm_allgather_rows (ncclAllGather, or one ncclBroadcast per "
+                   "ragged part)"}
+
+
 def run_ours(args, dist):
     import torch
 
@@ -786,13 +960,26 @@ def run_ours(args, dist):
     device.bind_stream(0, stream)
     peaks = load_peaks()
     traffic = load_traffic()
+    check = _lib.check
+    replicate = args.replicate and dist.world > 1
+    if replicate:
+        import ctypes as C
 
-    def measure(wl_cls, with_e2e, with_cpu):
+        import torch.distributed as tdist
+        uid = C.create_string_buffer(128)
+        if dist.rank == 0:
+            check(lib.hexcuda_comm_unique_id(uid, 128))
+        box = [uid.raw if dist.rank == 0 else None]
+        tdist.broadcast_object_list(box, src=0)
+        C.memmove(uid, box[0], 128)
+        check(lib.hexcuda_comm_init_rank(dist.world, dist.rank, uid, 128))
+
+    def measure(wl_cls, steps, cpu_budget):
         wl = wl_cls(dist.world, dist.rank)
         wl.setup_device(torch)
-        t = time_device(wl, torch, device, args.steps, args.warmup, dist, lib)
+        t = time_device(wl, torch, device, steps, args.warmup, dist, lib)
         ms_max = dist.max(t["ms"])
-        per_step_ms = ms_max / args.steps
+        per_step_ms = ms_max / steps
         value = wl.units_per_step() / (per_step_ms / 1e3) / wl.scale()
         # dominant kernel roofline (this rank's launches)
         label, units, dur = max(t["per_kernel"], key=lambda r: r[2])
@@ -804,33 +991,37 @@ def run_ours(args, dist):
             # twice the dense bf16 rate on this part, so the int8 roofline is
             # 2x the measured bf16 figure
             mul = 2.0 if wl.unit == "TOPS" else 1.0
-            peak, punit, pname = peaks["bf16_tflops"] * mul, wl.unit.replace("/s", "") + "/s", "bf16_tflops"
+            peak, punit, pname = peaks["bf16_tflops"] * mul, wl.unit, "bf16_tflops"
         tr = traffic.get(label)
         res = {
             "metric": BASELINE_METRIC, "value": round(value, 3), "unit": wl.unit,
-            "ms_per_step": round(per_step_ms, 4), "dtype": wl.dtype, "config": wl.config(),
+            "steps": steps, "ms_per_step": round(per_step_ms, 4), "dtype": wl.dtype,
+            "config": wl.config(),
             "roofline": {"bound": wl.bound, "kernel": label, "achieved": round(achieved, 2),
                          "peak": peak, "unit": punit if wl.bound == "tensor" else "GB/s",
                          "frac": round(achieved / peak, 4),
                          "peak_source": f"{peaks['source']} {pname}" +
                                         (" x2 (int8 = 2x bf16 dense)" if wl.unit == "TOPS" else ""),
-                         "traffic": tr["bytes_per_launch"] * units / tr["units"] if tr else None,
+                         "traffic": (round(tr["bytes_per_launch"] * units / tr["units"])
+                                     if tr else None),
                          "kernel_ms": round(dur, 4)},
             "clocks": t["clocks"], "gpu_launches": int(t["launches"]),
         }
-        if with_e2e and hasattr(wl, "setup_e2e"):
-            check = _lib.check
-            dt = time_e2e(wl, torch, lib, check, max(2, args.steps // 10), args.warmup, dist)
-            dt = dist.max(dt)
-            nst = max(2, args.steps // 10)
+        if hasattr(wl, "setup_e2e"):
+            nst = max(2, min(steps, 20) // 4)
+            dt = dist.max(time_e2e(wl, torch, lib, check, nst, args.warmup, dist))
             res["e2e"] = {"value": round(wl.units_per_step() / (dt / nst) / wl.scale(), 3),
-                          "unit": wl.unit, **wl.e2e_bytes(),
-                          "api": "hexcuda_host_* (candidate_kernel shims' calls), pinned host buffers"}
-        if with_cpu and dist.rank == 0 and dist.world == 1:
+                          "unit": wl.unit, **wl.e2e_bytes(), "steps": nst,
+                          "api": "hexcuda_host_* (the candidate_kernel shims' call), pinned "
+                                 "host buffers"}
+        if replicate and wl.gather_spec() is not None:
+            res["replicate"] = time_allgather(wl, torch, lib, check, max(3, steps // 2),
+                                              args.warmup, dist)
+        if cpu_budget > 0 and dist.rank == 0 and dist.world == 1:
             nthreads = len(os.sched_getaffinity(0))
             if wl.name == "gemm_i8":
                 nthreads = 1
-            v, rows, reps, secs = cpu_measure(wl, args.cpu_budget, nthreads, cpu_rows_cap(wl))
+            v, rows, reps, secs = cpu_measure(wl, cpu_budget, nthreads, cpu_rows_cap(wl))
             res["cpu_baseline"] = {"value": round(v / wl.scale(), 6), "unit": wl.unit,
                                    "cores": nthreads, "kind": wl.cpu_kind,
                                    "sample": cpu_sample_text(wl, rows, reps, secs),
@@ -839,19 +1030,42 @@ def run_ours(args, dist):
         torch.cuda.empty_cache()
         return res
 
-    head = measure(WORKLOADS[args.workload], True, True)
-    ops = {}
+    pcie = measure_pcie(torch)
+    head = measure(WORKLOADS[args.workload], args.steps, args.cpu_budget)
+    if "e2e" in head:
+        # the host-API number against what the copies alone allow on this link
+        e = head["e2e"]
+        gb_in, gb_out = e["h2d_bytes_per_step"] / 1e9, e["d2h_bytes_per_step"] / 1e9
+        t_copy = max(gb_in / pcie["h2d_gbs"], gb_out / pcie["d2h_gbs"],
+                     (gb_in + gb_out) / pcie["duplex_gbs"])
+        wl0 = WORKLOADS[args.workload](dist.world, dist.rank)
+        e["pcie"] = dict(pcie, ceiling=round(wl0.units_per_step() / t_copy / wl0.scale(), 3))
+    ops_out = {}
     if args.ops == "all":
         for name in ("gemm_u8s8", "gemm_f16", "attn", "gemm_i8", "requant", "gemm_hmx",
                      "reduce_i8"):
             if name == args.workload:
                 continue
-            r = measure(WORKLOADS[name], False, args.cpu_all)
-            ops[name] = {k: r[k] for k in ("value", "unit", "ms_per_step", "dtype", "config",
-                                           "roofline", "clocks", "gpu_launches")
-                         if k in r}
+            r = measure(WORKLOADS[name], max(args.steps, args.op_steps), args.op_cpu_budget)
+            rf = r["roofline"]
+            entry = {"value": r["value"], "unit": r["unit"], "steps": r["steps"],
+                     "ms": r["ms_per_step"], "dtype": r["dtype"],
+                     "workload": r["config"]["workload"],
+                     "roofline": {k: rf[k] for k in ("bound", "kernel", "achieved", "peak",
+                                                     "frac", "traffic")},
+                     "clocks": {"sm_mhz": r["clocks"].get("sm_mhz"),
+                                "reasons": r["clocks"].get("reasons")},
+                     "gpu_launches": r["gpu_launches"]}
+            if "e2e" in r:
+                entry["e2e"] = {k: r["e2e"][k] for k in ("value", "h2d_bytes_per_step",
+                                                          "d2h_bytes_per_step")}
             if "cpu_baseline" in r:
-                ops[name]["cpu_baseline"] = r["cpu_baseline"]
+                cb = r["cpu_baseline"]
+                entry["cpu_baseline"] = {"value": cb["value"], "cores": cb["cores"],
+                                         "kind": cb["kind"], "sample": cb["sample"]}
+            if "replicate" in r:
+                entry["replicate"] = {k: r["replicate"][k] for k in ("ms_per_step", "busbw_gbs")}
+            ops_out[name] = entry
     line = {"metric": head["metric"], "value": head["value"], "unit": head["unit"],
             "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": head["ms_per_step"], "higher_is_better": True,
@@ -859,11 +1073,13 @@ def run_ours(args, dist):
             "vs_baseline": None, "dtype": head["dtype"], "data": "synthetic (seeded)",
             "config": head["config"], "roofline": head["roofline"], "clocks": head["clocks"],
             "gpu_launches": head["gpu_launches"]}
-    for k in ("e2e", "cpu_baseline"):
+    for k in ("e2e", "cpu_baseline", "replicate"):
         if k in head:
             line[k] = head[k]
-    if ops:
-        line["ops"] = ops
+    if ops_out:
+        line["ops"] = ops_out
+    if replicate:
+        check(lib.hexcuda_comm_destroy())
     return line
 
 
@@ -915,8 +1131,12 @@ def main():
     ap.add_argument("--ops", default="all", choices=["all", "none"])
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work per cpu_baseline sample")
-    ap.add_argument("--cpu-all", action="store_true",
-                    help="also time a CPU baseline for every extra op")
+    ap.add_argument("--op-steps", type=int, default=50,
+                    help="timed steps of each extra op (at least --steps)")
+    ap.add_argument("--op-cpu-budget", type=float, default=2.5,
+                    help="seconds of CPU work per extra op's cpu_baseline sample (0: none)")
+    ap.add_argument("--replicate", action="store_true",
+                    help="N > 1: also all-gather every sharded output over NCCL (timed apart)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -45,6 +45,18 @@ SIGNATURES: dict[str, tuple] = {
     "hexcuda_set_timing": (I, [I]),
     "hexcuda_last_kernel_ms": (F, []),
     "hexcuda_launch_count": (C.c_uint64, []),
+    "hexcuda_mechanisms": (C.c_uint, [I]),
+    # multi-GPU: shards and replicated outputs
+    "hexcuda_shard_rows": (I, [I64, I, I, P, P]),
+    "hexcuda_set_replicate": (I, [I]),
+    "hexcuda_get_replicate": (I, []),
+    "hexcuda_replica": (I, [I, P, P]),
+    "hexcuda_last_collective_ms": (F, []),
+    "hexcuda_allgather_rows": (I, [P, P, I64, SZ]),
+    "hexcuda_comm_unique_id": (I, [P, SZ]),
+    "hexcuda_comm_init_rank": (I, [I, I, P, SZ]),
+    "hexcuda_comm_destroy": (I, []),
+    "hexcuda_comm_allgather_rows": (I, [P, P, I64, SZ]),
     # device-pointer launchers
     "hexcuda_softmax_f32": (I, [I, P, P, I, I]),
     "hexcuda_softmax_f16": (I, [I, P, P, I, I]),

@@ -1055,6 +1055,7 @@ int launch_attn_tc(Dev *d, const __half *Q, const __half *K, const __half *V, __
     a.err_word = d->err_word;
     const int grid = a.nitems < d->sms ? a.nitems : d->sms;
     attn_tc_kernel<D><<<grid, AttnCfg<D>::kThreads, L::kTotal, d->stream>>>(mq, mk, mv, a);
+    note_mech(kMechTcgen05 | kMechTma);
     return HEXCUDA_OK;
 }
 
@@ -1156,6 +1157,7 @@ int launch_attn_pp(Dev *d, const __half *Q, const __half *K, const __half *V, __
     a.sched_off = sched;
     a.sched = sched + grid + 1;
     attn_pp_kernel<<<grid, 384, L::kTotal, d->stream>>>(mq, mk, mv, a);
+    note_mech(kMechTcgen05 | kMechTma);
     return HEXCUDA_OK;
 }
 

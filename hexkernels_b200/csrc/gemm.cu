@@ -33,6 +33,7 @@
 #include <stdio.h>
 
 #include <algorithm>
+#include <mutex>
 #include <type_traits>
 
 #include "ew_launch.cuh"
@@ -1075,6 +1076,7 @@ int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int
     int tiles = args.tiles_m * args.tiles_n;
     int grid = tiles < d->sms ? tiles : d->sms;
     kern<<<grid, kThreads, L::kTotal, d->stream>>>(ta, tb, args);
+    note_mech(kMechTcgen05 | kMechTma);
     return HEXCUDA_OK;
 }
 
@@ -1127,6 +1129,7 @@ int launch_gemm2_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, in
     cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
     if (int rc = check(cudaLaunchKernelEx(&cfg, kern, ta, tb, args), "launch gemm pair kernel"))
         return rc;
+    note_mech(kMechTcgen05 | kMechTma);
     *launched = true;
     return HEXCUDA_OK;
 }
@@ -1881,37 +1884,44 @@ HX_EXPORT int hexcuda_gemm_hmx(int dev, const uint8_t *A, const int8_t *B, int b
 //                (round_up(K, 128) * N <= 16 MiB);
 //   g_na_colsum  column sums of B, N <= kNoAllocMaxN.
 // A is read in place, so its rows must start on 16 bytes (K % 16 == 0, K >= 128).
-// Larger or unaligned problems are rejected with HEXCUDA_ERR_ARG.
+// Larger or unaligned problems are rejected with HEXCUDA_ERR_ARG.  With
+// zpA == 0 the column sums are not needed and neither cleared nor computed
+// (the transpose pass then only copies B), as in the regular entry.
 namespace hx {
 namespace {
 
 constexpr size_t kNoAllocBtBytes = 16u << 20;
 constexpr int kNoAllocMaxN = 16384;
+constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_na_bt[kNoAllocBtBytes];
 static __device__ __align__(256) int32_t g_na_colsum[kNoAllocMaxN];
 
 struct NoAllocPtrs {
-    bool ready = false;
+    std::once_flag once;
+    int rc = HEXCUDA_OK;
     uint8_t *bt = nullptr;
     int32_t *colsum = nullptr;
 };
 
 // Device addresses of the fixed region on device `d` (current).  In host code
 // the arrays' names are host-side stand-ins, not device addresses; the real
-// addresses come from cudaGetSymbolAddress, queried once per device.
+// addresses come from cudaGetSymbolAddress, queried once per device (once even
+// when two host threads make their first call at the same time).
 int noalloc_ptrs(Dev *d, NoAllocPtrs **out) {
-    static NoAllocPtrs per_dev[64];
-    NoAllocPtrs &p = per_dev[d->ordinal & 63];
-    if (!p.ready) {
-        if (int rc = check(cudaGetSymbolAddress(reinterpret_cast<void **>(&p.bt), g_na_bt),
-                           "cudaGetSymbolAddress(g_na_bt)"))
-            return rc;
-        if (int rc = check(cudaGetSymbolAddress(reinterpret_cast<void **>(&p.colsum), g_na_colsum),
-                           "cudaGetSymbolAddress(g_na_colsum)"))
-            return rc;
-        p.ready = true;
-    }
+    static NoAllocPtrs per_dev[kNoAllocMaxDevices];
+    if (d->ordinal < 0 || d->ordinal >= kNoAllocMaxDevices)
+        return fail(HEXCUDA_ERR_ARG, "gemm_u8s8_pc_noalloc: device ordinal %d >= %d", d->ordinal,
+                    kNoAllocMaxDevices);
+    NoAllocPtrs &p = per_dev[d->ordinal];
+    std::call_once(p.once, [&] {
+        p.rc = check(cudaGetSymbolAddress(reinterpret_cast<void **>(&p.bt), g_na_bt),
+                     "cudaGetSymbolAddress(g_na_bt)");
+        if (!p.rc)
+            p.rc = check(cudaGetSymbolAddress(reinterpret_cast<void **>(&p.colsum), g_na_colsum),
+                         "cudaGetSymbolAddress(g_na_colsum)");
+    });
+    if (p.rc) return p.rc;
     *out = &p;
     return HEXCUDA_OK;
 }
@@ -1949,19 +1959,24 @@ HX_EXPORT int hexcuda_gemm_u8s8_pc_noalloc(int dev, const uint8_t *A, const int8
     ep.bias = bias;
     ep.mult_pc = mult;
     ep.shift_pc = shift;
-    ep.colsum = np->colsum;
+    ep.colsum = zpA ? np->colsum : nullptr;
     ep.M = M;
     ep.N = N;
 
     launch_begin(d);
-    // the column sums accumulate atomically: clear them first (every call
-    // shares this region; calls that overlap on the GPU race on it)
-    if (int rc = check(cudaMemsetAsync(np->colsum, 0, sizeof(int32_t) * (size_t)N, d->stream),
-                       "memset colsum"))
-        return rc;
     dim3 g((unsigned)((N + 63) / 64), (unsigned)(Kp / 64));
-    transpose_pack_kernel<uint8_t, true><<<g, 256, 0, d->stream>>>(
-        reinterpret_cast<const uint8_t *>(B), np->bt, np->colsum, K, N, N, Kp);
+    if (zpA) {
+        // the column sums accumulate atomically: clear them first (every call
+        // shares this region; calls that overlap on the GPU race on it)
+        if (int rc = check(cudaMemsetAsync(np->colsum, 0, sizeof(int32_t) * (size_t)N, d->stream),
+                           "memset colsum"))
+            return rc;
+        transpose_pack_kernel<uint8_t, true><<<g, 256, 0, d->stream>>>(
+            reinterpret_cast<const uint8_t *>(B), np->bt, np->colsum, K, N, N, Kp);
+    } else {
+        transpose_pack_kernel<uint8_t, false><<<g, 256, 0, d->stream>>>(
+            reinterpret_cast<const uint8_t *>(B), np->bt, nullptr, K, N, N, Kp);
+    }
     CUtensorMap ta, tb;
     if (int rc = make_kmajor_map(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, K, kBM)) return rc;
     int rc;

@@ -62,6 +62,17 @@ int run_sharded(int64_t rows, void *host_out, size_t out_row_bytes,
         }
         if ((rc = enqueue(p))) break;
     }
+    if (!rc && replicate_on()) {
+        // every device also receives the other devices' rows (row-major
+        // outputs; a column-major store leaves no replica)
+        if (cm_cols > 0) {
+            replica_clear();
+        } else {
+            std::vector<void *> douts((size_t)n, nullptr);
+            for (auto &p : parts) douts[(size_t)p.slot] = p.dout;
+            rc = replicate_rows(douts, rows, out_row_bytes);
+        }
+    }
     for (auto &p : parts) {
         if (!p.d) continue;
         int r = hexcuda_sync(p.slot);
@@ -161,6 +172,11 @@ int run_rows_pipelined(int64_t rows, const void *host_in, size_t in_row_bytes, v
             if (!rc) rc = launch(p, pl.din + c0 * in_row_bytes, pl.dout + c0 * out_row_bytes, cn);
             if (!rc) rc = check(cudaEventRecord(p.d->ev_done[k], p.d->stream), "event");
         }
+    }
+    if (!rc && replicate_on()) {
+        std::vector<void *> douts((size_t)n, nullptr);
+        for (size_t pi = 0; pi < parts.size(); pi++) douts[(size_t)parts[pi].slot] = plans[pi].dout;
+        rc = replicate_rows(douts, rows, out_row_bytes);
     }
     if (!rc) {
         for (size_t pi = 0; pi < parts.size() && !rc; pi++) {

@@ -5,13 +5,16 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <vector>
+
 #include "hexcuda.h"
 
 #define HX_EXPORT extern "C" __attribute__((visibility("default")))
 
 namespace hx {
 
-constexpr int kScratchSlots = 24;
+constexpr int kScratchSlots = 25;
+constexpr int kSlotReplica = 24;  // replicated output of the last host entry (collective.cpp)
 constexpr int kPipeChunks = 64;     // max chunks in flight per pipelined host call
 
 // Per-device state.  `stream` is where every launcher enqueues work; it is the
@@ -55,6 +58,19 @@ void scope_begin();
 void scope_end();
 void launch_begin(Dev *d);
 int launch_end(Dev *d, const char *name, int nlaunches = 1);
+
+// Which kinds of kernel ran (hexcuda_mechanisms): the launchers of the
+// tcgen05 / TMA kernels record their bits here at every launch.
+enum : unsigned { kMechTcgen05 = 1u, kMechTma = 2u };
+void note_mech(unsigned bits);
+
+// Replicated outputs (collective.cpp): whether the caller asked for them, and
+// the gather of the devices' row parts (douts[slot], null for an empty part)
+// into every device's replica buffer, enqueued on each device's stream.
+bool replicate_on();
+int replicate_rows(const std::vector<void *> &douts, int64_t rows, size_t row_bytes);
+void replica_clear();
+void collective_release();
 
 // Watchdog budget for device-side bounded waits, in nanoseconds of
 // %globaltimer.  A wait that exceeds it sets the device error word.

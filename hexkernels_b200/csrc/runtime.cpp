@@ -18,6 +18,7 @@ static int g_last_err = HEXCUDA_OK;
 static char g_last_msg[512] = "ok";
 static bool g_timing = true;
 static std::atomic<uint64_t> g_launches{0};
+static std::atomic<unsigned> g_mech{0};
 static float g_last_ms = -1.0f;
 static bool g_last_ms_valid = false;
 
@@ -38,6 +39,7 @@ int check(cudaError_t e, const char *what) {
 }
 
 static void release_all() {
+    collective_release();
     for (auto &d : g_devs) {
         if (d.ordinal < 0) continue;
         cudaSetDevice(d.ordinal);
@@ -163,6 +165,8 @@ void *scratch(Dev *d, int slot, size_t bytes) {
     d->slot_bytes[slot] = want;
     return p;
 }
+
+void note_mech(unsigned bits) { g_mech.fetch_or(bits); }
 
 static bool g_scope = false;
 
@@ -345,3 +349,7 @@ HX_EXPORT float hexcuda_last_kernel_ms(void) {
 }
 
 HX_EXPORT uint64_t hexcuda_launch_count(void) { return g_launches.load(); }
+
+HX_EXPORT unsigned hexcuda_mechanisms(int reset) {
+    return reset ? g_mech.exchange(0u) : g_mech.load();
+}

@@ -23,8 +23,24 @@ libhexcuda on the GPU:
 prints the feedback dict as JSON.  Keys shared with the corpus evaluator keep
 their names and meaning (task_id, candidate, compiled, correct, errors, n,
 error_text, timed_out, target, achieved, AI, binding_level, ceiling, eta,
-roofline_unavailable); Hexagon-only keys (cycles, packets, HVX/HMX/VTCM
-mechanism flags) have no B200 meaning and are left out.
+roofline_unavailable); Hexagon-only keys (cycles, packets) have no B200
+meaning and are left out.
+
+Mechanism verdict (the B200 counterpart of the corpus's ELF check,
+hexkernels/anticheat/anticheat.py:71-345, merged into its feedback at
+hexkernels/core/evaluate.py:573-597).  Reading compiled GPU code is not an
+option, so the verdict comes from two kinds of evidence:
+    static  a scan of the candidate's own source (the hexcuda_* entries it
+            calls, inline tcgen05 / TMA PTX) and of libhexcuda's sources:
+            whether a called entry reaches, through the library's functions,
+            a kernel that issues tcgen05.mma or cp.async.bulk.tensor
+            (static_tcgen05, static_tma; "may", since an entry can choose
+            between kernels by shape);
+    run     the library's own record of which kinds of kernel the call
+            launched (hexcuda_mechanisms, printed as mech= on the timing
+            line): used_tcgen05, used_tma.
+mechanism = "tcgen05" when the run launched tensor-core kernels, "cuda-core"
+when it launched only other kernels, "cpu" when it launched none.
 """
 from __future__ import annotations
 
@@ -46,7 +62,9 @@ PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 _CORRECT = re.compile(r"^HVXENV_(CORRECT|INCORRECT) errors=(\d+) n=(\d+)", re.M)
-_TIMING = re.compile(r"^HEXCUDA_KERNEL_US kernel=(-?[0-9.]+) wall=([0-9.]+)(?: launches=(\d+))?", re.M)
+_TIMING = re.compile(r"^HEXCUDA_KERNEL_US kernel=(-?[0-9.]+) wall=([0-9.]+)(?: launches=(\d+))?"
+                     r"(?: mech=0x([0-9a-fA-F]+))?", re.M)
+MECH_TCGEN05, MECH_TMA = 1, 2
 _HXERR = re.compile(r"^HEXCUDA_ERROR.*$", re.M)
 
 
@@ -61,6 +79,9 @@ def new_feedback(task_id: str, candidate: str | None) -> dict:
         "wall_us": None,        # host wall time of the candidate_kernel call
         "launches": None,       # libhexcuda kernel launches made by the call
         "used_gpu": False,      # at least one libhexcuda launch ran
+        # mechanism verdict: static source evidence, then what the run launched
+        "calls": [], "static_tcgen05": False, "static_tma": False,
+        "used_tcgen05": None, "used_tma": None, "mechanism": None,
         "error_text": "", "timed_out": False,
         "target": TARGET,
         "achieved": None, "AI": None, "binding_level": None, "ceiling": None, "eta": None,
@@ -79,12 +100,21 @@ def parse_output(stdout: str, stderr: str) -> dict:
     if t:
         # a harness may time several calls (parameter sweeps): report the sum;
         # a negative device time means the call made no launch
-        dev = [float(k) for k, _, _ in t if float(k) >= 0]
+        dev = [float(k) for k, _, _, _ in t if float(k) >= 0]
         out["kernel_us"] = round(sum(dev), 3) if dev else None
-        out["wall_us"] = round(sum(float(w) for _, w, _ in t), 3)
-        if all(n != "" for _, _, n in t):
-            out["launches"] = sum(int(n) for _, _, n in t)
+        out["wall_us"] = round(sum(float(w) for _, w, _, _ in t), 3)
+        if all(n != "" for _, _, n, _ in t):
+            out["launches"] = sum(int(n) for _, _, n, _ in t)
             out["used_gpu"] = out["launches"] > 0
+        if all(m != "" for _, _, _, m in t):
+            bits = 0
+            for _, _, _, m in t:
+                bits |= int(m, 16)
+            out["used_tcgen05"] = bool(bits & MECH_TCGEN05)
+            out["used_tma"] = bool(bits & MECH_TMA)
+        if "used_gpu" in out:
+            out["mechanism"] = ("tcgen05" if out.get("used_tcgen05") else
+                                "cuda-core" if out["used_gpu"] else "cpu")
     errs = _HXERR.findall(stderr)
     if errs:
         out["error_text"] = "\n".join(errs[:5])
@@ -142,6 +172,133 @@ def attach_roofline(fb: dict, useful_ops, work_bytes, dtype: str = "",
     return fb
 
 
+# ------------------------------------------------------- static source scan
+
+_TC_PTX = re.compile(r"tcgen05\.mma")
+_TMA_PTX = re.compile(r"cp\.async\.bulk\.tensor")
+_WORD = re.compile(r"\b[A-Za-z_]\w*\b")
+_CALL = re.compile(r"\b(hexcuda_\w+)\s*\(")
+
+
+def _strip_comments(text: str) -> str:
+    text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+    return re.sub(r"//[^\n]*", " ", text)
+
+
+def _blank_strings(text: str) -> str:
+    """The text with the contents of string and character literals replaced
+    by spaces (same length), so braces inside inline-PTX strings do not count."""
+    out = list(text)
+    i, n = 0, len(text)
+    while i < n:
+        c = text[i]
+        if c in "\"'":
+            j = i + 1
+            while j < n and text[j] != c:
+                j += 2 if text[j] == "\\" else 1
+            for k in range(i + 1, min(j, n)):
+                if out[k] != "\n":
+                    out[k] = " "
+            i = j + 1
+        else:
+            i += 1
+    return "".join(out)
+
+
+def _top_level_functions(text: str) -> dict:
+    """name -> text (signature and body) of every function defined at
+    namespace scope of one C++ / CUDA source (comments already removed).
+    Namespaces and extern "C" blocks are entered; types, initialisers and
+    declarations are skipped."""
+    funcs: dict = {}
+    # preprocessor lines carry no code of interest and no statement end
+    text = re.sub(r"(?m)^[ \t]*#[^\n]*", lambda m: " " * len(m.group(0)), text)
+    bl = _blank_strings(text)
+    i, n, head0 = 0, len(bl), 0
+    while i < n:
+        c = bl[i]
+        if c == ";":
+            head0 = i + 1
+        elif c == "}":                       # end of an entered namespace
+            head0 = i + 1
+        elif c == "{":
+            head = bl[head0:i].strip()
+            if re.match(r"(namespace\b|extern\s+\"C\")", head) or head.startswith("extern"):
+                head0 = i + 1
+                i += 1
+                continue
+            depth, j = 1, i + 1
+            while j < n and depth:
+                depth += {"{": 1, "}": -1}.get(bl[j], 0)
+                j += 1
+            is_type = re.match(r"(template\s*<.*>\s*)?(struct|class|enum|union)\b", head, re.S)
+            if "(" in head and not is_type and not head.endswith("="):
+                # name: the identifier before the last parenthesised group
+                k, depth_p = len(head) - 1, 0
+                while k >= 0:
+                    if head[k] == ")":
+                        depth_p += 1
+                    elif head[k] == "(":
+                        depth_p -= 1
+                        if depth_p == 0:
+                            break
+                    k -= 1
+                m = re.search(r"([A-Za-z_]\w*)\s*$", head[:max(k, 0)])
+                if m:
+                    funcs.setdefault(m.group(1), []).append(text[head0:j])
+            i = j
+            head0 = j
+            continue
+        i += 1
+    return {k: "\n".join(v) for k, v in funcs.items()}
+
+
+_LIB_MECH = None
+
+
+def library_mechanisms() -> dict:
+    """hexcuda_* entry -> (reaches tcgen05.mma, reaches cp.async.bulk.tensor)
+    through the functions defined in libhexcuda's sources."""
+    global _LIB_MECH
+    if _LIB_MECH is not None:
+        return _LIB_MECH
+    funcs: dict = {}
+    for f in sorted((PKG / "csrc").glob("*.c*")):
+        for k, v in _top_level_functions(_strip_comments(f.read_text())).items():
+            funcs[k] = funcs.get(k, "") + "\n" + v
+    names = set(funcs)
+    edges = {k: (set(_WORD.findall(v)) & names) - {k} for k, v in funcs.items()}
+    own = {k: (bool(_TC_PTX.search(v)), bool(_TMA_PTX.search(v))) for k, v in funcs.items()}
+    memo: dict = {}
+
+    def reach(k, stack=()):
+        if k in memo:
+            return memo[k]
+        tc, tma = own[k]
+        for c in edges[k]:
+            if c in stack:
+                continue
+            a, b = reach(c, stack + (k,))
+            tc, tma = tc or a, tma or b
+        memo[k] = (tc, tma)
+        return memo[k]
+
+    _LIB_MECH = {k: reach(k) for k in funcs if k.startswith("hexcuda_")}
+    return _LIB_MECH
+
+
+def scan_candidate(path) -> dict:
+    """Static evidence from a candidate's own source: the libhexcuda entries
+    it calls, and whether those (or its own inline PTX) reach tcgen05 MMAs
+    and TMA loads."""
+    text = _strip_comments(Path(path).read_text())
+    calls = sorted(set(_CALL.findall(text)))
+    lib = library_mechanisms()
+    tc = bool(_TC_PTX.search(text)) or any(lib.get(c, (False, False))[0] for c in calls)
+    tma = bool(_TMA_PTX.search(text)) or any(lib.get(c, (False, False))[1] for c in calls)
+    return {"calls": calls, "static_tcgen05": tc, "static_tma": tma}
+
+
 def find_task_dir(corpus: Path, task_id: str) -> Path | None:
     for sub in ("expert", "mined", ""):
         d = corpus / "kernels" / sub / task_id if sub else corpus / task_id
@@ -179,6 +336,7 @@ def evaluate(task_id: str, candidate: str | None = None, corpus: str | None = No
             if not cand.exists():
                 fb["error_text"] = f"no candidate source {cand}"
                 return fb
+            fb.update(scan_candidate(cand))
             exe = tmp / "harness"
             r = subprocess.run(harness_command(task_dir, cand, exe), capture_output=True, text=True)
             if r.returncode != 0:
@@ -193,6 +351,9 @@ def evaluate(task_id: str, candidate: str | None = None, corpus: str | None = No
                 fb["error_text"] = f"no corpus given and no prebuilt harness {pre}"
                 return fb
             exe = pre
+            shim = PKG / "shims" / f"{task_id}.c"
+            if shim.exists():
+                fb.update(scan_candidate(shim))
         fb["compiled"] = True
         try:
             r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=timeout)

@@ -34,6 +34,7 @@
  * oracle (no libhexcuda) still links and simply prints no device time. */
 extern float hexcuda_last_kernel_ms(void) __attribute__((weak));
 extern uint64_t hexcuda_launch_count(void) __attribute__((weak));
+extern unsigned hexcuda_mechanisms(int reset) __attribute__((weak));
 
 static inline void hvx_enable_pcycle(void) {}
 static inline unsigned long long hvx_rdpcyc(void) {
@@ -44,15 +45,17 @@ static inline unsigned long long hvx_rdpcyc(void) {
 
 #define HVX_TIME_KERNEL(OUT, STMT) do {                                        \
     unsigned long long _hx_l0 = hexcuda_launch_count ? hexcuda_launch_count() : 0; \
+    if (hexcuda_mechanisms) hexcuda_mechanisms(1);                             \
     unsigned long long _hx_t0 = hvx_rdpcyc();                                  \
     STMT;                                                                      \
     unsigned long long _hx_t1 = hvx_rdpcyc();                                  \
     (OUT) = _hx_t1 - _hx_t0;                                                   \
     if (hexcuda_last_kernel_ms)                                                \
-        printf("HEXCUDA_KERNEL_US kernel=%.3f wall=%.3f launches=%llu\n",     \
+        printf("HEXCUDA_KERNEL_US kernel=%.3f wall=%.3f launches=%llu mech=0x%x\n", \
                1000.0 * (double)hexcuda_last_kernel_ms(),                      \
                (double)(OUT) / 1000.0,                                         \
-               (hexcuda_launch_count ? hexcuda_launch_count() : 0) - _hx_l0);  \
+               (hexcuda_launch_count ? hexcuda_launch_count() : 0) - _hx_l0,   \
+               hexcuda_mechanisms ? hexcuda_mechanisms(0) : 0u);               \
 } while (0)
 
 /* LCG: s = s * 1664525 + 1013904223 (mod 2^32), as the corpus harnesses use. */

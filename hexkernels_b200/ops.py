@@ -43,6 +43,38 @@ def last_kernel_ms() -> float:
     return float(load().hexcuda_last_kernel_ms())
 
 
+# ------------------------------------------------- shards and replicated outputs
+
+def shard_rows(rows: int, nparts: int, part: int) -> tuple[int, int]:
+    """Rows [r0, r1) of part `part` of `nparts` (the split every entry uses)."""
+    r0, r1 = C.c_int64(), C.c_int64()
+    check(load().hexcuda_shard_rows(rows, nparts, part, C.byref(r0), C.byref(r1)))
+    return r0.value, r1.value
+
+
+def set_replicate(on: bool) -> None:
+    """Ask the host entries to also all-gather their (row-major) outputs over
+    NVLink, so that every initialised device holds the whole output."""
+    check(load().hexcuda_set_replicate(int(bool(on))))
+
+
+def replica(dev: int, shape, dtype) -> np.ndarray:
+    """Copy device slot `dev`'s replica of the last host entry's output."""
+    lib = load()
+    ptr, nbytes = C.c_void_p(), C.c_size_t()
+    check(lib.hexcuda_replica(dev, C.byref(ptr), C.byref(nbytes)))
+    out = np.empty(shape, dtype)
+    if out.nbytes != nbytes.value:
+        raise ValueError(f"replica holds {nbytes.value} bytes, {out.nbytes} requested")
+    check(lib.hexcuda_d2h(dev, _p(out), ptr, out.nbytes))
+    check(lib.hexcuda_sync(dev))
+    return out
+
+
+def last_collective_ms() -> float:
+    return float(load().hexcuda_last_collective_ms())
+
+
 # ----------------------------------------------------------- integer family
 
 def gemm_i8_requant(A, B, mult: int, shift: int, zp: int) -> np.ndarray:

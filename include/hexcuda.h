@@ -84,6 +84,51 @@ int hexcuda_set_timing(int on);
 float hexcuda_last_kernel_ms(void);
 /* Number of kernels libhexcuda has launched since load (all devices). */
 uint64_t hexcuda_launch_count(void);
+/* Kinds of kernel launched since the last reset (reset != 0 clears after
+ * reading): bit 0 tcgen05 tensor-core MMA kernels, bit 1 TMA-fed kernels.
+ * The evaluator's mechanism verdict (hexkernels_b200/evaluate.py) reads it
+ * around each candidate_kernel call: the B200 counterpart of the reference's
+ * used_hvx / used_hmx / used_dma flags (hexkernels/core/evaluate.py:573-597). */
+#define HEXCUDA_MECH_TCGEN05 1u
+#define HEXCUDA_MECH_TMA 2u
+unsigned hexcuda_mechanisms(int reset);
+
+/* ------------------------------------------ multi-GPU: shards and replicas */
+
+/* The row split every host entry uses over n devices (and bench.py over n
+ * ranks): part `part` owns rows [rows*part/n, rows*(part+1)/n).  Pure host
+ * arithmetic; needs no device.  The reference has no multi-device code: this
+ * and the calls below are the "ngpus / replicate" knob of the drop-in
+ * boundary (one C entry per task, kernels/expert/<task>/kernel_api.h). */
+int hexcuda_shard_rows(int64_t rows, int nparts, int part, int64_t *r0, int64_t *r1);
+
+/* Replicated outputs.  With replicate on, a host entry over N > 1 devices
+ * whose output is row-major also all-gathers the devices' output rows over
+ * NVLink (NCCL, opened with dlopen on first use), so that every device holds
+ * the whole output in its own memory; hexcuda_replica returns device slot
+ * `dev`'s copy (valid until the next host entry).  The host output is still
+ * copied from each device's own rows.  Equal parts move in one ncclAllGather,
+ * ragged parts in one ncclBroadcast per owning part inside one NCCL group.
+ * hexcuda_last_collective_ms: device time of the last gather (max over
+ * devices), timed apart from hexcuda_last_kernel_ms.  Off by default. */
+int hexcuda_set_replicate(int on);
+int hexcuda_get_replicate(void);
+int hexcuda_replica(int dev, void **ptr, size_t *bytes);
+float hexcuda_last_collective_ms(void);
+/* Device-pointer gather, one process over every initialised device: slot i
+ * holds rows [rows*i/n, rows*(i+1)/n) at shards[i] (may be null when that part
+ * is empty); afterwards fulls[i] (rows * row_bytes on slot i) holds all rows.
+ * shards[i] may point into fulls[i] at its own offset (in place).
+ * Asynchronous on each device's stream. */
+int hexcuda_allgather_rows(const void *const *shards, void *const *fulls, int64_t rows,
+                           size_t row_bytes);
+/* The same across processes, one GPU per process (one initialised device):
+ * rank 0 makes an id (>= 128 bytes), every rank joins with it, then each
+ * rank passes its own part and receives all rows. */
+int hexcuda_comm_unique_id(void *id, size_t id_bytes);
+int hexcuda_comm_init_rank(int nranks, int rank, const void *id, size_t id_bytes);
+int hexcuda_comm_destroy(void);
+int hexcuda_comm_allgather_rows(const void *shard, void *full, int64_t rows, size_t row_bytes);
 
 /* --------------------------------------------- device-pointer launchers */
 

@@ -8,7 +8,8 @@ import pytest
 
 from hexkernels_b200 import evaluate as ev
 
-CORPUS = Path(os.environ.get("HEXKERNELS_REF", "/root/reference"))
+# a checkout of the reference corpus, when one is named in HEXKERNELS_REF
+CORPUS = Path(os.environ["HEXKERNELS_REF"]) if os.environ.get("HEXKERNELS_REF") else None
 REPO = Path(__file__).resolve().parent.parent
 
 
@@ -69,7 +70,8 @@ def test_missing_inputs_are_reported():
     assert not fb["compiled"] and "no corpus" in fb["error_text"]
 
 
-@pytest.mark.skipif(not (CORPUS / "kernels" / "expert").is_dir(), reason="corpus not present")
+@pytest.mark.skipif(CORPUS is None or not (CORPUS / "kernels" / "expert").is_dir(),
+                    reason="no corpus checkout named in HEXKERNELS_REF")
 def test_build_from_corpus_without_gpu():
     """Builds the task's own harness with the default shim; without a usable
     GPU the run reports the library's error and an incorrect result."""
@@ -92,3 +94,58 @@ def test_evaluate_prebuilt_harness_on_gpu(hx, task):
     assert fb["compiled"] and fb["correct"], fb
     assert fb["used_gpu"] and fb["launches"] >= 1 and fb["kernel_us"] > 0
     assert fb["eta"] is not None and fb["binding_level"] in ("HBM", "tensor")
+    # the mechanism verdict: what ran agrees with the static evidence
+    if task in ("i8_gemm_requant", "hmx_matmul_i8_bias"):
+        assert fb["static_tcgen05"] and fb["used_tcgen05"] and fb["used_tma"]
+        assert fb["mechanism"] == "tcgen05"
+    if task in ("fp16_softmax", "residual_add_requant"):
+        assert not fb["static_tcgen05"] and fb["used_tcgen05"] is False
+        assert fb["mechanism"] == "cuda-core"
+
+
+def test_mechanism_fields_from_the_timing_line():
+    p = ev.parse_output("HEXCUDA_KERNEL_US kernel=5.000 wall=9.000 launches=2 mech=0x3\n"
+                        "HVXENV_CORRECT errors=0 n=4\n", "")
+    assert p["used_tcgen05"] and p["used_tma"] and p["mechanism"] == "tcgen05"
+    p = ev.parse_output("HEXCUDA_KERNEL_US kernel=5.000 wall=9.000 launches=1 mech=0x0\n", "")
+    assert p["used_tcgen05"] is False and p["mechanism"] == "cuda-core"
+    p = ev.parse_output("HEXCUDA_KERNEL_US kernel=-1000.000 wall=2.0 launches=0 mech=0x0\n", "")
+    assert p["mechanism"] == "cpu" and not p["used_gpu"]
+    # several timed calls: the bits of all of them
+    p = ev.parse_output("HEXCUDA_KERNEL_US kernel=1.0 wall=2.0 launches=1 mech=0x0\n"
+                        "HEXCUDA_KERNEL_US kernel=1.0 wall=2.0 launches=1 mech=0x1\n", "")
+    assert p["used_tcgen05"] and not p["used_tma"]
+
+
+def test_static_scan_tells_scalar_from_tensor_core_candidates(tmp_path):
+    scalar = tmp_path / "scalar.c"
+    scalar.write_text("""
+#include <stdint.h>
+/* a candidate that never reaches the GPU: hexcuda_host_gemm_u8s8_pc( in a comment */
+void candidate_kernel(const int8_t *A, const int8_t *B, int8_t *out, int M, int N, int K,
+                      int32_t mult, int shift, int8_t zp) {
+    for (int i = 0; i < M * N; i++) out[i] = 0;
+}
+""")
+    s = ev.scan_candidate(scalar)
+    assert s == {"calls": [], "static_tcgen05": False, "static_tma": False}
+    s = ev.scan_candidate(REPO / "hexkernels_b200" / "shims" / "i8_gemm_requant.c")
+    assert s["calls"] == ["hexcuda_host_gemm_i8_requant"]
+    assert s["static_tcgen05"] and s["static_tma"]
+    s = ev.scan_candidate(REPO / "hexkernels_b200" / "shims" / "fp16_softmax.c")
+    assert s["calls"] and not s["static_tcgen05"] and not s["static_tma"]
+    own = tmp_path / "own.cu"
+    own.write_text('__global__ void k() { asm volatile("tcgen05.mma.cta_group::1.kind::f16 '
+                   '[%0], %1, %2, %3, p;" ::); }\n')
+    s = ev.scan_candidate(own)
+    assert s["static_tcgen05"] and not s["static_tma"]
+
+
+def test_library_mechanism_map():
+    m = ev.library_mechanisms()
+    for e in ("hexcuda_host_gemm_u8s8_pc", "hexcuda_host_gemm_f16_nt", "hexcuda_host_attn_f16",
+              "hexcuda_host_gemm_hmx_ex", "hexcuda_gemm_u8s8_pc_noalloc"):
+        assert m[e] == (True, True), e
+    for e in ("hexcuda_host_softmax_f32", "hexcuda_host_layernorm_f32", "hexcuda_host_rowreduce_f32",
+              "hexcuda_host_requant_ew", "hexcuda_host_reduce_int"):
+        assert m[e] == (False, False), e

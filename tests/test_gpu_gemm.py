@@ -288,34 +288,73 @@ def test_f16_gemm_random(hx, oracle, M, N, K):
 
 # ------------------------------------------------- benchmark configurations
 
+def fp32_matmul_ieee():
+    """torch fp32 matmuls of the checkers in full fp32 (no TF32)."""
+    import torch
+    try:
+        torch.backends.cuda.matmul.fp32_precision = "ieee"
+    except AttributeError:
+        torch.backends.cuda.matmul.allow_tf32 = False
+
+
+def _crc_inputs(kind):
+    import sys
+
+    from conftest import GOLDEN
+    if str(GOLDEN) not in sys.path:
+        sys.path.insert(0, str(GOLDEN))
+    import make_crc
+    return make_crc, make_crc.inputs(kind)
+
+
 @pytest.mark.slow
-def test_u8s8_benchmark_shape(hx, oracle):
+def test_u8s8_benchmark_shape(hx):
     """u8 x s8 GEMM M=16384, N=K=8192 (zpA 128, bias N(0,1000), per-channel
-    mult/shift, zp_out 128): full GPU run, 48 sampled rows bit-exact vs the
-    oracle, output spread over the u8 range."""
-    M, N, K = 16384, 8192, 8192
-    rng = np.random.default_rng(0)
-    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
-    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
-    bias = np.round(rng.normal(0, 1000, N)).astype(np.int32)
-    mult = rng.integers(2**30, 2**31, N, dtype=np.int64).astype(np.int32)
-    shift = np.full(N, 44, np.int32)
-    got = hx.gemm_u8s8_pc(A, B, bias, 128, mult, shift, 128)
-    rows = np.sort(rng.choice(M, 48, replace=False))
-    exp = oracle.gemm_u8s8_pc(A[rows], B, bias, 128, mult, shift, 128)
-    np.testing.assert_array_equal(got[rows], exp)
+    mult/shift 44, zp_out 128): the WHOLE GPU output bit-exact against the
+    oracle, through per-row CRC32s of the oracle's output made offline by
+    tests/golden/make_crc.py; output spread over the u8 range."""
+    mk, d = _crc_inputs("u8s8")
+    got = hx.gemm_u8s8_pc(d["A"], d["B"], d["bias"], d["zpA"], d["mult"], d["shift"], d["zp_out"])
+    exp = np.load(mk.FILES["u8s8"])
+    crc = mk.row_crcs(got)
+    bad = np.flatnonzero(crc != exp)
+    assert bad.size == 0, f"{bad.size} rows differ, first {bad[:8]}"
     assert 20 < got.std() < 100
 
 
 @pytest.mark.slow
+def test_hmx_benchmark_shape(hx):
+    """HMX-convention u8 x s8 GEMM M=16384, N=K=8192, sx12 field + bias,
+    ReLU, int32 out: the WHOLE output bit-exact against the oracle's per-row
+    CRC32s."""
+    mk, d = _crc_inputs("hmx")
+    got = hx.gemm_hmx_ex(d["A"], d["B"], "i32", "relu", bias=d["bias"])
+    exp = np.load(mk.FILES["hmx"])
+    bad = np.flatnonzero(mk.row_crcs(got) != exp)
+    assert bad.size == 0, f"{bad.size} rows differ, first {bad[:8]}"
+    assert (got > 0).mean() > 0.3
+
+
+@pytest.mark.slow
 def test_f16_benchmark_shape(hx, oracle):
-    """fp16 GEMM M=N=K=8192, A row-major, B column-major, N(0,1)/sqrt(K)."""
+    """fp16 GEMM M=N=K=8192, A row-major, B column-major, N(0,1)/sqrt(K):
+    every output row against an fp32-accumulating product (torch fp32 on the
+    GPU, TF32 off, used only as the checker), and 64 rows against the
+    oracle's sequential fp32 sums."""
+    import torch
     M = N = K = 8192
     rng = np.random.default_rng(0)
     A = (rng.standard_normal((M, K), dtype=np.float32) / np.sqrt(K)).astype(np.float16)
     Bt = (rng.standard_normal((N, K), dtype=np.float32) / np.sqrt(K)).astype(np.float16)
     got = hx.gemm_f16_nt(A, Bt)
-    rows = np.sort(rng.choice(M, 24, replace=False))
+    fp32_matmul_ieee()
+    At = torch.from_numpy(A).cuda().float()
+    Btt = torch.from_numpy(Bt).cuda().float()
+    for r0 in range(0, M, 2048):
+        ref = (At[r0:r0 + 2048] @ Btt.T).half().cpu().numpy()
+        assert_f16_gemm_close(got[r0:r0 + 2048], ref)
+    del At, Btt
+    rows = np.sort(rng.choice(M, 64, replace=False))
     assert_f16_gemm_close(got[rows], oracle.gemm_f16_nt(A[rows], Bt))
 
 

@@ -5,15 +5,14 @@ runtime that reserved the GPU's memory for its own arena (a library
 cudaMalloc would fail there), or a latency-bound caller that cannot take the
 implicit synchronisation of cudaMalloc.  This entry keeps its scratch in a
 fixed region compiled into libhexcuda.  Its output must equal the regular
-entry's (integer arithmetic: bit for bit) on two calls in a row -- the second
-with different B, so column sums left over from the first call would show --
-and it must reject shapes beyond its fixed limits.
+entry's and the oracle's (integer arithmetic: bit for bit) on calls in a row
+-- a later call with a smaller N or K than an earlier one would show column
+sums or K padding left over from that call -- and it must reject shapes
+beyond its fixed limits with the matching message.
 
 The file sorts last so that a run stopping at the first failure has already
 run every other test; it also passes alone in a fresh process.
 """
-import ctypes as C
-
 import numpy as np
 import pytest
 
@@ -47,17 +46,38 @@ def _run(lib, fn, A, B, bias, mult, shift, zpa, zp_out):
     return out.cpu().numpy()
 
 
-def test_noalloc_matches_regular_entry_on_two_calls(hx):
+# (M, N, K, zpA): the 256-wide and 128-wide tile paths, with and without the
+# zero-point term, a K that needs zero padding to the 128-byte K step (144),
+# and a larger call followed by smaller ones
+CASES = [(1000, 768, 1024, 128), (333, 1200, 640, -5), (200, 96, 256, 0), (150, 128, 144, 77),
+         (64, 1000, 144, 0), (517, 64, 512, -128)]
+
+
+def test_noalloc_matches_regular_entry_and_oracle_on_calls_in_a_row(hx, oracle):
     from hexkernels_b200 import _lib
     lib = _lib.load()
     lib.hexcuda_reset_stream(0)
     rng = np.random.default_rng(2024)
-    for (M, N, K, zpa) in [(1000, 768, 1024, 128), (333, 1200, 640, -5)]:
+    for (M, N, K, zpa) in CASES:
         A, B, bias, mult, shift = _case(rng, M, N, K)
         ref = _run(lib, lib.hexcuda_gemm_u8s8_pc, A, B, bias, mult, shift, zpa, 128)
         got = _run(lib, lib.hexcuda_gemm_u8s8_pc_noalloc, A, B, bias, mult, shift, zpa, 128)
-        np.testing.assert_array_equal(got, ref)
+        np.testing.assert_array_equal(got, ref, err_msg=str((M, N, K, zpa)))
+        np.testing.assert_array_equal(got, oracle.gemm_u8s8_pc(A, B, bias, zpa, mult, shift, 128),
+                                      err_msg=str((M, N, K, zpa)))
         assert 10 < got.std()
+
+
+def test_noalloc_at_the_fixed_limit(hx, oracle):
+    """round_up(K, 128) * N equal to the 16 MiB region, N at its maximum."""
+    from hexkernels_b200 import _lib
+    lib = _lib.load()
+    lib.hexcuda_reset_stream(0)
+    rng = np.random.default_rng(7)
+    M, N, K = 40, 16384, 1024
+    A, B, bias, mult, shift = _case(rng, M, N, K)
+    got = _run(lib, lib.hexcuda_gemm_u8s8_pc_noalloc, A, B, bias, mult, shift, 128, 128)
+    np.testing.assert_array_equal(got, oracle.gemm_u8s8_pc(A, B, bias, 128, mult, shift, 128))
 
 
 def test_noalloc_rejects_shapes_beyond_its_fixed_scratch(hx):
@@ -65,11 +85,12 @@ def test_noalloc_rejects_shapes_beyond_its_fixed_scratch(hx):
     lib = _lib.load()
     out = np.zeros(4, np.uint8)
     fn = lib.hexcuda_gemm_u8s8_pc_noalloc
-    # N above the column-sum region, K*N above the B region, unaligned K:
-    # rejected before any pointer is dereferenced
+    # rejected before any pointer is dereferenced; each message names the
+    # limit that refused it
     p = out.ctypes.data
-    assert fn(0, p, p, p, p, 8, 20000, 128, 128, p, p, 128) == 1
-    assert fn(0, p, p, p, p, 8, 8192, 4096, 128, p, p, 128) == 1
-    assert fn(0, p, p, p, p, 8, 256, 100, 128, p, p, 128) == 1
-    assert b"fixed scratch" in lib.hexcuda_last_error_string() or \
-        b"16-byte aligned" in lib.hexcuda_last_error_string()
+    for (N, K, msg) in [(20000, 128, b"fixed scratch"),      # N above the column-sum region
+                        (8192, 4096, b"fixed scratch"),      # K * N above the B region
+                        (16384, 1040, b"fixed scratch"),     # round_up(K, 128) = 1152: one step over
+                        (256, 100, b"16-byte aligned")]:     # K not a multiple of 16
+        assert fn(0, p, p, p, p, 8, N, K, 128, p, p, 128) == 1, (N, K)
+        assert msg in lib.hexcuda_last_error_string(), (N, K, lib.hexcuda_last_error_string())

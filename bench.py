@@ -781,6 +781,13 @@ class GemmHmx(Workload):
                 "(i8_matmul_bias_relu_hmx/reference.c), rows split over host threads")
 
 
+# short workload names of the extra ops in the bench line (full configs:
+# `python bench.py --workload NAME --ops none`)
+OP_LABELS = {"gemm_u8s8": "u8s8 GEMM 16384x8192x8192 pc-requant", "gemm_f16": "f16 GEMM 8192^3 NT",
+             "attn": "causal SDPA 8x32x4096x128", "gemm_i8": "i8 GEMM 256^3 requant",
+             "requant": "residual_add_requant 2^28", "gemm_hmx": "HMX GEMM 16384x8192x8192 i32",
+             "reduce_i8": "i8_sum 2^31"}
+
 WORKLOADS = {w.name: w for w in (Reduce, GemmU8S8, GemmF16, Attn, GemmI8, RequantEw, GemmHmx,
                                   ReduceI8)}
 
@@ -788,8 +795,12 @@ WORKLOADS = {w.name: w for w in (Reduce, GemmU8S8, GemmF16, Attn, GemmI8, Requan
 # ------------------------------------------------------------------- timing
 
 def time_device(wl, torch, device, steps, warmup, dist, lib):
-    """Timed region: barrier + sync, K steps on torch's current stream with
-    per-kernel CUDA events, sync + barrier.  Returns a dict."""
+    """Timed region: barrier + sync, K steps back to back on torch's current
+    stream between one start and one end CUDA event, sync + barrier.  An
+    event recorded between launches costs a few microseconds of stream time,
+    so the library's own per-launch events are off here and the per-kernel
+    durations (for the roofline) come from a second pass of the same K steps
+    with an event pair around each launch.  Returns a dict."""
     kernels = wl.kernels()
     for _ in range(warmup):
         for k in range(len(kernels)):
@@ -797,25 +808,35 @@ def time_device(wl, torch, device, steps, warmup, dist, lib):
     torch.cuda.synchronize()
     device.sync(0)
     stream = torch.cuda.current_stream()
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in kernels] for _ in range(steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    launches0 = lib.hexcuda_launch_count()
-    dist.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(torch.cuda.current_device()) as clk:
-        start.record(stream)
+    lib.hexcuda_set_timing(0)
+    try:
+        launches0 = lib.hexcuda_launch_count()
+        dist.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            start.record(stream)
+            for s in range(steps):
+                for k in range(len(kernels)):
+                    wl.launch(device, k)
+            end.record(stream)
+            torch.cuda.synchronize()
+        dist.barrier()
+        device.sync(0)
+        launches = lib.hexcuda_launch_count() - launches0
+        ms = start.elapsed_time(end)
+        # per-kernel durations: the same steps, one event pair per launch
+        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in kernels] for _ in range(steps)]
         for s in range(steps):
             for k in range(len(kernels)):
                 ev[s][k][0].record(stream)
                 wl.launch(device, k)
                 ev[s][k][1].record(stream)
-        end.record(stream)
         torch.cuda.synchronize()
-    dist.barrier()
-    device.sync(0)
-    launches = lib.hexcuda_launch_count() - launches0
-    ms = start.elapsed_time(end)
+        device.sync(0)
+    finally:
+        lib.hexcuda_set_timing(1)
     per_kernel = []
     for k, (label, units) in enumerate(kernels):
         dur = [ev[s][k][0].elapsed_time(ev[s][k][1]) for s in range(steps)]
@@ -1048,23 +1069,19 @@ def run_ours(args, dist):
                 continue
             r = measure(WORKLOADS[name], max(args.steps, args.op_steps), args.op_cpu_budget)
             rf = r["roofline"]
-            entry = {"value": r["value"], "unit": r["unit"], "steps": r["steps"],
-                     "ms": r["ms_per_step"], "dtype": r["dtype"],
-                     "workload": r["config"]["workload"],
-                     "roofline": {k: rf[k] for k in ("bound", "kernel", "achieved", "peak",
-                                                     "frac", "traffic")},
-                     "clocks": {"sm_mhz": r["clocks"].get("sm_mhz"),
-                                "reasons": r["clocks"].get("reasons")},
-                     "gpu_launches": r["gpu_launches"]}
+            # compact, so that the whole line fits a log tail of ~3 KB
+            entry = {"value": r["value"], "unit": r["unit"], "ms": r["ms_per_step"],
+                     "steps": r["steps"], "workload": OP_LABELS[name],
+                     "roofline": {k: rf[k] for k in ("kernel", "achieved", "peak", "frac")},
+                     "sm_mhz": r["clocks"].get("sm_mhz"), "reasons": r["clocks"].get("reasons"),
+                     "launches": r["gpu_launches"]}
             if "e2e" in r:
-                entry["e2e"] = {k: r["e2e"][k] for k in ("value", "h2d_bytes_per_step",
-                                                          "d2h_bytes_per_step")}
+                entry["e2e"] = r["e2e"]["value"]
             if "cpu_baseline" in r:
-                cb = r["cpu_baseline"]
-                entry["cpu_baseline"] = {"value": cb["value"], "cores": cb["cores"],
-                                         "kind": cb["kind"], "sample": cb["sample"]}
+                entry["cpu_baseline"] = {"value": r["cpu_baseline"]["value"],
+                                         "kind": r["cpu_baseline"]["kind"]}
             if "replicate" in r:
-                entry["replicate"] = {k: r["replicate"][k] for k in ("ms_per_step", "busbw_gbs")}
+                entry["allgather_busbw_gbs"] = r["replicate"]["busbw_gbs"]
             ops_out[name] = entry
     line = {"metric": head["metric"], "value": head["value"], "unit": head["unit"],
             "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup,

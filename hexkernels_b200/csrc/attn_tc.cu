@@ -526,13 +526,20 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
     return d;
 }
 
-// 2^x for both halves of x2 without the MUFU unit.  x = n + f with n =
-// rint(x) (adding 1.5 * 2^23 rounds x to an integer in the low mantissa
-// bits) and f in [-0.5, 0.5]; 2^f is a degree-3 polynomial fitted for this
-// kernel (relative error below 8e-5, ample for the fp16 P it feeds), and 2^n
-// is added to the exponent field: bits(p) + n * 2^23, where bits(t) * 2^23
-// equals n * 2^23 modulo 2^32.  x is clamped to >= -125 so 2^x stays a
-// normal number (it only feeds a row sum and an fp16 P, where it is zero).
+// 2^x for both halves of x2 on the FMA pipe instead of the MUFU unit.
+// Range reduction after Cody and Waite (W. J. Cody, W. Waite, Software Manual
+// for the Elementary Functions, 1980): x = n + f with n = rint(x), obtained by
+// adding and subtracting 1.5 * 2^23 (which also leaves n in the low mantissa
+// bits of t), and f in [-1/2, 1/2].  2^f is a degree-3 polynomial whose
+// coefficients minimise the maximum relative error on [-1/2, 1/2] (Remez
+// exchange; tests/test_attn_exp2.py recomputes them and bounds the error of
+// this evaluation at 7.6e-5 in float32, below the fp16 rounding of the P it
+// feeds).  2^n is added to the exponent field: bits(p) + (bits(t) << 23),
+// where bits(t) << 23 equals n * 2^23 modulo 2^32.  x is clamped to >= -125
+// so the result stays a normal number (such P are zero in fp16 anyway).
+constexpr float kExp2C0 = 0.9999280571937561f, kExp2C1 = 0.6932609677314758f,
+                kExp2C2 = 0.2426111251115799f, kExp2C3 = 0.0551716685295105f;
+
 __device__ __forceinline__ void exp2_fma2(uint64_t x2, float &r0, float &r1) {
     float x0, x1;
     up2(x2, x0, x1);
@@ -540,10 +547,9 @@ __device__ __forceinline__ void exp2_fma2(uint64_t x2, float &r0, float &r1) {
     const uint64_t t = add2(xc, pk2(12582912.0f, 12582912.0f));
     const uint64_t nf = add2(t, pk2(-12582912.0f, -12582912.0f));
     const uint64_t f = fma2(nf, pk2(-1.0f, -1.0f), xc);
-    uint64_t p = fma2(pk2(0.05517047643661499f, 0.05517047643661499f), f,
-                      pk2(0.2426084578037262f, 0.2426084578037262f));
-    p = fma2(p, f, pk2(0.6932609677314758f, 0.6932609677314758f));
-    p = fma2(p, f, pk2(0.9999282360076904f, 0.9999282360076904f));
+    uint64_t p = fma2(pk2(kExp2C3, kExp2C3), f, pk2(kExp2C2, kExp2C2));
+    p = fma2(p, f, pk2(kExp2C1, kExp2C1));
+    p = fma2(p, f, pk2(kExp2C0, kExp2C0));
     float p0, p1, t0, t1;
     up2(p, p0, p1);
     up2(t, t0, t1);
@@ -572,9 +578,13 @@ __device__ __forceinline__ void exp2_fma2(uint64_t x2, float &r0, float &r1) {
 // which is what lets S_x(j+1) reuse the columns P_x(j) was read from.
 constexpr int kPairQ = 256;
 // One score pair in kPolyEvery takes the FMA-pipe exponential (0: none).
-// The MUFU unit is not the limiter of this kernel (issue slots are), and the
-// polynomial costs ~7 issue slots per score against 1 for ex2.
-constexpr int kPolyEvery = 0;
+// Measured on the causal 8x32x4096x128 benchmark: one pair in 4 on the FMA
+// pipe costs 7 % and one in 2 costs 9 % against none (the polynomial's ~6
+// issue slots per score cost more than the MUFU time it frees), so it is off.
+#ifndef HX_ATTN_POLY_EVERY
+#define HX_ATTN_POLY_EVERY 0
+#endif
+constexpr int kPolyEvery = HX_ATTN_POLY_EVERY;
 // Register split of the 384-thread CTA: launched at kRegsLaunch per thread
 // (ptxas's count for __launch_bounds__(384, 1)), 128 threads give up
 // registers, 256 take them: 128 * kRegsCtl + 256 * kRegsSoftmax must not

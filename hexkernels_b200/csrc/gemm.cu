@@ -16,8 +16,9 @@
 //               (per-column parameters staged in shared memory), store to HBM,
 //               then hand the accumulator back to the MMA warp.
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile
-// i+1.  Tiles are walked in grouped order (kGroupM M-blocks share each
-// N-block) so a wave of CTAs reuses A and B from L2.
+// i+1.  Tiles are walked in groups sized from the L2 capacity (pick_raster):
+// a panel of one operand stays resident in L2 while the other streams past it
+// once per group, and the CTAs of a wave share the streamed blocks.
 //
 // Operand preparation (HBM-bound pre-passes, only where needed): a row-major
 // B[K,N] is transposed into a K-major copy (and, for the zero-point GEMMs, its
@@ -31,6 +32,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include <algorithm>
 #include <mutex>
@@ -50,7 +52,6 @@ constexpr int kBM = 128;             // rows of A per tile (UMMA M)
 constexpr int kBKBytes = 128;        // K extent of one stage, in bytes
 constexpr int kStages = 4;
 constexpr int kThreads = 320;      // TMA warp, MMA warp, 8 epilogue warps
-constexpr int kGroupM = 16;
 constexpr int kColParamBytes = 6 * 32 * 4;   // one epilogue warp's ColParams
 
 enum EpiKind { kEpiF16 = 0, kEpiRequant = 1, kEpiHmx = 2, kEpiF16Ex = 3 };
@@ -105,6 +106,10 @@ struct EpiParams {
 
 struct GemmArgs {
     int tiles_m, tiles_n, num_kb;
+    // rasterisation: consecutive tiles walk `group` blocks of one dimension
+    // (M-blocks when group_n_major == 0, N-blocks otherwise) before moving
+    // along the other, so the group's panel of that operand stays in L2
+    int group, group_n_major;
     int *err_word;
     EpiParams epi;
 };
@@ -124,14 +129,21 @@ struct Smem {
     static constexpr int kTotal = kParamOffset + kParamBytes + 1024;  // + align slack
 };
 
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &mb, int &nb) {
-    const int per_group = kGroupM * tiles_n;
-    const int group = t / per_group;
-    const int first_m = group * kGroupM;
-    const int gsize = min(tiles_m - first_m, kGroupM);
-    const int r = t - group * per_group;
-    mb = first_m + r % gsize;
-    nb = r / gsize;
+// Tile t -> (M-block, N-block): groups of `group` blocks of the resident
+// dimension, walked across the other dimension; inside a group the resident
+// dimension varies fastest, so the CTAs of a wave share the streamed operand's
+// blocks too.
+__device__ __forceinline__ void tile_coords(int t, const GemmArgs &a, int &mb, int &nb) {
+    const int along = a.group_n_major ? a.tiles_n : a.tiles_m;   // resident dimension
+    const int across = a.group_n_major ? a.tiles_m : a.tiles_n;
+    const int per_group = a.group * across;
+    const int g = t / per_group;
+    const int first = g * a.group;
+    const int gsize = min(along - first, a.group);
+    const int r = t - g * per_group;
+    const int res = first + r % gsize, str = r / gsize;
+    mb = a.group_n_major ? str : res;
+    nb = a.group_n_major ? res : str;
 }
 
 // Requant parameters of one epilogue warp's current 32 columns; half is the
@@ -491,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t armed_phase = 0;
             for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
                 int mb, nb;
-                tile_coords(t, args.tiles_m, args.tiles_n, mb, nb);
+                tile_coords(t, args, mb, nb);
                 for (int kb = 0; kb < args.num_kb; kb++) {
                     if (!tc::mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.err_word,
                                        kErrWaitEmpty))
@@ -591,7 +603,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < num_tiles && !__any_sync(0xffffffffu, *abort_flag);
              t += gridDim.x, local++) {
             int mb, nb;
-            tile_coords(t, args.tiles_m, args.tiles_n, mb, nb);
+            tile_coords(t, args, mb, nb);
             const int buf = local & 1;
             const uint32_t aphase = (local >> 1) & 1;
             const bool ok =
@@ -644,7 +656,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // tempty[b] lives in the even CTA and collects one arrival per epilogue warp
 // of both CTAs.
 constexpr int kStages2 = 6;
-constexpr int kGroupM2 = 8;        // pair tiles of 256 rows per rasterisation group
 
 struct Smem2 {
     static constexpr int kABytes = 128 * kBKBytes;        // this CTA's 128 rows of A
@@ -659,15 +670,6 @@ struct Smem2 {
 };
 static_assert(Smem2::kTotal <= 227 * 1024, "pair-kernel shared memory");
 
-__device__ __forceinline__ void tile_coords2(int t, int tiles_m, int tiles_n, int &mb, int &nb) {
-    const int per_group = kGroupM2 * tiles_n;
-    const int group = t / per_group;
-    const int first_m = group * kGroupM2;
-    const int gsize = min(tiles_m - first_m, kGroupM2);
-    const int r = t - group * per_group;
-    mb = first_m + r % gsize;
-    nb = r / gsize;
-}
 
 template <MmaKind KIND, int EPI, bool A_SIGNED, bool B_SIGNED, bool B_MN = false>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -735,7 +737,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t armed = 0, armed_phase = 0;
             for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
                 int mb, nb;
-                tile_coords2(t, args.tiles_m, args.tiles_n, mb, nb);
+                tile_coords(t, args, mb, nb);
                 const int row0 = mb * 256 + (int)rank * 128;
                 const int col0 = nb * kTileN + (int)rank * 128;
                 for (int kb = 0; kb < args.num_kb; kb++) {
@@ -840,7 +842,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = pair; t < num_tiles && !__any_sync(0xffffffffu, *abort_flag);
              t += npairs, local++) {
             int mb, nb;
-            tile_coords2(t, args.tiles_m, args.tiles_n, mb, nb);
+            tile_coords(t, args, mb, nb);
             const int buf = local & 1;
             const uint32_t aphase = (local >> 1) & 1;
             const bool ok =
@@ -1052,6 +1054,38 @@ int make_mnmajor_map(CUtensorMap *map, const void *base, CUtensorMapDataType dt,
 inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
+// The rasterisation group from L2 capacity: hold a panel of one operand
+// (group blocks x K) resident in L2 while the other streams past it once per
+// group.  DRAM reads are then about   resident + streamed x groups;  the
+// orientation and group size minimising that, with the panel within
+// kL2PanelBytes (a share of the 126 MB L2 that leaves room for the streamed
+// operand and the output), are chosen.  HEXCUDA_GEMM_L2_PANEL_MB overrides the
+// panel budget (a tuning knob).
+constexpr int64_t kL2PanelBytes = 48ll << 20;
+
+void pick_raster(GemmArgs &a, int64_t bm, int64_t bn, int64_t kbytes) {
+    static int64_t budget = -1;
+    if (budget < 0) {
+        const char *e = getenv("HEXCUDA_GEMM_L2_PANEL_MB");
+        budget = e ? (int64_t)atoi(e) << 20 : kL2PanelBytes;
+    }
+    const int64_t a_blk = bm * kbytes, b_blk = bn * kbytes;
+    auto cost = [&](int64_t along, int64_t blk, int64_t across_bytes, int64_t own_bytes,
+                    int &g) {
+        g = (int)std::max<int64_t>(1, std::min<int64_t>(along, budget / std::max<int64_t>(blk, 1)));
+        const int64_t groups = (along + g - 1) / g;
+        // spread the blocks evenly over the groups
+        g = (int)((along + groups - 1) / groups);
+        return own_bytes + across_bytes * groups;
+    };
+    int gm = 1, gn = 1;
+    const int64_t a_bytes = a_blk * a.tiles_m, b_bytes = b_blk * a.tiles_n;
+    const int64_t cm = cost(a.tiles_m, a_blk, b_bytes, a_bytes, gm);
+    const int64_t cn = cost(a.tiles_n, b_blk, a_bytes, b_bytes, gn);
+    a.group_n_major = cn < cm ? 1 : 0;
+    a.group = cn < cm ? gn : gm;
+}
+
 template <MmaKind KIND, int BN, int EPI, bool AS, bool BS, bool BMN = false>
 int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K,
                        const EpiParams &ep) {
@@ -1073,6 +1107,7 @@ int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int
     args.num_kb = (K + kelems - 1) / kelems;
     args.err_word = d->err_word;
     args.epi = ep;
+    pick_raster(args, kBM, BN, (int64_t)args.num_kb * kBKBytes);
     int tiles = args.tiles_m * args.tiles_n;
     int grid = tiles < d->sms ? tiles : d->sms;
     kern<<<grid, kThreads, L::kTotal, d->stream>>>(ta, tb, args);
@@ -1124,6 +1159,7 @@ int launch_gemm2_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, in
     args.num_kb = (K + kelems - 1) / kelems;
     args.err_word = d->err_word;
     args.epi = ep;
+    pick_raster(args, 256, 256, (int64_t)args.num_kb * kBKBytes);
     const int tiles = args.tiles_m * args.tiles_n;
     const int pairs = tiles < pairs_resident[dev_slot] ? tiles : pairs_resident[dev_slot];
     cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
@@ -1146,6 +1182,29 @@ bool gemm_pair_enabled(int M, int N) {
     if (e && e[0] == '0') return false;
     if (e && e[0] == '1') return true;
     return EPI != kEpiRequant;
+}
+
+// 128-column tiles instead of 256-column ones: always for N <= 128, and when
+// the 256-column grid would leave the last of few waves mostly empty -- the
+// narrow tiles then finish sooner although each runs at about kNarrowEff of
+// the wide tile's rate (two 128 x 128 accumulators reuse each A stage half as
+// often).  E.g. 2048 x 8192 (one of eight row shards of the 16384-row GEMM):
+// 512 wide tiles = 4 waves of 148 SMs, 3.46 of them busy; 1024 narrow tiles =
+// 7 waves.  HEXCUDA_GEMM_BN=128 / 256 forces either (a tuning knob).
+constexpr double kNarrowEff = 0.92;
+
+bool narrow_tiles(const Dev *d, int M, int N) {
+    if (N <= 128) return true;
+    static int force = -1;
+    if (force < 0) {
+        const char *e = getenv("HEXCUDA_GEMM_BN");
+        force = e ? atoi(e) : 0;
+    }
+    if (force == 128 || force == 256) return force == 128;
+    const int64_t tm = (M + kBM - 1) / kBM;
+    const int64_t waves_w = (tm * ((N + 255) / 256) + d->sms - 1) / d->sms;
+    const int64_t waves_n = (tm * ((N + 127) / 128) + d->sms - 1) / d->sms;
+    return waves_n * 0.5 / kNarrowEff < (double)waves_w;
 }
 
 // Common driver: A [M,K] K-major (pitch lda elements), B given either as
@@ -1259,13 +1318,14 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
         if (rc) return rc;
         if (launched) return launch_end(d, name, nl + 1);
     }
+    const bool narrow = narrow_tiles(d, M, N);
     if (b_mn) {
         if ((rc = make_mnmajor_map(&tb, B, dt, esize, N, K, kelems))) return rc;
-        if (N <= 128)
+        if (narrow)
             rc = launch_gemm_kernel<KIND, 128, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep);
         else
             rc = launch_gemm_kernel<KIND, 256, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep);
-    } else if (N <= 128) {
+    } else if (narrow) {
         if ((rc = make_kmajor_map(&tb, bt, dt, esize, b_kdim, N, bt_pitch, 128))) return rc;
         rc = launch_gemm_kernel<KIND, 128, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep);
     } else {

@@ -798,9 +798,9 @@ def time_device(wl, torch, device, steps, warmup, dist, lib):
     """Timed region: barrier + sync, K steps back to back on torch's current
     stream between one start and one end CUDA event, sync + barrier.  An
     event recorded between launches costs a few microseconds of stream time,
-    so the library's own per-launch events are off here and the per-kernel
-    durations (for the roofline) come from a second pass of the same K steps
-    with an event pair around each launch.  Returns a dict."""
+    so the library's own per-launch events are off here; a second pass of the
+    same K steps with an event pair around each launch splits the step time
+    between the kernels (for the roofline).  Returns a dict."""
     kernels = wl.kernels()
     for _ in range(warmup):
         for k in range(len(kernels)):
@@ -837,10 +837,13 @@ def time_device(wl, torch, device, steps, warmup, dist, lib):
         device.sync(0)
     finally:
         lib.hexcuda_set_timing(1)
-    per_kernel = []
-    for k, (label, units) in enumerate(kernels):
-        dur = [ev[s][k][0].elapsed_time(ev[s][k][1]) for s in range(steps)]
-        per_kernel.append((label, units, float(np.mean(dur))))
+    # A kernel's duration: its share of the event-free step (the second pass
+    # only splits the step between the kernels; it runs later, on a GPU that
+    # may have settled to lower power-capped clocks, and with event overhead)
+    raw = [float(np.mean([ev[s][k][0].elapsed_time(ev[s][k][1]) for s in range(steps)]))
+           for k in range(len(kernels))]
+    per_kernel = [(label, units, ms / steps * raw[k] / sum(raw))
+                  for k, (label, units) in enumerate(kernels)]
     return {"ms": ms, "per_kernel": per_kernel, "clocks": clk.summary(), "launches": launches}
 
 

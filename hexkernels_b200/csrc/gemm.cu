@@ -1184,27 +1184,19 @@ bool gemm_pair_enabled(int M, int N) {
     return EPI != kEpiRequant;
 }
 
-// 128-column tiles instead of 256-column ones: always for N <= 128, and when
-// the 256-column grid would leave the last of few waves mostly empty -- the
-// narrow tiles then finish sooner although each runs at about kNarrowEff of
-// the wide tile's rate (two 128 x 128 accumulators reuse each A stage half as
-// often).  E.g. 2048 x 8192 (one of eight row shards of the 16384-row GEMM):
-// 512 wide tiles = 4 waves of 148 SMs, 3.46 of them busy; 1024 narrow tiles =
-// 7 waves.  HEXCUDA_GEMM_BN=128 / 256 forces either (a tuning knob).
-constexpr double kNarrowEff = 0.92;
-
-bool narrow_tiles(const Dev *d, int M, int N) {
-    if (N <= 128) return true;
+// 128-column tiles for N <= 128, 256-column ones otherwise.  (On a
+// 2048 x 8192 x 8192 row shard, where 256-column tiles leave the last of four
+// waves half empty, 128-column tiles measured 23 % slower all the same: they
+// reuse each A stage half as often.)  HEXCUDA_GEMM_BN=128 / 256 forces either
+// (a tuning knob).
+bool narrow_tiles(int N) {
     static int force = -1;
     if (force < 0) {
         const char *e = getenv("HEXCUDA_GEMM_BN");
         force = e ? atoi(e) : 0;
     }
     if (force == 128 || force == 256) return force == 128;
-    const int64_t tm = (M + kBM - 1) / kBM;
-    const int64_t waves_w = (tm * ((N + 255) / 256) + d->sms - 1) / d->sms;
-    const int64_t waves_n = (tm * ((N + 127) / 128) + d->sms - 1) / d->sms;
-    return waves_n * 0.5 / kNarrowEff < (double)waves_w;
+    return N <= 128;
 }
 
 // Common driver: A [M,K] K-major (pitch lda elements), B given either as
@@ -1318,7 +1310,7 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
         if (rc) return rc;
         if (launched) return launch_end(d, name, nl + 1);
     }
-    const bool narrow = narrow_tiles(d, M, N);
+    const bool narrow = narrow_tiles(N);
     if (b_mn) {
         if ((rc = make_mnmajor_map(&tb, B, dt, esize, N, K, kelems))) return rc;
         if (narrow)

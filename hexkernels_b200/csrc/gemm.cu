@@ -592,6 +592,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
+        // The column sums come from the kernel launched just before this one,
+        // which may still be running (programmatic dependent launch): wait
+        // for it before the first epilogue (a no-op without a prerequisite).
+        if (args.epi.colsum) tc::grid_dependency_wait();
         // ---------------- epilogue warps 2..9: TMEM lane quarter = warp % 4,
         // column half = (warp - 2) / 4.  Every decision below is warp-uniform
         // (__all_sync / __any_sync), so the .sync.aligned TMEM loads always run
@@ -832,6 +836,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
+        // The column sums come from the kernel launched just before this one,
+        // which may still be running (programmatic dependent launch): wait
+        // for it before the first epilogue (a no-op without a prerequisite).
+        if (args.epi.colsum) tc::grid_dependency_wait();
         // ---------------- epilogue warps 2..9 of both CTAs: this CTA's 128
         // rows of the tile, all 256 columns (warp halves as gemm_tc_kernel)
         const int q = warp & 3;
@@ -946,6 +954,7 @@ __global__ void __launch_bounds__(256) pad_rows_kernel(const T *__restrict__ src
 __global__ void __launch_bounds__(128) colsum_kernel(const int8_t *__restrict__ B,
                                                      int32_t *__restrict__ colsum, int K, int N,
                                                      int kchunk, int vec) {
+    tc::launch_dependents();
     const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * 16;
     if (n0 >= N) return;
     const int k0 = blockIdx.y * kchunk, k1 = min(K, k0 + kchunk);
@@ -971,6 +980,7 @@ __global__ void __launch_bounds__(128) colsum_kernel(const int8_t *__restrict__ 
 __global__ void __launch_bounds__(256) rowsum_i8_kernel(const int8_t *__restrict__ Bt,
                                                         int64_t ldb, int32_t *__restrict__ colsum,
                                                         int N, int K, int vec) {
+    tc::launch_dependents();
     const int n = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (n >= N) return;
@@ -1088,7 +1098,7 @@ void pick_raster(GemmArgs &a, int64_t bm, int64_t bn, int64_t kbytes) {
 
 template <MmaKind KIND, int BN, int EPI, bool AS, bool BS, bool BMN = false>
 int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K,
-                       const EpiParams &ep) {
+                       const EpiParams &ep, bool pdl = false) {
     using L = Smem<BN>;
     auto kern = gemm_tc_kernel<KIND, BN, EPI, AS, BS, BMN>;
     static bool attr_done[64] = {};
@@ -1110,7 +1120,23 @@ int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int
     pick_raster(args, kBM, BN, (int64_t)args.num_kb * kBKBytes);
     int tiles = args.tiles_m * args.tiles_n;
     int grid = tiles < d->sms ? tiles : d->sms;
-    kern<<<grid, kThreads, L::kTotal, d->stream>>>(ta, tb, args);
+    if (pdl) {
+        // a programmatic dependent of the column-sum pass launched just before
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)grid, 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = L::kTotal;
+        cfg.stream = d->stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (int rc = check(cudaLaunchKernelEx(&cfg, kern, ta, tb, args), "launch gemm kernel"))
+            return rc;
+    } else {
+        kern<<<grid, kThreads, L::kTotal, d->stream>>>(ta, tb, args);
+    }
     note_mech(kMechTcgen05 | kMechTma);
     return HEXCUDA_OK;
 }
@@ -1121,16 +1147,19 @@ int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int
 // the one-SM kernel.
 template <MmaKind KIND, int EPI, bool AS, bool BS, bool BMN = false>
 int launch_gemm2_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K,
-                        const EpiParams &ep, bool *launched) {
+                        const EpiParams &ep, bool *launched, bool pdl = false) {
     using L = Smem2;
     auto kern = gemm_tc2_kernel<KIND, EPI, AS, BS, BMN>;
     static int pairs_resident[64] = {};     // 0: not queried yet, -1: none
     const int dev_slot = d->ordinal & 63;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    // optionally a programmatic dependent of the column-sum pass before it
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = L::kTotal;
@@ -1163,6 +1192,7 @@ int launch_gemm2_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, in
     const int tiles = args.tiles_m * args.tiles_n;
     const int pairs = tiles < pairs_resident[dev_slot] ? tiles : pairs_resident[dev_slot];
     cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+    cfg.numAttrs = pdl ? 2 : 1;
     if (int rc = check(cudaLaunchKernelEx(&cfg, kern, ta, tb, args), "launch gemm pair kernel"))
         return rc;
     note_mech(kMechTcgen05 | kMechTma);
@@ -1225,6 +1255,10 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
 
     launch_begin(d);
     int nl = 0;
+    // The GEMM may start as a programmatic dependent (its mainloop overlapping
+    // the previous kernel) only when that kernel is the column-sum pass, whose
+    // output it reads in the epilogue, after griddepcontrol.wait.
+    bool pdl = false;
     // ---- B operand
     const T *bt = reinterpret_cast<const T *>(B);
     int64_t bt_pitch = (int64_t)K * esize, b_kdim = K;
@@ -1242,6 +1276,7 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
         rowsum_i8_kernel<<<(unsigned)((N + 7) / 8), 256, 0, d->stream>>>(
             reinterpret_cast<const int8_t *>(B), K, colsum, N, K, vec ? 1 : 0);
         nl++;
+        pdl = true;
     }
     // row-major B that TMA can read in place: MN-major operand, no copy
     const bool b_mn = !b_kmajor && ((int64_t)N * esize) % 16 == 0 && aligned16(B) &&
@@ -1253,6 +1288,7 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
             colsum_kernel<<<g, 128, 0, d->stream>>>(reinterpret_cast<const int8_t *>(B), colsum, K,
                                                      N, kchunk, 1);
             nl++;
+            pdl = true;
         }
     } else if (!b_kmajor) {
         T *tmp = reinterpret_cast<T *>(scratch(d, 0, (size_t)N * Kp * esize));
@@ -1265,6 +1301,7 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
             transpose_pack_kernel<T, false><<<g, 256, 0, d->stream>>>(
                 reinterpret_cast<const T *>(B), tmp, nullptr, K, N, N, Kp);
         nl++;
+        pdl = false;
         bt = tmp;
         bt_pitch = Kp * esize;
         b_kdim = Kp;
@@ -1274,6 +1311,7 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
         pad_rows_kernel<T><<<(unsigned)std::min<int64_t>((N * Kp + 255) / 256, 4096), 256, 0,
                              d->stream>>>(reinterpret_cast<const T *>(B), K, tmp, Kp, N, K);
         nl++;
+        pdl = false;
         bt = tmp;
         bt_pitch = Kp * esize;
         b_kdim = Kp;
@@ -1287,10 +1325,17 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
         pad_rows_kernel<T><<<(unsigned)std::min<int64_t>((M * Kp + 255) / 256, 4096), 256, 0,
                              d->stream>>>(reinterpret_cast<const T *>(A), lda, tmp, Kp, M, K);
         nl++;
+        pdl = false;
         a = tmp;
         a_pitch = Kp * esize;
         a_kdim = Kp;
     }
+    // Overlapping the column-sum pass pays on short GEMMs (a 2048 x 8192 x
+    // 8192 row shard: 0.152 -> 0.144 ms) and costs on long ones, whose early
+    // CTAs then compete with the pass for DRAM and hold their first
+    // accumulators until it ends (16384 x 8192 x 8192: 0.784 -> 0.800 ms):
+    // only GEMMs of at most 8 waves of 128 x 256 tiles take it.
+    if (pdl && (int64_t)((M + kBM - 1) / kBM) * ((N + 255) / 256) > 8ll * d->sms) pdl = false;
     CUtensorMap ta, tb;
     if (int rc = make_kmajor_map(&ta, a, dt, esize, a_kdim, M, a_pitch, kBM)) return rc;
     ep.colsum = colsum;
@@ -1302,10 +1347,11 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
         bool launched = false;
         if (b_mn) {
             if ((rc = make_mnmajor_map(&tb, B, dt, esize, N, K, kelems))) return rc;
-            rc = launch_gemm2_kernel<KIND, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep, &launched);
+            rc = launch_gemm2_kernel<KIND, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep, &launched,
+                                                              pdl);
         } else {
             if ((rc = make_kmajor_map(&tb, bt, dt, esize, b_kdim, N, bt_pitch, 128))) return rc;
-            rc = launch_gemm2_kernel<KIND, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep, &launched);
+            rc = launch_gemm2_kernel<KIND, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep, &launched, pdl);
         }
         if (rc) return rc;
         if (launched) return launch_end(d, name, nl + 1);
@@ -1314,15 +1360,15 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
     if (b_mn) {
         if ((rc = make_mnmajor_map(&tb, B, dt, esize, N, K, kelems))) return rc;
         if (narrow)
-            rc = launch_gemm_kernel<KIND, 128, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep);
+            rc = launch_gemm_kernel<KIND, 128, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep, pdl);
         else
-            rc = launch_gemm_kernel<KIND, 256, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep);
+            rc = launch_gemm_kernel<KIND, 256, EPI, AS, BS, true>(d, ta, tb, M, N, kdim, ep, pdl);
     } else if (narrow) {
         if ((rc = make_kmajor_map(&tb, bt, dt, esize, b_kdim, N, bt_pitch, 128))) return rc;
-        rc = launch_gemm_kernel<KIND, 128, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep);
+        rc = launch_gemm_kernel<KIND, 128, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep, pdl);
     } else {
         if ((rc = make_kmajor_map(&tb, bt, dt, esize, b_kdim, N, bt_pitch, 256))) return rc;
-        rc = launch_gemm_kernel<KIND, 256, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep);
+        rc = launch_gemm_kernel<KIND, 256, EPI, AS, BS>(d, ta, tb, M, N, kdim, ep, pdl);
     }
     if (rc) return rc;
     return launch_end(d, name, nl + 1);

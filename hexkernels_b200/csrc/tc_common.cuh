@@ -159,6 +159,16 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
 }
+// Programmatic dependent launch: a primary kernel lets the grid launched
+// after it on the stream start early; the dependent grid waits here until
+// the primary grid has finished and its memory writes are visible (a no-op
+// when the grid was launched without a prerequisite).
+__device__ __forceinline__ void launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
 // 3D tiled load into this CTA only.
 __device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
                                             int x, int y, int z) {

@@ -1069,9 +1069,12 @@ inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 // group.  DRAM reads are then about   resident + streamed x groups;  the
 // orientation and group size minimising that, with the panel within
 // kL2PanelBytes (a share of the 126 MB L2 that leaves room for the streamed
-// operand and the output), are chosen.  HEXCUDA_GEMM_L2_PANEL_MB overrides the
-// panel budget (a tuning knob).
-constexpr int64_t kL2PanelBytes = 48ll << 20;
+// operand and the output), are chosen.  Measured DRAM reads of the
+// 16384 x 8192 x 8192 u8 x s8 GEMM per panel budget: 24 MB 474 MB, 32 MB
+// 406, 40 MB 401 (modelled 384), 48 MB 488-509 (modelled 320: the panel is
+// no longer kept), 64 MB 1506; the time is flat from 24 to 48 MB.
+// HEXCUDA_GEMM_L2_PANEL_MB overrides the panel budget (a tuning knob).
+constexpr int64_t kL2PanelBytes = 40ll << 20;
 
 void pick_raster(GemmArgs &a, int64_t bm, int64_t bn, int64_t kbytes) {
     static int64_t budget = -1;

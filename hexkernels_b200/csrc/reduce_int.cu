@@ -230,6 +230,9 @@ __global__ void __launch_bounds__(256) reduce_int_kernel(const void *__restrict_
     const uint4 *vb = reinterpret_cast<const uint4 *>(b);
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    // the one-block finalize launched after this kernel may start now (it
+    // waits for this grid's partials before reading them)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     RedPart p = red_identity<OP>();
     int64_t done = 0;
     if (vec) {
@@ -312,6 +315,10 @@ template <int OP>
 __global__ void __launch_bounds__(256) red_finalize_kernel(const RedPart *__restrict__ part,
                                                            int nparts, int64_t n, long long base,
                                                            RedPart *one, void *out) {
+    // launched as a programmatic dependent of the block-partials kernel: wait
+    // until that grid has finished and its partials are visible (a no-op when
+    // launched without one)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     RedPart p = red_identity<OP>();
     for (int i = threadIdx.x; i < nparts; i += blockDim.x) p = red_combine<OP>(p, part[i]);
     p = red_block<OP>(p);
@@ -337,7 +344,21 @@ int reduce_launch(Dev *d, const void *a, const void *b, int64_t n, long long bas
     if (!part) return HEXCUDA_ERR_OOM;
     launch_begin(d);
     if (blocks > 0) kern<<<blocks, 256, 0, d->stream>>>(a, b, n, vec, part);
-    red_finalize_kernel<OP><<<1, 256, 0, d->stream>>>(part, blocks, n, base, one, out);
+    // the finalize as a programmatic dependent: its launch overlaps the
+    // partials kernel's tail instead of following it
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = d->stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = blocks > 0 ? 1 : 0;
+    if (int rc = check(cudaLaunchKernelEx(&cfg, red_finalize_kernel<OP>, (const RedPart *)part,
+                                          blocks, n, base, one, out),
+                       "launch reduce finalize"))
+        return rc;
     return launch_end(d, "reduce_int", blocks > 0 ? 2 : 1);
 }
 

@@ -53,6 +53,7 @@ constexpr int kBKBytes = 128;        // K extent of one stage, in bytes
 constexpr int kStages = 4;
 constexpr int kThreads = 320;      // TMA warp, MMA warp, 8 epilogue warps
 constexpr int kColParamBytes = 6 * 32 * 4;   // one epilogue warp's ColParams
+constexpr int kStoreStageBytes = 32 * 64;    // 32 rows x 64 B, one epilogue warp
 
 enum EpiKind { kEpiF16 = 0, kEpiRequant = 1, kEpiHmx = 2, kEpiF16Ex = 3 };
 
@@ -126,7 +127,9 @@ struct Smem {
     // read with 16-byte loads, so the region starts on a 128-byte boundary
     static constexpr int kParamOffset = (kBarOffset + kNumBars * 8 + 16 + 127) / 128 * 128;
     static constexpr int kParamBytes = 8 * kColParamBytes;
-    static constexpr int kTotal = kParamOffset + kParamBytes + 1024;  // + align slack
+    // per epilogue warp: a 2 KB staging block for coalesced 4-byte stores
+    static constexpr int kStoreOffset = kParamOffset + kParamBytes;
+    static constexpr int kTotal = kStoreOffset + 8 * kStoreStageBytes + 1024;  // + align slack
 };
 
 // Tile t -> (M-block, N-block): groups of `group` blocks of the resident
@@ -196,10 +199,70 @@ __device__ __forceinline__ void requant_chunk(const EpiParams &ep, const uint32_
     }
 }
 
+// The 32 x 64-byte block of a warp (lane i holding row row0 + i, 16 words)
+// stored with each row written by 4 consecutive lanes: staged through the
+// warp's 2 KB of shared memory (16-byte chunks XOR-swizzled by row pair, so
+// neither the row-wise writes nor the chunk-wise reads conflict), then 8 rows
+// of 64 contiguous bytes per store instruction instead of 32 scattered 16-byte
+// pieces.  Rows at or past `nrows` are not stored.
+__device__ __forceinline__ void store_block_coalesced(const uint32_t (&w)[16], uint4 *stage,
+                                                      uint8_t *g_row0, size_t ld_bytes,
+                                                      int nrows) {
+    const int lane = threadIdx.x & 31;
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+        stage[lane * 4 + (c ^ ((lane >> 1) & 3))] =
+            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int pass = 0; pass < 4; pass++) {
+        const int rr = pass * 8 + (lane >> 2), c = lane & 3;
+        const uint4 val = stage[rr * 4 + (c ^ ((rr >> 1) & 3))];
+        if (rr < nrows) *reinterpret_cast<uint4 *>(g_row0 + (size_t)rr * ld_bytes + c * 16) = val;
+    }
+}
+
+// The same for 32 rows of 32 bytes (lane i: row row0 + i, 8 words): 16-byte
+// chunks swizzled by row quad; each store instruction writes 16 rows of 32
+// contiguous bytes.
+__device__ __forceinline__ void store_block32_coalesced(const uint32_t (&w)[8], uint4 *stage,
+                                                        uint8_t *g_row0, size_t ld_bytes,
+                                                        int nrows) {
+    const int lane = threadIdx.x & 31;
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 2; c++)
+        stage[lane * 2 + (c ^ ((lane >> 2) & 1))] =
+            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int pass = 0; pass < 2; pass++) {
+        const int rr = pass * 16 + (lane >> 1), c = lane & 1;
+        const uint4 val = stage[rr * 2 + (c ^ ((rr >> 2) & 1))];
+        if (rr < nrows) *reinterpret_cast<uint4 *>(g_row0 + (size_t)rr * ld_bytes + c * 16) = val;
+    }
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32_t (&r)[32],
-                                               int row, int col0, const ColParams *cp) {
+                                               int row, int col0, const ColParams *cp,
+                                               uint4 *stage) {
     if constexpr (EPI == kEpiF16) {
+        const int lane = threadIdx.x & 31;
+        __half *o0 = reinterpret_cast<__half *>(ep.out) + (size_t)(row - lane) * ep.ldo + col0;
+        if (col0 + 32 <= ep.N && (ep.ldo & 7) == 0 && (reinterpret_cast<uintptr_t>(o0) & 15u) == 0) {
+            // warp-uniform: the warp's 32 rows x 32 fp16 through the staging block
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                __half2 h = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                w[i] = *reinterpret_cast<uint32_t *>(&h);
+            }
+            store_block_coalesced(w, stage, reinterpret_cast<uint8_t *>(o0), (size_t)ep.ldo * 2,
+                                  min(32, ep.M - (row - lane)));
+            return;
+        }
         if (row >= ep.M) return;
         __half *o = reinterpret_cast<__half *>(ep.out) + (size_t)row * ep.ldo + col0;
         if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
@@ -217,9 +280,9 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             for (int i = 0; i < 32 && col0 + i < ep.N; i++) o[i] = __float2half_rn(__uint_as_float(r[i]));
         }
     } else if constexpr (EPI == kEpiF16Ex) {
-        if (row >= ep.M) return;
-        __half *o = reinterpret_cast<__half *>(ep.out) + (size_t)row * ep.ldo + col0;
-        const __half *rr = ep.f16_res ? ep.f16_res + (size_t)row * ep.N + col0 : nullptr;
+        // rows past M compute on (unused) accumulators and store nothing
+        const __half *rr =
+            (ep.f16_res && row < ep.M) ? ep.f16_res + (size_t)row * ep.N + col0 : nullptr;
         __half hv[32];
 #pragma unroll
         for (int i = 0; i < 32; i++) {
@@ -245,6 +308,19 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             }
             hv[i] = __float2half_rn(v * ep.f16_scale);
         }
+        const int lane = threadIdx.x & 31;
+        __half *o0 = reinterpret_cast<__half *>(ep.out) + (size_t)(row - lane) * ep.ldo + col0;
+        if (col0 + 32 <= ep.N && (ep.ldo & 7) == 0 && (reinterpret_cast<uintptr_t>(o0) & 15u) == 0) {
+            // warp-uniform: the warp's 32 rows x 32 fp16 through the staging block
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) w[i] = reinterpret_cast<const uint32_t *>(hv)[i];
+            store_block_coalesced(w, stage, reinterpret_cast<uint8_t *>(o0), (size_t)ep.ldo * 2,
+                                  min(32, ep.M - (row - lane)));
+            return;
+        }
+        if (row >= ep.M) return;
+        __half *o = reinterpret_cast<__half *>(ep.out) + (size_t)row * ep.ldo + col0;
         if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
             const uint4 *src = reinterpret_cast<const uint4 *>(hv);
             uint4 *dst = reinterpret_cast<uint4 *>(o);
@@ -331,11 +407,49 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
                 v[4 * i4 + u] = x;
             }
         }
-        if (row >= ep.M) return;
         const int es = (ep.hmx_store == HEXCUDA_HMX_STORE_I32 ||
                         ep.hmx_store == HEXCUDA_HMX_STORE_LUT_I32 ||
                         ep.hmx_store == HEXCUDA_HMX_STORE_ACC_I32) ? 4
                        : ep.hmx_store == HEXCUDA_HMX_STORE_U16_FIELD ? 2 : 1;
+        const int lane = threadIdx.x & 31;
+        int32_t *o0 = reinterpret_cast<int32_t *>(ep.out) + (size_t)(row - lane) * ep.ldo + col0;
+        // (warp-uniform: col0, the row block and the pointers are the same in
+        // every lane of the warp)
+        if (es == 4 && !ep.col_major && full && (ep.ldo & 3) == 0 &&
+            (reinterpret_cast<uintptr_t>(o0) & 15u) == 0) {
+            // 32 rows x 32 int32: two 64-byte halves through the staging block
+            const int nrows = min(32, ep.M - (row - lane));
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; i++) w[i] = (uint32_t)v[16 * half + i];
+                store_block_coalesced(w, stage, reinterpret_cast<uint8_t *>(o0 + 16 * half),
+                                      (size_t)ep.ldo * 4, nrows);
+            }
+            return;
+        }
+        uint8_t *ob0 = reinterpret_cast<uint8_t *>(ep.out) + ((size_t)(row - lane) * ep.ldo + col0) * es;
+        if (es < 4 && !ep.col_major && full && ((ep.ldo * es) & 15) == 0 &&
+            (reinterpret_cast<uintptr_t>(ob0) & 15u) == 0) {
+            const int nrows = min(32, ep.M - (row - lane));
+            if (es == 2) {
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 16; i++)
+                    w[i] = ((uint32_t)v[2 * i] & 0xFFFFu) | ((uint32_t)v[2 * i + 1] << 16);
+                store_block_coalesced(w, stage, ob0, (size_t)ep.ldo * 2, nrows);
+            } else {
+                uint32_t w[8];
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+                    w[i] = ((uint32_t)v[4 * i] & 0xFFu) | (((uint32_t)v[4 * i + 1] & 0xFFu) << 8) |
+                           (((uint32_t)v[4 * i + 2] & 0xFFu) << 16) | ((uint32_t)v[4 * i + 3] << 24);
+                store_block32_coalesced(w, stage, ob0, (size_t)ep.ldo, nrows);
+            }
+            return;
+        }
+        if (row >= ep.M) return;
         if (ep.col_major) {
             // lanes are consecutive rows: each column's store is one
             // contiguous run across the warp
@@ -395,8 +509,7 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             requant_chunk<true>(ep, r, cp, w);
         else
             requant_chunk<false>(ep, r, cp, w);
-        if (row >= ep.M) return;
-        if (ep.rq_res) {
+        if (ep.rq_res && row < ep.M) {
             // q = sat8(q + res[i][j]): one signed saturating byte add per 4
             const int8_t *rp = ep.rq_res + (size_t)row * ep.N + col0;
 #pragma unroll
@@ -407,6 +520,14 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
                 w[i4] = __vaddss4(w[i4], rw);
             }
         }
+        const int lane = threadIdx.x & 31;
+        uint8_t *o0 = o - (size_t)lane * ep.ldo;
+        if (col0 + 32 <= ep.N && (ep.ldo & 15) == 0 && (reinterpret_cast<uintptr_t>(o0) & 15u) == 0) {
+            // warp-uniform: the warp's 32 rows x 32 bytes through the staging block
+            store_block32_coalesced(w, stage, o0, (size_t)ep.ldo, min(32, ep.M - (row - lane)));
+            return;
+        }
+        if (row >= ep.M) return;
         if (col0 + 32 <= ep.N && ((reinterpret_cast<uintptr_t>(o) & 15u) == 0)) {
             uint4 *dst = reinterpret_cast<uint4 *>(o);
             dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -603,6 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;
         const int chalf = (warp - 2) >> 2;
         ColParams *cp = reinterpret_cast<ColParams *>(smem + L::kParamOffset) + (warp - 2);
+        uint4 *stage = reinterpret_cast<uint4 *>(smem + L::kStoreOffset + (warp - 2) * kStoreStageBytes);
         int local = 0;
         for (int t = blockIdx.x; t < num_tiles && !__any_sync(0xffffffffu, *abort_flag);
              t += gridDim.x, local++) {
@@ -625,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
                 tc::tmem_ld_wait(r);
-                epilogue_chunk<EPI>(args.epi, r, row, nb * BN + c, cp);
+                epilogue_chunk<EPI>(args.epi, r, row, nb * BN + c, cp, stage);
                 __syncwarp();
             }
             tc::tc_fence_before();
@@ -670,7 +792,8 @@ struct Smem2 {
     static constexpr int kNumBars = 2 * kStages2 + 5;
     static constexpr int kParamOffset = (kBarOffset + kNumBars * 8 + 16 + 127) / 128 * 128;
     static constexpr int kParamBytes = 8 * kColParamBytes;
-    static constexpr int kTotal = kParamOffset + kParamBytes + 1024;
+    static constexpr int kStoreOffset = kParamOffset + kParamBytes;
+    static constexpr int kTotal = kStoreOffset + 8 * kStoreStageBytes + 1024;
 };
 static_assert(Smem2::kTotal <= 227 * 1024, "pair-kernel shared memory");
 
@@ -845,6 +968,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;
         const int chalf = (warp - 2) >> 2;
         ColParams *cp = reinterpret_cast<ColParams *>(smem + L::kParamOffset) + (warp - 2);
+        uint4 *stage = reinterpret_cast<uint4 *>(smem + L::kStoreOffset + (warp - 2) * kStoreStageBytes);
         const uint32_t tempty_even = tc::mapa_shared(tc::smem_u32(tempty), 0);
         int local = 0;
         for (int t = pair; t < num_tiles && !__any_sync(0xffffffffu, *abort_flag);
@@ -869,7 +993,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
                 tc::tmem_ld_wait(r);
-                epilogue_chunk<EPI>(args.epi, r, row, nb * kTileN + c, cp);
+                epilogue_chunk<EPI>(args.epi, r, row, nb * kTileN + c, cp, stage);
                 __syncwarp();
             }
             tc::tc_fence_before();

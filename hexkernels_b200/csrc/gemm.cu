@@ -199,51 +199,6 @@ __device__ __forceinline__ void requant_chunk(const EpiParams &ep, const uint32_
     }
 }
 
-// The 32 x 64-byte block of a warp (lane i holding row row0 + i, 16 words)
-// stored with each row written by 4 consecutive lanes: staged through the
-// warp's 2 KB of shared memory (16-byte chunks XOR-swizzled by row pair, so
-// neither the row-wise writes nor the chunk-wise reads conflict), then 8 rows
-// of 64 contiguous bytes per store instruction instead of 32 scattered 16-byte
-// pieces.  Rows at or past `nrows` are not stored.
-__device__ __forceinline__ void store_block_coalesced(const uint32_t (&w)[16], uint4 *stage,
-                                                      uint8_t *g_row0, size_t ld_bytes,
-                                                      int nrows) {
-    const int lane = threadIdx.x & 31;
-    __syncwarp();
-#pragma unroll
-    for (int c = 0; c < 4; c++)
-        stage[lane * 4 + (c ^ ((lane >> 1) & 3))] =
-            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-    __syncwarp();
-#pragma unroll
-    for (int pass = 0; pass < 4; pass++) {
-        const int rr = pass * 8 + (lane >> 2), c = lane & 3;
-        const uint4 val = stage[rr * 4 + (c ^ ((rr >> 1) & 3))];
-        if (rr < nrows) *reinterpret_cast<uint4 *>(g_row0 + (size_t)rr * ld_bytes + c * 16) = val;
-    }
-}
-
-// The same for 32 rows of 32 bytes (lane i: row row0 + i, 8 words): 16-byte
-// chunks swizzled by row quad; each store instruction writes 16 rows of 32
-// contiguous bytes.
-__device__ __forceinline__ void store_block32_coalesced(const uint32_t (&w)[8], uint4 *stage,
-                                                        uint8_t *g_row0, size_t ld_bytes,
-                                                        int nrows) {
-    const int lane = threadIdx.x & 31;
-    __syncwarp();
-#pragma unroll
-    for (int c = 0; c < 2; c++)
-        stage[lane * 2 + (c ^ ((lane >> 2) & 1))] =
-            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-    __syncwarp();
-#pragma unroll
-    for (int pass = 0; pass < 2; pass++) {
-        const int rr = pass * 16 + (lane >> 1), c = lane & 1;
-        const uint4 val = stage[rr * 2 + (c ^ ((rr >> 2) & 1))];
-        if (rr < nrows) *reinterpret_cast<uint4 *>(g_row0 + (size_t)rr * ld_bytes + c * 16) = val;
-    }
-}
-
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32_t (&r)[32],
                                                int row, int col0, const ColParams *cp,
@@ -259,7 +214,7 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
                 __half2 h = __floats2half2_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
                 w[i] = *reinterpret_cast<uint32_t *>(&h);
             }
-            store_block_coalesced(w, stage, reinterpret_cast<uint8_t *>(o0), (size_t)ep.ldo * 2,
+            tc::store_block_coalesced(w, stage, reinterpret_cast<uint8_t *>(o0), (size_t)ep.ldo * 2,
                                   min(32, ep.M - (row - lane)));
             return;
         }
@@ -315,7 +270,7 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
             uint32_t w[16];
 #pragma unroll
             for (int i = 0; i < 16; i++) w[i] = reinterpret_cast<const uint32_t *>(hv)[i];
-            store_block_coalesced(w, stage, reinterpret_cast<uint8_t *>(o0), (size_t)ep.ldo * 2,
+            tc::store_block_coalesced(w, stage, reinterpret_cast<uint8_t *>(o0), (size_t)ep.ldo * 2,
                                   min(32, ep.M - (row - lane)));
             return;
         }
@@ -424,7 +379,7 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
                 uint32_t w[16];
 #pragma unroll
                 for (int i = 0; i < 16; i++) w[i] = (uint32_t)v[16 * half + i];
-                store_block_coalesced(w, stage, reinterpret_cast<uint8_t *>(o0 + 16 * half),
+                tc::store_block_coalesced(w, stage, reinterpret_cast<uint8_t *>(o0 + 16 * half),
                                       (size_t)ep.ldo * 4, nrows);
             }
             return;
@@ -438,14 +393,14 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
 #pragma unroll
                 for (int i = 0; i < 16; i++)
                     w[i] = ((uint32_t)v[2 * i] & 0xFFFFu) | ((uint32_t)v[2 * i + 1] << 16);
-                store_block_coalesced(w, stage, ob0, (size_t)ep.ldo * 2, nrows);
+                tc::store_block_coalesced(w, stage, ob0, (size_t)ep.ldo * 2, nrows);
             } else {
                 uint32_t w[8];
 #pragma unroll
                 for (int i = 0; i < 8; i++)
                     w[i] = ((uint32_t)v[4 * i] & 0xFFu) | (((uint32_t)v[4 * i + 1] & 0xFFu) << 8) |
                            (((uint32_t)v[4 * i + 2] & 0xFFu) << 16) | ((uint32_t)v[4 * i + 3] << 24);
-                store_block32_coalesced(w, stage, ob0, (size_t)ep.ldo, nrows);
+                tc::store_block32_coalesced(w, stage, ob0, (size_t)ep.ldo, nrows);
             }
             return;
         }
@@ -524,7 +479,7 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams &ep, const uint32
         uint8_t *o0 = o - (size_t)lane * ep.ldo;
         if (col0 + 32 <= ep.N && (ep.ldo & 15) == 0 && (reinterpret_cast<uintptr_t>(o0) & 15u) == 0) {
             // warp-uniform: the warp's 32 rows x 32 bytes through the staging block
-            store_block32_coalesced(w, stage, o0, (size_t)ep.ldo, min(32, ep.M - (row - lane)));
+            tc::store_block32_coalesced(w, stage, o0, (size_t)ep.ldo, min(32, ep.M - (row - lane)));
             return;
         }
         if (row >= ep.M) return;

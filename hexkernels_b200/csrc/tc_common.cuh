@@ -438,6 +438,51 @@ __device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t
     return d;
 }
 
+// The 32 x 64-byte block of a warp (lane i holding row row0 + i, 16 words)
+// stored with each row written by 4 consecutive lanes: staged through the
+// warp's 2 KB of shared memory (16-byte chunks XOR-swizzled by row pair, so
+// neither the row-wise writes nor the chunk-wise reads conflict), then 8 rows
+// of 64 contiguous bytes per store instruction instead of 32 scattered 16-byte
+// pieces.  Rows at or past `nrows` are not stored.
+__device__ __forceinline__ void store_block_coalesced(const uint32_t (&w)[16], uint4 *stage,
+                                                      uint8_t *g_row0, size_t ld_bytes,
+                                                      int nrows) {
+    const int lane = threadIdx.x & 31;
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+        stage[lane * 4 + (c ^ ((lane >> 1) & 3))] =
+            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int pass = 0; pass < 4; pass++) {
+        const int rr = pass * 8 + (lane >> 2), c = lane & 3;
+        const uint4 val = stage[rr * 4 + (c ^ ((rr >> 1) & 3))];
+        if (rr < nrows) *reinterpret_cast<uint4 *>(g_row0 + (size_t)rr * ld_bytes + c * 16) = val;
+    }
+}
+
+// The same for 32 rows of 32 bytes (lane i: row row0 + i, 8 words): 16-byte
+// chunks swizzled by row quad; each store instruction writes 16 rows of 32
+// contiguous bytes.
+__device__ __forceinline__ void store_block32_coalesced(const uint32_t (&w)[8], uint4 *stage,
+                                                        uint8_t *g_row0, size_t ld_bytes,
+                                                        int nrows) {
+    const int lane = threadIdx.x & 31;
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 2; c++)
+        stage[lane * 2 + (c ^ ((lane >> 2) & 1))] =
+            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int pass = 0; pass < 2; pass++) {
+        const int rr = pass * 16 + (lane >> 1), c = lane & 1;
+        const uint4 val = stage[rr * 2 + (c ^ ((rr >> 2) & 1))];
+        if (rr < nrows) *reinterpret_cast<uint4 *>(g_row0 + (size_t)rr * ld_bytes + c * 16) = val;
+    }
+}
+
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major = false) {
     return (1u << 4)                          // D = f32
            | (0u << 7) | (0u << 10)           // A, B = f16

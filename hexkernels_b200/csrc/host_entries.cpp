@@ -1,9 +1,13 @@
 // host_entries.cpp -- host-pointer entry points (hexcuda_host_*): the calls
 // the candidate_kernel shims make.  Rows are split into contiguous shards,
-// one per initialised device; each shard is copied in on that device's
-// stream, computed, and only after every device finished without error copied
-// back, so a failed call leaves the caller's output untouched.  Per-column /
-// per-feature operands are replicated to every device.
+// one per initialised device.  Operators whose inputs and output are all
+// row-sharded (row operators, GEMMs along M, attention along heads, the
+// elementwise requant) pipeline each shard in chunks, copies in, kernels and
+// copies out overlapping (run_pipelined); the others copy a shard in on that
+// device's stream, compute, and only after every device finished without
+// error copy back (run_sharded).  In both, an argument or launch error leaves
+// the caller's output untouched.  Per-column / per-feature operands are
+// replicated to every device.
 #include <string.h>
 
 #include <algorithm>
@@ -105,19 +109,42 @@ int run_sharded(int64_t rows, void *host_out, size_t out_row_bytes,
     return HEXCUDA_OK;
 }
 
-// Pipelined variant for operators with one row-sharded input and one
-// row-sharded output (the HBM-bound row operators).  Each device's shard is
-// cut into up to kPipeChunks chunks of about 32 MiB; chunk k is copied in on
-// the device's input stream, computed on its launch stream once its copy
-// has landed (event), and copied out on its output stream once its kernel
-// has finished (event).  With pinned host memory the two copy directions and
-// the kernels of different chunks overlap.  All copies in and launches are
-// enqueued before any copy out, so an argument or launch error still leaves
-// the caller's output untouched.
-int run_rows_pipelined(int64_t rows, const void *host_in, size_t in_row_bytes, void *host_out,
-                       size_t out_row_bytes, const std::function<int(Part &)> &stage_replicated,
-                       const std::function<int(Part &, const void *, void *, int64_t)> &launch) {
+// One row-sharded input of a pipelined call: `host` holds the call's rows of
+// `row_bytes` bytes each; a device stages its shard in scratch slot `slot`.
+struct RowIn {
+    const void *host;
+    size_t row_bytes;
+    int slot;
+};
+constexpr int kMaxRowIns = 4;
+
+// launch(part, device inputs (one per RowIn, at the chunk's first row),
+//        device output at the chunk's first row, rows in the chunk)
+using ChunkLaunch = std::function<int(Part &, const uint8_t *const *, void *, int64_t)>;
+
+// Pipelined variant of run_sharded for operators whose inputs and output are
+// all row-sharded apart from replicated operands (the row operators, GEMMs
+// cut along M, attention cut along heads).  Each device's shard is cut into
+// up to kPipeChunks chunks of about `chunk_bytes` (counted on the larger of
+// a row's input and output bytes); chunk k is copied in on the device's input
+// stream, computed on its launch stream once its copies have landed (event),
+// and copied out on its output stream once its kernels have finished
+// (event).  With pinned host memory the two copy directions and the kernels
+// of different chunks overlap.  Chunks hold a multiple of 16 rows, so a
+// chunk starts 16-byte aligned whenever a row's bytes are a multiple of 16
+// (what the TMA operands need).  All copies in and launches are enqueued
+// before any copy out, so an argument or launch error still leaves the
+// caller's output untouched.
+int run_pipelined(int64_t rows, std::initializer_list<RowIn> in_list, void *host_out,
+                  size_t out_row_bytes, int64_t chunk_bytes,
+                  const std::function<int(Part &)> &stage_replicated, const ChunkLaunch &launch) {
     if (!ensure_init()) return HEXCUDA_ERR_NODEV;
+    const std::vector<RowIn> ins(in_list);
+    if (ins.empty() || ins.size() > (size_t)kMaxRowIns)
+        return fail(HEXCUDA_ERR_ARG, "pipelined call with %zu inputs", ins.size());
+    size_t row_bytes = out_row_bytes, in_row = 0;
+    for (const RowIn &in : ins) in_row += in.row_bytes;
+    row_bytes = std::max(row_bytes, in_row);
     const int n = ndev();
     std::vector<Part> parts;
     for (int i = 0; i < n; i++) {
@@ -126,13 +153,13 @@ int run_rows_pipelined(int64_t rows, const void *host_in, size_t in_row_bytes, v
     }
     if (parts.empty()) return HEXCUDA_OK;
     struct Plan {
-        uint8_t *din, *dout;
+        uint8_t *din[kMaxRowIns];
+        uint8_t *dout;
         int64_t chunk, nchunks;
     };
     std::vector<Plan> plans(parts.size());
     scope_begin();
     int rc = HEXCUDA_OK;
-    const int64_t target = 32ll << 20;
     for (size_t pi = 0; pi < parts.size() && !rc; pi++) {
         Part &p = parts[pi];
         Plan &pl = plans[pi];
@@ -142,15 +169,18 @@ int run_rows_pipelined(int64_t rows, const void *host_in, size_t in_row_bytes, v
             break;
         }
         const int64_t nr = p.r1 - p.r0;
-        pl.din = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotIn0, (size_t)nr * in_row_bytes));
-        pl.dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)nr * out_row_bytes));
-        if (!pl.din || !pl.dout) {
-            rc = hexcuda_last_error();
-            break;
+        for (size_t i = 0; i < ins.size() && !rc; i++) {
+            pl.din[i] = reinterpret_cast<uint8_t *>(
+                scratch(p.d, ins[i].slot, (size_t)nr * ins[i].row_bytes));
+            if (!pl.din[i]) rc = hexcuda_last_error();
         }
+        pl.dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)nr * out_row_bytes));
+        if (!rc && !pl.dout) rc = hexcuda_last_error();
+        if (rc) break;
         p.dout = pl.dout;
-        int64_t chunk = std::max<int64_t>(1, target / (int64_t)std::max<size_t>(in_row_bytes, 1));
+        int64_t chunk = std::max<int64_t>(1, chunk_bytes / (int64_t)std::max<size_t>(row_bytes, 1));
         chunk = std::max(chunk, (nr + kPipeChunks - 1) / kPipeChunks);
+        chunk = (chunk + 15) / 16 * 16;
         pl.chunk = std::min(chunk, nr);
         pl.nchunks = (nr + pl.chunk - 1) / pl.chunk;
         // replicated operands go first on the input stream, so every chunk's
@@ -159,17 +189,22 @@ int run_rows_pipelined(int64_t rows, const void *host_in, size_t in_row_bytes, v
         p.d->stream = p.d->s_in;
         rc = stage_replicated(p);
         p.d->stream = launch_stream;
+        const uint8_t *dchunk[kMaxRowIns] = {};
         for (int64_t k = 0; k < pl.nchunks && !rc; k++) {
             const int64_t c0 = k * pl.chunk, cn = std::min(pl.chunk, nr - c0);
-            rc = check(cudaMemcpyAsync(pl.din + c0 * in_row_bytes,
-                                       reinterpret_cast<const uint8_t *>(host_in) +
-                                           (p.r0 + c0) * in_row_bytes,
-                                       (size_t)cn * in_row_bytes, cudaMemcpyHostToDevice,
-                                       p.d->s_in),
-                       "h2d");
+            for (size_t i = 0; i < ins.size() && !rc; i++) {
+                const size_t rb = ins[i].row_bytes;
+                dchunk[i] = pl.din[i] + c0 * rb;
+                if (rb)
+                    rc = check(cudaMemcpyAsync(pl.din[i] + c0 * rb,
+                                               reinterpret_cast<const uint8_t *>(ins[i].host) +
+                                                   (p.r0 + c0) * rb,
+                                               (size_t)cn * rb, cudaMemcpyHostToDevice, p.d->s_in),
+                               "h2d");
+            }
             if (!rc) rc = check(cudaEventRecord(p.d->ev_in[k], p.d->s_in), "event");
             if (!rc) rc = check(cudaStreamWaitEvent(p.d->stream, p.d->ev_in[k], 0), "wait event");
-            if (!rc) rc = launch(p, pl.din + c0 * in_row_bytes, pl.dout + c0 * out_row_bytes, cn);
+            if (!rc) rc = launch(p, dchunk, pl.dout + c0 * out_row_bytes, cn);
             if (!rc) rc = check(cudaEventRecord(p.d->ev_done[k], p.d->stream), "event");
         }
     }
@@ -209,6 +244,27 @@ int run_rows_pipelined(int64_t rows, const void *host_in, size_t in_row_bytes, v
     return rc;
 }
 
+constexpr int64_t kRowChunkBytes = 32ll << 20;    // row operators
+constexpr int64_t kGemmChunkBytes = 16ll << 20;   // GEMMs along M, attention along heads
+
+// The row operators: one row-sharded input.
+int run_rows_pipelined(int64_t rows, const void *host_in, size_t in_row_bytes, void *host_out,
+                       size_t out_row_bytes, const std::function<int(Part &)> &stage_replicated,
+                       const std::function<int(Part &, const void *, void *, int64_t)> &launch) {
+    return run_pipelined(rows, {RowIn{host_in, in_row_bytes, kSlotIn0}}, host_out, out_row_bytes,
+                         kRowChunkBytes, stage_replicated,
+                         [&](Part &p, const uint8_t *const *din, void *dout, int64_t nr) {
+                             return launch(p, din[0], dout, nr);
+                         });
+}
+
+// Number of per-device slots for a call's replicated operands.  The library
+// is initialised first (a host entry may be the process's first call), so
+// this is the number of devices the call shards over; 0 when no device is
+// visible, and the call then fails in run_sharded / run_pipelined before any
+// slot is used.
+inline size_t dev_count() { return ensure_init() ? (size_t)ndev() : 0; }
+
 inline int null_check(const char *name, std::initializer_list<const void *> ptrs) {
     for (const void *p : ptrs)
         if (!p) return fail(HEXCUDA_ERR_ARG, "%s: null pointer", name);
@@ -247,7 +303,7 @@ HX_EXPORT int hexcuda_host_layernorm_f32(const float *x, const float *gamma, con
     if (R < 0 || C <= 0) return fail(HEXCUDA_ERR_ARG, "host_layernorm_f32: R=%d C=%d", R, C);
     if (int rc = null_check("host_layernorm_f32", {x, gamma, beta, out})) return rc;
     const size_t rb = sizeof(float) * (size_t)C;
-    std::vector<const float *> dg(ndev()), db(ndev());
+    std::vector<const float *> dg(dev_count()), db(dev_count());
     return run_rows_pipelined(
         R, x, rb, out, rb,
         [&](Part &p) {
@@ -420,19 +476,27 @@ HX_EXPORT int hexcuda_host_gemm_u8s8_pc(const uint8_t *A, const int8_t *B, const
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_u8s8_pc: bad shape");
     if (M == 0 || N == 0) return HEXCUDA_OK;
     if (int rc = null_check("host_gemm_u8s8_pc", {A, B, bias, out, mult, shift})) return rc;
-    return run_sharded(M, out, (size_t)N, [&](Part &p) {
-        int64_t nr = p.r1 - p.r0;
-        const uint8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
-        const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
-        const int32_t *dbias = stage_in(p.d, kSlotIn2, bias, (size_t)N);
-        const int32_t *dm = stage_in(p.d, kSlotIn3, mult, (size_t)N);
-        const int *ds = stage_in(p.d, kSlotIn4, shift, (size_t)N);
-        uint8_t *dout = reinterpret_cast<uint8_t *>(scratch(p.d, kSlotOut, (size_t)(nr * N)));
-        if (!dA || !dB || !dbias || !dm || !ds || !dout) return hexcuda_last_error();
-        p.dout = dout;
-        return hexcuda_gemm_u8s8_pc(p.slot, dA, dB, dbias, dout, (int)nr, N, K, zpA, dm, ds,
-                                    zp_out);
-    });
+    struct Rep {
+        const int8_t *B;
+        const int32_t *bias, *mult;
+        const int *shift;
+    };
+    std::vector<Rep> rep(dev_count());
+    return run_pipelined(
+        M, {RowIn{A, (size_t)K, kSlotIn0}}, out, (size_t)N, kGemmChunkBytes,
+        [&](Part &p) {
+            Rep &r = rep[(size_t)p.slot];
+            r.B = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+            r.bias = stage_in(p.d, kSlotIn2, bias, (size_t)N);
+            r.mult = stage_in(p.d, kSlotIn3, mult, (size_t)N);
+            r.shift = stage_in(p.d, kSlotIn4, shift, (size_t)N);
+            return (r.B && r.bias && r.mult && r.shift) ? HEXCUDA_OK : hexcuda_last_error();
+        },
+        [&](Part &p, const uint8_t *const *din, void *dout, int64_t nr) {
+            const Rep &r = rep[(size_t)p.slot];
+            return hexcuda_gemm_u8s8_pc(p.slot, din[0], r.B, r.bias, (uint8_t *)dout, (int)nr, N,
+                                        K, zpA, r.mult, r.shift, zp_out);
+        });
 }
 
 HX_EXPORT int hexcuda_host_requant_ew(const void *a, int a_i8, const void *b, int b_kind,
@@ -443,21 +507,20 @@ HX_EXPORT int hexcuda_host_requant_ew(const void *a, int a_i8, const void *b, in
     if (n == 0) return HEXCUDA_OK;
     if (int rc = null_check("host_requant_ew", {a, out, b_kind ? b : a})) return rc;
     const size_t ea = a_i8 ? 1 : 4, eb = b_kind == 2 ? 1 : 4;
-    return run_sharded(n, out, 1, [&](Part &p) {
-        const int64_t nr = p.r1 - p.r0;
-        const uint8_t *da = stage_in(p.d, kSlotIn0, reinterpret_cast<const uint8_t *>(a) + p.r0 * ea,
-                                     (size_t)nr * ea);
-        const uint8_t *db = b_kind ? stage_in(p.d, kSlotIn1,
-                                              reinterpret_cast<const uint8_t *>(b) + p.r0 * eb,
-                                              (size_t)nr * eb)
-                                   : nullptr;
-        const int8_t *dl = lut ? stage_in(p.d, kSlotIn2, lut, 256) : nullptr;
-        void *dout = scratch(p.d, kSlotOut, (size_t)nr);
-        if (!da || (b_kind && !db) || (lut && !dl) || !dout) return hexcuda_last_error();
-        p.dout = dout;
-        return hexcuda_requant_ew(p.slot, da, a_i8, db, b_kind, dout, nr, pre, pre_c, mult, shift,
-                                  zp, sign_of_a, lo1, hi1, lo2, hi2, dl);
-    });
+    std::vector<const int8_t *> dl(dev_count());
+    // one element per row; chunks of a multiple of 16 elements keep every
+    // operand's chunk 16-byte aligned
+    return run_pipelined(
+        n, {RowIn{a, ea, kSlotIn0}, RowIn{b, b_kind ? eb : 0, kSlotIn1}}, out, 1, kRowChunkBytes,
+        [&](Part &p) {
+            dl[(size_t)p.slot] = lut ? stage_in(p.d, kSlotIn2, lut, 256) : nullptr;
+            return (!lut || dl[(size_t)p.slot]) ? HEXCUDA_OK : hexcuda_last_error();
+        },
+        [&](Part &p, const uint8_t *const *din, void *dout, int64_t nr) {
+            return hexcuda_requant_ew(p.slot, din[0], a_i8, b_kind ? din[1] : nullptr, b_kind,
+                                      dout, nr, pre, pre_c, mult, shift, zp, sign_of_a, lo1, hi1,
+                                      lo2, hi2, dl[(size_t)p.slot]);
+        });
 }
 
 HX_EXPORT int hexcuda_host_epilogue_bias_i32(const int32_t *acc, const int32_t *bias,
@@ -508,6 +571,35 @@ HX_EXPORT int hexcuda_host_gemm_hmx_ex(const uint8_t *A, const int8_t *B, int b_
                          : store == HEXCUDA_HMX_STORE_U16_FIELD ? 2 : 1;
     const size_t rsize = res_kind == HEXCUDA_HMX_RES_I32 ? 4 : 1;
     const size_t lsize = store == HEXCUDA_HMX_STORE_LUT_I32 ? 4 : 1;
+    if (!col_major) {
+        struct Rep {
+            const int8_t *B;
+            const int32_t *bias;
+            const uint8_t *lut;
+        };
+        std::vector<Rep> rep(dev_count());
+        return run_pipelined(
+            M,
+            {RowIn{A, (size_t)K, kSlotIn0},
+             RowIn{res, res_kind ? (size_t)N * rsize : 0, kSlotIn3}},
+            out, (size_t)N * osize, kGemmChunkBytes,
+            [&](Part &p) {
+                Rep &r = rep[(size_t)p.slot];
+                r.B = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+                r.bias = bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
+                r.lut = has_lut ? stage_in(p.d, kSlotIn4, reinterpret_cast<const uint8_t *>(lut),
+                                           256 * lsize)
+                                : nullptr;
+                return (r.B && (!bias || r.bias) && (!has_lut || r.lut)) ? HEXCUDA_OK
+                                                                         : hexcuda_last_error();
+            },
+            [&](Part &p, const uint8_t *const *din, void *dout, int64_t nr) {
+                const Rep &r = rep[(size_t)p.slot];
+                return hexcuda_gemm_hmx_ex(p.slot, din[0], r.B, b_transposed, r.bias,
+                                           res_kind ? din[1] : nullptr, res_kind, r.lut, dout,
+                                           store, act, 0, (int)nr, N, K, zpA);
+            });
+    }
     return run_sharded(
         M, out, (size_t)N * osize,
         [&](Part &p) {
@@ -544,17 +636,21 @@ HX_EXPORT int hexcuda_host_gemm_hmx(const uint8_t *A, const int8_t *B, int b_tra
     if (int rc = null_check("host_gemm_hmx", {A, B, out, has_bias ? bias : (const void *)A}))
         return rc;
     const size_t osize = out_kind == HEXCUDA_HMX_OUT_I32 ? 4 : 1;
-    return run_sharded(M, out, (size_t)N * osize, [&](Part &p) {
-        int64_t nr = p.r1 - p.r0;
-        const uint8_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
-        const int8_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
-        const int32_t *dbias = has_bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
-        void *dout = scratch(p.d, kSlotOut, (size_t)(nr * N) * osize);
-        if (!dA || !dB || (has_bias && !dbias) || !dout) return hexcuda_last_error();
-        p.dout = dout;
-        return hexcuda_gemm_hmx(p.slot, dA, dB, b_transposed, dbias, dout, out_kind, (int)nr, N,
-                                K, zpA);
-    });
+    std::vector<const int8_t *> dB(dev_count());
+    std::vector<const int32_t *> dbias(dev_count());
+    return run_pipelined(
+        M, {RowIn{A, (size_t)K, kSlotIn0}}, out, (size_t)N * osize, kGemmChunkBytes,
+        [&](Part &p) {
+            const size_t s = (size_t)p.slot;
+            dB[s] = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+            dbias[s] = has_bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
+            return (dB[s] && (!has_bias || dbias[s])) ? HEXCUDA_OK : hexcuda_last_error();
+        },
+        [&](Part &p, const uint8_t *const *din, void *dout, int64_t nr) {
+            const size_t s = (size_t)p.slot;
+            return hexcuda_gemm_hmx(p.slot, din[0], dB[s], b_transposed, dbias[s], dout, out_kind,
+                                    (int)nr, N, K, zpA);
+        });
 }
 
 HX_EXPORT int hexcuda_host_attn_qkt_av_hmx(const uint8_t *Q, const int8_t *K, const int8_t *V,
@@ -666,18 +762,23 @@ HX_EXPORT int hexcuda_host_gemm_f16_ex(const uint16_t *A, const uint16_t *B, int
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_f16_ex: bad shape");
     if (M == 0 || N == 0) return HEXCUDA_OK;
     if (int rc = null_check("host_gemm_f16_ex", {A, B, out})) return rc;
-    return run_sharded(M, out, (size_t)N * 2, [&](Part &p) {
-        const int64_t nr = p.r1 - p.r0;
-        const uint16_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
-        const uint16_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
-        const uint16_t *dbias = bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
-        const uint16_t *dres = res ? stage_in(p.d, kSlotIn3, res + p.r0 * N, (size_t)(nr * N)) : nullptr;
-        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, (size_t)(nr * N) * 2));
-        if (!dA || !dB || (bias && !dbias) || (res && !dres) || !dout) return hexcuda_last_error();
-        p.dout = dout;
-        return hexcuda_gemm_f16_ex(p.slot, dA, dB, b_transposed, dbias, dres, dout, act, preround,
-                                   scale, (int)nr, N, K);
-    });
+    std::vector<const uint16_t *> dB(dev_count()), dbias(dev_count());
+    // without a residual the second row input has no bytes and is not read
+    return run_pipelined(
+        M, {RowIn{A, 2 * (size_t)K, kSlotIn0}, RowIn{res, res ? 2 * (size_t)N : 0, kSlotIn3}},
+        out, 2 * (size_t)N, kGemmChunkBytes,
+        [&](Part &p) {
+            const size_t s = (size_t)p.slot;
+            dB[s] = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+            dbias[s] = bias ? stage_in(p.d, kSlotIn2, bias, (size_t)N) : nullptr;
+            return (dB[s] && (!bias || dbias[s])) ? HEXCUDA_OK : hexcuda_last_error();
+        },
+        [&](Part &p, const uint8_t *const *din, void *dout, int64_t nr) {
+            const size_t s = (size_t)p.slot;
+            return hexcuda_gemm_f16_ex(p.slot, (const uint16_t *)din[0], dB[s], b_transposed,
+                                       dbias[s], res ? (const uint16_t *)din[1] : nullptr,
+                                       (uint16_t *)dout, act, preround, scale, (int)nr, N, K);
+        });
 }
 
 HX_EXPORT int hexcuda_host_gemm_i8_rq_ex(const int8_t *A, const int8_t *B, int b_transposed,
@@ -783,15 +884,17 @@ HX_EXPORT int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, ui
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_f16_nt: bad shape");
     if (M == 0 || N == 0) return HEXCUDA_OK;
     if (int rc = null_check("host_gemm_f16_nt", {A, Bt, out})) return rc;
-    return run_sharded(M, out, 2 * (size_t)N, [&](Part &p) {
-        int64_t nr = p.r1 - p.r0;
-        const uint16_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
-        const uint16_t *dB = stage_in(p.d, kSlotIn1, Bt, (size_t)N * K);
-        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * (size_t)(nr * N)));
-        if (!dA || !dB || !dout) return hexcuda_last_error();
-        p.dout = dout;
-        return hexcuda_gemm_f16_nt(p.slot, dA, dB, dout, (int)nr, N, K);
-    });
+    std::vector<const uint16_t *> dB(dev_count());
+    return run_pipelined(
+        M, {RowIn{A, 2 * (size_t)K, kSlotIn0}}, out, 2 * (size_t)N, kGemmChunkBytes,
+        [&](Part &p) {
+            dB[(size_t)p.slot] = stage_in(p.d, kSlotIn1, Bt, (size_t)N * K);
+            return dB[(size_t)p.slot] ? HEXCUDA_OK : hexcuda_last_error();
+        },
+        [&](Part &p, const uint8_t *const *din, void *dout, int64_t nr) {
+            return hexcuda_gemm_f16_nt(p.slot, (const uint16_t *)din[0], dB[(size_t)p.slot],
+                                       (uint16_t *)dout, (int)nr, N, K);
+        });
 }
 
 HX_EXPORT int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uint16_t *out, int M,
@@ -799,15 +902,17 @@ HX_EXPORT int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uin
     if (M < 0 || N < 0 || K < 0) return fail(HEXCUDA_ERR_ARG, "host_gemm_f16_nn: bad shape");
     if (M == 0 || N == 0) return HEXCUDA_OK;
     if (int rc = null_check("host_gemm_f16_nn", {A, B, out})) return rc;
-    return run_sharded(M, out, 2 * (size_t)N, [&](Part &p) {
-        int64_t nr = p.r1 - p.r0;
-        const uint16_t *dA = stage_in(p.d, kSlotIn0, A + p.r0 * K, (size_t)(nr * K));
-        const uint16_t *dB = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
-        uint16_t *dout = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * (size_t)(nr * N)));
-        if (!dA || !dB || !dout) return hexcuda_last_error();
-        p.dout = dout;
-        return hexcuda_gemm_f16_nn(p.slot, dA, dB, dout, (int)nr, N, K);
-    });
+    std::vector<const uint16_t *> dB(dev_count());
+    return run_pipelined(
+        M, {RowIn{A, 2 * (size_t)K, kSlotIn0}}, out, 2 * (size_t)N, kGemmChunkBytes,
+        [&](Part &p) {
+            dB[(size_t)p.slot] = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
+            return dB[(size_t)p.slot] ? HEXCUDA_OK : hexcuda_last_error();
+        },
+        [&](Part &p, const uint8_t *const *din, void *dout, int64_t nr) {
+            return hexcuda_gemm_f16_nn(p.slot, (const uint16_t *)din[0], dB[(size_t)p.slot],
+                                       (uint16_t *)dout, (int)nr, N, K);
+        });
 }
 
 HX_EXPORT int hexcuda_host_attn_f16(const uint16_t *Q, const uint16_t *K, const uint16_t *V,
@@ -818,16 +923,14 @@ HX_EXPORT int hexcuda_host_attn_f16(const uint16_t *Q, const uint16_t *K, const 
     if (BH == 0 || SQ == 0) return HEXCUDA_OK;
     if (int rc = null_check("host_attn_f16", {Q, K, V, O})) return rc;
     const size_t qh = (size_t)SQ * D, kh = (size_t)SK * D;
-    return run_sharded(BH, O, 2 * qh, [&](Part &p) {
-        int64_t nh = p.r1 - p.r0;
-        const uint16_t *dQ = stage_in(p.d, kSlotIn0, Q + p.r0 * qh, nh * qh);
-        const uint16_t *dK = stage_in(p.d, kSlotIn1, K + p.r0 * kh, nh * kh);
-        const uint16_t *dV = stage_in(p.d, kSlotIn2, V + p.r0 * kh, nh * kh);
-        uint16_t *dO = reinterpret_cast<uint16_t *>(scratch(p.d, kSlotOut, 2 * nh * qh));
-        if (!dQ || !dK || !dV || !dO) return hexcuda_last_error();
-        p.dout = dO;
-        return hexcuda_attn_f16(p.slot, dQ, dK, dV, dO, (int)nh, SQ, SK, D, scale, causal);
-    });
+    return run_pipelined(
+        BH, {RowIn{Q, 2 * qh, kSlotIn0}, RowIn{K, 2 * kh, kSlotIn1}, RowIn{V, 2 * kh, kSlotIn2}},
+        O, 2 * qh, kGemmChunkBytes, [](Part &) { return HEXCUDA_OK; },
+        [&](Part &p, const uint8_t *const *din, void *dout, int64_t nh) {
+            return hexcuda_attn_f16(p.slot, (const uint16_t *)din[0], (const uint16_t *)din[1],
+                                    (const uint16_t *)din[2], (uint16_t *)dout, (int)nh, SQ, SK,
+                                    D, scale, causal);
+        });
 }
 
 HX_EXPORT int hexcuda_host_online_softmax_step_f16(const uint16_t *scores, const uint16_t *V,

@@ -35,6 +35,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -111,6 +112,13 @@ struct GemmArgs {
     // (M-blocks when group_n_major == 0, N-blocks otherwise) before moving
     // along the other, so the group's panel of that operand stays in L2
     int group, group_n_major;
+    // work units (unit_of): tiles [0, dp_tiles) whole, then `split` K parts
+    // of each remaining tile; part_flag / part_ws hold the parts' arrival
+    // flags and raw accumulators, ticket is this launch's serial number
+    int units, dp_tiles, split;
+    uint32_t ticket;
+    int *part_flag;
+    int32_t *part_ws;
     int *err_word;
     EpiParams epi;
 };
@@ -147,6 +155,116 @@ __device__ __forceinline__ void tile_coords(int t, const GemmArgs &a, int &mb, i
     const int res = first + r % gsize, str = r / gsize;
     mb = a.group_n_major ? str : res;
     nb = a.group_n_major ? res : str;
+}
+
+// Work units of the persistent kernels.  Tiles [0, dp_tiles) run whole; each
+// remaining tile (the last, partial wave) is cut into `split` K ranges that
+// different CTAs (CTA pairs) run at the same time.  Part 0 owns the tile: its
+// epilogue warps wait until parts 1..split-1 have left their raw accumulators
+// in the workspace, add them and run the epilogue.  A part p >= 1 stores its
+// accumulator and sets its flag (one per epilogue warp) to the launch's
+// ticket.  The host makes dp_tiles a multiple of the grid and the parts at
+// most one grid, so every part is its CTA's last unit: a part p >= 1 never
+// waits, and the CTAs that run them have only whole tiles before them.
+struct Unit {
+    int t;          // tile
+    int kb0, kb1;   // K blocks [kb0, kb1)
+    int part;       // -1: whole tile; else this unit's K part of tile t
+};
+
+__device__ __forceinline__ Unit unit_of(int u, const GemmArgs &a) {
+    Unit w;
+    if (u < a.dp_tiles) {
+        w.t = u;
+        w.kb0 = 0;
+        w.kb1 = a.num_kb;
+        w.part = -1;
+        return w;
+    }
+    const int i = u - a.dp_tiles;
+    w.t = a.dp_tiles + i / a.split;
+    w.part = i % a.split;
+    w.kb0 = (int)((int64_t)w.part * a.num_kb / a.split);
+    w.kb1 = (int)((int64_t)(w.part + 1) * a.num_kb / a.split);
+    return w;
+}
+
+// Flag / workspace slot of (split tile, part p >= 1, CTA rank of the pair,
+// epilogue warp); a workspace slot holds one epilogue warp's 32 rows x
+// `cols` columns of int32 as [cols / 32][8][lane][4]: the warp's 32 lanes
+// store (and the owner's lanes load) 512 contiguous bytes per instruction.
+__device__ __forceinline__ size_t part_slot(const GemmArgs &a, int t, int p, int rank,
+                                            int nranks, int warp_slot) {
+    return (((size_t)(t - a.dp_tiles) * (a.split - 1) + (p - 1)) * nranks + rank) * 8 + warp_slot;
+}
+
+__device__ __forceinline__ void part_store(int32_t *ws, int chunk, int lane,
+                                           const uint32_t (&r)[32]) {
+    int4 *dst = reinterpret_cast<int4 *>(ws) + (size_t)chunk * 256 + lane;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        dst[e * 32] =
+            make_int4((int)r[4 * e], (int)r[4 * e + 1], (int)r[4 * e + 2], (int)r[4 * e + 3]);
+}
+
+// r += the stored part (int32 wrap-around, or fp32 for the fp16 GEMMs); the
+// loads bypass L1, whose lines are not kept coherent with other SMs' stores
+template <bool F32>
+__device__ __forceinline__ void part_add(const int32_t *ws, int chunk, int lane, uint32_t (&r)[32]) {
+    const int4 *src = reinterpret_cast<const int4 *>(ws) + (size_t)chunk * 256 + lane;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        const int4 v = __ldcg(src + e * 32);
+        const int w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            uint32_t &x = r[4 * e + i];
+            x = F32 ? __float_as_uint(__uint_as_float(x) + __int_as_float(w[i]))
+                    : x + (uint32_t)w[i];
+        }
+    }
+}
+
+__device__ __forceinline__ void part_flag_set(int *f, uint32_t ticket) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(ticket) : "memory");
+}
+
+// Bounded wait for a part's flag to reach this launch's ticket (kWaitBudgetNs;
+// on expiry the device error word gets kErrWaitPart and the CTA aborts).
+__device__ __forceinline__ bool part_flag_wait(const int *f, uint32_t ticket, volatile int *abort,
+                                               int *err_word) {
+    const uint64_t t0 = tc::globaltimer();
+    while (true) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (v == ticket) return true;
+        if (*abort) return false;
+        if (tc::globaltimer() - t0 > kWaitBudgetNs) {
+            atomicOr(err_word, kErrWaitPart);
+            *abort = 1;
+            return false;
+        }
+        __nanosleep(128);
+    }
+}
+
+// Owner of a split tile: adds the `nparts` other parts of this epilogue
+// warp's 32 rows x COLS columns (the first at ws, the next `stride` words on)
+// into its accumulator in TMEM (taddr = the warp's lane quarter and first
+// column), before the ordinary epilogue reads it.
+template <bool F32, int COLS>
+__device__ __forceinline__ void merge_parts(const int32_t *ws, size_t stride, int nparts,
+                                            uint32_t taddr, int lane) {
+#pragma unroll 1
+    for (int c = 0; c < COLS; c += 32) {
+        uint32_t r[32];
+        tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
+        tc::tmem_ld_wait(r);
+#pragma unroll 1
+        for (int p = 0; p < nparts; p++) part_add<F32>(ws + p * stride, c / 32, lane, r);
+        tc::tmem_st_32x32b_x32(taddr + (uint32_t)c, r);
+    }
+    tc::tmem_st_wait();
 }
 
 // Requant parameters of one epilogue warp's current 32 columns; half is the
@@ -543,7 +661,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int num_tiles = args.tiles_m * args.tiles_n;
     constexpr uint32_t kTmemCols = 2 * BN;
 
     if (threadIdx.x == 0) {
@@ -577,10 +694,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t armed = 0;    // bit s: stage s has a load in flight we may need to drain
             uint32_t armed_phase = 0;
-            for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+            for (int u = blockIdx.x; u < args.units && !*abort_flag; u += gridDim.x) {
+                const Unit w = unit_of(u, args);
                 int mb, nb;
-                tile_coords(t, args, mb, nb);
-                for (int kb = 0; kb < args.num_kb; kb++) {
+                tile_coords(w.t, args, mb, nb);
+                for (int kb = w.kb0; kb < w.kb1; kb++) {
                     if (!tc::mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.err_word,
                                        kErrWaitEmpty))
                         break;
@@ -625,7 +743,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             int local = 0;
             bool issued = false;
-            for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, local++) {
+            for (int u = blockIdx.x; u < args.units && !*abort_flag; u += gridDim.x, local++) {
+                const Unit w = unit_of(u, args);
                 const int buf = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
                 if (!tc::mbar_wait(&tempty[buf], aphase ^ 1, abort_flag, args.err_word,
@@ -633,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 tc::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
-                for (int kb = 0; kb < args.num_kb; kb++) {
+                for (int kb = w.kb0; kb < w.kb1; kb++) {
                     if (!tc::mbar_wait(&full[stage], phase, abort_flag, args.err_word,
                                        kErrWaitFull))
                         break;
@@ -648,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t bd =
                             B_MN ? tc::sdesc_mnmajor_sw128(sb + k * (32 / kEsize) * 128, kBoxBytes, 1024)
                                  : tc::sdesc_kmajor_sw128(sb + k * 32);
-                        tc::mma_ss<KIND>(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+                        tc::mma_ss<KIND>(d_tmem, ad, bd, idesc, (kb != w.kb0 || k != 0) ? 1u : 0u);
                     }
                     issued = true;
                     tc::mma_commit(&empty[stage]);
@@ -680,30 +799,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int chalf = (warp - 2) >> 2;
         ColParams *cp = reinterpret_cast<ColParams *>(smem + L::kParamOffset) + (warp - 2);
         uint4 *stage = reinterpret_cast<uint4 *>(smem + L::kStoreOffset + (warp - 2) * kStoreStageBytes);
+        const int wslot = warp - 2;
+        constexpr size_t kPartWords = (size_t)(BN / 2) * 32;
         int local = 0;
-        for (int t = blockIdx.x; t < num_tiles && !__any_sync(0xffffffffu, *abort_flag);
-             t += gridDim.x, local++) {
+        for (int u = blockIdx.x; u < args.units && !__any_sync(0xffffffffu, *abort_flag);
+             u += gridDim.x, local++) {
+            const Unit w = unit_of(u, args);
             int mb, nb;
-            tile_coords(t, args, mb, nb);
+            tile_coords(w.t, args, mb, nb);
             const int buf = local & 1;
             const uint32_t aphase = (local >> 1) & 1;
-            const bool ok =
-                tc::mbar_wait(&tfull[buf], aphase, abort_flag, args.err_word, kErrWaitAccum);
+            bool ok = tc::mbar_wait(&tfull[buf], aphase, abort_flag, args.err_word, kErrWaitAccum);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc::tc_fence_after();
             const int row = mb * kBM + q * 32 + lane;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+            if (w.part >= 1) {
+                // a K part of a split tile: raw accumulator to the workspace
+                const size_t ps = part_slot(args, w.t, w.part, 0, 1, wslot);
+                int32_t *ws = args.part_ws + ps * kPartWords;
 #pragma unroll 1
-            for (int c = chalf * (BN / 2); c < (chalf + 1) * (BN / 2); c += 32) {
-                uint32_t r[32];
-                if constexpr (EPI == kEpiRequant || EPI == kEpiHmx) {
-                    stage_params(args.epi, cp, nb * BN + c, lane);
+                for (int c = 0; c < BN / 2; c += 32) {
+                    uint32_t r[32];
+                    tc::tmem_ld_32x32b_x32(taddr + (uint32_t)(chalf * (BN / 2) + c), r);
+                    tc::tmem_ld_wait(r);
+                    part_store(ws, c / 32, lane, r);
                 }
+                __threadfence();
                 __syncwarp();
-                tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
-                tc::tmem_ld_wait(r);
-                epilogue_chunk<EPI>(args.epi, r, row, nb * BN + c, cp, stage);
-                __syncwarp();
+                if (lane == 0) part_flag_set(args.part_flag + ps, args.ticket);
+            } else {
+                if (w.part == 0) {
+                    // owner of a split tile: the other parts' accumulators are
+                    // added into this warp's TMEM columns first
+                    for (int p = 1; p < args.split && ok; p++)
+                        ok = part_flag_wait(args.part_flag + part_slot(args, w.t, p, 0, 1, wslot),
+                                            args.ticket, abort_flag, args.err_word);
+                    if (!__all_sync(0xffffffffu, ok)) break;
+                    merge_parts<KIND == MmaKind::F16, BN / 2>(
+                        args.part_ws + part_slot(args, w.t, 1, 0, 1, wslot) * kPartWords,
+                        8 * kPartWords, args.split - 1, taddr + (uint32_t)(chalf * (BN / 2)), lane);
+                }
+#pragma unroll 1
+                for (int c = chalf * (BN / 2); c < (chalf + 1) * (BN / 2); c += 32) {
+                    uint32_t r[32];
+                    if constexpr (EPI == kEpiRequant || EPI == kEpiHmx) {
+                        stage_params(args.epi, cp, nb * BN + c, lane);
+                    }
+                    __syncwarp();
+                    tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
+                    tc::tmem_ld_wait(r);
+                    epilogue_chunk<EPI>(args.epi, r, row, nb * BN + c, cp, stage);
+                    __syncwarp();
+                }
             }
             tc::tc_fence_before();
             __syncwarp();
@@ -782,7 +930,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool even = rank == 0;
     const int pair = blockIdx.x >> 1;
     const int npairs = gridDim.x >> 1;
-    const int num_tiles = args.tiles_m * args.tiles_n;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages2; s++) {
@@ -817,12 +964,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             uint32_t armed = 0, armed_phase = 0;
-            for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
+            for (int u = pair; u < args.units && !*abort_flag; u += npairs) {
+                const Unit w = unit_of(u, args);
                 int mb, nb;
-                tile_coords(t, args, mb, nb);
+                tile_coords(w.t, args, mb, nb);
                 const int row0 = mb * 256 + (int)rank * 128;
                 const int col0 = nb * kTileN + (int)rank * 128;
-                for (int kb = 0; kb < args.num_kb; kb++) {
+                for (int kb = w.kb0; kb < w.kb1; kb++) {
                     if (!tc::mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.err_word,
                                        kErrWaitEmpty))
                         break;
@@ -872,7 +1020,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             int local = 0;
             bool issued = false;
-            for (int t = pair; t < num_tiles && !*abort_flag; t += npairs, local++) {
+            for (int u = pair; u < args.units && !*abort_flag; u += npairs, local++) {
+                const Unit w = unit_of(u, args);
                 const int buf = local & 1;
                 const uint32_t aphase = (local >> 1) & 1;
                 if (!tc::mbar_wait_cluster(&tempty[buf], aphase ^ 1, abort_flag, args.err_word,
@@ -880,7 +1029,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 tc::tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kTileN);
-                for (int kb = 0; kb < args.num_kb; kb++) {
+                for (int kb = w.kb0; kb < w.kb1; kb++) {
                     if (!tc::mbar_wait(&full[stage], phase, abort_flag, args.err_word,
                                        kErrWaitFull))
                         break;
@@ -893,7 +1042,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t bd =
                             B_MN ? tc::sdesc_mnmajor_sw128(sb + k * (32 / kEsize) * 128, kBoxBytes, 1024)
                                  : tc::sdesc_kmajor_sw128(sb + k * 32);
-                        tc::mma_ss_pair<KIND>(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+                        tc::mma_ss_pair<KIND>(d_tmem, ad, bd, idesc,
+                                              (kb != w.kb0 || k != 0) ? 1u : 0u);
                     }
                     issued = true;
                     tc::mma_commit_pair(empty_own + (uint32_t)stage * 8u);
@@ -925,31 +1075,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         ColParams *cp = reinterpret_cast<ColParams *>(smem + L::kParamOffset) + (warp - 2);
         uint4 *stage = reinterpret_cast<uint4 *>(smem + L::kStoreOffset + (warp - 2) * kStoreStageBytes);
         const uint32_t tempty_even = tc::mapa_shared(tc::smem_u32(tempty), 0);
+        const int wslot = warp - 2;
+        constexpr size_t kPartWords = (size_t)(kTileN / 2) * 32;
         int local = 0;
-        for (int t = pair; t < num_tiles && !__any_sync(0xffffffffu, *abort_flag);
-             t += npairs, local++) {
+        for (int u = pair; u < args.units && !__any_sync(0xffffffffu, *abort_flag);
+             u += npairs, local++) {
+            const Unit w = unit_of(u, args);
             int mb, nb;
-            tile_coords(t, args, mb, nb);
+            tile_coords(w.t, args, mb, nb);
             const int buf = local & 1;
             const uint32_t aphase = (local >> 1) & 1;
-            const bool ok =
-                tc::mbar_wait(&tfull[buf], aphase, abort_flag, args.err_word, kErrWaitAccum);
+            bool ok = tc::mbar_wait(&tfull[buf], aphase, abort_flag, args.err_word, kErrWaitAccum);
             if (!__all_sync(0xffffffffu, ok)) break;
             tc::tc_fence_after();
             const int row = mb * 256 + (int)rank * 128 + q * 32 + lane;
             const uint32_t taddr =
                 tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kTileN);
+            if (w.part >= 1) {
+                // a K part of a split tile: this CTA's raw accumulator rows to
+                // the workspace
+                const size_t ps = part_slot(args, w.t, w.part, (int)rank, 2, wslot);
+                int32_t *ws = args.part_ws + ps * kPartWords;
 #pragma unroll 1
-            for (int c = chalf * (kTileN / 2); c < (chalf + 1) * (kTileN / 2); c += 32) {
-                uint32_t r[32];
-                if constexpr (EPI == kEpiRequant || EPI == kEpiHmx) {
-                    stage_params(args.epi, cp, nb * kTileN + c, lane);
+                for (int c = 0; c < kTileN / 2; c += 32) {
+                    uint32_t r[32];
+                    tc::tmem_ld_32x32b_x32(taddr + (uint32_t)(chalf * (kTileN / 2) + c), r);
+                    tc::tmem_ld_wait(r);
+                    part_store(ws, c / 32, lane, r);
                 }
+                __threadfence();
                 __syncwarp();
-                tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
-                tc::tmem_ld_wait(r);
-                epilogue_chunk<EPI>(args.epi, r, row, nb * kTileN + c, cp, stage);
-                __syncwarp();
+                if (lane == 0) part_flag_set(args.part_flag + ps, args.ticket);
+            } else {
+                if (w.part == 0) {
+                    for (int p = 1; p < args.split && ok; p++)
+                        ok = part_flag_wait(
+                            args.part_flag + part_slot(args, w.t, p, (int)rank, 2, wslot),
+                            args.ticket, abort_flag, args.err_word);
+                    if (!__all_sync(0xffffffffu, ok)) break;
+                    merge_parts<KIND == MmaKind::F16, kTileN / 2>(
+                        args.part_ws + part_slot(args, w.t, 1, (int)rank, 2, wslot) * kPartWords,
+                        16 * kPartWords, args.split - 1, taddr + (uint32_t)(chalf * (kTileN / 2)),
+                        lane);
+                }
+#pragma unroll 1
+                for (int c = chalf * (kTileN / 2); c < (chalf + 1) * (kTileN / 2); c += 32) {
+                    uint32_t r[32];
+                    if constexpr (EPI == kEpiRequant || EPI == kEpiHmx) {
+                        stage_params(args.epi, cp, nb * kTileN + c, lane);
+                    }
+                    __syncwarp();
+                    tc::tmem_ld_32x32b_x32(taddr + (uint32_t)c, r);
+                    tc::tmem_ld_wait(r);
+                    epilogue_chunk<EPI>(args.epi, r, row, nb * kTileN + c, cp, stage);
+                    __syncwarp();
+                }
             }
             tc::tc_fence_before();
             __syncwarp();
@@ -1027,31 +1207,72 @@ __global__ void __launch_bounds__(256) pad_rows_kernel(const T *__restrict__ src
     }
 }
 
-// colsum[n] += sum_k B[k][n] for a row-major int8 B [K, N] (colsum pre-zeroed).
-// Thread = 16 consecutive columns (one 128-bit load per row) over a chunk of
-// rows; integer sums, so the atomics' order does not matter.
-__global__ void __launch_bounds__(128) colsum_kernel(const int8_t *__restrict__ B,
+// colsum[n] += sum_{k in this block's rows} B[k][n] for a row-major int8 B
+// [K, N] (N a multiple of 16, rows 16-byte aligned; colsum pre-zeroed).
+// A block of 8 warps covers 512 columns (16 per lane) and kColsumRows rows
+// at most; warp w reads rows w, w + 8, ..., four rows per loop trip so that
+// 64 bytes per thread are in flight (the pass is bound by HBM latency
+// otherwise).  Bytes are summed as unsigned (b + 128) in packed 16-bit lanes
+// (even and odd bytes of each word; at most kColsumRows / 8 = 256 rows per
+// thread, so a lane stays below 65536) and unbiased at the end; the 8 warps'
+// sums meet in shared memory and each column takes one atomic per block.
+constexpr int kColsumRows = 2048;
+
+__global__ void __launch_bounds__(256) colsum_kernel(const int8_t *__restrict__ B,
                                                      int32_t *__restrict__ colsum, int K, int N,
-                                                     int kchunk, int vec) {
+                                                     int kchunk) {
     tc::launch_dependents();
-    const int n0 = (blockIdx.x * blockDim.x + threadIdx.x) * 16;
-    if (n0 >= N) return;
+    __shared__ int32_t red[8][512];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nblk = blockIdx.x * 512;
+    const int n0 = nblk + lane * 16;
     const int k0 = blockIdx.y * kchunk, k1 = min(K, k0 + kchunk);
-    int32_t acc[16];
+    uint32_t ev[4] = {0, 0, 0, 0}, od[4] = {0, 0, 0, 0};
+    int rows = 0;
+    if (n0 < N) {
+        const int8_t *col = B + n0;
+        auto add = [&](const int4 v) {
+            const uint32_t w[4] = {(uint32_t)v.x, (uint32_t)v.y, (uint32_t)v.z, (uint32_t)v.w};
 #pragma unroll
-    for (int i = 0; i < 16; i++) acc[i] = 0;
-    if (vec && n0 + 16 <= N) {
-        for (int k = k0; k < k1; k++) {
-            const int4 v = __ldg(reinterpret_cast<const int4 *>(B + (size_t)k * N + n0));
-            const int w[4] = {v.x, v.y, v.z, v.w};
+            for (int j = 0; j < 4; j++) {
+                const uint32_t x = w[j] ^ 0x80808080u;
+                ev[j] += x & 0x00FF00FFu;
+                od[j] += (x >> 8) & 0x00FF00FFu;
+            }
+        };
+        int k = k0 + warp;
+        for (; k + 24 < k1; k += 32) {
+            int4 v[4];
 #pragma unroll
-            for (int i = 0; i < 16; i++) acc[i] += (int32_t)(int8_t)(w[i >> 2] >> (8 * (i & 3)));
+            for (int u = 0; u < 4; u++)
+                v[u] = __ldg(reinterpret_cast<const int4 *>(col + (size_t)(k + 8 * u) * N));
+#pragma unroll
+            for (int u = 0; u < 4; u++) add(v[u]);
+            rows += 4;
         }
-    } else {
-        for (int k = k0; k < k1; k++)
-            for (int i = 0; i < 16 && n0 + i < N; i++) acc[i] += B[(size_t)k * N + n0 + i];
+        for (; k < k1; k += 8) {
+            add(__ldg(reinterpret_cast<const int4 *>(col + (size_t)k * N)));
+            rows++;
+        }
     }
-    for (int i = 0; i < 16 && n0 + i < N; i++) atomicAdd(colsum + n0 + i, acc[i]);
+    // column 4j + 0 / 4j + 2 in the low / high half of ev[j]; 4j + 1 / 4j + 3 of od[j]
+    const int bias = 128 * rows;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        red[warp][lane * 16 + 4 * j + 0] = (int32_t)(ev[j] & 0xFFFFu) - bias;
+        red[warp][lane * 16 + 4 * j + 1] = (int32_t)(od[j] & 0xFFFFu) - bias;
+        red[warp][lane * 16 + 4 * j + 2] = (int32_t)(ev[j] >> 16) - bias;
+        red[warp][lane * 16 + 4 * j + 3] = (int32_t)(od[j] >> 16) - bias;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int c = threadIdx.x * 2 + h;
+        int32_t sum = 0;
+#pragma unroll
+        for (int w = 0; w < 8; w++) sum += red[w][c];
+        if (nblk + c < N) atomicAdd(colsum + nblk + c, sum);
+    }
 }
 
 // colsum[n] = sum_k Bt[n][k] for a K-major int8 Bt [N, K] (pitch ldb): one
@@ -1178,9 +1399,68 @@ void pick_raster(GemmArgs &a, int64_t bm, int64_t bn, int64_t kbytes) {
     a.group = cn < cm ? gn : gm;
 }
 
+// Tail split (see unit_of): when the last wave of a persistent launch over
+// `slots` CTAs (or CTA pairs) would leave at least half of them idle, its
+// tiles are cut into K parts, up to kMaxSplit and at least kMinSplitKb K
+// blocks each, so that the wave keeps the idle slots busy and takes about
+// 1 / split of a tile's time.  The partial accumulators (part_bytes per
+// part) and arrival flags (flags_per_part per part) live in scratch slot
+// kSlotSplit: a fixed kSplitFlagBytes of flags, zeroed once per buffer and
+// afterwards written only with launch tickets, then the workspace.  Sets the
+// unit fields of `a` and the grid in slots.  single_wave_only: split only
+// when every tile is in the one, partial wave.  HEXCUDA_GEMM_SPLIT=0 turns
+// the split off (a tuning knob).  Measured on the 2048 x 8192 x 8192 u8 x s8
+// GEMM (the row shard of an 8-GPU run; 50 launches, two runs): 0.1271 ->
+// 0.1242 ms.
+constexpr int kMaxSplit = 4;
+constexpr int kMinSplitKb = 8;
+constexpr size_t kSplitFlagBytes = 64 << 10;
+std::atomic<uint32_t> g_split_ticket{0};
+
+int plan_tail_split(Dev *d, GemmArgs &a, int slots, size_t part_bytes, int flags_per_part,
+                    int &grid, bool allowed = true, bool single_wave_only = false) {
+    static int enabled = -1;
+    if (enabled < 0) {
+        const char *e = getenv("HEXCUDA_GEMM_SPLIT");
+        enabled = (e && atoi(e) == 0) ? 0 : 1;
+    }
+    const int tiles = a.tiles_m * a.tiles_n;
+    a.dp_tiles = tiles;
+    a.split = 1;
+    a.units = tiles;
+    a.ticket = 0;
+    a.part_flag = nullptr;
+    a.part_ws = nullptr;
+    grid = std::min(tiles, slots);
+    const int rem = tiles % slots;        // tiles of the last wave
+    if (!enabled || !allowed || rem == 0 || (single_wave_only && tiles > slots)) return HEXCUDA_OK;
+    const int split = std::min(std::min(slots / rem, a.num_kb / kMinSplitKb), kMaxSplit);
+    const size_t nparts = (size_t)rem * (size_t)(split - 1);
+    if (split < 2 || nparts * flags_per_part * sizeof(int) > kSplitFlagBytes) return HEXCUDA_OK;
+    uint8_t *buf =
+        reinterpret_cast<uint8_t *>(scratch(d, kSlotSplit, kSplitFlagBytes + nparts * part_bytes));
+    if (!buf) return hexcuda_last_error();
+    if (d->split_zeroed != buf || d->split_zeroed_bytes < kSplitFlagBytes) {
+        if (int rc = check(cudaMemsetAsync(buf, 0, kSplitFlagBytes, d->stream), "memset split flags"))
+            return rc;
+        d->split_zeroed = buf;
+        d->split_zeroed_bytes = kSplitFlagBytes;
+    }
+    uint32_t ticket = ++g_split_ticket;
+    if (ticket == 0) ticket = ++g_split_ticket;
+    a.dp_tiles = tiles - rem;
+    a.split = split;
+    a.units = a.dp_tiles + rem * split;
+    a.ticket = ticket;
+    a.part_flag = reinterpret_cast<int *>(buf);
+    a.part_ws = reinterpret_cast<int32_t *>(buf + kSplitFlagBytes);
+    grid = a.dp_tiles > 0 ? slots : rem * split;
+    return HEXCUDA_OK;
+}
+
 template <MmaKind KIND, int BN, int EPI, bool AS, bool BS, bool BMN = false>
 int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int M, int N, int K,
-                       const EpiParams &ep, bool pdl = false) {
+                       const EpiParams &ep, bool pdl = false, bool allow_split = true) {
     using L = Smem<BN>;
     auto kern = gemm_tc_kernel<KIND, BN, EPI, AS, BS, BMN>;
     static bool attr_done[64] = {};
@@ -1200,8 +1480,13 @@ int launch_gemm_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, int
     args.err_word = d->err_word;
     args.epi = ep;
     pick_raster(args, kBM, BN, (int64_t)args.num_kb * kBKBytes);
-    int tiles = args.tiles_m * args.tiles_n;
-    int grid = tiles < d->sms ? tiles : d->sms;
+    int grid = 0;
+    // integer GEMMs only: int32 parts add exactly, so the result does not
+    // depend on the split (an fp16 GEMM's would, by its fp32 rounding, and
+    // with it on how the caller's rows were cut into launches)
+    if (int rc = plan_tail_split(d, args, d->sms, (size_t)kBM * BN * 4, 8, grid,
+                                 allow_split && KIND == MmaKind::I8))
+        return rc;
     if (pdl) {
         // a programmatic dependent of the column-sum pass launched just before
         cudaLaunchAttribute attr[1];
@@ -1271,8 +1556,14 @@ int launch_gemm2_kernel(Dev *d, const CUtensorMap &ta, const CUtensorMap &tb, in
     args.err_word = d->err_word;
     args.epi = ep;
     pick_raster(args, 256, 256, (int64_t)args.num_kb * kBKBytes);
-    const int tiles = args.tiles_m * args.tiles_n;
-    const int pairs = tiles < pairs_resident[dev_slot] ? tiles : pairs_resident[dev_slot];
+    int pairs = 0;
+    // integer GEMMs only (as the one-SM kernel), and only when all tiles fit
+    // in one wave: behind full waves the split tail measured slower here
+    // (HMX int32 out, 2048 x 8192 x 8192: 0.139 -> 0.149 ms), the previous
+    // tile's heavy epilogue delaying the parts' hand-over
+    if (int rc = plan_tail_split(d, args, pairs_resident[dev_slot], (size_t)256 * 256 * 4, 16,
+                                 pairs, KIND == MmaKind::I8, true))
+        return rc;
     cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
     cfg.numAttrs = pdl ? 2 : 1;
     if (int rc = check(cudaLaunchKernelEx(&cfg, kern, ta, tb, args), "launch gemm pair kernel"))
@@ -1365,10 +1656,14 @@ int run_gemm(int dev, const void *A, int64_t lda, const void *B, bool b_kmajor, 
                       (int64_t)N * esize >= 128 && K >= kelems;
     if (b_mn) {
         if (want_colsum) {
-            const int kchunk = 64;
-            dim3 g((unsigned)((N + 16 * 128 - 1) / (16 * 128)), (unsigned)((K + kchunk - 1) / kchunk));
-            colsum_kernel<<<g, 128, 0, d->stream>>>(reinterpret_cast<const int8_t *>(B), colsum, K,
-                                                     N, kchunk, 1);
+            // about four 256-thread blocks per SM, each at most kColsumRows rows
+            const int nblk = (N + 511) / 512;
+            const int splits = std::max(1, (4 * d->sms + nblk - 1) / nblk);
+            int kchunk = (K + splits - 1) / splits;
+            kchunk = std::min(kColsumRows, std::max(32, (kchunk + 31) / 32 * 32));
+            dim3 g((unsigned)nblk, (unsigned)((K + kchunk - 1) / kchunk));
+            colsum_kernel<<<g, 256, 0, d->stream>>>(reinterpret_cast<const int8_t *>(B), colsum, K,
+                                                     N, kchunk);
             nl++;
             pdl = true;
         }
@@ -2163,13 +2458,16 @@ HX_EXPORT int hexcuda_gemm_u8s8_pc_noalloc(int dev, const uint8_t *A, const int8
     if (N <= 128) {
         if ((rc = make_kmajor_map(&tb, np->bt, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Kp, N, Kp, 128)))
             return rc;
+        // no tail split: its workspace would be allocated scratch
         rc = launch_gemm_kernel<MmaKind::I8, 128, kEpiRequant, false, true>(d, ta, tb, M, N,
-                                                                            (int)Kp, ep);
+                                                                            (int)Kp, ep, false,
+                                                                            false);
     } else {
         if ((rc = make_kmajor_map(&tb, np->bt, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Kp, N, Kp, 256)))
             return rc;
         rc = launch_gemm_kernel<MmaKind::I8, 256, kEpiRequant, false, true>(d, ta, tb, M, N,
-                                                                            (int)Kp, ep);
+                                                                            (int)Kp, ep, false,
+                                                                            false);
     }
     if (rc) return rc;
     return launch_end(d, "gemm_u8s8_pc_noalloc", 2);

@@ -13,8 +13,9 @@
 
 namespace hx {
 
-constexpr int kScratchSlots = 25;
+constexpr int kScratchSlots = 26;
 constexpr int kSlotReplica = 24;  // replicated output of the last host entry (collective.cpp)
+constexpr int kSlotSplit = 25;    // GEMM tail split: arrival flags + partial accumulators (gemm.cu)
 constexpr int kPipeChunks = 64;     // max chunks in flight per pipelined host call
 
 // Per-device state.  `stream` is where every launcher enqueues work; it is the
@@ -33,6 +34,10 @@ struct Dev {
     cudaEvent_t ev_in[kPipeChunks] = {}, ev_done[kPipeChunks] = {};
     void *slot_ptr[kScratchSlots] = {};
     size_t slot_bytes[kScratchSlots] = {};
+    // the GEMM tail split's flag region: which buffer and how many bytes of
+    // it have been zeroed (flags are only ever written with launch tickets)
+    void *split_zeroed = nullptr;
+    size_t split_zeroed_bytes = 0;
 };
 
 // Device slot -> state; records HEXCUDA_ERR_NODEV and returns null when the
@@ -82,6 +87,7 @@ enum : int {
     kErrWaitEmpty = 2,     // producer wait on a free-stage barrier expired
     kErrWaitAccum = 4,     // accumulator hand-off wait expired
     kErrWaitOther = 8,
+    kErrWaitPart = 16,     // GEMM tail split: wait for another CTA's partial expired
 };
 
 }  // namespace hx

@@ -158,6 +158,11 @@ void *scratch(Dev *d, int slot, size_t bytes) {
         d->slot_ptr[slot] = nullptr;
         d->slot_bytes[slot] = 0;
     }
+    if (slot == kSlotSplit) {
+        // a new buffer: its flag region is zeroed again before first use
+        d->split_zeroed = nullptr;
+        d->split_zeroed_bytes = 0;
+    }
     size_t want = (bytes + 4095) & ~(size_t)4095;
     void *p = nullptr;
     if (check(cudaMalloc(&p, want), "cudaMalloc(scratch)")) return nullptr;

@@ -335,6 +335,100 @@ def test_hmx_benchmark_shape(hx):
     assert (got > 0).mean() > 0.3
 
 
+def _dev_gemm(kind, d, rows):
+    """One device-pointer launch over rows [0, rows) of the benchmark inputs
+    (the per-rank problem of an 8-way row split when rows = 2048)."""
+    import torch
+
+    from hexkernels_b200 import _lib
+    lib = _lib.load()
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda() for k, v in d.items()
+         if isinstance(v, np.ndarray)}
+    A = t["A"][:rows].contiguous()
+    K, N = d["B"].shape
+    if kind == "u8s8":
+        out = torch.empty((rows, N), dtype=torch.uint8, device="cuda")
+        _lib.check(lib.hexcuda_gemm_u8s8_pc(0, A.data_ptr(), t["B"].data_ptr(),
+                                            t["bias"].data_ptr(), out.data_ptr(), rows, N, K,
+                                            d["zpA"], t["mult"].data_ptr(), t["shift"].data_ptr(),
+                                            d["zp_out"]))
+    else:
+        out = torch.empty((rows, N), dtype=torch.int32, device="cuda")
+        _lib.check(lib.hexcuda_gemm_hmx_ex(0, A.data_ptr(), t["B"].data_ptr(), 0,
+                                           t["bias"].data_ptr(), None, 0, None, out.data_ptr(),
+                                           hx_store("i32"), hx_act("relu"), 0, rows, N, K, 0))
+    _lib.check(lib.hexcuda_sync(0))
+    return out.cpu().numpy()
+
+
+def hx_store(name):
+    from hexkernels_b200 import ops
+    return ops.HMX_STORE[name][0]
+
+
+def hx_act(name):
+    from hexkernels_b200 import ops
+    return ops.HMX_ACT[name]
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("kind", ["u8s8", "hmx"])
+def test_split_tail_at_eight_way_shard(hx, kind):
+    """2048 x 8192 x 8192 (the benchmark GEMMs' per-rank rows at 8 GPUs):
+    512 one-SM tiles for u8s8, whose last wave is cut into two K parts per
+    tile; 256 CTA-pair tiles for HMX (not split behind full waves).  Rows
+    0..2047 must equal the oracle's per-row CRC32s of the full benchmark
+    output."""
+    mk, d = _crc_inputs(kind)
+    got = _dev_gemm(kind, d, 2048)
+    exp = np.load(mk.FILES[kind])[:2048]
+    bad = np.flatnonzero(mk.row_crcs(got) != exp)
+    assert bad.size == 0, f"{bad.size} rows differ, first {bad[:8]}"
+
+
+def test_split_tail_small_shapes_exact(hx, oracle):
+    """Fewer tiles than SMs with a deep K: every tile is cut into K parts
+    (u8s8 128 x 256 tiles: 4 tiles, 4 parts over 33 K blocks, ragged; HMX
+    CTA pairs: 4 pair tiles, 2 parts) and merged exactly."""
+    rng = np.random.default_rng(21)
+    M, N, K = 256, 384, 4224
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    bias = np.round(rng.normal(0, 3000, N)).astype(np.int32)
+    mult = rng.integers(2**30, 2**31, N, dtype=np.int64).astype(np.int32)
+    shift = rng.integers(38, 44, N).astype(np.int32)
+    np.testing.assert_array_equal(hx.gemm_u8s8_pc(A, B, bias, 77, mult, shift, 128),
+                                  oracle.gemm_u8s8_pc(A, B, bias, 77, mult, shift, 128))
+    M, N, K = 512, 512, 2048
+    A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+    B = rng.integers(-128, 128, (K, N), dtype=np.int8)
+    bias = rng.integers(-3000, 3000, N).astype(np.int32)
+    res = rng.integers(-128, 128, (M, N), dtype=np.int8)
+    for kw in (dict(store="i32", act="relu", bias=bias), dict(store="i8_sat", res=res, zpA=9),
+               dict(store="acc_i32")):
+        np.testing.assert_array_equal(hx.gemm_hmx_ex(A, B, **kw), oracle.gemm_hmx_ex(A, B, **kw),
+                                      err_msg=str(sorted(kw)))
+    # s8 x s8 requant GEMM: 2 row tiles of one 256-column tile, 2 parts
+    A8 = rng.integers(-128, 128, (256, 2048), dtype=np.int8)
+    B8 = rng.integers(-128, 128, (2048, 256), dtype=np.int8)
+    got = hx.gemm_i8_requant(A8, B8, 1 << 30, 42, 3)
+    np.testing.assert_array_equal(got, oracle.gemm_i8_requant(A8, B8, 1 << 30, 42, 3))
+    assert 20 < got.std() < 100
+
+
+def test_f16_gemm_never_split(hx):
+    """fp16 GEMMs with fewer tiles than SMs and a deep K are not cut into K
+    parts: a 100-row launch gives the same bits as the same rows inside a
+    16-row-tile launch (one-SM kernel) and a 512-row launch (CTA pairs)."""
+    rng = np.random.default_rng(22)
+    K, N = 8192, 512
+    A = (rng.standard_normal((2048, K)) / np.sqrt(K)).astype(np.float16)
+    Bt = rng.standard_normal((N, K)).astype(np.float16)
+    full = hx.gemm_f16_nt(A, Bt)
+    np.testing.assert_array_equal(hx.gemm_f16_nt(A[:100], Bt), full[:100])
+    np.testing.assert_array_equal(hx.gemm_f16_nt(A[:512], Bt), full[:512])
+
+
 @pytest.mark.slow
 def test_f16_benchmark_shape(hx, oracle):
     """fp16 GEMM M=N=K=8192, A row-major, B column-major, N(0,1)/sqrt(K):

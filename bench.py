@@ -19,6 +19,8 @@ larger than the 126 MB L2 so no flush is needed between steps):
 With N > 1 (torchrun) the rows (M rows, or B*H heads) are split across the
 ranks (strong scaling, no data-path collective); each rank times on its own
 device with CUDA events and the job time is the max over ranks.
+`--shard-of N` on one GPU times rank 0's part of an N-way split instead (the
+per-rank problem of an N-GPU run, without the other ranks).
 
 Rank 0 prints one JSON line.  `--impl reference` times the reference's scalar
 CPU code (or its restatement where the reference has no such shape) on all
@@ -1020,8 +1022,12 @@ def run_ours(args, dist):
         C.memmove(uid, box[0], 128)
         check(lib.hexcuda_comm_init_rank(dist.world, dist.rank, uid, 128))
 
+    # --shard-of N: this one GPU times rank 0's part of an N-way row split
+    wl_world, wl_rank = ((args.shard_of, 0) if args.shard_of > 1 and dist.world == 1
+                         else (dist.world, dist.rank))
+
     def measure(wl_cls, steps, cpu_budget):
-        wl = wl_cls(dist.world, dist.rank)
+        wl = wl_cls(wl_world, wl_rank)
         wl.setup_device(torch)
         t = time_device(wl, torch, device, steps, args.warmup, dist, lib)
         ms_max = dist.max(t["ms"])
@@ -1084,7 +1090,7 @@ def run_ours(args, dist):
         gb_in, gb_out = e["h2d_bytes_per_step"] / 1e9, e["d2h_bytes_per_step"] / 1e9
         t_copy = max(gb_in / pcie["h2d_gbs"], gb_out / pcie["d2h_gbs"],
                      (gb_in + gb_out) / pcie["duplex_gbs"])
-        wl0 = WORKLOADS[args.workload](dist.world, dist.rank)
+        wl0 = WORKLOADS[args.workload](wl_world, wl_rank)
         e["pcie"] = dict(pcie, ceiling=round(wl0.units_per_step() / t_copy / wl0.scale(), 3))
     ops_out = {}
     if args.ops == "all":
@@ -1120,6 +1126,8 @@ def run_ours(args, dist):
             line[k] = head[k]
     if ops_out:
         line["ops"] = ops_out
+    if wl_world != dist.world:
+        line["shard_of"] = {"parts": wl_world, "timed": "rank 0's part on this GPU"}
     if replicate:
         check(lib.hexcuda_comm_destroy())
     return line
@@ -1177,6 +1185,10 @@ def main():
                     help="timed steps of each extra op (at least --steps)")
     ap.add_argument("--op-cpu-budget", type=float, default=2.5,
                     help="seconds of CPU work per extra op's cpu_baseline sample (0: none)")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="one GPU: time rank 0's row shard of an N-way split (the per-rank "
+                         "problem of an N-GPU run); value = the whole problem's units over "
+                         "that time")
     ap.add_argument("--replicate", action="store_true",
                     help="N > 1: also all-gather every sharded output over NCCL (timed apart)")
     args = ap.parse_args()

@@ -244,15 +244,31 @@ int run_pipelined(int64_t rows, std::initializer_list<RowIn> in_list, void *host
     return rc;
 }
 
-constexpr int64_t kRowChunkBytes = 32ll << 20;    // row operators
-constexpr int64_t kGemmChunkBytes = 16ll << 20;   // GEMMs along M, attention along heads
+// Chunk size of the pipelined entries: 32 MiB for the row operators, 16 MiB
+// for GEMMs along M and attention along heads.  Measured through the host
+// entries with pinned buffers on one B200 (two runs each): the fp32
+// softmax + layernorm pair over 65536 x 4096 moved 91.7 GB/s with 32 MiB
+// chunks and 86.1 GB/s with 8 MiB chunks (smaller copies cost more per byte
+// than their shorter fill and drain save); the benchmark GEMMs and attention
+// ran 1-7 % slower with 8 MiB chunks than with 16 MiB.
+// HEXCUDA_PIPE_CHUNK_MB overrides both (a tuning knob).
+int64_t pipe_chunk_bytes(int64_t dflt) {
+    static int64_t env = -1;
+    if (env < 0) {
+        const char *e = getenv("HEXCUDA_PIPE_CHUNK_MB");
+        env = (e && atoi(e) > 0) ? (int64_t)atoi(e) << 20 : 0;
+    }
+    return env > 0 ? env : dflt;
+}
+constexpr int64_t kRowChunkBytes = 32ll << 20;
+constexpr int64_t kGemmChunkBytes = 16ll << 20;
 
 // The row operators: one row-sharded input.
 int run_rows_pipelined(int64_t rows, const void *host_in, size_t in_row_bytes, void *host_out,
                        size_t out_row_bytes, const std::function<int(Part &)> &stage_replicated,
                        const std::function<int(Part &, const void *, void *, int64_t)> &launch) {
     return run_pipelined(rows, {RowIn{host_in, in_row_bytes, kSlotIn0}}, host_out, out_row_bytes,
-                         kRowChunkBytes, stage_replicated,
+                         pipe_chunk_bytes(kRowChunkBytes), stage_replicated,
                          [&](Part &p, const uint8_t *const *din, void *dout, int64_t nr) {
                              return launch(p, din[0], dout, nr);
                          });
@@ -483,7 +499,8 @@ HX_EXPORT int hexcuda_host_gemm_u8s8_pc(const uint8_t *A, const int8_t *B, const
     };
     std::vector<Rep> rep(dev_count());
     return run_pipelined(
-        M, {RowIn{A, (size_t)K, kSlotIn0}}, out, (size_t)N, kGemmChunkBytes,
+        M, {RowIn{A, (size_t)K, kSlotIn0}}, out, (size_t)N,
+        pipe_chunk_bytes(kGemmChunkBytes),
         [&](Part &p) {
             Rep &r = rep[(size_t)p.slot];
             r.B = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
@@ -511,7 +528,8 @@ HX_EXPORT int hexcuda_host_requant_ew(const void *a, int a_i8, const void *b, in
     // one element per row; chunks of a multiple of 16 elements keep every
     // operand's chunk 16-byte aligned
     return run_pipelined(
-        n, {RowIn{a, ea, kSlotIn0}, RowIn{b, b_kind ? eb : 0, kSlotIn1}}, out, 1, kRowChunkBytes,
+        n, {RowIn{a, ea, kSlotIn0}, RowIn{b, b_kind ? eb : 0, kSlotIn1}}, out, 1,
+        pipe_chunk_bytes(kRowChunkBytes),
         [&](Part &p) {
             dl[(size_t)p.slot] = lut ? stage_in(p.d, kSlotIn2, lut, 256) : nullptr;
             return (!lut || dl[(size_t)p.slot]) ? HEXCUDA_OK : hexcuda_last_error();
@@ -582,7 +600,7 @@ HX_EXPORT int hexcuda_host_gemm_hmx_ex(const uint8_t *A, const int8_t *B, int b_
             M,
             {RowIn{A, (size_t)K, kSlotIn0},
              RowIn{res, res_kind ? (size_t)N * rsize : 0, kSlotIn3}},
-            out, (size_t)N * osize, kGemmChunkBytes,
+            out, (size_t)N * osize, pipe_chunk_bytes(kGemmChunkBytes),
             [&](Part &p) {
                 Rep &r = rep[(size_t)p.slot];
                 r.B = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
@@ -639,7 +657,8 @@ HX_EXPORT int hexcuda_host_gemm_hmx(const uint8_t *A, const int8_t *B, int b_tra
     std::vector<const int8_t *> dB(dev_count());
     std::vector<const int32_t *> dbias(dev_count());
     return run_pipelined(
-        M, {RowIn{A, (size_t)K, kSlotIn0}}, out, (size_t)N * osize, kGemmChunkBytes,
+        M, {RowIn{A, (size_t)K, kSlotIn0}}, out, (size_t)N * osize,
+        pipe_chunk_bytes(kGemmChunkBytes),
         [&](Part &p) {
             const size_t s = (size_t)p.slot;
             dB[s] = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
@@ -766,7 +785,7 @@ HX_EXPORT int hexcuda_host_gemm_f16_ex(const uint16_t *A, const uint16_t *B, int
     // without a residual the second row input has no bytes and is not read
     return run_pipelined(
         M, {RowIn{A, 2 * (size_t)K, kSlotIn0}, RowIn{res, res ? 2 * (size_t)N : 0, kSlotIn3}},
-        out, 2 * (size_t)N, kGemmChunkBytes,
+        out, 2 * (size_t)N, pipe_chunk_bytes(kGemmChunkBytes),
         [&](Part &p) {
             const size_t s = (size_t)p.slot;
             dB[s] = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
@@ -886,7 +905,8 @@ HX_EXPORT int hexcuda_host_gemm_f16_nt(const uint16_t *A, const uint16_t *Bt, ui
     if (int rc = null_check("host_gemm_f16_nt", {A, Bt, out})) return rc;
     std::vector<const uint16_t *> dB(dev_count());
     return run_pipelined(
-        M, {RowIn{A, 2 * (size_t)K, kSlotIn0}}, out, 2 * (size_t)N, kGemmChunkBytes,
+        M, {RowIn{A, 2 * (size_t)K, kSlotIn0}}, out, 2 * (size_t)N,
+        pipe_chunk_bytes(kGemmChunkBytes),
         [&](Part &p) {
             dB[(size_t)p.slot] = stage_in(p.d, kSlotIn1, Bt, (size_t)N * K);
             return dB[(size_t)p.slot] ? HEXCUDA_OK : hexcuda_last_error();
@@ -904,7 +924,8 @@ HX_EXPORT int hexcuda_host_gemm_f16_nn(const uint16_t *A, const uint16_t *B, uin
     if (int rc = null_check("host_gemm_f16_nn", {A, B, out})) return rc;
     std::vector<const uint16_t *> dB(dev_count());
     return run_pipelined(
-        M, {RowIn{A, 2 * (size_t)K, kSlotIn0}}, out, 2 * (size_t)N, kGemmChunkBytes,
+        M, {RowIn{A, 2 * (size_t)K, kSlotIn0}}, out, 2 * (size_t)N,
+        pipe_chunk_bytes(kGemmChunkBytes),
         [&](Part &p) {
             dB[(size_t)p.slot] = stage_in(p.d, kSlotIn1, B, (size_t)K * N);
             return dB[(size_t)p.slot] ? HEXCUDA_OK : hexcuda_last_error();
@@ -925,7 +946,7 @@ HX_EXPORT int hexcuda_host_attn_f16(const uint16_t *Q, const uint16_t *K, const 
     const size_t qh = (size_t)SQ * D, kh = (size_t)SK * D;
     return run_pipelined(
         BH, {RowIn{Q, 2 * qh, kSlotIn0}, RowIn{K, 2 * kh, kSlotIn1}, RowIn{V, 2 * kh, kSlotIn2}},
-        O, 2 * qh, kGemmChunkBytes, [](Part &) { return HEXCUDA_OK; },
+        O, 2 * qh, pipe_chunk_bytes(kGemmChunkBytes), [](Part &) { return HEXCUDA_OK; },
         [&](Part &p, const uint8_t *const *din, void *dout, int64_t nh) {
             return hexcuda_attn_f16(p.slot, (const uint16_t *)din[0], (const uint16_t *)din[1],
                                     (const uint16_t *)din[2], (uint16_t *)dout, (int)nh, SQ, SK,

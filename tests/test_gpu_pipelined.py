@@ -2,8 +2,9 @@
 attention along heads, the elementwise requant): shapes large enough for
 several chunks, with a ragged last chunk, give the same bytes as one
 device-pointer launch over the whole problem, and the integer GEMMs equal
-the oracle.  A chunk holds a multiple of 16 rows of about 16 MiB (counted on
-the larger of a row's input and output bytes)."""
+the oracle.  A chunk holds a multiple of 16 rows of about 16 MiB for GEMMs
+and attention, 32 MiB for the row operators and the elementwise requant
+(counted on the larger of a row's input and output bytes)."""
 import numpy as np
 import pytest
 
@@ -113,7 +114,8 @@ def test_attention_head_chunks_equal_one_launch(hx, causal):
     from hexkernels_b200 import _lib
     torch = _torch()
     rng = np.random.default_rng(16)
-    # 768 KiB of Q, K, V per head -> 32 heads per chunk: chunks 32, 32, 6
+    # 768 KiB of Q, K, V per head -> 32 heads per chunk (21 rounded up to
+    # a multiple of 16): chunks 32, 32, 6
     BH, S, D = 70, 1024, 128
     Q = rng.standard_normal((BH, S, D)).astype(np.float16)
     K = rng.standard_normal((BH, S, D)).astype(np.float16)

@@ -1276,7 +1276,8 @@ __global__ void __launch_bounds__(256) colsum_kernel(const int8_t *__restrict__ 
 }
 
 // colsum[n] = sum_k Bt[n][k] for a K-major int8 Bt [N, K] (pitch ldb): one
-// warp per row, 16-byte loads where the row allows them.
+// warp per row, 16-byte loads where the row allows them (four in flight per
+// lane), each word's four signed bytes summed by one dp4a against ones.
 __global__ void __launch_bounds__(256) rowsum_i8_kernel(const int8_t *__restrict__ Bt,
                                                         int64_t ldb, int32_t *__restrict__ colsum,
                                                         int N, int K, int vec) {
@@ -1288,13 +1289,23 @@ __global__ void __launch_bounds__(256) rowsum_i8_kernel(const int8_t *__restrict
     int32_t s = 0;
     int k0 = 0;
     if (vec) {
+        constexpr int kOnes = 0x01010101;
         const int kv = K & ~15;
-        for (int k = lane * 16; k < kv; k += 32 * 16) {
-            const int4 q = __ldg(reinterpret_cast<const int4 *>(row + k));
-            const int w[4] = {q.x, q.y, q.z, q.w};
+        auto add = [&](const int4 q) {
+            s = __dp4a(q.x, kOnes, s);
+            s = __dp4a(q.y, kOnes, s);
+            s = __dp4a(q.z, kOnes, s);
+            s = __dp4a(q.w, kOnes, s);
+        };
+        int k = lane * 16;
+        for (; k + 3 * 512 < kv; k += 4 * 512) {
+            int4 q[4];
 #pragma unroll
-            for (int i = 0; i < 16; i++) s += (int32_t)(int8_t)(w[i >> 2] >> (8 * (i & 3)));
+            for (int u = 0; u < 4; u++) q[u] = __ldg(reinterpret_cast<const int4 *>(row + k + u * 512));
+#pragma unroll
+            for (int u = 0; u < 4; u++) add(q[u]);
         }
+        for (; k < kv; k += 512) add(__ldg(reinterpret_cast<const int4 *>(row + k)));
         k0 = kv;
     }
     for (int k = k0 + lane; k < K; k += 32) s += row[k];

@@ -202,3 +202,26 @@ def test_host_entry_as_first_call_of_a_process(name):
                        timeout=300)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), (r.returncode, r.stdout,
                                                                     r.stderr[-2000:])
+
+
+def test_pipelined_entries_empty_inputs(hx):
+    """Zero rows (and zero columns) through every pipelined entry: nothing to
+    do, no error, empty outputs."""
+    u8 = np.zeros((0, 256), np.uint8)
+    B = np.zeros((256, 64), np.int8)
+    v32 = np.zeros(64, np.int32)
+    assert hx.gemm_u8s8_pc(u8, B, v32, 3, v32 + (1 << 30), v32 + 40, 128).shape == (0, 64)
+    assert hx.gemm_hmx_ex(u8, B, "i32", "relu", bias=v32).shape == (0, 64)
+    assert hx.gemm_hmx(u8, B, 0).shape == (0, 64)
+    assert hx.gemm_f16_nt(np.zeros((0, 64), np.float16),
+                          np.zeros((32, 64), np.float16)).shape == (0, 32)
+    assert hx.gemm_f16_nt(np.zeros((8, 64), np.float16),
+                          np.zeros((0, 64), np.float16)).shape == (8, 0)
+    q = np.zeros((0, 128, 128), np.float16)
+    assert hx.attn_f16(q, q, q, 0.125, True).shape == (0, 128, 128)
+    z = np.zeros(0, np.int32)
+    assert hx.requant_ew(z, z, pre="add", mult=1 << 30, shift=31).shape == (0,)
+    x = np.zeros((0, 512), np.float32)
+    assert hx.softmax(x).shape == (0, 512)
+    assert hx.layernorm(x, np.ones(512, np.float32), np.zeros(512, np.float32),
+                        1e-5).shape == (0, 512)

@@ -66,7 +66,7 @@ int launch_end(Dev *d, const char *name, int nlaunches = 1);
 
 // Which kinds of kernel ran (hexcuda_mechanisms): the launchers of the
 // tcgen05 / TMA kernels record their bits here at every launch.
-enum : unsigned { kMechTcgen05 = 1u, kMechTma = 2u };
+enum : unsigned { kMechTcgen05 = 1u, kMechTma = 2u, kMechVec128 = 4u };
 void note_mech(unsigned bits);
 
 // Replicated outputs (collective.cpp): whether the caller asked for them, and

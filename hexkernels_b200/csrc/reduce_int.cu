@@ -344,6 +344,7 @@ int reduce_launch(Dev *d, const void *a, const void *b, int64_t n, long long bas
     if (!part) return HEXCUDA_ERR_OOM;
     launch_begin(d);
     if (blocks > 0) kern<<<blocks, 256, 0, d->stream>>>(a, b, n, vec, part);
+    if (blocks > 0 && vec) note_mech(kMechVec128);
     // the finalize as a programmatic dependent: its launch overlaps the
     // partials kernel's tail instead of following it
     cudaLaunchAttribute attr[1];

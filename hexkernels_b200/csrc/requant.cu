@@ -347,6 +347,7 @@ HX_EXPORT int hexcuda_requantize_i32_u8(int dev, const int32_t *a, uint8_t *out,
     launch_begin(d);
     requantize_i32_u8_kernel<<<(unsigned)blocks, 256, 0, d->stream>>>(a, out, n, mult, shift,
                                                                        (int)zp, vec);
+    if (vec) note_mech(kMechVec128);
     return launch_end(d, "requantize_i32_u8");
 }
 
@@ -428,6 +429,7 @@ HX_EXPORT int hexcuda_requant_ew(int dev, const void *a, int a_i8, const void *b
         }
 #undef HX_RQ2
     }
+    if (vec) note_mech(kMechVec128);
     return launch_end(d, "requant_ew");
 }
 

@@ -320,6 +320,7 @@ int launch_rows(int dev, const T *x, const T *gamma, const T *beta, T *out, floa
         launch_reg<T, OP, 8>(d, x, gamma, beta, out, red_out, R, C, eps);
     else
         row_generic_kernel<T, OP><<<R, kNT, 0, d->stream>>>(x, gamma, beta, out, red_out, C, eps);
+    if (vec && nvec <= kNT * 8) note_mech(kMechVec128);
     return launch_end(d, name);
 }
 

@@ -33,12 +33,15 @@ option, so the verdict comes from two kinds of evidence:
     static  a scan of the candidate's own source (the hexcuda_* entries it
             calls, inline tcgen05 / TMA PTX) and of libhexcuda's sources:
             whether a called entry reaches, through the library's functions,
-            a kernel that issues tcgen05.mma or cp.async.bulk.tensor
-            (static_tcgen05, static_tma; "may", since an entry can choose
-            between kernels by shape);
+            a kernel that issues tcgen05.mma or cp.async.bulk.tensor, or
+            that moves 16-byte vectors (int4 / uint4 / float4 accesses, or
+            .v4 / .v8 global loads and stores in PTX) (static_tcgen05,
+            static_tma, static_vec128; "may", since an entry can choose
+            between kernels by shape and alignment);
     run     the library's own record of which kinds of kernel the call
             launched (hexcuda_mechanisms, printed as mech= on the timing
-            line): used_tcgen05, used_tma.
+            line): used_tcgen05, used_tma, and used_vec128 for the HBM-bound
+            kernels' 128-bit vector path (the north star's LDG.128).
 mechanism = "tcgen05" when the run launched tensor-core kernels, "cuda-core"
 when it launched only other kernels, "cpu" when it launched none.
 """
@@ -64,7 +67,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 _CORRECT = re.compile(r"^HVXENV_(CORRECT|INCORRECT) errors=(\d+) n=(\d+)", re.M)
 _TIMING = re.compile(r"^HEXCUDA_KERNEL_US kernel=(-?[0-9.]+) wall=([0-9.]+)(?: launches=(\d+))?"
                      r"(?: mech=0x([0-9a-fA-F]+))?", re.M)
-MECH_TCGEN05, MECH_TMA = 1, 2
+MECH_TCGEN05, MECH_TMA, MECH_VEC128 = 1, 2, 4
 _HXERR = re.compile(r"^HEXCUDA_ERROR.*$", re.M)
 
 
@@ -80,8 +83,8 @@ def new_feedback(task_id: str, candidate: str | None) -> dict:
         "launches": None,       # libhexcuda kernel launches made by the call
         "used_gpu": False,      # at least one libhexcuda launch ran
         # mechanism verdict: static source evidence, then what the run launched
-        "calls": [], "static_tcgen05": False, "static_tma": False,
-        "used_tcgen05": None, "used_tma": None, "mechanism": None,
+        "calls": [], "static_tcgen05": False, "static_tma": False, "static_vec128": False,
+        "used_tcgen05": None, "used_tma": None, "used_vec128": None, "mechanism": None,
         "error_text": "", "timed_out": False,
         "target": TARGET,
         "achieved": None, "AI": None, "binding_level": None, "ceiling": None, "eta": None,
@@ -112,6 +115,7 @@ def parse_output(stdout: str, stderr: str) -> dict:
                 bits |= int(m, 16)
             out["used_tcgen05"] = bool(bits & MECH_TCGEN05)
             out["used_tma"] = bool(bits & MECH_TMA)
+            out["used_vec128"] = bool(bits & MECH_VEC128)
         if "used_gpu" in out:
             out["mechanism"] = ("tcgen05" if out.get("used_tcgen05") else
                                 "cuda-core" if out["used_gpu"] else "cpu")
@@ -176,6 +180,8 @@ def attach_roofline(fb: dict, useful_ops, work_bytes, dtype: str = "",
 
 _TC_PTX = re.compile(r"tcgen05\.mma")
 _TMA_PTX = re.compile(r"cp\.async\.bulk\.tensor")
+_VEC128 = re.compile(r"\b(?:u?int4|float4|double2|u?longlong2)\b"
+                     r"|\b(?:ld|st)\.global[\w.:]*\.v[48]\b")
 _WORD = re.compile(r"\b[A-Za-z_]\w*\b")
 _CALL = re.compile(r"\b(hexcuda_\w+)\s*\(")
 
@@ -205,11 +211,12 @@ def _blank_strings(text: str) -> str:
     return "".join(out)
 
 
-def _top_level_functions(text: str) -> dict:
+def _top_level_functions(text: str, types: dict | None = None) -> dict:
     """name -> text (signature and body) of every function defined at
     namespace scope of one C++ / CUDA source (comments already removed).
-    Namespaces and extern "C" blocks are entered; types, initialisers and
-    declarations are skipped."""
+    Namespaces and extern "C" blocks are entered; initialisers and
+    declarations are skipped; struct / class / union definitions go to
+    `types` (name -> body, specialisations joined) when it is given."""
     funcs: dict = {}
     # preprocessor lines carry no code of interest and no statement end
     text = re.sub(r"(?m)^[ \t]*#[^\n]*", lambda m: " " * len(m.group(0)), text)
@@ -232,6 +239,10 @@ def _top_level_functions(text: str) -> dict:
                 depth += {"{": 1, "}": -1}.get(bl[j], 0)
                 j += 1
             is_type = re.match(r"(template\s*<.*>\s*)?(struct|class|enum|union)\b", head, re.S)
+            if is_type and types is not None:
+                m = re.search(r"\b(?:struct|class|union)\s+([A-Za-z_]\w*)", head)
+                if m:
+                    types.setdefault(m.group(1), []).append(text[head0:j])
             if "(" in head and not is_type and not head.endswith("="):
                 # name: the identifier before the last parenthesised group
                 k, depth_p = len(head) - 1, 0
@@ -257,30 +268,38 @@ _LIB_MECH = None
 
 
 def library_mechanisms() -> dict:
-    """hexcuda_* entry -> (reaches tcgen05.mma, reaches cp.async.bulk.tensor)
-    through the functions defined in libhexcuda's sources."""
+    """hexcuda_* entry -> (reaches tcgen05.mma, reaches cp.async.bulk.tensor,
+    reaches 16-byte vector accesses) through the functions defined in
+    libhexcuda's sources."""
     global _LIB_MECH
     if _LIB_MECH is not None:
         return _LIB_MECH
     funcs: dict = {}
     for f in sorted((PKG / "csrc").glob("*.c*")):
-        for k, v in _top_level_functions(_strip_comments(f.read_text())).items():
+        types: dict = {}
+        for k, v in _top_level_functions(_strip_comments(f.read_text()), types).items():
             funcs[k] = funcs.get(k, "") + "\n" + v
+        # a type's members count for the functions that name it (e.g. a
+        # vector-width trait whose loads a kernel uses)
+        for k, v in types.items():
+            funcs.setdefault(k, "")
+            funcs[k] += "\n" + "\n".join(v)
     names = set(funcs)
     edges = {k: (set(_WORD.findall(v)) & names) - {k} for k, v in funcs.items()}
-    own = {k: (bool(_TC_PTX.search(v)), bool(_TMA_PTX.search(v))) for k, v in funcs.items()}
+    own = {k: (bool(_TC_PTX.search(v)), bool(_TMA_PTX.search(v)), bool(_VEC128.search(v)))
+           for k, v in funcs.items()}
     memo: dict = {}
 
     def reach(k, stack=()):
         if k in memo:
             return memo[k]
-        tc, tma = own[k]
+        tc, tma, vec = own[k]
         for c in edges[k]:
             if c in stack:
                 continue
-            a, b = reach(c, stack + (k,))
-            tc, tma = tc or a, tma or b
-        memo[k] = (tc, tma)
+            a, b, v = reach(c, stack + (k,))
+            tc, tma, vec = tc or a, tma or b, vec or v
+        memo[k] = (tc, tma, vec)
         return memo[k]
 
     _LIB_MECH = {k: reach(k) for k in funcs if k.startswith("hexcuda_")}
@@ -289,14 +308,16 @@ def library_mechanisms() -> dict:
 
 def scan_candidate(path) -> dict:
     """Static evidence from a candidate's own source: the libhexcuda entries
-    it calls, and whether those (or its own inline PTX) reach tcgen05 MMAs
-    and TMA loads."""
+    it calls, and whether those (or its own code) reach tcgen05 MMAs, TMA
+    loads and 16-byte vector accesses."""
     text = _strip_comments(Path(path).read_text())
     calls = sorted(set(_CALL.findall(text)))
     lib = library_mechanisms()
-    tc = bool(_TC_PTX.search(text)) or any(lib.get(c, (False, False))[0] for c in calls)
-    tma = bool(_TMA_PTX.search(text)) or any(lib.get(c, (False, False))[1] for c in calls)
-    return {"calls": calls, "static_tcgen05": tc, "static_tma": tma}
+    none = (False, False, False)
+    tc = bool(_TC_PTX.search(text)) or any(lib.get(c, none)[0] for c in calls)
+    tma = bool(_TMA_PTX.search(text)) or any(lib.get(c, none)[1] for c in calls)
+    vec = bool(_VEC128.search(text)) or any(lib.get(c, none)[2] for c in calls)
+    return {"calls": calls, "static_tcgen05": tc, "static_tma": tma, "static_vec128": vec}
 
 
 def find_task_dir(corpus: Path, task_id: str) -> Path | None:

@@ -85,12 +85,14 @@ float hexcuda_last_kernel_ms(void);
 /* Number of kernels libhexcuda has launched since load (all devices). */
 uint64_t hexcuda_launch_count(void);
 /* Kinds of kernel launched since the last reset (reset != 0 clears after
- * reading): bit 0 tcgen05 tensor-core MMA kernels, bit 1 TMA-fed kernels.
+ * reading): bit 0 tcgen05 tensor-core MMA kernels, bit 1 TMA-fed kernels,
+ * bit 2 HBM-bound kernels on their 128-bit vector load / store path.
  * The evaluator's mechanism verdict (hexkernels_b200/evaluate.py) reads it
  * around each candidate_kernel call: the B200 counterpart of the reference's
  * used_hvx / used_hmx / used_dma flags (hexkernels/core/evaluate.py:573-597). */
 #define HEXCUDA_MECH_TCGEN05 1u
 #define HEXCUDA_MECH_TMA 2u
+#define HEXCUDA_MECH_VEC128 4u
 unsigned hexcuda_mechanisms(int reset);
 
 /* ------------------------------------------ multi-GPU: shards and replicas */

@@ -101,6 +101,8 @@ def test_evaluate_prebuilt_harness_on_gpu(hx, task):
     if task in ("fp16_softmax", "residual_add_requant"):
         assert not fb["static_tcgen05"] and fb["used_tcgen05"] is False
         assert fb["mechanism"] == "cuda-core"
+        # HBM-bound: the 16-byte vector path (rows of 256 fp16; 1024 bytes)
+        assert fb["static_vec128"] and fb["used_vec128"]
 
 
 def test_mechanism_fields_from_the_timing_line():
@@ -114,7 +116,9 @@ def test_mechanism_fields_from_the_timing_line():
     # several timed calls: the bits of all of them
     p = ev.parse_output("HEXCUDA_KERNEL_US kernel=1.0 wall=2.0 launches=1 mech=0x0\n"
                         "HEXCUDA_KERNEL_US kernel=1.0 wall=2.0 launches=1 mech=0x1\n", "")
-    assert p["used_tcgen05"] and not p["used_tma"]
+    assert p["used_tcgen05"] and not p["used_tma"] and p["used_vec128"] is False
+    p = ev.parse_output("HEXCUDA_KERNEL_US kernel=1.0 wall=2.0 launches=1 mech=0x4\n", "")
+    assert p["used_vec128"] and not p["used_tcgen05"] and p["mechanism"] == "cuda-core"
 
 
 def test_static_scan_tells_scalar_from_tensor_core_candidates(tmp_path):
@@ -128,12 +132,14 @@ void candidate_kernel(const int8_t *A, const int8_t *B, int8_t *out, int M, int 
 }
 """)
     s = ev.scan_candidate(scalar)
-    assert s == {"calls": [], "static_tcgen05": False, "static_tma": False}
+    assert s == {"calls": [], "static_tcgen05": False, "static_tma": False,
+                 "static_vec128": False}
     s = ev.scan_candidate(REPO / "hexkernels_b200" / "shims" / "i8_gemm_requant.c")
     assert s["calls"] == ["hexcuda_host_gemm_i8_requant"]
     assert s["static_tcgen05"] and s["static_tma"]
     s = ev.scan_candidate(REPO / "hexkernels_b200" / "shims" / "fp16_softmax.c")
     assert s["calls"] and not s["static_tcgen05"] and not s["static_tma"]
+    assert s["static_vec128"]           # the row kernels' 16-byte vector path
     own = tmp_path / "own.cu"
     own.write_text('__global__ void k() { asm volatile("tcgen05.mma.cta_group::1.kind::f16 '
                    '[%0], %1, %2, %3, p;" ::); }\n')
@@ -145,7 +151,9 @@ def test_library_mechanism_map():
     m = ev.library_mechanisms()
     for e in ("hexcuda_host_gemm_u8s8_pc", "hexcuda_host_gemm_f16_nt", "hexcuda_host_attn_f16",
               "hexcuda_host_gemm_hmx_ex", "hexcuda_gemm_u8s8_pc_noalloc"):
-        assert m[e] == (True, True), e
+        assert m[e][:2] == (True, True), e
+    # the HBM-bound operators: no tensor cores, 16-byte vector loads / stores
     for e in ("hexcuda_host_softmax_f32", "hexcuda_host_layernorm_f32", "hexcuda_host_rowreduce_f32",
-              "hexcuda_host_requant_ew", "hexcuda_host_reduce_int"):
-        assert m[e] == (False, False), e
+              "hexcuda_host_requant_ew", "hexcuda_host_reduce_int", "hexcuda_softmax_f32",
+              "hexcuda_reduce_int"):
+        assert m[e] == (False, False, True), e

@@ -18,13 +18,17 @@
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile
 // i+1.  Tiles are walked in groups sized from the L2 capacity (pick_raster):
 // a panel of one operand stays resident in L2 while the other streams past it
-// once per group, and the CTAs of a wave share the streamed blocks.
+// once per group, and the CTAs of a wave share the streamed blocks.  When
+// the last wave would leave most CTAs idle, the integer GEMMs cut its tiles
+// into K parts run by separate CTAs (tail split, unit_of).  A CTA-pair
+// variant (gemm_tc2_kernel, cta_group::2) computes 256 x 256 tiles on two SMs.
 //
 // Operand preparation (HBM-bound pre-passes, only where needed): a row-major
-// B[K,N] is transposed into a K-major copy (and, for the zero-point GEMMs, its
-// int32 column sums are accumulated in the same pass); an A whose row pitch is
-// not a multiple of 16 bytes is copied into a padded buffer, because TMA rows
-// must start on 16-byte boundaries.
+// B[K,N] whose rows TMA can address is read in place as an MN-major operand,
+// else transposed into a K-major copy; the zero-point GEMMs' int32 column
+// sums of B come from a separate read of B (or from the transpose pass); an
+// A whose row pitch is not a multiple of 16 bytes is copied into a padded
+// buffer, because TMA rows must start on 16-byte boundaries.
 //
 // Every mbarrier wait is bounded (tc::mbar_wait); on expiry the kernel raises
 // a CTA-wide abort flag, records the device error word, drains its own

@@ -640,18 +640,31 @@ class RequantEw(Workload):
 
     def cpu_step(self, o, rows, nthreads):
         import ctypes as C
+        ref = o.ref_lib()
         lib = o.lib()
 
         def part(r0, r1):
-            lib.oracle_requant_ew(C.c_void_p(self.ca.ctypes.data + 4 * r0), 0,
-                                  C.c_void_p(self.cb.ctypes.data + 4 * r0), 1, C.c_int64(r1 - r0),
-                                  1, C.c_int64(0), C.c_int32(self.MULT), self.SHIFT, self.ZP, 0,
-                                  -128, 127, -128, 127, None, C.c_void_p(self.cout.ctypes.data + r0))
+            a = C.c_void_p(self.ca.ctypes.data + 4 * r0)
+            b = C.c_void_p(self.cb.ctypes.data + 4 * r0)
+            out = C.c_void_p(self.cout.ctypes.data + r0)
+            if ref is not None:
+                # the reference's own reference.c, each thread on its slice
+                ref.ref_residual_add_requant(a, b, out, C.c_int(r1 - r0), C.c_int32(self.MULT),
+                                             C.c_int(self.SHIFT), C.c_int8(self.ZP))
+            else:
+                lib.oracle_requant_ew(a, 0, b, 1, C.c_int64(r1 - r0), 1, C.c_int64(0),
+                                      C.c_int32(self.MULT), self.SHIFT, self.ZP, 0, -128, 127,
+                                      -128, 127, None, out)
         _threaded(part, rows, nthreads)
         return 9.0 * rows
 
-    cpu_kind = "port"
-    cpu_what = "oracle/hexoracle.c restatement of residual_add_requant/reference.c"
+    @property
+    def cpu_kind(self):
+        from oracle import oracle as o
+        return "reference" if o.ref_lib() is not None else "port"
+
+    cpu_what = ("kernels/expert/residual_add_requant/reference.c (or its oracle/hexoracle.c "
+                "restatement where the reference is not built), one slice per thread")
 
 
 class ReduceI8(Workload):
@@ -701,18 +714,28 @@ class ReduceI8(Workload):
 
     def cpu_step(self, o, rows, nthreads):
         import ctypes as C
+        ref = o.ref_lib()
         lib = o.lib()
 
         def part(r0, r1):
             slot = min(255, r0 * max(1, nthreads) // max(1, rows))
-            lib.oracle_reduce_int(C.c_void_p(self.ca.ctypes.data + r0), None, 0,
-                                  C.c_int64(r1 - r0), 0,
-                                  C.c_void_p(self.cout.ctypes.data + 4 * slot))
+            a = C.c_void_p(self.ca.ctypes.data + r0)
+            out = C.c_void_p(self.cout.ctypes.data + 4 * slot)
+            if ref is not None:
+                # the reference's own reference.c, each thread on its slice
+                ref.ref_i8_sum_dma(a, C.c_int(r1 - r0), out)
+            else:
+                lib.oracle_reduce_int(a, None, 0, C.c_int64(r1 - r0), 0, out)
         _threaded(part, rows, nthreads)
         return float(rows)
 
-    cpu_kind = "port"
-    cpu_what = "oracle/hexoracle.c restatement of i8_sum_dma/reference.c (int32 sum)"
+    @property
+    def cpu_kind(self):
+        from oracle import oracle as o
+        return "reference" if o.ref_lib() is not None else "port"
+
+    cpu_what = ("kernels/expert/i8_sum_dma/reference.c (or its oracle/hexoracle.c restatement "
+                "where the reference is not built), one slice per thread, int32 partial sums")
 
 
 class GemmHmx(Workload):
